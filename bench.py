@@ -1,0 +1,370 @@
+#!/usr/bin/env python3
+"""Headline benchmark: GPT-2 124M training throughput, data parallel, on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+
+For N > 1 launch under torchrun (one process per GPU; RANK/LOCAL_RANK/
+WORLD_SIZE/MASTER_* from the environment), e.g.
+
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node 8 \
+        --master-addr 127.0.0.1 --master-port 29500 bench.py --gpus 8
+
+Config: GPT-2 small (12L, d=768, 12 heads, ctx 1024,
+vocab 50257, tied embeddings), per-GPU micro-batch 16 x 1024 of uniform-random
+tokens, random init, bf16 compute with fp32 master weights and fp32 gradient
+all-reduce in 25 MiB buckets, AdamW (lr 3e-4, betas 0.9/0.95, wd 0.1) with
+global-norm clipping at 1.0 -- every step is a full forward, backward,
+all-reduce and optimiser update.
+
+Timing: W untimed warm-up steps, then exactly K steps bracketed by a barrier and
+torch.cuda.synchronize() on both sides, timed with CUDA events on the compute
+stream; the step time is the MAX over ranks. Every step's working set (~10 GB
+of activations and weights) is far larger than the 126 MB L2, so no L2 flush is
+inserted. `value` is whole-job tokens/s (all N GPUs); `e2e` repeats the
+measurement through the public `Trainer.step` call with each step's inputs
+copied from pinned host memory and the loss read back to the host.
+
+`--impl reference` runs the UNMODIFIED reference (baseline/_ref, installed from
+the reference repository) through its own public API: its `GPT` under bf16
+autocast, `torch.optim.AdamW` from `configure_optimizers`, its
+`average_gradients` (25 MiB buckets over NCCL) for N > 1, and clipping.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "GPT-2 train tokens/s & MFU at 1/2/4/8 B200 per strategy, max over ranks"
+#: Reference's published GPT-2 124M training throughput (README.md:395; Apple
+#: M1 Max, MPS, fp32, B4 x T256) -- the only published throughput it has.
+BASELINE_TOKENS_PER_S = 4024.0
+
+
+# ------------------------------------------------------------------ clocks --
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons every 200 ms in a thread."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.gpus = set(gpu_indices)
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                idx = int(parts[0])
+                sm = float(parts[1])
+                smax = float(parts[2])
+                power = float(parts[3]) if parts[3] not in ("[N/A]", "N/A") else 0.0
+            except ValueError:
+                continue
+            if idx in self.gpus:
+                self.samples.append((idx, sm, smax, power, parts[5:9]))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sms = [s[1] for s in self.samples]
+        reasons = set()
+        for s in self.samples:
+            for name, val in zip(self.REASONS, s[4]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(s[2] for s in self.samples),
+                "reasons": sorted(reasons), "samples": len(self.samples),
+                "power_w_max": max(s[3] for s in self.samples)}
+
+
+# ------------------------------------------------------------- distributed --
+def setup_dist(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}; launch with torchrun for N>1")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier(device_ids=[torch.cuda.current_device()])
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def timed(step, steps: int, warmup: int, world: int, on_start=None, on_stop=None) -> float:
+    """ms per step: warmup, then K steps bracketed by barrier+sync, CUDA events."""
+    for i in range(warmup):
+        step(i)
+    barrier(world)
+    torch.cuda.synchronize()
+    if on_start:
+        on_start()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(steps):
+        step(warmup + i)
+    end.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    if on_stop:
+        on_stop()
+    ms = start.elapsed_time(end) / steps
+    return max_over_ranks(ms, world)
+
+
+def make_data(cfg, B, T, rank, pool=4):
+    g = torch.Generator().manual_seed(1234 + rank)
+    host = []
+    for _ in range(pool):
+        x = torch.randint(0, cfg.vocab_size, (B, T + 1), generator=g, dtype=torch.int64)
+        host.append((x[:, :-1].contiguous().pin_memory(), x[:, 1:].contiguous().pin_memory()))
+    dev = [(a.cuda(non_blocking=True), b.cuda(non_blocking=True)) for a, b in host]
+    torch.cuda.synchronize()
+    return host, dev
+
+
+# ------------------------------------------------------------------- arms --
+def run_native(args, world, rank):
+    from gpt2_harness_b200.config import TrainConfig, gpt2_config
+    from gpt2_harness_b200.ops import native as N
+    from gpt2_harness_b200.trainer import Trainer
+
+    cfg = gpt2_config(args.model)
+    tc = TrainConfig(lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, grad_clip=1.0, warmup_steps=0)
+    trainer = Trainer(cfg, args.batch, args.seq, train=tc, comm=args.comm, schedule=False)
+    host, dev = make_data(cfg, args.batch, args.seq, rank)
+    L = N.lib()
+
+    def dev_step(i):
+        idx, tgt = dev[i % len(dev)]
+        trainer.step_async(idx, tgt)
+
+    sampler = ClockSampler(gpu_list(world)) if rank == 0 else None
+    launches = {}
+
+    def start():
+        launches["a"] = L.launch_count()
+        if sampler:
+            sampler.start()
+
+    def stop():
+        launches["b"] = L.launch_count()
+        if sampler:
+            sampler.stop()
+
+    ms = timed(dev_step, args.steps, args.warmup, world, start, stop)
+    trainer.check()
+    n_launch = sum_over_ranks(launches["b"] - launches["a"], world)
+
+    def e2e_step(i):
+        idx, tgt = host[i % len(host)]
+        trainer.step(idx, tgt)  # H2D from pinned memory + loss read back
+
+    ms_e2e = timed(e2e_step, args.steps, 1, world)
+    trainer.check()
+    bi = 2 * args.batch * args.seq * 8  # idx + targets, int64
+    bo = 4  # fp32 loss scalar
+    out = finish_line(args, world, cfg, ms, ms_e2e, bi, bo, sampler, impl="native")
+    out["gpu_launches"] = int(n_launch)
+    out["config"]["comm"] = args.comm if world > 1 else "none"
+    trainer.close()
+    return out
+
+
+def run_reference(args, world, rank):
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "transformer_internals")):
+        return {"impl": "reference", "unavailable": "baseline/_ref not installed"}
+    sys.path.insert(0, ref_dir)
+    from transformer_internals.config import gpt2_config as ref_config
+    from transformer_internals.model import GPT as RefGPT
+    from transformer_internals.parallel.data_parallel import average_gradients
+
+    cfg = ref_config(args.model)
+    torch.manual_seed(0)
+    model = RefGPT(cfg).cuda()
+    if world > 1:
+        for p in model.parameters():
+            dist.broadcast(p.data, src=0)
+    opt = model.configure_optimizers(0.1, 3e-4, (0.9, 0.95))
+    host, dev = make_data(cfg, args.batch, args.seq, rank)
+
+    def train_step(idx, tgt):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = model(idx, tgt)["loss"]
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        if world > 1:
+            average_gradients(model.parameters(), world)
+        torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+        opt.step()
+        return loss
+
+    def dev_step(i):
+        idx, tgt = dev[i % len(dev)]
+        train_step(idx, tgt)
+
+    sampler = ClockSampler(gpu_list(world)) if rank == 0 else None
+    ms = timed(dev_step, args.steps, args.warmup, world,
+               sampler.start if sampler else None, sampler.stop if sampler else None)
+
+    def e2e_step(i):
+        idx, tgt = host[i % len(host)]
+        loss = train_step(idx.cuda(non_blocking=True), tgt.cuda(non_blocking=True))
+        loss.item()
+
+    ms_e2e = timed(e2e_step, args.steps, 1, world)
+    bi = 2 * args.batch * args.seq * 8
+    return finish_line(args, world, cfg, ms, ms_e2e, bi, 4, sampler, impl="reference")
+
+
+def gpu_list(world):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        try:
+            return [int(x) for x in vis.split(",")][:world]
+        except ValueError:
+            pass
+    return list(range(world))
+
+
+def finish_line(args, world, cfg, ms, ms_e2e, bi, bo, sampler, impl):
+    from gpt2_harness_b200.perf.mfu import flops_per_token_exact, measured_peak_tflops
+
+    tokens = args.batch * args.seq * world
+    tps = tokens / (ms / 1e3)
+    tps_e2e = tokens / (ms_e2e / 1e3)
+    fpt = flops_per_token_exact(cfg, args.seq)["training_flops_per_token"]
+    peak, label = measured_peak_tflops(sustained=True)
+    mfu = fpt * tps / (peak * 1e12 * world)
+    clocks = sampler.summary() if sampler else {}
+    line = {
+        "metric": METRIC,
+        "value": round(tps, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": round(tps / BASELINE_TOKENS_PER_S, 2),
+        "dtype": "bf16",
+        "data": "synthetic uniform-random tokens, random-init weights",
+        "mfu": round(mfu, 4),
+        "mfu_peak": f"{peak} TFLOP/s per GPU, {label}",
+        "flops_per_token": fpt,
+        "config": {
+            "model": f"{args.model} (124M)" if args.model == "gpt2" else args.model,
+            "global_batch": args.batch * world,
+            "per_gpu_batch": args.batch,
+            "seq_len": args.seq,
+            "parallelism": f"dp{world}",
+            "strategy": "ddp",
+            "bucket_mb": 25,
+            "optimizer": "AdamW + clip 1.0, fp32 master",
+            "l2": "inputs larger than L2 (per-step working set ~10 GB >> 126 MB), no flush",
+            "baseline": "README.md:395 (M1 Max MPS fp32, B4xT256, 4024 tokens/s)",
+        },
+        "e2e": {"value": round(tps_e2e, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
+                "ms_per_step": round(ms_e2e, 3)},
+        "clocks": {k: clocks.get(k) for k in ("sm_mhz", "sm_max_mhz", "reasons")},
+        "impl": impl,
+    }
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--model", default="gpt2")
+    ap.add_argument("--batch", type=int, default=16)
+    ap.add_argument("--seq", type=int, default=1024)
+    ap.add_argument("--comm", choices=["p2p", "nccl"], default="p2p")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    world, rank, _ = setup_dist(args.gpus)
+    try:
+        if args.impl == "reference":
+            out = run_reference(args, world, rank)
+        else:
+            out = run_native(args, world, rank)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+    finally:
+        if world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

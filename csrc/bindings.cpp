@@ -1,0 +1,264 @@
+// Python bindings of the gpt2_harness_b200 native library.
+//
+// The launchers take raw device addresses (Python ints from Tensor.data_ptr())
+// and a CUDA stream handle: validation of shapes, dtypes and devices happens
+// once in gpt2_harness_b200/ops/*.py, so a launch from Python costs one
+// pybind call and nothing else, and every call is capturable in a CUDA graph.
+#include <pybind11/pybind11.h>
+#include <cuda_runtime.h>
+#include <stdexcept>
+#include <string>
+
+#include "attention.cuh"
+#include "comm.cuh"
+#include "elementwise.cuh"
+#include "gemm.cuh"
+#include "launch_count.h"
+
+namespace py = pybind11;
+using namespace g2b;
+
+namespace {
+
+template <typename T>
+T* P(int64_t v) {
+  return reinterpret_cast<T*>(static_cast<uintptr_t>(v));
+}
+cudaStream_t S(int64_t v) { return reinterpret_cast<cudaStream_t>(static_cast<uintptr_t>(v)); }
+
+void check(int rc, const char* what) {
+  if (rc != 0) {
+    cudaError_t e = cudaPeekAtLastError();
+    throw std::runtime_error(std::string(what) + " failed (code " + std::to_string(rc) +
+                             ", cuda: " + cudaGetErrorString(e) + ")");
+  }
+}
+
+HeadView hv(int64_t base, int64_t sb, int64_t st, int64_t sh) {
+  HeadView v;
+  v.base = P<void>(base);
+  v.sb = sb;
+  v.st = st;
+  v.sh = sh;
+  return v;
+}
+
+}  // namespace
+
+PYBIND11_MODULE(_C, m) {
+  m.doc() = "sm_100a kernels of gpt2_harness_b200";
+  m.def("launch_count", []() { return (long long)launch_counter().load(); },
+        "Number of kernels this library has launched in this process.");
+
+  m.def(
+      "gemm",
+      [](int64_t A, int64_t lda, int a_mn, int64_t B, int64_t ldb, int b_mn, int M, int N, int K,
+         int epi, int64_t out, int64_t ldo, int64_t aux, int64_t ldaux, int64_t bias, float alpha,
+         int64_t alpha_ptr, int accumulate, int splits, int64_t workspace, int bn, int max_ctas,
+         int64_t err, int64_t stream) {
+        GemmArgs g;
+        g.A = P<void>(A);
+        g.lda = lda;
+        g.a_mn_major = a_mn;
+        g.B = P<void>(B);
+        g.ldb = ldb;
+        g.b_mn_major = b_mn;
+        g.M = M;
+        g.N = N;
+        g.K = K;
+        g.epilogue = epi;
+        g.out = P<void>(out);
+        g.ldo = ldo;
+        g.aux = P<void>(aux);
+        g.ldaux = ldaux;
+        g.bias = P<void>(bias);
+        g.alpha = alpha;
+        g.alpha_ptr = P<float>(alpha_ptr);
+        g.accumulate = accumulate;
+        g.splits = splits;
+        g.workspace = P<void>(workspace);
+        g.bn = bn;
+        g.max_ctas = max_ctas;
+        g.err = P<uint32_t>(err);
+        check(gemm_bf16_launch(g, S(stream)), "gemm_bf16");
+      });
+
+  m.def("attn_fwd", [](int64_t q, int64_t k, int64_t v, int64_t o, int64_t sb, int64_t st,
+                       int64_t sh, int64_t osb, int64_t ost, int64_t osh, int64_t lse, int B,
+                       int H, int Tq, int Tk, int q_offset, int causal, float scale,
+                       int64_t kv_sb, int64_t kv_st, int64_t kv_sh, int64_t err, int64_t stream) {
+    AttnArgs a;
+    a.q = hv(q, sb, st, sh);
+    a.k = hv(k, kv_sb, kv_st, kv_sh);
+    a.v = hv(v, kv_sb, kv_st, kv_sh);
+    a.o = hv(o, osb, ost, osh);
+    a.lse = P<float>(lse);
+    a.B = B;
+    a.H = H;
+    a.Tq = Tq;
+    a.Tk = Tk;
+    a.q_offset = q_offset;
+    a.causal = causal;
+    a.scale = scale;
+    a.err = P<uint32_t>(err);
+    check(attn_fwd_launch(a, S(stream)), "attn_fwd");
+  });
+
+  m.def("attn_bwd",
+        [](int64_t q, int64_t k, int64_t v, int64_t o, int64_t dout, int64_t dq, int64_t dk,
+           int64_t dv, int64_t sb, int64_t st, int64_t sh, int64_t osb, int64_t ost, int64_t osh,
+           int64_t dsb, int64_t dst, int64_t dsh, int64_t lse, int64_t delta, int B, int H,
+           int Tq, int Tk, int q_offset, int causal, float scale, int64_t kv_sb, int64_t kv_st,
+           int64_t kv_sh, int64_t dkv_sb, int64_t dkv_st, int64_t dkv_sh, int64_t err,
+           int64_t stream) {
+          AttnArgs a;
+          a.q = hv(q, sb, st, sh);
+          a.k = hv(k, kv_sb, kv_st, kv_sh);
+          a.v = hv(v, kv_sb, kv_st, kv_sh);
+          a.o = hv(o, osb, ost, osh);
+          a.dout = hv(dout, osb, ost, osh);
+          a.dq = hv(dq, dsb, dst, dsh);
+          a.dk = hv(dk, dkv_sb, dkv_st, dkv_sh);
+          a.dv = hv(dv, dkv_sb, dkv_st, dkv_sh);
+          a.lse = P<float>(lse);
+          a.delta = P<float>(delta);
+          a.B = B;
+          a.H = H;
+          a.Tq = Tq;
+          a.Tk = Tk;
+          a.q_offset = q_offset;
+          a.causal = causal;
+          a.scale = scale;
+          a.err = P<uint32_t>(err);
+          check(attn_bwd_launch(a, S(stream)), "attn_bwd");
+        });
+
+  m.def("layernorm_fwd", [](int64_t x, int64_t ldx, int64_t g, int64_t b, int64_t y, int64_t ldy,
+                            int64_t mean, int64_t rstd, int M, int C, float eps, int64_t stream) {
+    check(layernorm_fwd_launch(P<float>(x), ldx, P<void>(g), P<void>(b), P<void>(y), ldy,
+                               P<float>(mean), P<float>(rstd), M, C, eps, S(stream)),
+          "layernorm_fwd");
+  });
+
+  m.def("layernorm_bwd", [](int64_t dy, int64_t x, int64_t mean, int64_t rstd, int64_t g,
+                            int64_t dres, int64_t dres_bf16, int64_t partials, int M, int C,
+                            int accumulate, int64_t stream) {
+    int nblk = 0;
+    check(layernorm_bwd_launch(P<void>(dy), P<float>(x), P<float>(mean), P<float>(rstd),
+                               P<void>(g), P<float>(dres), P<void>(dres_bf16), P<float>(partials),
+                               &nblk, M, C, accumulate, S(stream)),
+          "layernorm_bwd");
+    return nblk;
+  });
+
+  m.def("layernorm_bwd_blocks", [](int M) { return (M + 31) / 32; });
+
+  m.def("colsum_f32", [](int64_t in, int R, int C, int64_t out, int acc, int64_t stream) {
+    check(colsum_f32_launch(P<float>(in), R, C, P<float>(out), acc, S(stream)), "colsum_f32");
+  });
+
+  m.def("colsum_bf16", [](int64_t in, int64_t ld, int M, int C, int64_t ws, int64_t out, int acc,
+                          int64_t stream) {
+    check(colsum_bf16_launch(P<void>(in), ld, M, C, P<float>(ws), P<float>(out), acc, S(stream)),
+          "colsum_bf16");
+  });
+
+  m.def("embedding_fwd", [](int64_t idx, int64_t wte, int64_t wpe, int64_t x, int B, int T, int C,
+                            int pos0, int64_t stream) {
+    check(embedding_fwd_launch(P<int64_t>(idx), P<void>(wte), P<void>(wpe), P<float>(x), B, T, C,
+                               pos0, S(stream)),
+          "embedding_fwd");
+  });
+
+  m.def("embedding_bwd", [](int64_t idx, int64_t dx, int64_t wte_grad, int64_t wpe_grad, int B,
+                            int T, int C, int V, int pos0, int64_t stream) {
+    check(embedding_bwd_launch(P<int64_t>(idx), P<float>(dx), P<float>(wte_grad),
+                               P<float>(wpe_grad), B, T, C, V, pos0, S(stream)),
+          "embedding_bwd");
+  });
+
+  m.def("cross_entropy", [](int64_t logits, int64_t ld, int64_t targets, int64_t loss_rows, int M,
+                            int V, int vocab_offset, int64_t stream) {
+    check(cross_entropy_fwd_bwd_launch(P<void>(logits), ld, P<int64_t>(targets),
+                                       P<float>(loss_rows), M, V, vocab_offset, S(stream)),
+          "cross_entropy");
+  });
+
+  m.def("loss_reduce", [](int64_t loss_rows, int64_t targets, int M, int64_t out, int64_t stream) {
+    check(loss_reduce_launch(P<float>(loss_rows), P<int64_t>(targets), M, P<float>(out),
+                             S(stream)),
+          "loss_reduce");
+  });
+
+  m.def("adamw", [](int64_t p, int64_t g, int64_t mm, int64_t v, int64_t pb, int64_t n,
+                    int64_t n_decay, int64_t ranges, int nr, int64_t hp, int64_t clip,
+                    int64_t stream) {
+    check(adamw_launch(P<float>(p), P<float>(g), P<float>(mm), P<float>(v), P<void>(pb), n,
+                       n_decay, P<int64_t>(ranges), nr, P<float>(hp), P<float>(clip), S(stream)),
+          "adamw");
+  });
+
+  m.def("sumsq", [](int64_t g, int64_t n, int64_t ws, int64_t out, int64_t stream) {
+    check(sumsq_launch(P<float>(g), n, P<float>(ws), P<float>(out), S(stream)), "sumsq");
+  });
+
+  m.def("clip_coef", [](int64_t sumsq, float scale2, float max_norm, int64_t clip,
+                        int64_t norm_out, int64_t stream) {
+    check(clip_coef_launch(P<float>(sumsq), scale2, max_norm, P<float>(clip), P<float>(norm_out),
+                           S(stream)),
+          "clip_coef");
+  });
+
+  m.def("cast_f32_bf16", [](int64_t in, int64_t out, int64_t n, int64_t stream) {
+    check(cast_f32_bf16_launch(P<float>(in), P<void>(out), n, S(stream)), "cast_f32_bf16");
+  });
+  m.def("cast_bf16_f32", [](int64_t in, int64_t out, int64_t n, int64_t stream) {
+    check(cast_bf16_f32_launch(P<void>(in), P<float>(out), n, S(stream)), "cast_bf16_f32");
+  });
+  m.def("scale_f32", [](int64_t x, int64_t n, float a, int64_t stream) {
+    check(scale_f32_launch(P<float>(x), n, a, S(stream)), "scale_f32");
+  });
+
+  // ----------------------------------------------------- peer-memory comm ---
+  m.def("ipc_handle", [](int64_t ptr) { return py::bytes(comm_ipc_handle(P<void>(ptr))); });
+  m.def("ipc_open", [](py::bytes h) {
+    void* p = comm_ipc_open(std::string(h));
+    if (!p) throw std::runtime_error("ipc_open: cudaIpcOpenMemHandle failed");
+    return (int64_t)(uintptr_t)p;
+  });
+  m.def("ipc_close", [](int64_t ptr) { comm_ipc_close(P<void>(ptr)); });
+  m.def("enable_peer_access", [](int peer) { return comm_enable_peer(peer); });
+  m.def("symm_alloc", [](int64_t bytes) {
+    void* p = comm_symm_alloc(bytes);
+    if (!p) throw std::runtime_error("symm_alloc: cudaMalloc failed");
+    return (int64_t)(uintptr_t)p;
+  });
+  m.def("symm_free", [](int64_t p) { comm_symm_free(P<void>(p)); });
+  m.def("allreduce_p2p",
+        [](int64_t peer_bufs, int64_t peer_flags, int rank, int world, int64_t offset, int64_t n,
+           int dtype, float scale, uint32_t epoch, int64_t counter, int64_t err, int nblocks,
+           int64_t wait_budget_ns, int64_t stream) {
+          CommArgs c;
+          c.peer_bufs = P<void*>(peer_bufs);
+          c.peer_flags = P<uint32_t*>(peer_flags);
+          c.rank = rank;
+          c.world = world;
+          c.offset = offset;
+          c.n = n;
+          c.dtype = dtype;
+          c.scale = scale;
+          c.epoch = epoch;
+          c.byte_counter = P<unsigned long long>(counter);
+          c.err = P<uint32_t>(err);
+          c.nblocks = nblocks;
+          c.wait_budget_ns = wait_budget_ns;
+          check(comm_allreduce_launch(c, S(stream)), "allreduce_p2p");
+        });
+  m.def("comm_flag_words", []() { return 2 * kCommMaxRanks * kCommMaxBlocks; });
+  m.def("flag_wait_test", [](int64_t flag, uint32_t value, int64_t budget_ns, int64_t err,
+                             int64_t stream) {
+    check(comm_flag_wait_test_launch(P<uint32_t>(flag), value, budget_ns, P<uint32_t>(err),
+                                     S(stream)),
+          "flag_wait_test");
+  });
+}

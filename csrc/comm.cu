@@ -1,0 +1,241 @@
+// Fused peer-memory all-reduce over NVLink 5 / NVSwitch (sm_100a).
+//
+// Replaces the DDP bucket all-reduce of the reference
+// (src/transformer_internals/parallel/data_parallel.py:98-152: SUM all-reduce
+// of 25 MB reverse-order buckets, then divide by p) with one kernel per bucket
+// that does the reduce-scatter, the 1/p scale and the all-gather itself:
+//
+//   1. every CTA j of every rank raises "arrived" flag j on all peers
+//      (st.release.sys through the peer mapping), then waits (bounded) until
+//      all peers' CTA j have arrived: the gradients each peer produced before
+//      this launch are complete;
+//   2. CTA j of rank r owns part j of slice r of the bucket: it loads that part
+//      from every peer's buffer (P2P loads over NVLink, fp32 accumulate),
+//      scales by 1/p and stores the result into every peer's buffer (P2P
+//      stores): reduce-scatter + all-gather with no staging copy;
+//   3. every CTA raises "done" on all peers and waits for all peers' "done",
+//      so on exit this rank's buffer holds the final reduced bucket.
+//
+// Bytes each rank moves: (p-1)/p * S loaded + (p-1)/p * S stored, the ring
+// optimum. All waits are bounded by a wall-clock budget; on expiry the kernel
+// records ERR_TIMEOUT_PEER and returns without touching peer data.
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <string.h>
+
+#include "comm.cuh"
+#include "common.cuh"
+
+namespace g2b {
+namespace {
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Wait until (int)(*flag - epoch) >= 0. Returns false on timeout.
+__device__ bool wait_flag(const uint32_t* flag, uint32_t epoch, int64_t budget) {
+  if ((int32_t)(ld_acquire_sys(flag) - epoch) >= 0) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if ((int32_t)(ld_acquire_sys(flag) - epoch) >= 0) return true;
+    if ((int64_t)(globaltimer_ns() - t0) > budget) return false;
+    __nanosleep(64);
+  }
+}
+
+__device__ __forceinline__ uint32_t* flag_slot(uint32_t* base, int phase, int src_rank, int blk) {
+  return base + ((phase * kCommMaxRanks + src_rank) * kCommMaxBlocks + blk);
+}
+
+// Arrive/wait handshake of one CTA against the same CTA index on every peer.
+__device__ bool handshake(const CommArgs& a, int phase, int* fail) {
+  const int j = blockIdx.x;
+  if (threadIdx.x < a.world) {
+    const int q = threadIdx.x;
+    st_release_sys(flag_slot(a.peer_flags[q], phase, a.rank, j), a.epoch);
+  }
+  if (threadIdx.x < a.world) {
+    const int q = threadIdx.x;
+    if (!wait_flag(flag_slot(a.peer_flags[a.rank], phase, q, j), a.epoch, a.wait_budget_ns)) {
+      *fail = 1;
+      report_error(a.err, ERR_TIMEOUT_PEER);
+    }
+  }
+  __syncthreads();
+  return *fail == 0;
+}
+
+template <typename T>
+struct Vec;
+template <>
+struct Vec<float> {
+  static constexpr int N = 4;  // elements per 16-byte vector
+};
+template <>
+struct Vec<__nv_bfloat16> {
+  static constexpr int N = 8;
+};
+
+__device__ __forceinline__ void acc_vec(float* acc, const uint4& w, float) {
+  acc[0] += __uint_as_float(w.x);
+  acc[1] += __uint_as_float(w.y);
+  acc[2] += __uint_as_float(w.z);
+  acc[3] += __uint_as_float(w.w);
+}
+__device__ __forceinline__ void acc_vec(float* acc, const uint4& w, __nv_bfloat16) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack_bf16x2(ws[i]);
+    acc[2 * i] += f.x;
+    acc[2 * i + 1] += f.y;
+  }
+}
+__device__ __forceinline__ uint4 pack_vec(const float* acc, float) {
+  return make_uint4(__float_as_uint(acc[0]), __float_as_uint(acc[1]), __float_as_uint(acc[2]),
+                    __float_as_uint(acc[3]));
+}
+__device__ __forceinline__ uint4 pack_vec(const float* acc, __nv_bfloat16) {
+  return make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                    pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+}
+
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <typename T>
+__device__ __forceinline__ T from_f32(float x);
+template <>
+__device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
+  return __float2bfloat16(x);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(512) allreduce_p2p_kernel(const CommArgs a) {
+  __shared__ int fail;
+  if (threadIdx.x == 0) fail = 0;
+  __syncthreads();
+  if (!handshake(a, 0, &fail)) return;
+
+  constexpr int VN = Vec<T>::N;
+  // Vectorised part: slices of whole 16-byte vectors; the scalar tail (< VN
+  // elements per rank boundary) is handled by rank 0's last CTA.
+  const int64_t nvec = a.n / VN;
+  const int64_t per_rank = (nvec + a.world - 1) / a.world;
+  const int64_t s0 = min(nvec, per_rank * a.rank), s1 = min(nvec, s0 + per_rank);
+  const int64_t per_blk = (s1 - s0 + gridDim.x - 1) / gridDim.x;
+  const int64_t b0 = min(s1, s0 + per_blk * blockIdx.x), b1 = min(s1, b0 + per_blk);
+  const T zero_tag{};
+  for (int64_t v = b0 + threadIdx.x; v < b1; v += blockDim.x) {
+    float acc[VN];
+#pragma unroll
+    for (int i = 0; i < VN; ++i) acc[i] = 0.f;
+    for (int q = 0; q < a.world; ++q) {
+      const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.peer_bufs[q]) + a.offset) + v;
+      const uint4 w = __ldcg(src);
+      acc_vec(acc, w, zero_tag);
+    }
+#pragma unroll
+    for (int i = 0; i < VN; ++i) acc[i] *= a.scale;
+    const uint4 out = pack_vec(acc, zero_tag);
+    for (int q = 0; q < a.world; ++q) {
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.peer_bufs[q]) + a.offset) + v;
+      __stcg(dst, out);
+    }
+  }
+  if (a.rank == 0 && blockIdx.x == gridDim.x - 1) {
+    for (int64_t e = nvec * VN + threadIdx.x; e < a.n; e += blockDim.x) {
+      float acc = 0.f;
+      for (int q = 0; q < a.world; ++q) {
+        const T* src = reinterpret_cast<const T*>(a.peer_bufs[q]) + a.offset + e;
+        acc += to_f32(__ldcg(src));
+      }
+      for (int q = 0; q < a.world; ++q)
+        reinterpret_cast<T*>(a.peer_bufs[q])[a.offset + e] = from_f32<T>(acc * a.scale);
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
+    atomicAdd(a.byte_counter, (unsigned long long)a.n * sizeof(T));
+  handshake(a, 1, &fail);
+}
+
+__global__ void flag_wait_test_kernel(uint32_t* flag, uint32_t value, int64_t budget,
+                                      uint32_t* err) {
+  if (!wait_flag(flag, value, budget)) report_error(err, ERR_TIMEOUT_PEER);
+}
+
+}  // namespace
+
+int comm_allreduce_launch(const CommArgs& a, cudaStream_t s) {
+  if (a.world < 1 || a.world > kCommMaxRanks || a.nblocks < 1 || a.nblocks > kCommMaxBlocks)
+    return -1;
+  if (a.n <= 0) return 0;
+  const int esz = a.dtype == 0 ? 4 : 2;
+  if ((a.offset * esz) % 16) return -2;  // bucket starts must be 16-byte aligned
+  if (a.dtype == 0)
+    allreduce_p2p_kernel<float><<<a.nblocks, 512, 0, s>>>(a);
+  else
+    allreduce_p2p_kernel<__nv_bfloat16><<<a.nblocks, 512, 0, s>>>(a);
+  count_launches(1);
+  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+}
+
+int comm_flag_wait_test_launch(uint32_t* flag, uint32_t value, int64_t budget_ns, uint32_t* err,
+                               cudaStream_t s) {
+  flag_wait_test_kernel<<<1, 1, 0, s>>>(flag, value, budget_ns, err);
+  count_launches(1);
+  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+}
+
+std::string comm_ipc_handle(void* ptr) {
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, ptr) != cudaSuccess) return std::string();
+  return std::string(reinterpret_cast<const char*>(&h), sizeof(h));
+}
+
+void* comm_ipc_open(const std::string& handle) {
+  if (handle.size() != sizeof(cudaIpcMemHandle_t)) return nullptr;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle.data(), sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return nullptr;
+  return p;
+}
+
+void comm_ipc_close(void* ptr) {
+  if (ptr) cudaIpcCloseMemHandle(ptr);
+}
+
+void* comm_symm_alloc(int64_t bytes) {
+  void* p = nullptr;
+  if (cudaMalloc(&p, (size_t)bytes) != cudaSuccess) return nullptr;
+  if (cudaMemset(p, 0, (size_t)bytes) != cudaSuccess) {
+    cudaFree(p);
+    return nullptr;
+  }
+  return p;
+}
+
+void comm_symm_free(void* p) {
+  if (p) cudaFree(p);
+}
+
+int comm_enable_peer(int peer) {
+  cudaError_t e = cudaDeviceEnablePeerAccess(peer, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    cudaGetLastError();
+    return 0;
+  }
+  return e == cudaSuccess ? 0 : (int)e;
+}
+
+}  // namespace g2b

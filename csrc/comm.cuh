@@ -1,0 +1,52 @@
+// Host-side interface of the peer-memory collectives (csrc/comm.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string>
+
+namespace g2b {
+
+constexpr int kCommMaxBlocks = 128;  // flag slots per (phase, rank)
+constexpr int kCommMaxRanks = 8;
+
+// One fused all-reduce over NVLink peer memory. Every rank owns a symmetric
+// buffer (same size, same element offsets on every rank); peer_bufs[q] is rank
+// q's buffer mapped into this process, peer_flags[q] rank q's flag array
+// ([2][kCommMaxRanks][kCommMaxBlocks] uint32). The kernel reduces elements
+// [offset, offset + n) across ranks, multiplies by `scale` and leaves the
+// result in every rank's buffer.
+struct CommArgs {
+  void** peer_bufs = nullptr;       // device array [world]
+  uint32_t** peer_flags = nullptr;  // device array [world]
+  int rank = 0, world = 1;
+  int64_t offset = 0, n = 0;        // elements
+  int dtype = 0;                    // 0 = fp32 buffer, 1 = bf16 buffer
+  float scale = 1.f;
+  uint32_t epoch = 0;               // strictly increasing per call, same on all ranks
+  unsigned long long* byte_counter = nullptr;  // payload bytes (reference convention)
+  uint32_t* err = nullptr;
+  int nblocks = 32;
+  int64_t wait_budget_ns = 2000000000ll;
+};
+
+int comm_allreduce_launch(const CommArgs& a, cudaStream_t s);
+
+// Launch a single-thread kernel that waits (bounded) for *flag == value and
+// records ERR_TIMEOUT_PEER in *err when the budget expires. Used to test the
+// bounded-wait path: a flag nobody sets must time out and leave the context
+// usable.
+int comm_flag_wait_test_launch(uint32_t* flag, uint32_t value, int64_t budget_ns, uint32_t* err,
+                               cudaStream_t s);
+
+// CUDA IPC helpers: export a device allocation, open a peer's, close it.
+std::string comm_ipc_handle(void* ptr);
+void* comm_ipc_open(const std::string& handle);
+void comm_ipc_close(void* ptr);
+int comm_enable_peer(int peer);
+
+// A zero-filled device allocation of its own (cudaMalloc), so that one CUDA
+// IPC handle covers exactly this buffer; released with comm_symm_free.
+void* comm_symm_alloc(int64_t bytes);
+void comm_symm_free(void* p);
+
+}  // namespace g2b

@@ -1,0 +1,672 @@
+// Memory-bound kernels of the GPT-2 training step (sm_100a).
+//
+// Reference ops covered (src/transformer_internals/...):
+//   model.py:382,384,473   nn.LayerNorm (eps 1e-5)        -> layernorm_fwd / _bwd
+//   model.py:561-564       wte[idx] + wpe[pos]             -> embedding_fwd / _bwd
+//   model.py:593-598       F.cross_entropy(ignore -100)    -> cross_entropy_fwd_bwd
+//   zero.py:158-186        AdamW (torch single-tensor order) -> adamw
+//   zero.py:194-233        global grad norm + clip coef    -> sumsq / clip_coef
+// Every reduction is deterministic (fixed order, no float atomics) except the
+// token-embedding scatter, which uses fp32 atomics.
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <math.h>
+
+#include <type_traits>
+
+#include "common.cuh"
+#include "elementwise.cuh"
+
+namespace g2b {
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffff, v, o));
+  return v;
+}
+
+int grid_for(int64_t work, int per_block, int cap = 148 * 16) {
+  int64_t g = (work + per_block - 1) / per_block;
+  if (g < 1) g = 1;
+  if (g > cap) g = cap;
+  return (int)g;
+}
+
+// --------------------------------------------------------------- LayerNorm ---
+constexpr int LN_MAXV_CAP = 16;  // float4 per lane -> C <= 2048
+
+// Smallest compiled float4-per-lane count covering C (keeps registers tight).
+template <typename F>
+int ln_dispatch(int C, F&& f) {
+  const int need = (C / 4 + 31) / 32;
+  if (need <= 1) return f(std::integral_constant<int, 1>{});
+  if (need <= 2) return f(std::integral_constant<int, 2>{});
+  if (need <= 4) return f(std::integral_constant<int, 4>{});
+  if (need <= 6) return f(std::integral_constant<int, 6>{});
+  if (need <= 8) return f(std::integral_constant<int, 8>{});
+  if (need <= 10) return f(std::integral_constant<int, 10>{});
+  if (need <= 13) return f(std::integral_constant<int, 13>{});
+  return f(std::integral_constant<int, 16>{});
+}
+
+template <int LN_MAXV>
+__global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x, int64_t ldx,
+                                                     const __nv_bfloat16* __restrict__ g,
+                                                     const __nv_bfloat16* __restrict__ bta,
+                                                     __nv_bfloat16* __restrict__ y, int64_t ldy,
+                                                     float* __restrict__ mean,
+                                                     float* __restrict__ rstd, int M, int C,
+                                                     float eps) {
+  const int warps = blockDim.x >> 5;
+  const int row = blockIdx.x * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const int C4 = C >> 2;
+  const float4* xr = reinterpret_cast<const float4*>(x + (int64_t)row * ldx);
+  float4 v[LN_MAXV];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < LN_MAXV; ++i) {
+    const int c = lane + 32 * i;
+    if (c < C4) {
+      v[i] = xr[c];
+      s += v[i].x + v[i].y + v[i].z + v[i].w;
+    }
+  }
+  const float mu = warp_sum(s) / C;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < LN_MAXV; ++i) {
+    const int c = lane + 32 * i;
+    if (c < C4) {
+      const float a = v[i].x - mu, b = v[i].y - mu, cc = v[i].z - mu, d = v[i].w - mu;
+      q += a * a + b * b + cc * cc + d * d;
+    }
+  }
+  const float var = warp_sum(q) / C;
+  const float rs = rsqrtf(var + eps);
+  __nv_bfloat16* yr = y + (int64_t)row * ldy;
+#pragma unroll
+  for (int i = 0; i < LN_MAXV; ++i) {
+    const int c = lane + 32 * i;
+    if (c < C4) {
+      const uint2 gw = *reinterpret_cast<const uint2*>(g + 4 * c);
+      const uint2 bw = *reinterpret_cast<const uint2*>(bta + 4 * c);
+      const float2 g01 = unpack_bf16x2(gw.x), g23 = unpack_bf16x2(gw.y);
+      const float2 b01 = unpack_bf16x2(bw.x), b23 = unpack_bf16x2(bw.y);
+      uint2 o;
+      o.x = pack_bf16x2((v[i].x - mu) * rs * g01.x + b01.x, (v[i].y - mu) * rs * g01.y + b01.y);
+      o.y = pack_bf16x2((v[i].z - mu) * rs * g23.x + b23.x, (v[i].w - mu) * rs * g23.y + b23.y);
+      *reinterpret_cast<uint2*>(yr + 4 * c) = o;
+    }
+  }
+  if (lane == 0) {
+    mean[row] = mu;
+    rstd[row] = rs;
+  }
+}
+
+constexpr int LNB_ROWS = 32;  // rows per CTA in backward (8 warps x 4 rows)
+
+template <int LN_MAXV>
+__global__ void __launch_bounds__(256) ln_bwd_kernel(
+    const __nv_bfloat16* __restrict__ dy, const float* __restrict__ x,
+    const float* __restrict__ mean, const float* __restrict__ rstd,
+    const __nv_bfloat16* __restrict__ g, float* __restrict__ dres,
+    __nv_bfloat16* __restrict__ dres_bf16, float* __restrict__ partials, int M, int C,
+    int accumulate) {
+  extern __shared__ float sred[];  // [8 warps][2][C]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int C4 = C >> 2;
+  float4 dg[LN_MAXV], db[LN_MAXV];
+#pragma unroll
+  for (int i = 0; i < LN_MAXV; ++i) dg[i] = db[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+  for (int rr = 0; rr < LNB_ROWS / 8; ++rr) {
+    const int row = blockIdx.x * LNB_ROWS + warp * (LNB_ROWS / 8) + rr;
+    if (row >= M) break;
+    const float mu = mean[row], rs = rstd[row];
+    const float4* xr = reinterpret_cast<const float4*>(x + (int64_t)row * C);
+    const __nv_bfloat16* dyr = dy + (int64_t)row * C;
+    float4 xh[LN_MAXV], gy[LN_MAXV];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < LN_MAXV; ++i) {
+      const int c = lane + 32 * i;
+      if (c < C4) {
+        const float4 xv = xr[c];
+        const uint2 dw = *reinterpret_cast<const uint2*>(dyr + 4 * c);
+        const uint2 gw = *reinterpret_cast<const uint2*>(g + 4 * c);
+        const float2 d01 = unpack_bf16x2(dw.x), d23 = unpack_bf16x2(dw.y);
+        const float2 g01 = unpack_bf16x2(gw.x), g23 = unpack_bf16x2(gw.y);
+        xh[i] = make_float4((xv.x - mu) * rs, (xv.y - mu) * rs, (xv.z - mu) * rs, (xv.w - mu) * rs);
+        gy[i] = make_float4(d01.x * g01.x, d01.y * g01.y, d23.x * g23.x, d23.y * g23.y);
+        dg[i].x += d01.x * xh[i].x;
+        dg[i].y += d01.y * xh[i].y;
+        dg[i].z += d23.x * xh[i].z;
+        dg[i].w += d23.y * xh[i].w;
+        db[i].x += d01.x;
+        db[i].y += d01.y;
+        db[i].z += d23.x;
+        db[i].w += d23.y;
+        s1 += gy[i].x + gy[i].y + gy[i].z + gy[i].w;
+        s2 += gy[i].x * xh[i].x + gy[i].y * xh[i].y + gy[i].z * xh[i].z + gy[i].w * xh[i].w;
+      }
+    }
+    s1 = warp_sum(s1) / C;
+    s2 = warp_sum(s2) / C;
+    float4* dr = reinterpret_cast<float4*>(dres + (int64_t)row * C);
+    __nv_bfloat16* db16 = dres_bf16 ? dres_bf16 + (int64_t)row * C : nullptr;
+#pragma unroll
+    for (int i = 0; i < LN_MAXV; ++i) {
+      const int c = lane + 32 * i;
+      if (c < C4) {
+        float4 d = make_float4(rs * (gy[i].x - s1 - xh[i].x * s2), rs * (gy[i].y - s1 - xh[i].y * s2),
+                               rs * (gy[i].z - s1 - xh[i].z * s2), rs * (gy[i].w - s1 - xh[i].w * s2));
+        if (accumulate) {
+          const float4 o = dr[c];
+          d.x += o.x;
+          d.y += o.y;
+          d.z += o.z;
+          d.w += o.w;
+        }
+        dr[c] = d;
+        if (db16) {
+          uint2 w;
+          w.x = pack_bf16x2(d.x, d.y);
+          w.y = pack_bf16x2(d.z, d.w);
+          *reinterpret_cast<uint2*>(db16 + 4 * c) = w;
+        }
+      }
+    }
+  }
+  // Deterministic CTA-level reduction of dgamma/dbeta across the 8 warps.
+#pragma unroll
+  for (int i = 0; i < LN_MAXV; ++i) {
+    const int c = lane + 32 * i;
+    if (c < C4) {
+      reinterpret_cast<float4*>(sred + (warp * 2) * C)[c] = dg[i];
+      reinterpret_cast<float4*>(sred + (warp * 2 + 1) * C)[c] = db[i];
+    }
+  }
+  __syncthreads();
+  const int nblk = gridDim.x;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float a = 0.f, b = 0.f;
+    for (int w = 0; w < 8; ++w) {
+      a += sred[(w * 2) * C + c];
+      b += sred[(w * 2 + 1) * C + c];
+    }
+    partials[(int64_t)blockIdx.x * C + c] = a;
+    partials[(int64_t)(nblk + blockIdx.x) * C + c] = b;
+  }
+}
+
+// out[c] (+)= sum_r in[r*C + c]
+__global__ void colsum_f32_kernel(const float* __restrict__ in, int R, int C,
+                                  float* __restrict__ out, int accumulate) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  float s = 0.f;
+  for (int r = 0; r < R; ++r) s += in[(int64_t)r * C + c];
+  out[c] = accumulate ? out[c] + s : s;
+}
+
+// Partial column sums of bf16 in[M, C] over 256-row chunks: ws[chunk, C].
+__global__ void colsum_bf16_partial_kernel(const __nv_bfloat16* __restrict__ in, int64_t ld,
+                                           int M, int C, float* __restrict__ ws) {
+  const int c2 = blockIdx.x * blockDim.x + threadIdx.x;  // pair of columns
+  if (2 * c2 >= C) return;
+  const int r0 = blockIdx.y * 256;
+  const int r1 = min(M, r0 + 256);
+  float a = 0.f, b = 0.f;
+  for (int r = r0; r < r1; ++r) {
+    const float2 f = __bfloat1622float2(
+        *reinterpret_cast<const __nv_bfloat162*>(in + (int64_t)r * ld + 2 * c2));
+    a += f.x;
+    b += f.y;
+  }
+  ws[(int64_t)blockIdx.y * C + 2 * c2] = a;
+  ws[(int64_t)blockIdx.y * C + 2 * c2 + 1] = b;
+}
+
+// --------------------------------------------------------------- embedding ---
+__global__ void emb_fwd_kernel(const int64_t* __restrict__ idx, const __nv_bfloat16* __restrict__ wte,
+                               const __nv_bfloat16* __restrict__ wpe, float* __restrict__ x, int B,
+                               int T, int C, int pos0) {
+  const int64_t total = (int64_t)B * T * (C / 4);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / (C / 4);
+    const int c = (int)(i % (C / 4)) * 4;
+    const int t = (int)(m % T);
+    const int64_t tok = idx[m];
+    const uint2 a = *reinterpret_cast<const uint2*>(wte + tok * C + c);
+    const uint2 p = *reinterpret_cast<const uint2*>(wpe + (int64_t)(pos0 + t) * C + c);
+    const float2 a01 = unpack_bf16x2(a.x), a23 = unpack_bf16x2(a.y);
+    const float2 p01 = unpack_bf16x2(p.x), p23 = unpack_bf16x2(p.y);
+    reinterpret_cast<float4*>(x)[i] =
+        make_float4(a01.x + p01.x, a01.y + p01.y, a23.x + p23.x, a23.y + p23.y);
+  }
+}
+
+__global__ void emb_bwd_wte_kernel(const int64_t* __restrict__ idx, const float* __restrict__ dx,
+                                   float* __restrict__ wte_grad, int64_t M, int C, int V) {
+  const int64_t total = M * C;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / C;
+    const int c = (int)(i % C);
+    const int64_t tok = idx[m];
+    if (tok >= 0 && tok < V) atomicAdd(wte_grad + tok * C + c, dx[i]);
+  }
+}
+
+__global__ void emb_bwd_wpe_kernel(const float* __restrict__ dx, float* __restrict__ wpe_grad,
+                                   int B, int T, int C, int pos0) {
+  const int64_t total = (int64_t)T * C;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i / C), c = (int)(i % C);
+    float s = 0.f;
+    for (int b = 0; b < B; ++b) s += dx[((int64_t)b * T + t) * C + c];
+    wpe_grad[(int64_t)(pos0 + t) * C + c] += s;
+  }
+}
+
+// ----------------------------------------------------------- cross-entropy ---
+constexpr int CE_THREADS = 512;
+
+__global__ void __launch_bounds__(CE_THREADS) ce_kernel(__nv_bfloat16* __restrict__ logits,
+                                                        int64_t ld,
+                                                        const int64_t* __restrict__ targets,
+                                                        float* __restrict__ loss_rows, int V,
+                                                        int vocab_offset) {
+  __shared__ float red_m[CE_THREADS / 32], red_s[CE_THREADS / 32];
+  const int64_t row = blockIdx.x;
+  __nv_bfloat16* lr = logits + row * ld;
+  const int64_t tgt_raw = targets[row];
+  const bool ignore = tgt_raw == -100;
+  const int64_t tgt = tgt_raw - vocab_offset;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Pass 1: online max / sum-exp over 8-element vectors.
+  const int V8 = V / 8;
+  float m = -INFINITY, s = 0.f;
+  for (int i = threadIdx.x; i < V8; i += CE_THREADS) {
+    const uint4 w = reinterpret_cast<const uint4*>(lr)[i];
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    float f[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 p = unpack_bf16x2(ws[j]);
+      f[2 * j] = p.x;
+      f[2 * j + 1] = p.y;
+    }
+    float lm = f[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) lm = fmaxf(lm, f[j]);
+    const float nm = fmaxf(m, lm);
+    float acc = s * __expf(m - nm);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc += __expf(f[j] - nm);
+    m = nm;
+    s = acc;
+  }
+  for (int i = V8 * 8 + threadIdx.x; i < V; i += CE_THREADS) {
+    const float f = __bfloat162float(lr[i]);
+    const float nm = fmaxf(m, f);
+    s = s * __expf(m - nm) + __expf(f - nm);
+    m = nm;
+  }
+  // Block reduce (m, s).
+  float wm = warp_max(m);
+  float ws_ = (m == -INFINITY) ? 0.f : s * __expf(m - wm);
+  ws_ = warp_sum(ws_);
+  if (lane == 0) {
+    red_m[warp] = wm;
+    red_s[warp] = ws_;
+  }
+  __syncthreads();
+  float gm = -INFINITY;
+  for (int w = 0; w < CE_THREADS / 32; ++w) gm = fmaxf(gm, red_m[w]);
+  float gs = 0.f;
+  for (int w = 0; w < CE_THREADS / 32; ++w)
+    gs += red_m[w] == -INFINITY ? 0.f : red_s[w] * __expf(red_m[w] - gm);
+  const float lse = gm + __logf(gs);
+  const float inv = 1.f / gs;
+  if (threadIdx.x == 0) {
+    float l = 0.f;
+    if (!ignore && tgt >= 0 && tgt < V) l = lse - __bfloat162float(lr[tgt]);
+    loss_rows[row] = ignore ? 0.f : l;
+  }
+  __syncthreads();  // the target logit is read above before being overwritten below
+  // Pass 2: dlogits = softmax - onehot (0 for ignored rows), padded tail zeroed.
+  for (int i = threadIdx.x; i < V8; i += CE_THREADS) {
+    uint4 w = reinterpret_cast<const uint4*>(lr)[i];
+    uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 p = unpack_bf16x2(ws[j]);
+      float a = ignore ? 0.f : __expf(p.x - gm) * inv;
+      float b = ignore ? 0.f : __expf(p.y - gm) * inv;
+      const int64_t c = (int64_t)i * 8 + 2 * j;
+      if (!ignore && c == tgt) a -= 1.f;
+      if (!ignore && c + 1 == tgt) b -= 1.f;
+      ws[j] = pack_bf16x2(a, b);
+    }
+    reinterpret_cast<uint4*>(lr)[i] = make_uint4(ws[0], ws[1], ws[2], ws[3]);
+  }
+  for (int i = V8 * 8 + threadIdx.x; i < ld; i += CE_THREADS) {
+    float a = 0.f;
+    if (i < V && !ignore) {
+      a = __expf(__bfloat162float(lr[i]) - gm) * inv;
+      if (i == tgt) a -= 1.f;
+    }
+    lr[i] = __float2bfloat16(a);
+  }
+}
+
+__global__ void loss_reduce_kernel(const float* __restrict__ loss_rows,
+                                   const int64_t* __restrict__ targets, int M,
+                                   float* __restrict__ out) {
+  __shared__ float rs[32], rc[32];
+  float s = 0.f, c = 0.f;
+  for (int i = threadIdx.x; i < M; i += blockDim.x) {
+    s += loss_rows[i];
+    c += targets[i] != -100 ? 1.f : 0.f;
+  }
+  s = warp_sum(s);
+  c = warp_sum(c);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    rs[warp] = s;
+    rc[warp] = c;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float ts = 0.f, tc = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      ts += rs[w];
+      tc += rc[w];
+    }
+    tc = fmaxf(tc, 1.f);
+    out[0] = ts / tc;
+    out[1] = 1.f / tc;
+  }
+}
+
+// ------------------------------------------------------------------ AdamW ---
+// True when element e lies in one of the sorted, disjoint [lo, hi) decay
+// ranges (ranges = [lo0, hi0, lo1, hi1, ...]); a null table means e < n_decay.
+__device__ __forceinline__ bool in_decay(int64_t e, int64_t n_decay,
+                                         const int64_t* __restrict__ ranges, int nr) {
+  if (ranges == nullptr) return e < n_decay;
+  int lo = 0, hi = nr;  // find the last range with start <= e
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (__ldg(ranges + 2 * mid) <= e) lo = mid; else hi = mid;
+  }
+  return nr > 0 && e >= __ldg(ranges + 2 * lo) && e < __ldg(ranges + 2 * lo + 1);
+}
+
+__global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
+                             float* __restrict__ m, float* __restrict__ v,
+                             __nv_bfloat16* __restrict__ pb, int64_t n, int64_t n_decay,
+                             const int64_t* __restrict__ ranges, int nr,
+                             const float* __restrict__ hp, const float* __restrict__ clip) {
+  const float lr = hp[0], b1 = hp[1], b2 = hp[2], eps = hp[3], wd = hp[4];
+  const float bc1 = hp[5], bc2s = hp[6];
+  const float gs = hp[7] * (clip ? clip[0] : 1.f);
+  const float step_size = lr / bc1;
+  const int64_t n4 = n / 4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float4 pv = reinterpret_cast<float4*>(p)[i];
+    const float4 gv = reinterpret_cast<const float4*>(g)[i];
+    float4 mv = reinterpret_cast<float4*>(m)[i];
+    float4 vv = reinterpret_cast<float4*>(v)[i];
+    float* pp = &pv.x;
+    const float* gg = &gv.x;
+    float* mm = &mv.x;
+    float* vq = &vv.x;
+    // Ranges start on 4-element boundaries, so one lookup covers the vector.
+    const bool decay = in_decay(i * 4, n_decay, ranges, nr);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float gj = gg[j] * gs;
+      if (decay) pp[j] *= (1.f - lr * wd);
+      mm[j] += (gj - mm[j]) * (1.f - b1);
+      vq[j] = vq[j] * b2 + (1.f - b2) * gj * gj;
+      const float denom = sqrtf(vq[j]) / bc2s + eps;
+      pp[j] += -step_size * (mm[j] / denom);
+    }
+    reinterpret_cast<float4*>(p)[i] = pv;
+    reinterpret_cast<float4*>(m)[i] = mv;
+    reinterpret_cast<float4*>(v)[i] = vv;
+    if (pb) {
+      uint2 w;
+      w.x = pack_bf16x2(pv.x, pv.y);
+      w.y = pack_bf16x2(pv.z, pv.w);
+      reinterpret_cast<uint2*>(pb)[i] = w;
+    }
+  }
+  // tail (n not a multiple of 4)
+  if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {
+    const int64_t e = n4 * 4 + threadIdx.x;
+    const float gj = g[e] * gs;
+    float pj = p[e];
+    if (in_decay(e, n_decay, ranges, nr)) pj *= (1.f - lr * wd);
+    m[e] += (gj - m[e]) * (1.f - b1);
+    v[e] = v[e] * b2 + (1.f - b2) * gj * gj;
+    const float denom = sqrtf(v[e]) / bc2s + eps;
+    pj += -step_size * (m[e] / denom);
+    p[e] = pj;
+    if (pb) pb[e] = __float2bfloat16(pj);
+  }
+}
+
+constexpr int SUMSQ_BLOCKS = 1024;
+
+__global__ void sumsq_partial_kernel(const float* __restrict__ g, int64_t n,
+                                     float* __restrict__ ws) {
+  __shared__ float red[32];
+  float s = 0.f;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float x = g[i];
+    s += x * x;
+  }
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+    ws[blockIdx.x] = t;
+  }
+}
+
+__global__ void sum_final_kernel(const float* __restrict__ ws, int n, float* __restrict__ out) {
+  __shared__ float red[32];
+  float s = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += ws[i];
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+    out[0] = t;
+  }
+}
+
+__global__ void clip_coef_kernel(const float* __restrict__ sumsq, float scale2, float max_norm,
+                                 float* __restrict__ clip, float* __restrict__ norm_out) {
+  const float norm = sqrtf(sumsq[0] * scale2);
+  float c = max_norm / (norm + 1e-6f);
+  c = fminf(c, 1.f);
+  if (clip) clip[0] = c;
+  if (norm_out) norm_out[0] = norm;
+}
+
+__global__ void cast_f32_bf16_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out,
+                                     int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = __float2bfloat16(in[i]);
+}
+__global__ void cast_bf16_f32_kernel(const __nv_bfloat16* __restrict__ in, float* __restrict__ out,
+                                     int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = __bfloat162float(in[i]);
+}
+__global__ void scale_f32_kernel(float* __restrict__ x, int64_t n, float a) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    x[i] *= a;
+}
+
+inline int ok() { return cudaGetLastError() == cudaSuccess ? 0 : -11; }
+
+}  // namespace
+
+int layernorm_fwd_launch(const float* x, int64_t ldx, const void* gamma, const void* beta, void* y,
+                         int64_t ldy, float* mean, float* rstd, int M, int C, float eps,
+                         cudaStream_t s) {
+  if (C % 4 || C > 4 * 32 * LN_MAXV_CAP) return -1;
+  return ln_dispatch(C, [&](auto nv) {
+    ln_fwd_kernel<decltype(nv)::value><<<(M + 7) / 8, 256, 0, s>>>(
+        x, ldx, (const __nv_bfloat16*)gamma, (const __nv_bfloat16*)beta, (__nv_bfloat16*)y, ldy,
+        mean, rstd, M, C, eps);
+        count_launches(1);
+    return ok();
+  });
+}
+
+int layernorm_bwd_launch(const void* dy, const float* x, const float* mean, const float* rstd,
+                         const void* gamma, float* dres, void* dres_bf16, float* partials,
+                         int* nblk_out, int M, int C, int accumulate, cudaStream_t s) {
+  if (C % 4 || C > 4 * 32 * LN_MAXV_CAP) return -1;
+  const int nblk = (M + LNB_ROWS - 1) / LNB_ROWS;
+  const int smem = 16 * C * (int)sizeof(float);
+  if (nblk_out) *nblk_out = nblk;
+  return ln_dispatch(C, [&](auto nv) {
+    auto kern = ln_bwd_kernel<decltype(nv)::value>;
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    kern<<<nblk, 256, smem, s>>>((const __nv_bfloat16*)dy, x, mean, rstd,
+                                 (const __nv_bfloat16*)gamma, dres, (__nv_bfloat16*)dres_bf16,
+                                 partials, M, C, accumulate);
+                                 count_launches(1);
+    return ok();
+  });
+}
+
+int colsum_f32_launch(const float* in, int R, int C, float* out, int accumulate, cudaStream_t s) {
+  colsum_f32_kernel<<<(C + 255) / 256, 256, 0, s>>>(in, R, C, out, accumulate);
+  count_launches(1);
+  return ok();
+}
+
+int colsum_bf16_launch(const void* in, int64_t ld, int M, int C, float* ws, float* out,
+                       int accumulate, cudaStream_t s) {
+  if (C % 2 || ld % 2) return -1;
+  const int chunks = (M + 255) / 256;
+  dim3 grid((C / 2 + 127) / 128, chunks);
+  colsum_bf16_partial_kernel<<<grid, 128, 0, s>>>((const __nv_bfloat16*)in, ld, M, C, ws);
+  count_launches(1);
+  colsum_f32_kernel<<<(C + 255) / 256, 256, 0, s>>>(ws, chunks, C, out, accumulate);
+  count_launches(1);
+  return ok();
+}
+
+int embedding_fwd_launch(const int64_t* idx, const void* wte, const void* wpe, float* x, int B,
+                         int T, int C, int pos0, cudaStream_t s) {
+  if (C % 4) return -1;
+  emb_fwd_kernel<<<grid_for((int64_t)B * T * C / 4, 256), 256, 0, s>>>(
+      idx, (const __nv_bfloat16*)wte, (const __nv_bfloat16*)wpe, x, B, T, C, pos0);
+      count_launches(1);
+  return ok();
+}
+
+int embedding_bwd_launch(const int64_t* idx, const float* dx, float* wte_grad, float* wpe_grad,
+                         int B, int T, int C, int V, int pos0, cudaStream_t s) {
+  const int64_t M = (int64_t)B * T;
+  if (wte_grad)
+    emb_bwd_wte_kernel<<<grid_for(M * C, 256), 256, 0, s>>>(idx, dx, wte_grad, M, C, V);
+    count_launches(1);
+  if (wpe_grad)
+    emb_bwd_wpe_kernel<<<grid_for((int64_t)T * C, 256), 256, 0, s>>>(dx, wpe_grad, B, T, C, pos0);
+    count_launches(1);
+  return ok();
+}
+
+int cross_entropy_fwd_bwd_launch(void* logits, int64_t ld, const int64_t* targets,
+                                 float* loss_rows, int M, int V, int vocab_offset,
+                                 cudaStream_t s) {
+  if (ld % 8 || (reinterpret_cast<uintptr_t>(logits) & 15)) return -1;
+  ce_kernel<<<M, CE_THREADS, 0, s>>>((__nv_bfloat16*)logits, ld, targets, loss_rows, V,
+                                     vocab_offset);
+                                     count_launches(1);
+  return ok();
+}
+
+int loss_reduce_launch(const float* loss_rows, const int64_t* targets, int M, float* loss_out,
+                       cudaStream_t s) {
+  loss_reduce_kernel<<<1, 1024, 0, s>>>(loss_rows, targets, M, loss_out);
+  count_launches(1);
+  return ok();
+}
+
+int adamw_launch(float* p, const float* g, float* m, float* v, void* p_bf16, int64_t n,
+                 int64_t n_decay, const int64_t* ranges, int nr, const float* hp,
+                 const float* clip, cudaStream_t s) {
+  if ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(g) |
+       reinterpret_cast<uintptr_t>(m) | reinterpret_cast<uintptr_t>(v)) & 15)
+    return -1;
+  if (p_bf16 && (reinterpret_cast<uintptr_t>(p_bf16) & 7)) return -1;
+  adamw_kernel<<<grid_for(n / 4, 256, 148 * 8), 256, 0, s>>>(p, g, m, v, (__nv_bfloat16*)p_bf16, n,
+                                                           n_decay, ranges, nr, hp, clip);
+                                                           count_launches(1);
+  return ok();
+}
+
+int sumsq_launch(const float* g, int64_t n, float* ws, float* out, cudaStream_t s) {
+  sumsq_partial_kernel<<<SUMSQ_BLOCKS, 256, 0, s>>>(g, n, ws);
+  count_launches(1);
+  sum_final_kernel<<<1, 1024, 0, s>>>(ws, SUMSQ_BLOCKS, out);
+  count_launches(1);
+  return ok();
+}
+
+int clip_coef_launch(const float* sumsq, float scale2, float max_norm, float* clip,
+                     float* norm_out, cudaStream_t s) {
+  clip_coef_kernel<<<1, 1, 0, s>>>(sumsq, scale2, max_norm, clip, norm_out);
+  count_launches(1);
+  return ok();
+}
+
+int cast_f32_bf16_launch(const float* in, void* out, int64_t n, cudaStream_t s) {
+  cast_f32_bf16_kernel<<<grid_for(n, 256), 256, 0, s>>>(in, (__nv_bfloat16*)out, n);
+  count_launches(1);
+  return ok();
+}
+int cast_bf16_f32_launch(const void* in, float* out, int64_t n, cudaStream_t s) {
+  cast_bf16_f32_kernel<<<grid_for(n, 256), 256, 0, s>>>((const __nv_bfloat16*)in, out, n);
+  count_launches(1);
+  return ok();
+}
+int scale_f32_launch(float* x, int64_t n, float a, cudaStream_t s) {
+  scale_f32_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, n, a);
+  count_launches(1);
+  return ok();
+}
+
+}  // namespace g2b

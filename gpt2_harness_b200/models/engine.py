@@ -1,0 +1,472 @@
+"""Native GPT-2 training engine for one B200 (and, with a gradient hook, DDP).
+
+The reference trains ``GPT`` through autograd with ``torch.optim.AdamW``
+(src/transformer_internals/train.py:184-308, model.py:528-599). This engine
+runs the same mathematics as an explicit, preplanned sequence of sm_100a
+kernels with no autograd and no per-step allocation:
+
+* **Flat parameter storage.** fp32 master weights, a bf16 shadow the kernels
+  read, fp32 gradients, and AdamW moments are four flat buffers sharing one
+  layout (:class:`ParamLayout`). Every tensor starts on a 64-element (128-byte)
+  boundary so any view is a valid TMA base. The layout is ordered the way
+  backward produces gradients (ln_f, blocks L-1 .. 0, then wte/wpe), so DDP
+  buckets are contiguous ranges that complete in order.
+* **Forward.** embedding -> per block: LN1 -> c_attn GEMM (+bias) -> flash
+  attention straight on the fused qkv buffer -> c_proj GEMM whose epilogue adds
+  bias and the fp32 residual out of place -> LN2 -> c_fc GEMM with fused
+  bias+GELU (pre-activation kept) -> mlp c_proj GEMM with fused residual add ->
+  ln_f -> lm_head GEMM into a padded-vocab bf16 logits buffer -> one
+  cross-entropy kernel that writes the loss and overwrites logits with
+  dlogits = softmax - onehot.
+* **Backward.** dgrad GEMMs read weights MN-major (no transposes), the
+  mlp dgrad fuses GELU backward, wgrad GEMMs read activations MN-major and
+  split K over tokens with a deterministic reduction, LayerNorm backward adds
+  into the fp32 residual gradient and emits its bf16 copy, bias gradients are
+  deterministic column sums, the 1/N_tokens loss scale enters the lm_head
+  GEMMs through a device scalar.
+* **Optimiser.** global grad-norm, clip coefficient and AdamW (torch
+  single-tensor order, decay on rank>=2 tensors) as two reductions plus one
+  fused kernel that also refreshes the bf16 shadow.
+
+Residual-stream and gradient precision follow bf16 autocast with fp32 master
+weights: matmul inputs bf16, accumulation and the residual stream fp32.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Callable, Optional
+
+import torch
+
+from gpt2_harness_b200.config import GPTConfig
+from gpt2_harness_b200.ops import native as N
+
+__all__ = ["ParamSpec", "ParamLayout", "Engine", "OptimConfig", "choose_splits"]
+
+ALIGN = 64  # elements; 128 bytes of bf16, 256 bytes of fp32
+
+
+@dataclass
+class ParamSpec:
+    name: str
+    shape: tuple
+    offset: int
+    decay: bool
+    group: str  # "root" or "h.<i>"
+
+    @property
+    def numel(self) -> int:
+        n = 1
+        for s in self.shape:
+            n *= s
+        return n
+
+
+class ParamLayout:
+    """Flat, aligned layout of every GPT-2 parameter (tied weights once).
+
+    Order: ln_f, h.{L-1}, ..., h.0, wte, wpe -- the order in which backward
+    finishes each tensor's gradient.
+    """
+
+    def __init__(self, config: GPTConfig, align: int = ALIGN) -> None:
+        if not config.tie_weights:
+            raise ValueError("the native engine implements GPT-2's tied lm_head")
+        if config.pos_embedding != "learned" or config.norm_position != "pre":
+            raise ValueError("the native engine implements pre-LN GPT-2 with learned positions")
+        if config.activation != "gelu_tanh" or config.head_dim != 64 or config.kv_heads != config.n_head:
+            raise ValueError("the native engine implements gelu_tanh, head_dim 64, MHA")
+        if not (config.attn_bias and config.mlp_bias):
+            raise ValueError("the native engine expects biased projections")
+        self.config = config
+        C, L = config.n_embd, config.n_layer
+        specs: list[tuple[str, tuple, bool, str]] = [
+            ("ln_f.weight", (C,), False, "root"),
+            ("ln_f.bias", (C,), False, "root"),
+        ]
+        for i in reversed(range(L)):
+            p = f"h.{i}."
+            g = f"h.{i}"
+            specs += [
+                (p + "ln_1.weight", (C,), False, g),
+                (p + "ln_1.bias", (C,), False, g),
+                (p + "attn.c_attn.weight", (3 * C, C), True, g),
+                (p + "attn.c_attn.bias", (3 * C,), False, g),
+                (p + "attn.c_proj.weight", (C, C), True, g),
+                (p + "attn.c_proj.bias", (C,), False, g),
+                (p + "ln_2.weight", (C,), False, g),
+                (p + "ln_2.bias", (C,), False, g),
+                (p + "mlp.c_fc.weight", (4 * C, C), True, g),
+                (p + "mlp.c_fc.bias", (4 * C,), False, g),
+                (p + "mlp.c_proj.weight", (C, 4 * C), True, g),
+                (p + "mlp.c_proj.bias", (C,), False, g),
+            ]
+        specs += [
+            ("wte.weight", (config.vocab_size, C), True, "root"),
+            ("wpe.weight", (config.n_positions, C), True, "root"),
+        ]
+        self.specs: list[ParamSpec] = []
+        off = 0
+        for name, shape, decay, group in specs:
+            self.specs.append(ParamSpec(name, shape, off, decay, group))
+            n = 1
+            for s in shape:
+                n *= s
+            off += (n + align - 1) // align * align
+        self.total = off
+        self.by_name = {s.name: s for s in self.specs}
+
+    @property
+    def num_parameters(self) -> int:
+        return sum(s.numel for s in self.specs)
+
+    def view(self, flat: torch.Tensor, name: str) -> torch.Tensor:
+        s = self.by_name[name]
+        return flat[s.offset : s.offset + s.numel].view(s.shape)
+
+    def group_range(self, group: str) -> tuple[int, int]:
+        specs = [s for s in self.specs if s.group == group]
+        lo = specs[0].offset
+        last = specs[-1]
+        hi = last.offset + (last.numel + ALIGN - 1) // ALIGN * ALIGN
+        return lo, hi
+
+    def decay_segments(self) -> list[tuple[int, int, bool]]:
+        return [(s.offset, s.numel, s.decay) for s in self.specs]
+
+
+def choose_splits(m: int, n: int, k: int, bm: int = 128, bn: int = 256, sms: int = 148,
+                  max_splits: int = 16, min_k: int = 1024) -> int:
+    """Split-K factor for a wgrad GEMM: best wave efficiency, fewest splits."""
+    tiles = -(-m // bm) * -(-n // bn)
+    best, best_score = 1, -1.0
+    for s in range(1, max_splits + 1):
+        if s > 1 and k // s < min_k:
+            break
+        t = tiles * s
+        eff = t / (-(-t // sms) * sms)
+        score = eff - 0.015 * (s - 1)
+        if score > best_score + 1e-9:
+            best, best_score = s, score
+    return best
+
+
+@dataclass
+class OptimConfig:
+    lr: float = 3e-4
+    betas: tuple = (0.9, 0.95)
+    eps: float = 1e-8
+    weight_decay: float = 0.1
+    grad_clip: float = 1.0  # <= 0 disables clipping
+
+
+class _Acts:
+    """Activation and workspace buffers for one (B, T) shape."""
+
+    def __init__(self, cfg: GPTConfig, B: int, T: int, dev: torch.device) -> None:
+        C, L, H = cfg.n_embd, cfg.n_layer, cfg.n_head
+        M = B * T
+        self.B, self.T, self.M = B, T, M
+        bf, f32 = torch.bfloat16, torch.float32
+        self.x = [torch.empty(M, C, dtype=f32, device=dev) for _ in range(2 * L + 1)]
+        self.h1 = [torch.empty(M, C, dtype=bf, device=dev) for _ in range(L)]
+        self.qkv = [torch.empty(M, 3 * C, dtype=bf, device=dev) for _ in range(L)]
+        self.y = [torch.empty(M, C, dtype=bf, device=dev) for _ in range(L)]
+        self.lse = [torch.empty(B, H, T, dtype=f32, device=dev) for _ in range(L)]
+        self.h2 = [torch.empty(M, C, dtype=bf, device=dev) for _ in range(L)]
+        self.u = [torch.empty(M, 4 * C, dtype=bf, device=dev) for _ in range(L)]
+        self.g = [torch.empty(M, 4 * C, dtype=bf, device=dev) for _ in range(L)]
+        self.mu = [torch.empty(M, dtype=f32, device=dev) for _ in range(2 * L + 1)]
+        self.rs = [torch.empty(M, dtype=f32, device=dev) for _ in range(2 * L + 1)]
+        self.hf = torch.empty(M, C, dtype=bf, device=dev)
+        vp = cfg.padded_vocab_size()
+        self.logits = torch.empty(M, vp, dtype=bf, device=dev)
+        self.loss_rows = torch.empty(M, dtype=f32, device=dev)
+        self.loss_out = torch.zeros(2, dtype=f32, device=dev)
+        # backward scratch (reused across layers)
+        self.dres = torch.empty(M, C, dtype=f32, device=dev)
+        self.dres16 = torch.empty(M, C, dtype=bf, device=dev)
+        self.dh = torch.empty(M, C, dtype=bf, device=dev)
+        self.dy = torch.empty(M, C, dtype=bf, device=dev)
+        self.du = torch.empty(M, 4 * C, dtype=bf, device=dev)
+        self.dqkv = torch.empty(M, 3 * C, dtype=bf, device=dev)
+        self.delta = torch.empty(B, H, T, dtype=f32, device=dev)
+        self.ln_parts = N.layernorm_bwd_partials(M, C, dev)
+        self.col_ws = torch.empty(N.colsum_ws_numel(M, 4 * C), dtype=f32, device=dev)
+        # split-K plans for the four wgrad shapes
+        self.splits = {
+            "c_attn": choose_splits(3 * C, C, M),
+            "c_proj": choose_splits(C, C, M),
+            "c_fc": choose_splits(4 * C, C, M),
+            "mlp_proj": choose_splits(C, 4 * C, M),
+        }
+        ws = max(self.splits["c_attn"] * 3 * C * C, self.splits["c_proj"] * C * C,
+                 self.splits["c_fc"] * 4 * C * C, self.splits["mlp_proj"] * 4 * C * C)
+        self.splitk_ws = torch.empty(ws, dtype=f32, device=dev)
+
+
+class Engine:
+    """GPT-2 training engine on native kernels.
+
+    Args:
+        config: model architecture (pre-LN GPT-2 with tied embeddings).
+        device: CUDA device.
+        optim: AdamW / clipping settings.
+        grad_buffer: optional externally owned fp32 flat gradient buffer of
+            ``layout.total`` elements (DDP passes its peer-mapped buffer).
+        seed: init seed for :meth:`init_weights` (ignored if weights loaded).
+    """
+
+    def __init__(self, config: GPTConfig, device: torch.device | str = "cuda", *,
+                 optim: Optional[OptimConfig] = None, grad_buffer: Optional[torch.Tensor] = None,
+                 seed: Optional[int] = 0) -> None:
+        self.config = config
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("the native engine runs on CUDA devices")
+        N.lib()  # fail loudly if the extension is missing
+        self.layout = ParamLayout(config)
+        self.optim = optim or OptimConfig()
+        n = self.layout.total
+        dev = self.device
+        self.master = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.shadow = torch.zeros(n, dtype=torch.bfloat16, device=dev)
+        if grad_buffer is not None:
+            if grad_buffer.numel() < n or grad_buffer.dtype != torch.float32:
+                raise ValueError("grad_buffer too small or not fp32")
+            self.grad = grad_buffer[:n]
+        else:
+            self.grad = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.exp_avg = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.exp_avg_sq = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.step_count = 0
+        self._acts: Optional[_Acts] = None
+        self._hp_host = torch.zeros(8, dtype=torch.float32).pin_memory()
+        self.hp = torch.zeros(8, dtype=torch.float32, device=dev)
+        self._norm_ws = torch.empty(1024, dtype=torch.float32, device=dev)
+        self.sumsq = torch.zeros(1, dtype=torch.float32, device=dev)
+        self.clip = torch.ones(1, dtype=torch.float32, device=dev)
+        self.grad_norm = torch.zeros(1, dtype=torch.float32, device=dev)
+        # Hook called after each block's gradients are final (DDP buckets);
+        # signature: hook(group_name) with group in {"root_head", "h.i", "root_tail"}.
+        self.grad_ready_hook: Optional[Callable[[str], None]] = None
+        self.grad_scale = 1.0  # multiplies gradients inside AdamW
+        # Decayed tensors (rank >= 2) are not contiguous in backward order: the
+        # fused AdamW reads this table of [lo, hi) decay ranges.
+        ranges = [x for lo, hi, d in self._merge_segments() if d for x in (lo, hi)]
+        self.decay_ranges = torch.tensor(ranges, dtype=torch.int64, device=dev)
+        if seed is not None:
+            self.init_weights(seed)
+
+    # ------------------------------------------------------------ weights --
+    def _merge_segments(self):
+        segs = []
+        for s in self.layout.specs:
+            lo = s.offset
+            hi = s.offset + (s.numel + ALIGN - 1) // ALIGN * ALIGN
+            if segs and segs[-1][2] == s.decay and segs[-1][1] == lo:
+                segs[-1] = (segs[-1][0], hi, s.decay)
+            else:
+                segs.append((lo, hi, s.decay))
+        return segs
+
+    def p32(self, name: str) -> torch.Tensor:
+        return self.layout.view(self.master, name)
+
+    def p16(self, name: str) -> torch.Tensor:
+        return self.layout.view(self.shadow, name)
+
+    def g32(self, name: str) -> torch.Tensor:
+        return self.layout.view(self.grad, name)
+
+    @torch.no_grad()
+    def init_weights(self, seed: int = 0) -> None:
+        """GPT-2 init on the device: N(0, 0.02) for matmul weights and
+        embeddings, N(0, 0.02/sqrt(2L)) for the two residual projections,
+        zero biases, unit LayerNorm gains (reference model.py:488-518)."""
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed)
+        self.master.zero_()
+        res_std = 0.02 / math.sqrt(2 * self.config.n_layer)
+        for s in self.layout.specs:
+            v = self.p32(s.name)
+            if s.name.endswith(("ln_1.weight", "ln_2.weight", "ln_f.weight")):
+                v.fill_(1.0)
+            elif s.name.endswith("bias"):
+                v.zero_()
+            elif s.name.endswith(("attn.c_proj.weight", "mlp.c_proj.weight")):
+                v.normal_(0.0, res_std, generator=g)
+            else:
+                v.normal_(0.0, 0.02, generator=g)
+        self.sync_shadow()
+
+    @torch.no_grad()
+    def sync_shadow(self) -> None:
+        self.shadow.copy_(self.master)
+
+    @torch.no_grad()
+    def load_state_dict(self, sd: dict) -> None:
+        """Load a reference-named state dict (GPT.state_dict())."""
+        for s in self.layout.specs:
+            src = sd[s.name] if s.name in sd else sd.get("lm_head.weight") if s.name == "wte.weight" else None
+            if src is None:
+                raise KeyError(s.name)
+            self.p32(s.name).copy_(src.to(self.device, torch.float32).view(s.shape))
+        self.sync_shadow()
+
+    def state_dict(self) -> dict:
+        """Reference-named fp32 state dict (``lm_head.weight`` tied to wte)."""
+        out = {s.name: self.p32(s.name).detach().clone() for s in self.layout.specs}
+        out["lm_head.weight"] = out["wte.weight"]
+        return out
+
+    @classmethod
+    def from_module(cls, model, device="cuda", **kw) -> "Engine":
+        eng = cls(model.config, device, seed=None, **kw)
+        eng.load_state_dict(model.state_dict())
+        return eng
+
+    # --------------------------------------------------------- activations --
+    def acts(self, B: int, T: int) -> _Acts:
+        if self._acts is None or (self._acts.B, self._acts.T) != (B, T):
+            self._acts = None
+            torch.cuda.empty_cache()
+            self._acts = _Acts(self.config, B, T, self.device)
+        return self._acts
+
+    # ------------------------------------------------------------- forward --
+    def forward(self, idx: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        """Forward pass; returns the device scalar loss (loss_out[0]).
+        Also leaves dlogits in the logits buffer for :meth:`backward`."""
+        cfg = self.config
+        B, T = idx.shape
+        if T > cfg.n_positions:
+            raise ValueError(f"sequence of length {T} exceeds n_positions={cfg.n_positions}")
+        A = self.acts(B, T)
+        C, H, L, V = cfg.n_embd, cfg.n_head, cfg.n_layer, cfg.vocab_size
+        eps = cfg.layer_norm_epsilon
+        p = self.p16
+        N.embedding_fwd(idx, p("wte.weight"), p("wpe.weight"), A.x[0])
+        for l in range(L):
+            pre = f"h.{l}."
+            N.layernorm_fwd(A.x[2 * l], p(pre + "ln_1.weight"), p(pre + "ln_1.bias"), A.h1[l],
+                            A.mu[2 * l], A.rs[2 * l], eps)
+            N.gemm(A.h1[l], p(pre + "attn.c_attn.weight"), A.qkv[l], bias=p(pre + "attn.c_attn.bias"))
+            qkv = A.qkv[l]
+            N.attention_fwd(qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:], A.y[l], A.lse[l], B, H, T)
+            N.gemm(A.y[l], p(pre + "attn.c_proj.weight"), A.x[2 * l + 1], epilogue=N.EPI_RESID_F32,
+                   bias=p(pre + "attn.c_proj.bias"), aux=A.x[2 * l])
+            N.layernorm_fwd(A.x[2 * l + 1], p(pre + "ln_2.weight"), p(pre + "ln_2.bias"), A.h2[l],
+                            A.mu[2 * l + 1], A.rs[2 * l + 1], eps)
+            N.gemm(A.h2[l], p(pre + "mlp.c_fc.weight"), A.g[l], epilogue=N.EPI_BIAS_GELU,
+                   bias=p(pre + "mlp.c_fc.bias"), aux=A.u[l])
+            N.gemm(A.g[l], p(pre + "mlp.c_proj.weight"), A.x[2 * l + 2], epilogue=N.EPI_RESID_F32,
+                   bias=p(pre + "mlp.c_proj.bias"), aux=A.x[2 * l + 1])
+        N.layernorm_fwd(A.x[2 * L], p("ln_f.weight"), p("ln_f.bias"), A.hf, A.mu[2 * L], A.rs[2 * L], eps)
+        N.gemm(A.hf, p("wte.weight"), A.logits[:, :V])
+        N.cross_entropy_fwd_bwd(A.logits, targets.view(-1), A.loss_rows, A.loss_out, V)
+        return A.loss_out[0]
+
+    # ------------------------------------------------------------ backward --
+    def backward(self, idx: torch.Tensor, accumulate: bool = False) -> None:
+        """Backward of the last :meth:`forward`; gradients land in ``self.grad``
+        (added to it when ``accumulate``)."""
+        cfg = self.config
+        A = self._acts
+        B, T, M = A.B, A.T, A.M
+        C, H, L, V = cfg.n_embd, cfg.n_head, cfg.n_layer, cfg.vocab_size
+        p, g = self.p16, self.g32
+        acc = bool(accumulate)
+        inv_count = A.loss_out[1:2]
+        hook = self.grad_ready_hook
+        logits = A.logits[:, :V]
+        # lm_head (tied): dhf = dlogits @ wte / count ; dwte = dlogits^T @ hf / count
+        N.gemm(logits, p("wte.weight"), A.dh, b_t=True, alpha_ptr=inv_count)
+        N.gemm(logits, A.hf, g("wte.weight"), a_t=True, b_t=True, epilogue=N.EPI_F32,
+               alpha_ptr=inv_count, accumulate=acc)
+        N.layernorm_bwd(A.dh, A.x[2 * L], A.mu[2 * L], A.rs[2 * L], p("ln_f.weight"), A.dres,
+                        A.dres16, g("ln_f.weight"), g("ln_f.bias"), A.ln_parts,
+                        accumulate_dres=False, accumulate_params=acc)
+        if hook:
+            hook("root_head")
+        ws = A.splitk_ws
+        for l in reversed(range(L)):
+            pre = f"h.{l}."
+            # mlp.c_proj
+            N.gemm(A.dres16, p(pre + "mlp.c_proj.weight"), A.du, b_t=True, epilogue=N.EPI_GELU_BWD,
+                   aux=A.u[l])
+            N.gemm(A.dres16, A.g[l], g(pre + "mlp.c_proj.weight"), a_t=True, b_t=True,
+                   epilogue=N.EPI_F32, accumulate=acc, splits=A.splits["mlp_proj"], workspace=ws)
+            N.colsum_bf16(A.dres16, g(pre + "mlp.c_proj.bias"), A.col_ws, accumulate=acc)
+            # mlp.c_fc
+            N.gemm(A.du, p(pre + "mlp.c_fc.weight"), A.dh, b_t=True)
+            N.gemm(A.du, A.h2[l], g(pre + "mlp.c_fc.weight"), a_t=True, b_t=True,
+                   epilogue=N.EPI_F32, accumulate=acc, splits=A.splits["c_fc"], workspace=ws)
+            N.colsum_bf16(A.du, g(pre + "mlp.c_fc.bias"), A.col_ws, accumulate=acc)
+            N.layernorm_bwd(A.dh, A.x[2 * l + 1], A.mu[2 * l + 1], A.rs[2 * l + 1],
+                            p(pre + "ln_2.weight"), A.dres, A.dres16, g(pre + "ln_2.weight"),
+                            g(pre + "ln_2.bias"), A.ln_parts, accumulate_dres=True,
+                            accumulate_params=acc)
+            # attn.c_proj
+            N.gemm(A.dres16, p(pre + "attn.c_proj.weight"), A.dy, b_t=True)
+            N.gemm(A.dres16, A.y[l], g(pre + "attn.c_proj.weight"), a_t=True, b_t=True,
+                   epilogue=N.EPI_F32, accumulate=acc, splits=A.splits["c_proj"], workspace=ws)
+            N.colsum_bf16(A.dres16, g(pre + "attn.c_proj.bias"), A.col_ws, accumulate=acc)
+            # attention
+            qkv, dqkv = A.qkv[l], A.dqkv
+            N.attention_bwd(qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:], A.y[l], A.dy,
+                            dqkv[:, :C], dqkv[:, C:2 * C], dqkv[:, 2 * C:], A.lse[l], A.delta, B, H, T)
+            # attn.c_attn
+            N.gemm(dqkv, p(pre + "attn.c_attn.weight"), A.dh, b_t=True)
+            N.gemm(dqkv, A.h1[l], g(pre + "attn.c_attn.weight"), a_t=True, b_t=True,
+                   epilogue=N.EPI_F32, accumulate=acc, splits=A.splits["c_attn"], workspace=ws)
+            N.colsum_bf16(dqkv, g(pre + "attn.c_attn.bias"), A.col_ws, accumulate=acc)
+            N.layernorm_bwd(A.dh, A.x[2 * l], A.mu[2 * l], A.rs[2 * l], p(pre + "ln_1.weight"),
+                            A.dres, A.dres16, g(pre + "ln_1.weight"), g(pre + "ln_1.bias"),
+                            A.ln_parts, accumulate_dres=True, accumulate_params=acc)
+            if hook:
+                hook(f"h.{l}")
+        wpe_g = g("wpe.weight")
+        if not acc:
+            wpe_g.zero_()
+        N.embedding_bwd(idx, A.dres, g("wte.weight"), wpe_g, V)
+        if hook:
+            hook("root_tail")
+
+    # ----------------------------------------------------------- optimiser --
+    def set_lr(self, lr: float) -> None:
+        self.optim.lr = lr
+
+    def optimizer_step(self) -> None:
+        """Clip (global norm) + AdamW over the whole flat buffer."""
+        o = self.optim
+        self.step_count += 1
+        t = self.step_count
+        hp = self._hp_host
+        hp[0] = o.lr
+        hp[1] = o.betas[0]
+        hp[2] = o.betas[1]
+        hp[3] = o.eps
+        hp[4] = o.weight_decay
+        hp[5] = 1.0 - o.betas[0] ** t
+        hp[6] = math.sqrt(1.0 - o.betas[1] ** t)
+        hp[7] = self.grad_scale
+        self.hp.copy_(hp, non_blocking=True)
+        clip = None
+        if o.grad_clip and o.grad_clip > 0:
+            N.grad_sumsq(self.grad, self._norm_ws, self.sumsq)
+            N.clip_coef(self.sumsq, o.grad_clip, self.clip, self.grad_norm,
+                        scale2=self.grad_scale * self.grad_scale)
+            clip = self.clip
+        N.adamw_step(self.master, self.grad, self.exp_avg, self.exp_avg_sq, self.shadow, 0,
+                     self.hp, clip, decay_ranges=self.decay_ranges)
+
+    # ---------------------------------------------------------------- step --
+    def train_step(self, idx: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        """One optimiser step on one micro-batch; returns the device loss."""
+        loss = self.forward(idx, targets)
+        self.backward(idx)
+        self.optimizer_step()
+        return loss

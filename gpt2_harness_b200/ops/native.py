@@ -1,0 +1,348 @@
+"""Loader and thin, validated Python wrappers over the sm_100a native library.
+
+The shared object ``gpt2_harness_b200/_C*.so`` is built in-tree by
+``python setup.py build_ext --inplace`` (or ``__graft_entry__.build()``). On a
+machine with a CUDA device the library MUST load: :func:`lib` raises instead of
+silently falling back to PyTorch, so a test that passes has run our kernels.
+
+Every wrapper checks shapes, dtypes, contiguity and alignment on the host and
+then passes raw device addresses plus the current CUDA stream to the launcher,
+so the launch itself is one pybind call and is capturable in a CUDA graph.
+"""
+
+from __future__ import annotations
+
+import importlib
+import math
+from typing import Optional
+
+import torch
+
+__all__ = [
+    "lib",
+    "available",
+    "error_word",
+    "check_errors",
+    "EPI_BF16",
+    "EPI_BIAS_GELU",
+    "EPI_RESID_F32",
+    "EPI_F32",
+    "EPI_GELU_BWD",
+    "gemm",
+    "linear_fwd",
+    "attention_fwd",
+    "attention_bwd",
+    "layernorm_fwd",
+    "layernorm_bwd",
+    "colsum_bf16",
+    "embedding_fwd",
+    "embedding_bwd",
+    "cross_entropy_fwd_bwd",
+    "adamw_step",
+]
+
+EPI_BF16, EPI_BIAS_GELU, EPI_RESID_F32, EPI_F32, EPI_GELU_BWD = 0, 1, 2, 3, 4
+
+_LIB = None
+_LOAD_ERROR: Optional[BaseException] = None
+_ERR_WORDS: dict[int, torch.Tensor] = {}
+
+ERROR_NAMES = {
+    1 << 0: "GEMM producer wait timed out",
+    1 << 1: "GEMM MMA wait timed out",
+    1 << 2: "GEMM epilogue wait timed out",
+    1 << 3: "peer flag wait timed out",
+    1 << 4: "bad shape",
+    1 << 5: "attention pipeline wait timed out",
+}
+
+
+def lib():
+    """The native module. Raises ImportError with the build hint if absent."""
+    global _LIB, _LOAD_ERROR
+    if _LIB is None:
+        try:
+            _LIB = importlib.import_module("gpt2_harness_b200._C")
+        except BaseException as exc:  # pragma: no cover - depends on the build
+            _LOAD_ERROR = exc
+            raise ImportError(
+                "gpt2_harness_b200._C is not built; run `python setup.py build_ext --inplace` "
+                f"(original error: {exc!r})"
+            ) from exc
+    return _LIB
+
+
+def available() -> bool:
+    """True when the native library imports and a CUDA device is present."""
+    if not torch.cuda.is_available():
+        return False
+    try:
+        lib()
+    except ImportError:
+        return False
+    return True
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def error_word(device: Optional[torch.device] = None) -> torch.Tensor:
+    """Per-device uint32 word the kernels OR their error codes into."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    if key not in _ERR_WORDS:
+        _ERR_WORDS[key] = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", key))
+    return _ERR_WORDS[key]
+
+
+def _err_ptr() -> int:
+    return error_word().data_ptr()
+
+
+def check_errors(device: Optional[torch.device] = None, reset: bool = True) -> None:
+    """Raise RuntimeError if any kernel on `device` recorded an error (syncs)."""
+    w = error_word(device)
+    val = int(w.item())
+    if val:
+        if reset:
+            w.zero_()
+        names = [n for bit, n in ERROR_NAMES.items() if val & bit]
+        raise RuntimeError(f"native kernel error 0x{val:x}: {', '.join(names) or 'unknown'}")
+
+
+def _ptr(t: Optional[torch.Tensor]) -> int:
+    return 0 if t is None else t.data_ptr()
+
+
+def _row_stride(t: torch.Tensor) -> int:
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"expected a 2-D row-major view, got shape {tuple(t.shape)} strides {t.stride()}")
+    return t.stride(0)
+
+
+def _check_cuda(*ts: Optional[torch.Tensor]) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("native ops need CUDA tensors")
+
+
+# ---------------------------------------------------------------------- GEMM --
+def gemm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    out: torch.Tensor,
+    *,
+    a_t: bool = False,
+    b_t: bool = False,
+    epilogue: int = EPI_BF16,
+    bias: Optional[torch.Tensor] = None,
+    aux: Optional[torch.Tensor] = None,
+    alpha: float = 1.0,
+    alpha_ptr: Optional[torch.Tensor] = None,
+    accumulate: bool = False,
+    splits: int = 1,
+    workspace: Optional[torch.Tensor] = None,
+    bn: int = 256,
+    max_ctas: int = 0,
+) -> torch.Tensor:
+    """out[M,N] (epilogue) = op(a) @ op(b)^T on the tcgen05 tensor cores.
+
+    ``a`` is [M, K] (or [K, M] with ``a_t``), ``b`` is [N, K] (or [K, N] with
+    ``b_t``), both bf16 row-major views. ``a_t``/``b_t`` select the MN-major
+    operand layout in the kernel: no transpose is ever materialised.
+    """
+    _check_cuda(a, b, out, bias, aux, alpha_ptr, workspace)
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise TypeError("gemm operands must be bf16")
+    M, K = (a.shape[1], a.shape[0]) if a_t else (a.shape[0], a.shape[1])
+    if b_t:
+        N, Kb = b.shape[1], b.shape[0]
+    else:
+        N, Kb = b.shape[0], b.shape[1]
+    if K != Kb:
+        raise ValueError(f"inner dimensions differ: {K} vs {Kb}")
+    if out.shape[0] != M or out.shape[1] < N:
+        raise ValueError(f"out shape {tuple(out.shape)} cannot hold [{M}, {N}]")
+    want = torch.float32 if epilogue in (EPI_RESID_F32, EPI_F32) else torch.bfloat16
+    if out.dtype != want:
+        raise TypeError(f"epilogue {epilogue} writes {want}, out is {out.dtype}")
+    if bias is not None and (bias.dtype != torch.bfloat16 or bias.numel() < N):
+        raise TypeError("bias must be bf16 with at least N elements")
+    if epilogue in (EPI_BIAS_GELU, EPI_GELU_BWD) and (aux is None or aux.dtype != torch.bfloat16):
+        raise TypeError("this epilogue needs a bf16 aux tensor")
+    if epilogue == EPI_RESID_F32 and aux is not None and aux.dtype != torch.float32:
+        raise TypeError("the residual epilogue's source (aux) must be fp32")
+    if splits > 1:
+        if epilogue != EPI_F32:
+            raise ValueError("split-K needs the fp32 epilogue")
+        if workspace is None or workspace.numel() < splits * M * N:
+            raise ValueError("split-K workspace too small")
+    lib().gemm(
+        a.data_ptr(), _row_stride(a), int(a_t), b.data_ptr(), _row_stride(b), int(b_t),
+        M, N, K, epilogue, out.data_ptr(), _row_stride(out), _ptr(aux),
+        0 if aux is None else _row_stride(aux), _ptr(bias), float(alpha), _ptr(alpha_ptr),
+        int(accumulate), int(splits), _ptr(workspace), int(bn), int(max_ctas), _err_ptr(), _stream(),
+    )
+    return out
+
+
+def linear_fwd(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = x @ w^T + bias with bf16 I/O (nn.Linear layout: w is [out, in])."""
+    y = torch.empty(x.shape[0], w.shape[0], dtype=torch.bfloat16, device=x.device)
+    return gemm(x, w, y, bias=bias)
+
+
+# ----------------------------------------------------------------- attention --
+def _head_strides(t: torch.Tensor, T: int, H: int):
+    # t is [B*T, >=H*64] row-major; element (b,h,t,d) at b*T*ld + t*ld + h*64 + d
+    ld = _row_stride(t)
+    return T * ld, ld, 64
+
+
+def attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor,
+                  lse: torch.Tensor, B: int, H: int, Tq: int, Tk: Optional[int] = None,
+                  q_offset: int = 0, causal: bool = True, scale: Optional[float] = None) -> None:
+    """Causal flash attention on head_dim 64.
+
+    q, o: [B*Tq, ...] row-major views whose columns h*64..h*64+63 hold head h
+    (e.g. the q section of the fused qkv buffer); k, v: [B*Tk, ...] likewise.
+    lse: fp32 [B, H, Tq] (log2-domain log-sum-exp, saved for backward).
+    """
+    Tk = Tq if Tk is None else Tk
+    scale = 1.0 / math.sqrt(64) if scale is None else scale
+    qsb, qst, qsh = _head_strides(q, Tq, H)
+    ksb, kst, ksh = _head_strides(k, Tk, H)
+    if _head_strides(v, Tk, H) != (ksb, kst, ksh):
+        raise ValueError("k and v must share strides")
+    osb, ost, osh = _head_strides(o, Tq, H)
+    lib().attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), qsb, qst, qsh,
+                   osb, ost, osh, lse.data_ptr(), B, H, Tq, Tk, q_offset, int(causal),
+                   float(scale), ksb, kst, ksh, _err_ptr(), _stream())
+
+
+def attention_bwd(q, k, v, o, dout, dq, dk, dv, lse, delta, B: int, H: int, Tq: int,
+                  Tk: Optional[int] = None, q_offset: int = 0, causal: bool = True,
+                  scale: Optional[float] = None) -> None:
+    """Deterministic flash-attention backward (dK/dV pass, then dQ pass).
+
+    dout shares o's strides; dq shares q's layout family; dk/dv share a layout.
+    delta: fp32 scratch [B, H, Tq].
+    """
+    Tk = Tq if Tk is None else Tk
+    scale = 1.0 / math.sqrt(64) if scale is None else scale
+    qsb, qst, qsh = _head_strides(q, Tq, H)
+    ksb, kst, ksh = _head_strides(k, Tk, H)
+    osb, ost, osh = _head_strides(o, Tq, H)
+    if _head_strides(dout, Tq, H) != (osb, ost, osh):
+        raise ValueError("dout must share o's strides")
+    dsb, dst, dsh = _head_strides(dq, Tq, H)
+    dksb, dkst, dksh = _head_strides(dk, Tk, H)
+    if _head_strides(dv, Tk, H) != (dksb, dkst, dksh):
+        raise ValueError("dk and dv must share strides")
+    lib().attn_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dout.data_ptr(),
+                   dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), qsb, qst, qsh, osb, ost, osh,
+                   dsb, dst, dsh, lse.data_ptr(), delta.data_ptr(), B, H, Tq, Tk, q_offset,
+                   int(causal), float(scale), ksb, kst, ksh, dksb, dkst, dksh, _err_ptr(),
+                   _stream())
+
+
+# ----------------------------------------------------------------- layernorm --
+def layernorm_fwd(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, y: torch.Tensor,
+                  mean: torch.Tensor, rstd: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    """y(bf16) = LN(x fp32) * gamma + beta over the last dim; saves mean/rstd."""
+    M, C = x.shape
+    lib().layernorm_fwd(x.data_ptr(), _row_stride(x), gamma.data_ptr(), beta.data_ptr(),
+                        y.data_ptr(), _row_stride(y), mean.data_ptr(), rstd.data_ptr(), M, C,
+                        float(eps), _stream())
+    return y
+
+
+def layernorm_bwd_partials(M: int, C: int, device) -> torch.Tensor:
+    nblk = lib().layernorm_bwd_blocks(M)
+    return torch.empty(2, nblk, C, dtype=torch.float32, device=device)
+
+
+def layernorm_bwd(dy: torch.Tensor, x: torch.Tensor, mean: torch.Tensor, rstd: torch.Tensor,
+                  gamma: torch.Tensor, dres: torch.Tensor, dres_bf16: Optional[torch.Tensor],
+                  dgamma: torch.Tensor, dbeta: torch.Tensor, partials: torch.Tensor,
+                  accumulate_dres: bool, accumulate_params: bool = True) -> None:
+    """LN backward: dres (+)= dx (fp32, plus optional bf16 copy); dgamma/dbeta (+)=."""
+    M, C = x.shape
+    L = lib()
+    nblk = L.layernorm_bwd(dy.data_ptr(), x.data_ptr(), mean.data_ptr(), rstd.data_ptr(),
+                           gamma.data_ptr(), dres.data_ptr(), _ptr(dres_bf16),
+                           partials.data_ptr(), M, C, int(accumulate_dres), _stream())
+    L.colsum_f32(partials.data_ptr(), nblk, C, dgamma.data_ptr(), int(accumulate_params), _stream())
+    L.colsum_f32(partials.data_ptr() + nblk * C * 4, nblk, C, dbeta.data_ptr(),
+                 int(accumulate_params), _stream())
+
+
+def colsum_bf16(x: torch.Tensor, out: torch.Tensor, ws: torch.Tensor, accumulate: bool = True) -> None:
+    """out(fp32) (+)= x.sum(0) for a bf16 [M, C] view (bias gradients)."""
+    M, C = x.shape
+    lib().colsum_bf16(x.data_ptr(), _row_stride(x), M, C, ws.data_ptr(), out.data_ptr(),
+                      int(accumulate), _stream())
+
+
+def colsum_ws_numel(M: int, C: int) -> int:
+    return ((M + 255) // 256) * C
+
+
+# ----------------------------------------------------------------- embedding --
+def embedding_fwd(idx: torch.Tensor, wte: torch.Tensor, wpe: torch.Tensor, x: torch.Tensor,
+                  pos0: int = 0) -> torch.Tensor:
+    B, T = idx.shape
+    C = wte.shape[1]
+    lib().embedding_fwd(idx.data_ptr(), wte.data_ptr(), wpe.data_ptr(), x.data_ptr(), B, T, C,
+                        pos0, _stream())
+    return x
+
+
+def embedding_bwd(idx: torch.Tensor, dx: torch.Tensor, wte_grad: Optional[torch.Tensor],
+                  wpe_grad: Optional[torch.Tensor], vocab: int, pos0: int = 0) -> None:
+    B, T = idx.shape
+    C = dx.shape[-1]
+    lib().embedding_bwd(idx.data_ptr(), dx.data_ptr(), _ptr(wte_grad), _ptr(wpe_grad), B, T, C,
+                        vocab, pos0, _stream())
+
+
+# --------------------------------------------------------------- cross-entropy --
+def cross_entropy_fwd_bwd(logits: torch.Tensor, targets: torch.Tensor, loss_rows: torch.Tensor,
+                          loss_out: torch.Tensor, vocab: int) -> None:
+    """Loss + in-place dlogits (softmax - onehot) over a bf16 [M, ld] logits view.
+
+    loss_out[0] = mean loss over non-ignored targets, loss_out[1] = 1/count
+    (the scale the lm_head backward GEMMs apply through alpha_ptr).
+    """
+    M = logits.shape[0]
+    L = lib()
+    L.cross_entropy(logits.data_ptr(), _row_stride(logits), targets.data_ptr(),
+                    loss_rows.data_ptr(), M, vocab, 0, _stream())
+    L.loss_reduce(loss_rows.data_ptr(), targets.data_ptr(), M, loss_out.data_ptr(), _stream())
+
+
+# ---------------------------------------------------------------- optimiser --
+def adamw_step(p: torch.Tensor, g: torch.Tensor, m: torch.Tensor, v: torch.Tensor,
+               p_bf16: Optional[torch.Tensor], n_decay: int, hp: torch.Tensor,
+               clip: Optional[torch.Tensor] = None,
+               decay_ranges: Optional[torch.Tensor] = None) -> None:
+    """Fused AdamW over flat fp32 buffers (see csrc/elementwise.cuh for hp).
+
+    Decay applies to ``[0, n_decay)`` or, when ``decay_ranges`` (int64 device
+    tensor ``[lo0, hi0, lo1, hi1, ...]``, sorted, 4-aligned) is given, inside
+    those ranges.
+    """
+    nr = 0 if decay_ranges is None else decay_ranges.numel() // 2
+    lib().adamw(p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), _ptr(p_bf16), p.numel(),
+                int(n_decay), _ptr(decay_ranges), nr, hp.data_ptr(), _ptr(clip), _stream())
+
+
+def grad_sumsq(g: torch.Tensor, ws: torch.Tensor, out: torch.Tensor) -> None:
+    lib().sumsq(g.data_ptr(), g.numel(), ws.data_ptr(), out.data_ptr(), _stream())
+
+
+def clip_coef(sumsq: torch.Tensor, max_norm: float, clip: torch.Tensor,
+              norm_out: Optional[torch.Tensor] = None, scale2: float = 1.0) -> None:
+    lib().clip_coef(sumsq.data_ptr(), float(scale2), float(max_norm), clip.data_ptr(),
+                    _ptr(norm_out), _stream())

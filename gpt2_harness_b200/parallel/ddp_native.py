@@ -1,0 +1,178 @@
+"""Data parallelism for the native engine, overlapped with backward.
+
+Reference semantics (src/transformer_internals/parallel/data_parallel.py:
+45-152): gradients are averaged with SUM all-reduces over 25 MiB buckets built
+greedily in reverse parameter order, then divided by p; a bf16 wire casts each
+bucket down before the reduction. Payload per rank per step is 4N bytes (2N on
+a bf16 wire) in the reference's counting convention.
+
+B200 design:
+
+* The engine's flat fp32 gradient buffer IS a :class:`SymmetricBuffer`: every
+  rank's buffer is mapped into every other rank, so no bucket is ever
+  flattened or copied (reference :136-151 concatenates and copies back).
+* The engine calls :meth:`NativeDDP.on_grads_ready` as soon as a block's
+  gradients are final; every bucket whose last tensor is now final is
+  launched on a dedicated communication stream, ordered after the compute
+  stream by an event. Communication overlaps the rest of backward.
+* ``comm="p2p"`` (default): one fused kernel per bucket
+  (csrc/comm.cu ``allreduce_p2p``) performs reduce-scatter, the 1/p scale and
+  all-gather over NVLink with in-kernel flags; ``comm="nccl"``: the bucket is
+  a ``dist.all_reduce`` view of the flat buffer and the 1/p is folded into the
+  AdamW kernel. Both charge the same counter entries.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from gpt2_harness_b200.models.engine import ALIGN, ParamLayout
+from gpt2_harness_b200.ops import native as N
+from gpt2_harness_b200.parallel import comms
+from gpt2_harness_b200.parallel.symm import SymmetricBuffer
+
+__all__ = ["Bucket", "build_layout_buckets", "NativeDDP", "DEFAULT_BUCKET_BYTES"]
+
+DEFAULT_BUCKET_BYTES = 25 * 1024 * 1024
+
+
+@dataclass
+class Bucket:
+    lo: int          # first element (flat layout), 64-element aligned
+    hi: int          # one past the last element including alignment padding
+    numel: int       # parameter elements (no padding): the counted payload
+    ready: int       # index of the gradient group that completes this bucket
+
+
+def group_order(layout: ParamLayout) -> list[str]:
+    L = layout.config.n_layer
+    return ["root_head"] + [f"h.{i}" for i in reversed(range(L))] + ["root_tail"]
+
+
+def _spec_group(spec) -> str:
+    if spec.group != "root":
+        return spec.group
+    return "root_head" if spec.name.startswith("ln_f") else "root_tail"
+
+
+def build_layout_buckets(layout: ParamLayout, bucket_bytes: int = DEFAULT_BUCKET_BYTES,
+                         elem_bytes: int = 4) -> list[Bucket]:
+    """Greedy buckets over the layout (= backward) order; a tensor larger than
+    the cap gets a bucket of its own (reference data_parallel.py:64-95)."""
+    order = {g: i for i, g in enumerate(group_order(layout))}
+    buckets: list[Bucket] = []
+    cur: list = []
+    size = 0
+    for s in layout.specs:
+        nbytes = s.numel * elem_bytes
+        if cur and size + nbytes > bucket_bytes:
+            buckets.append(_mk(cur, order))
+            cur, size = [], 0
+        cur.append(s)
+        size += nbytes
+    if cur:
+        buckets.append(_mk(cur, order))
+    return buckets
+
+
+def _mk(specs, order) -> Bucket:
+    lo = specs[0].offset
+    last = specs[-1]
+    hi = last.offset + (last.numel + ALIGN - 1) // ALIGN * ALIGN
+    return Bucket(lo, hi, sum(s.numel for s in specs), max(order[_spec_group(s)] for s in specs))
+
+
+class NativeDDP:
+    """Bucketed, backward-overlapped gradient averaging for :class:`Engine`.
+
+    Construct it BEFORE the engine and pass :attr:`grad_buffer` to the engine
+    (``Engine(..., grad_buffer=ddp.grad_buffer)``), then :meth:`attach`.
+    """
+
+    def __init__(self, layout: ParamLayout, group=None, comm: str = "p2p",
+                 bucket_bytes: int = DEFAULT_BUCKET_BYTES, nblocks: int = 64,
+                 device: Optional[torch.device] = None) -> None:
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.comm = comm if self.world > 1 else "none"
+        if self.comm not in ("p2p", "nccl", "none"):
+            raise ValueError(f"unknown comm {comm!r}")
+        self.layout = layout
+        self.buckets = build_layout_buckets(layout, bucket_bytes)
+        self.order = {g: i for i, g in enumerate(group_order(layout))}
+        self.nblocks = nblocks
+        self.symm: Optional[SymmetricBuffer] = None
+        self.flags: Optional[SymmetricBuffer] = None
+        if self.comm == "p2p":
+            self.symm = SymmetricBuffer(layout.total * 4, group, self.device)
+            self.grad_buffer = self.symm.view(torch.float32, layout.total)
+            words = N.lib().comm_flag_words()
+            self.flags = SymmetricBuffer(words * 4, group, self.device)
+        else:
+            self.grad_buffer = torch.zeros(layout.total, dtype=torch.float32, device=self.device)
+        self.stream = torch.cuda.Stream(device=self.device) if self.world > 1 else None
+        self.epoch = 0
+        self.byte_counter = torch.zeros(1, dtype=torch.int64, device=self.device)
+        self._next = 0
+        self.engine = None
+
+    @property
+    def grad_scale(self) -> float:
+        """Multiplier the optimiser applies to gradients (1/p for NCCL SUM)."""
+        return 1.0 / self.world if self.comm == "nccl" else 1.0
+
+    def attach(self, engine) -> None:
+        self.engine = engine
+        engine.grad_ready_hook = self.on_grads_ready
+        engine.grad_scale = self.grad_scale
+
+    # ----------------------------------------------------------- hooks --
+    def on_grads_ready(self, group: str) -> None:
+        if self.comm == "none":
+            return
+        idx = self.order[group]
+        while self._next < len(self.buckets) and self.buckets[self._next].ready <= idx:
+            self._launch(self.buckets[self._next])
+            self._next += 1
+
+    def _launch(self, b: Bucket) -> None:
+        ev = torch.cuda.Event()
+        ev.record()
+        self.stream.wait_event(ev)
+        comms.record_external("all_reduce", b.numel, b.numel * 4)
+        with torch.cuda.stream(self.stream):
+            if self.comm == "p2p":
+                self.epoch += 1
+                N.lib().allreduce_p2p(
+                    self.symm.peer_ptrs_dev.data_ptr(), self.flags.peer_ptrs_dev.data_ptr(),
+                    self.rank, self.world, b.lo, b.hi - b.lo, 0, 1.0 / self.world,
+                    self.epoch & 0xFFFFFFFF, self.byte_counter.data_ptr(), N.error_word().data_ptr(),
+                    self.nblocks, 2_000_000_000, self.stream.cuda_stream)
+            else:
+                dist.all_reduce(self.grad_buffer[b.lo:b.hi], group=self.group)
+
+    def finish(self) -> None:
+        """Make the compute stream wait for every launched bucket."""
+        if self.comm == "none":
+            return
+        if self._next != len(self.buckets):
+            # backward did not announce every group (e.g. a frozen tail):
+            # launch the rest now so every rank issues the same sequence.
+            while self._next < len(self.buckets):
+                self._launch(self.buckets[self._next])
+                self._next += 1
+        torch.cuda.current_stream().wait_stream(self.stream)
+        self._next = 0
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.device)
+        if self.symm is not None:
+            self.symm.close()
+        if self.flags is not None:
+            self.flags.close()

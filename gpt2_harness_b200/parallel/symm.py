@@ -1,0 +1,96 @@
+"""Symmetric device buffers mapped into every rank over NVLink (CUDA IPC).
+
+Each rank allocates a buffer of the same size with its own ``cudaMalloc`` and
+publishes a CUDA IPC handle through the process group; every rank opens all
+peers' handles. A native kernel then holds one device pointer per rank and
+reads or writes any peer's buffer with ordinary loads/stores, which NVSwitch
+routes over NVLink 5. This is the data plane of the fused collectives; the
+process group (NCCL or gloo) is only the control plane used to exchange the
+handles once.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from gpt2_harness_b200.ops import native as N
+
+__all__ = ["SymmetricBuffer", "wrap_device_pointer"]
+
+_TYPESTR = {torch.float32: "<f4", torch.bfloat16: "<V2", torch.int32: "<i4", torch.int64: "<i8",
+            torch.uint8: "|u1"}
+
+
+class _CudaArray:
+    """Minimal ``__cuda_array_interface__`` exporter around a raw pointer."""
+
+    def __init__(self, ptr: int, numel: int, typestr: str) -> None:
+        self.__cuda_array_interface__ = {
+            "shape": (numel,),
+            "typestr": typestr,
+            "data": (ptr, False),
+            "version": 3,
+            "strides": None,
+        }
+
+
+def wrap_device_pointer(ptr: int, numel: int, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    """A torch tensor aliasing ``numel`` elements at ``ptr`` (no copy, no
+    ownership: the caller keeps the allocation alive)."""
+    if dtype == torch.bfloat16:
+        raw = torch.as_tensor(_CudaArray(ptr, numel, "<i2"), device=device)
+        return raw.view(torch.bfloat16)
+    return torch.as_tensor(_CudaArray(ptr, numel, _TYPESTR[dtype]), device=device)
+
+
+class SymmetricBuffer:
+    """One equally sized buffer per rank, all mapped into this process.
+
+    Attributes:
+        local: this rank's buffer as a flat uint8 tensor.
+        peer_ptrs: python list of every rank's buffer address in THIS process.
+        peer_ptrs_dev: the same as an int64 device tensor (kernel argument).
+    """
+
+    def __init__(self, nbytes: int, group=None, device: Optional[torch.device] = None) -> None:
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.nbytes = int((nbytes + 255) // 256 * 256)
+        L = N.lib()
+        self.ptr = L.symm_alloc(self.nbytes)
+        handle = L.ipc_handle(self.ptr)
+        if not handle:
+            raise RuntimeError("cudaIpcGetMemHandle failed")
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        self.peer_ptrs = []
+        self._opened = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                self.peer_ptrs.append(self.ptr)
+            else:
+                p = L.ipc_open(h)
+                self._opened.append(p)
+                self.peer_ptrs.append(p)
+        self.peer_ptrs_dev = torch.tensor(self.peer_ptrs, dtype=torch.int64, device=self.device)
+        self.local = wrap_device_pointer(self.ptr, self.nbytes, torch.uint8, self.device)
+
+    def view(self, dtype: torch.dtype, numel: Optional[int] = None, offset_bytes: int = 0) -> torch.Tensor:
+        esz = torch.tensor([], dtype=dtype).element_size()
+        n = (self.nbytes - offset_bytes) // esz if numel is None else numel
+        return wrap_device_pointer(self.ptr + offset_bytes, n, dtype, self.device)
+
+    def close(self) -> None:
+        L = N.lib()
+        for p in self._opened:
+            L.ipc_close(p)
+        self._opened = []
+        if self.ptr:
+            torch.cuda.synchronize(self.device)
+            L.symm_free(self.ptr)
+            self.ptr = 0

@@ -1,0 +1,132 @@
+"""Public training API on the native B200 engine.
+
+``Trainer`` is the call a user makes: give it a config and a per-rank batch
+shape, then call :meth:`Trainer.step` with token ids and targets (host or
+device tensors). Under ``torchrun`` with more than one rank it runs data
+parallel (:class:`~gpt2_harness_b200.parallel.ddp_native.NativeDDP`) with the
+gradient all-reduce overlapped with backward.
+
+The learning-rate schedule is the reference's (train.py:72-99): linear warmup
+to ``lr`` over ``warmup_steps``, then cosine decay to ``lr * min_lr_ratio``.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from gpt2_harness_b200.config import GPTConfig, TrainConfig
+from gpt2_harness_b200.models.engine import Engine, OptimConfig
+from gpt2_harness_b200.ops import native as N
+
+__all__ = ["Trainer", "lr_at_step"]
+
+
+def lr_at_step(step: int, cfg: TrainConfig) -> float:
+    """Warmup + cosine schedule. ``step`` counts from 0."""
+    if cfg.warmup_steps > 0 and step < cfg.warmup_steps:
+        return cfg.lr * (step + 1) / cfg.warmup_steps
+    span = max(cfg.steps - cfg.warmup_steps, 1)
+    frac = min(max((step - cfg.warmup_steps) / span, 0.0), 1.0)
+    floor = cfg.lr * cfg.min_lr_ratio
+    return floor + 0.5 * (cfg.lr - floor) * (1.0 + math.cos(math.pi * frac))
+
+
+class Trainer:
+    """GPT-2 training on native sm_100a kernels, one process per GPU.
+
+    Args:
+        config: model architecture.
+        batch_size / seq_len: per-rank micro-batch shape (fixed: buffers are
+            preallocated for it).
+        train: optimiser settings and LR schedule (``TrainConfig``); ``None``
+            uses a constant ``lr`` from its defaults.
+        comm: ``"p2p"`` (fused peer-memory all-reduce) or ``"nccl"`` when the
+            default process group has more than one rank.
+        seed: weight init seed (identical on every rank; rank 0's weights are
+            broadcast to make sure).
+    """
+
+    def __init__(self, config: GPTConfig, batch_size: int, seq_len: int, *,
+                 train: Optional[TrainConfig] = None, comm: str = "p2p",
+                 device: Optional[torch.device] = None, seed: int = 0,
+                 bucket_bytes: int = 25 * 1024 * 1024, schedule: bool = True) -> None:
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        self.device = torch.device(device)
+        torch.cuda.set_device(self.device)
+        self.config = config
+        self.train_cfg = train or TrainConfig()
+        self.schedule = schedule and train is not None
+        self.B, self.T = batch_size, seq_len
+        self.world = dist.get_world_size() if dist.is_initialized() else 1
+        self.rank = dist.get_rank() if dist.is_initialized() else 0
+        tc = self.train_cfg
+        optim = OptimConfig(lr=tc.lr, betas=tuple(tc.betas), eps=tc.eps,
+                            weight_decay=tc.weight_decay, grad_clip=tc.grad_clip)
+        self.ddp = None
+        grad_buffer = None
+        if self.world > 1:
+            from gpt2_harness_b200.models.engine import ParamLayout
+            from gpt2_harness_b200.parallel.ddp_native import NativeDDP
+
+            self.ddp = NativeDDP(ParamLayout(config), comm=comm, bucket_bytes=bucket_bytes,
+                                 device=self.device)
+            grad_buffer = self.ddp.grad_buffer
+        self.engine = Engine(config, self.device, optim=optim, grad_buffer=grad_buffer, seed=seed)
+        if self.ddp is not None:
+            dist.broadcast(self.engine.master, src=0)
+            self.engine.sync_shadow()
+            self.ddp.attach(self.engine)
+        self.engine.acts(batch_size, seq_len)
+        self.idx = torch.zeros(batch_size, seq_len, dtype=torch.int64, device=self.device)
+        self.tgt = torch.zeros(batch_size, seq_len, dtype=torch.int64, device=self.device)
+        self.step_num = 0
+
+    @property
+    def num_parameters(self) -> int:
+        return self.engine.layout.num_parameters
+
+    def _load_inputs(self, idx: torch.Tensor, targets: torch.Tensor):
+        if idx.shape != (self.B, self.T) or targets.shape != (self.B, self.T):
+            raise ValueError(f"expected ({self.B}, {self.T}) batches, got {tuple(idx.shape)}")
+        if idx.device == self.device and targets.device == self.device:
+            return idx, targets
+        self.idx.copy_(idx, non_blocking=True)
+        self.tgt.copy_(targets, non_blocking=True)
+        return self.idx, self.tgt
+
+    def step_async(self, idx: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        """One optimiser step; returns the loss as a device scalar (no sync).
+        Host inputs should be pinned for the copy to be asynchronous."""
+        eng = self.engine
+        if self.schedule:
+            eng.set_lr(lr_at_step(self.step_num, self.train_cfg))
+        i, t = self._load_inputs(idx, targets)
+        loss = eng.forward(i, t)
+        eng.backward(i)
+        if self.ddp is not None:
+            self.ddp.finish()
+        eng.optimizer_step()
+        self.step_num += 1
+        return loss
+
+    def step(self, idx: torch.Tensor, targets: torch.Tensor) -> float:
+        """One optimiser step; returns this rank's loss as a Python float."""
+        return float(self.step_async(idx, targets).item())
+
+    def check(self) -> None:
+        """Raise if any native kernel recorded an error (synchronises)."""
+        N.check_errors(self.device)
+
+    def state_dict(self) -> dict:
+        return {"model": self.engine.state_dict(), "step": self.step_num,
+                "exp_avg": self.engine.exp_avg.clone(), "exp_avg_sq": self.engine.exp_avg_sq.clone(),
+                "optim_step": self.engine.step_count}
+
+    def close(self) -> None:
+        if self.ddp is not None:
+            self.ddp.close()

@@ -1,0 +1,317 @@
+"""Numerics of every native sm_100a kernel against a plain PyTorch fp32
+reference of the same op (inputs rounded to bf16 first, math in fp32)."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from gpt2_harness_b200.ops import native as N  # noqa: E402
+
+
+def dev():
+    return torch.device("cuda", 0)
+
+
+def rel_err(a, b):
+    a = a.float()
+    b = b.float()
+    return ((a - b).abs().max() / (b.abs().max() + 1e-6)).item()
+
+
+@pytest.fixture(autouse=True)
+def _errors_clean():
+    torch.cuda.set_device(0)
+    N.error_word().zero_()
+    yield
+    torch.cuda.synchronize()
+    N.check_errors()
+
+
+# ------------------------------------------------------------------- GEMM --
+SHAPES = [(128, 256, 64), (256, 512, 128), (200, 136, 72), (384, 768, 768), (1000, 520, 264)]
+
+
+@pytest.mark.parametrize("M,Nn,K", SHAPES)
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("bn", [256, 128])
+def test_gemm_layouts(M, Nn, K, a_t, b_t, bn):
+    g = torch.Generator(device="cpu").manual_seed(M * 7 + Nn + K)
+    A = torch.randn(M, K, generator=g).to(dev(), torch.bfloat16)
+    B = torch.randn(Nn, K, generator=g).to(dev(), torch.bfloat16)
+    a_in = A.t().contiguous() if a_t else A
+    b_in = B.t().contiguous() if b_t else B
+    out = torch.empty(M, Nn, dtype=torch.bfloat16, device=dev())
+    N.gemm(a_in, b_in, out, a_t=a_t, b_t=b_t, bn=bn)
+    ref = A.float() @ B.float().t()
+    assert rel_err(out, ref) < 1e-2
+
+
+def test_gemm_bias_gelu_and_bwd():
+    M, Nn, K = 512, 1024, 256
+    A = torch.randn(M, K, device=dev()).bfloat16()
+    W = (torch.randn(Nn, K, device=dev()) * 0.05).bfloat16()
+    bias = torch.randn(Nn, device=dev()).bfloat16()
+    pre = torch.empty(M, Nn, dtype=torch.bfloat16, device=dev())
+    act = torch.empty_like(pre)
+    N.gemm(A, W, act, epilogue=N.EPI_BIAS_GELU, bias=bias, aux=pre)
+    ref_pre = A.float() @ W.float().t() + bias.float()
+    ref_act = 0.5 * ref_pre * (1 + torch.tanh(math.sqrt(2 / math.pi) * (ref_pre + 0.044715 * ref_pre**3)))
+    assert rel_err(pre, ref_pre) < 1e-2
+    assert rel_err(act, ref_act) < 1e-2
+    # GELU backward epilogue: out = (G @ W2^T) * gelu'(pre)
+    G = torch.randn(M, 256, device=dev()).bfloat16()
+    W2 = (torch.randn(Nn, 256, device=dev()) * 0.05).bfloat16()
+    dact = torch.empty(M, Nn, dtype=torch.bfloat16, device=dev())
+    N.gemm(G, W2, dact, epilogue=N.EPI_GELU_BWD, aux=pre)
+    x = pre.float().requires_grad_(True)
+    y = 0.5 * x * (1 + torch.tanh(math.sqrt(2 / math.pi) * (x + 0.044715 * x**3)))
+    up = G.float() @ W2.float().t()
+    (gx,) = torch.autograd.grad(y, x, up)
+    assert rel_err(dact, gx) < 2e-2
+
+
+def test_gemm_resid_and_f32_accumulate_splitk():
+    M, Nn, K = 768, 512, 2048
+    A = torch.randn(M, K, device=dev()).bfloat16()
+    B = torch.randn(Nn, K, device=dev()).bfloat16()
+    bias = torch.randn(Nn, device=dev()).bfloat16()
+    resid = torch.randn(M, Nn, device=dev())
+    ref = resid + A.float() @ B.float().t() + bias.float()
+    N.gemm(A, B, resid, epilogue=N.EPI_RESID_F32, bias=bias)
+    assert rel_err(resid, ref) < 1e-4
+    # wgrad style: both operands MN-major, fp32 out, accumulate, split-K 4
+    X = torch.randn(K, M, device=dev()).bfloat16()   # [tokens, in]
+    dY = torch.randn(K, Nn, device=dev()).bfloat16()  # [tokens, out]
+    gw = torch.randn(Nn, M, device=dev())
+    ref = gw + dY.float().t() @ X.float()
+    ws = torch.empty(4 * Nn * M, device=dev())
+    N.gemm(dY, X, gw, a_t=True, b_t=True, epilogue=N.EPI_F32, accumulate=True, splits=4, workspace=ws)
+    assert rel_err(gw, ref) < 1e-4
+
+
+def test_gemm_alpha_ptr():
+    A = torch.randn(256, 128, device=dev()).bfloat16()
+    B = torch.randn(256, 128, device=dev()).bfloat16()
+    out = torch.empty(256, 256, device=dev())
+    a = torch.tensor([0.25], device=dev())
+    N.gemm(A, B, out, epilogue=N.EPI_F32, alpha=2.0, alpha_ptr=a)
+    assert rel_err(out, 0.5 * (A.float() @ B.float().t())) < 1e-4
+
+
+def test_gemm_large_vocab_shape():
+    # lm_head-like: N not a multiple of the tile, padded row stride
+    M, V, C = 512, 50257, 768
+    ld = 50304
+    x = torch.randn(M, C, device=dev()).bfloat16()
+    w = (torch.randn(V, C, device=dev()) * 0.02).bfloat16()
+    logits = torch.zeros(M, ld, dtype=torch.bfloat16, device=dev())
+    N.gemm(x, w, logits[:, :V])
+    ref = x.float() @ w.float().t()
+    assert rel_err(logits[:, :V], ref) < 1e-2
+
+
+# -------------------------------------------------------------- attention --
+def ref_attention(q, k, v, causal=True, q_offset=0):
+    # q: [B, H, Tq, 64], k/v: [B, H, Tk, 64] fp32
+    s = q @ k.transpose(-1, -2) / 8.0
+    Tq, Tk = q.shape[-2], k.shape[-2]
+    if causal:
+        qi = torch.arange(Tq, device=q.device)[:, None] + q_offset
+        kj = torch.arange(Tk, device=q.device)[None, :]
+        s = s.masked_fill(kj > qi, float("-inf"))
+    return torch.softmax(s, -1) @ v
+
+
+@pytest.mark.parametrize("B,H,T", [(1, 1, 64), (2, 3, 128), (2, 2, 200), (1, 12, 1024)])
+def test_attention_fwd_bwd(B, H, T):
+    C = H * 64
+    torch.manual_seed(T + H)
+    qkv = torch.randn(B * T, 3 * C, device=dev()).bfloat16()
+    o = torch.empty(B * T, C, dtype=torch.bfloat16, device=dev())
+    lse = torch.empty(B, H, T, device=dev())
+    N.attention_fwd(qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:], o, lse, B, H, T)
+
+    def heads(x):
+        return x.float().view(B, T, H, 64).transpose(1, 2)
+
+    q, k, v = heads(qkv[:, :C]), heads(qkv[:, C:2 * C]), heads(qkv[:, 2 * C:])
+    q.requires_grad_(True), k.requires_grad_(True), v.requires_grad_(True)
+    ref = ref_attention(q, k, v)
+    got = o.float().view(B, T, H, 64).transpose(1, 2)
+    assert rel_err(got, ref.detach()) < 2e-2
+
+    do = torch.randn(B * T, C, device=dev()).bfloat16()
+    dqkv = torch.empty_like(qkv)
+    delta = torch.empty(B, H, T, device=dev())
+    N.attention_bwd(qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:], o, do, dqkv[:, :C],
+                    dqkv[:, C:2 * C], dqkv[:, 2 * C:], lse, delta, B, H, T)
+    gq, gk, gv = torch.autograd.grad(ref, (q, k, v), heads(do))
+    for got_g, ref_g in ((dqkv[:, :C], gq), (dqkv[:, C:2 * C], gk), (dqkv[:, 2 * C:], gv)):
+        assert rel_err(heads(got_g), ref_g) < 3e-2
+
+
+def test_attention_q_offset():
+    # context-parallel shard: 64 local queries at absolute offset 128 vs 256 keys
+    B, H, Tq, Tk, off = 1, 2, 64, 256, 128
+    C = H * 64
+    q = torch.randn(B * Tq, C, device=dev()).bfloat16()
+    kv = torch.randn(B * Tk, 2 * C, device=dev()).bfloat16()
+    o = torch.empty(B * Tq, C, dtype=torch.bfloat16, device=dev())
+    lse = torch.empty(B, H, Tq, device=dev())
+    N.attention_fwd(q, kv[:, :C], kv[:, C:], o, lse, B, H, Tq, Tk=Tk, q_offset=off)
+    qh = q.float().view(B, Tq, H, 64).transpose(1, 2)
+    kh = kv[:, :C].float().view(B, Tk, H, 64).transpose(1, 2)
+    vh = kv[:, C:].float().view(B, Tk, H, 64).transpose(1, 2)
+    ref = ref_attention(qh, kh, vh, q_offset=off)
+    assert rel_err(o.float().view(B, Tq, H, 64).transpose(1, 2), ref) < 2e-2
+
+
+def test_attention_deterministic():
+    B, H, T = 2, 4, 256
+    C = H * 64
+    qkv = torch.randn(B * T, 3 * C, device=dev()).bfloat16()
+    o = torch.empty(B * T, C, dtype=torch.bfloat16, device=dev())
+    lse = torch.empty(B, H, T, device=dev())
+    N.attention_fwd(qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:], o, lse, B, H, T)
+    do = torch.randn(B * T, C, device=dev()).bfloat16()
+    outs = []
+    for _ in range(2):
+        d = torch.empty_like(qkv)
+        delta = torch.empty(B, H, T, device=dev())
+        N.attention_bwd(qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:], o, do, d[:, :C], d[:, C:2 * C],
+                        d[:, 2 * C:], lse, delta, B, H, T)
+        outs.append(d)
+    assert torch.equal(outs[0], outs[1])
+
+
+# -------------------------------------------------------------- layernorm --
+@pytest.mark.parametrize("M,C", [(64, 128), (1000, 768), (300, 1600)])
+def test_layernorm(M, C):
+    x = torch.randn(M, C, device=dev()) * 3 + 1
+    g = (1 + 0.1 * torch.randn(C, device=dev())).bfloat16()
+    b = (0.1 * torch.randn(C, device=dev())).bfloat16()
+    y = torch.empty(M, C, dtype=torch.bfloat16, device=dev())
+    mean = torch.empty(M, device=dev())
+    rstd = torch.empty(M, device=dev())
+    N.layernorm_fwd(x, g, b, y, mean, rstd)
+    xr = x.clone().requires_grad_(True)
+    gr = g.float().requires_grad_(True)
+    br = b.float().requires_grad_(True)
+    ref = torch.nn.functional.layer_norm(xr, (C,), gr, br, 1e-5)
+    assert rel_err(y, ref.detach()) < 1e-2
+    dy = torch.randn(M, C, device=dev()).bfloat16()
+    gx, gg, gb = torch.autograd.grad(ref, (xr, gr, br), dy.float())
+    dres = torch.ones(M, C, device=dev())
+    dres16 = torch.empty(M, C, dtype=torch.bfloat16, device=dev())
+    dg = torch.zeros(C, device=dev())
+    db = torch.zeros(C, device=dev())
+    parts = N.layernorm_bwd_partials(M, C, dev())
+    N.layernorm_bwd(dy, x, mean, rstd, g, dres, dres16, dg, db, parts, accumulate_dres=True)
+    assert rel_err(dres - 1, gx) < 1e-4
+    assert rel_err(dres16, gx + 1) < 1e-2
+    assert rel_err(dg, gg) < 1e-4
+    assert rel_err(db, gb) < 1e-4
+
+
+def test_colsum_bf16():
+    x = torch.randn(1000, 768, device=dev()).bfloat16()
+    out = torch.ones(768, device=dev())
+    ws = torch.empty(N.colsum_ws_numel(1000, 768), device=dev())
+    N.colsum_bf16(x, out, ws, accumulate=True)
+    assert rel_err(out, 1 + x.float().sum(0)) < 1e-5
+
+
+# --------------------------------------------------------------- embedding --
+def test_embedding():
+    V, C, B, T = 1000, 128, 3, 50
+    wte = torch.randn(V, C, device=dev()).bfloat16()
+    wpe = torch.randn(64, C, device=dev()).bfloat16()
+    idx = torch.randint(0, V, (B, T), device=dev())
+    x = torch.empty(B * T, C, device=dev())
+    N.embedding_fwd(idx, wte, wpe, x)
+    ref = wte.float()[idx] + wpe.float()[:T][None]
+    assert rel_err(x.view(B, T, C), ref) < 1e-6
+    dx = torch.randn(B * T, C, device=dev())
+    gw = torch.zeros(V, C, device=dev())
+    gp = torch.zeros(64, C, device=dev())
+    N.embedding_bwd(idx, dx, gw, gp, V)
+    ref_w = torch.zeros(V, C, device=dev()).index_add_(0, idx.flatten(), dx)
+    assert rel_err(gw, ref_w) < 1e-5
+    assert rel_err(gp[:T], dx.view(B, T, C).sum(0)) < 1e-5
+
+
+# ----------------------------------------------------------- cross-entropy --
+def test_cross_entropy():
+    M, V, ld = 300, 50257, 50304
+    logits = torch.zeros(M, ld, dtype=torch.bfloat16, device=dev())
+    logits[:, :V] = (torch.randn(M, V, device=dev()) * 2).bfloat16()
+    tgt = torch.randint(0, V, (M,), device=dev())
+    tgt[::7] = -100
+    ref_in = logits[:, :V].float().requires_grad_(True)
+    ref = torch.nn.functional.cross_entropy(ref_in, tgt, ignore_index=-100)
+    (g,) = torch.autograd.grad(ref, ref_in)
+    rows = torch.empty(M, device=dev())
+    out = torch.empty(2, device=dev())
+    N.cross_entropy_fwd_bwd(logits, tgt, rows, out, V)
+    assert abs(out[0].item() - ref.item()) < 1e-3 * abs(ref.item())
+    count = (tgt != -100).sum().item()
+    assert abs(out[1].item() - 1.0 / count) < 1e-9
+    assert rel_err(logits[:, :V].float() * out[1], g) < 2e-2
+    assert logits[:, V:].abs().max().item() == 0
+
+
+# ------------------------------------------------------------------- AdamW --
+def test_adamw_matches_torch():
+    n = 10007
+    n_decay = 6000
+    torch.manual_seed(0)
+    p = torch.randn(n, device=dev())
+    grads = [torch.randn(n, device=dev()) for _ in range(3)]
+    ref_a = torch.nn.Parameter(p[:n_decay].clone())
+    ref_b = torch.nn.Parameter(p[n_decay:].clone())
+    opt = torch.optim.AdamW([{"params": [ref_a], "weight_decay": 0.1},
+                             {"params": [ref_b], "weight_decay": 0.0}],
+                            lr=3e-4, betas=(0.9, 0.95), eps=1e-8, foreach=False, fused=False)
+    mine = p.clone()
+    m = torch.zeros(n, device=dev())
+    v = torch.zeros(n, device=dev())
+    pb = torch.empty(n, dtype=torch.bfloat16, device=dev())
+    for step, gr in enumerate(grads, start=1):
+        ref_a.grad = gr[:n_decay].clone()
+        ref_b.grad = gr[n_decay:].clone()
+        opt.step()
+        hp = torch.tensor([3e-4, 0.9, 0.95, 1e-8, 0.1, 1 - 0.9**step, math.sqrt(1 - 0.95**step), 1.0],
+                          device=dev())
+        N.adamw_step(mine, gr, m, v, pb, n_decay, hp)
+    ref = torch.cat([ref_a.detach(), ref_b.detach()])
+    assert (mine - ref).abs().max().item() < 1e-6
+    assert torch.equal(pb, mine.bfloat16())
+
+
+def test_grad_norm_clip():
+    g = torch.randn(123457, device=dev())
+    ws = torch.empty(1024, device=dev())
+    ss = torch.empty(1, device=dev())
+    clip = torch.empty(1, device=dev())
+    norm = torch.empty(1, device=dev())
+    N.grad_sumsq(g, ws, ss)
+    N.clip_coef(ss, 1.0, clip, norm)
+    ref = g.norm().item()
+    assert abs(norm.item() - ref) < 1e-4 * ref
+    assert abs(clip.item() - min(1.0, 1.0 / (ref + 1e-6))) < 1e-6
+
+
+def test_bounded_wait_returns_error():
+    """A flag nobody sets must time out in-kernel and leave the context usable."""
+    flag = torch.zeros(1, dtype=torch.int32, device=dev())
+    err = torch.zeros(1, dtype=torch.int32, device=dev())
+    N.lib().flag_wait_test(flag.data_ptr(), 1, 200_000_000, err.data_ptr(),
+                           torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert err.item() == 1 << 3
+    # the context still works
+    x = torch.ones(4, device=dev())
+    assert x.sum().item() == 4
