@@ -44,8 +44,7 @@ _SQRT_2_OVER_PI = math.sqrt(2.0 / math.pi)
 def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
     """GELU with the tanh approximation GPT-2 shipped:
     ``0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))``."""
-    inner = _SQRT_2_OVER_PI * (x + 0.044715 * x * x * x)
-    return 0.5 * x * (1.0 + torch.tanh(inner))
+    return 0.5 * x * (1.0 + torch.tanh(_SQRT_2_OVER_PI * (x + 0.044715 * x.pow(3))))
 
 
 def sinusoidal_position_embeddings(n_positions: int, n_embd: int) -> torch.Tensor:

@@ -56,9 +56,9 @@ def device_scope(device) -> Iterator[torch.device]:
 
 def parallel_config(**overrides: Any) -> GPTConfig:
     """The toy shape every equivalence worker uses by default: vocab 128,
-    context 32, 4 layers, 4 heads, width 32 (the reference's
+    context 64, 4 layers, 4 heads, width 32, no dropout (the reference's
     parallel_config; its byte closed forms are quoted at this size)."""
-    base = dict(vocab_size=128, n_positions=32, n_layer=4, n_head=4, n_embd=32, dropout=0.0)
+    base = dict(vocab_size=128, n_positions=64, n_layer=4, n_head=4, n_embd=32, dropout=0.0)
     base.update(overrides)
     return GPTConfig(**base)
 

@@ -301,20 +301,26 @@ def _entry(fn, rank, world, backend, init_file, timeout_s, device_kind, kwargs, 
 
 
 def spawn_workers(fn: Callable, world_size: int, kwargs: Optional[dict] = None,
-                  backend: Optional[str] = None, timeout_s: float = 300.0,
-                  device: str = "cpu") -> list[WorkerResult]:
+                  backend: Optional[str] = None, timeout: float = 300.0, caps=None,
+                  allow_oversubscribe: bool = False) -> list[WorkerResult]:
     """Run ``fn(rank, world_size, **kwargs)`` in `world_size` fresh processes.
 
-    One spawned process per rank, FileStore rendezvous, the device bound before
-    ``init_process_group``. Fails fast: if any rank raises or dies without
-    reporting, the others are terminated and RuntimeError carries the first
-    traceback. ``fn`` must be importable (module-level).
+    The backend is chosen (or a request validated) from the machine's
+    capabilities and the placement is checked in the parent, so an impossible
+    placement fails before any process starts. One spawned process per rank,
+    FileStore rendezvous, the device bound before ``init_process_group``.
+    Fails fast: if any rank raises or dies without reporting, the others are
+    terminated and RuntimeError carries the first traceback. ``fn`` must be
+    importable (module-level).
     """
+    from gpt2_harness_b200 import hardware
+
     kwargs = dict(kwargs or {})
-    backend = backend or ("nccl" if device == "cuda" else "gloo")
-    if device == "cuda" and torch.cuda.device_count() < world_size:
-        raise RuntimeError(f"{world_size} ranks need {world_size} GPUs; "
-                           f"{torch.cuda.device_count()} visible")
+    caps = caps if caps is not None else hardware.Capabilities.detect()
+    backend = hardware.select_backend(caps, backend)
+    hardware.check_placement(caps, world_size, backend, allow_oversubscribe)
+    device = "cuda" if backend == "nccl" else "cpu"
+    timeout_s = float(timeout)
     ctx = mp.get_context("spawn")
     out_q = ctx.Queue()
     tmpdir = tempfile.mkdtemp(prefix="g2b_rdzv_")
