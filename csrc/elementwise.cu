@@ -208,32 +208,68 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(
   }
 }
 
-// out[c] (+)= sum_r in[r*C + c]
-__global__ void colsum_f32_kernel(const float* __restrict__ in, int R, int C,
-                                  float* __restrict__ out, int accumulate) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= C) return;
+// out[c] (+)= sum_r in[r*C + c]. Block = 32 columns x 8 row lanes; each
+// lane sums rows y, y+8, ... (several loads in flight), then the 8 lane sums
+// are added in fixed order through shared memory: deterministic.
+__global__ void __launch_bounds__(256) colsum_f32_kernel(const float* __restrict__ in, int R, int C,
+                                                         float* __restrict__ out, int accumulate) {
+  __shared__ float red[8][33];
+  const int c = blockIdx.x * 32 + threadIdx.x;
   float s = 0.f;
-  for (int r = 0; r < R; ++r) s += in[(int64_t)r * C + c];
-  out[c] = accumulate ? out[c] + s : s;
+  if (c < C) {
+#pragma unroll 4
+    for (int r = threadIdx.y; r < R; r += 8) s += __ldg(in + (int64_t)r * C + c);
+  }
+  red[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y == 0 && c < C) {
+    float t = 0.f;
+#pragma unroll
+    for (int y = 0; y < 8; ++y) t += red[y][threadIdx.x];
+    out[c] = accumulate ? out[c] + t : t;
+  }
 }
 
-// Partial column sums of bf16 in[M, C] over 256-row chunks: ws[chunk, C].
-__global__ void colsum_bf16_partial_kernel(const __nv_bfloat16* __restrict__ in, int64_t ld,
-                                           int M, int C, float* __restrict__ ws) {
-  const int c2 = blockIdx.x * blockDim.x + threadIdx.x;  // pair of columns
-  if (2 * c2 >= C) return;
-  const int r0 = blockIdx.y * 256;
-  const int r1 = min(M, r0 + 256);
-  float a = 0.f, b = 0.f;
-  for (int r = r0; r < r1; ++r) {
-    const float2 f = __bfloat1622float2(
-        *reinterpret_cast<const __nv_bfloat162*>(in + (int64_t)r * ld + 2 * c2));
-    a += f.x;
-    b += f.y;
+constexpr int COLSUM_ROWS = 128;  // rows per partial in the bf16 column sum
+
+// Partial column sums of bf16 in[M, C] over COLSUM_ROWS-row chunks into
+// ws[chunk, C]. Block = 32 column groups of 8 (one 16-byte load each) x 8 row
+// lanes; fixed-order reduction across the lanes.
+__global__ void __launch_bounds__(256) colsum_bf16_partial_kernel(
+    const __nv_bfloat16* __restrict__ in, int64_t ld, int M, int C, float* __restrict__ ws) {
+  __shared__ float red[8][32 * 8 + 4];
+  const int cg = blockIdx.x * 32 + threadIdx.x;  // 8-column group
+  const bool active = cg * 8 < C;
+  const int r0 = blockIdx.y * COLSUM_ROWS;
+  const int r1 = min(M, r0 + COLSUM_ROWS);
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  if (active) {
+#pragma unroll 4
+    for (int r = r0 + threadIdx.y; r < r1; r += 8) {
+      const uint4 w = __ldcs(reinterpret_cast<const uint4*>(in + (int64_t)r * ld + cg * 8));
+      const uint32_t ws4[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(ws4[j]);
+        acc[2 * j] += f.x;
+        acc[2 * j + 1] += f.y;
+      }
+    }
   }
-  ws[(int64_t)blockIdx.y * C + 2 * c2] = a;
-  ws[(int64_t)blockIdx.y * C + 2 * c2 + 1] = b;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[threadIdx.y][threadIdx.x * 8 + j] = acc[j];
+  __syncthreads();
+  // 256 threads finish 256 columns of this block (32 groups x 8)
+  const int t = threadIdx.y * 32 + threadIdx.x;
+  const int col = blockIdx.x * 256 + t;
+  if (col < C) {
+    float sum = 0.f;
+#pragma unroll
+    for (int y = 0; y < 8; ++y) sum += red[y][t];
+    ws[(int64_t)blockIdx.y * C + col] = sum;
+  }
 }
 
 // --------------------------------------------------------------- embedding ---
@@ -570,19 +606,19 @@ int layernorm_bwd_launch(const void* dy, const float* x, const float* mean, cons
 }
 
 int colsum_f32_launch(const float* in, int R, int C, float* out, int accumulate, cudaStream_t s) {
-  colsum_f32_kernel<<<(C + 255) / 256, 256, 0, s>>>(in, R, C, out, accumulate);
+  colsum_f32_kernel<<<(C + 31) / 32, dim3(32, 8), 0, s>>>(in, R, C, out, accumulate);
   count_launches(1);
   return ok();
 }
 
 int colsum_bf16_launch(const void* in, int64_t ld, int M, int C, float* ws, float* out,
                        int accumulate, cudaStream_t s) {
-  if (C % 2 || ld % 2) return -1;
-  const int chunks = (M + 255) / 256;
-  dim3 grid((C / 2 + 127) / 128, chunks);
-  colsum_bf16_partial_kernel<<<grid, 128, 0, s>>>((const __nv_bfloat16*)in, ld, M, C, ws);
+  if (C % 8 || ld % 8 || (reinterpret_cast<uintptr_t>(in) & 15)) return -1;
+  const int chunks = (M + COLSUM_ROWS - 1) / COLSUM_ROWS;
+  dim3 grid((C + 255) / 256, chunks);
+  colsum_bf16_partial_kernel<<<grid, dim3(32, 8), 0, s>>>((const __nv_bfloat16*)in, ld, M, C, ws);
   count_launches(1);
-  colsum_f32_kernel<<<(C + 255) / 256, 256, 0, s>>>(ws, chunks, C, out, accumulate);
+  colsum_f32_kernel<<<(C + 31) / 32, dim3(32, 8), 0, s>>>(ws, chunks, C, out, accumulate);
   count_launches(1);
   return ok();
 }

@@ -25,7 +25,7 @@ int layernorm_bwd_launch(const void* dy, const float* x, const float* mean, cons
 int colsum_f32_launch(const float* in, int R, int C, float* out, int accumulate, cudaStream_t s);
 
 // Bias gradient: out[c] (+)= sum_m in[m, c] for bf16 in[M, C] (row stride ld),
-// deterministic two-stage (partials in `ws`, >= ceil(M/256)*C floats).
+// deterministic two-stage (partials in `ws`, >= ceil(M/128)*C floats).
 int colsum_bf16_launch(const void* in, int64_t ld, int M, int C, float* ws, float* out,
                        int accumulate, cudaStream_t s);
 

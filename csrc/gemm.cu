@@ -3,7 +3,7 @@
 //
 //   C[M,N] = A[M,K] . B[N,K]^T   (A and B each K-major or MN-major)
 //
-// One CTA per SM (persistent; tiles strided by gridDim.x), 192 threads:
+// One CTA per SM (persistent; tiles strided by gridDim.x), 320 threads:
 //   warp 0      TMA producer: one elected lane streams A/B k-blocks into a
 //               STAGES-deep ring of 128B-swizzled shared-memory stages.
 //   warp 1      MMA issuer: allocates TMEM, one elected lane issues
@@ -11,9 +11,15 @@
 //               stage back to the producer; the accumulator is double buffered
 //               in TMEM (2 x BN fp32 columns) so tile i+1's MMAs overlap tile
 //               i's epilogue.
-//   warps 2..5  epilogue: tcgen05.ld the accumulator (one TMEM lane = one
-//               output row per thread), apply the fused epilogue (bias, GELU,
-//               GELU backward, fp32 residual add, split-K partial) and store.
+//   warps 2..9  epilogue: two warps per TMEM lane quarter (tcgen05.ld lets warp
+//               w read lanes 32*(w%4)..+31), each owning half the tile's
+//               columns. A warp turns 32 accumulator columns of its 32 rows at
+//               a time into the fused epilogue result (bias, GELU, GELU
+//               backward, fp32 residual add, split-K partial), writes them into
+//               a swizzled shared-memory box and issues one TMA bulk tensor
+//               store for the box, so global writes are full-line bulk copies.
+//               Operands the epilogue reads (residual stream, GELU input) are
+//               prefetched into registers one chunk ahead.
 //
 // The GEMMs of GPT-2 (reference: src/transformer_internals/model.py:201-203
 // c_attn, :318-319 c_proj, :333-334 c_fc/c_proj, :474-480 lm_head) all map on
@@ -25,6 +31,8 @@
 #include <cuda_bf16.h>
 #include <stdio.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "gemm.cuh"
 
@@ -34,7 +42,9 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kStageBuf = 4096;  // per epilogue warp: one 32x32 fp32 box / two bf16 boxes
 
 template <int BN>
 struct GemmCfg {
@@ -43,7 +53,9 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int EPI_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFFSET = EPI_OFFSET + kEpiWarps * kStageBuf;
+  static constexpr int SMEM_BYTES = BAR_OFFSET + 256 + 1024 /*alignment slack*/;
 };
 
 struct GemmDev {
@@ -62,46 +74,163 @@ struct GemmDev {
   uint32_t* err;
 };
 
+// ---------------------------------------------------------------- TMA store
+__device__ __forceinline__ void tma_store_3d(const void* tmap, const void* smem_src, int32_t x,
+                                             int32_t y, int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(tmap)),
+      "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;"); }
+__device__ __forceinline__ void bulk_wait_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Per-chunk operand the epilogue reads besides the accumulator (prefetched).
+struct EpiIn {
+  float f[32];  // fp32 residual source / old fp32 output, or unpacked GELU input
+};
+
 template <int EPI>
-__device__ __forceinline__ void epilogue_chunk(const GemmDev& p, int row, int n0, float* v) {
-  if (row >= p.M || n0 >= p.N) return;
+__device__ __forceinline__ void load_epi_in(const GemmDev& p, int row, int n0, EpiIn& in) {
+  const bool rd_f32 = (EPI == EPI_RESID_F32) || (EPI == EPI_F32 && p.accumulate);
+  const bool rd_bf16 = (EPI == EPI_GELU_BWD);
+  if (!rd_f32 && !rd_bf16) return;
+  if (row >= p.M || n0 >= p.N) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) in.f[i] = 0.f;
+    return;
+  }
   const bool full = (n0 + 32 <= p.N) && p.vec_ok;
-  float bias[32];
-  if (p.bias != nullptr && (EPI == EPI_BF16 || EPI == EPI_BIAS_GELU || EPI == EPI_RESID_F32)) {
+  if (rd_f32) {
+    const float* src = (EPI == EPI_RESID_F32 && p.aux != nullptr)
+                           ? reinterpret_cast<const float*>(p.aux) + (int64_t)row * p.ldaux + n0
+                           : reinterpret_cast<const float*>(p.out) + (int64_t)row * p.ldo + n0;
     if (full) {
-      const uint4* bp = reinterpret_cast<const uint4*>(p.bias + n0);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 w = __ldcs(reinterpret_cast<const float4*>(src) + q);
+        in.f[4 * q] = w.x;
+        in.f[4 * q + 1] = w.y;
+        in.f[4 * q + 2] = w.z;
+        in.f[4 * q + 3] = w.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) in.f[i] = (n0 + i < p.N) ? src[i] : 0.f;
+    }
+  } else {
+    const __nv_bfloat16* a =
+        reinterpret_cast<const __nv_bfloat16*>(p.aux) + (int64_t)row * p.ldaux + n0;
+    if (full) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        uint4 w = __ldg(bp + q);
-        uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        const uint4 u = __ldcs(reinterpret_cast<const uint4*>(a) + q);
+        const uint32_t us[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          float2 f = unpack_bf16x2(ws[j]);
-          bias[q * 8 + 2 * j] = f.x;
-          bias[q * 8 + 2 * j + 1] = f.y;
+          const float2 f = unpack_bf16x2(us[j]);
+          in.f[q * 8 + 2 * j] = f.x;
+          in.f[q * 8 + 2 * j + 1] = f.y;
         }
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        bias[i] = (n0 + i < p.N) ? __bfloat162float(p.bias[n0 + i]) : 0.f;
+      for (int i = 0; i < 32; ++i) in.f[i] = (n0 + i < p.N) ? __bfloat162float(a[i]) : 0.f;
+    }
+  }
+}
+
+// Turns the scaled accumulator chunk v[32] into the epilogue result(s):
+// v (main output) and z (second output: GELU pre-activation).
+template <int EPI>
+__device__ __forceinline__ void epi_math(const GemmDev& p, int n0, float* v, const EpiIn& in,
+                                         float* z) {
+  if (EPI == EPI_BF16 || EPI == EPI_BIAS_GELU || EPI == EPI_RESID_F32) {
+    if (p.bias != nullptr) {
+      if (n0 + 32 <= p.N && p.vec_ok) {
+        const uint4* bp = reinterpret_cast<const uint4*>(p.bias + n0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 w = __ldg(bp + q);
+          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = unpack_bf16x2(ws[j]);
+            v[q * 8 + 2 * j] += f.x;
+            v[q * 8 + 2 * j + 1] += f.y;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (n0 + i < p.N) v[i] += __bfloat162float(p.bias[n0 + i]);
+      }
+    }
+  }
+  if (EPI == EPI_BIAS_GELU) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      z[i] = v[i];
+      v[i] = gelu_tanh_f(v[i]);
+    }
+  } else if (EPI == EPI_GELU_BWD) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] *= gelu_tanh_grad_f(in.f[i]);
+  } else if (EPI == EPI_RESID_F32 || (EPI == EPI_F32 && p.accumulate)) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] += in.f[i];
+  }
+}
+
+// Write one thread's 32 results into its row of a swizzled staging box:
+// bf16 rows are 64 B (SWIZZLE_64B: 16-byte chunk ^= (row/2)%4), fp32 rows
+// 128 B (SWIZZLE_128B: chunk ^= row%8), matching the output tensor maps.
+__device__ __forceinline__ void stage_bf16(uint8_t* box, int r, const float* y) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w;
+    w.x = pack_bf16x2(y[q * 8 + 0], y[q * 8 + 1]);
+    w.y = pack_bf16x2(y[q * 8 + 2], y[q * 8 + 3]);
+    w.z = pack_bf16x2(y[q * 8 + 4], y[q * 8 + 5]);
+    w.w = pack_bf16x2(y[q * 8 + 6], y[q * 8 + 7]);
+    *reinterpret_cast<uint4*>(box + r * 64 + ((q ^ ((r >> 1) & 3)) << 4)) = w;
+  }
+}
+__device__ __forceinline__ void stage_f32(uint8_t* box, int r, const float* y) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    *reinterpret_cast<float4*>(box + r * 128 + ((q ^ (r & 7)) << 4)) =
+        make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
+}
+
+// Direct (non-TMA) store of one thread's row chunk, for unaligned outputs.
+template <int EPI>
+__device__ __forceinline__ void store_direct(const GemmDev& p, int row, int n0, const float* y,
+                                             const float* z, int split) {
+  if (row >= p.M || n0 >= p.N) return;
+  const bool full = (n0 + 32 <= p.N) && p.vec_ok;
+  if (EPI == EPI_RESID_F32 || EPI == EPI_F32) {
+    float* o = reinterpret_cast<float*>(p.out) + (int64_t)split * p.split_stride +
+               (int64_t)row * p.ldo + n0;
+    if (full) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        reinterpret_cast<float4*>(o)[q] = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
+    } else {
+      for (int i = 0; i < 32 && n0 + i < p.N; ++i) o[i] = y[i];
     }
   } else {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) bias[i] = 0.f;
-  }
-
-  if (EPI == EPI_BF16 || EPI == EPI_BIAS_GELU) {
     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo + n0;
     __nv_bfloat16* a = EPI == EPI_BIAS_GELU
                            ? reinterpret_cast<__nv_bfloat16*>(p.aux) + (int64_t)row * p.ldaux + n0
                            : nullptr;
-    float y[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      v[i] += bias[i];
-      y[i] = EPI == EPI_BIAS_GELU ? gelu_tanh_f(v[i]) : v[i];
-    }
     if (full) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -113,88 +242,35 @@ __device__ __forceinline__ void epilogue_chunk(const GemmDev& p, int row, int n0
         reinterpret_cast<uint4*>(o)[q] = w;
         if (EPI == EPI_BIAS_GELU) {
           uint4 u;
-          u.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
-          u.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
-          u.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
-          u.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+          u.x = pack_bf16x2(z[q * 8 + 0], z[q * 8 + 1]);
+          u.y = pack_bf16x2(z[q * 8 + 2], z[q * 8 + 3]);
+          u.z = pack_bf16x2(z[q * 8 + 4], z[q * 8 + 5]);
+          u.w = pack_bf16x2(z[q * 8 + 6], z[q * 8 + 7]);
           reinterpret_cast<uint4*>(a)[q] = u;
         }
       }
     } else {
       for (int i = 0; i < 32 && n0 + i < p.N; ++i) {
         o[i] = __float2bfloat16(y[i]);
-        if (EPI == EPI_BIAS_GELU) a[i] = __float2bfloat16(v[i]);
-      }
-    }
-  } else if (EPI == EPI_GELU_BWD) {
-    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo + n0;
-    const __nv_bfloat16* a =
-        reinterpret_cast<const __nv_bfloat16*>(p.aux) + (int64_t)row * p.ldaux + n0;
-    if (full) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint4 u = reinterpret_cast<const uint4*>(a)[q];
-        uint32_t us[4] = {u.x, u.y, u.z, u.w};
-        float g[8];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float2 f = unpack_bf16x2(us[j]);
-          g[2 * j] = v[q * 8 + 2 * j] * gelu_tanh_grad_f(f.x);
-          g[2 * j + 1] = v[q * 8 + 2 * j + 1] * gelu_tanh_grad_f(f.y);
-        }
-        uint4 w;
-        w.x = pack_bf16x2(g[0], g[1]);
-        w.y = pack_bf16x2(g[2], g[3]);
-        w.z = pack_bf16x2(g[4], g[5]);
-        w.w = pack_bf16x2(g[6], g[7]);
-        reinterpret_cast<uint4*>(o)[q] = w;
-      }
-    } else {
-      for (int i = 0; i < 32 && n0 + i < p.N; ++i)
-        o[i] = __float2bfloat16(v[i] * gelu_tanh_grad_f(__bfloat162float(a[i])));
-    }
-  } else {  // fp32 outputs
-    float* o = reinterpret_cast<float*>(p.out) + (int64_t)row * p.ldo + n0;
-    const bool add_old = (EPI == EPI_RESID_F32) || (p.accumulate != 0);
-    // The residual epilogue may read its old value from a separate fp32 source
-    // (aux) so the stream can advance out of place: out = aux + acc + bias.
-    const float* src = (EPI == EPI_RESID_F32 && p.aux != nullptr)
-                           ? reinterpret_cast<const float*>(p.aux) + (int64_t)row * p.ldaux + n0
-                           : o;
-    if (full) {
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        float4 r = make_float4(v[q * 4] + bias[q * 4], v[q * 4 + 1] + bias[q * 4 + 1],
-                               v[q * 4 + 2] + bias[q * 4 + 2], v[q * 4 + 3] + bias[q * 4 + 3]);
-        if (add_old) {
-          float4 old = reinterpret_cast<const float4*>(src)[q];
-          r.x += old.x;
-          r.y += old.y;
-          r.z += old.z;
-          r.w += old.w;
-        }
-        reinterpret_cast<float4*>(o)[q] = r;
-      }
-    } else {
-      for (int i = 0; i < 32 && n0 + i < p.N; ++i) {
-        float r = v[i] + bias[i];
-        if (add_old) r += src[i];
-        o[i] = r;
+        if (EPI == EPI_BIAS_GELU) a[i] = __float2bfloat16(z[i]);
       }
     }
   }
 }
 
-template <int BN, int EPI, int A_MN, int B_MN>
+template <int BN, int EPI, int A_MN, int B_MN, int TMA_ST>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, const GemmDev p) {
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmO,
+                        const __grid_constant__ CUtensorMap tmX, const GemmDev p) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
+  constexpr bool F32_OUT = (EPI == EPI_RESID_F32 || EPI == EPI_F32);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFFSET);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -212,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], 128);
+      mbar_init(&tempty_bar[b], 32 * kEpiWarps);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -220,6 +296,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane_id() == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (TMA_ST) {
+      tma_prefetch_desc(&tmO);
+      if (EPI == EPI_BIAS_GELU) tma_prefetch_desc(&tmX);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
@@ -326,42 +406,72 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // --------------------------------------------------------- epilogue
-    const int lane_grp = warp & 3;  // TMEM lanes 32*lane_grp .. +31
-    const int row_in_tile = lane_grp * 32 + lane_id();
+    const int ew = warp - 2;              // 0..7
+    const int lg = warp & 3;              // TMEM lane quarter this warp may read
+    const int col_half = ew >> 2;         // which half of the tile's columns
+    const int lane = (int)lane_id();
+    const int r_local = lg * 32 + lane;   // row within the tile
+    constexpr int CHUNKS = BN / 64;       // 32-column chunks per warp
+    uint8_t* box = smem + Cfg::EPI_OFFSET + ew * kStageBuf;
     int acc = 0;
     uint32_t acc_phase = 0;
     float alpha = p.alpha;
     if (p.alpha_ptr) alpha *= *p.alpha_ptr;
+    EpiIn in_next;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int split = tile / tiles_per_split;
       const int rem = tile % tiles_per_split;
       const int m0 = (rem / p.n_tiles) * BM;
       const int n0 = (rem % p.n_tiles) * BN;
+      const int row = m0 + r_local;
+      const int c0 = n0 + col_half * (BN / 2);
+      load_epi_in<EPI>(p, row, c0, in_next);
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, p.err, ERR_TIMEOUT_EPILOGUE, abort_flag))
         break;
       tc_fence_after();
-      const uint32_t t_row = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + acc * BN;
-      GemmDev q = p;
-      if (EPI == EPI_F32 && p.splits > 1)
-        q.out = reinterpret_cast<float*>(p.out) + (int64_t)split * p.split_stride;
+      const uint32_t t_row =
+          tmem_base + ((uint32_t)(lg * 32) << 16) + acc * BN + col_half * (BN / 2);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
+      for (int c = 0; c < CHUNKS; ++c) {
+        float v[32], z[32];
         tmem_ld32(t_row + c * 32, v);
         tmem_wait_ld();
-        if (c == BN / 32 - 1) {
+        if (c == CHUNKS - 1) {
           tc_fence_before();
           mbar_arrive(&tempty_bar[acc]);
         }
+        EpiIn in = in_next;
+        if (c + 1 < CHUNKS) load_epi_in<EPI>(p, row, c0 + (c + 1) * 32, in_next);
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] *= alpha;
-        epilogue_chunk<EPI>(q, m0 + row_in_tile, n0 + c * 32, v);
+        epi_math<EPI>(p, c0 + c * 32, v, in, z);
+        if (TMA_ST) {
+          // the previous chunk's bulk store must have finished reading the box
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+          if (F32_OUT) {
+            stage_f32(box, lane, v);
+          } else {
+            stage_bf16(box, lane, v);
+            if (EPI == EPI_BIAS_GELU) stage_bf16(box + 2048, lane, z);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tmO, box, c0 + c * 32, m0 + lg * 32, split);
+            if (EPI == EPI_BIAS_GELU) tma_store_3d(&tmX, box + 2048, c0 + c * 32, m0 + lg * 32, 0);
+            bulk_commit();
+          }
+        } else {
+          store_direct<EPI>(p, row, c0 + c * 32, v, z, split);
+        }
       }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
       }
     }
+    if (TMA_ST && lane == 0) bulk_wait0();
   }
 
   tc_fence_before();
@@ -387,7 +497,7 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-// 2-D bf16 tensor map: inner extent `inner` (contiguous), outer extent `outer`
+// 2-D bf16 operand map: inner extent `inner` (contiguous), outer extent `outer`
 // with row stride `ld` elements; box = 64 (inner, 128 B) x box_outer; 128B swizzle.
 bool make_tmap_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer, int64_t ld,
                   uint32_t box_outer) {
@@ -403,6 +513,25 @@ bool make_tmap_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t ou
   return r == CUDA_SUCCESS;
 }
 
+// 3-D output map {N, M, S} (row stride ld, S slabs of M rows), 32x32x1 boxes,
+// swizzle 64B for bf16 / 128B for fp32 (one box row = the swizzle span).
+bool make_tmap_out(CUtensorMap* tm, const void* base, uint64_t N, uint64_t M, uint64_t S,
+                   int64_t ld, int esize) {
+  auto enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {N, M, S};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * esize,
+                           static_cast<cuuint64_t>(ld) * esize * M};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(tm, esize == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                   3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   esize == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 int num_sms() {
   static int n = 0;
   if (!n) {
@@ -413,10 +542,13 @@ int num_sms() {
   return n;
 }
 
-template <int BN, int EPI, int A_MN, int B_MN>
-int launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmDev& d, int grid,
-               cudaStream_t s) {
-  auto kern = gemm_tcgen05_kernel<BN, EPI, A_MN, B_MN>;
+struct Maps {
+  CUtensorMap a, b, o, x;
+};
+
+template <int BN, int EPI, int A_MN, int B_MN, int TMA_ST>
+int launch_cfg(const Maps& m, const GemmDev& d, int grid, cudaStream_t s) {
+  auto kern = gemm_tcgen05_kernel<BN, EPI, A_MN, B_MN, TMA_ST>;
   constexpr int smem = GemmCfg<BN>::SMEM_BYTES;
   static bool attr_set = false;
   if (!attr_set) {
@@ -425,29 +557,35 @@ int launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmDev& d, i
       return -10;
     attr_set = true;
   }
-  kern<<<grid, kThreads, smem, s>>>(ta, tb, d);
+  kern<<<grid, kThreads, smem, s>>>(m.a, m.b, m.o, m.x, d);
   count_launches(1);
   return cudaGetLastError() == cudaSuccess ? 0 : -11;
 }
 
+template <int BN, int EPI, int TMA_ST>
+int dispatch_major(int amn, int bmn, const Maps& m, const GemmDev& d, int grid, cudaStream_t s) {
+  if (!amn && !bmn) return launch_cfg<BN, EPI, 0, 0, TMA_ST>(m, d, grid, s);
+  if (!amn && bmn) return launch_cfg<BN, EPI, 0, 1, TMA_ST>(m, d, grid, s);
+  if (amn && bmn) return launch_cfg<BN, EPI, 1, 1, TMA_ST>(m, d, grid, s);
+  return launch_cfg<BN, EPI, 1, 0, TMA_ST>(m, d, grid, s);
+}
+
 template <int BN, int EPI>
-int dispatch_major(int amn, int bmn, const CUtensorMap& ta, const CUtensorMap& tb,
-                   const GemmDev& d, int grid, cudaStream_t s) {
-  if (!amn && !bmn) return launch_cfg<BN, EPI, 0, 0>(ta, tb, d, grid, s);
-  if (!amn && bmn) return launch_cfg<BN, EPI, 0, 1>(ta, tb, d, grid, s);
-  if (amn && bmn) return launch_cfg<BN, EPI, 1, 1>(ta, tb, d, grid, s);
-  return launch_cfg<BN, EPI, 1, 0>(ta, tb, d, grid, s);
+int dispatch_st(int tma_st, int amn, int bmn, const Maps& m, const GemmDev& d, int grid,
+                cudaStream_t s) {
+  return tma_st ? dispatch_major<BN, EPI, 1>(amn, bmn, m, d, grid, s)
+                : dispatch_major<BN, EPI, 0>(amn, bmn, m, d, grid, s);
 }
 
 template <int BN>
-int dispatch_epi(int epi, int amn, int bmn, const CUtensorMap& ta, const CUtensorMap& tb,
-                 const GemmDev& d, int grid, cudaStream_t s) {
+int dispatch_epi(int epi, int tma_st, int amn, int bmn, const Maps& m, const GemmDev& d, int grid,
+                 cudaStream_t s) {
   switch (epi) {
-    case EPI_BF16: return dispatch_major<BN, EPI_BF16>(amn, bmn, ta, tb, d, grid, s);
-    case EPI_BIAS_GELU: return dispatch_major<BN, EPI_BIAS_GELU>(amn, bmn, ta, tb, d, grid, s);
-    case EPI_RESID_F32: return dispatch_major<BN, EPI_RESID_F32>(amn, bmn, ta, tb, d, grid, s);
-    case EPI_F32: return dispatch_major<BN, EPI_F32>(amn, bmn, ta, tb, d, grid, s);
-    case EPI_GELU_BWD: return dispatch_major<BN, EPI_GELU_BWD>(amn, bmn, ta, tb, d, grid, s);
+    case EPI_BF16: return dispatch_st<BN, EPI_BF16>(tma_st, amn, bmn, m, d, grid, s);
+    case EPI_BIAS_GELU: return dispatch_st<BN, EPI_BIAS_GELU>(tma_st, amn, bmn, m, d, grid, s);
+    case EPI_RESID_F32: return dispatch_st<BN, EPI_RESID_F32>(tma_st, amn, bmn, m, d, grid, s);
+    case EPI_F32: return dispatch_st<BN, EPI_F32>(tma_st, amn, bmn, m, d, grid, s);
+    case EPI_GELU_BWD: return dispatch_st<BN, EPI_GELU_BWD>(tma_st, amn, bmn, m, d, grid, s);
   }
   return -3;
 }
@@ -462,7 +600,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits,
     const int64_t r = i / n4, c = (i % n4) * 4;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int s = 0; s < splits; ++s) {
-      float4 v = *reinterpret_cast<const float4*>(ws + s * split_stride + r * N + c);
+      const float4 v = __ldcs(reinterpret_cast<const float4*>(ws + s * split_stride + r * N + c));
       acc.x += v.x;
       acc.y += v.y;
       acc.z += v.z;
@@ -470,7 +608,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits,
     }
     float4* o = reinterpret_cast<float4*>(out + r * ldo + c);
     if (accumulate) {
-      float4 old = *o;
+      const float4 old = *o;
       acc.x += old.x;
       acc.y += old.y;
       acc.z += old.z;
@@ -480,27 +618,24 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits,
   }
 }
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 }  // namespace
 
 int gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return -1;
   if (a.bn != 256 && a.bn != 128) return -2;
-  // TMA: 16-byte aligned base and row stride.
-  if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15)) return -4;
+  // TMA operand loads: 16-byte aligned base and row stride.
+  if (!aligned16(a.A) || !aligned16(a.B)) return -4;
   if ((a.lda * 2) % 16 || (a.ldb * 2) % 16) return -5;
   if (a.splits > 1 && a.epilogue != EPI_F32) return -6;
-  CUtensorMap ta, tb;
+  Maps maps;
   const int BN = a.bn;
-  bool ok;
-  if (a.a_mn_major)
-    ok = make_tmap_2d(&ta, a.A, a.M, a.K, a.lda, BK);
-  else
-    ok = make_tmap_2d(&ta, a.A, a.K, a.M, a.lda, BM);
+  bool ok = a.a_mn_major ? make_tmap_2d(&maps.a, a.A, a.M, a.K, a.lda, BK)
+                         : make_tmap_2d(&maps.a, a.A, a.K, a.M, a.lda, BM);
   if (!ok) return -7;
-  if (a.b_mn_major)
-    ok = make_tmap_2d(&tb, a.B, a.N, a.K, a.ldb, BK);
-  else
-    ok = make_tmap_2d(&tb, a.B, a.K, a.N, a.ldb, BN);
+  ok = a.b_mn_major ? make_tmap_2d(&maps.b, a.B, a.N, a.K, a.ldb, BK)
+                    : make_tmap_2d(&maps.b, a.B, a.K, a.N, a.ldb, BN);
   if (!ok) return -8;
 
   GemmDev d;
@@ -526,23 +661,35 @@ int gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   d.alpha_ptr = a.alpha_ptr;
   d.alpha = a.alpha;
   d.accumulate = split_mode ? 0 : a.accumulate;
-  d.split_stride = (int64_t)a.M * a.N;
+  d.split_stride = split_mode ? (int64_t)a.M * a.N : 0;
   d.err = a.err;
   const int esz = (a.epilogue == EPI_F32 || a.epilogue == EPI_RESID_F32) ? 4 : 2;
-  bool vec = (reinterpret_cast<uintptr_t>(d.out) % 16 == 0) && ((d.ldo * esz) % 16 == 0);
+  bool vec = aligned16(d.out) && ((d.ldo * esz) % 16 == 0);
   if (a.aux)
-    vec = vec && (reinterpret_cast<uintptr_t>(a.aux) % 16 == 0) &&
+    vec = vec && aligned16(a.aux) &&
           ((a.ldaux * (a.epilogue == EPI_RESID_F32 ? 4 : 2)) % 16 == 0);
-  if (a.bias) vec = vec && (reinterpret_cast<uintptr_t>(a.bias) % 16 == 0);
-  if (split_mode) vec = vec && (d.split_stride * 4) % 16 == 0;
+  if (a.bias) vec = vec && aligned16(a.bias);
   d.vec_ok = vec ? 1 : 0;
+
+  // TMA stores need the same alignment as the vector path.
+  int tma_st = vec ? 1 : 0;
+  if (tma_st) {
+    ok = make_tmap_out(&maps.o, d.out, a.N, a.M, d.splits, d.ldo, esz);
+    if (ok && a.epilogue == EPI_BIAS_GELU) ok = make_tmap_out(&maps.x, a.aux, a.N, a.M, 1, a.ldaux, 2);
+    if (!ok) tma_st = 0;
+  }
+  if (!tma_st) {
+    maps.o = maps.a;  // unused placeholders
+    maps.x = maps.a;
+  } else if (a.epilogue != EPI_BIAS_GELU) {
+    maps.x = maps.o;
+  }
 
   const int tiles = d.m_tiles * d.n_tiles * d.splits;
   int grid = a.max_ctas > 0 ? a.max_ctas : num_sms();
   if (grid > tiles) grid = tiles;
-  int rc = BN == 256
-               ? dispatch_epi<256>(a.epilogue, a.a_mn_major, a.b_mn_major, ta, tb, d, grid, stream)
-               : dispatch_epi<128>(a.epilogue, a.a_mn_major, a.b_mn_major, ta, tb, d, grid, stream);
+  int rc = BN == 256 ? dispatch_epi<256>(a.epilogue, tma_st, a.a_mn_major, a.b_mn_major, maps, d, grid, stream)
+                     : dispatch_epi<128>(a.epilogue, tma_st, a.a_mn_major, a.b_mn_major, maps, d, grid, stream);
   if (rc != 0 || !split_mode) return rc;
   return splitk_reduce_launch(reinterpret_cast<const float*>(a.workspace), d.splits,
                               d.split_stride, reinterpret_cast<float*>(a.out), a.ldo, a.M, a.N,

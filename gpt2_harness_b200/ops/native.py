@@ -286,7 +286,7 @@ def colsum_bf16(x: torch.Tensor, out: torch.Tensor, ws: torch.Tensor, accumulate
 
 
 def colsum_ws_numel(M: int, C: int) -> int:
-    return ((M + 255) // 256) * C
+    return ((M + 127) // 128) * C
 
 
 # ----------------------------------------------------------------- embedding --
