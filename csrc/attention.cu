@@ -515,8 +515,17 @@ __global__ void __launch_bounds__(BWD_THREADS) attn_bwd_dq_kernel(const AttnArgs
 
 }  // namespace
 
+static int g_attn_impl = 0;
+void attn_set_impl(int impl) { g_attn_impl = impl; }
+int attn_get_impl() { return g_attn_impl; }
+
 int attn_fwd_launch(const AttnArgs& a, cudaStream_t s) {
   if (a.B <= 0 || a.H <= 0 || a.Tq <= 0 || a.Tk <= 0) return -1;
+  if (g_attn_impl == 0) {
+    const int rc = attn_fwd_tc_launch(a, s);
+    if (rc == 1) return 0;
+    if (rc < 0) return rc;
+  }
   const int smem = (FWD_BQ + 4 * FWD_BK) * 128;
   dim3 grid((a.Tq + FWD_BQ - 1) / FWD_BQ, a.B * a.H);
   attn_fwd_kernel<<<grid, FWD_THREADS, smem, s>>>(a);

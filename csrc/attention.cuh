@@ -25,6 +25,14 @@ struct AttnArgs {
 };
 
 int attn_fwd_launch(const AttnArgs& a, cudaStream_t s);
+
+// Tensor-core (tcgen05) forward: 1 = ran, 0 = layout not TMA-compatible.
+int attn_fwd_tc_launch(const AttnArgs& a, cudaStream_t s);
+
+// Kernel selection for the forward: 0 = tensor cores when possible (default),
+// 1 = always the mma.sync kernel (kept as a cross-check).
+void attn_set_impl(int impl);
+int attn_get_impl();
 int attn_bwd_launch(const AttnArgs& a, cudaStream_t s);
 
 }  // namespace g2b

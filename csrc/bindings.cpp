@@ -133,6 +133,10 @@ PYBIND11_MODULE(_C, m) {
           check(attn_bwd_launch(a, S(stream)), "attn_bwd");
         });
 
+  m.def("attn_set_impl", [](int impl) { attn_set_impl(impl); },
+        "0: tensor-core forward when the layout allows (default); 1: mma.sync forward");
+  m.def("attn_get_impl", []() { return attn_get_impl(); });
+
   m.def("layernorm_fwd", [](int64_t x, int64_t ldx, int64_t g, int64_t b, int64_t y, int64_t ldy,
                             int64_t mean, int64_t rstd, int M, int C, float eps, int64_t stream) {
     check(layernorm_fwd_launch(P<float>(x), ldx, P<void>(g), P<void>(b), P<void>(y), ldy,

@@ -19,6 +19,7 @@ SOURCES = [
     "csrc/bindings.cpp",
     "csrc/gemm.cu",
     "csrc/attention.cu",
+    "csrc/attention_tc.cu",
     "csrc/elementwise.cu",
     "csrc/comm.cu",
 ]

@@ -315,3 +315,26 @@ def test_bounded_wait_returns_error():
     # the context still works
     x = torch.ones(4, device=dev())
     assert x.sum().item() == 4
+
+
+@pytest.mark.parametrize("B,H,T,off,Tk", [(2, 3, 384, 0, None), (1, 2, 200, 0, None),
+                                         (1, 12, 1024, 0, None), (1, 2, 128, 256, 384)])
+def test_attention_tensor_core_matches_mma_sync(B, H, T, off, Tk):
+    """tcgen05 forward (default) vs the mma.sync forward on the same inputs."""
+    Tk = T if Tk is None else Tk
+    C = H * 64
+    q = torch.randn(B * T, C, device=dev()).bfloat16()
+    kv = torch.randn(B * Tk, 2 * C, device=dev()).bfloat16()
+    outs = []
+    L = N.lib()
+    try:
+        for impl in (0, 1):
+            L.attn_set_impl(impl)
+            o = torch.empty(B * T, C, dtype=torch.bfloat16, device=dev())
+            lse = torch.empty(B, H, T, device=dev())
+            N.attention_fwd(q, kv[:, :C], kv[:, C:], o, lse, B, H, T, Tk=Tk, q_offset=off)
+            outs.append((o.float(), lse))
+    finally:
+        L.attn_set_impl(0)
+    assert rel_err(outs[0][0], outs[1][0]) < 2e-2
+    assert (outs[0][1] - outs[1][1]).abs().max().item() < 2e-2
