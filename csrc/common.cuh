@@ -117,7 +117,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
 
-// 2-D tiled TMA load (no multicast) into this CTA's shared memory; completion is
+// 2-D tiled TMA load into this CTA's own shared memory only; completion is
 // signalled as transaction bytes on `bar`.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, uint64_t* bar,
                                             int32_t x, int32_t y) {
@@ -128,7 +128,7 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, ui
       : "memory");
 }
 
-// 3-D tiled TMA load (no multicast).
+// 3-D tiled TMA load into this CTA's own shared memory.
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, uint64_t* bar,
                                             int32_t x, int32_t y, int32_t z) {
   asm volatile(
@@ -138,7 +138,7 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, ui
       : "memory");
 }
 
-// 4-D tiled TMA load (no multicast).
+// 4-D tiled TMA load into this CTA's own shared memory.
 __device__ __forceinline__ void tma_load_4d(void* smem_dst, const void* tmap, uint64_t* bar,
                                             int32_t x, int32_t y, int32_t z, int32_t w) {
   asm volatile(
