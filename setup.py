@@ -22,6 +22,7 @@ SOURCES = [
     "csrc/attention_tc.cu",
     "csrc/elementwise.cu",
     "csrc/comm.cu",
+    "csrc/noalloc.cu",
 ]
 
 NVCC_FLAGS = [
