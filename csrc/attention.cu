@@ -537,6 +537,14 @@ int attn_bwd_launch(const AttnArgs& a, cudaStream_t s) {
   if (a.B <= 0 || a.H <= 0 || a.Tq <= 0 || a.Tk <= 0) return -1;
   const int64_t rows = (int64_t)a.B * a.H * a.Tq;
   attn_bwd_delta_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, s>>>(a);
+  if (g_attn_impl == 0) {
+    const int rc = attn_bwd_tc_launch(a, s);
+    if (rc == 1) {
+      count_launches(1);  // the delta kernel
+      return cudaGetLastError() == cudaSuccess ? 0 : -11;
+    }
+    if (rc < 0) return rc;
+  }
   const int smem_kv = 6 * BWD_B * 128 + 4 * BWD_B * 4;
   static bool attr = false;
   if (!attr) {

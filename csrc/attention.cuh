@@ -35,4 +35,8 @@ void attn_set_impl(int impl);
 int attn_get_impl();
 int attn_bwd_launch(const AttnArgs& a, cudaStream_t s);
 
+// Tensor-core (tcgen05) backward, run after delta is computed: 1 = ran,
+// 0 = layout not TMA-compatible.
+int attn_bwd_tc_launch(const AttnArgs& a, cudaStream_t s);
+
 }  // namespace g2b

@@ -20,6 +20,7 @@ SOURCES = [
     "csrc/gemm.cu",
     "csrc/attention.cu",
     "csrc/attention_tc.cu",
+    "csrc/attention_bwd_tc.cu",
     "csrc/elementwise.cu",
     "csrc/comm.cu",
     "csrc/noalloc.cu",

@@ -338,3 +338,33 @@ def test_attention_tensor_core_matches_mma_sync(B, H, T, off, Tk):
         L.attn_set_impl(0)
     assert rel_err(outs[0][0], outs[1][0]) < 2e-2
     assert (outs[0][1] - outs[1][1]).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("B,H,T,off,Tk", [(2, 3, 384, 0, None), (1, 2, 200, 0, None),
+                                         (2, 12, 1024, 0, None), (1, 2, 128, 256, 384)])
+def test_attention_backward_tensor_core_matches_mma_sync(B, H, T, off, Tk):
+    """tcgen05 backward (default) vs the mma.sync backward on the same inputs."""
+    Tk = T if Tk is None else Tk
+    C = H * 64
+    torch.manual_seed(T + H)
+    q = torch.randn(B * T, C, device=dev()).bfloat16()
+    kv = torch.randn(B * Tk, 2 * C, device=dev()).bfloat16()
+    o = torch.empty(B * T, C, dtype=torch.bfloat16, device=dev())
+    lse = torch.empty(B, H, T, device=dev())
+    N.attention_fwd(q, kv[:, :C], kv[:, C:], o, lse, B, H, T, Tk=Tk, q_offset=off)
+    do = torch.randn(B * T, C, device=dev()).bfloat16()
+    outs = []
+    L = N.lib()
+    try:
+        for impl in (0, 1):
+            L.attn_set_impl(impl)
+            dq = torch.empty_like(q)
+            dkv = torch.empty_like(kv)
+            delta = torch.empty(B, H, T, device=dev())
+            N.attention_bwd(q, kv[:, :C], kv[:, C:], o, do, dq, dkv[:, :C], dkv[:, C:], lse, delta,
+                            B, H, T, Tk=Tk, q_offset=off)
+            outs.append((dq.float(), dkv.float()))
+    finally:
+        L.attn_set_impl(0)
+    assert rel_err(outs[0][0], outs[1][0]) < 2e-2
+    assert rel_err(outs[0][1], outs[1][1]) < 2e-2
