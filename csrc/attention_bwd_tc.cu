@@ -4,21 +4,27 @@
 // Q/K/V/O/dO/dQ/dK/dV, log2-domain LSE from the forward, delta = rowsum(dO*O)
 // computed first), deterministic (no atomics), re-designed around tcgen05:
 //
-//  MODE_KV  one CTA owns 128 keys (K_j, V_j stay in shared memory) and walks
-//           the 128-query blocks that can see them. Per block:
+//  MODE_KV  a tile is 128 keys (K_j, V_j stay in shared memory); the CTA walks
+//           the 64-query steps that can see them. Per step:
 //             S^T  = K Q^T    and   dP^T = V dO^T        (two MMAs -> TMEM)
 //             P^T  = 2^(S^T*scale*log2e - LSE[q])   (masked),
 //             dS^T = P^T * (dP^T - delta[q])              (8 warps, -> smem)
 //             dV  += P^T dO   and   dK  += dS^T Q        (TMEM accumulators)
-//  MODE_Q   one CTA owns 128 queries (Q_i, dO_i stay) and walks the key blocks
-//           they can see:  S = Q K^T, dP = dO V^T, P and dS as above,
+//  MODE_Q   a tile is 128 queries (Q_i, dO_i stay); the CTA walks the 64-key
+//           steps they can see:  S = Q K^T, dP = dO V^T, P and dS as above,
 //             dQ  += dS K.
+//
+// Pipelining. S/dP live in two TMEM buffers (64 columns each per step), and
+// P/dS in two shared-memory buffers, so while the elementwise warps turn step
+// g into P/dS, the tensor core accumulates step g-1 and computes S/dP of
+// step g+1. The kernel is persistent (one CTA per SM, heavy tiles first under
+// the causal mask) with two TMEM accumulator sets, so the write-out of one
+// tile overlaps the first steps of the next. In MODE_KV the producer warp
+// stages each step's 64 LSE / delta values next to the Q/dO tiles.
 //
 // A query/key tile is loaded once (TMA, 128B swizzle, rows = sequence
 // positions, 64 contiguous head dims): it is the K-major operand of the first
 // MMAs and, unchanged, the MN-major operand of the accumulating ones.
-// Elementwise work needs no row reductions in backward, so the 128x128 tile is
-// split by columns across two warps per TMEM lane quarter (8 warps).
 // All mbarrier waits are bounded (ERR_TIMEOUT_ATTN).
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -35,23 +41,27 @@ PFN_cuTensorMapEncodeTiled_v12000 attn_get_encode_fn();
 namespace {
 
 constexpr int MODE_KV = 0, MODE_Q = 1;
-constexpr int TB = 128;                       // rows per tile
-constexpr int TILE = TB * 128;                // 128 rows x 64 bf16
-constexpr int STAGES = 2;                     // streaming-operand ring
+constexpr int TB = 128;                       // stationary rows per tile
+constexpr int SB = 64;                        // streaming rows per step
+constexpr int ATILE = TB * 128;               // 128 rows x 64 bf16 (16 KB)
+constexpr int XTILE = SB * 128;               // 64 rows x 64 bf16 (8 KB)
+constexpr int STAGES = 4;                     // streaming-operand ring
 constexpr int kThreads = 64 + 256;
-// smem: stationary A (16K), stationary A2 (16K), ring of 2 x (X 16K + Y 16K),
-// P tile (2 x 16K chunks), dS tile (2 x 16K chunks)
+// smem: stationary A, A2 (16 KB each); ring of STAGES x (X 8K + Y 8K);
+// P and dS double buffers (128 rows x 64 cols bf16 = 16 KB each);
+// per-stage LSE/delta (2 x 64 floats); barriers.
 constexpr int SA_OFF = 0;
-constexpr int SA2_OFF = SA_OFF + TILE;
-constexpr int RING_OFF = SA2_OFF + TILE;
-constexpr int P_OFF = RING_OFF + STAGES * 2 * TILE;
-constexpr int DS_OFF = P_OFF + 2 * TILE;
-constexpr int BAR_OFF = DS_OFF + 2 * TILE;
+constexpr int SA2_OFF = SA_OFF + ATILE;
+constexpr int RING_OFF = SA2_OFF + ATILE;
+constexpr int P_OFF = RING_OFF + STAGES * 2 * XTILE;
+constexpr int DS_OFF = P_OFF + 2 * ATILE;
+constexpr int LD_OFF = DS_OFF + 2 * ATILE;
+constexpr int BAR_OFF = LD_OFF + STAGES * 2 * SB * 4;
 constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct BwdParams {
-  int H, Tq, Tk, q_offset, causal;
+  int H, BH, Tq, Tk, q_offset, causal, n_blk, n_tiles;
   float sl2, scale;
   const float* lse;
   const float* delta;
@@ -67,14 +77,42 @@ __device__ __forceinline__ float ex2f(float x) {
   return y;
 }
 
-// Write 32 values (quarter `c` of row half `half`) as bf16 into a K-major
-// 128B-swizzled tile made of two 16 KB chunks of 64 columns.
-__device__ __forceinline__ void put_row_quarter(uint8_t* tile, int r, int half, int c,
-                                                const float* v) {
-  uint8_t* base = tile + half * TILE + r * 128;
+// Tile t of the persistent schedule: (batch*head, first stationary row,
+// first streaming row, number of 64-row steps).
+struct TileInfo {
+  int bh, r0, s0, n;
+};
+
+template <int MODE>
+__device__ __forceinline__ TileInfo tile_info(const BwdParams& p, int t) {
+  TileInfo ti;
+  // Heaviest blocks first: under the causal mask the work of a key block
+  // falls with its index (MODE_KV) and that of a query block rises (MODE_Q).
+  const int rank = t / p.BH;
+  ti.bh = t % p.BH;
+  const int blk = (MODE == MODE_KV) ? rank : (p.n_blk - 1 - rank);
+  ti.r0 = blk * TB;
+  if (MODE == MODE_KV) {
+    int q0 = p.causal ? max(0, ti.r0 - p.q_offset) : 0;
+    q0 = (q0 / SB) * SB;
+    ti.s0 = q0;
+    ti.n = (ti.r0 < p.Tk && q0 < p.Tq) ? (p.Tq - q0 + SB - 1) / SB : 0;
+  } else {
+    int kv_end = p.Tk;
+    if (p.causal) kv_end = min(p.Tk, p.q_offset + ti.r0 + TB);
+    ti.s0 = 0;
+    ti.n = (ti.r0 < p.Tq && kv_end > 0) ? (kv_end + SB - 1) / SB : 0;
+  }
+  return ti;
+}
+
+// Write 32 values (columns 32*half .. +32 of row r) as bf16 into a K-major
+// 128B-swizzled 128x64 tile.
+__device__ __forceinline__ void put_row_half(uint8_t* tile, int r, int half, const float* v) {
+  uint8_t* base = tile + r * 128;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const int q = c * 4 + j;
+    const int q = half * 4 + j;
     uint4 w;
     w.x = pack_bf16x2(v[j * 8 + 0], v[j * 8 + 1]);
     w.y = pack_bf16x2(v[j * 8 + 2], v[j * 8 + 3]);
@@ -89,50 +127,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
                        const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmY,
                        const BwdParams p) {
-  // MODE_KV: A = K, A2 = V (stationary); X = Q_i, Y = dO_i (streaming)
-  // MODE_Q : A = Q, A2 = dO (stationary); X = K_j, Y = V_j (streaming)
+  // MODE_KV: A = K, A2 = V (stationary); X = Q, Y = dO (streaming)
+  // MODE_Q : A = Q, A2 = dO (stationary); X = K, Y = V (streaming)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
-  uint64_t* a_full = bars;                 // 1
-  uint64_t* x_full = bars + 1;             // STAGES
-  uint64_t* x_empty = x_full + STAGES;     // STAGES
-  uint64_t* s_full = x_empty + STAGES;     // 1: S and dP ready in TMEM
-  uint64_t* e_full = s_full + 1;           // 1: P / dS written to smem (256 arrivals)
-  uint64_t* e_free = e_full + 1;           // 1: accumulating MMAs done with P / dS
-  uint64_t* acc_full = e_free + 1;         // 1: final accumulators ready
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* a_full = bars;                 // stationary tiles landed
+  uint64_t* a_empty = bars + 1;            // last S/dP MMA of the tile done
+  uint64_t* x_full = bars + 2;             // [STAGES]
+  uint64_t* x_empty = x_full + STAGES;     // [STAGES]
+  uint64_t* s_full = x_empty + STAGES;     // [2] S/dP of a step in TMEM
+  uint64_t* e_full = s_full + 2;           // [2] P/dS in smem, S/dP consumed (256 arrivals)
+  uint64_t* pds_free = e_full + 2;         // [2] accumulating MMAs done with P/dS
+  uint64_t* acc_full = pds_free + 2;       // [2] tile accumulators final
+  uint64_t* acc_empty = acc_full + 2;      // [2] accumulators drained (256 arrivals)
+  uint64_t* drain = acc_empty + 2;         // abort path: issued MMAs retired
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* ld_smem = reinterpret_cast<float*>(smem + LD_OFF);  // [STAGES][2][SB]
 
   const int warp = threadIdx.x >> 5;
-  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
-  const int blk = (MODE == MODE_Q) ? (gridDim.x - 1 - blockIdx.x) : blockIdx.x;
-  const int r0 = blk * TB;  // first key (KV) / query (Q) row of this CTA
-
-  // Range of streaming blocks.
-  int it0 = 0, it1 = 0;
-  if (MODE == MODE_KV) {
-    const int nq = (p.Tq + TB - 1) / TB;
-    it0 = p.causal ? max(0, (r0 - p.q_offset) / TB) : 0;
-    it1 = (r0 < p.Tk) ? nq : 0;
-  } else {
-    int kv_end = p.Tk;
-    if (p.causal) kv_end = min(p.Tk, p.q_offset + r0 + TB);
-    it1 = (r0 < p.Tq && kv_end > 0) ? (kv_end + TB - 1) / TB : 0;
-  }
-  const int n_it = max(0, it1 - it0);
 
   if (threadIdx.x == 0) {
     mbar_init(a_full, 1);
+    mbar_init(a_empty, 1);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&x_full[s], 1);
       mbar_init(&x_empty[s], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(e_full, 256);
-    mbar_init(e_free, 1);
-    mbar_init(acc_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&e_full[i], 256);
+      mbar_init(&pds_free[i], 1);
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 256);
+    }
+    mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -144,156 +175,284 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: S [0,128) dP [128,256) acc1 [256,320) acc2 [320,384)
-  const uint32_t T_S = 0, T_DP = 128, T_A1 = 256, T_A2 = 320;
+  // TMEM columns: S/dP buffer i at [128 i, 128 i + 128) (S then dP, 64 each);
+  // accumulator set j at 256 + 128 j: acc1 (+0, 64 cols), acc2 (+64, 64 cols).
+  constexpr uint32_t T_ACC = 256;
 
   if (warp == 0) {
-    if (elect_one() && n_it > 0) {
-      mbar_arrive_expect_tx(a_full, 2 * TILE);
-      tma_load_4d(smem + SA_OFF, &tmA, a_full, 0, h, r0, b);
-      tma_load_4d(smem + SA2_OFF, &tmA2, a_full, 0, h, r0, b);
-      for (int k = 0; k < n_it; ++k) {
-        const int st = k % STAGES;
-        if (!mbar_wait_bounded(&x_empty[st], ((k / STAGES) & 1) ^ 1, p.err, ERR_TIMEOUT_ATTN,
-                               abort_flag))
-          break;
-        mbar_arrive_expect_tx(&x_full[st], 2 * TILE);
-        const int row = (it0 + k) * TB;
-        tma_load_4d(smem + RING_OFF + st * 2 * TILE, &tmX, &x_full[st], 0, h, row, b);
-        tma_load_4d(smem + RING_OFF + st * 2 * TILE + TILE, &tmY, &x_full[st], 0, h, row, b);
+    // ------------------------------------------------------------ producer
+    const int lane = (int)lane_id();
+    uint32_t g = 0, i = 0, a_issued = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.n_tiles && ok; t += gridDim.x) {
+      const TileInfo ti = tile_info<MODE>(p, t);
+      if (ti.n == 0) continue;
+      const int b = ti.bh / p.H, h = ti.bh % p.H;
+      if (!mbar_wait_bounded(a_empty, (i & 1) ^ 1, p.err, ERR_TIMEOUT_ATTN, abort_flag)) {
+        ok = false;
+        break;
       }
-    }
-  } else if (warp == 1) {
-    if (elect_one() && n_it > 0) {
-      constexpr uint32_t id_ss = umma_idesc_bf16(128, 128, 0, 0);  // K-major x K-major
-      constexpr uint32_t id_acc = umma_idesc_bf16(128, 64, 0, 1);  // K-major A, MN-major B
-      const uint32_t sa = smem_u32(smem + SA_OFF), sa2 = smem_u32(smem + SA2_OFF);
-      const uint32_t sp = smem_u32(smem + P_OFF), sds = smem_u32(smem + DS_OFF);
-      bool ok = mbar_wait_bounded(a_full, 0, p.err, ERR_TIMEOUT_ATTN, abort_flag);
-      for (int k = 0; k < n_it && ok; ++k) {
-        const int st = k % STAGES;
-        if (!mbar_wait_bounded(&x_full[st], (k / STAGES) & 1, p.err, ERR_TIMEOUT_ATTN, abort_flag)) {
+      if (lane == 0) {
+        mbar_arrive_expect_tx(a_full, 2 * ATILE);
+        tma_load_4d(smem + SA_OFF, &tmA, a_full, 0, h, ti.r0, b);
+        tma_load_4d(smem + SA2_OFF, &tmA2, a_full, 0, h, ti.r0, b);
+      }
+      ++a_issued;
+      for (int j = 0; j < ti.n; ++j, ++g) {
+        const uint32_t st = g % STAGES;
+        if (!mbar_wait_bounded(&x_empty[st], ((g / STAGES) & 1) ^ 1, p.err, ERR_TIMEOUT_ATTN,
+                               abort_flag)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        const uint32_t sx = smem_u32(smem + RING_OFF + st * 2 * TILE), sy = sx + TILE;
-        // S(^T) = A X^T and dP(^T) = A2 Y^T  (K = head dim 64)
+        const int row = ti.s0 + j * SB;
+        if (MODE == MODE_KV) {
+          // stage the step's LSE and delta (queries row .. row+63)
+          float* dst = ld_smem + st * 2 * SB;
+          const int64_t base = (int64_t)ti.bh * p.Tq;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          umma_bf16(tmem + T_S, umma_desc_sw128(sa + kk * 32, 16, 1024),
-                    umma_desc_sw128(sx + kk * 32, 16, 1024), id_ss, kk > 0 ? 1u : 0u);
-          umma_bf16(tmem + T_DP, umma_desc_sw128(sa2 + kk * 32, 16, 1024),
-                    umma_desc_sw128(sy + kk * 32, 16, 1024), id_ss, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(s_full);
-        // P / dS written by the elementwise warps (they have also consumed S, dP)
-        if (!mbar_wait_bounded(e_full, k & 1, p.err, ERR_TIMEOUT_ATTN, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        // accumulate over the streaming dimension (K = 128 rows of the tile)
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t off = (ks >> 2) * TILE + (ks & 3) * 32;
-          const uint32_t acc = (k > 0 || ks > 0) ? 1u : 0u;
-          if (MODE == MODE_KV) {
-            // dV += P^T dO ; dK += dS^T Q
-            umma_bf16(tmem + T_A2, umma_desc_sw128(sp + off, 16, 1024),
-                      umma_desc_sw128(sy + ks * 2048, 8192, 1024), id_acc, acc);
-            umma_bf16(tmem + T_A1, umma_desc_sw128(sds + off, 16, 1024),
-                      umma_desc_sw128(sx + ks * 2048, 8192, 1024), id_acc, acc);
-          } else {
-            // dQ += dS K
-            umma_bf16(tmem + T_A1, umma_desc_sw128(sds + off, 16, 1024),
-                      umma_desc_sw128(sx + ks * 2048, 8192, 1024), id_acc, acc);
+          for (int u = 0; u < 2; ++u) {
+            const int q = row + u * 32 + lane;
+            const bool in = q < p.Tq;
+            dst[u * 32 + lane] = in ? __ldg(p.lse + base + q) : 0.f;
+            dst[SB + u * 32 + lane] = in ? __ldg(p.delta + base + q) : 0.f;
           }
+          __syncwarp();
         }
-        umma_commit(e_free);
-        umma_commit(&x_empty[st]);
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&x_full[st], 2 * XTILE);
+          uint8_t* xs = smem + RING_OFF + st * 2 * XTILE;
+          tma_load_4d(xs, &tmX, &x_full[st], 0, h, row, b);
+          tma_load_4d(xs + XTILE, &tmY, &x_full[st], 0, h, row, b);
+        }
+        __syncwarp();
       }
-      if (ok) umma_commit(acc_full);
+      ++i;
+    }
+    if (*abort_flag && lane == 0) {
+      // Another role gave up: wait (bounded) for this warp's copies still in
+      // flight before the CTA's shared memory is released.
+      if (a_issued) mbar_wait_bounded(a_full, (a_issued - 1) & 1, p.err, ERR_TIMEOUT_ATTN, nullptr);
+      for (uint32_t gg = g > STAGES ? g - STAGES : 0; gg < g; ++gg)
+        mbar_wait_bounded(&x_full[gg % STAGES], (gg / STAGES) & 1, p.err, ERR_TIMEOUT_ATTN, nullptr);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t id_ss = umma_idesc_bf16(128, SB, 0, 0);  // K-major x K-major
+      constexpr uint32_t id_acc = umma_idesc_bf16(128, 64, 0, 1); // K-major A, MN-major B
+      const uint32_t sa = smem_u32(smem + SA_OFF), sa2 = smem_u32(smem + SA2_OFF);
+      const uint32_t sp0 = smem_u32(smem + P_OFF), sds0 = smem_u32(smem + DS_OFF);
+      const uint32_t ring = smem_u32(smem + RING_OFF);
+      uint32_t g = 0, i = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.n_tiles && ok; t += gridDim.x) {
+        const TileInfo ti = tile_info<MODE>(p, t);
+        if (ti.n == 0) continue;
+        const uint32_t acc_base = tmem + T_ACC + (i & 1) * 128;
+        if (!mbar_wait_bounded(a_full, i & 1, p.err, ERR_TIMEOUT_ATTN, abort_flag) ||
+            !mbar_wait_bounded(&acc_empty[i & 1], ((i >> 1) & 1) ^ 1, p.err, ERR_TIMEOUT_ATTN,
+                               abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // S(^T) = A X^T and dP(^T) = A2 Y^T for global step gg (K = head dim)
+        auto issue_sd = [&](uint32_t gg, bool last) -> bool {
+          const uint32_t st = gg % STAGES;
+          if (!mbar_wait_bounded(&x_full[st], (gg / STAGES) & 1, p.err, ERR_TIMEOUT_ATTN, abort_flag))
+            return false;
+          tc_fence_after();
+          const uint32_t sx = ring + st * 2 * XTILE, sy = sx + XTILE;
+          const uint32_t tb = tmem + (gg & 1) * 128;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            umma_bf16(tb, umma_desc_sw128(sa + kk * 32, 16, 1024),
+                      umma_desc_sw128(sx + kk * 32, 16, 1024), id_ss, kk > 0 ? 1u : 0u);
+            umma_bf16(tb + SB, umma_desc_sw128(sa2 + kk * 32, 16, 1024),
+                      umma_desc_sw128(sy + kk * 32, 16, 1024), id_ss, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[gg & 1]);
+          if (last) umma_commit(a_empty);
+          return true;
+        };
+        ok = issue_sd(g, ti.n == 1);
+        if (ok && ti.n > 1) ok = issue_sd(g + 1, ti.n == 2);
+        for (int j = 0; j < ti.n && ok; ++j, ++g) {
+          const uint32_t pb = g & 1, st = g % STAGES;
+          if (!mbar_wait_bounded(&e_full[pb], (g >> 1) & 1, p.err, ERR_TIMEOUT_ATTN, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sx = ring + st * 2 * XTILE, sy = sx + XTILE;
+          const uint32_t sp = sp0 + pb * ATILE, sds = sds0 + pb * ATILE;
+          // accumulate over the streaming dimension (K = 64 rows of the step)
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint32_t acc = (j > 0 || ks > 0) ? 1u : 0u;
+            if (MODE == MODE_KV) {
+              // dV += P^T dO ; dK += dS^T Q
+              umma_bf16(acc_base + 64, umma_desc_sw128(sp + ks * 32, 16, 1024),
+                        umma_desc_sw128(sy + ks * 2048, 8192, 1024), id_acc, acc);
+              umma_bf16(acc_base, umma_desc_sw128(sds + ks * 32, 16, 1024),
+                        umma_desc_sw128(sx + ks * 2048, 8192, 1024), id_acc, acc);
+            } else {
+              // dQ += dS K
+              umma_bf16(acc_base, umma_desc_sw128(sds + ks * 32, 16, 1024),
+                        umma_desc_sw128(sx + ks * 2048, 8192, 1024), id_acc, acc);
+            }
+          }
+          umma_commit(&pds_free[pb]);
+          umma_commit(&x_empty[st]);
+          if (j + 2 < ti.n) ok = issue_sd(g + 2, j + 3 == ti.n);
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[i & 1]);
+        ++i;
+      }
+      if (*abort_flag) {
+        // retire every MMA issued so far before TMEM is released
+        umma_commit(drain);
+        mbar_wait_bounded(drain, 0, p.err, ERR_TIMEOUT_ATTN, nullptr);
+      }
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------- elementwise
     const int ew = warp - 2;
     const int lg = warp & 3;
-    const int half = ew >> 2;             // which 64 columns of the 128
+    const int half = ew >> 2;             // which 32 columns of the 64-wide step
     const int lane = (int)lane_id();
     const int r = lg * 32 + lane;         // row of the tile (TMEM lane)
-    const int row_pos = r0 + r;           // key (KV) or query (Q) position
-    const uint32_t lane_base = tmem + ((uint32_t)(lg * 32) << 16);
-    uint8_t* ptile = smem + P_OFF;
-    uint8_t* dstile = smem + DS_OFF;
-    // MODE_Q: per-row LSE / delta
-    float row_lse = 0.f, row_delta = 0.f;
-    if (MODE == MODE_Q && row_pos < p.Tq) {
-      row_lse = p.lse[(int64_t)bh * p.Tq + row_pos];
-      row_delta = p.delta[(int64_t)bh * p.Tq + row_pos];
-    }
-    const int abs_row = (MODE == MODE_Q) ? p.q_offset + row_pos : row_pos;
+    const uint32_t lane_off = (uint32_t)(lg * 32) << 16;
+    uint8_t* ptile0 = smem + P_OFF;
+    uint8_t* dstile0 = smem + DS_OFF;
+    uint32_t g = 0, i = 0;
     bool ok = true;
-    for (int k = 0; k < n_it && ok; ++k) {
-      const int c0 = (it0 + k) * TB + half * 64;  // first column position of this half
-      if (!mbar_wait_bounded(s_full, k & 1, p.err, ERR_TIMEOUT_ATTN, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      // P/dS smem is free once the previous accumulation finished; MMAs
-      // complete in issue order, so that happened before S/dP(k) landed.
-      if (k > 0 && !mbar_wait_bounded(e_free, (k - 1) & 1, p.err, ERR_TIMEOUT_ATTN, abort_flag)) {
-        ok = false;
-        break;
-      }
+    for (int t = blockIdx.x; t < p.n_tiles && ok; t += gridDim.x) {
+      const TileInfo ti = tile_info<MODE>(p, t);
+      const int b = ti.bh / p.H, h = ti.bh % p.H;
+      const int row_pos = ti.r0 + r;      // key (KV) or query (Q) position
+      const bool row_in = (MODE == MODE_KV) ? row_pos < p.Tk : row_pos < p.Tq;
+      if (ti.n == 0) {
+        // no visible partner: the gradient of these rows is zero
+        if (row_in) {
+          const int nacc = (MODE == MODE_KV) ? 2 : 1;
+          for (int a = 0; a < nacc; ++a) {
+            __nv_bfloat16* dst = (a == 0) ? p.out1 + (int64_t)b * p.o1_sb + (int64_t)row_pos * p.o1_st +
+                                                (int64_t)h * p.o1_sh
+                                          : p.out2 + (int64_t)b * p.o2_sb + (int64_t)row_pos * p.o2_st +
+                                                (int64_t)h * p.o2_sh;
+            dst += half * 32;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+            for (int q = 0; q < 4; ++q) reinterpret_cast<uint4*>(dst)[q] = make_uint4(0, 0, 0, 0);
+          }
+        }
+        continue;
+      }
+      // MODE_Q: per-row LSE / delta
+      float row_lse = 0.f, row_delta = 0.f;
+      if (MODE == MODE_Q && row_in) {
+        row_lse = __ldg(p.lse + (int64_t)ti.bh * p.Tq + row_pos);
+        row_delta = __ldg(p.delta + (int64_t)ti.bh * p.Tq + row_pos);
+      }
+      const int abs_row = (MODE == MODE_Q) ? p.q_offset + row_pos : row_pos;
+      // tile rows are the stationary block [r0, r0 + 128)
+      const int last_row = ti.r0 + TB - 1;
+      const bool rows_full = (MODE == MODE_KV) ? last_row < p.Tk : last_row < p.Tq;
+      for (int j = 0; j < ti.n; ++j, ++g) {
+        const uint32_t pb = g & 1, st = g % STAGES;
+        const int c0 = ti.s0 + j * SB + half * 32;  // first column position of this thread
+        // Block-uniform: is every element of this step visible?
+        const int cs = ti.s0 + j * SB, ce = cs + SB;  // step columns [cs, ce)
+        bool full;
+        if (MODE == MODE_KV)
+          full = rows_full && ce <= p.Tq && (!p.causal || p.q_offset + cs >= last_row);
+        else
+          full = rows_full && ce <= p.Tk && (!p.causal || ce - 1 <= p.q_offset + ti.r0);
+        if (!mbar_wait_bounded(&s_full[pb], (g >> 1) & 1, p.err, ERR_TIMEOUT_ATTN, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
         uint32_t sv[32], dv[32];
-        tmem_ld32_async(lane_base + T_S + half * 64 + c * 32, sv);
-        tmem_ld32_async(lane_base + T_DP + half * 64 + c * 32, dv);
+        const uint32_t tb = tmem + lane_off + pb * 128 + half * 32;
+        tmem_ld32_async(tb, sv);
+        tmem_ld32_async(tb + SB, dv);
+        // P/dS buffer pb is free once the accumulation of step g-2 finished
+        if (!mbar_wait_bounded(&pds_free[pb], ((g >> 1) & 1) ^ 1, p.err, ERR_TIMEOUT_ATTN,
+                               abort_flag)) {
+          tmem_wait_ld_into(sv);
+          tmem_wait_ld_into(dv);
+          ok = false;
+          break;
+        }
         tmem_wait_ld_into(sv);
         tmem_wait_ld_into(dv);
         float pv[32], dsv[32];
+        if (MODE == MODE_KV) {
+          const float4* lse4 = reinterpret_cast<const float4*>(ld_smem + st * 2 * SB + half * 32);
+          const float4* dl4 = reinterpret_cast<const float4*>(ld_smem + st * 2 * SB + SB + half * 32);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int col = c0 + c * 32 + i;
-          const float sc = __uint_as_float(sv[i]);
-          const float dp = __uint_as_float(dv[i]);
-          float lse, dl;
-          bool vis;
-          if (MODE == MODE_KV) {
-            const bool in = col < p.Tq;
-            lse = in ? __ldg(p.lse + (int64_t)bh * p.Tq + col) : 0.f;
-            dl = in ? __ldg(p.delta + (int64_t)bh * p.Tq + col) : 0.f;
-            vis = in && row_pos < p.Tk && (!p.causal || p.q_offset + col >= abs_row);
-          } else {
-            lse = row_lse;
-            dl = row_delta;
-            vis = col < p.Tk && row_pos < p.Tq && (!p.causal || col <= abs_row);
+          for (int q = 0; q < 8; ++q) {
+            const float4 l = lse4[q], d = dl4[q];
+            const float la[4] = {l.x, l.y, l.z, l.w}, da[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int ii = q * 4 + u;
+              float pr = ex2f(fmaf(__uint_as_float(sv[ii]), p.sl2, -la[u]));
+              if (!full) {
+                const int col = c0 + ii;
+                const bool vis = col < p.Tq && row_in && (!p.causal || p.q_offset + col >= abs_row);
+                pr = vis ? pr : 0.f;
+              }
+              pv[ii] = pr;
+              dsv[ii] = pr * (__uint_as_float(dv[ii]) - da[u]);
+            }
           }
-          const float pr = vis ? ex2f(fmaf(sc, p.sl2, -lse)) : 0.f;
-          pv[i] = pr;
-          dsv[i] = pr * (dp - dl);
+          put_row_half(ptile0 + pb * ATILE, r, half, pv);
+        } else {
+#pragma unroll
+          for (int ii = 0; ii < 32; ++ii) {
+            float pr = ex2f(fmaf(__uint_as_float(sv[ii]), p.sl2, -row_lse));
+            if (!full) {
+              const int col = c0 + ii;
+              const bool vis = col < p.Tk && row_in && (!p.causal || col <= abs_row);
+              pr = vis ? pr : 0.f;
+            }
+            dsv[ii] = pr * (__uint_as_float(dv[ii]) - row_delta);
+          }
         }
-        if (MODE == MODE_KV) put_row_quarter(ptile, r, half, c, pv);
-        put_row_quarter(dstile, r, half, c, dsv);
+        put_row_half(dstile0 + pb * ATILE, r, half, dsv);
+        fence_proxy_async_shared();
+        tc_fence_before();
+        mbar_arrive(&e_full[pb]);
       }
-      fence_proxy_async_shared();
-      tc_fence_before();
-      mbar_arrive(e_full);
-    }
-    // final accumulators -> global (each warp writes its 32 rows, its half of d)
-    if (ok && n_it > 0 && mbar_wait_bounded(acc_full, 0, p.err, ERR_TIMEOUT_ATTN, abort_flag)) {
+      if (!ok) break;
+      // final accumulators -> global (each warp writes its 32 rows, its half of d)
+      if (!mbar_wait_bounded(&acc_full[i & 1], (i >> 1) & 1, p.err, ERR_TIMEOUT_ATTN, abort_flag)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
-      const int nacc = (MODE == MODE_KV) ? 2 : 1;
-      for (int a = 0; a < nacc; ++a) {
-        uint32_t v[32];
-        tmem_ld32_async(lane_base + (a == 0 ? T_A1 : T_A2) + half * 32, v);
-        tmem_wait_ld_into(v);
-        const bool inb = (MODE == MODE_KV) ? row_pos < p.Tk : row_pos < p.Tq;
-        if (inb) {
+      const uint32_t acc_base = tmem + lane_off + T_ACC + (i & 1) * 128;
+      uint32_t v1[32], v2[32];
+      tmem_ld32_async(acc_base + half * 32, v1);
+      tmem_wait_ld_into(v1);
+      if (MODE == MODE_KV) {
+        tmem_ld32_async(acc_base + 64 + half * 32, v2);
+        tmem_wait_ld_into(v2);
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[i & 1]);
+      ++i;
+      if (row_in) {
+        const int nacc = (MODE == MODE_KV) ? 2 : 1;
+#pragma unroll
+        for (int a = 0; a < nacc; ++a) {
+          const uint32_t* v = a == 0 ? v1 : v2;
           const float sc = (a == 0) ? p.scale : 1.f;  // dK / dQ carry the softmax scale
           __nv_bfloat16* dst = (a == 0) ? p.out1 + (int64_t)b * p.o1_sb + (int64_t)row_pos * p.o1_st +
                                               (int64_t)h * p.o1_sh
@@ -311,21 +470,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-    } else if (n_it == 0) {
-      // no visible partner block: the gradient of this row is zero
-      const bool inb = (MODE == MODE_KV) ? row_pos < p.Tk : row_pos < p.Tq;
-      if (inb) {
-        const int nacc = (MODE == MODE_KV) ? 2 : 1;
-        for (int a = 0; a < nacc; ++a) {
-          __nv_bfloat16* dst = (a == 0) ? p.out1 + (int64_t)b * p.o1_sb + (int64_t)row_pos * p.o1_st +
-                                              (int64_t)h * p.o1_sh
-                                        : p.out2 + (int64_t)b * p.o2_sb + (int64_t)row_pos * p.o2_st +
-                                              (int64_t)h * p.o2_sh;
-          dst += half * 32;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) reinterpret_cast<uint4*>(dst)[q] = make_uint4(0, 0, 0, 0);
-        }
-      }
     }
   }
 
@@ -337,12 +481,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-bool head_map(CUtensorMap* tm, const HeadView& v, int H, int T, int B) {
+bool head_map(CUtensorMap* tm, const HeadView& v, int H, int T, int B, int rows) {
   auto enc = attn_get_encode_fn();
   if (!enc) return false;
   cuuint64_t dims[4] = {64, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)v.sh * 2, (cuuint64_t)v.st * 2, (cuuint64_t)v.sb * 2};
-  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t box[4] = {64, 1, (cuuint32_t)rows, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   return enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, v.base, dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -359,9 +503,20 @@ bool out_ok(const HeadView& v) {
          (v.st * 2) % 16 == 0;
 }
 
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
 template <int MODE>
 int launch_mode(const CUtensorMap& a, const CUtensorMap& a2, const CUtensorMap& x,
-                const CUtensorMap& y, const BwdParams& p, dim3 grid, cudaStream_t s) {
+                const CUtensorMap& y, const BwdParams& p, cudaStream_t s) {
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(attn_bwd_tc_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -369,6 +524,7 @@ int launch_mode(const CUtensorMap& a, const CUtensorMap& a2, const CUtensorMap& 
       return -10;
     attr = true;
   }
+  const int grid = p.n_tiles < num_sms() ? p.n_tiles : num_sms();
   attn_bwd_tc_kernel<MODE><<<grid, kThreads, SMEM_BYTES, s>>>(a, a2, x, y, p);
   count_launches(1);
   return cudaGetLastError() == cudaSuccess ? 0 : -11;
@@ -382,12 +538,16 @@ int attn_bwd_tc_launch(const AttnArgs& a, cudaStream_t s) {
   if (!tma_ok(a.q) || !tma_ok(a.k) || !tma_ok(a.v) || !tma_ok(a.dout) || !out_ok(a.dq) ||
       !out_ok(a.dk) || !out_ok(a.dv))
     return 0;
-  CUtensorMap tq, tk, tv, tdo;
-  if (!head_map(&tq, a.q, a.H, a.Tq, a.B) || !head_map(&tk, a.k, a.H, a.Tk, a.B) ||
-      !head_map(&tv, a.v, a.H, a.Tk, a.B) || !head_map(&tdo, a.dout, a.H, a.Tq, a.B))
+  if (a.B * a.H <= 0 || a.Tq <= 0 || a.Tk <= 0) return 0;
+  CUtensorMap tq_a, tk_a, tv_a, tdo_a, tq_x, tk_x, tv_x, tdo_x;
+  if (!head_map(&tq_a, a.q, a.H, a.Tq, a.B, TB) || !head_map(&tk_a, a.k, a.H, a.Tk, a.B, TB) ||
+      !head_map(&tv_a, a.v, a.H, a.Tk, a.B, TB) || !head_map(&tdo_a, a.dout, a.H, a.Tq, a.B, TB) ||
+      !head_map(&tq_x, a.q, a.H, a.Tq, a.B, SB) || !head_map(&tk_x, a.k, a.H, a.Tk, a.B, SB) ||
+      !head_map(&tv_x, a.v, a.H, a.Tk, a.B, SB) || !head_map(&tdo_x, a.dout, a.H, a.Tq, a.B, SB))
     return 0;
   BwdParams p;
   p.H = a.H;
+  p.BH = a.B * a.H;
   p.Tq = a.Tq;
   p.Tk = a.Tk;
   p.q_offset = a.q_offset;
@@ -406,7 +566,9 @@ int attn_bwd_tc_launch(const AttnArgs& a, cudaStream_t s) {
   p.o2_sb = a.dv.sb;
   p.o2_st = a.dv.st;
   p.o2_sh = a.dv.sh;
-  int rc = launch_mode<MODE_KV>(tk, tv, tq, tdo, p, dim3((a.Tk + TB - 1) / TB, a.B * a.H), s);
+  p.n_blk = (a.Tk + TB - 1) / TB;
+  p.n_tiles = p.n_blk * p.BH;
+  int rc = launch_mode<MODE_KV>(tk_a, tv_a, tq_x, tdo_x, p, s);
   if (rc) return rc;
   // dQ
   p.out1 = reinterpret_cast<__nv_bfloat16*>(a.dq.base);
@@ -414,7 +576,9 @@ int attn_bwd_tc_launch(const AttnArgs& a, cudaStream_t s) {
   p.o1_st = a.dq.st;
   p.o1_sh = a.dq.sh;
   p.out2 = nullptr;
-  rc = launch_mode<MODE_Q>(tq, tdo, tk, tv, p, dim3((a.Tq + TB - 1) / TB, a.B * a.H), s);
+  p.n_blk = (a.Tq + TB - 1) / TB;
+  p.n_tiles = p.n_blk * p.BH;
+  rc = launch_mode<MODE_Q>(tq_a, tdo_a, tk_x, tv_x, p, s);
   return rc ? rc : 1;
 }
 
