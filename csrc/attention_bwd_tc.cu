@@ -46,7 +46,13 @@ constexpr int SB = 64;                        // streaming rows per step
 constexpr int ATILE = TB * 128;               // 128 rows x 64 bf16 (16 KB)
 constexpr int XTILE = SB * 128;               // 64 rows x 64 bf16 (8 KB)
 constexpr int STAGES = 4;                     // streaming-operand ring
-constexpr int kThreads = 64 + 256;
+#ifndef G2B_BWD_EW_WARPS
+#define G2B_BWD_EW_WARPS 16
+#endif
+constexpr int kEw = G2B_BWD_EW_WARPS;         // elementwise warps (kEw/4 per TMEM lane quarter)
+constexpr int NC = 64 / (kEw / 4);            // columns of a step per elementwise thread
+constexpr int kEwThreads = kEw * 32;
+constexpr int kThreads = 64 + kEwThreads;
 // smem: stationary A, A2 (16 KB each); ring of STAGES x (X 8K + Y 8K);
 // P and dS double buffers (128 rows x 64 cols bf16 = 16 KB each);
 // per-stage LSE/delta (2 x 64 floats); barriers.
@@ -69,7 +75,21 @@ struct BwdParams {
   __nv_bfloat16* out2;  // dV (MODE_KV)
   int64_t o1_sb, o1_st, o1_sh, o2_sb, o2_st, o2_sh;
   uint32_t* err;
+#ifdef G2B_ATTN_TRACE
+  unsigned long long* trace;  // [4 roles][128 steps][4 events] of CTA 0 (clock64)
+#endif
 };
+
+#ifdef G2B_ATTN_TRACE
+#define TR(role, gg, ev)                                                              \
+  do {                                                                                \
+    if (blockIdx.x == 0 && (gg) < 128) p.trace[((role) * 128 + (gg)) * 4 + (ev)] = clock64(); \
+  } while (0)
+#else
+#define TR(role, gg, ev) \
+  do {                   \
+  } while (0)
+#endif
 
 __device__ __forceinline__ float ex2f(float x) {
   float y;
@@ -106,19 +126,84 @@ __device__ __forceinline__ TileInfo tile_info(const BwdParams& p, int t) {
   return ti;
 }
 
-// Write 32 values (columns 32*half .. +32 of row r) as bf16 into a K-major
-// 128B-swizzled 128x64 tile.
-__device__ __forceinline__ void put_row_half(uint8_t* tile, int r, int half, const float* v) {
+// N-column TMEM load of this thread's lane (asynchronous; see tmem_wait_into).
+template <int N>
+__device__ __forceinline__ void tmem_ld_nc(uint32_t taddr, uint32_t (&r)[N]) {
+  static_assert(N == 16 || N == 32, "16 or 32 columns");
+  if constexpr (N == 32) tmem_ld32_async(taddr, r);
+  else tmem_ld16_async(taddr, r);
+}
+template <int N>
+__device__ __forceinline__ void tmem_wait_into(uint32_t (&a)[N], uint32_t (&b)[N]) {
+  if constexpr (N == 32) {
+    tmem_wait_ld_into(a);
+    tmem_wait_ld_into(b);
+  } else {
+    tmem_wait_ld_into16x2(a, b);
+  }
+}
+
+// Write NC values (columns NC*grp .. +NC of row r) as bf16 into a K-major
+// 128B-swizzled 128x64 tile (NC/8 16-byte chunks of the row's 128 bytes).
+__device__ __forceinline__ void put_row(uint8_t* tile, int r, int grp, const uint32_t (&v)[NC]) {
   uint8_t* base = tile + r * 128;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int q = half * 4 + j;
+  for (int j = 0; j < NC / 8; ++j) {
+    const int q = grp * (NC / 8) + j;
     uint4 w;
-    w.x = pack_bf16x2(v[j * 8 + 0], v[j * 8 + 1]);
-    w.y = pack_bf16x2(v[j * 8 + 2], v[j * 8 + 3]);
-    w.z = pack_bf16x2(v[j * 8 + 4], v[j * 8 + 5]);
-    w.w = pack_bf16x2(v[j * 8 + 6], v[j * 8 + 7]);
+    w.x = pack_bf16x2(__uint_as_float(v[j * 8 + 0]), __uint_as_float(v[j * 8 + 1]));
+    w.y = pack_bf16x2(__uint_as_float(v[j * 8 + 2]), __uint_as_float(v[j * 8 + 3]));
+    w.z = pack_bf16x2(__uint_as_float(v[j * 8 + 4]), __uint_as_float(v[j * 8 + 5]));
+    w.w = pack_bf16x2(__uint_as_float(v[j * 8 + 6]), __uint_as_float(v[j * 8 + 7]));
     *reinterpret_cast<uint4*>(base + ((q ^ (r & 7)) << 4)) = w;
+  }
+}
+
+// Elementwise step of MODE_KV for one thread's NC columns (queries c0..),
+// in place: S^T -> P^T = 2^(S^T*sl2 - lse[q]), dP^T -> dS^T = P^T (dP^T - delta[q]).
+// With MASK an element is kept iff its query is in range, the row is in range
+// and (causal) the query position is >= min_q (= key position - q_offset).
+// The mask test sits outside the element loop so each variant is one
+// straight-line block the compiler can interleave across elements.
+template <bool MASK>
+__device__ __forceinline__ void ew_kv(uint32_t (&sv)[NC], uint32_t (&dv)[NC], const float* lse_s,
+                                      float sl2, int c0, int Tq, bool row_in, int causal, int min_q) {
+  const float4* lse4 = reinterpret_cast<const float4*>(lse_s);
+  const float4* dl4 = reinterpret_cast<const float4*>(lse_s + SB);
+#pragma unroll
+  for (int q = 0; q < NC / 4; ++q) {
+    const float4 l = lse4[q], d = dl4[q];
+    const float la[4] = {l.x, l.y, l.z, l.w}, da[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int ii = q * 4 + u;
+      float pr = ex2f(fmaf(__uint_as_float(sv[ii]), sl2, -la[u]));
+      if (MASK) {
+        const int col = c0 + ii;
+        const bool vis = col < Tq && row_in && (!causal || col >= min_q);
+        pr = vis ? pr : 0.f;
+      }
+      sv[ii] = __float_as_uint(pr);
+      dv[ii] = __float_as_uint(pr * (__uint_as_float(dv[ii]) - da[u]));
+    }
+  }
+}
+
+// Elementwise step of MODE_Q for one thread's NC columns (keys c0..):
+// dP -> dS in place.
+template <bool MASK>
+__device__ __forceinline__ void ew_q(const uint32_t (&sv)[NC], uint32_t (&dv)[NC], float lse,
+                                     float delta, float sl2, int c0, int Tk, bool row_in, int causal,
+                                     int abs_row) {
+#pragma unroll
+  for (int ii = 0; ii < NC; ++ii) {
+    float pr = ex2f(fmaf(__uint_as_float(sv[ii]), sl2, -lse));
+    if (MASK) {
+      const int col = c0 + ii;
+      const bool vis = col < Tk && row_in && (!causal || col <= abs_row);
+      pr = vis ? pr : 0.f;
+    }
+    dv[ii] = __float_as_uint(pr * (__uint_as_float(dv[ii]) - delta));
   }
 }
 
@@ -138,10 +223,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* x_full = bars + 2;             // [STAGES]
   uint64_t* x_empty = x_full + STAGES;     // [STAGES]
   uint64_t* s_full = x_empty + STAGES;     // [2] S/dP of a step in TMEM
-  uint64_t* e_full = s_full + 2;           // [2] P/dS in smem, S/dP consumed (256 arrivals)
+  uint64_t* s_free = s_full + 2;           // [2] S/dP of a step read out of TMEM (kEwThreads arrivals)
+  uint64_t* e_full = s_free + 2;           // [2] P/dS in smem, S/dP consumed (kEwThreads arrivals)
   uint64_t* pds_free = e_full + 2;         // [2] accumulating MMAs done with P/dS
   uint64_t* acc_full = pds_free + 2;       // [2] tile accumulators final
-  uint64_t* acc_empty = acc_full + 2;      // [2] accumulators drained (256 arrivals)
+  uint64_t* acc_empty = acc_full + 2;      // [2] accumulators drained (kEwThreads arrivals)
   uint64_t* drain = acc_empty + 2;         // abort path: issued MMAs retired
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -158,10 +244,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&e_full[i], 256);
+      mbar_init(&s_free[i], kEwThreads);
+      mbar_init(&e_full[i], kEwThreads);
       mbar_init(&pds_free[i], 1);
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 256);
+      mbar_init(&acc_empty[i], kEwThreads);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -205,6 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        if (lane == 0) TR(0, g, 0);
         const int row = ti.s0 + j * SB;
         if (MODE == MODE_KV) {
           // stage the step's LSE and delta (queries row .. row+63)
@@ -224,6 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* xs = smem + RING_OFF + st * 2 * XTILE;
           tma_load_4d(xs, &tmX, &x_full[st], 0, h, row, b);
           tma_load_4d(xs + XTILE, &tmY, &x_full[st], 0, h, row, b);
+          TR(0, g, 1);
         }
         __syncwarp();
       }
@@ -259,9 +348,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         // S(^T) = A X^T and dP(^T) = A2 Y^T for global step gg (K = head dim)
+        // The TMEM buffer of step gg was last used by step gg-2: wait until the
+        // elementwise warps have read it out (not until they finish step gg-2).
         auto issue_sd = [&](uint32_t gg, bool last) -> bool {
+          TR(1, gg, 2);
           const uint32_t st = gg % STAGES;
-          if (!mbar_wait_bounded(&x_full[st], (gg / STAGES) & 1, p.err, ERR_TIMEOUT_ATTN, abort_flag))
+          if (!mbar_wait_bounded(&s_free[gg & 1], ((gg >> 1) & 1) ^ 1, p.err, ERR_TIMEOUT_ATTN,
+                                 abort_flag) ||
+              !mbar_wait_bounded(&x_full[st], (gg / STAGES) & 1, p.err, ERR_TIMEOUT_ATTN, abort_flag))
             return false;
           tc_fence_after();
           const uint32_t sx = ring + st * 2 * XTILE, sy = sx + XTILE;
@@ -274,6 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       umma_desc_sw128(sy + kk * 32, 16, 1024), id_ss, kk > 0 ? 1u : 0u);
           }
           umma_commit(&s_full[gg & 1]);
+          TR(1, gg, 3);
           if (last) umma_commit(a_empty);
           return true;
         };
@@ -281,11 +376,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok && ti.n > 1) ok = issue_sd(g + 1, ti.n == 2);
         for (int j = 0; j < ti.n && ok; ++j, ++g) {
           const uint32_t pb = g & 1, st = g % STAGES;
+          // S/dP of step g+2 go to the tensor core before the accumulation of
+          // step g, so they are computed while the elementwise warps work on g.
+          if (j + 2 < ti.n && !issue_sd(g + 2, j + 3 == ti.n)) {
+            ok = false;
+            break;
+          }
           if (!mbar_wait_bounded(&e_full[pb], (g >> 1) & 1, p.err, ERR_TIMEOUT_ATTN, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          TR(1, g, 0);
           const uint32_t sx = ring + st * 2 * XTILE, sy = sx + XTILE;
           const uint32_t sp = sp0 + pb * ATILE, sds = sds0 + pb * ATILE;
           // accumulate over the streaming dimension (K = 64 rows of the step)
@@ -306,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           umma_commit(&pds_free[pb]);
           umma_commit(&x_empty[st]);
-          if (j + 2 < ti.n) ok = issue_sd(g + 2, j + 3 == ti.n);
+          TR(1, g, 1);
         }
         if (!ok) break;
         umma_commit(&acc_full[i & 1]);
@@ -321,9 +423,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------- elementwise
+    // Warp w reads TMEM lane quarter w % 4 (a hardware rule) and column group
+    // grp (NC of the step's 64 columns).
     const int ew = warp - 2;
     const int lg = warp & 3;
-    const int half = ew >> 2;             // which 32 columns of the 64-wide step
+    const int grp = ew >> 2;
     const int lane = (int)lane_id();
     const int r = lg * 32 + lane;         // row of the tile (TMEM lane)
     const uint32_t lane_off = (uint32_t)(lg * 32) << 16;
@@ -345,9 +449,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                 (int64_t)h * p.o1_sh
                                           : p.out2 + (int64_t)b * p.o2_sb + (int64_t)row_pos * p.o2_st +
                                                 (int64_t)h * p.o2_sh;
-            dst += half * 32;
+            dst += grp * NC;
 #pragma unroll
-            for (int q = 0; q < 4; ++q) reinterpret_cast<uint4*>(dst)[q] = make_uint4(0, 0, 0, 0);
+            for (int q = 0; q < NC / 8; ++q) reinterpret_cast<uint4*>(dst)[q] = make_uint4(0, 0, 0, 0);
           }
         }
         continue;
@@ -364,87 +468,65 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool rows_full = (MODE == MODE_KV) ? last_row < p.Tk : last_row < p.Tq;
       for (int j = 0; j < ti.n; ++j, ++g) {
         const uint32_t pb = g & 1, st = g % STAGES;
-        const int c0 = ti.s0 + j * SB + half * 32;  // first column position of this thread
-        // Block-uniform: is every element of this step visible?
-        const int cs = ti.s0 + j * SB, ce = cs + SB;  // step columns [cs, ce)
+        const int cst = ti.s0 + j * SB;               // step columns [cst, cst + 64)
+        const int c0 = cst + grp * NC;                // this thread's first column
         bool full;
         if (MODE == MODE_KV)
-          full = rows_full && ce <= p.Tq && (!p.causal || p.q_offset + cs >= last_row);
+          full = rows_full && cst + SB <= p.Tq && (!p.causal || p.q_offset + cst >= last_row);
         else
-          full = rows_full && ce <= p.Tk && (!p.causal || ce - 1 <= p.q_offset + ti.r0);
+          full = rows_full && cst + SB <= p.Tk && (!p.causal || cst + SB - 1 <= p.q_offset + ti.r0);
+        if (lane == 0 && (warp == 2 || warp == 1 + kEw)) TR(warp == 2 ? 2 : 3, g, 0);
         if (!mbar_wait_bounded(&s_full[pb], (g >> 1) & 1, p.err, ERR_TIMEOUT_ATTN, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        uint32_t sv[32], dv[32];
-        const uint32_t tb = tmem + lane_off + pb * 128 + half * 32;
-        tmem_ld32_async(tb, sv);
-        tmem_ld32_async(tb + SB, dv);
+        if (lane == 0 && (warp == 2 || warp == 1 + kEw)) TR(warp == 2 ? 2 : 3, g, 1);
+        uint32_t sv[NC], dv[NC];
+        const uint32_t tb = tmem + lane_off + pb * 128 + grp * NC;
+        tmem_ld_nc(tb, sv);
+        tmem_ld_nc(tb + SB, dv);
+        tmem_wait_into(sv, dv);
+        // S/dP are in registers: the tensor core may overwrite this buffer
+        tc_fence_before();
+        mbar_arrive(&s_free[pb]);
+        if (lane == 0 && (warp == 2 || warp == 1 + kEw)) TR(warp == 2 ? 2 : 3, g, 2);
+        if (MODE == MODE_KV) {
+          const float* lse_s = ld_smem + st * 2 * SB + grp * NC;
+          if (full)
+            ew_kv<false>(sv, dv, lse_s, p.sl2, 0, 0, false, 0, 0);
+          else
+            ew_kv<true>(sv, dv, lse_s, p.sl2, c0, p.Tq, row_in, p.causal, abs_row - p.q_offset);
+        } else {
+          if (full)
+            ew_q<false>(sv, dv, row_lse, row_delta, p.sl2, 0, 0, false, 0, 0);
+          else
+            ew_q<true>(sv, dv, row_lse, row_delta, p.sl2, c0, p.Tk, row_in, p.causal, abs_row);
+        }
         // P/dS buffer pb is free once the accumulation of step g-2 finished
-        if (!mbar_wait_bounded(&pds_free[pb], ((g >> 1) & 1) ^ 1, p.err, ERR_TIMEOUT_ATTN,
-                               abort_flag)) {
-          tmem_wait_ld_into(sv);
-          tmem_wait_ld_into(dv);
+        if (!mbar_wait_bounded(&pds_free[pb], ((g >> 1) & 1) ^ 1, p.err, ERR_TIMEOUT_ATTN, abort_flag)) {
           ok = false;
           break;
         }
-        tmem_wait_ld_into(sv);
-        tmem_wait_ld_into(dv);
-        float pv[32], dsv[32];
-        if (MODE == MODE_KV) {
-          const float4* lse4 = reinterpret_cast<const float4*>(ld_smem + st * 2 * SB + half * 32);
-          const float4* dl4 = reinterpret_cast<const float4*>(ld_smem + st * 2 * SB + SB + half * 32);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float4 l = lse4[q], d = dl4[q];
-            const float la[4] = {l.x, l.y, l.z, l.w}, da[4] = {d.x, d.y, d.z, d.w};
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int ii = q * 4 + u;
-              float pr = ex2f(fmaf(__uint_as_float(sv[ii]), p.sl2, -la[u]));
-              if (!full) {
-                const int col = c0 + ii;
-                const bool vis = col < p.Tq && row_in && (!p.causal || p.q_offset + col >= abs_row);
-                pr = vis ? pr : 0.f;
-              }
-              pv[ii] = pr;
-              dsv[ii] = pr * (__uint_as_float(dv[ii]) - da[u]);
-            }
-          }
-          put_row_half(ptile0 + pb * ATILE, r, half, pv);
-        } else {
-#pragma unroll
-          for (int ii = 0; ii < 32; ++ii) {
-            float pr = ex2f(fmaf(__uint_as_float(sv[ii]), p.sl2, -row_lse));
-            if (!full) {
-              const int col = c0 + ii;
-              const bool vis = col < p.Tk && row_in && (!p.causal || col <= abs_row);
-              pr = vis ? pr : 0.f;
-            }
-            dsv[ii] = pr * (__uint_as_float(dv[ii]) - row_delta);
-          }
-        }
-        put_row_half(dstile0 + pb * ATILE, r, half, dsv);
+        if (MODE == MODE_KV) put_row(ptile0 + pb * ATILE, r, grp, sv);
+        put_row(dstile0 + pb * ATILE, r, grp, dv);
         fence_proxy_async_shared();
         tc_fence_before();
         mbar_arrive(&e_full[pb]);
+        if (lane == 0 && (warp == 2 || warp == 1 + kEw)) TR(warp == 2 ? 2 : 3, g, 3);
       }
       if (!ok) break;
-      // final accumulators -> global (each warp writes its 32 rows, its half of d)
+      // final accumulators -> global (each warp writes its 32 rows, NC dims)
       if (!mbar_wait_bounded(&acc_full[i & 1], (i >> 1) & 1, p.err, ERR_TIMEOUT_ATTN, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t acc_base = tmem + lane_off + T_ACC + (i & 1) * 128;
-      uint32_t v1[32], v2[32];
-      tmem_ld32_async(acc_base + half * 32, v1);
-      tmem_wait_ld_into(v1);
-      if (MODE == MODE_KV) {
-        tmem_ld32_async(acc_base + 64 + half * 32, v2);
-        tmem_wait_ld_into(v2);
-      }
+      const uint32_t acc_base = tmem + lane_off + T_ACC + (i & 1) * 128 + grp * NC;
+      uint32_t v1[NC], v2[NC];
+      tmem_ld_nc(acc_base, v1);
+      if (MODE == MODE_KV) tmem_ld_nc(acc_base + 64, v2);
+      tmem_wait_into(v1, v2);
       tc_fence_before();
       mbar_arrive(&acc_empty[i & 1]);
       ++i;
@@ -458,9 +540,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                                               (int64_t)h * p.o1_sh
                                         : p.out2 + (int64_t)b * p.o2_sb + (int64_t)row_pos * p.o2_st +
                                               (int64_t)h * p.o2_sh;
-          dst += half * 32;
+          dst += grp * NC;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
+          for (int q = 0; q < NC / 8; ++q) {
             uint4 w;
             w.x = pack_bf16x2(__uint_as_float(v[q * 8 + 0]) * sc, __uint_as_float(v[q * 8 + 1]) * sc);
             w.y = pack_bf16x2(__uint_as_float(v[q * 8 + 2]) * sc, __uint_as_float(v[q * 8 + 3]) * sc);
@@ -532,6 +614,10 @@ int launch_mode(const CUtensorMap& a, const CUtensorMap& a2, const CUtensorMap& 
 
 }  // namespace
 
+#ifdef G2B_ATTN_TRACE
+unsigned long long* g_attn_trace = nullptr;  // KV trace, then Q trace
+#endif
+
 // Tensor-core backward (after delta has been computed into a.delta): returns
 // 1 if it ran, 0 when a layout is not TMA-compatible, negative on failure.
 int attn_bwd_tc_launch(const AttnArgs& a, cudaStream_t s) {
@@ -568,6 +654,9 @@ int attn_bwd_tc_launch(const AttnArgs& a, cudaStream_t s) {
   p.o2_sh = a.dv.sh;
   p.n_blk = (a.Tk + TB - 1) / TB;
   p.n_tiles = p.n_blk * p.BH;
+#ifdef G2B_ATTN_TRACE
+  p.trace = g_attn_trace;
+#endif
   int rc = launch_mode<MODE_KV>(tk_a, tv_a, tq_x, tdo_x, p, s);
   if (rc) return rc;
   // dQ
@@ -578,6 +667,9 @@ int attn_bwd_tc_launch(const AttnArgs& a, cudaStream_t s) {
   p.out2 = nullptr;
   p.n_blk = (a.Tq + TB - 1) / TB;
   p.n_tiles = p.n_blk * p.BH;
+#ifdef G2B_ATTN_TRACE
+  p.trace = g_attn_trace + 4 * 128 * 4;
+#endif
   rc = launch_mode<MODE_Q>(tq_a, tdo_a, tk_x, tv_x, p, s);
   return rc ? rc : 1;
 }
