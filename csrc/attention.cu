@@ -293,7 +293,9 @@ __global__ void __launch_bounds__(FWD_THREADS) attn_fwd_kernel(const AttnArgs a)
 
 // ------------------------------------------------------ backward: delta ---
 // delta[b,h,t] = sum_d dO[b,t,h,d] * O[b,t,h,d]; one warp per (b,h,t).
-__global__ void attn_bwd_delta_kernel(const AttnArgs a) {
+// Scalar variant for views whose rows are not 16-byte aligned: one warp per
+// row, 4 bytes per lane.
+__global__ void attn_bwd_delta_scalar_kernel(const AttnArgs a) {
   const int64_t gw = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t total = (int64_t)a.B * a.H * a.Tq;
@@ -308,6 +310,33 @@ __global__ void attn_bwd_delta_kernel(const AttnArgs a) {
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffff, s, off);
   if (lane == 0) a.delta[gw] = s;
+}
+
+__global__ void attn_bwd_delta_kernel(const AttnArgs a) {
+  // 8 lanes per row, 16 bytes each: a row's 64 bf16 of O and dO are two
+  // 128-byte coalesced reads, and a warp covers 4 rows.
+  const int64_t gt = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t row = gt >> 3;
+  const int sub = threadIdx.x & 7;
+  const int64_t total = (int64_t)a.B * a.H * a.Tq;
+  float s = 0.f;
+  if (row < total) {
+    const int t = row % a.Tq;
+    const int64_t bh = row / a.Tq;
+    const int b = bh / a.H, h = bh % a.H;
+    const uint4 ov = reinterpret_cast<const uint4*>(head_ptr(a.o, b, h) + (int64_t)t * a.o.st)[sub];
+    const uint4 gv = reinterpret_cast<const uint4*>(head_ptr(a.dout, b, h) + (int64_t)t * a.dout.st)[sub];
+    const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 o2 = unpack_bf16x2(ow[i]), g2 = unpack_bf16x2(gw[i]);
+      s = fmaf(o2.x, g2.x, s);
+      s = fmaf(o2.y, g2.y, s);
+    }
+  }
+#pragma unroll
+  for (int off = 4; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffff, s, off);
+  if (row < total && sub == 0) a.delta[row] = s;
 }
 
 // ---------------------------------------------------- backward: dK / dV ---
@@ -536,7 +565,14 @@ int attn_fwd_launch(const AttnArgs& a, cudaStream_t s) {
 int attn_bwd_launch(const AttnArgs& a, cudaStream_t s) {
   if (a.B <= 0 || a.H <= 0 || a.Tq <= 0 || a.Tk <= 0) return -1;
   const int64_t rows = (int64_t)a.B * a.H * a.Tq;
-  attn_bwd_delta_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, s>>>(a);
+  auto rows16 = [](const HeadView& v) {
+    return (reinterpret_cast<uintptr_t>(v.base) & 15) == 0 && (v.st * 2) % 16 == 0 &&
+           (v.sh * 2) % 16 == 0 && (v.sb * 2) % 16 == 0;
+  };
+  if (rows16(a.o) && rows16(a.dout))
+    attn_bwd_delta_kernel<<<(unsigned)((rows * 8 + 255) / 256), 256, 0, s>>>(a);
+  else
+    attn_bwd_delta_scalar_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, s>>>(a);
   if (g_attn_impl == 0) {
     const int rc = attn_bwd_tc_launch(a, s);
     if (rc == 1) {
