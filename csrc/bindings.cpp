@@ -11,6 +11,7 @@
 
 #include "attention.cuh"
 #include "comm.cuh"
+#include "decode.cuh"
 #include "elementwise.cuh"
 #include "gemm.cuh"
 #include "launch_count.h"
@@ -264,5 +265,25 @@ PYBIND11_MODULE(_C, m) {
     check(comm_flag_wait_test_launch(P<uint32_t>(flag), value, budget_ns, P<uint32_t>(err),
                                      S(stream)),
           "flag_wait_test");
+  });
+m.def("decode_embed", [](int64_t tok, int64_t lens, int64_t wte, int64_t wpe, int64_t x, int B, int C,
+                           int64_t stream) {
+    check(decode_embed_launch(P<int64_t>(tok), P<int>(lens), P<void>(wte), P<void>(wpe), P<float>(x), B, C,
+                              S(stream)),
+          "decode_embed");
+  });
+  m.def("decode_attn", [](int64_t qkv, int64_t ld, int64_t kc, int64_t vc, int64_t lens, int64_t part_o,
+                          int64_t part_ml, int64_t out, int64_t ld_out, int B, int H, int Hkv, int Tmax,
+                          float scale, int64_t stream) {
+    check(decode_attn_launch(P<void>(qkv), ld, P<void>(kc), P<void>(vc), P<int>(lens), P<float>(part_o),
+                             P<float>(part_ml), P<void>(out), ld_out, B, H, Hkv, Tmax, scale, S(stream)),
+          "decode_attn");
+  });
+  m.def("decode_partials_numel", [](int B, int H, int Tmax) { return decode_partials_numel(B, H, Tmax); });
+  m.def("decode_argmax", [](int64_t logits, int64_t ld, int V, int64_t tok, int64_t lens, int64_t hist,
+                            int Tmax, int B, int64_t stream) {
+    check(decode_argmax_launch(P<void>(logits), ld, V, P<int64_t>(tok), P<int>(lens), P<int64_t>(hist), Tmax,
+                               B, S(stream)),
+          "decode_argmax");
   });
 }

@@ -346,3 +346,47 @@ def clip_coef(sumsq: torch.Tensor, max_norm: float, clip: torch.Tensor,
               norm_out: Optional[torch.Tensor] = None, scale2: float = 1.0) -> None:
     lib().clip_coef(sumsq.data_ptr(), float(scale2), float(max_norm), clip.data_ptr(),
                     _ptr(norm_out), _stream())
+
+
+# ------------------------------------------------------------------ decoding --
+def decode_embed(tok: torch.Tensor, lens: torch.Tensor, wte: torch.Tensor, wpe: torch.Tensor,
+                 x: torch.Tensor) -> None:
+    """x[b] (fp32) = wte[tok[b]] + wpe[lens[b]] with bf16 tables."""
+    B, C = x.shape
+    lib().decode_embed(tok.data_ptr(), lens.data_ptr(), wte.data_ptr(), wpe.data_ptr(), x.data_ptr(), B, C,
+                       _stream())
+
+
+def decode_partials(B: int, H: int, Tmax: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    n = lib().decode_partials_numel(B, H, Tmax)
+    return (torch.empty(n, dtype=torch.float32, device=device),
+            torch.empty(n // 32, dtype=torch.float32, device=device))
+
+
+def decode_attn(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, lens: torch.Tensor,
+                part_o: torch.Tensor, part_ml: torch.Tensor, out: torch.Tensor, H: int, Hkv: int,
+                scale: Optional[float] = None) -> None:
+    """One decode step of attention with the KV append fused in.
+
+    qkv: [B, (H + 2 Hkv) * 64] bf16 (this step's projections); k_cache/v_cache:
+    [B, Hkv, Tmax, 64] bf16; lens: int32 [B] cached positions (the new token's
+    k/v are written at lens[b]); out: [B, H * 64] bf16.
+    """
+    B = qkv.shape[0]
+    Tmax = k_cache.shape[2]
+    if k_cache.shape != (B, Hkv, Tmax, 64) or v_cache.shape != k_cache.shape:
+        raise ValueError("cache must be [B, Hkv, Tmax, 64]")
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("cache must be contiguous")
+    scale = 1.0 / math.sqrt(64) if scale is None else scale
+    lib().decode_attn(qkv.data_ptr(), _row_stride(qkv), k_cache.data_ptr(), v_cache.data_ptr(),
+                      lens.data_ptr(), part_o.data_ptr(), part_ml.data_ptr(), out.data_ptr(),
+                      _row_stride(out), B, H, Hkv, Tmax, float(scale), _stream())
+
+
+def decode_argmax(logits: torch.Tensor, vocab: int, tok: torch.Tensor, lens: torch.Tensor,
+                  hist: torch.Tensor) -> None:
+    """Greedy next token per row: tok[b], hist[b, lens[b] + 1] = argmax; lens += 1."""
+    B = logits.shape[0]
+    lib().decode_argmax(logits.data_ptr(), _row_stride(logits), vocab, tok.data_ptr(), lens.data_ptr(),
+                        hist.data_ptr(), hist.shape[1], B, _stream())

@@ -23,7 +23,7 @@ SOURCES = [
     "csrc/attention_bwd_tc.cu",
     "csrc/elementwise.cu",
     "csrc/comm.cu",
-    "csrc/noalloc.cu",
+    "csrc/noalloc.cu", "csrc/decode.cu",
 ]
 
 NVCC_FLAGS = [
