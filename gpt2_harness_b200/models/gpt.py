@@ -144,7 +144,9 @@ class CausalSelfAttention(nn.Module):
                 weights = probs
             y = self.attn_dropout(probs) @ v
         if self.head_mask is not None:
-            y = y * self.head_mask.to(y.device, y.dtype).view(1, -1, 1, 1)
+            # (n_head,) for every sequence, or (B, n_head) per sequence
+            m = self.head_mask.to(y.device, y.dtype)
+            y = y * (m.view(1, -1, 1, 1) if m.dim() == 1 else m.view(m.shape[0], -1, 1, 1))
         y = y.transpose(1, 2).contiguous().view(B, T, C)
         return self.resid_dropout(self.c_proj(y)), weights
 

@@ -1,0 +1,149 @@
+"""Quantization, pruning, distillation, induction-head scoring and the
+ablation grid, on tiny models (CPU)."""
+
+import math
+
+import pytest
+import torch
+
+from gpt2_harness_b200.config import GPTConfig, TrainConfig
+from gpt2_harness_b200.data import TokenDataset
+from gpt2_harness_b200.models.gpt import GPT
+
+
+@pytest.fixture(scope="module")
+def dataset():
+    g = torch.Generator().manual_seed(0)
+    # a learnable stream: a repeating random motif with noise
+    motif = torch.randint(0, 64, (37,), generator=g)
+    toks = motif.repeat(200)
+    noise = torch.rand(toks.shape, generator=g) < 0.1
+    toks[noise] = torch.randint(0, 64, (int(noise.sum()),), generator=g)
+    return TokenDataset(toks.numpy(), block_size=32)
+
+
+def _model(**kw):
+    torch.manual_seed(0)
+    base = dict(vocab_size=64, n_positions=64, n_layer=2, n_head=4, n_embd=32)
+    base.update(kw)
+    return GPT(GPTConfig(**base)).eval()
+
+
+# ------------------------------------------------------------ quantization --
+def test_quantize_tensor_ranges_and_error():
+    from gpt2_harness_b200.quantization import quantize_dequantize, quantize_tensor
+    w = torch.randn(16, 64)
+    for bits in (8, 4, 2):
+        q, s = quantize_tensor(w, bits)
+        assert int(q.max()) <= 2 ** (bits - 1) - 1 and int(q.min()) >= -(2 ** (bits - 1))
+    e8 = (quantize_dequantize(w, 8) - w).abs().max()
+    e4 = (quantize_dequantize(w, 4) - w).abs().max()
+    assert e8 < e4 and e8 <= (w.abs().amax(1) / 127).max() * 0.5001
+    ef = (quantize_dequantize(w, "fp8") - w).abs().max()
+    assert ef < e4
+    with pytest.raises(ValueError):
+        quantize_tensor(w, 9)
+
+
+def test_int4_pack_roundtrip():
+    from gpt2_harness_b200.quantization import pack_int4, unpack_int4
+    q = torch.randint(-8, 8, (33,), dtype=torch.int8)
+    p = pack_int4(q)
+    assert p.dtype == torch.uint8 and p.numel() == 17
+    assert torch.equal(unpack_int4(p, 33), q)
+
+
+def test_quantize_model_and_sweep(dataset):
+    from gpt2_harness_b200.quantization import quantization_sweep, quantize_model
+    m = _model()
+    qm, st = quantize_model(m, 4)
+    assert st["n_quantized_tensors"] == 8 and st["compression_ratio"] > 1.5
+    assert not torch.equal(qm.h[0].mlp.c_fc.weight, m.h[0].mlp.c_fc.weight)
+    assert torch.equal(qm.wte.weight, m.wte.weight)
+    rows = quantization_sweep(m, dataset, n_chunks=2, batches_per_chunk=1, batch_size=2)
+    assert rows[0].label == "fp32" and len(rows) == 5
+    assert all(math.isfinite(r.ppl_mean) for r in rows)
+
+
+# ----------------------------------------------------------------- pruning --
+def test_head_and_neuron_importance_and_sweep(dataset):
+    from gpt2_harness_b200.pruning import (head_importance, keep_mask, neuron_importance,
+                                           params_removed_by_head_pruning, prune_sweep, pruned)
+    m = _model()
+    hi = head_importance(m, dataset, n_batches=2, batch_size=2)
+    assert hi.shape == (2, 4) and torch.allclose(hi.norm(dim=1), torch.ones(2), atol=1e-5)
+    ni = neuron_importance(m, dataset, n_batches=2, batch_size=2)
+    assert ni.shape == (2, 128)
+    mask = keep_mask(hi, 0.25)
+    assert int((mask == 0).sum()) == 2
+    assert params_removed_by_head_pruning(m, mask) == 2 * (4 * 8 * 32 + 3 * 8)
+    x = torch.randint(0, 64, (1, 16))
+    with pruned(m, head_mask=torch.zeros(2, 4)):
+        a = m(x)["logits"]
+    assert m.h[0].attn.head_mask is None
+    assert not torch.allclose(a, m(x)["logits"])
+    res, _ = prune_sweep(m, dataset, [0.0, 0.5], kind="neurons", n_eval_batches=2, batch_size=2)
+    assert res[0].params_removed == 0 and res[1].params_removed > 0
+
+
+# ------------------------------------------------------------- distillation --
+def test_distillation_loss_properties():
+    from gpt2_harness_b200.distill import distillation_loss
+    s, t = torch.randn(2, 5, 11), torch.randn(2, 5, 11)
+    y = torch.randint(0, 11, (2, 5))
+    tot, ce, kl = distillation_loss(s, t, y, alpha=0.0)
+    assert torch.equal(tot, ce) and float(kl) == 0.0
+    tot, ce, kl = distillation_loss(s, s, y, alpha=1.0)
+    assert abs(float(kl)) < 1e-5
+    _, _, kl = distillation_loss(s, t, y, temperature=2.0, alpha=0.5)
+    assert float(kl) > 0
+
+
+def test_train_student_runs(dataset):
+    from gpt2_harness_b200.distill import train_student
+    teacher = _model()
+    cfg = GPTConfig(vocab_size=64, n_positions=64, n_layer=1, n_head=2, n_embd=16)
+    tc = TrainConfig(steps=6, batch_size=4, block_size=32, eval_interval=3, eval_batches=1, warmup_steps=1)
+    _, r = train_student(cfg, tc, dataset, teacher=teacher, alpha=0.5, device="cpu")
+    assert len(r.history) == 2 and math.isfinite(r.final_val_loss) and r.teacher_params > r.n_params
+    with pytest.raises(ValueError):
+        train_student(cfg, tc, dataset, alpha=0.5)
+
+
+# --------------------------------------------------------------- induction --
+def test_rank_correlation_with_ties():
+    from gpt2_harness_b200.induction import rank_correlation
+    a = torch.tensor([0.0, 0.0, 1.0, 2.0])
+    assert rank_correlation(a, a * 3) == pytest.approx(1.0)
+    assert rank_correlation(a, -a) == pytest.approx(-1.0)
+
+
+def test_induction_scores_shapes_and_batched_ablation():
+    from gpt2_harness_b200.induction import (ablation_scores, in_context_learning_curve, make_repeated_sequence,
+                                             score_heads)
+    m = _model()
+    s = make_repeated_sequence(2, 10, 64, 0, torch.Generator().manual_seed(0))
+    assert s.shape == (2, 21) and torch.equal(s[:, 1:11], s[:, 11:])
+    sc = score_heads(m, seq_len=10, batch_size=2, n_copy_tokens=50)
+    assert sc.prefix_matching.shape == sc.copying.shape == sc.ablation.shape == (2, 4)
+    assert 0 < sc.chance_level < 1 and len(sc.top_heads(3)) == 3
+    one, b1 = ablation_scores(m, seq_len=10, batch_size=2, heads_per_forward=1)
+    allb, b2 = ablation_scores(m, seq_len=10, batch_size=2, heads_per_forward=8)
+    assert b1 == b2 and torch.allclose(one, allb, atol=1e-5)
+    c = in_context_learning_curve(m, seq_len=10, batch_size=2)
+    assert len(c["per_position_loss"]) == 20
+
+
+# --------------------------------------------------------------- ablations --
+def test_ablation_grid_and_verdicts(dataset):
+    from gpt2_harness_b200.ablations import build_arms, run_grid, summarize
+    arms = build_arms()
+    assert len(arms) == 9 and arms[0].is_baseline
+    base = GPTConfig(vocab_size=64, n_positions=32, n_layer=2, n_head=4, n_embd=32)
+    tc = TrainConfig(steps=4, batch_size=4, block_size=32, eval_interval=4, eval_batches=1, warmup_steps=1)
+    sel = [a for a in arms if a.key in ("baseline", "relu", "post_ln")]
+    res = run_grid(dataset, seeds=(0, 1), arms=sel, base_model=base, base_train=tc, device="cpu")
+    summ = summarize(res, sel)
+    verdicts = {r["arm"]: r["verdict"] for r in summ["rows"]}
+    assert verdicts["baseline"] == "reference"
+    assert set(verdicts.values()) <= {"reference", "indistinguishable", "worse", "better"}
