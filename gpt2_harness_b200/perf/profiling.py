@@ -59,6 +59,12 @@ class ProfileReport:
     def as_dict(self) -> dict:
         return asdict(self)
 
+    def memory_bound_fraction(self) -> float:
+        """Share of kernel time in operators with no tensor-core work
+        (normalisation, loss, optimiser, elementwise, embedding)."""
+        return sum(v for k, v in self.categories.items()
+                   if k in ("normalization", "loss", "optimizer", "elementwise", "embedding"))
+
     def format(self, k: int = 25) -> str:
         lines = [f"device time per step: {self.total_device_us / 1e3:.3f} ms over {self.steps} step(s)"]
         for name, us, share, calls in self.top[:k]:
@@ -88,12 +94,19 @@ def profile_training_step(step_fn: Callable[[], None], wait: int = 1, warmup: in
     if trace_path:
         prof.export_chrome_trace(trace_path)
     per: dict[str, list] = {}
+    on_gpu = torch.cuda.is_available()
     for ev in prof.events():
         dt = getattr(ev, "device_type", None)
         is_dev = dt is not None and str(dt).endswith("CUDA")
-        if not is_dev:
-            continue
-        dur = float(getattr(ev, "device_time", 0.0) or getattr(ev, "cuda_time", 0.0) or 0.0)
+        if on_gpu:
+            if not is_dev:
+                continue
+            dur = float(getattr(ev, "device_time", 0.0) or getattr(ev, "cuda_time", 0.0) or 0.0)
+        else:
+            # no GPU: aggregate the self CPU time of aten ops (the kernels of a CPU run)
+            if is_dev or not ev.name.startswith("aten::"):
+                continue
+            dur = float(getattr(ev, "self_cpu_time_total", 0.0) or 0.0)
         if dur <= 0:
             continue
         rec = per.setdefault(ev.name, [0.0, 0])
