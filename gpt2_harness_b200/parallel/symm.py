@@ -94,3 +94,35 @@ class SymmetricBuffer:
             torch.cuda.synchronize(self.device)
             L.symm_free(self.ptr)
             self.ptr = 0
+
+
+class P2PAllReducer:
+    """Standalone fused peer-memory all-reduce over a symmetric fp32 buffer.
+
+    ``tensor`` is this rank's buffer (write the data there); ``all_reduce(n,
+    scale)`` reduces its first ``n`` elements across the group in one kernel
+    (reduce-scatter by peer loads, scale, all-gather by peer stores, per-CTA
+    flags with bounded waits) on the current stream.
+    """
+
+    def __init__(self, nbytes: int, group=None, device: Optional[torch.device] = None, nblocks: int = 64) -> None:
+        self.data = SymmetricBuffer(nbytes, group, device)
+        self.flags = SymmetricBuffer(N.lib().comm_flag_words() * 4, group, device)
+        self.rank, self.world, self.device = self.data.rank, self.data.world, self.data.device
+        self.tensor = self.data.view(torch.float32)
+        self.nblocks = nblocks
+        self.epoch = 0
+        self.counter = torch.zeros(1, dtype=torch.int64, device=self.device)
+
+    def all_reduce(self, numel: Optional[int] = None, scale: float = 1.0) -> torch.Tensor:
+        n = self.tensor.numel() if numel is None else int(numel)
+        self.epoch += 1
+        N.lib().allreduce_p2p(self.data.peer_ptrs_dev.data_ptr(), self.flags.peer_ptrs_dev.data_ptr(), self.rank,
+                              self.world, 0, n, 0, float(scale), self.epoch & 0xFFFFFFFF, self.counter.data_ptr(),
+                              N.error_word().data_ptr(), self.nblocks, 2_000_000_000,
+                              torch.cuda.current_stream(self.device).cuda_stream)
+        return self.tensor[:n]
+
+    def close(self) -> None:
+        self.data.close()
+        self.flags.close()
