@@ -130,13 +130,26 @@ class TokenDataset:
         win = data[starts[:, None] + np.arange(T + 1)[None, :]].astype(np.int64)
         dev = torch.device(device)
         if pin and dev.type == "cuda":
+            # two (x, y) pinned pairs used alternately; a pair is refilled only
+            # after the device copy that last read it has completed
             key = (split, batch_size)
-            buf = self._pinned.get(key)
-            if buf is None:
-                buf = self._pinned[key] = torch.empty(batch_size, T + 1, dtype=torch.int64).pin_memory()
-            buf.copy_(torch.from_numpy(win))
-            both = buf.to(dev, non_blocking=True)
-            return both[:, :-1], both[:, 1:]
+            ring = self._pinned.get(key)
+            if ring is None:
+                ring = self._pinned[key] = {"i": 0, "pairs": [
+                    [torch.empty(batch_size, T, dtype=torch.int64).pin_memory() for _ in range(2)] + [None]
+                    for _ in range(2)]}
+            pair = ring["pairs"][ring["i"]]
+            ring["i"] ^= 1
+            if pair[2] is not None:
+                pair[2].synchronize()
+            w = torch.from_numpy(win)
+            pair[0].copy_(w[:, :-1])
+            pair[1].copy_(w[:, 1:])
+            x, y = pair[0].to(dev, non_blocking=True), pair[1].to(dev, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record()
+            pair[2] = ev
+            return x, y
         b = torch.from_numpy(win)
         return b[:, :-1].contiguous().to(dev), b[:, 1:].contiguous().to(dev)
 

@@ -1,0 +1,159 @@
+"""Distributed training job (one process per GPU, under torchrun / srun / a
+Kubernetes indexed job / Ray): the native B200 engine with fused,
+backward-overlapped gradient all-reduce, a resumable sharded token stream,
+and asynchronous sharded checkpoints in the reference's format.
+
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m gpt2_harness_b200.launch \\
+        --model gpt2 --data tokens.bin --steps 5000 --ckpt-dir ckpt --ckpt-every 500
+
+On start it resumes from the newest complete checkpoint under ``--ckpt-dir``
+(model, AdamW moments, optimiser step, every rank's stream position), so a
+requeued job (Slurm ``--requeue``, a restarted pod) continues where it left
+off; checkpoints are written by rank 0 to ``step_<n>/`` and swapped in
+atomically. ``SIGUSR1`` / ``SIGTERM`` (the pre-emption warning of most
+schedulers) trigger a checkpoint at the next step boundary, then a clean exit.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import signal
+import time
+from pathlib import Path
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from .cluster.checkpoint import AsyncCheckpointer, engine_state_dict, load_full, load_extra, load_into_engine
+from .cluster.streaming import ShardedStream, StreamState, TokenShardSource
+from .config import TrainConfig, gpt2_config
+from .trainer import Trainer
+
+__all__ = ["latest_checkpoint", "main"]
+
+_STOP = {"flag": False}
+
+
+def _on_signal(signum, _frame) -> None:
+    _STOP["flag"] = True
+
+
+def latest_checkpoint(ckpt_dir) -> Optional[Path]:
+    d = Path(ckpt_dir)
+    if not d.is_dir():
+        return None
+    steps = sorted((int(p.name.split("_")[1]), p) for p in d.glob("step_*") if (p / "index.json").exists())
+    return steps[-1][1] if steps else None
+
+
+class _SyntheticTokens:
+    """Uniform random windows (the benchmark's data) as a stream source."""
+
+    def __init__(self, vocab: int, block: int, n: int = 1 << 20, seed: int = 0) -> None:
+        self.vocab, self.block, self.n, self.seed = vocab, block, n, seed
+
+    def __len__(self) -> int:
+        return self.n
+
+    def __getitem__(self, i: int):
+        g = torch.Generator().manual_seed(self.seed * 1_000_003 + int(i))
+        w = torch.randint(0, self.vocab, (self.block + 1,), generator=g)
+        return w[:-1], w[1:]
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--model", default="gpt2")
+    ap.add_argument("--data", default=None, help="uint16 token file; synthetic tokens when absent")
+    ap.add_argument("--batch", type=int, default=16, help="per-GPU micro-batch")
+    ap.add_argument("--seq", type=int, default=1024)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--lr", type=float, default=6e-4)
+    ap.add_argument("--warmup", type=int, default=100)
+    ap.add_argument("--comm", choices=["p2p", "nccl"], default="p2p")
+    ap.add_argument("--ckpt-dir", default=None)
+    ap.add_argument("--ckpt-every", type=int, default=500)
+    ap.add_argument("--log", default=None, help="JSONL metrics (rank 0)")
+    ap.add_argument("--seed", type=int, default=0)
+    a = ap.parse_args(argv)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(minutes=10))
+    for s in (signal.SIGUSR1, signal.SIGTERM):
+        signal.signal(s, _on_signal)
+
+    cfg = gpt2_config(a.model, n_positions=max(a.seq, gpt2_config(a.model).n_positions))
+    tc = TrainConfig(steps=a.steps, batch_size=a.batch, block_size=a.seq, lr=a.lr, warmup_steps=a.warmup)
+    trainer = Trainer(cfg, a.batch, a.seq, train=tc, comm=a.comm, device=dev, seed=a.seed)
+    src = TokenShardSource(a.data, a.seq) if a.data else _SyntheticTokens(cfg.vocab_size, a.seq, seed=a.seed)
+
+    start_step, state = 0, None
+    ck = latest_checkpoint(a.ckpt_dir) if a.ckpt_dir else None
+    if ck is not None:
+        full, extra = load_full(ck), load_extra(ck, 0)
+        load_into_engine(trainer.engine, {k: v.to(dev) for k, v in full.items()}, extra)
+        if trainer.ddp is not None:
+            trainer.engine.sync_shadow()
+        start_step = int(extra.get("step", 0))
+        state = StreamState.from_dict(extra["stream"]) if "stream" in extra else None
+        trainer.step_num = start_step
+    stream = ShardedStream(src, rank=rank, world_size=world, state=state, seed=a.seed, prefetch=4)
+    batches = stream.batches(a.batch, pin=True)
+    ckpt = AsyncCheckpointer()
+    logf = open(a.log, "a") if a.log and rank == 0 else None
+    t0, tok0 = time.perf_counter(), 0
+    step = start_step
+    try:
+        while step < a.steps:
+            trainer.h2d_done.synchronize()  # the previous batch's buffers are free again
+            x, y = next(batches)
+            loss = trainer.step_async(x, y)
+            step += 1
+            tok0 += a.batch * a.seq * world
+            stop = _STOP["flag"]
+            if world > 1 and step % 10 == 0:  # agree on a pre-emption signal every 10 steps
+                flag = torch.tensor([1 if stop else 0], device=dev)
+                dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+                stop = bool(flag.item())
+            due = a.ckpt_dir and (step % a.ckpt_every == 0 or step == a.steps or stop)
+            if due:
+                pos = [stream.position]
+                if world > 1:
+                    allp = [None] * world
+                    dist.all_gather_object(allp, stream.position)
+                    pos = allp
+                if rank == 0:
+                    sd, extra = engine_state_dict(trainer.engine, with_optimizer=True)
+                    extra.update(step=step, stream=stream.state_dict(pos))
+                    ckpt.save(Path(a.ckpt_dir) / f"step_{step}", sd, plan={}, rank=0, world_size=1, step=step,
+                              global_shapes={k: list(v.shape) for k, v in sd.items()}, extra=extra)
+                if world > 1:
+                    dist.barrier()
+            if logf and (step % 10 == 0 or step == a.steps):
+                dt = time.perf_counter() - t0
+                logf.write(json.dumps({"step": step, "loss": float(loss.item()), "tokens_per_s": tok0 / dt}) + "\n")
+                logf.flush()
+            if stop:
+                break
+        trainer.check()
+    finally:
+        ckpt.wait()
+        if logf:
+            logf.close()
+        trainer.close()
+        if world > 1:
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

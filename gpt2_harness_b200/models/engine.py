@@ -340,7 +340,20 @@ class Engine:
     def forward(self, idx: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
         """Forward pass; returns the device scalar loss (loss_out[0]).
         Also leaves dlogits in the logits buffer for :meth:`backward`."""
+        targets = targets.contiguous()
+        A = self._forward_to_logits(idx)
+        N.cross_entropy_fwd_bwd(A.logits, targets.view(-1), A.loss_rows, A.loss_out, self.config.vocab_size)
+        return A.loss_out[0]
+
+    @torch.no_grad()
+    def logits(self, idx: torch.Tensor) -> torch.Tensor:
+        """Forward without the loss: (B*T, vocab) bf16 logits (a view of the
+        engine's buffer, valid until the next forward)."""
+        return self._forward_to_logits(idx).logits[:, : self.config.vocab_size]
+
+    def _forward_to_logits(self, idx: torch.Tensor) -> _Acts:
         cfg = self.config
+        idx = idx.contiguous()
         B, T = idx.shape
         if T > cfg.n_positions:
             raise ValueError(f"sequence of length {T} exceeds n_positions={cfg.n_positions}")
@@ -366,8 +379,7 @@ class Engine:
                    bias=p(pre + "mlp.c_proj.bias"), aux=A.x[2 * l + 1])
         N.layernorm_fwd(A.x[2 * L], p("ln_f.weight"), p("ln_f.bias"), A.hf, A.mu[2 * L], A.rs[2 * L], eps)
         N.gemm(A.hf, p("wte.weight"), A.logits[:, :V])
-        N.cross_entropy_fwd_bwd(A.logits, targets.view(-1), A.loss_rows, A.loss_out, V)
-        return A.loss_out[0]
+        return A
 
     # ------------------------------------------------------------ backward --
     def backward(self, idx: torch.Tensor, accumulate: bool = False) -> None:

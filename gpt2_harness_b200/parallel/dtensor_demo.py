@@ -53,7 +53,7 @@ def dtensor_worker(rank: int, world_size: int, batch: int = 4, seq: int = 8,
     dx = distribute_tensor(x, mesh, [Replicate()])
     h = F.gelu(F.linear(dx, w1, b1))
     y = F.linear(h, w2).redistribute(mesh, [Replicate()]) + b2
-    dt_err = float((y.to_local() - ref).abs().max())
+    dt_err = float((y.to_local() - ref).detach().abs().max())
     plan = nn.Sequential()
     plan.add_module("fc", nn.Linear(C, 4 * C))
     plan.add_module("proj", nn.Linear(4 * C, C))

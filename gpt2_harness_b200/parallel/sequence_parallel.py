@@ -165,9 +165,12 @@ def ring_attention(q_local, k_local, v_local, rank: int, world_size: int, group=
 
 def cp_payload_bytes(B: int, T: int, C: int, world: int, elem_bytes: int = 4) -> dict[str, float]:
     """Closed forms per rank per attention layer and step."""
+    fwd = 2 * (world - 1) / world * elem_bytes * B * T * C
+    # backward: K, V travel p-1 hops again; dK, dV travel p hops (back to their owner)
+    bwd = (2 * (world - 1) + 2 * world) / world * elem_bytes * B * T * C
     return {"all_gather_kv_forward": 2 * elem_bytes * B * T * C,
             "all_gather_kv_backward_reduce_scatter": 2 * elem_bytes * B * T * C,
-            "ring_forward_send": 2 * (world - 1) / world * elem_bytes * B * T * C}
+            "ring_forward_send": fwd, "ring_backward_send": bwd, "ring_send_total": fwd + bwd}
 
 
 def _project(attn, x):

@@ -85,6 +85,7 @@ class Trainer:
         self.idx = torch.zeros(batch_size, seq_len, dtype=torch.int64, device=self.device)
         self.tgt = torch.zeros(batch_size, seq_len, dtype=torch.int64, device=self.device)
         self.step_num = 0
+        self.h2d_done = torch.cuda.Event()
 
     @property
     def num_parameters(self) -> int:
@@ -97,6 +98,9 @@ class Trainer:
             return idx, targets
         self.idx.copy_(idx, non_blocking=True)
         self.tgt.copy_(targets, non_blocking=True)
+        # a caller that refills the same pinned host buffers waits on this
+        # before overwriting them
+        self.h2d_done.record()
         return self.idx, self.tgt
 
     def step_async(self, idx: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:

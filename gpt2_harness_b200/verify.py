@@ -207,10 +207,8 @@ def compare_native_logits(model: GPT, x: torch.Tensor, device="cuda") -> dict:
     from .models.engine import Engine
     B, T = x.shape
     eng = Engine.from_module(model, device=device)
-    xd = x.to(device)
-    eng.forward(xd, torch.zeros_like(xd))
     V = model.config.vocab_size
-    native = eng.acts(B, T).logits[:, :V].float().cpu().reshape(B, T, V)
+    native = eng.logits(x.to(device)).float().cpu().reshape(B, T, V)
     with torch.no_grad():
         ref = model.to("cpu")(x)["logits"].float()
     d = (native - ref).abs()
