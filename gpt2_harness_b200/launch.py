@@ -99,7 +99,7 @@ def main(argv=None) -> int:
     start_step, state = 0, None
     ck = latest_checkpoint(a.ckpt_dir) if a.ckpt_dir else None
     if ck is not None:
-        full, extra = load_full(ck), load_extra(ck, 0)
+        (full, _), extra = load_full(ck), load_extra(ck, 0)
         load_into_engine(trainer.engine, {k: v.to(dev) for k, v in full.items()}, extra)
         if trainer.ddp is not None:
             trainer.engine.sync_shadow()
