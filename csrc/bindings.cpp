@@ -146,17 +146,17 @@ PYBIND11_MODULE(_C, m) {
   });
 
   m.def("layernorm_bwd", [](int64_t dy, int64_t x, int64_t mean, int64_t rstd, int64_t g,
-                            int64_t dres, int64_t dres_bf16, int64_t partials, int M, int C,
-                            int accumulate, int64_t stream) {
-    int nblk = 0;
+                            int64_t dres, int64_t dres_bf16, int64_t partials, int64_t dgamma,
+                            int64_t dbeta, int64_t dsum, int M, int C, int accumulate,
+                            int acc_params, int acc_sum, int64_t stream) {
     check(layernorm_bwd_launch(P<void>(dy), P<float>(x), P<float>(mean), P<float>(rstd),
                                P<void>(g), P<float>(dres), P<void>(dres_bf16), P<float>(partials),
-                               &nblk, M, C, accumulate, S(stream)),
+                               P<float>(dgamma), P<float>(dbeta), P<float>(dsum), M, C,
+                               accumulate, acc_params, acc_sum, S(stream)),
           "layernorm_bwd");
-    return nblk;
   });
 
-  m.def("layernorm_bwd_blocks", [](int M) { return (M + 31) / 32; });
+  m.def("layernorm_bwd_partial_rows", [](int M) { return layernorm_bwd_partial_rows(M); });
 
   m.def("colsum_f32", [](int64_t in, int R, int C, int64_t out, int acc, int64_t stream) {
     check(colsum_f32_launch(P<float>(in), R, C, P<float>(out), acc, S(stream)), "colsum_f32");

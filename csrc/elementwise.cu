@@ -112,70 +112,93 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x
   }
 }
 
-constexpr int LNB_ROWS = 32;  // rows per CTA in backward (8 warps x 4 rows)
+// LayerNorm backward, one warp per row, CTAs in clusters of LNB_CLUSTER.
+//
+// Per row: dx = rstd * (g*dy - mean(g*dy) - xhat * mean(g*dy*xhat)), written
+// to (or added into) the fp32 residual gradient together with its bf16 copy.
+// The column sums dgamma = sum dy*xhat, dbeta = sum dy and (optionally)
+// dsum = sum dres_out -- the bias gradient of the projection whose output fed
+// this residual stream -- are accumulated per warp in shared memory, reduced
+// across the CTA's 8 warps, then across the cluster's CTAs through
+// distributed shared memory, so each cluster writes ONE partial row
+// [3][C]; ln_param_reduce_kernel adds the per-cluster rows in fixed order.
+// Every load of a row (x, dy and the old dres) is issued before its two
+// reductions, so a warp keeps ~3 row-loads in flight.
+constexpr int LNB_WARPS = 8;
+constexpr int LNB_CLUSTER = 8;
+constexpr int LNB_NSUM = 3;  // dgamma, dbeta, dsum
 
 template <int LN_MAXV>
-__global__ void __launch_bounds__(256) ln_bwd_kernel(
+__global__ void __cluster_dims__(LNB_CLUSTER, 1, 1) __launch_bounds__(256) ln_bwd_kernel(
     const __nv_bfloat16* __restrict__ dy, const float* __restrict__ x,
     const float* __restrict__ mean, const float* __restrict__ rstd,
     const __nv_bfloat16* __restrict__ g, float* __restrict__ dres,
     __nv_bfloat16* __restrict__ dres_bf16, float* __restrict__ partials, int M, int C,
-    int accumulate) {
-  extern __shared__ float sred[];  // [8 warps][2][C]
+    int accumulate, int with_dsum) {
+  extern __shared__ float4 sacc[];  // [LNB_WARPS][LNB_NSUM][C/4]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C4 = C >> 2;
-  float4 dg[LN_MAXV], db[LN_MAXV];
+  const int nsum4 = LNB_NSUM * C4;
+  float4* my = sacc + warp * nsum4;
+  for (int c = lane; c < nsum4; c += 32) my[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  uint2 gw[LN_MAXV];
 #pragma unroll
-  for (int i = 0; i < LN_MAXV; ++i) dg[i] = db[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-
-  for (int rr = 0; rr < LNB_ROWS / 8; ++rr) {
-    const int row = blockIdx.x * LNB_ROWS + warp * (LNB_ROWS / 8) + rr;
-    if (row >= M) break;
-    const float mu = mean[row], rs = rstd[row];
+  for (int i = 0; i < LN_MAXV; ++i) {
+    const int c = lane + 32 * i;
+    gw[i] = c < C4 ? *reinterpret_cast<const uint2*>(g + 4 * c) : make_uint2(0, 0);
+  }
+  const int rpc = (M + gridDim.x - 1) / gridDim.x;
+  const int r0 = blockIdx.x * rpc, r1 = min(M, r0 + rpc);
+  for (int row = r0 + warp; row < r1; row += LNB_WARPS) {
+    const float mu = __ldg(mean + row), rs = __ldg(rstd + row);
     const float4* xr = reinterpret_cast<const float4*>(x + (int64_t)row * C);
     const __nv_bfloat16* dyr = dy + (int64_t)row * C;
-    float4 xh[LN_MAXV], gy[LN_MAXV];
+    float4* dr = reinterpret_cast<float4*>(dres + (int64_t)row * C);
+    float4 xv[LN_MAXV], ov[LN_MAXV];
+    uint2 dw[LN_MAXV];
+#pragma unroll
+    for (int i = 0; i < LN_MAXV; ++i) {
+      const int c = lane + 32 * i;
+      if (c < C4) {
+        xv[i] = __ldcs(xr + c);
+        dw[i] = __ldcs(reinterpret_cast<const uint2*>(dyr + 4 * c));
+        ov[i] = accumulate ? __ldcs(dr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
     for (int i = 0; i < LN_MAXV; ++i) {
       const int c = lane + 32 * i;
       if (c < C4) {
-        const float4 xv = xr[c];
-        const uint2 dw = *reinterpret_cast<const uint2*>(dyr + 4 * c);
-        const uint2 gw = *reinterpret_cast<const uint2*>(g + 4 * c);
-        const float2 d01 = unpack_bf16x2(dw.x), d23 = unpack_bf16x2(dw.y);
-        const float2 g01 = unpack_bf16x2(gw.x), g23 = unpack_bf16x2(gw.y);
-        xh[i] = make_float4((xv.x - mu) * rs, (xv.y - mu) * rs, (xv.z - mu) * rs, (xv.w - mu) * rs);
-        gy[i] = make_float4(d01.x * g01.x, d01.y * g01.y, d23.x * g23.x, d23.y * g23.y);
-        dg[i].x += d01.x * xh[i].x;
-        dg[i].y += d01.y * xh[i].y;
-        dg[i].z += d23.x * xh[i].z;
-        dg[i].w += d23.y * xh[i].w;
-        db[i].x += d01.x;
-        db[i].y += d01.y;
-        db[i].z += d23.x;
-        db[i].w += d23.y;
-        s1 += gy[i].x + gy[i].y + gy[i].z + gy[i].w;
-        s2 += gy[i].x * xh[i].x + gy[i].y * xh[i].y + gy[i].z * xh[i].z + gy[i].w * xh[i].w;
+        const float2 d01 = unpack_bf16x2(dw[i].x), d23 = unpack_bf16x2(dw[i].y);
+        const float2 g01 = unpack_bf16x2(gw[i].x), g23 = unpack_bf16x2(gw[i].y);
+        // xv becomes xhat, dw is kept; gy is recomputed below from dw and gw
+        xv[i] = make_float4((xv[i].x - mu) * rs, (xv[i].y - mu) * rs, (xv[i].z - mu) * rs,
+                            (xv[i].w - mu) * rs);
+        const float gy0 = d01.x * g01.x, gy1 = d01.y * g01.y, gy2 = d23.x * g23.x,
+                    gy3 = d23.y * g23.y;
+        s1 += gy0 + gy1 + gy2 + gy3;
+        s2 += gy0 * xv[i].x + gy1 * xv[i].y + gy2 * xv[i].z + gy3 * xv[i].w;
       }
     }
     s1 = warp_sum(s1) / C;
     s2 = warp_sum(s2) / C;
-    float4* dr = reinterpret_cast<float4*>(dres + (int64_t)row * C);
     __nv_bfloat16* db16 = dres_bf16 ? dres_bf16 + (int64_t)row * C : nullptr;
 #pragma unroll
     for (int i = 0; i < LN_MAXV; ++i) {
       const int c = lane + 32 * i;
       if (c < C4) {
-        float4 d = make_float4(rs * (gy[i].x - s1 - xh[i].x * s2), rs * (gy[i].y - s1 - xh[i].y * s2),
-                               rs * (gy[i].z - s1 - xh[i].z * s2), rs * (gy[i].w - s1 - xh[i].w * s2));
-        if (accumulate) {
-          const float4 o = dr[c];
-          d.x += o.x;
-          d.y += o.y;
-          d.z += o.z;
-          d.w += o.w;
-        }
+        const float2 d01 = unpack_bf16x2(dw[i].x), d23 = unpack_bf16x2(dw[i].y);
+        const float2 g01 = unpack_bf16x2(gw[i].x), g23 = unpack_bf16x2(gw[i].y);
+        const float4 xh = xv[i];
+        float4 d = make_float4(rs * (d01.x * g01.x - s1 - xh.x * s2),
+                               rs * (d01.y * g01.y - s1 - xh.y * s2),
+                               rs * (d23.x * g23.x - s1 - xh.z * s2),
+                               rs * (d23.y * g23.y - s1 - xh.w * s2));
+        d.x += ov[i].x;
+        d.y += ov[i].y;
+        d.z += ov[i].z;
+        d.w += ov[i].w;
         dr[c] = d;
         if (db16) {
           uint2 w;
@@ -183,28 +206,92 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(
           w.y = pack_bf16x2(d.z, d.w);
           *reinterpret_cast<uint2*>(db16 + 4 * c) = w;
         }
+        float4 a = my[c];
+        a.x += d01.x * xh.x;
+        a.y += d01.y * xh.y;
+        a.z += d23.x * xh.z;
+        a.w += d23.y * xh.w;
+        my[c] = a;
+        float4 b = my[C4 + c];
+        b.x += d01.x;
+        b.y += d01.y;
+        b.z += d23.x;
+        b.w += d23.y;
+        my[C4 + c] = b;
+        if (with_dsum) {
+          float4 e = my[2 * C4 + c];
+          e.x += d.x;
+          e.y += d.y;
+          e.z += d.z;
+          e.w += d.w;
+          my[2 * C4 + c] = e;
+        }
       }
     }
   }
-  // Deterministic CTA-level reduction of dgamma/dbeta across the 8 warps.
-#pragma unroll
-  for (int i = 0; i < LN_MAXV; ++i) {
-    const int c = lane + 32 * i;
-    if (c < C4) {
-      reinterpret_cast<float4*>(sred + (warp * 2) * C)[c] = dg[i];
-      reinterpret_cast<float4*>(sred + (warp * 2 + 1) * C)[c] = db[i];
-    }
-  }
   __syncthreads();
-  const int nblk = gridDim.x;
-  for (int c = threadIdx.x; c < C; c += blockDim.x) {
-    float a = 0.f, b = 0.f;
-    for (int w = 0; w < 8; ++w) {
-      a += sred[(w * 2) * C + c];
-      b += sred[(w * 2 + 1) * C + c];
+  // CTA: fold the 8 warps' sums into warp 0's slot (fixed order).
+  for (int c = threadIdx.x; c < nsum4; c += blockDim.x) {
+    float4 t = sacc[c];
+#pragma unroll
+    for (int w = 1; w < LNB_WARPS; ++w) {
+      const float4 u = sacc[w * nsum4 + c];
+      t.x += u.x;
+      t.y += u.y;
+      t.z += u.z;
+      t.w += u.w;
     }
-    partials[(int64_t)blockIdx.x * C + c] = a;
-    partials[(int64_t)(nblk + blockIdx.x) * C + c] = b;
+    sacc[c] = t;
+  }
+  cluster_sync_all();
+  // Cluster: CTA k adds chunk k of the columns across the cluster's CTAs
+  // through DSMEM, in rank order, and writes the cluster's partial row.
+  const uint32_t rank = cluster_ctarank();
+  const int per = (nsum4 + LNB_CLUSTER - 1) / LNB_CLUSTER;
+  const int c0 = rank * per, c1 = min(nsum4, c0 + per);
+  float4* out = reinterpret_cast<float4*>(partials) + (int64_t)cluster_id_x() * nsum4;
+  for (int c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
+    const uint32_t local = smem_u32(sacc + c);
+    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < LNB_CLUSTER; ++q) {
+      const float4 u = ld_shared_cluster_f4(map_shared_rank(local, q));
+      t.x += u.x;
+      t.y += u.y;
+      t.z += u.z;
+      t.w += u.w;
+    }
+    out[c] = t;
+  }
+  cluster_sync_all();  // peers' shared memory must outlive the reads above
+}
+
+// dgamma/dbeta/dsum (+)= sum over the P per-cluster rows of partials[P][3][C]
+// (fixed row order). Block = 32 columns x 8 row lanes.
+__global__ void __launch_bounds__(256) ln_param_reduce_kernel(
+    const float* __restrict__ partials, int P, int C, float* __restrict__ dgamma,
+    float* __restrict__ dbeta, float* __restrict__ dsum, int acc_params, int acc_sum) {
+  __shared__ float red[8][33];
+  const int n = (dsum ? 3 : 2) * C;
+  const int c = blockIdx.x * 32 + threadIdx.x;
+  float s = 0.f;
+  if (c < n) {
+#pragma unroll 4
+    for (int r = threadIdx.y; r < P; r += 8) s += partials[(int64_t)r * 3 * C + c];
+  }
+  red[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y == 0 && c < n) {
+    float t = 0.f;
+#pragma unroll
+    for (int y = 0; y < 8; ++y) t += red[y][threadIdx.x];
+    if (c < C) {
+      dgamma[c] = acc_params ? dgamma[c] + t : t;
+    } else if (c < 2 * C) {
+      dbeta[c - C] = acc_params ? dbeta[c - C] + t : t;
+    } else {
+      dsum[c - 2 * C] = acc_sum ? dsum[c - 2 * C] + t : t;
+    }
   }
 }
 
@@ -586,23 +673,51 @@ int layernorm_fwd_launch(const float* x, int64_t ldx, const void* gamma, const v
   });
 }
 
+static int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+int layernorm_bwd_ctas(int M) {
+  // Two resident CTAs per SM, a whole number of clusters, at least 8 rows each.
+  int n = 2 * sm_count();
+  const int by_rows = (M + 7) / 8;
+  if (n > by_rows) n = by_rows;
+  n = (n + LNB_CLUSTER - 1) / LNB_CLUSTER * LNB_CLUSTER;
+  return n < LNB_CLUSTER ? LNB_CLUSTER : n;
+}
+
+int layernorm_bwd_partial_rows(int M) { return layernorm_bwd_ctas(M) / LNB_CLUSTER; }
+
 int layernorm_bwd_launch(const void* dy, const float* x, const float* mean, const float* rstd,
                          const void* gamma, float* dres, void* dres_bf16, float* partials,
-                         int* nblk_out, int M, int C, int accumulate, cudaStream_t s) {
-  if (C % 4 || C > 4 * 32 * LN_MAXV_CAP) return -1;
-  const int nblk = (M + LNB_ROWS - 1) / LNB_ROWS;
-  const int smem = 16 * C * (int)sizeof(float);
-  if (nblk_out) *nblk_out = nblk;
-  return ln_dispatch(C, [&](auto nv) {
+                         float* dgamma, float* dbeta, float* dsum, int M, int C, int accumulate,
+                         int acc_params, int acc_sum, cudaStream_t s) {
+  if (C % 4 || C > 4 * 32 * LN_MAXV_CAP || M <= 0) return -1;
+  const int nblk = layernorm_bwd_ctas(M);
+  const int smem = LNB_WARPS * LNB_NSUM * C * (int)sizeof(float);
+  const int rc = ln_dispatch(C, [&](auto nv) {
     auto kern = ln_bwd_kernel<decltype(nv)::value>;
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     kern<<<nblk, 256, smem, s>>>((const __nv_bfloat16*)dy, x, mean, rstd,
                                  (const __nv_bfloat16*)gamma, dres, (__nv_bfloat16*)dres_bf16,
-                                 partials, M, C, accumulate);
-                                 count_launches(1);
+                                 partials, M, C, accumulate, dsum != nullptr);
+    count_launches(1);
     return ok();
   });
+  if (rc) return rc;
+  const int n = (dsum ? 3 : 2) * C;
+  ln_param_reduce_kernel<<<(n + 31) / 32, dim3(32, 8), 0, s>>>(
+      partials, nblk / LNB_CLUSTER, C, dgamma, dbeta, dsum, acc_params, acc_sum);
+  count_launches(1);
+  return ok();
 }
 
 int colsum_f32_launch(const float* in, int R, int C, float* out, int accumulate, cudaStream_t s) {

@@ -14,12 +14,16 @@ int layernorm_fwd_launch(const float* x, int64_t ldx, const void* gamma, const v
 
 // LayerNorm backward. dy bf16 [M,C]; x fp32; writes/accumulates the fp32
 // residual gradient dres[M,C] (dres = (accumulate ? dres : 0) + dx) and its bf16
-// copy dres_bf16 (may be null). Per-CTA partial dgamma/dbeta rows go to
-// `partials` ([2, nblk, C] fp32); *nblk_out receives nblk. Reduce with
-// colsum_f32_launch.
+// copy dres_bf16 (may be null); dgamma/dbeta (+)= their column sums
+// (acc_params) and, when dsum is non-null, dsum (+)= the column sum of the
+// written dres (acc_sum) -- the bias gradient of the projection that produced
+// this residual stream. `partials` is scratch of
+// layernorm_bwd_partial_rows(M) * 3 * C floats. Two launches, deterministic.
 int layernorm_bwd_launch(const void* dy, const float* x, const float* mean, const float* rstd,
                          const void* gamma, float* dres, void* dres_bf16, float* partials,
-                         int* nblk_out, int M, int C, int accumulate, cudaStream_t s);
+                         float* dgamma, float* dbeta, float* dsum, int M, int C, int accumulate,
+                         int acc_params, int acc_sum, cudaStream_t s);
+int layernorm_bwd_partial_rows(int M);
 
 // out[c] (+)= sum_r in[r, c] for fp32 in[R, C] (deterministic, row order).
 int colsum_f32_launch(const float* in, int R, int C, float* out, int accumulate, cudaStream_t s);

@@ -243,7 +243,12 @@ class Engine:
         self.exp_avg_sq = torch.zeros(n, dtype=torch.float32, device=dev)
         self.step_count = 0
         self._acts: Optional[_Acts] = None
-        self._hp_host = torch.zeros(8, dtype=torch.float32).pin_memory()
+        # Hyperparameters reach the device by an async copy from pinned memory
+        # each step. The host may run several steps ahead of the GPU, so the
+        # pinned source rotates through a ring and a slot is reused only after
+        # the copy that read it has executed.
+        self._hp_ring = [torch.zeros(8, dtype=torch.float32).pin_memory() for _ in range(4)]
+        self._hp_events: list = [None] * len(self._hp_ring)
         self.hp = torch.zeros(8, dtype=torch.float32, device=dev)
         self._norm_ws = torch.empty(1024, dtype=torch.float32, device=dev)
         self.sumsq = torch.zeros(1, dtype=torch.float32, device=dev)
@@ -398,9 +403,12 @@ class Engine:
         N.gemm(logits, p("wte.weight"), A.dh, b_t=True, alpha_ptr=inv_count)
         N.gemm(logits, A.hf, g("wte.weight"), a_t=True, b_t=True, epilogue=N.EPI_F32,
                alpha_ptr=inv_count, accumulate=acc)
+        # LN backward also sums the residual gradient it writes: that column
+        # sum is the bias gradient of the projection that produced the stream
         N.layernorm_bwd(A.dh, A.x[2 * L], A.mu[2 * L], A.rs[2 * L], p("ln_f.weight"), A.dres,
                         A.dres16, g("ln_f.weight"), g("ln_f.bias"), A.ln_parts,
-                        accumulate_dres=False, accumulate_params=acc)
+                        accumulate_dres=False, accumulate_params=acc,
+                        dsum=g(f"h.{L - 1}.mlp.c_proj.bias"), accumulate_dsum=acc)
         if hook:
             hook("root_head")
         ws = A.splitk_ws
@@ -411,7 +419,6 @@ class Engine:
                    aux=A.u[l])
             N.gemm(A.dres16, A.g[l], g(pre + "mlp.c_proj.weight"), a_t=True, b_t=True,
                    epilogue=N.EPI_F32, accumulate=acc, splits=A.splits["mlp_proj"], workspace=ws)
-            N.colsum_bf16(A.dres16, g(pre + "mlp.c_proj.bias"), A.col_ws, accumulate=acc)
             # mlp.c_fc
             N.gemm(A.du, p(pre + "mlp.c_fc.weight"), A.dh, b_t=True)
             N.gemm(A.du, A.h2[l], g(pre + "mlp.c_fc.weight"), a_t=True, b_t=True,
@@ -420,12 +427,12 @@ class Engine:
             N.layernorm_bwd(A.dh, A.x[2 * l + 1], A.mu[2 * l + 1], A.rs[2 * l + 1],
                             p(pre + "ln_2.weight"), A.dres, A.dres16, g(pre + "ln_2.weight"),
                             g(pre + "ln_2.bias"), A.ln_parts, accumulate_dres=True,
-                            accumulate_params=acc)
+                            accumulate_params=acc, dsum=g(pre + "attn.c_proj.bias"),
+                            accumulate_dsum=acc)
             # attn.c_proj
             N.gemm(A.dres16, p(pre + "attn.c_proj.weight"), A.dy, b_t=True)
             N.gemm(A.dres16, A.y[l], g(pre + "attn.c_proj.weight"), a_t=True, b_t=True,
                    epilogue=N.EPI_F32, accumulate=acc, splits=A.splits["c_proj"], workspace=ws)
-            N.colsum_bf16(A.dres16, g(pre + "attn.c_proj.bias"), A.col_ws, accumulate=acc)
             # attention
             qkv, dqkv = A.qkv[l], A.dqkv
             N.attention_bwd(qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:], A.y[l], A.dy,
@@ -437,7 +444,9 @@ class Engine:
             N.colsum_bf16(dqkv, g(pre + "attn.c_attn.bias"), A.col_ws, accumulate=acc)
             N.layernorm_bwd(A.dh, A.x[2 * l], A.mu[2 * l], A.rs[2 * l], p(pre + "ln_1.weight"),
                             A.dres, A.dres16, g(pre + "ln_1.weight"), g(pre + "ln_1.bias"),
-                            A.ln_parts, accumulate_dres=True, accumulate_params=acc)
+                            A.ln_parts, accumulate_dres=True, accumulate_params=acc,
+                            dsum=g(f"h.{l - 1}.mlp.c_proj.bias") if l > 0 else None,
+                            accumulate_dsum=acc)
             if hook:
                 hook(f"h.{l}")
         wpe_g = g("wpe.weight")
@@ -456,7 +465,10 @@ class Engine:
         o = self.optim
         self.step_count += 1
         t = self.step_count
-        hp = self._hp_host
+        slot = t % len(self._hp_ring)
+        if self._hp_events[slot] is not None:
+            self._hp_events[slot].synchronize()
+        hp = self._hp_ring[slot]
         hp[0] = o.lr
         hp[1] = o.betas[0]
         hp[2] = o.betas[1]
@@ -466,6 +478,9 @@ class Engine:
         hp[6] = math.sqrt(1.0 - o.betas[1] ** t)
         hp[7] = self.grad_scale
         self.hp.copy_(hp, non_blocking=True)
+        ev = self._hp_events[slot] or torch.cuda.Event()
+        ev.record()
+        self._hp_events[slot] = ev
         clip = None
         if o.grad_clip and o.grad_clip > 0:
             N.grad_sumsq(self.grad, self._norm_ws, self.sumsq)

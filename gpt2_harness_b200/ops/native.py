@@ -259,23 +259,30 @@ def layernorm_fwd(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, y: t
 
 
 def layernorm_bwd_partials(M: int, C: int, device) -> torch.Tensor:
-    nblk = lib().layernorm_bwd_blocks(M)
-    return torch.empty(2, nblk, C, dtype=torch.float32, device=device)
+    """Scratch for :func:`layernorm_bwd`: one [3, C] fp32 row per CTA cluster."""
+    rows = lib().layernorm_bwd_partial_rows(M)
+    return torch.empty(rows, 3, C, dtype=torch.float32, device=device)
 
 
 def layernorm_bwd(dy: torch.Tensor, x: torch.Tensor, mean: torch.Tensor, rstd: torch.Tensor,
                   gamma: torch.Tensor, dres: torch.Tensor, dres_bf16: Optional[torch.Tensor],
                   dgamma: torch.Tensor, dbeta: torch.Tensor, partials: torch.Tensor,
-                  accumulate_dres: bool, accumulate_params: bool = True) -> None:
-    """LN backward: dres (+)= dx (fp32, plus optional bf16 copy); dgamma/dbeta (+)=."""
+                  accumulate_dres: bool, accumulate_params: bool = True,
+                  dsum: Optional[torch.Tensor] = None, accumulate_dsum: bool = False) -> None:
+    """LN backward: dres (+)= dx (fp32, plus optional bf16 copy); dgamma/dbeta (+)=.
+
+    With ``dsum`` (fp32 [C]), also dsum (+)= the column sum of the written
+    dres: the bias gradient of the projection whose output is this residual
+    stream, fused here instead of a separate reduction over its bf16 copy.
+    """
     M, C = x.shape
-    L = lib()
-    nblk = L.layernorm_bwd(dy.data_ptr(), x.data_ptr(), mean.data_ptr(), rstd.data_ptr(),
-                           gamma.data_ptr(), dres.data_ptr(), _ptr(dres_bf16),
-                           partials.data_ptr(), M, C, int(accumulate_dres), _stream())
-    L.colsum_f32(partials.data_ptr(), nblk, C, dgamma.data_ptr(), int(accumulate_params), _stream())
-    L.colsum_f32(partials.data_ptr() + nblk * C * 4, nblk, C, dbeta.data_ptr(),
-                 int(accumulate_params), _stream())
+    if partials.numel() < lib().layernorm_bwd_partial_rows(M) * 3 * C:
+        raise ValueError("layernorm_bwd partials too small")
+    lib().layernorm_bwd(dy.data_ptr(), x.data_ptr(), mean.data_ptr(), rstd.data_ptr(),
+                        gamma.data_ptr(), dres.data_ptr(), _ptr(dres_bf16), partials.data_ptr(),
+                        dgamma.data_ptr(), dbeta.data_ptr(), _ptr(dsum), M, C,
+                        int(accumulate_dres), int(accumulate_params), int(accumulate_dsum),
+                        _stream())
 
 
 def colsum_bf16(x: torch.Tensor, out: torch.Tensor, ws: torch.Tensor, accumulate: bool = True) -> None:

@@ -208,12 +208,23 @@ def test_layernorm(M, C):
     dres16 = torch.empty(M, C, dtype=torch.bfloat16, device=dev())
     dg = torch.zeros(C, device=dev())
     db = torch.zeros(C, device=dev())
+    ds = torch.full((C,), 2.0, device=dev())
     parts = N.layernorm_bwd_partials(M, C, dev())
-    N.layernorm_bwd(dy, x, mean, rstd, g, dres, dres16, dg, db, parts, accumulate_dres=True)
+    N.layernorm_bwd(dy, x, mean, rstd, g, dres, dres16, dg, db, parts, accumulate_dres=True,
+                    dsum=ds, accumulate_dsum=True)
     assert rel_err(dres - 1, gx) < 1e-4
     assert rel_err(dres16, gx + 1) < 1e-2
     assert rel_err(dg, gg) < 1e-4
     assert rel_err(db, gb) < 1e-4
+    # dsum = 2 + column sum of the written residual gradient (gx + 1)
+    assert rel_err(ds, 2 + (gx + 1).sum(0)) < 1e-4
+    # deterministic: a second identical launch gives bit-identical sums
+    dres2 = torch.ones(M, C, device=dev())
+    dg2 = torch.zeros(C, device=dev())
+    db2 = torch.zeros(C, device=dev())
+    N.layernorm_bwd(dy, x, mean, rstd, g, dres2, None, dg2, db2, parts, accumulate_dres=True,
+                    accumulate_params=False)
+    assert torch.equal(dres2, dres) and torch.equal(dg2, dg) and torch.equal(db2, db)
 
 
 def test_colsum_bf16():
