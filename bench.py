@@ -28,6 +28,11 @@ copied from pinned host memory and the loss read back to the host.
 the reference repository) through its own public API: its `GPT` under bf16
 autocast, `torch.optim.AdamW` from `configure_optimizers`, its
 `average_gradients` (25 MiB buckets over NCCL) for N > 1, and clipping.
+
+`--strategy zero2` measures the same model and batch under ZeRO-2 instead of
+DDP: natively the bucketed peer-memory reduce-scatter overlapped with backward
+plus the fused clip/AdamW/bf16 all-gather kernel; on the reference arm its
+`ShardedAdamW(stage=2, grad_clip=1.0, param_dtype=bf16)` over NCCL.
 """
 
 from __future__ import annotations
@@ -196,7 +201,8 @@ def run_native(args, world, rank):
 
     cfg = gpt2_config(args.model)
     tc = TrainConfig(lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, grad_clip=1.0, warmup_steps=0)
-    trainer = Trainer(cfg, args.batch, args.seq, train=tc, comm=args.comm, schedule=False)
+    trainer = Trainer(cfg, args.batch, args.seq, train=tc, comm=args.comm, schedule=False,
+                      strategy=args.strategy)
     host, dev = make_data(cfg, args.batch, args.seq, rank)
     L = N.lib()
 
@@ -231,7 +237,7 @@ def run_native(args, world, rank):
     bo = 4  # fp32 loss scalar
     out = finish_line(args, world, cfg, ms, ms_e2e, bi, bo, sampler, impl="native")
     out["gpu_launches"] = int(n_launch)
-    out["config"]["comm"] = args.comm if world > 1 else "none"
+    out["config"]["comm"] = (args.comm if args.strategy == "ddp" else "p2p") if world > 1 else "none"
     trainer.close()
     return out
 
@@ -251,19 +257,35 @@ def run_reference(args, world, rank):
     if world > 1:
         for p in model.parameters():
             dist.broadcast(p.data, src=0)
-    opt = model.configure_optimizers(0.1, 3e-4, (0.9, 0.95))
     host, dev = make_data(cfg, args.batch, args.seq, rank)
+    if args.strategy == "zero2":
+        from transformer_internals.parallel.zero import ShardedAdamW
 
-    def train_step(idx, tgt):
-        with torch.autocast("cuda", dtype=torch.bfloat16):
-            loss = model(idx, tgt)["loss"]
-        opt.zero_grad(set_to_none=True)
-        loss.backward()
-        if world > 1:
-            average_gradients(model.parameters(), world)
-        torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
-        opt.step()
-        return loss
+        zopt = ShardedAdamW(list(model.parameters()), rank, world, stage=2, lr=3e-4,
+                            betas=(0.9, 0.95), weight_decay=0.1, grad_clip=1.0,
+                            param_dtype=torch.bfloat16)
+
+        def train_step(idx, tgt):
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                loss = model(idx, tgt)["loss"]
+            for p in model.parameters():
+                p.grad = None
+            loss.backward()
+            zopt.step()
+            return loss
+    else:
+        opt = model.configure_optimizers(0.1, 3e-4, (0.9, 0.95))
+
+        def train_step(idx, tgt):
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                loss = model(idx, tgt)["loss"]
+            opt.zero_grad(set_to_none=True)
+            loss.backward()
+            if world > 1:
+                average_gradients(model.parameters(), world)
+            torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+            opt.step()
+            return loss
 
     def dev_step(i):
         idx, tgt = dev[i % len(dev)]
@@ -324,8 +346,8 @@ def finish_line(args, world, cfg, ms, ms_e2e, bi, bo, sampler, impl):
             "global_batch": args.batch * world,
             "per_gpu_batch": args.batch,
             "seq_len": args.seq,
-            "parallelism": f"dp{world}",
-            "strategy": "ddp",
+            "parallelism": f"dp{world}" if args.strategy == "ddp" else f"zero2-dp{world}",
+            "strategy": args.strategy,
             "bucket_mb": 25,
             "optimizer": "AdamW + clip 1.0, fp32 master",
             "l2": "inputs larger than L2 (per-step working set ~10 GB >> 126 MB), no flush",
@@ -350,6 +372,7 @@ def main():
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--seq", type=int, default=1024)
     ap.add_argument("--comm", choices=["p2p", "nccl"], default="p2p")
+    ap.add_argument("--strategy", choices=["ddp", "zero2"], default="ddp")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

@@ -15,6 +15,7 @@
 #include "elementwise.cuh"
 #include "gemm.cuh"
 #include "launch_count.h"
+#include "zero.cuh"
 
 namespace py = pybind11;
 using namespace g2b;
@@ -259,6 +260,47 @@ PYBIND11_MODULE(_C, m) {
           c.wait_budget_ns = wait_budget_ns;
           check(comm_allreduce_launch(c, S(stream)), "allreduce_p2p");
         });
+  // ZeRO-2 kernels: every argument is passed by name in a dict (int pointers,
+  // ints, floats); see csrc/zero.cuh for their meaning.
+  auto zero_args = [](const py::dict& d) {
+    auto I = [&](const char* k) { return d[k].cast<int64_t>(); };
+    ZeroArgs z;
+    z.peer_grad = P<float*>(I("peer_grad"));
+    z.peer_shadow = P<__nv_bfloat16*>(I("peer_shadow"));
+    z.peer_flags = P<uint32_t*>(I("peer_flags"));
+    z.peer_norm = P<unsigned long long*>(I("peer_norm"));
+    z.rank = (int)I("rank");
+    z.world = (int)I("world");
+    z.buckets = P<int64_t>(I("buckets"));
+    z.nb = (int)I("nb");
+    z.bucket = (int)I("bucket");
+    z.rs_blocks = (int)I("rs_blocks");
+    z.gsh = P<float>(I("gsh"));
+    z.master = P<float>(I("master"));
+    z.exp_avg = P<float>(I("exp_avg"));
+    z.exp_avg_sq = P<float>(I("exp_avg_sq"));
+    z.sumsq_parts = P<float>(I("sumsq_parts"));
+    z.decay_ranges = P<int64_t>(I("decay_ranges"));
+    z.nr = (int)I("nr");
+    z.hp = P<float>(I("hp"));
+    z.max_norm = d["max_norm"].cast<float>();
+    z.scale = d["scale"].cast<float>();
+    z.epoch = (uint32_t)I("epoch");
+    z.byte_counter = P<unsigned long long>(I("byte_counter"));
+    z.norm_out = P<float>(I("norm_out"));
+    z.err = P<uint32_t>(I("err"));
+    z.wait_budget_ns = I("wait_budget_ns");
+    return z;
+  };
+  m.def("zero_rs", [zero_args](const py::dict& d, int64_t stream) {
+    check(zero_rs_launch(zero_args(d), S(stream)), "zero_rs");
+  });
+  m.def("zero_adamw_ag", [zero_args](const py::dict& d, int nblocks, int64_t stream) {
+    check(zero_adamw_ag_launch(zero_args(d), nblocks, S(stream)), "zero_adamw_ag");
+  });
+  m.def("zero_flag_words", []() { return 2 * kCommMaxRanks * kZeroMaxBlocks; });
+  m.def("zero_norm_words", []() { return 2 * kZeroMaxBlocks * kCommMaxRanks; });
+  m.def("zero_max_blocks", []() { return kZeroMaxBlocks; });
   m.def("comm_flag_words", []() { return 2 * kCommMaxRanks * kCommMaxBlocks; });
   m.def("flag_wait_test", [](int64_t flag, uint32_t value, int64_t budget_ns, int64_t err,
                              int64_t stream) {

@@ -273,19 +273,45 @@ def load_extra(directory, rank: int) -> dict:
 
 
 # ------------------------------------------------------------- native engine --
-def engine_state_dict(engine, with_optimizer: bool = False) -> tuple[dict, dict]:
+def engine_state_dict(engine, with_optimizer: bool = False, zero=None) -> tuple[dict, dict]:
     """(tensors, extra) of a native Engine in the reference naming (fp32);
-    with_optimizer adds flat AdamW moments and step to `extra`."""
-    sd = {s.name: engine.p32(s.name).detach() for s in engine.layout.specs}
+    with_optimizer adds flat AdamW moments and step to `extra`.
+
+    Under ZeRO-2 pass the engine's ``NativeZeRO`` as `zero`: the master
+    weights and moments are then gathered from the shards (a collective that
+    every rank must enter) into the same full-vector format DDP writes, so a
+    checkpoint resumes under either strategy and any world size."""
     extra: dict[str, Any] = {"optim_step": engine.step_count}
+    if zero is not None:
+        full = zero.full_master()
+        sd = {s.name: engine.layout.view(full, s.name) for s in engine.layout.specs}
+        if with_optimizer:
+            extra["exp_avg"] = zero.gather_full(zero.exp_avg).cpu()
+            extra["exp_avg_sq"] = zero.gather_full(zero.exp_avg_sq).cpu()
+        return sd, extra
+    sd = {s.name: engine.p32(s.name).detach() for s in engine.layout.specs}
     if with_optimizer:
         extra["exp_avg"] = engine.exp_avg.detach().cpu()
         extra["exp_avg_sq"] = engine.exp_avg_sq.detach().cpu()
     return sd, extra
 
 
-def load_into_engine(engine, state: dict, extra: Optional[dict] = None) -> None:
-    """Load reference-named tensors (+ optional moments) into an Engine."""
+def load_into_engine(engine, state: dict, extra: Optional[dict] = None, zero=None) -> None:
+    """Load reference-named tensors (+ optional moments) into an Engine (or,
+    with `zero`, into the ZeRO-2 shards and the full bf16 parameters)."""
+    if zero is not None:
+        full = torch.zeros(engine.layout.total, dtype=torch.float32, device=engine.device)
+        for s in engine.layout.specs:
+            src = state[s.name] if s.name in state else state["lm_head.weight"]
+            engine.layout.view(full, s.name).copy_(src.to(engine.device, torch.float32).view(s.shape))
+        ea = eq = None
+        if extra and "exp_avg" in extra:
+            ea = extra["exp_avg"].to(engine.device)
+            eq = extra["exp_avg_sq"].to(engine.device)
+        zero.load_full(full, ea, eq)
+        if extra:
+            engine.step_count = int(extra.get("optim_step", engine.step_count))
+        return
     engine.load_state_dict(state)
     if extra:
         if "exp_avg" in extra:

@@ -77,6 +77,7 @@ def main(argv=None) -> int:
     ap.add_argument("--ckpt-dir", default=None)
     ap.add_argument("--ckpt-every", type=int, default=500)
     ap.add_argument("--log", default=None, help="JSONL metrics (rank 0)")
+    ap.add_argument("--strategy", choices=["ddp", "zero2"], default="ddp")
     ap.add_argument("--seed", type=int, default=0)
     a = ap.parse_args(argv)
 
@@ -93,15 +94,17 @@ def main(argv=None) -> int:
 
     cfg = gpt2_config(a.model, n_positions=max(a.seq, gpt2_config(a.model).n_positions))
     tc = TrainConfig(steps=a.steps, batch_size=a.batch, block_size=a.seq, lr=a.lr, warmup_steps=a.warmup)
-    trainer = Trainer(cfg, a.batch, a.seq, train=tc, comm=a.comm, device=dev, seed=a.seed)
+    trainer = Trainer(cfg, a.batch, a.seq, train=tc, comm=a.comm, device=dev, seed=a.seed,
+                      strategy=a.strategy)
     src = TokenShardSource(a.data, a.seq) if a.data else _SyntheticTokens(cfg.vocab_size, a.seq, seed=a.seed)
 
     start_step, state = 0, None
     ck = latest_checkpoint(a.ckpt_dir) if a.ckpt_dir else None
     if ck is not None:
         (full, _), extra = load_full(ck), load_extra(ck, 0)
-        load_into_engine(trainer.engine, {k: v.to(dev) for k, v in full.items()}, extra)
-        if trainer.ddp is not None:
+        zero = trainer.ddp if trainer.strategy == "zero2" else None
+        load_into_engine(trainer.engine, {k: v.to(dev) for k, v in full.items()}, extra, zero=zero)
+        if trainer.ddp is not None and zero is None:
             trainer.engine.sync_shadow()
         start_step = int(extra.get("step", 0))
         state = StreamState.from_dict(extra["stream"]) if "stream" in extra else None
@@ -131,8 +134,12 @@ def main(argv=None) -> int:
                     allp = [None] * world
                     dist.all_gather_object(allp, stream.position)
                     pos = allp
+                zero = trainer.ddp if trainer.strategy == "zero2" else None
+                if zero is not None:  # gathering the shards is a collective
+                    sd, extra = engine_state_dict(trainer.engine, with_optimizer=True, zero=zero)
                 if rank == 0:
-                    sd, extra = engine_state_dict(trainer.engine, with_optimizer=True)
+                    if zero is None:
+                        sd, extra = engine_state_dict(trainer.engine, with_optimizer=True)
                     extra.update(step=step, stream=stream.state_dict(pos))
                     ckpt.save(Path(a.ckpt_dir) / f"step_{step}", sd, plan={}, rank=0, world_size=1, step=step,
                               global_shapes={k: list(v.shape) for k, v in sd.items()}, extra=extra)

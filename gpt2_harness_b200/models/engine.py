@@ -216,12 +216,18 @@ class Engine:
         optim: AdamW / clipping settings.
         grad_buffer: optional externally owned fp32 flat gradient buffer of
             ``layout.total`` elements (DDP passes its peer-mapped buffer).
+        shadow_buffer: optional externally owned bf16 flat parameter buffer
+            the kernels read (ZeRO passes a peer-mapped buffer that every rank
+            writes its updated slice into).
         seed: init seed for :meth:`init_weights` (ignored if weights loaded).
+        optimizer_state: ``False`` skips allocating the full-size AdamW
+            moments (a sharded optimiser owns them).
     """
 
     def __init__(self, config: GPTConfig, device: torch.device | str = "cuda", *,
                  optim: Optional[OptimConfig] = None, grad_buffer: Optional[torch.Tensor] = None,
-                 seed: Optional[int] = 0) -> None:
+                 shadow_buffer: Optional[torch.Tensor] = None, seed: Optional[int] = 0,
+                 optimizer_state: bool = True) -> None:
         self.config = config
         self.device = torch.device(device)
         if self.device.type != "cuda":
@@ -232,15 +238,23 @@ class Engine:
         n = self.layout.total
         dev = self.device
         self.master = torch.zeros(n, dtype=torch.float32, device=dev)
-        self.shadow = torch.zeros(n, dtype=torch.bfloat16, device=dev)
+        if shadow_buffer is not None:
+            if shadow_buffer.numel() < n or shadow_buffer.dtype != torch.bfloat16:
+                raise ValueError("shadow_buffer too small or not bf16")
+            self.shadow = shadow_buffer[:n]
+        else:
+            self.shadow = torch.zeros(n, dtype=torch.bfloat16, device=dev)
         if grad_buffer is not None:
             if grad_buffer.numel() < n or grad_buffer.dtype != torch.float32:
                 raise ValueError("grad_buffer too small or not fp32")
             self.grad = grad_buffer[:n]
         else:
             self.grad = torch.zeros(n, dtype=torch.float32, device=dev)
-        self.exp_avg = torch.zeros(n, dtype=torch.float32, device=dev)
-        self.exp_avg_sq = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.exp_avg = torch.zeros(n, dtype=torch.float32, device=dev) if optimizer_state else None
+        self.exp_avg_sq = torch.zeros(n, dtype=torch.float32, device=dev) if optimizer_state else None
+        # A sharded optimiser replaces the update: optimizer_impl(hp) is called
+        # with the device hyperparameter vector instead of the local AdamW.
+        self.optimizer_impl: Optional[Callable[[torch.Tensor], None]] = None
         self.step_count = 0
         self._acts: Optional[_Acts] = None
         # Hyperparameters reach the device by an async copy from pinned memory
@@ -481,6 +495,9 @@ class Engine:
         ev = self._hp_events[slot] or torch.cuda.Event()
         ev.record()
         self._hp_events[slot] = ev
+        if self.optimizer_impl is not None:
+            self.optimizer_impl(self.hp)
+            return
         clip = None
         if o.grad_clip and o.grad_clip > 0:
             N.grad_sumsq(self.grad, self._norm_ws, self.sumsq)

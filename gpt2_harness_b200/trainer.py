@@ -3,8 +3,11 @@
 ``Trainer`` is the call a user makes: give it a config and a per-rank batch
 shape, then call :meth:`Trainer.step` with token ids and targets (host or
 device tensors). Under ``torchrun`` with more than one rank it runs data
-parallel (:class:`~gpt2_harness_b200.parallel.ddp_native.NativeDDP`) with the
-gradient all-reduce overlapped with backward.
+parallel with the gradient communication overlapped with backward, either as
+DDP (:class:`~gpt2_harness_b200.parallel.ddp_native.NativeDDP`, all-reduce,
+every rank updates every parameter) or as ZeRO-2
+(:class:`~gpt2_harness_b200.parallel.zero_native.NativeZeRO`, reduce-scatter,
+sharded AdamW and optimiser state, fused bf16 all-gather).
 
 The learning-rate schedule is the reference's (train.py:72-99): linear warmup
 to ``lr`` over ``warmup_steps``, then cosine decay to ``lr * min_lr_ratio``.
@@ -45,7 +48,8 @@ class Trainer:
         train: optimiser settings and LR schedule (``TrainConfig``); ``None``
             uses a constant ``lr`` from its defaults.
         comm: ``"p2p"`` (fused peer-memory all-reduce) or ``"nccl"`` when the
-            default process group has more than one rank.
+            default process group has more than one rank (DDP only).
+        strategy: ``"ddp"`` or ``"zero2"`` (ignored on one rank).
         seed: weight init seed (identical on every rank; rank 0's weights are
             broadcast to make sure).
     """
@@ -53,7 +57,8 @@ class Trainer:
     def __init__(self, config: GPTConfig, batch_size: int, seq_len: int, *,
                  train: Optional[TrainConfig] = None, comm: str = "p2p",
                  device: Optional[torch.device] = None, seed: int = 0,
-                 bucket_bytes: int = 25 * 1024 * 1024, schedule: bool = True) -> None:
+                 bucket_bytes: int = 25 * 1024 * 1024, schedule: bool = True,
+                 strategy: str = "ddp") -> None:
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device())
         self.device = torch.device(device)
@@ -67,16 +72,29 @@ class Trainer:
         tc = self.train_cfg
         optim = OptimConfig(lr=tc.lr, betas=tuple(tc.betas), eps=tc.eps,
                             weight_decay=tc.weight_decay, grad_clip=tc.grad_clip)
+        if strategy not in ("ddp", "zero2"):
+            raise ValueError(f"unknown strategy {strategy!r}")
+        self.strategy = strategy if self.world > 1 else "single"
         self.ddp = None
-        grad_buffer = None
+        grad_buffer = shadow_buffer = None
         if self.world > 1:
             from gpt2_harness_b200.models.engine import ParamLayout
-            from gpt2_harness_b200.parallel.ddp_native import NativeDDP
 
-            self.ddp = NativeDDP(ParamLayout(config), comm=comm, bucket_bytes=bucket_bytes,
-                                 device=self.device)
+            layout = ParamLayout(config)
+            if strategy == "zero2":
+                from gpt2_harness_b200.parallel.zero_native import NativeZeRO
+
+                self.ddp = NativeZeRO(layout, bucket_bytes=bucket_bytes, device=self.device)
+                shadow_buffer = self.ddp.shadow_buffer
+            else:
+                from gpt2_harness_b200.parallel.ddp_native import NativeDDP
+
+                self.ddp = NativeDDP(layout, comm=comm, bucket_bytes=bucket_bytes,
+                                     device=self.device)
             grad_buffer = self.ddp.grad_buffer
-        self.engine = Engine(config, self.device, optim=optim, grad_buffer=grad_buffer, seed=seed)
+        self.engine = Engine(config, self.device, optim=optim, grad_buffer=grad_buffer,
+                             shadow_buffer=shadow_buffer, seed=seed,
+                             optimizer_state=self.strategy != "zero2")
         if self.ddp is not None:
             dist.broadcast(self.engine.master, src=0)
             self.engine.sync_shadow()
@@ -127,6 +145,18 @@ class Trainer:
         N.check_errors(self.device)
 
     def state_dict(self) -> dict:
+        """Model (reference names, fp32), step counters and optimiser state.
+        Under ZeRO-2 the optimiser state is this rank's shard (a collective
+        call: every rank must call it)."""
+        if self.strategy == "zero2":
+            eng = self.engine
+            full = self.ddp.full_master()
+            model = {s.name: eng.layout.view(full, s.name).clone() for s in eng.layout.specs}
+            model["lm_head.weight"] = model["wte.weight"]
+            return {"model": model, "step": self.step_num, "optim_step": eng.step_count,
+                    "exp_avg_shard": self.ddp.exp_avg.clone(),
+                    "exp_avg_sq_shard": self.ddp.exp_avg_sq.clone(), "rank": self.rank,
+                    "world_size": self.world}
         return {"model": self.engine.state_dict(), "step": self.step_num,
                 "exp_avg": self.engine.exp_avg.clone(), "exp_avg_sq": self.engine.exp_avg_sq.clone(),
                 "optim_step": self.engine.step_count}

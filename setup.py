@@ -23,7 +23,9 @@ SOURCES = [
     "csrc/attention_bwd_tc.cu",
     "csrc/elementwise.cu",
     "csrc/comm.cu",
-    "csrc/noalloc.cu", "csrc/decode.cu",
+    "csrc/noalloc.cu",
+    "csrc/decode.cu",
+    "csrc/zero.cu",
 ]
 
 NVCC_FLAGS = [
