@@ -33,6 +33,10 @@ autocast, `torch.optim.AdamW` from `configure_optimizers`, its
 DDP: natively the bucketed peer-memory reduce-scatter overlapped with backward
 plus the fused clip/AdamW/bf16 all-gather kernel; on the reference arm its
 `ShardedAdamW(stage=2, grad_clip=1.0, param_dtype=bf16)` over NCCL.
+`--strategy zero3 --model gpt2-medium --batch 8` is BASELINE config 3: block
+parameters sharded, gathered one block ahead over NVLink, gradients
+reduce-scattered per block; the reference arm runs its `Zero3Model`
+(param_dtype bf16) with `Zero3AdamW(grad_clip=1.0)`.
 """
 
 from __future__ import annotations
@@ -238,6 +242,8 @@ def run_native(args, world, rank):
     out = finish_line(args, world, cfg, ms, ms_e2e, bi, bo, sampler, impl="native")
     out["gpu_launches"] = int(n_launch)
     out["config"]["comm"] = (args.comm if args.strategy == "ddp" else "p2p") if world > 1 else "none"
+    if args.strategy == "zero3":
+        out["config"]["activations"] = "kept (no recompute): MFU counts the model FLOPs run"
     trainer.close()
     return out
 
@@ -258,7 +264,20 @@ def run_reference(args, world, rank):
         for p in model.parameters():
             dist.broadcast(p.data, src=0)
     host, dev = make_data(cfg, args.batch, args.seq, rank)
-    if args.strategy == "zero2":
+    if args.strategy == "zero3" and world > 1:
+        from transformer_internals.parallel.zero import Zero3AdamW, Zero3Model
+
+        zmodel = Zero3Model(model, rank, world, param_dtype=torch.bfloat16)
+        zopt = Zero3AdamW(zmodel, lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, grad_clip=1.0)
+
+        def train_step(idx, tgt):
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                loss = zmodel(idx, tgt)["loss"]
+            zopt.zero_grad()
+            loss.backward()
+            zopt.step()
+            return loss
+    elif args.strategy == "zero2":
         from transformer_internals.parallel.zero import ShardedAdamW
 
         zopt = ShardedAdamW(list(model.parameters()), rank, world, stage=2, lr=3e-4,
@@ -342,11 +361,12 @@ def finish_line(args, world, cfg, ms, ms_e2e, bi, bo, sampler, impl):
         "mfu_peak": f"{peak} TFLOP/s per GPU, {label}",
         "flops_per_token": fpt,
         "config": {
-            "model": f"{args.model} (124M)" if args.model == "gpt2" else args.model,
+            "model": {"gpt2": "gpt2 (124M)", "gpt2-medium": "gpt2-medium (350M)",
+                      "gpt2-large": "gpt2-large (774M)", "gpt2-xl": "gpt2-xl (1.5B)"}.get(args.model, args.model),
             "global_batch": args.batch * world,
             "per_gpu_batch": args.batch,
             "seq_len": args.seq,
-            "parallelism": f"dp{world}" if args.strategy == "ddp" else f"zero2-dp{world}",
+            "parallelism": f"dp{world}" if args.strategy == "ddp" else f"{args.strategy}-dp{world}",
             "strategy": args.strategy,
             "bucket_mb": 25,
             "optimizer": "AdamW + clip 1.0, fp32 master",
@@ -372,7 +392,7 @@ def main():
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--seq", type=int, default=1024)
     ap.add_argument("--comm", choices=["p2p", "nccl"], default="p2p")
-    ap.add_argument("--strategy", choices=["ddp", "zero2"], default="ddp")
+    ap.add_argument("--strategy", choices=["ddp", "zero2", "zero3"], default="ddp")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

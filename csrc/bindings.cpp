@@ -290,6 +290,14 @@ PYBIND11_MODULE(_C, m) {
     z.norm_out = P<float>(I("norm_out"));
     z.err = P<uint32_t>(I("err"));
     z.wait_budget_ns = I("wait_budget_ns");
+    if (d.contains("done_handshake")) z.done_handshake = (int)I("done_handshake");
+    if (d.contains("peer_shard")) {
+      z.peer_shard = P<__nv_bfloat16*>(I("peer_shard"));
+      z.gather_dst = P<__nv_bfloat16>(I("gather_dst"));
+      z.ag_span = I("ag_span");
+      z.ag_slice = I("ag_slice");
+      z.ag_offset = I("ag_offset");
+    }
     return z;
   };
   m.def("zero_rs", [zero_args](const py::dict& d, int64_t stream) {
@@ -297,6 +305,9 @@ PYBIND11_MODULE(_C, m) {
   });
   m.def("zero_adamw_ag", [zero_args](const py::dict& d, int nblocks, int64_t stream) {
     check(zero_adamw_ag_launch(zero_args(d), nblocks, S(stream)), "zero_adamw_ag");
+  });
+  m.def("zero_ag", [zero_args](const py::dict& d, int nblocks, int64_t stream) {
+    check(zero_ag_launch(zero_args(d), nblocks, S(stream)), "zero_ag");
   });
   m.def("zero_flag_words", []() { return 2 * kCommMaxRanks * kZeroMaxBlocks; });
   m.def("zero_norm_words", []() { return 2 * kZeroMaxBlocks * kCommMaxRanks; });

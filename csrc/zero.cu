@@ -135,10 +135,33 @@ __global__ void __launch_bounds__(512) zero_rs_kernel(const ZeroArgs a) {
     ss += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
   }
   const float t = block_sum(ss, red);
-  if (threadIdx.x == 0) a.sumsq_parts[(int64_t)a.bucket * a.rs_blocks + blockIdx.x] = t;
+  if (threadIdx.x == 0 && a.sumsq_parts)
+    a.sumsq_parts[(int64_t)a.bucket * a.rs_blocks + blockIdx.x] = t;
   if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
     atomicAdd(a.byte_counter, (unsigned long long)(a.buckets[4 * a.bucket + 1] -
                                                    a.buckets[4 * a.bucket]) * 4ull);
+  if (a.done_handshake) {
+    __syncthreads();
+    zero_handshake(a, 1, &fail);
+  }
+}
+
+__global__ void __launch_bounds__(512) zero_ag_kernel(const ZeroArgs a) {
+  __shared__ int fail;
+  if (threadIdx.x == 0) fail = 0;
+  __syncthreads();
+  if (!zero_handshake(a, 0, &fail)) return;
+  const int64_t nv = a.ag_span / 8;
+  const int64_t sv = a.ag_slice / 8;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nv;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    const int q = (int)(v / sv);
+    const int64_t i = v - (int64_t)q * sv;
+    const uint4 w = __ldcg(reinterpret_cast<const uint4*>(a.peer_shard[q] + a.ag_offset) + i);
+    reinterpret_cast<uint4*>(a.gather_dst)[v] = w;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
+    atomicAdd(a.byte_counter, (unsigned long long)a.ag_span * 2ull);
 }
 
 __device__ __forceinline__ bool zero_in_decay(int64_t e, const int64_t* __restrict__ r, int nr) {
@@ -261,6 +284,16 @@ int zero_rs_launch(const ZeroArgs& a, cudaStream_t s) {
       a.bucket < 0 || a.bucket >= a.nb)
     return -1;
   zero_rs_kernel<<<a.rs_blocks, 512, 0, s>>>(a);
+  count_launches(1);
+  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+}
+
+int zero_ag_launch(const ZeroArgs& a, int nblocks, cudaStream_t s) {
+  if (a.world < 1 || a.world > kCommMaxRanks || nblocks < 1 || nblocks > kZeroMaxBlocks ||
+      a.ag_slice <= 0 || a.ag_slice % 64 || a.ag_span % 64 || a.ag_offset % 8 ||
+      (a.ag_span + a.ag_slice - 1) / a.ag_slice > a.world)
+    return -1;
+  zero_ag_kernel<<<nblocks, 512, 0, s>>>(a);
   count_launches(1);
   return cudaGetLastError() == cudaSuccess ? 0 : -11;
 }

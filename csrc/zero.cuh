@@ -41,9 +41,23 @@ struct ZeroArgs {
   float* norm_out = nullptr;
   uint32_t* err = nullptr;
   int64_t wait_budget_ns = 2000000000ll;
+  // zero_rs: end with a second handshake so that on exit every peer has
+  // finished reading this rank's gradient buffer (ZeRO-3 reuses it at once).
+  int done_handshake = 0;
+  // zero_ag (ZeRO-3 parameter gather): peer_shard[q] is rank q's bf16 shard
+  // storage; the unit's slices are gathered into gather_dst[0, span).
+  __nv_bfloat16** peer_shard = nullptr;
+  __nv_bfloat16* gather_dst = nullptr;
+  int64_t ag_span = 0, ag_slice = 0, ag_offset = 0;
 };
 
 int zero_rs_launch(const ZeroArgs& a, cudaStream_t s);
 int zero_adamw_ag_launch(const ZeroArgs& a, int nblocks, cudaStream_t s);
+
+// ZeRO-3 all-gather of one unit: gather_dst[e] = shard of rank e / ag_slice at
+// ag_offset + e % ag_slice, for e in [0, ag_span), by P2P loads (16-byte
+// vectors; ag_slice and ag_span multiples of 64). Starts with a handshake so
+// that every peer's previous optimiser step has finished writing its shard.
+int zero_ag_launch(const ZeroArgs& a, int nblocks, cudaStream_t s);
 
 }  // namespace g2b

@@ -277,7 +277,7 @@ def engine_state_dict(engine, with_optimizer: bool = False, zero=None) -> tuple[
     """(tensors, extra) of a native Engine in the reference naming (fp32);
     with_optimizer adds flat AdamW moments and step to `extra`.
 
-    Under ZeRO-2 pass the engine's ``NativeZeRO`` as `zero`: the master
+    Under ZeRO-2/3 pass the engine's ``NativeZeRO``/``NativeZeRO3`` as `zero`: the master
     weights and moments are then gathered from the shards (a collective that
     every rank must enter) into the same full-vector format DDP writes, so a
     checkpoint resumes under either strategy and any world size."""
@@ -286,8 +286,9 @@ def engine_state_dict(engine, with_optimizer: bool = False, zero=None) -> tuple[
         full = zero.full_master()
         sd = {s.name: engine.layout.view(full, s.name) for s in engine.layout.specs}
         if with_optimizer:
-            extra["exp_avg"] = zero.gather_full(zero.exp_avg).cpu()
-            extra["exp_avg_sq"] = zero.gather_full(zero.exp_avg_sq).cpu()
+            m, v = zero.full_moments()
+            extra["exp_avg"] = m.cpu()
+            extra["exp_avg_sq"] = v.cpu()
         return sd, extra
     sd = {s.name: engine.p32(s.name).detach() for s in engine.layout.specs}
     if with_optimizer:

@@ -77,7 +77,7 @@ def main(argv=None) -> int:
     ap.add_argument("--ckpt-dir", default=None)
     ap.add_argument("--ckpt-every", type=int, default=500)
     ap.add_argument("--log", default=None, help="JSONL metrics (rank 0)")
-    ap.add_argument("--strategy", choices=["ddp", "zero2"], default="ddp")
+    ap.add_argument("--strategy", choices=["ddp", "zero2", "zero3"], default="ddp")
     ap.add_argument("--seed", type=int, default=0)
     a = ap.parse_args(argv)
 
@@ -102,7 +102,7 @@ def main(argv=None) -> int:
     ck = latest_checkpoint(a.ckpt_dir) if a.ckpt_dir else None
     if ck is not None:
         (full, _), extra = load_full(ck), load_extra(ck, 0)
-        zero = trainer.ddp if trainer.strategy == "zero2" else None
+        zero = trainer.ddp if trainer.strategy in ("zero2", "zero3") else None
         load_into_engine(trainer.engine, {k: v.to(dev) for k, v in full.items()}, extra, zero=zero)
         if trainer.ddp is not None and zero is None:
             trainer.engine.sync_shadow()
@@ -134,7 +134,7 @@ def main(argv=None) -> int:
                     allp = [None] * world
                     dist.all_gather_object(allp, stream.position)
                     pos = allp
-                zero = trainer.ddp if trainer.strategy == "zero2" else None
+                zero = trainer.ddp if trainer.strategy in ("zero2", "zero3") else None
                 if zero is not None:  # gathering the shards is a collective
                     sd, extra = engine_state_dict(trainer.engine, with_optimizer=True, zero=zero)
                 if rank == 0:

@@ -255,6 +255,18 @@ class Engine:
         # A sharded optimiser replaces the update: optimizer_impl(hp) is called
         # with the device hyperparameter vector instead of the local AdamW.
         self.optimizer_impl: Optional[Callable[[torch.Tensor], None]] = None
+        # Parameter sharding (ZeRO-3) supplies block parameters and gradient
+        # destinations from its own buffers: param_source(name) /
+        # grad_source(name) return a view or None (use the flat buffers), and
+        # block_hook(phase, l) runs before block l's forward ("fwd") or
+        # backward ("bwd") kernels are issued.
+        self.param_source: Optional[Callable[[str], Optional[torch.Tensor]]] = None
+        self.grad_source: Optional[Callable[[str], Optional[torch.Tensor]]] = None
+        self.block_hook: Optional[Callable[[str, int], None]] = None
+        # LayerNorm backward also produces the c_proj bias gradients of the
+        # block that fed it (one block earlier for ln_1); a sharded gradient
+        # buffer per block turns this off so each block writes only its own.
+        self.fuse_bias_grad_into_ln = True
         self.step_count = 0
         self._acts: Optional[_Acts] = None
         # Hyperparameters reach the device by an async copy from pinned memory
@@ -295,9 +307,17 @@ class Engine:
         return self.layout.view(self.master, name)
 
     def p16(self, name: str) -> torch.Tensor:
+        if self.param_source is not None:
+            v = self.param_source(name)
+            if v is not None:
+                return v
         return self.layout.view(self.shadow, name)
 
     def g32(self, name: str) -> torch.Tensor:
+        if self.grad_source is not None:
+            v = self.grad_source(name)
+            if v is not None:
+                return v
         return self.layout.view(self.grad, name)
 
     @torch.no_grad()
@@ -381,8 +401,11 @@ class Engine:
         eps = cfg.layer_norm_epsilon
         p = self.p16
         N.embedding_fwd(idx, p("wte.weight"), p("wpe.weight"), A.x[0])
+        bh = self.block_hook
         for l in range(L):
             pre = f"h.{l}."
+            if bh:
+                bh("fwd", l)
             N.layernorm_fwd(A.x[2 * l], p(pre + "ln_1.weight"), p(pre + "ln_1.bias"), A.h1[l],
                             A.mu[2 * l], A.rs[2 * l], eps)
             N.gemm(A.h1[l], p(pre + "attn.c_attn.weight"), A.qkv[l], bias=p(pre + "attn.c_attn.bias"))
@@ -419,20 +442,26 @@ class Engine:
                alpha_ptr=inv_count, accumulate=acc)
         # LN backward also sums the residual gradient it writes: that column
         # sum is the bias gradient of the projection that produced the stream
+        fuse = self.fuse_bias_grad_into_ln
+        bh = self.block_hook
         N.layernorm_bwd(A.dh, A.x[2 * L], A.mu[2 * L], A.rs[2 * L], p("ln_f.weight"), A.dres,
                         A.dres16, g("ln_f.weight"), g("ln_f.bias"), A.ln_parts,
                         accumulate_dres=False, accumulate_params=acc,
-                        dsum=g(f"h.{L - 1}.mlp.c_proj.bias"), accumulate_dsum=acc)
+                        dsum=g(f"h.{L - 1}.mlp.c_proj.bias") if fuse else None, accumulate_dsum=acc)
         if hook:
             hook("root_head")
         ws = A.splitk_ws
         for l in reversed(range(L)):
             pre = f"h.{l}."
+            if bh:
+                bh("bwd", l)
             # mlp.c_proj
             N.gemm(A.dres16, p(pre + "mlp.c_proj.weight"), A.du, b_t=True, epilogue=N.EPI_GELU_BWD,
                    aux=A.u[l])
             N.gemm(A.dres16, A.g[l], g(pre + "mlp.c_proj.weight"), a_t=True, b_t=True,
                    epilogue=N.EPI_F32, accumulate=acc, splits=A.splits["mlp_proj"], workspace=ws)
+            if not fuse:
+                N.colsum_bf16(A.dres16, g(pre + "mlp.c_proj.bias"), A.col_ws, accumulate=acc)
             # mlp.c_fc
             N.gemm(A.du, p(pre + "mlp.c_fc.weight"), A.dh, b_t=True)
             N.gemm(A.du, A.h2[l], g(pre + "mlp.c_fc.weight"), a_t=True, b_t=True,
@@ -441,12 +470,15 @@ class Engine:
             N.layernorm_bwd(A.dh, A.x[2 * l + 1], A.mu[2 * l + 1], A.rs[2 * l + 1],
                             p(pre + "ln_2.weight"), A.dres, A.dres16, g(pre + "ln_2.weight"),
                             g(pre + "ln_2.bias"), A.ln_parts, accumulate_dres=True,
-                            accumulate_params=acc, dsum=g(pre + "attn.c_proj.bias"),
+                            accumulate_params=acc,
+                            dsum=g(pre + "attn.c_proj.bias") if fuse else None,
                             accumulate_dsum=acc)
             # attn.c_proj
             N.gemm(A.dres16, p(pre + "attn.c_proj.weight"), A.dy, b_t=True)
             N.gemm(A.dres16, A.y[l], g(pre + "attn.c_proj.weight"), a_t=True, b_t=True,
                    epilogue=N.EPI_F32, accumulate=acc, splits=A.splits["c_proj"], workspace=ws)
+            if not fuse:
+                N.colsum_bf16(A.dres16, g(pre + "attn.c_proj.bias"), A.col_ws, accumulate=acc)
             # attention
             qkv, dqkv = A.qkv[l], A.dqkv
             N.attention_bwd(qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:], A.y[l], A.dy,
@@ -459,7 +491,7 @@ class Engine:
             N.layernorm_bwd(A.dh, A.x[2 * l], A.mu[2 * l], A.rs[2 * l], p(pre + "ln_1.weight"),
                             A.dres, A.dres16, g(pre + "ln_1.weight"), g(pre + "ln_1.bias"),
                             A.ln_parts, accumulate_dres=True, accumulate_params=acc,
-                            dsum=g(f"h.{l - 1}.mlp.c_proj.bias") if l > 0 else None,
+                            dsum=g(f"h.{l - 1}.mlp.c_proj.bias") if (fuse and l > 0) else None,
                             accumulate_dsum=acc)
             if hook:
                 hook(f"h.{l}")

@@ -226,6 +226,10 @@ class NativeZeRO:
         """The full fp32 master vector (collective)."""
         return self.gather_full(self.master)
 
+    def full_moments(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """Full exp_avg and exp_avg_sq vectors (collective)."""
+        return self.gather_full(self.exp_avg), self.gather_full(self.exp_avg_sq)
+
     @torch.no_grad()
     def load_full(self, master: torch.Tensor, exp_avg: Optional[torch.Tensor] = None,
                   exp_avg_sq: Optional[torch.Tensor] = None) -> None:

@@ -7,7 +7,9 @@ parallel with the gradient communication overlapped with backward, either as
 DDP (:class:`~gpt2_harness_b200.parallel.ddp_native.NativeDDP`, all-reduce,
 every rank updates every parameter) or as ZeRO-2
 (:class:`~gpt2_harness_b200.parallel.zero_native.NativeZeRO`, reduce-scatter,
-sharded AdamW and optimiser state, fused bf16 all-gather).
+sharded AdamW and optimiser state, fused bf16 all-gather) or as ZeRO-3
+(:class:`~gpt2_harness_b200.parallel.zero3_native.NativeZeRO3`, block
+parameters sharded and gathered one block ahead over NVLink).
 
 The learning-rate schedule is the reference's (train.py:72-99): linear warmup
 to ``lr`` over ``warmup_steps``, then cosine decay to ``lr * min_lr_ratio``.
@@ -49,7 +51,7 @@ class Trainer:
             uses a constant ``lr`` from its defaults.
         comm: ``"p2p"`` (fused peer-memory all-reduce) or ``"nccl"`` when the
             default process group has more than one rank (DDP only).
-        strategy: ``"ddp"`` or ``"zero2"`` (ignored on one rank).
+        strategy: ``"ddp"``, ``"zero2"`` or ``"zero3"`` (ignored on one rank).
         seed: weight init seed (identical on every rank; rank 0's weights are
             broadcast to make sure).
     """
@@ -72,7 +74,7 @@ class Trainer:
         tc = self.train_cfg
         optim = OptimConfig(lr=tc.lr, betas=tuple(tc.betas), eps=tc.eps,
                             weight_decay=tc.weight_decay, grad_clip=tc.grad_clip)
-        if strategy not in ("ddp", "zero2"):
+        if strategy not in ("ddp", "zero2", "zero3"):
             raise ValueError(f"unknown strategy {strategy!r}")
         self.strategy = strategy if self.world > 1 else "single"
         self.ddp = None
@@ -86,6 +88,10 @@ class Trainer:
 
                 self.ddp = NativeZeRO(layout, bucket_bytes=bucket_bytes, device=self.device)
                 shadow_buffer = self.ddp.shadow_buffer
+            elif strategy == "zero3":
+                from gpt2_harness_b200.parallel.zero3_native import NativeZeRO3
+
+                self.ddp = NativeZeRO3(layout, device=self.device)
             else:
                 from gpt2_harness_b200.parallel.ddp_native import NativeDDP
 
@@ -94,7 +100,7 @@ class Trainer:
             grad_buffer = self.ddp.grad_buffer
         self.engine = Engine(config, self.device, optim=optim, grad_buffer=grad_buffer,
                              shadow_buffer=shadow_buffer, seed=seed,
-                             optimizer_state=self.strategy != "zero2")
+                             optimizer_state=self.strategy not in ("zero2", "zero3"))
         if self.ddp is not None:
             dist.broadcast(self.engine.master, src=0)
             self.engine.sync_shadow()
@@ -148,7 +154,7 @@ class Trainer:
         """Model (reference names, fp32), step counters and optimiser state.
         Under ZeRO-2 the optimiser state is this rank's shard (a collective
         call: every rank must call it)."""
-        if self.strategy == "zero2":
+        if self.strategy in ("zero2", "zero3"):
             eng = self.engine
             full = self.ddp.full_master()
             model = {s.name: eng.layout.view(full, s.name).clone() for s in eng.layout.specs}
