@@ -559,7 +559,7 @@ int attn_fwd_launch(const AttnArgs& a, cudaStream_t s) {
   dim3 grid((a.Tq + FWD_BQ - 1) / FWD_BQ, a.B * a.H);
   attn_fwd_kernel<<<grid, FWD_THREADS, smem, s>>>(a);
   count_launches(1);
-  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+  return launch_succeeded() ? 0 : -11;
 }
 
 int attn_bwd_launch(const AttnArgs& a, cudaStream_t s) {
@@ -577,7 +577,7 @@ int attn_bwd_launch(const AttnArgs& a, cudaStream_t s) {
     const int rc = attn_bwd_tc_launch(a, s);
     if (rc == 1) {
       count_launches(1);  // the delta kernel
-      return cudaGetLastError() == cudaSuccess ? 0 : -11;
+      return launch_succeeded() ? 0 : -11;
     }
     if (rc < 0) return rc;
   }
@@ -595,7 +595,7 @@ int attn_bwd_launch(const AttnArgs& a, cudaStream_t s) {
   dim3 gq((a.Tq + BWD_B - 1) / BWD_B, a.B * a.H);
   attn_bwd_dq_kernel<<<gq, BWD_THREADS, smem_q, s>>>(a);
   count_launches(3);
-  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+  return launch_succeeded() ? 0 : -11;
 }
 
 }  // namespace g2b

@@ -83,7 +83,7 @@ struct BwdParams {
 #ifdef G2B_ATTN_TRACE
 #define TR(role, gg, ev)                                                              \
   do {                                                                                \
-    if (blockIdx.x == 0 && (gg) < 128) p.trace[((role) * 128 + (gg)) * 4 + (ev)] = clock64(); \
+    if (p.trace && blockIdx.x == 0 && (gg) < 128) p.trace[((role) * 128 + (gg)) * 4 + (ev)] = clock64(); \
   } while (0)
 #else
 #define TR(role, gg, ev) \
@@ -609,7 +609,7 @@ int launch_mode(const CUtensorMap& a, const CUtensorMap& a2, const CUtensorMap& 
   const int grid = p.n_tiles < num_sms() ? p.n_tiles : num_sms();
   attn_bwd_tc_kernel<MODE><<<grid, kThreads, SMEM_BYTES, s>>>(a, a2, x, y, p);
   count_launches(1);
-  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+  return launch_succeeded() ? 0 : -11;
 }
 
 }  // namespace

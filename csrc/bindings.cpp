@@ -30,7 +30,9 @@ cudaStream_t S(int64_t v) { return reinterpret_cast<cudaStream_t>(static_cast<ui
 
 void check(int rc, const char* what) {
   if (rc != 0) {
-    cudaError_t e = cudaPeekAtLastError();
+    cudaError_t e = last_launch_error();
+    last_launch_error() = cudaSuccess;
+    if (e == cudaSuccess) e = cudaPeekAtLastError();
     throw std::runtime_error(std::string(what) + " failed (code " + std::to_string(rc) +
                              ", cuda: " + cudaGetErrorString(e) + ")");
   }

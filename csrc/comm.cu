@@ -186,14 +186,14 @@ int comm_allreduce_launch(const CommArgs& a, cudaStream_t s) {
   else
     allreduce_p2p_kernel<__nv_bfloat16><<<a.nblocks, 512, 0, s>>>(a);
   count_launches(1);
-  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+  return launch_succeeded() ? 0 : -11;
 }
 
 int comm_flag_wait_test_launch(uint32_t* flag, uint32_t value, int64_t budget_ns, uint32_t* err,
                                cudaStream_t s) {
   flag_wait_test_kernel<<<1, 1, 0, s>>>(flag, value, budget_ns, err);
   count_launches(1);
-  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+  return launch_succeeded() ? 0 : -11;
 }
 
 std::string comm_ipc_handle(void* ptr) {

@@ -241,7 +241,7 @@ int decode_embed_launch(const int64_t* tok, const int* lens, const void* wte, co
   decode_embed_kernel<<<B, 256, 0, s>>>(tok, lens, reinterpret_cast<const __nv_bfloat16*>(wte),
                                         reinterpret_cast<const __nv_bfloat16*>(wpe), x, C);
   count_launches(1);
-  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+  return launch_succeeded() ? 0 : -11;
 }
 
 int decode_attn_launch(const void* qkv, int64_t ld, void* kc, void* vc, const int* lens, float* part_o,
@@ -267,7 +267,7 @@ int decode_attn_launch(const void* qkv, int64_t ld, void* kc, void* vc, const in
   decode_attn_kernel<<<dim3(a.S, Hkv, B), 128, 0, s>>>(a);
   decode_combine_kernel<<<dim3(H, B), 64, 0, s>>>(a);
   count_launches(2);
-  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+  return launch_succeeded() ? 0 : -11;
 }
 
 int decode_partials_numel(int B, int H, int Tmax) {
@@ -279,7 +279,7 @@ int decode_argmax_launch(const void* logits, int64_t ld, int V, int64_t* tok, in
   decode_argmax_kernel<<<B, 1024, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(logits), ld, V, tok,
                                           lens, hist, Tmax);
   count_launches(1);
-  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+  return launch_succeeded() ? 0 : -11;
 }
 
 }  // namespace g2b

@@ -656,7 +656,7 @@ __global__ void scale_f32_kernel(float* __restrict__ x, int64_t n, float a) {
     x[i] *= a;
 }
 
-inline int ok() { return cudaGetLastError() == cudaSuccess ? 0 : -11; }
+inline int ok() { return launch_succeeded() ? 0 : -11; }
 
 }  // namespace
 

@@ -559,7 +559,7 @@ int launch_cfg(const Maps& m, const GemmDev& d, int grid, cudaStream_t s) {
   }
   kern<<<grid, kThreads, smem, s>>>(m.a, m.b, m.o, m.x, d);
   count_launches(1);
-  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+  return launch_succeeded() ? 0 : -11;
 }
 
 template <int BN, int EPI, int TMA_ST>
@@ -704,7 +704,7 @@ int splitk_reduce_launch(const float* ws, int splits, int64_t split_stride, floa
   splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(ws, splits, split_stride, out, ldo, M, N,
                                                    accumulate);
   count_launches(1);
-  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+  return launch_succeeded() ? 0 : -11;
 }
 
 }  // namespace g2b

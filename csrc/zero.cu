@@ -285,7 +285,7 @@ int zero_rs_launch(const ZeroArgs& a, cudaStream_t s) {
     return -1;
   zero_rs_kernel<<<a.rs_blocks, 512, 0, s>>>(a);
   count_launches(1);
-  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+  return launch_succeeded() ? 0 : -11;
 }
 
 int zero_ag_launch(const ZeroArgs& a, int nblocks, cudaStream_t s) {
@@ -295,14 +295,14 @@ int zero_ag_launch(const ZeroArgs& a, int nblocks, cudaStream_t s) {
     return -1;
   zero_ag_kernel<<<nblocks, 512, 0, s>>>(a);
   count_launches(1);
-  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+  return launch_succeeded() ? 0 : -11;
 }
 
 int zero_adamw_ag_launch(const ZeroArgs& a, int nblocks, cudaStream_t s) {
   if (a.world < 1 || a.world > kCommMaxRanks || nblocks < 1 || nblocks > kZeroMaxBlocks) return -1;
   zero_adamw_ag_kernel<<<nblocks, 512, 0, s>>>(a);
   count_launches(1);
-  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+  return launch_succeeded() ? 0 : -11;
 }
 
 }  // namespace g2b

@@ -329,7 +329,8 @@ def test_bounded_wait_returns_error():
 
 
 @pytest.mark.parametrize("B,H,T,off,Tk", [(2, 3, 384, 0, None), (1, 2, 200, 0, None),
-                                         (1, 12, 1024, 0, None), (1, 2, 128, 256, 384)])
+                                         (1, 12, 1024, 0, None), (1, 2, 128, 256, 384),
+                                         (8, 12, 1024, 0, None), (3, 5, 640, 0, None)])
 def test_attention_tensor_core_matches_mma_sync(B, H, T, off, Tk):
     """tcgen05 forward (default) vs the mma.sync forward on the same inputs."""
     Tk = T if Tk is None else Tk
@@ -349,6 +350,33 @@ def test_attention_tensor_core_matches_mma_sync(B, H, T, off, Tk):
         L.attn_set_impl(0)
     assert rel_err(outs[0][0], outs[1][0]) < 2e-2
     assert (outs[0][1] - outs[1][1]).abs().max().item() < 2e-2
+
+
+def test_attention_tensor_core_lazy_rescale():
+    """Keys whose scores grow along the sequence force the running row max up
+    by far more than the lazy-rescale threshold several times per row."""
+    B, H, T = 2, 4, 1024
+    C = H * 64
+    torch.manual_seed(7)
+    q = torch.randn(B * T, C, device=dev())
+    k = torch.randn(B * T, C, device=dev())
+    grow = (1.0 + torch.arange(T, device=dev()).float() / 48.0).repeat(B)[:, None]
+    k = (k * grow).bfloat16()
+    q = q.bfloat16()
+    v = torch.randn(B * T, C, device=dev()).bfloat16()
+    outs = []
+    L = N.lib()
+    try:
+        for impl in (0, 1):
+            L.attn_set_impl(impl)
+            o = torch.empty(B * T, C, dtype=torch.bfloat16, device=dev())
+            lse = torch.empty(B, H, T, device=dev())
+            N.attention_fwd(q, k, v, o, lse, B, H, T)
+            outs.append((o.float(), lse))
+    finally:
+        L.attn_set_impl(0)
+    assert rel_err(outs[0][0], outs[1][0]) < 2e-2
+    assert (outs[0][1] - outs[1][1]).abs().max().item() < 2e-2 * outs[1][1].abs().max().item()
 
 
 @pytest.mark.parametrize("B,H,T,off,Tk", [(2, 3, 384, 0, None), (1, 2, 200, 0, None),
