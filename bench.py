@@ -206,7 +206,8 @@ def run_native(args, world, rank):
     cfg = gpt2_config(args.model)
     tc = TrainConfig(lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, grad_clip=1.0, warmup_steps=0)
     trainer = Trainer(cfg, args.batch, args.seq, train=tc, comm=args.comm, schedule=False,
-                      strategy=args.strategy)
+                      strategy=args.strategy, bucket_bytes=int(args.bucket_mb * 2**20),
+                      comm_blocks=args.comm_blocks)
     host, dev = make_data(cfg, args.batch, args.seq, rank)
     L = N.lib()
 
@@ -368,7 +369,7 @@ def finish_line(args, world, cfg, ms, ms_e2e, bi, bo, sampler, impl):
             "seq_len": args.seq,
             "parallelism": f"dp{world}" if args.strategy == "ddp" else f"{args.strategy}-dp{world}",
             "strategy": args.strategy,
-            "bucket_mb": 25,
+            "bucket_mb": args.bucket_mb,
             "optimizer": "AdamW + clip 1.0, fp32 master",
             "l2": "inputs larger than L2 (per-step working set ~10 GB >> 126 MB), no flush",
             "baseline": "README.md:395 (M1 Max MPS fp32, B4xT256, 4024 tokens/s)",
@@ -393,6 +394,8 @@ def main():
     ap.add_argument("--seq", type=int, default=1024)
     ap.add_argument("--comm", choices=["p2p", "nccl"], default="p2p")
     ap.add_argument("--strategy", choices=["ddp", "zero2", "zero3"], default="ddp")
+    ap.add_argument("--bucket-mb", type=float, default=25.0, help="gradient bucket size (MiB)")
+    ap.add_argument("--comm-blocks", type=int, default=128, help="CTAs per fused all-reduce")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

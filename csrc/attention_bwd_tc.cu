@@ -75,21 +75,8 @@ struct BwdParams {
   __nv_bfloat16* out2;  // dV (MODE_KV)
   int64_t o1_sb, o1_st, o1_sh, o2_sb, o2_st, o2_sh;
   uint32_t* err;
-#ifdef G2B_ATTN_TRACE
-  unsigned long long* trace;  // [4 roles][128 steps][4 events] of CTA 0 (clock64)
-#endif
 };
 
-#ifdef G2B_ATTN_TRACE
-#define TR(role, gg, ev)                                                              \
-  do {                                                                                \
-    if (p.trace && blockIdx.x == 0 && (gg) < 128) p.trace[((role) * 128 + (gg)) * 4 + (ev)] = clock64(); \
-  } while (0)
-#else
-#define TR(role, gg, ev) \
-  do {                   \
-  } while (0)
-#endif
 
 __device__ __forceinline__ float ex2f(float x) {
   float y;
@@ -292,7 +279,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        if (lane == 0) TR(0, g, 0);
         const int row = ti.s0 + j * SB;
         if (MODE == MODE_KV) {
           // stage the step's LSE and delta (queries row .. row+63)
@@ -312,7 +298,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* xs = smem + RING_OFF + st * 2 * XTILE;
           tma_load_4d(xs, &tmX, &x_full[st], 0, h, row, b);
           tma_load_4d(xs + XTILE, &tmY, &x_full[st], 0, h, row, b);
-          TR(0, g, 1);
         }
         __syncwarp();
       }
@@ -351,7 +336,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // The TMEM buffer of step gg was last used by step gg-2: wait until the
         // elementwise warps have read it out (not until they finish step gg-2).
         auto issue_sd = [&](uint32_t gg, bool last) -> bool {
-          TR(1, gg, 2);
           const uint32_t st = gg % STAGES;
           if (!mbar_wait_bounded(&s_free[gg & 1], ((gg >> 1) & 1) ^ 1, p.err, ERR_TIMEOUT_ATTN,
                                  abort_flag) ||
@@ -368,7 +352,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                       umma_desc_sw128(sy + kk * 32, 16, 1024), id_ss, kk > 0 ? 1u : 0u);
           }
           umma_commit(&s_full[gg & 1]);
-          TR(1, gg, 3);
           if (last) umma_commit(a_empty);
           return true;
         };
@@ -387,7 +370,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          TR(1, g, 0);
           const uint32_t sx = ring + st * 2 * XTILE, sy = sx + XTILE;
           const uint32_t sp = sp0 + pb * ATILE, sds = sds0 + pb * ATILE;
           // accumulate over the streaming dimension (K = 64 rows of the step)
@@ -408,7 +390,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           umma_commit(&pds_free[pb]);
           umma_commit(&x_empty[st]);
-          TR(1, g, 1);
         }
         if (!ok) break;
         umma_commit(&acc_full[i & 1]);
@@ -475,13 +456,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           full = rows_full && cst + SB <= p.Tq && (!p.causal || p.q_offset + cst >= last_row);
         else
           full = rows_full && cst + SB <= p.Tk && (!p.causal || cst + SB - 1 <= p.q_offset + ti.r0);
-        if (lane == 0 && (warp == 2 || warp == 1 + kEw)) TR(warp == 2 ? 2 : 3, g, 0);
         if (!mbar_wait_bounded(&s_full[pb], (g >> 1) & 1, p.err, ERR_TIMEOUT_ATTN, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (lane == 0 && (warp == 2 || warp == 1 + kEw)) TR(warp == 2 ? 2 : 3, g, 1);
         uint32_t sv[NC], dv[NC];
         const uint32_t tb = tmem + lane_off + pb * 128 + grp * NC;
         tmem_ld_nc(tb, sv);
@@ -490,7 +469,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // S/dP are in registers: the tensor core may overwrite this buffer
         tc_fence_before();
         mbar_arrive(&s_free[pb]);
-        if (lane == 0 && (warp == 2 || warp == 1 + kEw)) TR(warp == 2 ? 2 : 3, g, 2);
         if (MODE == MODE_KV) {
           const float* lse_s = ld_smem + st * 2 * SB + grp * NC;
           if (full)
@@ -513,7 +491,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async_shared();
         tc_fence_before();
         mbar_arrive(&e_full[pb]);
-        if (lane == 0 && (warp == 2 || warp == 1 + kEw)) TR(warp == 2 ? 2 : 3, g, 3);
       }
       if (!ok) break;
       // final accumulators -> global (each warp writes its 32 rows, NC dims)
@@ -614,9 +591,6 @@ int launch_mode(const CUtensorMap& a, const CUtensorMap& a2, const CUtensorMap& 
 
 }  // namespace
 
-#ifdef G2B_ATTN_TRACE
-unsigned long long* g_attn_trace = nullptr;  // KV trace, then Q trace
-#endif
 
 // Tensor-core backward (after delta has been computed into a.delta): returns
 // 1 if it ran, 0 when a layout is not TMA-compatible, negative on failure.
@@ -654,9 +628,6 @@ int attn_bwd_tc_launch(const AttnArgs& a, cudaStream_t s) {
   p.o2_sh = a.dv.sh;
   p.n_blk = (a.Tk + TB - 1) / TB;
   p.n_tiles = p.n_blk * p.BH;
-#ifdef G2B_ATTN_TRACE
-  p.trace = g_attn_trace;
-#endif
   int rc = launch_mode<MODE_KV>(tk_a, tv_a, tq_x, tdo_x, p, s);
   if (rc) return rc;
   // dQ
@@ -667,9 +638,6 @@ int attn_bwd_tc_launch(const AttnArgs& a, cudaStream_t s) {
   p.out2 = nullptr;
   p.n_blk = (a.Tq + TB - 1) / TB;
   p.n_tiles = p.n_blk * p.BH;
-#ifdef G2B_ATTN_TRACE
-  p.trace = g_attn_trace + 4 * 128 * 4;
-#endif
   rc = launch_mode<MODE_Q>(tq_a, tdo_a, tk_x, tv_x, p, s);
   return rc ? rc : 1;
 }

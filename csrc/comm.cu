@@ -117,7 +117,7 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
   return __float2bfloat16(x);
 }
 
-template <typename T>
+template <typename T, int W>
 __global__ void __launch_bounds__(512) allreduce_p2p_kernel(const CommArgs a) {
   __shared__ int fail;
   if (threadIdx.x == 0) fail = 0;
@@ -128,36 +128,57 @@ __global__ void __launch_bounds__(512) allreduce_p2p_kernel(const CommArgs a) {
   // Vectorised part: slices of whole 16-byte vectors; the scalar tail (< VN
   // elements per rank boundary) is handled by rank 0's last CTA.
   const int64_t nvec = a.n / VN;
-  const int64_t per_rank = (nvec + a.world - 1) / a.world;
+  const int64_t per_rank = (nvec + W - 1) / W;
   const int64_t s0 = min(nvec, per_rank * a.rank), s1 = min(nvec, s0 + per_rank);
   const int64_t per_blk = (s1 - s0 + gridDim.x - 1) / gridDim.x;
   const int64_t b0 = min(s1, s0 + per_blk * blockIdx.x), b1 = min(s1, b0 + per_blk);
   const T zero_tag{};
-  for (int64_t v = b0 + threadIdx.x; v < b1; v += blockDim.x) {
-    float acc[VN];
+  // U vectors per thread per iteration, every peer's loads issued before any
+  // sum: U x W = 8 sixteen-byte loads in flight per thread, so a few CTAs
+  // already cover NVLink latency and the kernel holds few SMs while it
+  // overlaps the backward.
+  constexpr int U = W >= 8 ? 1 : 8 / W;
+  const int64_t span = (int64_t)blockDim.x * U;
+  for (int64_t v0 = b0 + threadIdx.x; v0 < b1; v0 += span) {
+    uint4 w[U][W];
 #pragma unroll
-    for (int i = 0; i < VN; ++i) acc[i] = 0.f;
-    for (int q = 0; q < a.world; ++q) {
-      const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.peer_bufs[q]) + a.offset) + v;
-      const uint4 w = __ldcg(src);
-      acc_vec(acc, w, zero_tag);
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = v0 + (int64_t)u * blockDim.x;
+      if (v < b1) {
+#pragma unroll
+        for (int q = 0; q < W; ++q)
+          w[u][q] = __ldcg(reinterpret_cast<const uint4*>(
+                               reinterpret_cast<const T*>(a.peer_bufs[q]) + a.offset) + v);
+      }
     }
 #pragma unroll
-    for (int i = 0; i < VN; ++i) acc[i] *= a.scale;
-    const uint4 out = pack_vec(acc, zero_tag);
-    for (int q = 0; q < a.world; ++q) {
-      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.peer_bufs[q]) + a.offset) + v;
-      __stcg(dst, out);
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = v0 + (int64_t)u * blockDim.x;
+      if (v < b1) {
+        float acc[VN];
+#pragma unroll
+        for (int i = 0; i < VN; ++i) acc[i] = 0.f;
+#pragma unroll
+        for (int q = 0; q < W; ++q) acc_vec(acc, w[u][q], zero_tag);
+#pragma unroll
+        for (int i = 0; i < VN; ++i) acc[i] *= a.scale;
+        const uint4 out = pack_vec(acc, zero_tag);
+#pragma unroll
+        for (int q = 0; q < W; ++q) {
+          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.peer_bufs[q]) + a.offset) + v;
+          __stcg(dst, out);
+        }
+      }
     }
   }
   if (a.rank == 0 && blockIdx.x == gridDim.x - 1) {
     for (int64_t e = nvec * VN + threadIdx.x; e < a.n; e += blockDim.x) {
       float acc = 0.f;
-      for (int q = 0; q < a.world; ++q) {
+      for (int q = 0; q < W; ++q) {
         const T* src = reinterpret_cast<const T*>(a.peer_bufs[q]) + a.offset + e;
         acc += to_f32(__ldcg(src));
       }
-      for (int q = 0; q < a.world; ++q)
+      for (int q = 0; q < W; ++q)
         reinterpret_cast<T*>(a.peer_bufs[q])[a.offset + e] = from_f32<T>(acc * a.scale);
     }
   }
@@ -166,6 +187,20 @@ __global__ void __launch_bounds__(512) allreduce_p2p_kernel(const CommArgs a) {
   if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
     atomicAdd(a.byte_counter, (unsigned long long)a.n * sizeof(T));
   handshake(a, 1, &fail);
+}
+
+template <typename T>
+void launch_allreduce(const CommArgs& a, cudaStream_t s) {
+  switch (a.world) {
+    case 1: allreduce_p2p_kernel<T, 1><<<a.nblocks, 512, 0, s>>>(a); break;
+    case 2: allreduce_p2p_kernel<T, 2><<<a.nblocks, 512, 0, s>>>(a); break;
+    case 3: allreduce_p2p_kernel<T, 3><<<a.nblocks, 512, 0, s>>>(a); break;
+    case 4: allreduce_p2p_kernel<T, 4><<<a.nblocks, 512, 0, s>>>(a); break;
+    case 5: allreduce_p2p_kernel<T, 5><<<a.nblocks, 512, 0, s>>>(a); break;
+    case 6: allreduce_p2p_kernel<T, 6><<<a.nblocks, 512, 0, s>>>(a); break;
+    case 7: allreduce_p2p_kernel<T, 7><<<a.nblocks, 512, 0, s>>>(a); break;
+    default: allreduce_p2p_kernel<T, 8><<<a.nblocks, 512, 0, s>>>(a); break;
+  }
 }
 
 __global__ void flag_wait_test_kernel(uint32_t* flag, uint32_t value, int64_t budget,
@@ -182,9 +217,9 @@ int comm_allreduce_launch(const CommArgs& a, cudaStream_t s) {
   const int esz = a.dtype == 0 ? 4 : 2;
   if ((a.offset * esz) % 16) return -2;  // bucket starts must be 16-byte aligned
   if (a.dtype == 0)
-    allreduce_p2p_kernel<float><<<a.nblocks, 512, 0, s>>>(a);
+    launch_allreduce<float>(a, s);
   else
-    allreduce_p2p_kernel<__nv_bfloat16><<<a.nblocks, 512, 0, s>>>(a);
+    launch_allreduce<__nv_bfloat16>(a, s);
   count_launches(1);
   return launch_succeeded() ? 0 : -11;
 }

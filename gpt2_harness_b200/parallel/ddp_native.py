@@ -24,6 +24,7 @@ B200 design:
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import Optional
 
@@ -94,8 +95,8 @@ class NativeDDP:
     """
 
     def __init__(self, layout: ParamLayout, group=None, comm: str = "p2p",
-                 bucket_bytes: int = DEFAULT_BUCKET_BYTES, nblocks: int = 64,
-                 device: Optional[torch.device] = None) -> None:
+                 bucket_bytes: int = DEFAULT_BUCKET_BYTES, nblocks: int = 128,
+                 device: Optional[torch.device] = None, tail_blocks: int = 128) -> None:
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -106,7 +107,12 @@ class NativeDDP:
         self.layout = layout
         self.buckets = build_layout_buckets(layout, bucket_bytes)
         self.order = {g: i for i, g in enumerate(group_order(layout))}
+        # Buckets completed during backward share the GPU with it and use
+        # `nblocks` CTAs; the buckets completed by the last gradient group are
+        # reduced while nothing else runs, so they get `tail_blocks`.
         self.nblocks = nblocks
+        self.tail_blocks = tail_blocks
+        self.last_group = len(self.order) - 1
         self.symm: Optional[SymmetricBuffer] = None
         self.flags: Optional[SymmetricBuffer] = None
         if self.comm == "p2p":
@@ -116,7 +122,12 @@ class NativeDDP:
             self.flags = SymmetricBuffer(words * 4, group, self.device)
         else:
             self.grad_buffer = torch.zeros(layout.total, dtype=torch.float32, device=self.device)
-        self.stream = torch.cuda.Stream(device=self.device) if self.world > 1 else None
+        # The reduction kernels get a higher stream priority than the compute
+        # stream: their CTAs are placed as soon as SMs free up, so each bucket
+        # finishes (and hands its SMs back to the backward) as early as possible.
+        prio = int(os.environ.get("G2B_COMM_PRIORITY", "-1"))
+        self.stream = (torch.cuda.Stream(device=self.device, priority=prio)
+                       if self.world > 1 else None)
         self.epoch = 0
         self.byte_counter = torch.zeros(1, dtype=torch.int64, device=self.device)
         self._next = 0
@@ -137,11 +148,12 @@ class NativeDDP:
         if self.comm == "none":
             return
         idx = self.order[group]
+        blocks = self.tail_blocks if idx == self.last_group else self.nblocks
         while self._next < len(self.buckets) and self.buckets[self._next].ready <= idx:
-            self._launch(self.buckets[self._next])
+            self._launch(self.buckets[self._next], blocks)
             self._next += 1
 
-    def _launch(self, b: Bucket) -> None:
+    def _launch(self, b: Bucket, nblocks: Optional[int] = None) -> None:
         ev = torch.cuda.Event()
         ev.record()
         self.stream.wait_event(ev)
@@ -153,7 +165,7 @@ class NativeDDP:
                     self.symm.peer_ptrs_dev.data_ptr(), self.flags.peer_ptrs_dev.data_ptr(),
                     self.rank, self.world, b.lo, b.hi - b.lo, 0, 1.0 / self.world,
                     self.epoch & 0xFFFFFFFF, self.byte_counter.data_ptr(), N.error_word().data_ptr(),
-                    self.nblocks, 2_000_000_000, self.stream.cuda_stream)
+                    nblocks or self.nblocks, 2_000_000_000, self.stream.cuda_stream)
             else:
                 dist.all_reduce(self.grad_buffer[b.lo:b.hi], group=self.group)
 
@@ -165,7 +177,7 @@ class NativeDDP:
             # backward did not announce every group (e.g. a frozen tail):
             # launch the rest now so every rank issues the same sequence.
             while self._next < len(self.buckets):
-                self._launch(self.buckets[self._next])
+                self._launch(self.buckets[self._next], self.tail_blocks)
                 self._next += 1
         torch.cuda.current_stream().wait_stream(self.stream)
         self._next = 0

@@ -52,6 +52,8 @@ class Trainer:
         comm: ``"p2p"`` (fused peer-memory all-reduce) or ``"nccl"`` when the
             default process group has more than one rank (DDP only).
         strategy: ``"ddp"``, ``"zero2"`` or ``"zero3"`` (ignored on one rank).
+        comm_blocks: CTAs of each fused peer-memory all-reduce (DDP, p2p):
+            fewer leave more of the GPU to the backward it overlaps.
         seed: weight init seed (identical on every rank; rank 0's weights are
             broadcast to make sure).
     """
@@ -60,7 +62,7 @@ class Trainer:
                  train: Optional[TrainConfig] = None, comm: str = "p2p",
                  device: Optional[torch.device] = None, seed: int = 0,
                  bucket_bytes: int = 25 * 1024 * 1024, schedule: bool = True,
-                 strategy: str = "ddp") -> None:
+                 strategy: str = "ddp", comm_blocks: int = 128) -> None:
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device())
         self.device = torch.device(device)
@@ -96,7 +98,7 @@ class Trainer:
                 from gpt2_harness_b200.parallel.ddp_native import NativeDDP
 
                 self.ddp = NativeDDP(layout, comm=comm, bucket_bytes=bucket_bytes,
-                                     device=self.device)
+                                     device=self.device, nblocks=comm_blocks)
             grad_buffer = self.ddp.grad_buffer
         self.engine = Engine(config, self.device, optim=optim, grad_buffer=grad_buffer,
                              shadow_buffer=shadow_buffer, seed=seed,
