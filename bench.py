@@ -37,6 +37,11 @@ plus the fused clip/AdamW/bf16 all-gather kernel; on the reference arm its
 parameters sharded, gathered one block ahead over NVLink, gradients
 reduce-scattered per block; the reference arm runs its `Zero3Model`
 (param_dtype bf16) with `Zero3AdamW(grad_clip=1.0)`.
+`--strategy tp --model gpt2-xl --batch 32` is BASELINE config 4: tensor +
+sequence parallelism over all N GPUs with `--batch` the GLOBAL batch (strong
+scaling); the reference has no tensor-parallel GPT training entry point (and
+its TensorParallelBlock needs n_head % N == 0; XL has 25 heads), so its arm
+prints `unavailable` for N > 1.
 """
 
 from __future__ import annotations
@@ -259,6 +264,12 @@ def run_reference(args, world, rank):
     from transformer_internals.parallel.data_parallel import average_gradients
 
     cfg = ref_config(args.model)
+    if args.strategy == "tp" and world > 1:
+        why = ("the reference has no tensor-parallel GPT training entry point (its "
+               "TensorParallelBlock covers single blocks, without a vocabulary-parallel head)")
+        if cfg.n_head % world:
+            why += f"; it also requires n_head % world == 0 ({args.model}: {cfg.n_head} heads)"
+        return {"impl": "reference", "unavailable": why}
     torch.manual_seed(0)
     model = RefGPT(cfg).cuda()
     if world > 1:
@@ -338,7 +349,7 @@ def gpu_list(world):
 def finish_line(args, world, cfg, ms, ms_e2e, bi, bo, sampler, impl):
     from gpt2_harness_b200.perf.mfu import flops_per_token_exact, measured_peak_tflops
 
-    tokens = args.batch * args.seq * world
+    tokens = args.batch * args.seq * (1 if args.strategy == "tp" else world)
     tps = tokens / (ms / 1e3)
     tps_e2e = tokens / (ms_e2e / 1e3)
     fpt = flops_per_token_exact(cfg, args.seq)["training_flops_per_token"]
@@ -354,7 +365,7 @@ def finish_line(args, world, cfg, ms, ms_e2e, bi, bo, sampler, impl):
         "warmup": args.warmup,
         "ms_per_step": round(ms, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if args.strategy == "tp" else "weak",
         "vs_baseline": round(tps / BASELINE_TOKENS_PER_S, 2),
         "dtype": "bf16",
         "data": "synthetic uniform-random tokens, random-init weights",
@@ -364,10 +375,11 @@ def finish_line(args, world, cfg, ms, ms_e2e, bi, bo, sampler, impl):
         "config": {
             "model": {"gpt2": "gpt2 (124M)", "gpt2-medium": "gpt2-medium (350M)",
                       "gpt2-large": "gpt2-large (774M)", "gpt2-xl": "gpt2-xl (1.5B)"}.get(args.model, args.model),
-            "global_batch": args.batch * world,
-            "per_gpu_batch": args.batch,
+            "global_batch": args.batch * (1 if args.strategy == "tp" else world),
+            "per_gpu_batch": args.batch if args.strategy != "tp" else None,
             "seq_len": args.seq,
-            "parallelism": f"dp{world}" if args.strategy == "ddp" else f"{args.strategy}-dp{world}",
+            "parallelism": (f"dp{world}" if args.strategy == "ddp" else
+                            f"tp{world}-sp" if args.strategy == "tp" else f"{args.strategy}-dp{world}"),
             "strategy": args.strategy,
             "bucket_mb": args.bucket_mb,
             "optimizer": "AdamW + clip 1.0, fp32 master",
@@ -393,7 +405,7 @@ def main():
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--seq", type=int, default=1024)
     ap.add_argument("--comm", choices=["p2p", "nccl"], default="p2p")
-    ap.add_argument("--strategy", choices=["ddp", "zero2", "zero3"], default="ddp")
+    ap.add_argument("--strategy", choices=["ddp", "zero2", "zero3", "tp"], default="ddp")
     ap.add_argument("--bucket-mb", type=float, default=25.0, help="gradient bucket size (MiB)")
     ap.add_argument("--comm-blocks", type=int, default=128, help="CTAs per fused all-reduce")
     args = ap.parse_args()

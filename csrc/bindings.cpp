@@ -16,6 +16,7 @@
 #include "gemm.cuh"
 #include "launch_count.h"
 #include "zero.cuh"
+#include "tp.cuh"
 
 namespace py = pybind11;
 using namespace g2b;
@@ -311,6 +312,56 @@ PYBIND11_MODULE(_C, m) {
   m.def("zero_ag", [zero_args](const py::dict& d, int nblocks, int64_t stream) {
     check(zero_ag_launch(zero_args(d), nblocks, S(stream)), "zero_ag");
   });
+  // Tensor-parallel kernels: arguments by name (see csrc/tp.cuh).
+  auto tp_args = [](const py::dict& d) {
+    auto I = [&](const char* k) -> int64_t { return d.contains(k) ? d[k].cast<int64_t>() : 0; };
+    TpArgs t;
+    t.peer_bufs = P<void*>(I("peer_bufs"));
+    t.peer_flags = P<uint32_t*>(I("peer_flags"));
+    t.rank = (int)I("rank");
+    t.world = (int)I("world");
+    t.rows = I("rows");
+    t.cols = (int)I("cols");
+    t.nblocks = d.contains("nblocks") ? (int)I("nblocks") : 64;
+    t.epoch = (uint32_t)I("epoch");
+    t.bias = P<const __nv_bfloat16>(I("bias"));
+    t.resid = P<const float>(I("resid"));
+    t.out_f32 = P<float>(I("out_f32"));
+    t.out_bf16 = P<__nv_bfloat16>(I("out_bf16"));
+    t.idx = P<const int64_t>(I("idx"));
+    t.wpe = P<const __nv_bfloat16>(I("wpe"));
+    t.T = d.contains("T") ? (int)I("T") : 1;
+    t.vocab_per_rank = I("vocab_per_rank");
+    t.logits = P<__nv_bfloat16>(I("logits"));
+    t.ld = I("ld");
+    t.vocab_valid = (int)I("vocab_valid");
+    t.vocab_start = I("vocab_start");
+    t.stats = P<float>(I("stats"));
+    t.loss_rows = P<float>(I("loss_rows"));
+    t.byte_counter = P<unsigned long long>(I("byte_counter"));
+    t.err = P<uint32_t>(I("err"));
+    if (d.contains("wait_budget_ns")) t.wait_budget_ns = I("wait_budget_ns");
+    return t;
+  };
+  m.def("tp_ag_rows", [tp_args](const py::dict& d, int64_t st) {
+    check(tp_ag_rows_launch(tp_args(d), S(st)), "tp_ag_rows");
+  });
+  m.def("tp_rs_rows", [tp_args](const py::dict& d, int64_t st) {
+    check(tp_rs_rows_launch(tp_args(d), S(st)), "tp_rs_rows");
+  });
+  m.def("tp_embed_fwd", [tp_args](const py::dict& d, int64_t st) {
+    check(tp_embed_fwd_launch(tp_args(d), S(st)), "tp_embed_fwd");
+  });
+  m.def("tp_embed_bwd", [tp_args](const py::dict& d, int64_t st) {
+    check(tp_embed_bwd_launch(tp_args(d), S(st)), "tp_embed_bwd");
+  });
+  m.def("tp_ce_stats", [tp_args](const py::dict& d, int64_t st) {
+    check(tp_ce_stats_launch(tp_args(d), S(st)), "tp_ce_stats");
+  });
+  m.def("tp_ce_finish", [tp_args](const py::dict& d, int64_t st) {
+    check(tp_ce_finish_launch(tp_args(d), S(st)), "tp_ce_finish");
+  });
+  m.def("tp_flag_words", []() { return 2 * kTpMaxRanks * kTpMaxBlocks; });
   m.def("zero_flag_words", []() { return 2 * kCommMaxRanks * kZeroMaxBlocks; });
   m.def("zero_norm_words", []() { return 2 * kZeroMaxBlocks * kCommMaxRanks; });
   m.def("zero_max_blocks", []() { return kZeroMaxBlocks; });

@@ -3,7 +3,12 @@
 //
 //   C[M,N] = A[M,K] . B[N,K]^T   (A and B each K-major or MN-major)
 //
-// One CTA per SM (persistent; tiles strided by gridDim.x), 320 threads:
+// One CTA per SM (persistent), 320 threads. Tiles are scheduled dynamically:
+// CTA b starts with tile b and then takes the next unclaimed tile from a
+// global counter, so a CTA that starts late (its SM held by a communication
+// kernel running alongside) simply processes fewer tiles. The producer warp
+// claims tiles and hands their indices to the MMA and epilogue warps through
+// a 4-deep shared-memory queue guarded by mbarriers.
 //   warp 0      TMA producer: one elected lane streams A/B k-blocks into a
 //               STAGES-deep ring of 128B-swizzled shared-memory stages.
 //   warp 1      MMA issuer: allocates TMEM, one elected lane issues
@@ -32,6 +37,7 @@
 #include <stdio.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "common.cuh"
 #include "gemm.cuh"
@@ -72,7 +78,14 @@ struct GemmDev {
   int64_t split_stride;
   int vec_ok;
   uint32_t* err;
+  int* sched;  // {next tile - gridDim.x, finished CTAs}: dynamic scheduling, or null
 };
+
+// Per-launch tile counters for dynamic scheduling (see gemm_tcgen05_kernel).
+// Launches take slots round-robin; the last CTA of a launch resets its slot,
+// so a slot is zero again long before it is handed out anew.
+constexpr int kSchedSlots = 64;
+__device__ int g_gemm_sched[kSchedSlots * 2];
 
 // ---------------------------------------------------------------- TMA store
 __device__ __forceinline__ void tma_store_3d(const void* tmap, const void* smem_src, int32_t x,
@@ -274,7 +287,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  uint64_t* tq_full = tempty_bar + 2;   // [4] tile index written
+  uint64_t* tq_empty = tq_full + 4;      // [4] tile index read by MMA + epilogue
+  int* tile_q = reinterpret_cast<int*>(tq_empty + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_q + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
@@ -289,6 +305,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
       mbar_init(&tempty_bar[b], 32 * kEpiWarps);
+    }
+    for (int q = 0; q < 4; ++q) {
+      mbar_init(&tq_full[q], 1);
+      mbar_init(&tq_empty[q], 1 + 32 * kEpiWarps);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -316,9 +336,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int split = tile / tiles_per_split;
-        const int rem = tile % tiles_per_split;
+      int tile = blockIdx.x;
+      for (int r = 0; ok; ++r) {
+        // publish this tile (or the end marker) to the MMA and epilogue warps
+        const int slot = r & 3;
+        if (!mbar_wait_bounded(&tq_empty[slot], ((r >> 2) & 1) ^ 1, p.err, ERR_TIMEOUT_PRODUCER,
+                               abort_flag))
+          break;
+        tile_q[slot] = tile < num_tiles ? tile : -1;
+        mbar_arrive(&tq_full[slot]);
+        if (tile >= num_tiles) break;
+        const int cur = tile;
+        tile = p.sched ? (int)gridDim.x + atomicAdd(p.sched, 1) : tile + (int)gridDim.x;
+        const int split = cur / tiles_per_split;
+        const int rem = cur % tiles_per_split;
         const int m0 = (rem / p.n_tiles) * BM;
         const int n0 = (rem % p.n_tiles) * BN;
         const int kb0 = split * p.kb_per_split;
@@ -362,7 +393,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int r = 0; ok; ++r) {
+        const int slot = r & 3;
+        if (!mbar_wait_bounded(&tq_full[slot], (r >> 2) & 1, p.err, ERR_TIMEOUT_MMA, abort_flag))
+          break;
+        const int tile = tile_q[slot];
+        mbar_arrive(&tq_empty[slot]);
+        if (tile < 0) break;
         const int split = tile / tiles_per_split;
         const int kb0 = split * p.kb_per_split;
         const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
@@ -418,7 +455,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     float alpha = p.alpha;
     if (p.alpha_ptr) alpha *= *p.alpha_ptr;
     EpiIn in_next;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    for (int r = 0;; ++r) {
+      const int slot = r & 3;
+      if (!mbar_wait_bounded(&tq_full[slot], (r >> 2) & 1, p.err, ERR_TIMEOUT_EPILOGUE, abort_flag))
+        break;
+      const int tile = tile_q[slot];
+      mbar_arrive(&tq_empty[slot]);
+      if (tile < 0) break;
       const int split = tile / tiles_per_split;
       const int rem = tile % tiles_per_split;
       const int m0 = (rem / p.n_tiles) * BM;
@@ -480,9 +523,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
+  if (p.sched && threadIdx.x == 0) {
+    // every claim of this CTA precedes this point; the last CTA to get here
+    // knows no claim on this slot is outstanding and resets it
+    __threadfence();
+    if (atomicAdd(p.sched + 1, 1) == (int)gridDim.x - 1) {
+      p.sched[0] = 0;
+      p.sched[1] = 0;
+      __threadfence();
+    }
+  }
 }
 
 // ------------------------------------------------------------------ host ---
+// Device address of a scheduling slot (the symbol's address on the current
+// device, looked up once per device).
+int* gemm_sched_slot() {
+  static int* base[64] = {nullptr};
+  static std::atomic<unsigned> seq{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!base[dev]) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_gemm_sched) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;  // static scheduling
+    }
+    base[dev] = static_cast<int*>(ptr);
+  }
+  return base[dev] + 2 * (seq.fetch_add(1, std::memory_order_relaxed) % kSchedSlots);
+}
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -688,6 +758,9 @@ int gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   const int tiles = d.m_tiles * d.n_tiles * d.splits;
   int grid = a.max_ctas > 0 ? a.max_ctas : num_sms();
   if (grid > tiles) grid = tiles;
+  // more tiles than CTAs: claim them dynamically (each tile's result is
+  // independent, so the order of claims does not change any output bit)
+  d.sched = tiles > grid ? gemm_sched_slot() : nullptr;
   int rc = BN == 256 ? dispatch_epi<256>(a.epilogue, tma_st, a.a_mn_major, a.b_mn_major, maps, d, grid, stream)
                      : dispatch_epi<128>(a.epilogue, tma_st, a.a_mn_major, a.b_mn_major, maps, d, grid, stream);
   if (rc != 0 || !split_mode) return rc;

@@ -1,0 +1,53 @@
+// Host-side interface of the tensor-/sequence-parallel kernels (csrc/tp.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace g2b {
+
+constexpr int kTpMaxRanks = 8;
+constexpr int kTpMaxBlocks = 160;  // flag slots per (phase, rank)
+
+// peer_bufs[q] is rank q's symmetric buffer of the operation (bf16 rows for
+// the gather / reduce-scatter / embedding table, fp32 for the embedding
+// gradient, fp32 [M, 4] statistics for the cross-entropy); peer_flags[q] is
+// rank q's flag array ([2][kTpMaxRanks][kTpMaxBlocks] uint32).
+struct TpArgs {
+  void** peer_bufs = nullptr;
+  uint32_t** peer_flags = nullptr;
+  int rank = 0, world = 1;
+  int64_t rows = 0;   // rows per rank (gather / reduce-scatter / embedding), all rows (CE)
+  int cols = 0;       // row length in elements
+  int nblocks = 64;
+  uint32_t epoch = 1;
+  // reduce-scatter epilogue
+  const __nv_bfloat16* bias = nullptr;  // [cols] or null
+  const float* resid = nullptr;         // fp32 [rows, cols] or null (embedding bwd: dx)
+  float* out_f32 = nullptr;             // fp32 [rows, cols] (embedding: x / wpe grad)
+  __nv_bfloat16* out_bf16 = nullptr;
+  // embedding
+  const int64_t* idx = nullptr;         // all M token ids (CE: targets)
+  const __nv_bfloat16* wpe = nullptr;
+  int T = 1;
+  int64_t vocab_per_rank = 0;
+  // cross-entropy
+  __nv_bfloat16* logits = nullptr;      // [rows, ld] local vocabulary slice
+  int64_t ld = 0;
+  int vocab_valid = 0;                  // real (unpadded) columns of the slice
+  int64_t vocab_start = 0;
+  float* stats = nullptr;               // this rank's [rows, 4]
+  float* loss_rows = nullptr;
+  unsigned long long* byte_counter = nullptr;
+  uint32_t* err = nullptr;
+  int64_t wait_budget_ns = 2000000000ll;
+};
+
+int tp_ag_rows_launch(TpArgs a, cudaStream_t s);
+int tp_rs_rows_launch(TpArgs a, cudaStream_t s);
+int tp_embed_fwd_launch(TpArgs a, cudaStream_t s);
+int tp_embed_bwd_launch(TpArgs a, cudaStream_t s);
+int tp_ce_stats_launch(TpArgs a, cudaStream_t s);
+int tp_ce_finish_launch(TpArgs a, cudaStream_t s);
+
+}  // namespace g2b

@@ -43,7 +43,7 @@ import torch
 from gpt2_harness_b200.config import GPTConfig
 from gpt2_harness_b200.ops import native as N
 
-__all__ = ["ParamSpec", "ParamLayout", "Engine", "OptimConfig", "choose_splits"]
+__all__ = ["ParamSpec", "ParamLayout", "Engine", "OptimConfig", "choose_splits", "init_flat_weights"]
 
 ALIGN = 64  # elements; 128 bytes of bf16, 256 bytes of fp32
 
@@ -135,6 +135,29 @@ class ParamLayout:
 
     def decay_segments(self) -> list[tuple[int, int, bool]]:
         return [(s.offset, s.numel, s.decay) for s in self.specs]
+
+
+@torch.no_grad()
+def init_flat_weights(layout: ParamLayout, flat: torch.Tensor, seed: int = 0) -> torch.Tensor:
+    """Fill `flat` (fp32, ``layout.total`` elements, on a CUDA device) with the
+    GPT-2 init in layout order from one seeded generator: the same weights for
+    the same seed wherever the layout is instantiated (single GPU, data
+    parallel, or sliced into tensor-parallel shards)."""
+    g = torch.Generator(device=flat.device)
+    g.manual_seed(seed)
+    flat.zero_()
+    res_std = 0.02 / math.sqrt(2 * layout.config.n_layer)
+    for s in layout.specs:
+        v = layout.view(flat, s.name)
+        if s.name.endswith(("ln_1.weight", "ln_2.weight", "ln_f.weight")):
+            v.fill_(1.0)
+        elif s.name.endswith("bias"):
+            v.zero_()
+        elif s.name.endswith(("attn.c_proj.weight", "mlp.c_proj.weight")):
+            v.normal_(0.0, res_std, generator=g)
+        else:
+            v.normal_(0.0, 0.02, generator=g)
+    return flat
 
 
 def choose_splits(m: int, n: int, k: int, bm: int = 128, bn: int = 256, sms: int = 148,
@@ -325,20 +348,7 @@ class Engine:
         """GPT-2 init on the device: N(0, 0.02) for matmul weights and
         embeddings, N(0, 0.02/sqrt(2L)) for the two residual projections,
         zero biases, unit LayerNorm gains (reference model.py:488-518)."""
-        g = torch.Generator(device=self.device)
-        g.manual_seed(seed)
-        self.master.zero_()
-        res_std = 0.02 / math.sqrt(2 * self.config.n_layer)
-        for s in self.layout.specs:
-            v = self.p32(s.name)
-            if s.name.endswith(("ln_1.weight", "ln_2.weight", "ln_f.weight")):
-                v.fill_(1.0)
-            elif s.name.endswith("bias"):
-                v.zero_()
-            elif s.name.endswith(("attn.c_proj.weight", "mlp.c_proj.weight")):
-                v.normal_(0.0, res_std, generator=g)
-            else:
-                v.normal_(0.0, 0.02, generator=g)
+        init_flat_weights(self.layout, self.master, seed)
         self.sync_shadow()
 
     @torch.no_grad()

@@ -269,10 +269,11 @@ class TensorParallelBlock(nn.Module):
 
 
 # ----------------------------------------------------------- vocab parallel --
-def padded_vocab(vocab: int, world_size: int, multiple: int = 64) -> int:
-    """Vocabulary rounded up so every rank holds an equal multiple of
-    `multiple` rows (50257 -> 50304 for p in 1, 2, 4, 8)."""
-    step = multiple * world_size
+def padded_vocab(vocab: int, world_size: int, multiple: int = 64, per_rank: int = 16) -> int:
+    """Vocabulary rounded up to a multiple of `multiple` that also splits into
+    equal per-rank blocks of a multiple of `per_rank` rows: 50257 -> 50304
+    for p in 1, 2, 4 and 8 (the padded GPT-2 vocabulary)."""
+    step = math.lcm(multiple, per_rank * world_size)
     return (vocab + step - 1) // step * step
 
 

@@ -51,7 +51,9 @@ class Trainer:
             uses a constant ``lr`` from its defaults.
         comm: ``"p2p"`` (fused peer-memory all-reduce) or ``"nccl"`` when the
             default process group has more than one rank (DDP only).
-        strategy: ``"ddp"``, ``"zero2"`` or ``"zero3"`` (ignored on one rank).
+        strategy: ``"ddp"``, ``"zero2"`` or ``"zero3"`` (ignored on one rank),
+            or ``"tp"``: tensor + sequence parallelism over all ranks, where
+            ``batch_size`` is the GLOBAL batch every rank receives.
         comm_blocks: CTAs of each fused peer-memory all-reduce (DDP, p2p):
             fewer leave more of the GPU to the backward it overlaps.
         seed: weight init seed (identical on every rank; rank 0's weights are
@@ -76,9 +78,21 @@ class Trainer:
         tc = self.train_cfg
         optim = OptimConfig(lr=tc.lr, betas=tuple(tc.betas), eps=tc.eps,
                             weight_decay=tc.weight_decay, grad_clip=tc.grad_clip)
-        if strategy not in ("ddp", "zero2", "zero3"):
+        if strategy not in ("ddp", "zero2", "zero3", "tp"):
             raise ValueError(f"unknown strategy {strategy!r}")
-        self.strategy = strategy if self.world > 1 else "single"
+        self.strategy = strategy if (self.world > 1 or strategy == "tp") else "single"
+        if strategy == "tp":
+            # tensor + sequence parallelism: every rank takes the same global
+            # batch (batch_size x seq_len) and holds 1/p of every block
+            from gpt2_harness_b200.parallel.tp_native import TPEngine
+
+            self.ddp = None
+            self.engine = TPEngine(config, batch_size, seq_len, self.device, optim=optim, seed=seed)
+            self.idx = torch.zeros(batch_size, seq_len, dtype=torch.int64, device=self.device)
+            self.tgt = torch.zeros(batch_size, seq_len, dtype=torch.int64, device=self.device)
+            self.step_num = 0
+            self.h2d_done = torch.cuda.Event()
+            return
         self.ddp = None
         grad_buffer = shadow_buffer = None
         if self.world > 1:
@@ -115,6 +129,10 @@ class Trainer:
 
     @property
     def num_parameters(self) -> int:
+        if self.strategy == "tp":
+            from gpt2_harness_b200.models.engine import ParamLayout
+
+            return ParamLayout(self.config).num_parameters
         return self.engine.layout.num_parameters
 
     def _load_inputs(self, idx: torch.Tensor, targets: torch.Tensor):
@@ -137,7 +155,10 @@ class Trainer:
             eng.set_lr(lr_at_step(self.step_num, self.train_cfg))
         i, t = self._load_inputs(idx, targets)
         loss = eng.forward(i, t)
-        eng.backward(i)
+        if self.strategy == "tp":
+            eng.backward()
+        else:
+            eng.backward(i)
         if self.ddp is not None:
             self.ddp.finish()
         eng.optimizer_step()
@@ -156,6 +177,11 @@ class Trainer:
         """Model (reference names, fp32), step counters and optimiser state.
         Under ZeRO-2 the optimiser state is this rank's shard (a collective
         call: every rank must call it)."""
+        if self.strategy == "tp":
+            eng = self.engine
+            return {"model": eng.full_state("master"), "step": self.step_num,
+                    "optim_step": eng.step_count, "exp_avg": eng.full_state("exp_avg"),
+                    "exp_avg_sq": eng.full_state("exp_avg_sq")}
         if self.strategy in ("zero2", "zero3"):
             eng = self.engine
             full = self.ddp.full_master()
@@ -170,5 +196,8 @@ class Trainer:
                 "optim_step": self.engine.step_count}
 
     def close(self) -> None:
+        if self.strategy == "tp":
+            self.engine.close()
+            return
         if self.ddp is not None:
             self.ddp.close()

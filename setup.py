@@ -26,6 +26,7 @@ SOURCES = [
     "csrc/noalloc.cu",
     "csrc/decode.cu",
     "csrc/zero.cu",
+    "csrc/tp.cu",
 ]
 
 NVCC_FLAGS = [
