@@ -341,8 +341,18 @@ PYBIND11_MODULE(_C, m) {
     t.byte_counter = P<unsigned long long>(I("byte_counter"));
     t.err = P<uint32_t>(I("err"));
     if (d.contains("wait_budget_ns")) t.wait_budget_ns = I("wait_budget_ns");
+    t.src = P<const __nv_bfloat16>(I("src"));
+    t.src_ld = I("src_ld");
+    t.B = (int)I("B");
+    t.Tl = (int)I("Tl");
     return t;
   };
+  m.def("cp_kv_gather", [tp_args](const py::dict& d, int64_t st) {
+    check(cp_kv_gather_launch(tp_args(d), S(st)), "cp_kv_gather");
+  });
+  m.def("cp_kv_reduce", [tp_args](const py::dict& d, int64_t st) {
+    check(cp_kv_reduce_launch(tp_args(d), S(st)), "cp_kv_reduce");
+  });
   m.def("tp_ag_rows", [tp_args](const py::dict& d, int64_t st) {
     check(tp_ag_rows_launch(tp_args(d), S(st)), "tp_ag_rows");
   });

@@ -28,6 +28,11 @@
 //   tp_ce_finish    combine every rank's row statistics (P2P loads) into the
 //                   row log-sum-exp and loss, and overwrite the local logits
 //                   with softmax - onehot.
+//   cp_kv_gather    context parallelism: this rank's k/v rows into its block
+//                   of the symmetric key/value buffer, then the blocks of the
+//                   earlier ranks (P2P loads): all a causal query here sees.
+//   cp_kv_reduce    the key/value gradient of this rank's block summed over
+//                   the ranks whose queries saw it (P2P loads, rank order).
 //
 // Every kernel starts with an arrive/wait handshake of CTA j against CTA j of
 // every peer (the data it reads were written by kernels that precede the
@@ -320,6 +325,85 @@ __global__ void __launch_bounds__(CE_T) tp_ce_finish_kernel(const TpArgs a) {
   finish(a, &fail);
 }
 
+// ---------------------------------------------------- context parallelism --
+// Row (b, t) of block q in a [B, world*Tl, cols] buffer.
+__device__ __forceinline__ int64_t cp_row(const TpArgs& a, int q, int64_t i) {
+  const int64_t b = i / a.Tl, t = i % a.Tl;
+  return b * (int64_t)a.world * a.Tl + (int64_t)q * a.Tl + t;
+}
+
+__global__ void __launch_bounds__(512) cp_kv_gather_kernel(const TpArgs a) {
+  __shared__ int fail;
+  if (threadIdx.x == 0) fail = 0;
+  __syncthreads();
+  const int C = a.cols / 2;
+  const int vpr = a.cols / 8;                       // 16-byte vectors per k/v row
+  const int64_t nvec = (int64_t)a.B * a.Tl * vpr;   // vectors per block
+  __nv_bfloat16* mine = reinterpret_cast<__nv_bfloat16*>(a.peer_bufs[a.rank]);
+  // 1. own block from the local qkv rows
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = v / vpr;
+    const int c = (int)(v % vpr) * 8;
+    const uint4 w = *reinterpret_cast<const uint4*>(a.src + i * a.src_ld + C + c);
+    *reinterpret_cast<uint4*>(mine + cp_row(a, a.rank, i) * a.cols + c) = w;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (!tp_handshake(a, 0, &fail)) return;
+  // 2. blocks of the earlier ranks from their buffers
+  const int64_t total = nvec * a.rank;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < total;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    const int q = (int)(v / nvec);
+    const int64_t vv = v % nvec;
+    const int64_t i = vv / vpr;
+    const int c = (int)(vv % vpr) * 8;
+    const int64_t off = cp_row(a, q, i) * a.cols + c;
+    *reinterpret_cast<uint4*>(mine + off) =
+        __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.peer_bufs[q]) + off));
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
+    atomicAdd(a.byte_counter, (unsigned long long)(nvec * 16 * (a.rank + 1)));
+  finish(a, &fail);
+}
+
+__global__ void __launch_bounds__(512) cp_kv_reduce_kernel(const TpArgs a) {
+  __shared__ int fail;
+  if (threadIdx.x == 0) fail = 0;
+  __syncthreads();
+  if (!tp_handshake(a, 0, &fail)) return;
+  const int C = a.cols / 2;
+  const int vpr = a.cols / 8;
+  const int64_t nvec = (int64_t)a.B * a.Tl * vpr;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = v / vpr;
+    const int c = (int)(v % vpr) * 8;
+    const int64_t off = cp_row(a, a.rank, i) * a.cols + c;
+    float acc[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+    for (int q = a.rank; q < a.world; ++q) {
+      const uint4 w = __ldcg(reinterpret_cast<const uint4*>(
+          reinterpret_cast<const __nv_bfloat16*>(a.peer_bufs[q]) + off));
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = unpack_bf16x2(ws[k]);
+        acc[2 * k] += f.x;
+        acc[2 * k + 1] += f.y;
+      }
+    }
+    *reinterpret_cast<uint4*>(a.out_bf16 + i * a.src_ld + C + c) =
+        make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                   pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
+    atomicAdd(a.byte_counter, (unsigned long long)(nvec * 16 * (a.world - a.rank)));
+  finish(a, &fail);
+}
+
 int grid_for_rows(int64_t rows, int per_cta, int cap) {
   int64_t g = (rows + per_cta - 1) / per_cta;
   if (g < 1) g = 1;
@@ -374,6 +458,21 @@ int tp_embed_bwd_launch(TpArgs a, cudaStream_t s) {
 int tp_ce_stats_launch(TpArgs a, cudaStream_t s) {
   if (a.rows <= 0 || a.vocab_valid <= 0) return -1;
   tp_ce_stats_kernel<<<(unsigned)a.rows, CE_T, 0, s>>>(a);
+  count_launches(1);
+  return launch_succeeded() ? 0 : -11;
+}
+
+int cp_kv_gather_launch(TpArgs a, cudaStream_t s) {
+  if (!common_ok(a) || a.cols % 16 || a.src_ld % 8 || a.B <= 0 || a.Tl <= 0 || !a.src) return -1;
+  cp_kv_gather_kernel<<<a.nblocks, 512, 0, s>>>(a);
+  count_launches(1);
+  return launch_succeeded() ? 0 : -11;
+}
+
+int cp_kv_reduce_launch(TpArgs a, cudaStream_t s) {
+  if (!common_ok(a) || a.cols % 16 || a.src_ld % 8 || a.B <= 0 || a.Tl <= 0 || !a.out_bf16)
+    return -1;
+  cp_kv_reduce_kernel<<<a.nblocks, 512, 0, s>>>(a);
   count_launches(1);
   return launch_succeeded() ? 0 : -11;
 }

@@ -41,6 +41,14 @@ struct TpArgs {
   unsigned long long* byte_counter = nullptr;
   uint32_t* err = nullptr;
   int64_t wait_budget_ns = 2000000000ll;
+  // context parallelism (cp_kv_gather / cp_kv_reduce): B sequences of
+  // world * Tl tokens; this rank owns tokens [rank*Tl, (rank+1)*Tl) of each.
+  // peer_bufs[q] is rank q's [B, world*Tl, 2C] bf16 key/value buffer; `src`
+  // (gather) / `out_bf16` (reduce) is this rank's fused qkv [B*Tl, ld] whose
+  // columns [C, 3C) hold k and v.
+  const __nv_bfloat16* src = nullptr;
+  int64_t src_ld = 0;
+  int B = 0, Tl = 0;
 };
 
 int tp_ag_rows_launch(TpArgs a, cudaStream_t s);
@@ -49,5 +57,14 @@ int tp_embed_fwd_launch(TpArgs a, cudaStream_t s);
 int tp_embed_bwd_launch(TpArgs a, cudaStream_t s);
 int tp_ce_stats_launch(TpArgs a, cudaStream_t s);
 int tp_ce_finish_launch(TpArgs a, cudaStream_t s);
+
+// Context parallelism, all-gather-KV form: copy this rank's k/v rows into its
+// own block of the symmetric key/value buffer, then pull the blocks of every
+// earlier rank (the only keys a causal query of this rank can see). `cols` = 2C.
+int cp_kv_gather_launch(TpArgs a, cudaStream_t s);
+// Reduce-scatter of the key/value gradients: this rank's block summed over
+// ranks rank..world-1 (the ranks whose queries saw these keys), in rank
+// order, into columns [C, 3C) of the local dqkv rows (out_bf16, ld).
+int cp_kv_reduce_launch(TpArgs a, cudaStream_t s);
 
 }  // namespace g2b

@@ -105,7 +105,7 @@ class P2PAllReducer:
     flags with bounded waits) on the current stream.
     """
 
-    def __init__(self, nbytes: int, group=None, device: Optional[torch.device] = None, nblocks: int = 64) -> None:
+    def __init__(self, nbytes: int, group=None, device: Optional[torch.device] = None, nblocks: int = 128) -> None:
         self.data = SymmetricBuffer(nbytes, group, device)
         self.flags = SymmetricBuffer(N.lib().comm_flag_words() * 4, group, device)
         self.rank, self.world, self.device = self.data.rank, self.data.world, self.data.device
