@@ -52,9 +52,11 @@ def test_sequence_parallel_payload_is_twice_raw_same_ar_equivalent():
 
 
 def test_padded_vocab():
-    assert padded_vocab(50257, 1) == 50304
-    assert padded_vocab(50257, 8) == 50688 or padded_vocab(50257, 8) % 8 == 0
-    assert all(padded_vocab(50257, p) % (64 * p) == 0 for p in (1, 2, 4, 8))
+    # the padded GPT-2 vocabulary at every power-of-two group size up to 8:
+    # a multiple of 64, split in equal per-rank blocks of a multiple of 16 rows
+    assert all(padded_vocab(50257, p) == 50304 for p in (1, 2, 4, 8))
+    assert all(padded_vocab(50257, p) % 64 == 0 and (padded_vocab(50257, p) // p) % 16 == 0
+               for p in (1, 2, 3, 4, 5, 6, 7, 8))
 
 
 @pytest.mark.parametrize("world", [2, 4])
