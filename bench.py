@@ -42,6 +42,10 @@ sequence parallelism over all N GPUs with `--batch` the GLOBAL batch (strong
 scaling); the reference has no tensor-parallel GPT training entry point (and
 its TensorParallelBlock needs n_head % N == 0; XL has 25 heads), so its arm
 prints `unavailable` for N > 1.
+`--strategy cp --model gpt2-large --batch 1 --seq 16384` runs context
+parallelism over all N GPUs (each GPU computes T/N tokens of every sequence,
+causal all-gather of K/V over peer memory, weight gradients averaged like
+DDP); the reference has no such entry point.
 """
 
 from __future__ import annotations
@@ -208,12 +212,14 @@ def run_native(args, world, rank):
     from gpt2_harness_b200.ops import native as N
     from gpt2_harness_b200.trainer import Trainer
 
-    cfg = gpt2_config(args.model)
+    # learned positions extended to the benchmark context when it is longer
+    cfg = gpt2_config(args.model, n_positions=max(args.seq, gpt2_config(args.model).n_positions))
     tc = TrainConfig(lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, grad_clip=1.0, warmup_steps=0)
     trainer = Trainer(cfg, args.batch, args.seq, train=tc, comm=args.comm, schedule=False,
                       strategy=args.strategy, bucket_bytes=int(args.bucket_mb * 2**20),
                       comm_blocks=args.comm_blocks)
-    host, dev = make_data(cfg, args.batch, args.seq, rank)
+    # tensor and context parallel ranks all take the same global batch
+    host, dev = make_data(cfg, args.batch, args.seq, 0 if args.strategy in ("tp", "cp") else rank)
     L = N.lib()
 
     def dev_step(i):
@@ -264,6 +270,11 @@ def run_reference(args, world, rank):
     from transformer_internals.parallel.data_parallel import average_gradients
 
     cfg = ref_config(args.model)
+    if args.strategy == "cp":
+        return {"impl": "reference", "unavailable": (
+            "the reference has no context-parallel GPT training entry point (all_gather_kv_attention "
+            "covers one attention call); at the long contexts CP is for, its single-GPU model "
+            "materialises T x T attention scores per layer")}
     if args.strategy == "tp" and world > 1:
         why = ("the reference has no tensor-parallel GPT training entry point (its "
                "TensorParallelBlock covers single blocks, without a vocabulary-parallel head)")
@@ -349,7 +360,7 @@ def gpu_list(world):
 def finish_line(args, world, cfg, ms, ms_e2e, bi, bo, sampler, impl):
     from gpt2_harness_b200.perf.mfu import flops_per_token_exact, measured_peak_tflops
 
-    tokens = args.batch * args.seq * (1 if args.strategy == "tp" else world)
+    tokens = args.batch * args.seq * (1 if args.strategy in ("tp", "cp") else world)
     tps = tokens / (ms / 1e3)
     tps_e2e = tokens / (ms_e2e / 1e3)
     fpt = flops_per_token_exact(cfg, args.seq)["training_flops_per_token"]
@@ -365,7 +376,7 @@ def finish_line(args, world, cfg, ms, ms_e2e, bi, bo, sampler, impl):
         "warmup": args.warmup,
         "ms_per_step": round(ms, 3),
         "higher_is_better": True,
-        "scaling": "strong" if args.strategy == "tp" else "weak",
+        "scaling": "strong" if args.strategy in ("tp", "cp") else "weak",
         "vs_baseline": round(tps / BASELINE_TOKENS_PER_S, 2),
         "dtype": "bf16",
         "data": "synthetic uniform-random tokens, random-init weights",
@@ -375,11 +386,12 @@ def finish_line(args, world, cfg, ms, ms_e2e, bi, bo, sampler, impl):
         "config": {
             "model": {"gpt2": "gpt2 (124M)", "gpt2-medium": "gpt2-medium (350M)",
                       "gpt2-large": "gpt2-large (774M)", "gpt2-xl": "gpt2-xl (1.5B)"}.get(args.model, args.model),
-            "global_batch": args.batch * (1 if args.strategy == "tp" else world),
-            "per_gpu_batch": args.batch if args.strategy != "tp" else None,
+            "global_batch": args.batch * (1 if args.strategy in ("tp", "cp") else world),
+            "per_gpu_batch": args.batch if args.strategy not in ("tp", "cp") else None,
             "seq_len": args.seq,
             "parallelism": (f"dp{world}" if args.strategy == "ddp" else
-                            f"tp{world}-sp" if args.strategy == "tp" else f"{args.strategy}-dp{world}"),
+                            f"tp{world}-sp" if args.strategy == "tp" else
+                            f"cp{world}" if args.strategy == "cp" else f"{args.strategy}-dp{world}"),
             "strategy": args.strategy,
             "bucket_mb": args.bucket_mb,
             "optimizer": "AdamW + clip 1.0, fp32 master",
@@ -405,7 +417,7 @@ def main():
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--seq", type=int, default=1024)
     ap.add_argument("--comm", choices=["p2p", "nccl"], default="p2p")
-    ap.add_argument("--strategy", choices=["ddp", "zero2", "zero3", "tp"], default="ddp")
+    ap.add_argument("--strategy", choices=["ddp", "zero2", "zero3", "tp", "cp"], default="ddp")
     ap.add_argument("--bucket-mb", type=float, default=25.0, help="gradient bucket size (MiB)")
     ap.add_argument("--comm-blocks", type=int, default=128, help="CTAs per fused all-reduce")
     args = ap.parse_args()

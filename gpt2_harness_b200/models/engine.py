@@ -286,6 +286,13 @@ class Engine:
         self.param_source: Optional[Callable[[str], Optional[torch.Tensor]]] = None
         self.grad_source: Optional[Callable[[str], Optional[torch.Tensor]]] = None
         self.block_hook: Optional[Callable[[str, int], None]] = None
+        # Context parallelism: this rank's tokens sit at positions
+        # [pos0, pos0 + T) of the full sequence, and attention is delegated to
+        # attn_fwd_hook(l, qkv, y, lse, B, H, T) / attn_bwd_hook(l, qkv, y, dy,
+        # dqkv, lse, delta, B, H, T) when set.
+        self.pos0 = 0
+        self.attn_fwd_hook: Optional[Callable] = None
+        self.attn_bwd_hook: Optional[Callable] = None
         # LayerNorm backward also produces the c_proj bias gradients of the
         # block that fed it (one block earlier for ln_1); a sharded gradient
         # buffer per block turns this off so each block writes only its own.
@@ -404,13 +411,13 @@ class Engine:
         cfg = self.config
         idx = idx.contiguous()
         B, T = idx.shape
-        if T > cfg.n_positions:
-            raise ValueError(f"sequence of length {T} exceeds n_positions={cfg.n_positions}")
+        if self.pos0 + T > cfg.n_positions:
+            raise ValueError(f"positions up to {self.pos0 + T} exceed n_positions={cfg.n_positions}")
         A = self.acts(B, T)
         C, H, L, V = cfg.n_embd, cfg.n_head, cfg.n_layer, cfg.vocab_size
         eps = cfg.layer_norm_epsilon
         p = self.p16
-        N.embedding_fwd(idx, p("wte.weight"), p("wpe.weight"), A.x[0])
+        N.embedding_fwd(idx, p("wte.weight"), p("wpe.weight"), A.x[0], pos0=self.pos0)
         bh = self.block_hook
         for l in range(L):
             pre = f"h.{l}."
@@ -420,7 +427,10 @@ class Engine:
                             A.mu[2 * l], A.rs[2 * l], eps)
             N.gemm(A.h1[l], p(pre + "attn.c_attn.weight"), A.qkv[l], bias=p(pre + "attn.c_attn.bias"))
             qkv = A.qkv[l]
-            N.attention_fwd(qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:], A.y[l], A.lse[l], B, H, T)
+            if self.attn_fwd_hook is not None:
+                self.attn_fwd_hook(l, qkv, A.y[l], A.lse[l], B, H, T)
+            else:
+                N.attention_fwd(qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:], A.y[l], A.lse[l], B, H, T)
             N.gemm(A.y[l], p(pre + "attn.c_proj.weight"), A.x[2 * l + 1], epilogue=N.EPI_RESID_F32,
                    bias=p(pre + "attn.c_proj.bias"), aux=A.x[2 * l])
             N.layernorm_fwd(A.x[2 * l + 1], p(pre + "ln_2.weight"), p(pre + "ln_2.bias"), A.h2[l],
@@ -491,8 +501,12 @@ class Engine:
                 N.colsum_bf16(A.dres16, g(pre + "attn.c_proj.bias"), A.col_ws, accumulate=acc)
             # attention
             qkv, dqkv = A.qkv[l], A.dqkv
-            N.attention_bwd(qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:], A.y[l], A.dy,
-                            dqkv[:, :C], dqkv[:, C:2 * C], dqkv[:, 2 * C:], A.lse[l], A.delta, B, H, T)
+            if self.attn_bwd_hook is not None:
+                self.attn_bwd_hook(l, qkv, A.y[l], A.dy, dqkv, A.lse[l], A.delta, B, H, T)
+            else:
+                N.attention_bwd(qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:], A.y[l], A.dy,
+                                dqkv[:, :C], dqkv[:, C:2 * C], dqkv[:, 2 * C:], A.lse[l], A.delta,
+                                B, H, T)
             # attn.c_attn
             N.gemm(dqkv, p(pre + "attn.c_attn.weight"), A.dh, b_t=True)
             N.gemm(dqkv, A.h1[l], g(pre + "attn.c_attn.weight"), a_t=True, b_t=True,
@@ -508,7 +522,7 @@ class Engine:
         wpe_g = g("wpe.weight")
         if not acc:
             wpe_g.zero_()
-        N.embedding_bwd(idx, A.dres, g("wte.weight"), wpe_g, V)
+        N.embedding_bwd(idx, A.dres, g("wte.weight"), wpe_g, V, pos0=self.pos0)
         if hook:
             hook("root_tail")
 

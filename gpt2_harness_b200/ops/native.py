@@ -202,18 +202,22 @@ def _head_strides(t: torch.Tensor, T: int, H: int):
 
 def attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor,
                   lse: torch.Tensor, B: int, H: int, Tq: int, Tk: Optional[int] = None,
-                  q_offset: int = 0, causal: bool = True, scale: Optional[float] = None) -> None:
+                  q_offset: int = 0, causal: bool = True, scale: Optional[float] = None,
+                  kv_rows: Optional[int] = None) -> None:
     """Causal flash attention on head_dim 64.
 
     q, o: [B*Tq, ...] row-major views whose columns h*64..h*64+63 hold head h
     (e.g. the q section of the fused qkv buffer); k, v: [B*Tk, ...] likewise.
     lse: fp32 [B, H, Tq] (log2-domain log-sum-exp, saved for backward).
+    kv_rows: rows per sequence in the k/v buffers when they hold more than the
+    Tk keys attended (context parallelism: a full-length key buffer of which
+    a prefix is visible); defaults to Tk.
     """
     Tk = Tq if Tk is None else Tk
     scale = 1.0 / math.sqrt(64) if scale is None else scale
     qsb, qst, qsh = _head_strides(q, Tq, H)
-    ksb, kst, ksh = _head_strides(k, Tk, H)
-    if _head_strides(v, Tk, H) != (ksb, kst, ksh):
+    ksb, kst, ksh = _head_strides(k, Tk if kv_rows is None else kv_rows, H)
+    if _head_strides(v, Tk if kv_rows is None else kv_rows, H) != (ksb, kst, ksh):
         raise ValueError("k and v must share strides")
     osb, ost, osh = _head_strides(o, Tq, H)
     lib().attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), qsb, qst, qsh,
@@ -223,22 +227,23 @@ def attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Te
 
 def attention_bwd(q, k, v, o, dout, dq, dk, dv, lse, delta, B: int, H: int, Tq: int,
                   Tk: Optional[int] = None, q_offset: int = 0, causal: bool = True,
-                  scale: Optional[float] = None) -> None:
+                  scale: Optional[float] = None, kv_rows: Optional[int] = None) -> None:
     """Deterministic flash-attention backward (dK/dV pass, then dQ pass).
 
     dout shares o's strides; dq shares q's layout family; dk/dv share a layout.
     delta: fp32 scratch [B, H, Tq].
     """
     Tk = Tq if Tk is None else Tk
+    kr = Tk if kv_rows is None else kv_rows
     scale = 1.0 / math.sqrt(64) if scale is None else scale
     qsb, qst, qsh = _head_strides(q, Tq, H)
-    ksb, kst, ksh = _head_strides(k, Tk, H)
+    ksb, kst, ksh = _head_strides(k, kr, H)
     osb, ost, osh = _head_strides(o, Tq, H)
     if _head_strides(dout, Tq, H) != (osb, ost, osh):
         raise ValueError("dout must share o's strides")
     dsb, dst, dsh = _head_strides(dq, Tq, H)
-    dksb, dkst, dksh = _head_strides(dk, Tk, H)
-    if _head_strides(dv, Tk, H) != (dksb, dkst, dksh):
+    dksb, dkst, dksh = _head_strides(dk, kr, H)
+    if _head_strides(dv, kr, H) != (dksb, dkst, dksh):
         raise ValueError("dk and dv must share strides")
     lib().attn_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dout.data_ptr(),
                    dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), qsb, qst, qsh, osb, ost, osh,

@@ -1,0 +1,129 @@
+"""Context parallelism (all-gather-KV form) on the native engine.
+
+Reference semantics: src/transformer_internals/parallel/sequence_parallel.py
+:60-132 (``all_gather_kv_attention``: every rank holds a contiguous shard of
+the sequence, all-gathers K and V along the sequence, attends causally at
+absolute positions ``rank * T_local``; backward reduce-scatters dK and dV; the
+weight gradients are all-reduced over the group).
+
+B200 design:
+
+* Each rank runs the engine on its T/p tokens of every sequence, with
+  positions offset by ``rank * T/p`` (learned position embeddings read at the
+  absolute position).
+* Attention of layer l: ``cp_kv_gather`` (csrc/tp.cu) copies this rank's k/v
+  rows into its block of a per-layer symmetric [B, T, 2C] key/value buffer and
+  pulls the blocks of the EARLIER ranks by P2P loads -- a causal query of rank
+  r never sees later keys, so rank r moves r/p of the sequence, not all of it.
+  The tcgen05 attention then runs with ``q_offset = r*T/p`` over the first
+  (r+1)*T/p keys of that buffer.
+* Backward: the attention backward writes dK/dV of every key it saw into a
+  symmetric partial buffer; ``cp_kv_reduce`` sums this rank's key block over
+  the ranks whose queries saw it (r..p-1, in rank order) straight into the
+  k/v columns of the local dqkv, which the c_attn backward then consumes.
+* Weight gradients: the data-parallel machinery over the same group
+  (:class:`~gpt2_harness_b200.parallel.ddp_native.NativeDDP`: bucketed P2P
+  all-reduce overlapped with backward, mean over ranks) -- with equal token
+  counts per rank the mean of the per-rank mean losses is the global mean.
+
+Payload per rank per layer in the reference convention: the gather is charged
+its output (2 x B x T x C x 2 bytes: K and V, bf16), the reduce-scatter its
+input (the same), as for ``_GatherSequence``.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from gpt2_harness_b200.config import GPTConfig
+from gpt2_harness_b200.ops import native as N
+from gpt2_harness_b200.parallel import comms
+from gpt2_harness_b200.parallel.symm import SymmetricBuffer
+
+__all__ = ["NativeCP"]
+
+
+class NativeCP:
+    """Sequence sharding of attention for :class:`~gpt2_harness_b200.models.engine.Engine`.
+
+    Build it with the full sequence length ``T`` and batch ``B``; the engine
+    then runs on ``B x T/p`` tokens per rank (this rank's shard of every
+    sequence). Call :meth:`attach` on the engine.
+    """
+
+    def __init__(self, config: GPTConfig, B: int, T: int, group=None,
+                 device: Optional[torch.device] = None, nblocks: int = 128) -> None:
+        if not dist.is_initialized():
+            raise RuntimeError("NativeCP needs an initialised process group")
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("NativeCP supports up to 8 ranks (one NVSwitch domain)")
+        if T % self.world:
+            raise ValueError("the sequence length must split evenly over the group")
+        self.device = dev = device or torch.device("cuda", torch.cuda.current_device())
+        self.config = config
+        self.B, self.T = B, T
+        self.Tl = T // self.world
+        self.pos0 = self.rank * self.Tl
+        C, L = config.n_embd, config.n_layer
+        self.C = C
+        self.nblocks = nblocks
+        bf = torch.bfloat16
+        rows = B * T
+        self._kv = SymmetricBuffer(L * rows * 2 * C * 2, group, dev)      # per-layer gathered k/v
+        self._dkv = SymmetricBuffer(rows * 2 * C * 2, group, dev)         # dk/dv partials (reused)
+        self._flags = SymmetricBuffer(N.lib().tp_flag_words() * 4, group, dev)
+        kv = self._kv.view(bf, L * rows * 2 * C).view(L, rows, 2 * C)
+        self.kv = [kv[l] for l in range(L)]
+        self.dkv = self._dkv.view(bf, rows * 2 * C).view(rows, 2 * C)
+        self._kv_ptrs = [torch.tensor([p + l * rows * 2 * C * 2 for p in self._kv.peer_ptrs],
+                                      dtype=torch.int64, device=dev) for l in range(L)]
+        self.byte_counter = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.epoch = 0
+
+    def attach(self, engine) -> None:
+        engine.pos0 = self.pos0
+        engine.attn_fwd_hook = self.attention_fwd
+        engine.attn_bwd_hook = self.attention_bwd
+
+    def _args(self, ptrs: int, **kw) -> dict:
+        self.epoch += 1
+        d = {"peer_bufs": ptrs, "peer_flags": self._flags.peer_ptrs_dev.data_ptr(), "rank": self.rank,
+             "world": self.world, "nblocks": self.nblocks, "epoch": self.epoch & 0xFFFFFFFF,
+             "err": N.error_word(self.device).data_ptr(), "byte_counter": self.byte_counter.data_ptr(),
+             "cols": 2 * self.C, "B": self.B, "Tl": self.Tl}
+        d.update(kw)
+        return d
+
+    # ------------------------------------------------------------ hooks --
+    def attention_fwd(self, l: int, qkv, y, lse, B: int, H: int, Tl: int) -> None:
+        C, T = self.C, self.T
+        kv = self.kv[l]
+        nbytes = B * T * 2 * C * 2
+        comms.record_external("all_gather", B * T * 2 * C, nbytes)
+        d = self._args(self._kv_ptrs[l].data_ptr(), src=qkv.data_ptr(), src_ld=qkv.stride(0))
+        N.lib().cp_kv_gather(d, torch.cuda.current_stream(self.device).cuda_stream)
+        Tk = (self.rank + 1) * self.Tl
+        N.attention_fwd(qkv[:, :C], kv[:, :C], kv[:, C:], y, lse, B, H, Tl, Tk=Tk,
+                        q_offset=self.pos0, kv_rows=T)
+
+    def attention_bwd(self, l: int, qkv, y, dy, dqkv, lse, delta, B: int, H: int, Tl: int) -> None:
+        C, T = self.C, self.T
+        kv, dkv = self.kv[l], self.dkv
+        Tk = (self.rank + 1) * self.Tl
+        N.attention_bwd(qkv[:, :C], kv[:, :C], kv[:, C:], y, dy, dqkv[:, :C], dkv[:, :C], dkv[:, C:],
+                        lse, delta, B, H, Tl, Tk=Tk, q_offset=self.pos0, kv_rows=T)
+        nbytes = B * T * 2 * C * 2
+        comms.record_external("reduce_scatter", B * T * 2 * C, nbytes)
+        d = self._args(self._dkv.peer_ptrs_dev.data_ptr(), out_bf16=dqkv.data_ptr(), src_ld=dqkv.stride(0))
+        N.lib().cp_kv_reduce(d, torch.cuda.current_stream(self.device).cuda_stream)
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.device)
+        for b in (self._kv, self._dkv, self._flags):
+            b.close()

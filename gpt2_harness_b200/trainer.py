@@ -53,7 +53,10 @@ class Trainer:
             default process group has more than one rank (DDP only).
         strategy: ``"ddp"``, ``"zero2"`` or ``"zero3"`` (ignored on one rank),
             or ``"tp"``: tensor + sequence parallelism over all ranks, where
-            ``batch_size`` is the GLOBAL batch every rank receives.
+            ``batch_size`` is the GLOBAL batch every rank receives, or
+            ``"cp"``: context parallelism, every rank receives the same
+            ``batch_size`` full sequences of ``seq_len`` tokens and computes
+            its contiguous ``seq_len / p`` slice of each.
         comm_blocks: CTAs of each fused peer-memory all-reduce (DDP, p2p):
             fewer leave more of the GPU to the backward it overlaps.
         seed: weight init seed (identical on every rank; rank 0's weights are
@@ -78,7 +81,7 @@ class Trainer:
         tc = self.train_cfg
         optim = OptimConfig(lr=tc.lr, betas=tuple(tc.betas), eps=tc.eps,
                             weight_decay=tc.weight_decay, grad_clip=tc.grad_clip)
-        if strategy not in ("ddp", "zero2", "zero3", "tp"):
+        if strategy not in ("ddp", "zero2", "zero3", "tp", "cp"):
             raise ValueError(f"unknown strategy {strategy!r}")
         self.strategy = strategy if (self.world > 1 or strategy == "tp") else "single"
         if strategy == "tp":
@@ -94,8 +97,22 @@ class Trainer:
             self.h2d_done = torch.cuda.Event()
             return
         self.ddp = None
+        self.cp = None
         grad_buffer = shadow_buffer = None
-        if self.world > 1:
+        if strategy == "cp" and self.world > 1:
+            # context parallelism: every rank takes the same batch of full
+            # sequences and computes its contiguous T/p slice of each;
+            # weight gradients are averaged over the group like DDP
+            from gpt2_harness_b200.models.engine import ParamLayout
+            from gpt2_harness_b200.parallel.cp_native import NativeCP
+            from gpt2_harness_b200.parallel.ddp_native import NativeDDP
+
+            self.cp = NativeCP(config, batch_size, seq_len, device=self.device)
+            self.ddp = NativeDDP(ParamLayout(config), comm=comm, bucket_bytes=bucket_bytes,
+                                 device=self.device, nblocks=comm_blocks)
+            grad_buffer = self.ddp.grad_buffer
+            self.T_local = seq_len // self.world
+        elif self.world > 1:
             from gpt2_harness_b200.models.engine import ParamLayout
 
             layout = ParamLayout(config)
@@ -121,7 +138,12 @@ class Trainer:
             dist.broadcast(self.engine.master, src=0)
             self.engine.sync_shadow()
             self.ddp.attach(self.engine)
-        self.engine.acts(batch_size, seq_len)
+        if self.cp is not None:
+            self.cp.attach(self.engine)
+        self.engine.acts(batch_size, seq_len if self.cp is None else self.T_local)
+        if self.cp is not None:
+            self.idx_l = torch.zeros(batch_size, self.T_local, dtype=torch.int64, device=self.device)
+            self.tgt_l = torch.zeros(batch_size, self.T_local, dtype=torch.int64, device=self.device)
         self.idx = torch.zeros(batch_size, seq_len, dtype=torch.int64, device=self.device)
         self.tgt = torch.zeros(batch_size, seq_len, dtype=torch.int64, device=self.device)
         self.step_num = 0
@@ -138,6 +160,16 @@ class Trainer:
     def _load_inputs(self, idx: torch.Tensor, targets: torch.Tensor):
         if idx.shape != (self.B, self.T) or targets.shape != (self.B, self.T):
             raise ValueError(f"expected ({self.B}, {self.T}) batches, got {tuple(idx.shape)}")
+        if self.cp is not None:
+            # this rank's slice of every sequence
+            a, b = self.cp.pos0, self.cp.pos0 + self.T_local
+            idx, targets = idx[:, a:b], targets[:, a:b]
+            if idx.device.type == "cpu":
+                idx, targets = idx.contiguous(), targets.contiguous()
+            self.idx_l.copy_(idx, non_blocking=True)
+            self.tgt_l.copy_(targets, non_blocking=True)
+            self.h2d_done.record()
+            return self.idx_l, self.tgt_l
         if idx.device == self.device and targets.device == self.device:
             return idx, targets
         self.idx.copy_(idx, non_blocking=True)
@@ -199,5 +231,7 @@ class Trainer:
         if self.strategy == "tp":
             self.engine.close()
             return
+        if self.cp is not None:
+            self.cp.close()
         if self.ddp is not None:
             self.ddp.close()

@@ -1,0 +1,112 @@
+"""Native context parallelism (per-layer causal all-gather of K/V over peer
+memory, dK/dV reduce-scatter, weight gradients averaged over the group)
+against the single-GPU engine on the full sequences: loss and every
+gradient. Child processes, one per GPU; the 2-GPU case is skipped when fewer
+are visible."""
+
+import json
+import os
+import socket
+import subprocess
+import sys
+import textwrap
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+WORKER = textwrap.dedent(r'''
+    import os, sys, json, datetime
+    import torch, torch.distributed as dist
+    sys.path.insert(0, os.environ["G2B_ROOT"])
+    from gpt2_harness_b200.config import gpt2_config
+    from gpt2_harness_b200.models.engine import Engine, OptimConfig, ParamLayout
+    from gpt2_harness_b200.parallel.cp_native import NativeCP
+    from gpt2_harness_b200.parallel.ddp_native import NativeDDP
+    from gpt2_harness_b200.parallel import comms
+    from gpt2_harness_b200.ops import native as N
+
+    rank = int(os.environ["RANK"]); world = int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    cfg = gpt2_config("gpt2", n_layer=2, n_positions=1024)
+    B, T = 2, 1024
+    Tl = T // world
+    cp = NativeCP(cfg, B, T)
+    ddp = NativeDDP(ParamLayout(cfg), comm="p2p")
+    eng = Engine(cfg, "cuda", grad_buffer=ddp.grad_buffer, seed=0)
+    ddp.attach(eng)
+    cp.attach(eng)
+    ref = Engine(cfg, "cuda", seed=0)
+    g = torch.Generator().manual_seed(11)
+    idx = torch.randint(0, cfg.vocab_size, (B, T), generator=g).cuda()
+    tgt = torch.randint(0, cfg.vocab_size, (B, T), generator=g).cuda()
+    a, b = rank * Tl, (rank + 1) * Tl
+    with comms.counter_scope(world) as ctr:
+        loss = eng.forward(idx[:, a:b].contiguous(), tgt[:, a:b].contiguous())
+        eng.backward(idx[:, a:b].contiguous()); ddp.finish()
+        ctr.steps += 1
+        torch.cuda.synchronize()
+        N.check_errors()
+        summary = ctr.summary()
+    mean_loss = loss.clone(); dist.all_reduce(mean_loss); mean_loss /= world
+    ref_loss = float(ref.forward(idx, tgt).item())
+    ref.backward(idx)
+    torch.cuda.synchronize()
+    errs = {}
+    for s in ref.layout.specs:
+        r = ref.g32(s.name)
+        errs[s.name] = ((eng.g32(s.name) - r).norm() / (r.norm() + 1e-12)).item()
+    worst = max(errs, key=errs.get)
+    out = {"rank": rank, "loss": float(mean_loss.item()), "ref_loss": ref_loss, "worst": worst,
+           "worst_err": errs[worst], "payload": summary["payload_bytes_per_step"]}
+    print("RESULT " + json.dumps(out), flush=True)
+    ddp.close(); cp.close()
+    dist.destroy_process_group()
+''')
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _run(world: int):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    port = _free_port()
+    procs = []
+    for r in range(world):
+        env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r),
+                   MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), G2B_ROOT=ROOT,
+                   NCCL_NVLS_ENABLE="0")
+        procs.append(subprocess.Popen([sys.executable, "-c", WORKER], env=env, stdout=subprocess.PIPE,
+                                      stderr=subprocess.STDOUT, text=True))
+    results = []
+    for p in procs:
+        try:
+            out, _ = p.communicate(timeout=240)
+        except subprocess.TimeoutExpired:
+            for q in procs:
+                q.kill()
+            outs = [q.communicate()[0] for q in procs]
+            raise AssertionError("CP workers timed out:\n" + "\n-----\n".join(o[-4000:] for o in outs))
+        assert p.returncode == 0, out[-3000:]
+        line = [l for l in out.splitlines() if l.startswith("RESULT ")]
+        assert line, out[-3000:]
+        results.append(json.loads(line[-1][7:]))
+    return results
+
+
+@pytest.mark.parametrize("world", [1, 2])
+def test_native_cp_matches_single_gpu(world):
+    res = _run(world)
+    print(res)
+    for r in res:
+        assert abs(r["loss"] - r["ref_loss"]) < 1e-3 * abs(r["ref_loss"]), r
+        assert r["worst_err"] < 2e-2, r
