@@ -29,7 +29,7 @@ import torch.distributed as dist
 __all__ = ["OPS", "DEFAULT_SIZES", "bus_factor", "bus_bandwidth", "fit_link_model", "run"]
 
 OPS = ("all_reduce", "all_gather", "reduce_scatter")
-DEFAULT_SIZES = [1 << k for k in range(10, 27, 2)]  # 1 KiB .. 64 MiB
+DEFAULT_SIZES = [1 << k for k in range(10, 29, 2)]  # 1 KiB .. 256 MiB
 
 
 def bus_factor(op: str, world: int) -> float:

@@ -84,6 +84,7 @@ class Trainer:
         if strategy not in ("ddp", "zero2", "zero3", "tp", "cp"):
             raise ValueError(f"unknown strategy {strategy!r}")
         self.strategy = strategy if (self.world > 1 or strategy == "tp") else "single"
+        self.cp = None
         if strategy == "tp":
             # tensor + sequence parallelism: every rank takes the same global
             # batch (batch_size x seq_len) and holds 1/p of every block
