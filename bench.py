@@ -46,6 +46,13 @@ prints `unavailable` for N > 1.
 parallelism over all N GPUs (each GPU computes T/N tokens of every sequence,
 causal all-gather of K/V over peer memory, weight gradients averaged like
 DDP); the reference has no such entry point.
+`--strategy pp --pp 4 --cp 2 --model gpt2-large --batch 1 --seq 16384
+--micro-batches 8` is BASELINE config 5: pipeline parallelism (1F1B over NCCL
+point-to-point, `--schedule gpipe` for GPipe) with context parallelism inside
+every stage; `--batch` is the micro-batch and every step runs all
+micro-batches (strong scaling: the global batch is fixed). The reference's
+pipeline runs only inside its equivalence harness (pipeline_worker on the tiny
+config), so its arm prints `unavailable`.
 """
 
 from __future__ import annotations
@@ -207,10 +214,72 @@ def make_data(cfg, B, T, rank, pool=4):
 
 
 # ------------------------------------------------------------------- arms --
+def tokens_per_step(args, world) -> int:
+    if args.strategy == "pp":
+        return args.micro_batches * args.batch * args.seq
+    return args.batch * args.seq * (1 if args.strategy in ("tp", "cp") else world)
+
+
+def run_pipeline(args, world, rank):
+    """PP (x CP) arm: every rank receives the same global batch."""
+    from gpt2_harness_b200.config import TrainConfig, gpt2_config
+    from gpt2_harness_b200.ops import native as N
+    from gpt2_harness_b200.trainer import PipelineTrainer
+
+    cfg = gpt2_config(args.model, n_positions=max(args.seq, gpt2_config(args.model).n_positions))
+    tc = TrainConfig(lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, grad_clip=1.0, warmup_steps=0)
+    cp = args.cp
+    pp = args.pp or world // cp
+    trainer = PipelineTrainer(cfg, args.batch, args.seq, args.micro_batches, pp=pp, cp=cp,
+                              schedule=args.schedule, train=tc, comm_blocks=args.comm_blocks)
+    trainer.schedule = False
+    host, dev = make_data(cfg, args.micro_batches * args.batch, args.seq, 0, pool=2)
+    L = N.lib()
+
+    def dev_step(i):
+        idx, tgt = dev[i % len(dev)]
+        trainer.step_async(idx, tgt)
+
+    sampler = ClockSampler(gpu_list(world)) if rank == 0 else None
+    launches = {}
+
+    def start():
+        launches["a"] = L.launch_count()
+        if sampler:
+            sampler.start()
+
+    def stop():
+        launches["b"] = L.launch_count()
+        if sampler:
+            sampler.stop()
+
+    ms = timed(dev_step, args.steps, args.warmup, world, start, stop)
+    trainer.check()
+    n_launch = sum_over_ranks(launches["b"] - launches["a"], world)
+
+    def e2e_step(i):
+        idx, tgt = host[i % len(host)]
+        trainer.step(idx, tgt)  # H2D of this rank's inputs + loss read back on the last stage
+
+    ms_e2e = timed(e2e_step, args.steps, 1, world)
+    trainer.check()
+    bi = int(max_over_ranks(trainer.h2d_bytes_per_step, world))
+    out = finish_line(args, world, cfg, ms, ms_e2e, bi, 4, sampler, impl="native")
+    out["gpu_launches"] = int(n_launch)
+    out["config"]["comm"] = "nccl p2p between stages, peer-memory kernels inside a CP group"
+    out["config"]["pp"], out["config"]["cp"] = pp, cp
+    out["config"]["micro_batches"], out["config"]["schedule"] = args.micro_batches, args.schedule
+    trainer.close()
+    return out
+
+
 def run_native(args, world, rank):
     from gpt2_harness_b200.config import TrainConfig, gpt2_config
     from gpt2_harness_b200.ops import native as N
     from gpt2_harness_b200.trainer import Trainer
+
+    if args.strategy == "pp":
+        return run_pipeline(args, world, rank)
 
     # learned positions extended to the benchmark context when it is longer
     cfg = gpt2_config(args.model, n_positions=max(args.seq, gpt2_config(args.model).n_positions))
@@ -270,6 +339,11 @@ def run_reference(args, world, rank):
     from transformer_internals.parallel.data_parallel import average_gradients
 
     cfg = ref_config(args.model)
+    if args.strategy == "pp":
+        return {"impl": "reference", "unavailable": (
+            "the reference's pipeline parallelism runs only inside its equivalence harness "
+            "(pipeline_worker on the tiny config, blocking send/recv per micro-batch); it has no "
+            "GPT-2 training entry point for a pipeline, and none composed with context parallelism")}
     if args.strategy == "cp":
         return {"impl": "reference", "unavailable": (
             "the reference has no context-parallel GPT training entry point (all_gather_kv_attention "
@@ -360,7 +434,7 @@ def gpu_list(world):
 def finish_line(args, world, cfg, ms, ms_e2e, bi, bo, sampler, impl):
     from gpt2_harness_b200.perf.mfu import flops_per_token_exact, measured_peak_tflops
 
-    tokens = args.batch * args.seq * (1 if args.strategy in ("tp", "cp") else world)
+    tokens = tokens_per_step(args, world)
     tps = tokens / (ms / 1e3)
     tps_e2e = tokens / (ms_e2e / 1e3)
     fpt = flops_per_token_exact(cfg, args.seq)["training_flops_per_token"]
@@ -376,7 +450,7 @@ def finish_line(args, world, cfg, ms, ms_e2e, bi, bo, sampler, impl):
         "warmup": args.warmup,
         "ms_per_step": round(ms, 3),
         "higher_is_better": True,
-        "scaling": "strong" if args.strategy in ("tp", "cp") else "weak",
+        "scaling": "strong" if args.strategy in ("tp", "cp", "pp") else "weak",
         "vs_baseline": round(tps / BASELINE_TOKENS_PER_S, 2),
         "dtype": "bf16",
         "data": "synthetic uniform-random tokens, random-init weights",
@@ -386,12 +460,14 @@ def finish_line(args, world, cfg, ms, ms_e2e, bi, bo, sampler, impl):
         "config": {
             "model": {"gpt2": "gpt2 (124M)", "gpt2-medium": "gpt2-medium (350M)",
                       "gpt2-large": "gpt2-large (774M)", "gpt2-xl": "gpt2-xl (1.5B)"}.get(args.model, args.model),
-            "global_batch": args.batch * (1 if args.strategy in ("tp", "cp") else world),
-            "per_gpu_batch": args.batch if args.strategy not in ("tp", "cp") else None,
+            "global_batch": tokens // args.seq,
+            "per_gpu_batch": args.batch if args.strategy not in ("tp", "cp", "pp") else None,
             "seq_len": args.seq,
             "parallelism": (f"dp{world}" if args.strategy == "ddp" else
                             f"tp{world}-sp" if args.strategy == "tp" else
-                            f"cp{world}" if args.strategy == "cp" else f"{args.strategy}-dp{world}"),
+                            f"cp{world}" if args.strategy == "cp" else
+                            f"pp{args.pp or world // args.cp}xcp{args.cp}-{args.schedule}"
+                            if args.strategy == "pp" else f"{args.strategy}-dp{world}"),
             "strategy": args.strategy,
             "bucket_mb": args.bucket_mb,
             "optimizer": "AdamW + clip 1.0, fp32 master",
@@ -417,7 +493,11 @@ def main():
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--seq", type=int, default=1024)
     ap.add_argument("--comm", choices=["p2p", "nccl"], default="p2p")
-    ap.add_argument("--strategy", choices=["ddp", "zero2", "zero3", "tp", "cp"], default="ddp")
+    ap.add_argument("--strategy", choices=["ddp", "zero2", "zero3", "tp", "cp", "pp"], default="ddp")
+    ap.add_argument("--pp", type=int, default=0, help="pipeline stages (pp strategy; default N / cp)")
+    ap.add_argument("--cp", type=int, default=1, help="context-parallel ranks per stage (pp strategy)")
+    ap.add_argument("--micro-batches", type=int, default=8, help="micro-batches per step (pp strategy)")
+    ap.add_argument("--schedule", choices=["1f1b", "gpipe"], default="1f1b")
     ap.add_argument("--bucket-mb", type=float, default=25.0, help="gradient bucket size (MiB)")
     ap.add_argument("--comm-blocks", type=int, default=128, help="CTAs per fused all-reduce")
     args = ap.parse_args()

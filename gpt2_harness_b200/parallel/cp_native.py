@@ -52,10 +52,17 @@ class NativeCP:
     Build it with the full sequence length ``T`` and batch ``B``; the engine
     then runs on ``B x T/p`` tokens per rank (this rank's shard of every
     sequence). Call :meth:`attach` on the engine.
+
+    ``layers`` (default all) names the absolute layer indices whose gathered
+    K/V are kept (a pipeline stage's blocks); ``slots`` keeps that many
+    independent sets, one per micro-batch in flight: the backward of a
+    micro-batch reads the K/V its forward gathered, after the forwards of
+    later micro-batches. :attr:`slot` selects the set.
     """
 
     def __init__(self, config: GPTConfig, B: int, T: int, group=None,
-                 device: Optional[torch.device] = None, nblocks: int = 128) -> None:
+                 device: Optional[torch.device] = None, nblocks: int = 128,
+                 layers: Optional[list] = None, slots: int = 1) -> None:
         if not dist.is_initialized():
             raise RuntimeError("NativeCP needs an initialised process group")
         self.group = group
@@ -75,21 +82,37 @@ class NativeCP:
         self.nblocks = nblocks
         bf = torch.bfloat16
         rows = B * T
-        self._kv = SymmetricBuffer(L * rows * 2 * C * 2, group, dev)      # per-layer gathered k/v
+        layers = list(range(L)) if layers is None else list(layers)
+        self.layer_index = {l: i for i, l in enumerate(layers)}
+        nl = len(layers) * slots
+        self.slots = slots
+        self.slot = 0
+        self._kv = SymmetricBuffer(nl * rows * 2 * C * 2, group, dev)     # per-layer gathered k/v
         self._dkv = SymmetricBuffer(rows * 2 * C * 2, group, dev)         # dk/dv partials (reused)
         self._flags = SymmetricBuffer(N.lib().tp_flag_words() * 4, group, dev)
-        kv = self._kv.view(bf, L * rows * 2 * C).view(L, rows, 2 * C)
-        self.kv = [kv[l] for l in range(L)]
+        kv = self._kv.view(bf, nl * rows * 2 * C).view(nl, rows, 2 * C)
+        self.kv = [kv[i] for i in range(nl)]
         self.dkv = self._dkv.view(bf, rows * 2 * C).view(rows, 2 * C)
-        self._kv_ptrs = [torch.tensor([p + l * rows * 2 * C * 2 for p in self._kv.peer_ptrs],
-                                      dtype=torch.int64, device=dev) for l in range(L)]
+        self._kv_ptrs = [torch.tensor([p + i * rows * 2 * C * 2 for p in self._kv.peer_ptrs],
+                                      dtype=torch.int64, device=dev) for i in range(nl)]
         self.byte_counter = torch.zeros(1, dtype=torch.int64, device=dev)
         self.epoch = 0
 
     def attach(self, engine) -> None:
+        """Route the engine's (or a pipeline stage engine's) attention here."""
         engine.pos0 = self.pos0
         engine.attn_fwd_hook = self.attention_fwd
         engine.attn_bwd_hook = self.attention_bwd
+        if hasattr(engine, "slot_hook"):
+            engine.slot_hook = self.set_slot
+
+    def set_slot(self, slot: int) -> None:
+        if not 0 <= slot < self.slots:
+            raise ValueError(f"slot {slot} out of range ({self.slots} kept)")
+        self.slot = slot
+
+    def _kv_index(self, l: int) -> int:
+        return self.slot * len(self.layer_index) + self.layer_index[l]
 
     def _args(self, ptrs: int, **kw) -> dict:
         self.epoch += 1
@@ -103,10 +126,11 @@ class NativeCP:
     # ------------------------------------------------------------ hooks --
     def attention_fwd(self, l: int, qkv, y, lse, B: int, H: int, Tl: int) -> None:
         C, T = self.C, self.T
-        kv = self.kv[l]
+        i = self._kv_index(l)
+        kv = self.kv[i]
         nbytes = B * T * 2 * C * 2
         comms.record_external("all_gather", B * T * 2 * C, nbytes)
-        d = self._args(self._kv_ptrs[l].data_ptr(), src=qkv.data_ptr(), src_ld=qkv.stride(0))
+        d = self._args(self._kv_ptrs[i].data_ptr(), src=qkv.data_ptr(), src_ld=qkv.stride(0))
         N.lib().cp_kv_gather(d, torch.cuda.current_stream(self.device).cuda_stream)
         Tk = (self.rank + 1) * self.Tl
         N.attention_fwd(qkv[:, :C], kv[:, :C], kv[:, C:], y, lse, B, H, Tl, Tk=Tk,
@@ -114,7 +138,7 @@ class NativeCP:
 
     def attention_bwd(self, l: int, qkv, y, dy, dqkv, lse, delta, B: int, H: int, Tl: int) -> None:
         C, T = self.C, self.T
-        kv, dkv = self.kv[l], self.dkv
+        kv, dkv = self.kv[self._kv_index(l)], self.dkv
         Tk = (self.rank + 1) * self.Tl
         N.attention_bwd(qkv[:, :C], kv[:, :C], kv[:, C:], y, dy, dqkv[:, :C], dkv[:, :C], dkv[:, C:],
                         lse, delta, B, H, Tl, Tk=Tk, q_offset=self.pos0, kv_rows=T)

@@ -10,6 +10,8 @@ every rank updates every parameter) or as ZeRO-2
 sharded AdamW and optimiser state, fused bf16 all-gather) or as ZeRO-3
 (:class:`~gpt2_harness_b200.parallel.zero3_native.NativeZeRO3`, block
 parameters sharded and gathered one block ahead over NVLink).
+``PipelineTrainer`` runs pipeline parallelism (GPipe or 1F1B over NCCL
+point-to-point), optionally with context parallelism inside every stage.
 
 The learning-rate schedule is the reference's (train.py:72-99): linear warmup
 to ``lr`` over ``warmup_steps``, then cosine decay to ``lr * min_lr_ratio``.
@@ -27,7 +29,7 @@ from gpt2_harness_b200.config import GPTConfig, TrainConfig
 from gpt2_harness_b200.models.engine import Engine, OptimConfig
 from gpt2_harness_b200.ops import native as N
 
-__all__ = ["Trainer", "lr_at_step"]
+__all__ = ["Trainer", "PipelineTrainer", "lr_at_step"]
 
 
 def lr_at_step(step: int, cfg: TrainConfig) -> float:
@@ -236,3 +238,112 @@ class Trainer:
             self.cp.close()
         if self.ddp is not None:
             self.ddp.close()
+
+
+class PipelineTrainer:
+    """Pipeline (x context) parallel GPT-2 training on native kernels.
+
+    The world is a ``pp x cp`` mesh (global rank = stage * cp + c): ``pp``
+    stages of ``n_layer / pp`` blocks each (stage 0 also the embeddings, the
+    last stage ln_f and an untied lm_head), and within every stage ``cp``
+    ranks splitting each sequence into contiguous slices (causal all-gather of
+    K/V over peer memory, weight gradients averaged over the slice group).
+    Every rank calls :meth:`step` with the same global batch ``[m * B, T]``
+    of token ids and targets; stage 0 reads the ids, the last stage the
+    targets, each of the micro-batches ``m`` rows ``[i*B, (i+1)*B)``.
+
+    Reference semantics: src/transformer_internals/parallel/pipeline_parallel.py
+    (stage split, GPipe / 1F1B, loss / m, untied head) composed with
+    sequence_parallel.py (all-gather-KV attention).
+    """
+
+    def __init__(self, config: GPTConfig, micro_batch: int, seq_len: int, micro_batches: int, *,
+                 pp: Optional[int] = None, cp: int = 1, schedule: str = "1f1b",
+                 train: Optional[TrainConfig] = None, device: Optional[torch.device] = None,
+                 seed: int = 0, comm_blocks: int = 128) -> None:
+        from gpt2_harness_b200.parallel.cp_native import NativeCP
+        from gpt2_harness_b200.parallel.pp_native import StageEngine, make_mesh
+
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        self.device = torch.device(device)
+        torch.cuda.set_device(self.device)
+        if not dist.is_initialized():
+            dist.init_process_group("nccl", store=dist.HashStore(), rank=0, world_size=1,
+                                    device_id=self.device)
+        world = dist.get_world_size()
+        pp = world // cp if pp is None else pp
+        if seq_len % cp:
+            raise ValueError(f"seq_len={seq_len} must split evenly over cp={cp}")
+        self.config, self.B, self.T, self.m = config, micro_batch, seq_len, micro_batches
+        self.train_cfg = train or TrainConfig()
+        self.schedule = train is not None
+        tc = self.train_cfg
+        optim = OptimConfig(lr=tc.lr, betas=tuple(tc.betas), eps=tc.eps,
+                            weight_decay=tc.weight_decay, grad_clip=tc.grad_clip)
+        self.mesh = mesh = make_mesh(pp, cp)
+        self.Tl = seq_len // cp
+        self.engine = StageEngine(config, micro_batch, self.Tl, micro_batches, schedule=schedule,
+                                  optim=optim, group=mesh.pp_group,
+                                  p2p_groups=(mesh.fwd_group, mesh.bwd_group), dp_group=mesh.cp_group,
+                                  device=self.device, seed=seed, comm_blocks=comm_blocks)
+        self.cp = None
+        if cp > 1:
+            lay = self.engine.lay
+            self.cp = NativeCP(config, micro_batch, seq_len, group=mesh.cp_group, device=self.device,
+                               nblocks=comm_blocks, layers=range(lay.l0, lay.l1),
+                               slots=len(self.engine.slots))
+            self.cp.attach(self.engine)
+        self.pos0 = mesh.cp_rank * self.Tl
+        lay = self.engine.lay
+        mB = micro_batches * micro_batch
+        self.idx = torch.zeros(mB, self.Tl, dtype=torch.int64, device=self.device) if lay.first else None
+        self.tgt = torch.zeros(mB, self.Tl, dtype=torch.int64, device=self.device) if lay.last else None
+        self.h2d_done = torch.cuda.Event()
+        self.step_num = 0
+
+    @property
+    def h2d_bytes_per_step(self) -> int:
+        """Bytes of inputs this rank copies to the device per step."""
+        return sum(t.numel() * 8 for t in (self.idx, self.tgt) if t is not None)
+
+    def _load(self, idx: torch.Tensor, targets: torch.Tensor):
+        mB = self.m * self.B
+        if idx.shape != (mB, self.T) or targets.shape != (mB, self.T):
+            raise ValueError(f"expected ({mB}, {self.T}) batches, got {tuple(idx.shape)}")
+        a, b = self.pos0, self.pos0 + self.Tl
+        for src, dst in ((idx, self.idx), (targets, self.tgt)):
+            if dst is None:
+                continue
+            src = src[:, a:b]
+            if src.device.type == "cpu" and not src.is_contiguous():
+                src = src.contiguous()
+            dst.copy_(src, non_blocking=True)
+        self.h2d_done.record()
+        B = self.B
+        split = lambda t: [t[i * B:(i + 1) * B] for i in range(self.m)] if t is not None else [None] * self.m
+        return split(self.idx), split(self.tgt)
+
+    def step_async(self, idx: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        """One optimiser step over the m micro-batches; returns the mean loss
+        as a device scalar (meaningful on the last stage)."""
+        if self.schedule:
+            self.engine.optim.lr = lr_at_step(self.step_num, self.train_cfg)
+        mi, mt = self._load(idx, targets)
+        loss = self.engine.train_step(mi, mt)
+        self.step_num += 1
+        return loss
+
+    def step(self, idx: torch.Tensor, targets: torch.Tensor) -> Optional[float]:
+        """One optimiser step; the last stage returns its mean loss as a
+        Python float, other stages ``None``."""
+        loss = self.step_async(idx, targets)
+        return float(loss.item()) if self.engine.lay.last else None
+
+    def check(self) -> None:
+        N.check_errors(self.device)
+
+    def close(self) -> None:
+        if self.cp is not None:
+            self.cp.close()
+        self.engine.close()

@@ -1,0 +1,129 @@
+"""Native pipeline parallelism (stage engine on the sm_100a kernels, NCCL
+point-to-point between stages, GPipe and 1F1B), alone and with context
+parallelism inside the stages, through the public PipelineTrainer, against
+the single-GPU engine accumulating the same micro-batches of full sequences:
+mean loss, every block gradient, and the embedding gradient (the untied
+lm_head's gradient plus stage 0's wte gradient equal the tied gradient).
+Child processes, one per GPU; cases are skipped when fewer GPUs are visible."""
+
+import json
+import os
+import socket
+import subprocess
+import sys
+import textwrap
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+WORKER = textwrap.dedent(r'''
+    import os, sys, json, datetime
+    import torch, torch.distributed as dist
+    sys.path.insert(0, os.environ["G2B_ROOT"])
+    from gpt2_harness_b200.config import gpt2_config
+    from gpt2_harness_b200.models.engine import Engine
+    from gpt2_harness_b200.trainer import PipelineTrainer
+    from gpt2_harness_b200.ops import native as N
+
+    rank = int(os.environ["RANK"]); world = int(os.environ["WORLD_SIZE"])
+    pp, cp = int(os.environ["G2B_PP"]), int(os.environ["G2B_CP"])
+    schedule = os.environ["G2B_SCHEDULE"]
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    cfg = gpt2_config("gpt2", n_layer=4, n_positions=1024)
+    B, T, m = 2, 1024, 4
+    tr = PipelineTrainer(cfg, B, T, m, pp=pp, cp=cp, schedule=schedule, seed=0)
+    st = tr.engine
+    ref = Engine(cfg, "cuda", seed=0)
+    g = torch.Generator().manual_seed(5)
+    idx = torch.randint(0, cfg.vocab_size, (m * B, T), generator=g).cuda()
+    tgt = torch.randint(0, cfg.vocab_size, (m * B, T), generator=g).cuda()
+    loss = tr.step_async(idx, tgt)
+    torch.cuda.synchronize()
+    N.check_errors()
+    ref_losses = []
+    for i in range(m):
+        sl = slice(i * B, (i + 1) * B)
+        ref_losses.append(float(ref.forward(idx[sl], tgt[sl]).item()))
+        ref.backward(idx[sl], accumulate=i > 0)
+    torch.cuda.synchronize()
+    errs = {}
+    for name in st.lay.specs:
+        if name in ("wte.weight", "lm_head.weight"):
+            continue
+        r = ref.g32(name) / m
+        errs[name] = ((st.g32(name) - r).norm() / (r.norm() + 1e-12)).item()
+    # tied embedding: stage 0's wte gradient + the last stage's lm_head gradient
+    V, C = cfg.vocab_size, cfg.n_embd
+    head = st.g32("lm_head.weight").clone() if st.lay.last else torch.empty(V, C, device="cuda")
+    dist.broadcast(head, src=world - 1)
+    if st.lay.first:
+        r = ref.g32("wte.weight") / m
+        errs["wte+lm_head"] = ((st.g32("wte.weight") + head - r).norm() / r.norm()).item()
+    worst = max(errs, key=errs.get)
+    # the global mean loss: the last stage's slices averaged over its CP ranks
+    mean_loss = (loss.detach().clone() if st.lay.last else torch.zeros((), device="cuda")).reshape(1)
+    dist.all_reduce(mean_loss)
+    mean_loss /= cp
+    losses = [float(loss.item())]
+    for _ in range(3):
+        losses.append(float(tr.step_async(idx, tgt).item()))
+    torch.cuda.synchronize()
+    N.check_errors()
+    out = {"rank": rank, "last": st.lay.last, "loss": losses, "mean_loss": float(mean_loss.item()),
+           "ref_loss": sum(ref_losses) / m, "worst": worst, "worst_err": errs[worst],
+           "slots": len(st.slots)}
+    print("RESULT " + json.dumps(out), flush=True)
+    tr.close()
+    dist.destroy_process_group()
+''')
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _run(world: int, pp: int, cp: int, schedule: str):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    port = _free_port()
+    procs = []
+    for r in range(world):
+        env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r),
+                   MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), G2B_ROOT=ROOT,
+                   G2B_SCHEDULE=schedule, G2B_PP=str(pp), G2B_CP=str(cp), NCCL_NVLS_ENABLE="0")
+        procs.append(subprocess.Popen([sys.executable, "-c", WORKER], env=env, stdout=subprocess.PIPE,
+                                      stderr=subprocess.STDOUT, text=True))
+    results = []
+    for p in procs:
+        try:
+            out, _ = p.communicate(timeout=240)
+        except subprocess.TimeoutExpired:
+            for q in procs:
+                q.kill()
+            outs = [q.communicate()[0] for q in procs]
+            raise AssertionError("PP workers timed out:\n" + "\n-----\n".join(o[-4000:] for o in outs))
+        assert p.returncode == 0, out[-3000:]
+        line = [l for l in out.splitlines() if l.startswith("RESULT ")]
+        assert line, out[-3000:]
+        results.append(json.loads(line[-1][7:]))
+    return results
+
+
+@pytest.mark.parametrize("pp,cp,schedule", [(1, 1, "1f1b"), (2, 1, "1f1b"), (2, 1, "gpipe"),
+                                           (1, 2, "1f1b"), (2, 2, "1f1b")])
+def test_native_pp_matches_single_gpu(pp, cp, schedule):
+    res = _run(pp * cp, pp, cp, schedule)
+    print(res)
+    for r in res:
+        assert r["worst_err"] < 2e-2, r
+        assert abs(r["mean_loss"] - r["ref_loss"]) < 1e-3 * r["ref_loss"], r
+        if r["last"]:
+            assert r["loss"][-1] < r["loss"][0], r
