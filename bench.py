@@ -231,7 +231,8 @@ def run_pipeline(args, world, rank):
     cp = args.cp
     pp = args.pp or world // cp
     trainer = PipelineTrainer(cfg, args.batch, args.seq, args.micro_batches, pp=pp, cp=cp,
-                              schedule=args.schedule, train=tc, comm_blocks=args.comm_blocks)
+                              schedule=args.schedule, train=tc, comm_blocks=args.comm_blocks,
+                              cp_balance=args.cp_balance)
     trainer.schedule = False
     host, dev = make_data(cfg, args.micro_batches * args.batch, args.seq, 0, pool=2)
     L = N.lib()
@@ -269,6 +270,7 @@ def run_pipeline(args, world, rank):
     out["config"]["comm"] = "nccl p2p between stages, peer-memory kernels inside a CP group"
     out["config"]["pp"], out["config"]["cp"] = pp, cp
     out["config"]["micro_batches"], out["config"]["schedule"] = args.micro_batches, args.schedule
+    out["config"]["cp_balance"] = args.cp_balance if cp > 1 else None
     trainer.close()
     return out
 
@@ -286,7 +288,7 @@ def run_native(args, world, rank):
     tc = TrainConfig(lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, grad_clip=1.0, warmup_steps=0)
     trainer = Trainer(cfg, args.batch, args.seq, train=tc, comm=args.comm, schedule=False,
                       strategy=args.strategy, bucket_bytes=int(args.bucket_mb * 2**20),
-                      comm_blocks=args.comm_blocks)
+                      comm_blocks=args.comm_blocks, cp_balance=args.cp_balance)
     # tensor and context parallel ranks all take the same global batch
     host, dev = make_data(cfg, args.batch, args.seq, 0 if args.strategy in ("tp", "cp") else rank)
     L = N.lib()
@@ -323,6 +325,8 @@ def run_native(args, world, rank):
     out = finish_line(args, world, cfg, ms, ms_e2e, bi, bo, sampler, impl="native")
     out["gpu_launches"] = int(n_launch)
     out["config"]["comm"] = (args.comm if args.strategy == "ddp" else "p2p") if world > 1 else "none"
+    if args.strategy == "cp":
+        out["config"]["cp_balance"] = args.cp_balance
     if args.strategy == "zero3":
         out["config"]["activations"] = "kept (no recompute): MFU counts the model FLOPs run"
     trainer.close()
@@ -498,6 +502,8 @@ def main():
     ap.add_argument("--cp", type=int, default=1, help="context-parallel ranks per stage (pp strategy)")
     ap.add_argument("--micro-batches", type=int, default=8, help="micro-batches per step (pp strategy)")
     ap.add_argument("--schedule", choices=["1f1b", "gpipe"], default="1f1b")
+    ap.add_argument("--cp-balance", choices=["zigzag", "contiguous"], default="zigzag",
+                    help="context-parallel split (cp and pp strategies)")
     ap.add_argument("--bucket-mb", type=float, default=25.0, help="gradient bucket size (MiB)")
     ap.add_argument("--comm-blocks", type=int, default=128, help="CTAs per fused all-reduce")
     args = ap.parse_args()

@@ -173,16 +173,16 @@ PYBIND11_MODULE(_C, m) {
   });
 
   m.def("embedding_fwd", [](int64_t idx, int64_t wte, int64_t wpe, int64_t x, int B, int T, int C,
-                            int pos0, int64_t stream) {
+                            int pos0, int split, int pos1, int64_t stream) {
     check(embedding_fwd_launch(P<int64_t>(idx), P<void>(wte), P<void>(wpe), P<float>(x), B, T, C,
-                               pos0, S(stream)),
+                               pos0, split, pos1, S(stream)),
           "embedding_fwd");
   });
 
   m.def("embedding_bwd", [](int64_t idx, int64_t dx, int64_t wte_grad, int64_t wpe_grad, int B,
-                            int T, int C, int V, int pos0, int64_t stream) {
+                            int T, int C, int V, int pos0, int split, int pos1, int64_t stream) {
     check(embedding_bwd_launch(P<int64_t>(idx), P<float>(dx), P<float>(wte_grad),
-                               P<float>(wpe_grad), B, T, C, V, pos0, S(stream)),
+                               P<float>(wpe_grad), B, T, C, V, pos0, split, pos1, S(stream)),
           "embedding_bwd");
   });
 
@@ -345,6 +345,8 @@ PYBIND11_MODULE(_C, m) {
     t.src_ld = I("src_ld");
     t.B = (int)I("B");
     t.Tl = (int)I("Tl");
+    t.zigzag = (int)I("zigzag");
+    t.peer_bufs2 = P<void*>(I("peer_bufs2"));
     return t;
   };
   m.def("cp_kv_gather", [tp_args](const py::dict& d, int64_t st) {

@@ -360,9 +360,16 @@ __global__ void __launch_bounds__(256) colsum_bf16_partial_kernel(
 }
 
 // --------------------------------------------------------------- embedding ---
+// Position of column t of a sequence: pos0 + t below `split`, pos1 + (t -
+// split) from it on (a sequence assembled from two separate chunks of the
+// full context, as in load-balanced context parallelism).
+__device__ __forceinline__ int emb_pos(int t, int pos0, int split, int pos1) {
+  return t < split ? pos0 + t : pos1 + (t - split);
+}
+
 __global__ void emb_fwd_kernel(const int64_t* __restrict__ idx, const __nv_bfloat16* __restrict__ wte,
                                const __nv_bfloat16* __restrict__ wpe, float* __restrict__ x, int B,
-                               int T, int C, int pos0) {
+                               int T, int C, int pos0, int split, int pos1) {
   const int64_t total = (int64_t)B * T * (C / 4);
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -371,7 +378,8 @@ __global__ void emb_fwd_kernel(const int64_t* __restrict__ idx, const __nv_bfloa
     const int t = (int)(m % T);
     const int64_t tok = idx[m];
     const uint2 a = *reinterpret_cast<const uint2*>(wte + tok * C + c);
-    const uint2 p = *reinterpret_cast<const uint2*>(wpe + (int64_t)(pos0 + t) * C + c);
+    const uint2 p =
+        *reinterpret_cast<const uint2*>(wpe + (int64_t)emb_pos(t, pos0, split, pos1) * C + c);
     const float2 a01 = unpack_bf16x2(a.x), a23 = unpack_bf16x2(a.y);
     const float2 p01 = unpack_bf16x2(p.x), p23 = unpack_bf16x2(p.y);
     reinterpret_cast<float4*>(x)[i] =
@@ -392,14 +400,14 @@ __global__ void emb_bwd_wte_kernel(const int64_t* __restrict__ idx, const float*
 }
 
 __global__ void emb_bwd_wpe_kernel(const float* __restrict__ dx, float* __restrict__ wpe_grad,
-                                   int B, int T, int C, int pos0) {
+                                   int B, int T, int C, int pos0, int split, int pos1) {
   const int64_t total = (int64_t)T * C;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int t = (int)(i / C), c = (int)(i % C);
     float s = 0.f;
     for (int b = 0; b < B; ++b) s += dx[((int64_t)b * T + t) * C + c];
-    wpe_grad[(int64_t)(pos0 + t) * C + c] += s;
+    wpe_grad[(int64_t)emb_pos(t, pos0, split, pos1) * C + c] += s;
   }
 }
 
@@ -739,23 +747,27 @@ int colsum_bf16_launch(const void* in, int64_t ld, int M, int C, float* ws, floa
 }
 
 int embedding_fwd_launch(const int64_t* idx, const void* wte, const void* wpe, float* x, int B,
-                         int T, int C, int pos0, cudaStream_t s) {
-  if (C % 4) return -1;
+                         int T, int C, int pos0, int split, int pos1, cudaStream_t s) {
+  if (C % 4 || split < 0 || split > T || pos0 < 0 || pos1 < 0) return -1;
   emb_fwd_kernel<<<grid_for((int64_t)B * T * C / 4, 256), 256, 0, s>>>(
-      idx, (const __nv_bfloat16*)wte, (const __nv_bfloat16*)wpe, x, B, T, C, pos0);
-      count_launches(1);
+      idx, (const __nv_bfloat16*)wte, (const __nv_bfloat16*)wpe, x, B, T, C, pos0, split, pos1);
+  count_launches(1);
   return ok();
 }
 
 int embedding_bwd_launch(const int64_t* idx, const float* dx, float* wte_grad, float* wpe_grad,
-                         int B, int T, int C, int V, int pos0, cudaStream_t s) {
+                         int B, int T, int C, int V, int pos0, int split, int pos1, cudaStream_t s) {
+  if (split < 0 || split > T || pos0 < 0 || pos1 < 0) return -1;
   const int64_t M = (int64_t)B * T;
-  if (wte_grad)
+  if (wte_grad) {
     emb_bwd_wte_kernel<<<grid_for(M * C, 256), 256, 0, s>>>(idx, dx, wte_grad, M, C, V);
     count_launches(1);
-  if (wpe_grad)
-    emb_bwd_wpe_kernel<<<grid_for((int64_t)T * C, 256), 256, 0, s>>>(dx, wpe_grad, B, T, C, pos0);
+  }
+  if (wpe_grad) {
+    emb_bwd_wpe_kernel<<<grid_for((int64_t)T * C, 256), 256, 0, s>>>(dx, wpe_grad, B, T, C, pos0,
+                                                                     split, pos1);
     count_launches(1);
+  }
   return ok();
 }
 

@@ -33,14 +33,16 @@ int colsum_f32_launch(const float* in, int R, int C, float* out, int accumulate,
 int colsum_bf16_launch(const void* in, int64_t ld, int M, int C, float* ws, float* out,
                        int accumulate, cudaStream_t s);
 
-// x[b*T+t, :] = wte[idx[b,t]] + wpe[pos0 + t]   (bf16 tables, fp32 out).
+// x[b*T+t, :] = wte[idx[b,t]] + wpe[pos(t)]   (bf16 tables, fp32 out), with
+// pos(t) = pos0 + t for t < split and pos1 + (t - split) from there on
+// (split = T: one contiguous range).
 int embedding_fwd_launch(const int64_t* idx, const void* wte, const void* wpe, float* x, int B,
-                         int T, int C, int pos0, cudaStream_t s);
+                         int T, int C, int pos0, int split, int pos1, cudaStream_t s);
 
 // Embedding backward: wte_grad[idx[m]] += dx[m] (fp32 atomics), and
-// wpe_grad[pos0+t] (+)= sum_b dx[b*T+t] (deterministic).
+// wpe_grad[pos(t)] (+)= sum_b dx[b*T+t] (deterministic; pos as above).
 int embedding_bwd_launch(const int64_t* idx, const float* dx, float* wte_grad, float* wpe_grad,
-                         int B, int T, int C, int V, int pos0, cudaStream_t s);
+                         int B, int T, int C, int V, int pos0, int split, int pos1, cudaStream_t s);
 
 // Cross-entropy over bf16 logits [M, V] (row stride ld) against int64 targets
 // (ignore_index -100). Writes loss_rows[M] (0 for ignored rows) and overwrites

@@ -332,6 +332,109 @@ __device__ __forceinline__ int64_t cp_row(const TpArgs& a, int q, int64_t i) {
   return b * (int64_t)a.world * a.Tl + (int64_t)q * a.Tl + t;
 }
 
+// Zig-zag split: chunk k (of 2*world, Tl/2 tokens each) belongs to rank
+// k (k < world) or 2*world-1-k; a rank stores its two chunks as the halves of
+// each local sequence. zz_row: natural buffer row of row (b, t) of chunk k.
+__device__ __forceinline__ int64_t zz_row(const TpArgs& a, int k, int64_t b, int64_t t) {
+  const int h = a.Tl / 2;
+  return b * (int64_t)a.world * a.Tl + (int64_t)k * h + t;
+}
+// Chunk of local row i (sequence b = i / Tl; first half -> chunk rank,
+// second half -> chunk 2*world-1-rank).
+__device__ __forceinline__ int zz_local_chunk(const TpArgs& a, int64_t i, int64_t* b, int64_t* t) {
+  const int h = a.Tl / 2;
+  const int64_t j = i % a.Tl;
+  *b = i / a.Tl;
+  *t = j % h;
+  return j < h ? a.rank : 2 * a.world - 1 - a.rank;
+}
+
+__global__ void __launch_bounds__(512) cp_kv_gather_zz_kernel(const TpArgs a) {
+  __shared__ int fail;
+  if (threadIdx.x == 0) fail = 0;
+  __syncthreads();
+  const int C = a.cols / 2;
+  const int vpr = a.cols / 8;
+  const int h = a.Tl / 2;
+  const int64_t nvec = (int64_t)a.B * a.Tl * vpr;   // own vectors (both chunks)
+  __nv_bfloat16* mine = reinterpret_cast<__nv_bfloat16*>(a.peer_bufs[a.rank]);
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = v / vpr;
+    const int c = (int)(v % vpr) * 8;
+    int64_t b, t;
+    const int k = zz_local_chunk(a, i, &b, &t);
+    const uint4 w = *reinterpret_cast<const uint4*>(a.src + i * a.src_ld + C + c);
+    *reinterpret_cast<uint4*>(mine + zz_row(a, k, b, t) * a.cols + c) = w;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (!tp_handshake(a, 0, &fail)) return;
+  // chunks 0..2w-1-r except the own ones (r and 2w-1-r): e -> e (e < r) or e + 1
+  const int nk = 2 * a.world - 2 - a.rank;
+  const int64_t cvec = (int64_t)a.B * h * vpr;      // vectors per chunk
+  const int64_t total = cvec * nk;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < total;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    const int e = (int)(v / cvec);
+    const int k = e < a.rank ? e : e + 1;
+    const int q = k < a.world ? k : 2 * a.world - 1 - k;
+    const int64_t vv = v % cvec;
+    const int64_t row = vv / vpr;                   // b * h + t
+    const int c = (int)(vv % vpr) * 8;
+    const int64_t off = zz_row(a, k, row / h, row % h) * a.cols + c;
+    *reinterpret_cast<uint4*>(mine + off) =
+        __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.peer_bufs[q]) + off));
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
+    atomicAdd(a.byte_counter, (unsigned long long)(cvec * 16 * (nk + 2)));
+  finish(a, &fail);
+}
+
+__global__ void __launch_bounds__(512) cp_kv_reduce_zz_kernel(const TpArgs a) {
+  __shared__ int fail;
+  if (threadIdx.x == 0) fail = 0;
+  __syncthreads();
+  if (!tp_handshake(a, 0, &fail)) return;
+  const int C = a.cols / 2;
+  const int vpr = a.cols / 8;
+  const int64_t nvec = (int64_t)a.B * a.Tl * vpr;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = v / vpr;
+    const int c = (int)(v % vpr) * 8;
+    int64_t b, t;
+    const int k = zz_local_chunk(a, i, &b, &t);
+    const int64_t off = zz_row(a, k, b, t) * a.cols + c;
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    for (int q = 0; q < a.world; ++q) {
+      for (int part = 0; part < 2; ++part) {
+        // first-half queries of rank q see chunks 0..q, second-half 0..2w-1-q
+        const int last = part == 0 ? q : 2 * a.world - 1 - q;
+        if (k > last) continue;
+        const void* src = part == 0 ? a.peer_bufs[q] : a.peer_bufs2[q];
+        const uint4 w = __ldcg(reinterpret_cast<const uint4*>(
+            reinterpret_cast<const __nv_bfloat16*>(src) + off));
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack_bf16x2(ws[j]);
+          acc[2 * j] += f.x;
+          acc[2 * j + 1] += f.y;
+        }
+      }
+    }
+    *reinterpret_cast<uint4*>(a.out_bf16 + i * a.src_ld + C + c) =
+        make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                   pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
+    atomicAdd(a.byte_counter, (unsigned long long)(nvec * 16 * 2 * a.world));
+  finish(a, &fail);
+}
+
 __global__ void __launch_bounds__(512) cp_kv_gather_kernel(const TpArgs a) {
   __shared__ int fail;
   if (threadIdx.x == 0) fail = 0;
@@ -464,6 +567,12 @@ int tp_ce_stats_launch(TpArgs a, cudaStream_t s) {
 
 int cp_kv_gather_launch(TpArgs a, cudaStream_t s) {
   if (!common_ok(a) || a.cols % 16 || a.src_ld % 8 || a.B <= 0 || a.Tl <= 0 || !a.src) return -1;
+  if (a.zigzag) {
+    if (a.Tl % 2) return -1;
+    cp_kv_gather_zz_kernel<<<a.nblocks, 512, 0, s>>>(a);
+    count_launches(1);
+    return launch_succeeded() ? 0 : -11;
+  }
   cp_kv_gather_kernel<<<a.nblocks, 512, 0, s>>>(a);
   count_launches(1);
   return launch_succeeded() ? 0 : -11;
@@ -472,6 +581,12 @@ int cp_kv_gather_launch(TpArgs a, cudaStream_t s) {
 int cp_kv_reduce_launch(TpArgs a, cudaStream_t s) {
   if (!common_ok(a) || a.cols % 16 || a.src_ld % 8 || a.B <= 0 || a.Tl <= 0 || !a.out_bf16)
     return -1;
+  if (a.zigzag) {
+    if (a.Tl % 2 || !a.peer_bufs2) return -1;
+    cp_kv_reduce_zz_kernel<<<a.nblocks, 512, 0, s>>>(a);
+    count_launches(1);
+    return launch_succeeded() ? 0 : -11;
+  }
   cp_kv_reduce_kernel<<<a.nblocks, 512, 0, s>>>(a);
   count_launches(1);
   return launch_succeeded() ? 0 : -11;

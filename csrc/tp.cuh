@@ -49,6 +49,13 @@ struct TpArgs {
   const __nv_bfloat16* src = nullptr;
   int64_t src_ld = 0;
   int B = 0, Tl = 0;
+  // Load-balanced (zig-zag) split: the sequence is 2*world chunks of Tl/2
+  // tokens and rank r owns chunks r and 2*world-1-r, stored as the two
+  // halves of each local sequence; the key/value buffers keep the natural
+  // order. The reduce then reads two partial buffers per rank: peer_bufs
+  // (queries of the first half) and peer_bufs2 (queries of the second half).
+  int zigzag = 0;
+  void** peer_bufs2 = nullptr;
 };
 
 int tp_ag_rows_launch(TpArgs a, cudaStream_t s);
@@ -61,10 +68,14 @@ int tp_ce_finish_launch(TpArgs a, cudaStream_t s);
 // Context parallelism, all-gather-KV form: copy this rank's k/v rows into its
 // own block of the symmetric key/value buffer, then pull the blocks of every
 // earlier rank (the only keys a causal query of this rank can see). `cols` = 2C.
+// Zig-zag: own chunks to their natural rows, then every other chunk up to
+// 2*world-1-rank from its owner.
 int cp_kv_gather_launch(TpArgs a, cudaStream_t s);
 // Reduce-scatter of the key/value gradients: this rank's block summed over
 // ranks rank..world-1 (the ranks whose queries saw these keys), in rank
 // order, into columns [C, 3C) of the local dqkv rows (out_bf16, ld).
+// Zig-zag: each own chunk k summed over ranks q (ascending) of the first-half
+// partials where k <= q and the second-half partials where k <= 2*world-1-q.
 int cp_kv_reduce_launch(TpArgs a, cudaStream_t s);
 
 }  // namespace g2b

@@ -291,6 +291,11 @@ class Engine:
         # attn_fwd_hook(l, qkv, y, lse, B, H, T) / attn_bwd_hook(l, qkv, y, dy,
         # dqkv, lse, delta, B, H, T) when set.
         self.pos0 = 0
+        # a local sequence made of two chunks of the full context (load-
+        # balanced context parallelism): columns from pos_split on sit at
+        # pos1 + (t - pos_split)
+        self.pos_split: Optional[int] = None
+        self.pos1 = 0
         self.attn_fwd_hook: Optional[Callable] = None
         self.attn_bwd_hook: Optional[Callable] = None
         # LayerNorm backward also produces the c_proj bias gradients of the
@@ -411,13 +416,16 @@ class Engine:
         cfg = self.config
         idx = idx.contiguous()
         B, T = idx.shape
-        if self.pos0 + T > cfg.n_positions:
-            raise ValueError(f"positions up to {self.pos0 + T} exceed n_positions={cfg.n_positions}")
+        top = self.pos0 + T if self.pos_split is None else max(self.pos0 + self.pos_split,
+                                                               self.pos1 + T - self.pos_split)
+        if top > cfg.n_positions:
+            raise ValueError(f"positions up to {top} exceed n_positions={cfg.n_positions}")
         A = self.acts(B, T)
         C, H, L, V = cfg.n_embd, cfg.n_head, cfg.n_layer, cfg.vocab_size
         eps = cfg.layer_norm_epsilon
         p = self.p16
-        N.embedding_fwd(idx, p("wte.weight"), p("wpe.weight"), A.x[0], pos0=self.pos0)
+        N.embedding_fwd(idx, p("wte.weight"), p("wpe.weight"), A.x[0], pos0=self.pos0,
+                        pos_split=self.pos_split, pos1=self.pos1)
         bh = self.block_hook
         for l in range(L):
             pre = f"h.{l}."
@@ -522,7 +530,8 @@ class Engine:
         wpe_g = g("wpe.weight")
         if not acc:
             wpe_g.zero_()
-        N.embedding_bwd(idx, A.dres, g("wte.weight"), wpe_g, V, pos0=self.pos0)
+        N.embedding_bwd(idx, A.dres, g("wte.weight"), wpe_g, V, pos0=self.pos0,
+                        pos_split=self.pos_split, pos1=self.pos1)
         if hook:
             hook("root_tail")
 

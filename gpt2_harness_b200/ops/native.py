@@ -203,7 +203,7 @@ def _head_strides(t: torch.Tensor, T: int, H: int):
 def attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor,
                   lse: torch.Tensor, B: int, H: int, Tq: int, Tk: Optional[int] = None,
                   q_offset: int = 0, causal: bool = True, scale: Optional[float] = None,
-                  kv_rows: Optional[int] = None) -> None:
+                  kv_rows: Optional[int] = None, q_rows: Optional[int] = None) -> None:
     """Causal flash attention on head_dim 64.
 
     q, o: [B*Tq, ...] row-major views whose columns h*64..h*64+63 hold head h
@@ -212,14 +212,18 @@ def attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Te
     kv_rows: rows per sequence in the k/v buffers when they hold more than the
     Tk keys attended (context parallelism: a full-length key buffer of which
     a prefix is visible); defaults to Tk.
+    q_rows: rows per sequence in the q/o buffers when each sequence's Tq
+    queries are a slice of a longer row range (load-balanced context
+    parallelism: two chunks per sequence); defaults to Tq.
     """
     Tk = Tq if Tk is None else Tk
+    qr = Tq if q_rows is None else q_rows
     scale = 1.0 / math.sqrt(64) if scale is None else scale
-    qsb, qst, qsh = _head_strides(q, Tq, H)
+    qsb, qst, qsh = _head_strides(q, qr, H)
     ksb, kst, ksh = _head_strides(k, Tk if kv_rows is None else kv_rows, H)
     if _head_strides(v, Tk if kv_rows is None else kv_rows, H) != (ksb, kst, ksh):
         raise ValueError("k and v must share strides")
-    osb, ost, osh = _head_strides(o, Tq, H)
+    osb, ost, osh = _head_strides(o, qr, H)
     lib().attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), qsb, qst, qsh,
                    osb, ost, osh, lse.data_ptr(), B, H, Tq, Tk, q_offset, int(causal),
                    float(scale), ksb, kst, ksh, _err_ptr(), _stream())
@@ -227,21 +231,23 @@ def attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Te
 
 def attention_bwd(q, k, v, o, dout, dq, dk, dv, lse, delta, B: int, H: int, Tq: int,
                   Tk: Optional[int] = None, q_offset: int = 0, causal: bool = True,
-                  scale: Optional[float] = None, kv_rows: Optional[int] = None) -> None:
+                  scale: Optional[float] = None, kv_rows: Optional[int] = None,
+                  q_rows: Optional[int] = None) -> None:
     """Deterministic flash-attention backward (dK/dV pass, then dQ pass).
 
     dout shares o's strides; dq shares q's layout family; dk/dv share a layout.
-    delta: fp32 scratch [B, H, Tq].
+    delta: fp32 scratch [B, H, Tq]. kv_rows / q_rows as in :func:`attention_fwd`.
     """
     Tk = Tq if Tk is None else Tk
     kr = Tk if kv_rows is None else kv_rows
+    qr = Tq if q_rows is None else q_rows
     scale = 1.0 / math.sqrt(64) if scale is None else scale
-    qsb, qst, qsh = _head_strides(q, Tq, H)
+    qsb, qst, qsh = _head_strides(q, qr, H)
     ksb, kst, ksh = _head_strides(k, kr, H)
-    osb, ost, osh = _head_strides(o, Tq, H)
-    if _head_strides(dout, Tq, H) != (osb, ost, osh):
+    osb, ost, osh = _head_strides(o, qr, H)
+    if _head_strides(dout, qr, H) != (osb, ost, osh):
         raise ValueError("dout must share o's strides")
-    dsb, dst, dsh = _head_strides(dq, Tq, H)
+    dsb, dst, dsh = _head_strides(dq, qr, H)
     dksb, dkst, dksh = _head_strides(dk, kr, H)
     if _head_strides(dv, kr, H) != (dksb, dkst, dksh):
         raise ValueError("dk and dv must share strides")
@@ -303,20 +309,25 @@ def colsum_ws_numel(M: int, C: int) -> int:
 
 # ----------------------------------------------------------------- embedding --
 def embedding_fwd(idx: torch.Tensor, wte: torch.Tensor, wpe: torch.Tensor, x: torch.Tensor,
-                  pos0: int = 0) -> torch.Tensor:
+                  pos0: int = 0, pos_split: Optional[int] = None, pos1: int = 0) -> torch.Tensor:
+    """x = wte[idx] + wpe[pos]; column t of every sequence sits at position
+    pos0 + t, or pos1 + (t - pos_split) from ``pos_split`` on."""
     B, T = idx.shape
     C = wte.shape[1]
+    split = T if pos_split is None else int(pos_split)
     lib().embedding_fwd(idx.data_ptr(), wte.data_ptr(), wpe.data_ptr(), x.data_ptr(), B, T, C,
-                        pos0, _stream())
+                        pos0, split, pos1, _stream())
     return x
 
 
 def embedding_bwd(idx: torch.Tensor, dx: torch.Tensor, wte_grad: Optional[torch.Tensor],
-                  wpe_grad: Optional[torch.Tensor], vocab: int, pos0: int = 0) -> None:
+                  wpe_grad: Optional[torch.Tensor], vocab: int, pos0: int = 0,
+                  pos_split: Optional[int] = None, pos1: int = 0) -> None:
     B, T = idx.shape
     C = dx.shape[-1]
+    split = T if pos_split is None else int(pos_split)
     lib().embedding_bwd(idx.data_ptr(), dx.data_ptr(), _ptr(wte_grad), _ptr(wpe_grad), B, T, C,
-                        vocab, pos0, _stream())
+                        vocab, pos0, split, pos1, _stream())
 
 
 # --------------------------------------------------------------- cross-entropy --

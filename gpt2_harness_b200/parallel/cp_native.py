@@ -26,6 +26,18 @@ B200 design:
   all-reduce overlapped with backward, mean over ranks) -- with equal token
   counts per rank the mean of the per-rank mean losses is the global mean.
 
+Load balancing (``balance="zigzag"``, the default): under the contiguous
+split rank p-1 attends to p times the keys of rank 0 (causal work grows with
+the position), so the step waits for the last rank. The zig-zag split cuts
+every sequence into 2p chunks of T/(2p) tokens and gives rank r chunks r and
+2p-1-r, stored as the two halves of its local sequence (positions read from
+two offsets by the embedding). Every rank then attends over the same area:
+half 1 (queries of chunk r) over keys [0, (r+1)T/2p), half 2 (chunk 2p-1-r)
+over [0, (2p-r)T/2p) -- two attention calls on strided half views. The K/V
+buffer keeps the natural order; the gather pulls every chunk up to 2p-1-r
+from its owner, and the reduce sums each own chunk over the two halves'
+dK/dV partials of every rank that saw it.
+
 Payload per rank per layer in the reference convention: the gather is charged
 its output (2 x B x T x C x 2 bytes: K and V, bf16), the reduce-scatter its
 input (the same), as for ``_GatherSequence``.
@@ -62,7 +74,7 @@ class NativeCP:
 
     def __init__(self, config: GPTConfig, B: int, T: int, group=None,
                  device: Optional[torch.device] = None, nblocks: int = 128,
-                 layers: Optional[list] = None, slots: int = 1) -> None:
+                 layers: Optional[list] = None, slots: int = 1, balance: str = "zigzag") -> None:
         if not dist.is_initialized():
             raise RuntimeError("NativeCP needs an initialised process group")
         self.group = group
@@ -76,7 +88,20 @@ class NativeCP:
         self.config = config
         self.B, self.T = B, T
         self.Tl = T // self.world
-        self.pos0 = self.rank * self.Tl
+        if balance not in ("zigzag", "contiguous"):
+            raise ValueError(f"unknown balance {balance!r}")
+        self.zigzag = balance == "zigzag"
+        self.balance = balance
+        if self.zigzag:
+            h = self.Tl // 2
+            if self.Tl % 2 or h % 128:
+                raise ValueError(f"zig-zag needs T / (2p) a multiple of 128, got {self.Tl / 2}")
+            self.h = h
+            # local sequence = [chunk r ; chunk 2p-1-r]
+            self.chunks = (self.rank, 2 * self.world - 1 - self.rank)
+            self.pos0, self.pos_split, self.pos1 = self.rank * h, h, self.chunks[1] * h
+        else:
+            self.pos0, self.pos_split, self.pos1 = self.rank * self.Tl, None, 0
         C, L = config.n_embd, config.n_layer
         self.C = C
         self.nblocks = nblocks
@@ -89,10 +114,13 @@ class NativeCP:
         self.slot = 0
         self._kv = SymmetricBuffer(nl * rows * 2 * C * 2, group, dev)     # per-layer gathered k/v
         self._dkv = SymmetricBuffer(rows * 2 * C * 2, group, dev)         # dk/dv partials (reused)
+        # zig-zag: the second half's queries write their own partials
+        self._dkv2 = SymmetricBuffer(rows * 2 * C * 2, group, dev) if self.zigzag else None
         self._flags = SymmetricBuffer(N.lib().tp_flag_words() * 4, group, dev)
         kv = self._kv.view(bf, nl * rows * 2 * C).view(nl, rows, 2 * C)
         self.kv = [kv[i] for i in range(nl)]
         self.dkv = self._dkv.view(bf, rows * 2 * C).view(rows, 2 * C)
+        self.dkv2 = self._dkv2.view(bf, rows * 2 * C).view(rows, 2 * C) if self.zigzag else None
         self._kv_ptrs = [torch.tensor([p + i * rows * 2 * C * 2 for p in self._kv.peer_ptrs],
                                       dtype=torch.int64, device=dev) for i in range(nl)]
         self.byte_counter = torch.zeros(1, dtype=torch.int64, device=dev)
@@ -100,7 +128,7 @@ class NativeCP:
 
     def attach(self, engine) -> None:
         """Route the engine's (or a pipeline stage engine's) attention here."""
-        engine.pos0 = self.pos0
+        engine.pos0, engine.pos_split, engine.pos1 = self.pos0, self.pos_split, self.pos1
         engine.attn_fwd_hook = self.attention_fwd
         engine.attn_bwd_hook = self.attention_bwd
         if hasattr(engine, "slot_hook"):
@@ -110,6 +138,20 @@ class NativeCP:
         if not 0 <= slot < self.slots:
             raise ValueError(f"slot {slot} out of range ({self.slots} kept)")
         self.slot = slot
+
+    def local_tokens(self, t: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Copy this rank's tokens of the full [B, T] batch ``t`` into ``out``
+        ([B, T/p], any device): its slice, or under zig-zag its two chunks."""
+        if not self.zigzag:
+            a = self.rank * self.Tl
+            src = t[:, a:a + self.Tl]
+            if src.device.type == "cpu" and not src.is_contiguous():
+                src = src.contiguous()
+            return out.copy_(src, non_blocking=True)
+        h = self.h
+        for half, k in enumerate(self.chunks):
+            out[:, half * h:(half + 1) * h].copy_(t[:, k * h:(k + 1) * h], non_blocking=True)
+        return out
 
     def _kv_index(self, l: int) -> int:
         return self.slot * len(self.layer_index) + self.layer_index[l]
@@ -130,24 +172,45 @@ class NativeCP:
         kv = self.kv[i]
         nbytes = B * T * 2 * C * 2
         comms.record_external("all_gather", B * T * 2 * C, nbytes)
-        d = self._args(self._kv_ptrs[i].data_ptr(), src=qkv.data_ptr(), src_ld=qkv.stride(0))
+        d = self._args(self._kv_ptrs[i].data_ptr(), src=qkv.data_ptr(), src_ld=qkv.stride(0),
+                       zigzag=int(self.zigzag))
         N.lib().cp_kv_gather(d, torch.cuda.current_stream(self.device).cuda_stream)
-        Tk = (self.rank + 1) * self.Tl
-        N.attention_fwd(qkv[:, :C], kv[:, :C], kv[:, C:], y, lse, B, H, Tl, Tk=Tk,
-                        q_offset=self.pos0, kv_rows=T)
+        if not self.zigzag:
+            Tk = (self.rank + 1) * self.Tl
+            N.attention_fwd(qkv[:, :C], kv[:, :C], kv[:, C:], y, lse, B, H, Tl, Tk=Tk,
+                            q_offset=self.pos0, kv_rows=T)
+            return
+        h = self.h
+        lse2 = lse.view(-1)[: 2 * B * H * h].view(2, B, H, h)
+        for half, k in enumerate(self.chunks):
+            N.attention_fwd(qkv[half * h:, :C], kv[:, :C], kv[:, C:], y[half * h:], lse2[half],
+                            B, H, h, Tk=(k + 1) * h, q_offset=k * h, kv_rows=T, q_rows=Tl)
 
     def attention_bwd(self, l: int, qkv, y, dy, dqkv, lse, delta, B: int, H: int, Tl: int) -> None:
         C, T = self.C, self.T
         kv, dkv = self.kv[self._kv_index(l)], self.dkv
-        Tk = (self.rank + 1) * self.Tl
-        N.attention_bwd(qkv[:, :C], kv[:, :C], kv[:, C:], y, dy, dqkv[:, :C], dkv[:, :C], dkv[:, C:],
-                        lse, delta, B, H, Tl, Tk=Tk, q_offset=self.pos0, kv_rows=T)
+        if not self.zigzag:
+            Tk = (self.rank + 1) * self.Tl
+            N.attention_bwd(qkv[:, :C], kv[:, :C], kv[:, C:], y, dy, dqkv[:, :C], dkv[:, :C],
+                            dkv[:, C:], lse, delta, B, H, Tl, Tk=Tk, q_offset=self.pos0, kv_rows=T)
+            extra = {}
+        else:
+            h = self.h
+            lse2 = lse.view(-1)[: 2 * B * H * h].view(2, B, H, h)
+            delta2 = delta.view(-1)[: 2 * B * H * h].view(2, B, H, h)
+            for half, (k, part) in enumerate(zip(self.chunks, (self.dkv, self.dkv2))):
+                N.attention_bwd(qkv[half * h:, :C], kv[:, :C], kv[:, C:], y[half * h:], dy[half * h:],
+                                dqkv[half * h:, :C], part[:, :C], part[:, C:], lse2[half], delta2[half],
+                                B, H, h, Tk=(k + 1) * h, q_offset=k * h, kv_rows=T, q_rows=Tl)
+            extra = {"zigzag": 1, "peer_bufs2": self._dkv2.peer_ptrs_dev.data_ptr()}
         nbytes = B * T * 2 * C * 2
         comms.record_external("reduce_scatter", B * T * 2 * C, nbytes)
-        d = self._args(self._dkv.peer_ptrs_dev.data_ptr(), out_bf16=dqkv.data_ptr(), src_ld=dqkv.stride(0))
+        d = self._args(self._dkv.peer_ptrs_dev.data_ptr(), out_bf16=dqkv.data_ptr(), src_ld=dqkv.stride(0),
+                       **extra)
         N.lib().cp_kv_reduce(d, torch.cuda.current_stream(self.device).cuda_stream)
 
     def close(self) -> None:
         torch.cuda.synchronize(self.device)
-        for b in (self._kv, self._dkv, self._flags):
-            b.close()
+        for b in (self._kv, self._dkv, self._dkv2, self._flags):
+            if b is not None:
+                b.close()

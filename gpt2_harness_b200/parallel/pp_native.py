@@ -205,6 +205,8 @@ class StageEngine:
         self.step_count = 0
         # context-parallel composition (same hooks as the single-GPU engine)
         self.pos0 = 0
+        self.pos_split: Optional[int] = None
+        self.pos1 = 0
         self.attn_fwd_hook: Optional[Callable] = None
         self.attn_bwd_hook: Optional[Callable] = None
         self.slot_hook: Optional[Callable[[int], None]] = None
@@ -258,7 +260,8 @@ class StageEngine:
         eps = cfg.layer_norm_epsilon
         p = self.p16
         if lay.first:
-            N.embedding_fwd(idx, p("wte.weight"), p("wpe.weight"), S.x[0], pos0=self.pos0)
+            N.embedding_fwd(idx, p("wte.weight"), p("wpe.weight"), S.x[0], pos0=self.pos0,
+                            pos_split=self.pos_split, pos1=self.pos1)
         for j in range(self.n):
             pre = f"h.{lay.l0 + j}."
             N.layernorm_fwd(S.x[2 * j], p(pre + "ln_1.weight"), p(pre + "ln_1.bias"), S.h1[j],
@@ -349,7 +352,8 @@ class StageEngine:
             if not acc:
                 g("wte.weight").zero_()
                 wpe_g.zero_()
-            N.embedding_bwd(idx, self.dres, g("wte.weight"), wpe_g, V, pos0=self.pos0)
+            N.embedding_bwd(idx, self.dres, g("wte.weight"), wpe_g, V, pos0=self.pos0,
+                            pos_split=self.pos_split, pos1=self.pos1)
 
     # -------------------------------------------------------------- step --
     def train_step(self, micro_idx: list, micro_tgt: list) -> torch.Tensor:

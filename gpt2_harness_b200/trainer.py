@@ -61,6 +61,8 @@ class Trainer:
             its contiguous ``seq_len / p`` slice of each.
         comm_blocks: CTAs of each fused peer-memory all-reduce (DDP, p2p):
             fewer leave more of the GPU to the backward it overlaps.
+        cp_balance: context-parallel split, ``"zigzag"`` (two chunks per rank,
+            equal causal work) or ``"contiguous"`` (one slice per rank).
         seed: weight init seed (identical on every rank; rank 0's weights are
             broadcast to make sure).
     """
@@ -69,7 +71,7 @@ class Trainer:
                  train: Optional[TrainConfig] = None, comm: str = "p2p",
                  device: Optional[torch.device] = None, seed: int = 0,
                  bucket_bytes: int = 25 * 1024 * 1024, schedule: bool = True,
-                 strategy: str = "ddp", comm_blocks: int = 128) -> None:
+                 strategy: str = "ddp", comm_blocks: int = 128, cp_balance: str = "zigzag") -> None:
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device())
         self.device = torch.device(device)
@@ -110,7 +112,7 @@ class Trainer:
             from gpt2_harness_b200.parallel.cp_native import NativeCP
             from gpt2_harness_b200.parallel.ddp_native import NativeDDP
 
-            self.cp = NativeCP(config, batch_size, seq_len, device=self.device)
+            self.cp = NativeCP(config, batch_size, seq_len, device=self.device, balance=cp_balance)
             self.ddp = NativeDDP(ParamLayout(config), comm=comm, bucket_bytes=bucket_bytes,
                                  device=self.device, nblocks=comm_blocks)
             grad_buffer = self.ddp.grad_buffer
@@ -164,13 +166,9 @@ class Trainer:
         if idx.shape != (self.B, self.T) or targets.shape != (self.B, self.T):
             raise ValueError(f"expected ({self.B}, {self.T}) batches, got {tuple(idx.shape)}")
         if self.cp is not None:
-            # this rank's slice of every sequence
-            a, b = self.cp.pos0, self.cp.pos0 + self.T_local
-            idx, targets = idx[:, a:b], targets[:, a:b]
-            if idx.device.type == "cpu":
-                idx, targets = idx.contiguous(), targets.contiguous()
-            self.idx_l.copy_(idx, non_blocking=True)
-            self.tgt_l.copy_(targets, non_blocking=True)
+            # this rank's tokens of every sequence
+            self.cp.local_tokens(idx, self.idx_l)
+            self.cp.local_tokens(targets, self.tgt_l)
             self.h2d_done.record()
             return self.idx_l, self.tgt_l
         if idx.device == self.device and targets.device == self.device:
@@ -260,7 +258,7 @@ class PipelineTrainer:
     def __init__(self, config: GPTConfig, micro_batch: int, seq_len: int, micro_batches: int, *,
                  pp: Optional[int] = None, cp: int = 1, schedule: str = "1f1b",
                  train: Optional[TrainConfig] = None, device: Optional[torch.device] = None,
-                 seed: int = 0, comm_blocks: int = 128) -> None:
+                 seed: int = 0, comm_blocks: int = 128, cp_balance: str = "zigzag") -> None:
         from gpt2_harness_b200.parallel.cp_native import NativeCP
         from gpt2_harness_b200.parallel.pp_native import StageEngine, make_mesh
 
@@ -292,9 +290,8 @@ class PipelineTrainer:
             lay = self.engine.lay
             self.cp = NativeCP(config, micro_batch, seq_len, group=mesh.cp_group, device=self.device,
                                nblocks=comm_blocks, layers=range(lay.l0, lay.l1),
-                               slots=len(self.engine.slots))
+                               slots=len(self.engine.slots), balance=cp_balance)
             self.cp.attach(self.engine)
-        self.pos0 = mesh.cp_rank * self.Tl
         lay = self.engine.lay
         mB = micro_batches * micro_batch
         self.idx = torch.zeros(mB, self.Tl, dtype=torch.int64, device=self.device) if lay.first else None
@@ -311,14 +308,13 @@ class PipelineTrainer:
         mB = self.m * self.B
         if idx.shape != (mB, self.T) or targets.shape != (mB, self.T):
             raise ValueError(f"expected ({mB}, {self.T}) batches, got {tuple(idx.shape)}")
-        a, b = self.pos0, self.pos0 + self.Tl
         for src, dst in ((idx, self.idx), (targets, self.tgt)):
             if dst is None:
                 continue
-            src = src[:, a:b]
-            if src.device.type == "cpu" and not src.is_contiguous():
-                src = src.contiguous()
-            dst.copy_(src, non_blocking=True)
+            if self.cp is not None:
+                self.cp.local_tokens(src, dst)
+            else:
+                dst.copy_(src, non_blocking=True)
         self.h2d_done.record()
         B = self.B
         split = lambda t: [t[i * B:(i + 1) * B] for i in range(self.m)] if t is not None else [None] * self.m

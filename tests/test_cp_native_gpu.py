@@ -36,7 +36,7 @@ WORKER = textwrap.dedent(r'''
     cfg = gpt2_config("gpt2", n_layer=2, n_positions=1024)
     B, T = 2, 1024
     Tl = T // world
-    cp = NativeCP(cfg, B, T)
+    cp = NativeCP(cfg, B, T, balance=os.environ["G2B_BALANCE"])
     ddp = NativeDDP(ParamLayout(cfg), comm="p2p")
     eng = Engine(cfg, "cuda", grad_buffer=ddp.grad_buffer, seed=0)
     ddp.attach(eng)
@@ -45,10 +45,11 @@ WORKER = textwrap.dedent(r'''
     g = torch.Generator().manual_seed(11)
     idx = torch.randint(0, cfg.vocab_size, (B, T), generator=g).cuda()
     tgt = torch.randint(0, cfg.vocab_size, (B, T), generator=g).cuda()
-    a, b = rank * Tl, (rank + 1) * Tl
+    idx_l = cp.local_tokens(idx, torch.empty(B, Tl, dtype=idx.dtype, device="cuda"))
+    tgt_l = cp.local_tokens(tgt, torch.empty(B, Tl, dtype=tgt.dtype, device="cuda"))
     with comms.counter_scope(world) as ctr:
-        loss = eng.forward(idx[:, a:b].contiguous(), tgt[:, a:b].contiguous())
-        eng.backward(idx[:, a:b].contiguous()); ddp.finish()
+        loss = eng.forward(idx_l, tgt_l)
+        eng.backward(idx_l); ddp.finish()
         ctr.steps += 1
         torch.cuda.synchronize()
         N.check_errors()
@@ -76,7 +77,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _run(world: int):
+def _run(world: int, balance: str):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     port = _free_port()
@@ -84,7 +85,7 @@ def _run(world: int):
     for r in range(world):
         env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r),
                    MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), G2B_ROOT=ROOT,
-                   NCCL_NVLS_ENABLE="0")
+                   NCCL_NVLS_ENABLE="0", G2B_BALANCE=balance)
         procs.append(subprocess.Popen([sys.executable, "-c", WORKER], env=env, stdout=subprocess.PIPE,
                                       stderr=subprocess.STDOUT, text=True))
     results = []
@@ -103,9 +104,9 @@ def _run(world: int):
     return results
 
 
-@pytest.mark.parametrize("world", [1, 2])
-def test_native_cp_matches_single_gpu(world):
-    res = _run(world)
+@pytest.mark.parametrize("world,balance", [(1, "zigzag"), (2, "contiguous"), (2, "zigzag")])
+def test_native_cp_matches_single_gpu(world, balance):
+    res = _run(world, balance)
     print(res)
     for r in res:
         assert abs(r["loss"] - r["ref_loss"]) < 1e-3 * abs(r["ref_loss"]), r

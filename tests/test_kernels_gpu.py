@@ -254,6 +254,23 @@ def test_embedding():
     assert rel_err(gp[:T], dx.view(B, T, C).sum(0)) < 1e-5
 
 
+def test_embedding_two_chunks():
+    """Positions from two offsets (the zig-zag context-parallel layout)."""
+    V, C, B, T, split, pos0, pos1 = 1000, 128, 2, 48, 16, 8, 40
+    wte = torch.randn(V, C, device=dev()).bfloat16()
+    wpe = torch.randn(128, C, device=dev()).bfloat16()
+    idx = torch.randint(0, V, (B, T), device=dev())
+    pos = torch.cat([torch.arange(pos0, pos0 + split), torch.arange(pos1, pos1 + T - split)]).to(dev())
+    x = torch.empty(B * T, C, device=dev())
+    N.embedding_fwd(idx, wte, wpe, x, pos0=pos0, pos_split=split, pos1=pos1)
+    assert rel_err(x.view(B, T, C), wte.float()[idx] + wpe.float()[pos][None]) < 1e-6
+    dx = torch.randn(B * T, C, device=dev())
+    gp = torch.zeros(128, C, device=dev())
+    N.embedding_bwd(idx, dx, None, gp, V, pos0=pos0, pos_split=split, pos1=pos1)
+    ref = torch.zeros(128, C, device=dev()).index_add_(0, pos, dx.view(B, T, C).sum(0))
+    assert rel_err(gp, ref) < 1e-5
+
+
 # ----------------------------------------------------------- cross-entropy --
 def test_cross_entropy():
     M, V, ld = 300, 50257, 50304
