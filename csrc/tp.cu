@@ -430,8 +430,9 @@ __global__ void __launch_bounds__(512) cp_kv_reduce_zz_kernel(const TpArgs a) {
         make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
                    pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
   }
+  // chunk r is read from 2w-r partials, chunk 2w-1-r from r+1
   if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
-    atomicAdd(a.byte_counter, (unsigned long long)(nvec * 16 * 2 * a.world));
+    atomicAdd(a.byte_counter, (unsigned long long)(nvec / 2 * 16 * (2 * a.world + 1)));
   finish(a, &fail);
 }
 

@@ -138,8 +138,9 @@ class StageEngine:
                  comm_blocks: int = 128) -> None:
         if not dist.is_initialized():
             raise RuntimeError("StageEngine needs an initialised process group")
-        if config.head_dim != 64 or not config.tie_weights:
-            raise ValueError("the stage engine implements head_dim 64 GPT-2")
+        # the full-model layout (tied GPT-2, head_dim 64) defines the init;
+        # the last stage then unties lm_head from wte
+        ParamLayout(config)
         self.group = group
         self.p = dist.get_world_size(group)
         self.stage = dist.get_rank(group)
@@ -445,6 +446,29 @@ class StageEngine:
         """This stage's parameters (fp32 master, reference names; the last
         stage's untied ``lm_head.weight`` included)."""
         return {name: self.lay.view(self.master, name).clone() for name in self.lay.specs}
+
+    def optimizer_state(self) -> dict:
+        """AdamW moments of this stage (reference names) and the step count."""
+        return {"step": self.step_count,
+                "exp_avg": {n: self.lay.view(self.exp_avg, n).clone() for n in self.lay.specs},
+                "exp_avg_sq": {n: self.lay.view(self.exp_avg_sq, n).clone() for n in self.lay.specs}}
+
+    @torch.no_grad()
+    def load_state_dict(self, sd: dict, optim: Optional[dict] = None) -> None:
+        """Load this stage's tensors from a dict keyed by reference names (a
+        full-model state dict works: only this stage's names are read; a
+        missing ``lm_head.weight`` is taken from ``wte.weight``)."""
+        for name in self.lay.specs:
+            src = sd.get(name)
+            if src is None and name == "lm_head.weight":
+                src = sd["wte.weight"]
+            self.lay.view(self.master, name).copy_(src)
+        self.shadow.copy_(self.master)
+        if optim is not None:
+            self.step_count = int(optim["step"])
+            for n in self.lay.specs:
+                self.lay.view(self.exp_avg, n).copy_(optim["exp_avg"][n])
+                self.lay.view(self.exp_avg_sq, n).copy_(optim["exp_avg_sq"][n])
 
     def close(self) -> None:
         torch.cuda.synchronize(self.device)

@@ -339,6 +339,21 @@ class PipelineTrainer:
     def check(self) -> None:
         N.check_errors(self.device)
 
+    def state_dict(self) -> dict:
+        """This rank's stage: parameters (reference names, fp32), AdamW state,
+        and where it sits in the mesh. Ranks of one CP group hold identical
+        copies."""
+        m = self.mesh
+        return {"model": self.engine.state_dict(), "optim": self.engine.optimizer_state(),
+                "step": self.step_num, "stage": m.stage, "pp": m.pp, "cp": m.cp,
+                "layers": (self.engine.lay.l0, self.engine.lay.l1)}
+
+    def load_state_dict(self, sd: dict) -> None:
+        """Restore :meth:`state_dict` output of the same stage (or load a
+        full-model ``{"model": ...}`` dict: only this stage's tensors are read)."""
+        self.engine.load_state_dict(sd["model"], sd.get("optim"))
+        self.step_num = int(sd.get("step", 0))
+
     def close(self) -> None:
         if self.cp is not None:
             self.cp.close()
