@@ -478,7 +478,9 @@ class StageEngine:
 
 
 class PipelineMesh:
-    """Process groups of a pp x cp mesh: global rank = stage * cp + c."""
+    """Process groups of a pp x cp mesh (global rank = stage * cp + c): the
+    pipeline line of this rank with one extra communicator per transfer
+    direction, and the context-parallel group of its stage."""
 
     def __init__(self, pp: int, cp: int, stage: int, cp_rank: int, pp_group, fwd_group, bwd_group,
                  cp_group) -> None:
@@ -489,19 +491,16 @@ class PipelineMesh:
 def make_mesh(pp: int, cp: int = 1) -> PipelineMesh:
     """Create the mesh's groups. Collective over the default group: every
     rank calls it with the same arguments (``pp * cp`` = world size)."""
-    world, rank = dist.get_world_size(), dist.get_rank()
-    if pp * cp != world:
-        raise ValueError(f"pp={pp} x cp={cp} must equal the world size {world}")
-    stage, c = divmod(rank, cp)
-    mine = None
-    for cc in range(cp):
-        ranks = [s * cp + cc for s in range(pp)]
-        gs = tuple(dist.new_group(ranks) for _ in range(3))
-        if cc == c:
-            mine = gs
-    cp_group = None
-    for s in range(pp):
-        g = dist.new_group(list(range(s * cp, (s + 1) * cp)))
-        if s == stage:
-            cp_group = g
-    return PipelineMesh(pp, cp, stage, c, mine[0], mine[1], mine[2], cp_group if cp > 1 else None)
+    from gpt2_harness_b200.parallel.mesh import Mesh
+
+    mesh = Mesh({"pp": pp, "cp": cp})
+    # the activation and gradient communicators of every pipeline line, made
+    # in the same order on every rank
+    p2p = None
+    for c in range(cp):
+        ranks = [mesh.rank_of({"pp": s, "cp": c}) for s in range(pp)]
+        gs = (dist.new_group(ranks), dist.new_group(ranks))
+        if c == mesh.coord("cp"):
+            p2p = gs
+    return PipelineMesh(pp, cp, mesh.coord("pp"), mesh.coord("cp"), mesh.group("pp"), p2p[0], p2p[1],
+                        mesh.group("cp") if cp > 1 else None)
