@@ -46,6 +46,10 @@ from gpt2_harness_b200.ops import native as N
 __all__ = ["ParamSpec", "ParamLayout", "Engine", "OptimConfig", "choose_splits", "init_flat_weights"]
 
 ALIGN = 64  # elements; 128 bytes of bf16, 256 bytes of fp32
+#: Device types the engine accepts. Only CUDA runs the native kernels; the
+#: host-orchestration tests widen this while the ops are replaced by torch
+#: implementations of the same contracts.
+DEVICE_TYPES = ("cuda",)
 
 
 @dataclass
@@ -253,7 +257,7 @@ class Engine:
                  optimizer_state: bool = True) -> None:
         self.config = config
         self.device = torch.device(device)
-        if self.device.type != "cuda":
+        if self.device.type not in DEVICE_TYPES:
             raise ValueError("the native engine runs on CUDA devices")
         N.lib()  # fail loudly if the extension is missing
         self.layout = ParamLayout(config)

@@ -345,6 +345,14 @@ def cross_entropy_fwd_bwd(logits: torch.Tensor, targets: torch.Tensor, loss_rows
     L.loss_reduce(loss_rows.data_ptr(), targets.data_ptr(), M, loss_out.data_ptr(), _stream())
 
 
+def cast_f32_bf16(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out(bf16) = x(fp32), elementwise over contiguous buffers."""
+    if x.numel() != out.numel():
+        raise ValueError("cast_f32_bf16: sizes differ")
+    lib().cast_f32_bf16(x.data_ptr(), out.data_ptr(), x.numel(), _stream())
+    return out
+
+
 # ---------------------------------------------------------------- optimiser --
 def adamw_step(p: torch.Tensor, g: torch.Tensor, m: torch.Tensor, v: torch.Tensor,
                p_bf16: Optional[torch.Tensor], n_decay: int, hp: torch.Tensor,

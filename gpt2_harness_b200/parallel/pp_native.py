@@ -310,8 +310,7 @@ class StageEngine:
         else:
             # self.dres holds the gradient received from the next stage; its
             # column sum is the bias gradient of this stage's last projection
-            N.lib().cast_f32_bf16(self.dres.data_ptr(), self.dres16.data_ptr(), self.dres.numel(),
-                                  torch.cuda.current_stream().cuda_stream)
+            N.cast_f32_bf16(self.dres, self.dres16)
             N.colsum_bf16(self.dres16, top_bias, self.col_ws, accumulate=acc)
         for j in reversed(range(n)):
             pre = f"h.{l0 + j}."
