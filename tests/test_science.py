@@ -147,3 +147,81 @@ def test_ablation_grid_and_verdicts(dataset):
     verdicts = {r["arm"]: r["verdict"] for r in summ["rows"]}
     assert verdicts["baseline"] == "reference"
     assert set(verdicts.values()) <= {"reference", "indistinguishable", "worse", "better"}
+
+
+# ------------------------------------------------- quantization / pruning properties --
+def test_quantization_granularity_properties():
+    from gpt2_harness_b200.quantization import quantize_dequantize, quantize_tensor
+    torch.manual_seed(1)
+    w = torch.randn(8, 32)
+    _, s = quantize_tensor(w, 8, "per_tensor")
+    assert s.numel() == 1
+    _, sc = quantize_tensor(w, 8, "per_channel")
+    assert sc.numel() == 8
+    w[3] *= 100.0  # one outlier row: per-tensor scaling wastes the others' codes
+    err_t = (quantize_dequantize(w, 4, "per_tensor") - w)[[0, 1, 2, 4, 5, 6, 7]].abs().mean()
+    err_c = (quantize_dequantize(w, 4, "per_channel") - w)[[0, 1, 2, 4, 5, 6, 7]].abs().mean()
+    assert err_c < err_t / 5
+    prev = float("inf")
+    for bits in (2, 4, 8):
+        e = (quantize_dequantize(w, bits) - w).abs().max().item()
+        assert e <= prev
+        prev = e
+    w[5] = 0.0
+    out = quantize_dequantize(w, 4)
+    assert torch.all(out[5] == 0) and torch.isfinite(out).all()
+
+
+def test_int4_pack_full_code_range():
+    from gpt2_harness_b200.quantization import pack_int4, unpack_int4
+    q = torch.arange(-8, 8, dtype=torch.int8)
+    assert torch.equal(unpack_int4(pack_int4(q), 16), q)
+
+
+def test_quantized_model_logits_are_finite_and_size_counts_tied_once():
+    from gpt2_harness_b200.inference.benchmark import model_size_bytes
+    from gpt2_harness_b200.quantization import quantize_model
+    m = _model()
+    qm, _ = quantize_model(m, 4)
+    assert torch.isfinite(qm(torch.randint(0, 64, (1, 12)))["logits"]).all()
+    tied = sum(p.numel() * 4 for p in m.parameters())
+    assert model_size_bytes(m) == tied
+    assert model_size_bytes(m, count_tied_once=False) == tied + m.wte.weight.numel() * 4
+
+
+def test_zeroed_head_removes_exactly_its_contribution_and_zero_sparsity_is_noop(dataset):
+    from gpt2_harness_b200.pruning import keep_mask, pruned
+    m = _model()
+    x = torch.randint(0, 64, (1, 10))
+    blk = m.h[0]
+    h = blk.ln_1(m.wte(x) + m.wpe(torch.arange(10)))
+    mask = torch.ones(4)
+    mask[2] = 0
+    blk.attn.head_mask = mask
+    y_masked, _ = blk.attn(h)
+    blk.attn.head_mask = None
+    # recompute by hand with head 2's output removed before the projection
+    B, T, C = h.shape
+    q, k, v = blk.attn.c_attn(h).split(C, dim=2)
+    q, k, v = (t.view(B, T, 4, 8).transpose(1, 2) for t in (q, k, v))
+    att = torch.softmax((q @ k.transpose(-1, -2) / math.sqrt(8)).masked_fill(
+        torch.ones(T, T, dtype=torch.bool).triu(1), float("-inf")), -1) @ v
+    att[:, 2] = 0
+    want = blk.attn.c_proj(att.transpose(1, 2).reshape(B, T, C))
+    assert torch.allclose(y_masked, want, atol=1e-6)
+    scores = torch.rand(2, 4)
+    assert torch.all(keep_mask(scores, 0.0) == 1)
+    base = m(x)["logits"]
+    with pruned(m, head_mask=keep_mask(scores, 0.0)):
+        assert torch.allclose(m(x)["logits"], base)
+
+
+def test_rank_correlation_hand_computed():
+    from gpt2_harness_b200.induction import rank_correlation
+    # ranks of a: [1.5, 1.5, 3, 4]; of b: [4, 3, 2, 1] -> Pearson of the ranks
+    a = torch.tensor([1.0, 1.0, 2.0, 3.0])
+    b = torch.tensor([4.0, 3.0, 2.0, 1.0])
+    ra = torch.tensor([1.5, 1.5, 3.0, 4.0])
+    rb = torch.tensor([4.0, 3.0, 2.0, 1.0])
+    want = float(torch.corrcoef(torch.stack([ra, rb]))[0, 1])
+    assert rank_correlation(a, b) == pytest.approx(want)
