@@ -110,3 +110,70 @@ def test_async_checkpointer_matches_sync_and_surfaces_errors(tmp_path):
     ck.save(tmp_path / "b", sd, plan=plan, rank=0, world_size=1, step=3, global_shapes=None)
     with pytest.raises(ValueError):
         ck.wait()
+
+
+# ------------------------------------------------------ plan and shard math --
+def test_plan_covers_every_parameter_and_shards_the_right_ones():
+    sd = tiny_gpt().state_dict()
+    plan = gpt2_tp_plan(sd)
+    assert set(plan) == set(sd)
+    for n, spec in plan.items():
+        if n.endswith(("c_attn.weight", "c_attn.bias")):
+            assert (spec.kind, spec.dim, spec.sections) == ("shard", 0, 3)
+        elif n.endswith(("attn.c_proj.weight", "mlp.c_proj.weight")):
+            assert (spec.kind, spec.dim) == ("shard", 1)
+        elif n.endswith(("mlp.c_fc.weight", "mlp.c_fc.bias")) or n in ("wte.weight", "lm_head.weight"):
+            assert (spec.kind, spec.dim) == ("shard", 0)
+        else:
+            assert spec.kind == "replicate", n
+    assert gpt2_tp_plan(sd, vocab_parallel=False)["wte.weight"].kind == "replicate"
+
+
+def test_column_and_row_parallel_shards_reproduce_the_full_matmul():
+    torch.manual_seed(3)
+    x = torch.randn(5, 32, dtype=torch.float64)
+    w_fc = torch.randn(128, 32, dtype=torch.float64)
+    w_pr = torch.randn(32, 128, dtype=torch.float64)
+    full = (x @ w_fc.t()).relu() @ w_pr.t()
+    for p in (1, 2, 4):
+        cols = split_tensor(w_fc, ShardSpec("shard", dim=0), p)
+        rows = split_tensor(w_pr, ShardSpec("shard", dim=1), p)
+        # column shards give slices of the hidden layer; row shards' partial
+        # products sum to the output
+        out = sum((x @ c.t()).relu() @ r.t() for c, r in zip(cols, rows))
+        assert torch.allclose(out, full)
+
+
+def test_reshard_reads_only_the_shards_it_needs(tmp_path):
+    m = tiny_gpt()
+    _, plan = save_layout(tmp_path, m, 4)
+    # 4 -> 4 same layout: each rank's shards sit in one file (replicated
+    # tensors are read from that same file)
+    _, _, files = load_reshard(tmp_path, rank=2, world_size=4)
+    assert files == 1
+    # 4 -> 2: rank 0 of 2 needs source ranks 0 and 1
+    _, _, files = load_reshard(tmp_path, rank=0, world_size=2)
+    assert files == 2
+    # 4 -> 1: everything
+    _, _, files = load_reshard(tmp_path, rank=0, world_size=1)
+    assert files == 4
+
+
+def test_reserved_port_stays_reserved_and_launch_replaces_a_taken_port():
+    import socket
+    from dataclasses import replace
+
+    from gpt2_harness_b200.cluster.failure import JobSpec, _usable_port, port_is_free, reserved_port
+
+    with reserved_port() as p:
+        assert not port_is_free(p)
+        spec = JobSpec(data_path="d", ckpt_dir="c", log_path="l", master_port=p)
+        fixed = _usable_port(spec)
+        assert fixed.master_port != p and fixed.master_port > 0
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        s.listen(1)
+        taken = s.getsockname()[1]
+        assert _usable_port(JobSpec(data_path="d", ckpt_dir="c", log_path="l", master_port=taken)).master_port != taken
+    free = _usable_port(replace(spec, master_port=0))
+    assert free.master_port > 0
