@@ -93,3 +93,36 @@ def test_zero3_closed_form_at_gpt2_medium_p8():
     """The BASELINE ZeRO-3 config: 24 units of 12,596,224 params + 52,513,792 root."""
     assert zero3_payload_bytes([12_596_224] * 24, 52_513_792, 8) == 3_837_767_680
     assert zero3_payload_bytes([12_596_224] * 24, 52_513_792, 8, 2, 2, 2) == 1_918_883_840
+
+
+# -------------------------------------------- reduced-precision wires and clipping --
+def test_bf16_gradient_reduction_error_is_fresh_each_step_and_bounded():
+    fp = run(zero_equivalence_worker, 2, stage=2)[0].value
+    bf = run(zero_equivalence_worker, 2, stage=2, reduce_dtype="bf16")[0].value
+    # a bf16 reduce-scatter costs accuracy, but the fp32 master keeps it from
+    # compounding: every step's error stays within a small multiple of the first
+    assert bf["max_param_error"] > fp["max_param_error"]
+    errs = bf["param_errors"]
+    assert max(errs) < 1e-2 and max(errs) < 8 * max(errs[0], 1e-12)
+
+
+def test_bf16_parameter_gather_keeps_an_fp32_master_shard():
+    v = run(zero_equivalence_worker, 2, stage=2, param_dtype="bf16")[0].value
+    assert v["param_dtype"] == "bf16"
+    # the error of the gathered bf16 parameters saturates at bf16's resolution
+    # of the parameter scale, it does not grow step by step
+    assert v["max_param_error"] <= v["reference_param_scale"] * 2 ** -7
+    assert v["sharded_bytes"]["params"] > 0
+
+
+@pytest.mark.parametrize("stage", [1, 2])
+def test_sharded_clip_reproduces_single_process_clip_and_bites(stage):
+    v = run(zero_equivalence_worker, 2, stage=stage, grad_clip=0.05)[0].value
+    assert v["max_grad_norm_error"] < 1e-5
+    assert any(n["reference"] > 0.05 for n in v["grad_norms"])  # the clip was active
+
+
+def test_zero3_clips_shards_and_roots_consistently():
+    res = run(zero3_equivalence_worker, 2, grad_clip=0.05)
+    for r in res:
+        assert r.value["max_param_error"] < TOL
