@@ -61,3 +61,26 @@ def test_bubble_scan_orders_with_micro_batches():
     rows = res[0].value["rows"]
     assert {r["kind"] for r in rows} == {"gpipe", "1f1b"}
     assert all(r["analytic_bubble"] == pytest.approx(analytic_bubble(2, r["micro_batches"])) for r in rows)
+
+
+def test_pipeline_stages_partition_the_model():
+    import torch
+
+    from gpt2_harness_b200.parallel.common import identical_model, parallel_config
+    from gpt2_harness_b200.parallel.pipeline_parallel import PipelineStage
+
+    cfg = parallel_config()
+    full = identical_model(cfg)
+    total = sum(p.numel() for p in full.parameters())
+    counts = []
+    for s in range(4):
+        stage = PipelineStage(identical_model(cfg), s, 4)
+        counts.append(sum(p.numel() for p in stage.parameters()))
+        assert len(stage.blocks) == 1 and stage.is_first == (s == 0) and stage.is_last == (s == 3)
+    # the tied table is held twice once the head is split off onto the last stage
+    assert sum(counts) == total + cfg.vocab_size * cfg.n_embd
+    with pytest.raises(ValueError):
+        PipelineStage(identical_model(cfg), 0, 3)
+    x = torch.randint(0, cfg.vocab_size, (2, 8))
+    s0 = PipelineStage(identical_model(cfg), 0, 1)
+    assert torch.allclose(s0(x), identical_model(cfg)(x)["logits"])

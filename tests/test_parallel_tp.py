@@ -68,3 +68,19 @@ def test_vocab_parallel_embedding_and_cross_entropy(world):
     pay = res[0].payload["per_collective"]
     # one embedding all-reduce (B*T*C) + three (B*T,) loss all-reduces + f's backward
     assert pay["all_reduce"]["calls"] == 5
+
+
+def test_tensor_parallel_holds_a_fraction_of_the_block():
+    import torch
+
+    from gpt2_harness_b200.parallel.common import identical_block, parallel_config
+    from gpt2_harness_b200.parallel.tensor_parallel import TensorParallelBlock
+
+    cfg = parallel_config()
+    C = cfg.n_embd
+    full = sum(p.numel() for p in identical_block(cfg).parameters())
+    replicated = 4 * C + C + C  # two LayerNorms, c_proj and mlp c_proj biases (added once)
+    for p in (2, 4):
+        tp = TensorParallelBlock(identical_block(cfg), 0, p)
+        held = sum(t.numel() for t in tp.parameters())
+        assert held == (full - replicated) // p + replicated
