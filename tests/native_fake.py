@@ -2,7 +2,7 @@
 tests on CPU.
 
 The engine, the pipeline stage engine and the trainers drive the sm_100a
-kernels through ``gpt2_harness_b200.ops.native``. :func:`install` replaces
+kernels through ``gpt2_harness_b200.ops.native``. :func:`installed` replaces
 those calls (and the CUDA stream/event/pinned-memory calls around them) with
 plain torch code that follows each kernel's documented contract -- the same
 output dtypes, bf16 rounding points, accumulate flags, strided views, partial
@@ -14,11 +14,15 @@ kernels themselves; their numerics are the GPU tier's job.
 
 from __future__ import annotations
 
+import ctypes
 import math
+import os
+import tempfile
 from contextlib import contextmanager
 from types import SimpleNamespace
 
 import torch
+import torch.distributed as dist
 
 from gpt2_harness_b200.models import gpt as _gpt
 from gpt2_harness_b200.ops import native as N
@@ -220,6 +224,107 @@ def cast_f32_bf16(x, out):
     return out.copy_(x)
 
 
+# ------------------------------------------------------ symmetric memory --
+def _at(ptr: int, numel: int, dtype: torch.dtype) -> torch.Tensor:
+    """A CPU tensor aliasing ``numel`` elements at address ``ptr``."""
+    esz = torch.empty((), dtype=dtype).element_size()
+    return torch.frombuffer((ctypes.c_char * (numel * esz)).from_address(ptr), dtype=dtype)
+
+
+def _ptr_list(ptr: int, n: int) -> list:
+    return [int(x) for x in _at(ptr, n, torch.int64)]
+
+
+class FakeSymmetricBuffer:
+    """Equal-sized host buffers mapped into every rank's process through
+    shared files: the CPU stand-in for the CUDA-IPC symmetric buffers, with
+    the same attributes (peer_ptrs / peer_ptrs_dev hold this process's
+    addresses of every rank's mapping)."""
+
+    def __init__(self, nbytes: int, group=None, device=None) -> None:
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.device = torch.device("cpu")
+        self.nbytes = int((nbytes + 255) // 256 * 256)
+        tag = [tempfile.mkdtemp(prefix="g2b_symm_") if self.rank == 0 else None]
+        dist.broadcast_object_list(tag, src=dist.get_global_rank(group, 0) if group is not None else 0,
+                                   group=group)
+        self.dir = tag[0]
+        path = lambda r: os.path.join(self.dir, f"buf_{r}")
+        self.local = torch.from_file(path(self.rank), shared=True, size=self.nbytes, dtype=torch.uint8)
+        self.local.zero_()
+        dist.barrier(group=group)
+        self._maps = [self.local if r == self.rank else
+                      torch.from_file(path(r), shared=True, size=self.nbytes, dtype=torch.uint8)
+                      for r in range(self.world)]
+        self.peer_ptrs = [m.data_ptr() for m in self._maps]
+        self.ptr = self.peer_ptrs[self.rank]
+        self.peer_ptrs_dev = torch.tensor(self.peer_ptrs, dtype=torch.int64)
+
+    def view(self, dtype, numel=None, offset_bytes: int = 0):
+        esz = torch.empty((), dtype=dtype).element_size()
+        n = (self.nbytes - offset_bytes) // esz if numel is None else numel
+        return self.local[offset_bytes:offset_bytes + n * esz].view(dtype)
+
+    def close(self) -> None:
+        self._maps = []
+
+
+# ---------------------------------------- context-parallel gather / reduce --
+def _cp_layout(d):
+    rank, world, B, Tl, cols = d["rank"], d["world"], d["B"], d["Tl"], d["cols"]
+    T = world * Tl
+    if d.get("zigzag", 0):
+        h = Tl // 2
+        segs = [(rank * h, 0, h), ((2 * world - 1 - rank) * h, h, h)]   # (global start, local start, len)
+        owner = lambda k: k if k < world else 2 * world - 1 - k
+        needed = [(k * h, h, owner(k)) for k in range(2 * world - rank) if k not in (rank, 2 * world - 1 - rank)]
+    else:
+        segs = [(rank * Tl, 0, Tl)]
+        needed = [(q * Tl, Tl, q) for q in range(rank)]
+    return rank, world, B, Tl, cols, T, segs, needed
+
+
+def cp_kv_gather(d, stream=0):
+    rank, world, B, Tl, cols, T, segs, needed = _cp_layout(d)
+    C = cols // 2
+    bufs = [_at(p, B * T * cols, torch.bfloat16).view(B, T, cols) for p in _ptr_list(d["peer_bufs"], world)]
+    src = _at(d["src"], (B * Tl - 1) * d["src_ld"] + 3 * C, torch.bfloat16)
+    rows = torch.as_strided(src, (B, Tl, cols), (Tl * d["src_ld"], d["src_ld"], 1), C)
+    for g0, l0, n in segs:
+        bufs[rank][:, g0:g0 + n] = rows[:, l0:l0 + n]
+    dist.barrier()
+    for g0, n, q in needed:
+        bufs[rank][:, g0:g0 + n] = bufs[q][:, g0:g0 + n]
+    dist.barrier()
+
+
+def cp_kv_reduce(d, stream=0):
+    rank, world, B, Tl, cols, T, segs, _ = _cp_layout(d)
+    C = cols // 2
+    dist.barrier()
+    parts1 = [_at(p, B * T * cols, torch.bfloat16).view(B, T, cols) for p in _ptr_list(d["peer_bufs"], world)]
+    parts2 = ([_at(p, B * T * cols, torch.bfloat16).view(B, T, cols) for p in _ptr_list(d["peer_bufs2"], world)]
+              if d.get("zigzag", 0) else None)
+    out = _at(d["out_bf16"], (B * Tl - 1) * d["src_ld"] + 3 * C, torch.bfloat16)
+    dst = torch.as_strided(out, (B, Tl, cols), (Tl * d["src_ld"], d["src_ld"], 1), C)
+    for g0, l0, n in segs:
+        acc = torch.zeros(B, n, cols)
+        for q in range(world):
+            if parts2 is None:
+                if q >= rank:
+                    acc += parts1[q][:, g0:g0 + n].float()
+                continue
+            h = Tl // 2
+            k = g0 // h
+            if k <= q:
+                acc += parts1[q][:, g0:g0 + n].float()
+            if k <= 2 * world - 1 - q:
+                acc += parts2[q][:, g0:g0 + n].float()
+        dst[:, l0:l0 + n] = acc.to(torch.bfloat16)
+    dist.barrier()
+
+
 class _Event:
     def record(self, *a, **k):
         pass
@@ -240,6 +345,8 @@ OPS = {
     "adamw_step": adamw_step, "cast_f32_bf16": cast_f32_bf16,
 }
 
+LIB = SimpleNamespace(cp_kv_gather=cp_kv_gather, cp_kv_reduce=cp_kv_reduce, tp_flag_words=lambda: 16)
+
 
 @contextmanager
 def installed(monkeypatch):
@@ -249,8 +356,13 @@ def installed(monkeypatch):
 
     for name, fn in OPS.items():
         monkeypatch.setattr(N, name, fn)
-    monkeypatch.setattr(N, "lib", lambda: SimpleNamespace())
+    from gpt2_harness_b200.parallel import cp_native
+
+    monkeypatch.setattr(N, "lib", lambda: LIB)
     monkeypatch.setattr(N, "check_errors", lambda *a, **k: None)
+    monkeypatch.setattr(N, "error_word", lambda *a, **k: torch.zeros(1, dtype=torch.int32))
+    monkeypatch.setattr(cp_native, "SymmetricBuffer", FakeSymmetricBuffer)
+    monkeypatch.setattr(torch.cuda, "current_stream", lambda *a, **k: SimpleNamespace(cuda_stream=0))
     monkeypatch.setattr(engine_mod, "DEVICE_TYPES", ("cuda", "cpu"))
     monkeypatch.setattr(torch.Tensor, "pin_memory", lambda self, *a, **k: self)
     monkeypatch.setattr(torch.cuda, "Event", _Event)
