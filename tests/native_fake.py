@@ -325,6 +325,44 @@ def cp_kv_reduce(d, stream=0):
     dist.barrier()
 
 
+# ------------------------------------------------------ fused all-reduce --
+def allreduce_p2p(peer_bufs, peer_flags, rank, world, offset, n, dtype, scale, epoch, counter, err,
+                  nblocks, budget_ns, stream):
+    """Sum of every rank's [offset, offset + n) elements, times `scale`,
+    left in every rank's buffer (the fused kernel's contract)."""
+    if n <= 0:
+        return
+    dt = torch.float32 if dtype == 0 else torch.bfloat16
+    esz = 4 if dtype == 0 else 2
+    bufs = [_at(p + offset * esz, n, dt) for p in _ptr_list(peer_bufs, world)]
+    dist.barrier()
+    total = sum(b.float() for b in bufs) * scale
+    dist.barrier()
+    bufs[rank].copy_(total)
+    if counter:
+        c = _at(counter, 1, torch.int64)
+        c += n * esz
+    dist.barrier()
+
+
+class _Stream:
+    cuda_stream = 0
+
+    def __init__(self, *a, **k):
+        pass
+
+    def wait_event(self, ev):
+        pass
+
+    def wait_stream(self, other):
+        pass
+
+
+@contextmanager
+def _stream_ctx(s):
+    yield
+
+
 class _Event:
     def record(self, *a, **k):
         pass
@@ -345,7 +383,8 @@ OPS = {
     "adamw_step": adamw_step, "cast_f32_bf16": cast_f32_bf16,
 }
 
-LIB = SimpleNamespace(cp_kv_gather=cp_kv_gather, cp_kv_reduce=cp_kv_reduce, tp_flag_words=lambda: 16)
+LIB = SimpleNamespace(cp_kv_gather=cp_kv_gather, cp_kv_reduce=cp_kv_reduce, tp_flag_words=lambda: 16,
+                      allreduce_p2p=allreduce_p2p, comm_flag_words=lambda: 16)
 
 
 @contextmanager
@@ -356,13 +395,17 @@ def installed(monkeypatch):
 
     for name, fn in OPS.items():
         monkeypatch.setattr(N, name, fn)
-    from gpt2_harness_b200.parallel import cp_native
+    from gpt2_harness_b200.parallel import cp_native, ddp_native, symm
 
     monkeypatch.setattr(N, "lib", lambda: LIB)
     monkeypatch.setattr(N, "check_errors", lambda *a, **k: None)
     monkeypatch.setattr(N, "error_word", lambda *a, **k: torch.zeros(1, dtype=torch.int32))
     monkeypatch.setattr(cp_native, "SymmetricBuffer", FakeSymmetricBuffer)
-    monkeypatch.setattr(torch.cuda, "current_stream", lambda *a, **k: SimpleNamespace(cuda_stream=0))
+    monkeypatch.setattr(ddp_native, "SymmetricBuffer", FakeSymmetricBuffer)
+    monkeypatch.setattr(symm, "SymmetricBuffer", FakeSymmetricBuffer)
+    monkeypatch.setattr(torch.cuda, "current_stream", lambda *a, **k: _Stream())
+    monkeypatch.setattr(torch.cuda, "Stream", _Stream)
+    monkeypatch.setattr(torch.cuda, "stream", _stream_ctx)
     monkeypatch.setattr(engine_mod, "DEVICE_TYPES", ("cuda", "cpu"))
     monkeypatch.setattr(torch.Tensor, "pin_memory", lambda self, *a, **k: self)
     monkeypatch.setattr(torch.cuda, "Event", _Event)

@@ -142,3 +142,50 @@ def test_context_parallel_matches_full_sequence(world, balance):
         assert abs(r["loss"] - r["ref_loss"]) < 1e-4 * r["ref_loss"], r
         # bf16 rounding of the summed dK/dV partials is the only difference
         assert r["worst"] < 1e-2, r
+
+
+def _ddp_worker(rank, world, bucket_mb):
+    import torch.distributed as dist
+
+    import native_fake as nf
+    from gpt2_harness_b200.config import GPTConfig
+    from gpt2_harness_b200.models.engine import Engine
+    from gpt2_harness_b200.parallel import comms
+    from gpt2_harness_b200.trainer import Trainer
+
+    nf.install_in_process()
+    cfg = GPTConfig(**CFG)
+    B, T = 2, 32
+    tr = Trainer(cfg, B, T, strategy="ddp", device="cpu", bucket_bytes=int(bucket_mb * 2**20))
+    g = torch.Generator().manual_seed(11)
+    idx = torch.randint(0, CFG["vocab_size"], (B * world, T), generator=g)
+    tgt = torch.randint(0, CFG["vocab_size"], (B * world, T), generator=g)
+    sl = slice(rank * B, (rank + 1) * B)
+    eng = tr.engine
+    with comms.counter_scope(world) as ctr:
+        loss = eng.forward(idx[sl], tgt[sl]).clone()
+        eng.backward(idx[sl])
+        tr.ddp.finish()
+        ctr.steps += 1
+        payload = ctr.summary()["payload_bytes_per_step"]
+    dist.all_reduce(loss)
+    ref = Engine(cfg, "cpu", seed=0)
+    ref_loss = float(ref.forward(idx, tgt))
+    ref.backward(idx)
+    errs = {s.name: float((eng.g32(s.name) - ref.g32(s.name)).norm() / (ref.g32(s.name).norm() + 1e-12))
+            for s in ref.layout.specs}
+    return {"loss": float(loss) / world, "ref_loss": ref_loss, "worst": max(errs.values()),
+            "payload": payload, "device_bytes": int(tr.ddp.byte_counter.item()),
+            "buckets": len(tr.ddp.buckets), "grad_bytes": eng.layout.total * 4}
+
+
+@pytest.mark.parametrize("world,bucket_mb", [(2, 0.25), (2, 25.0), (4, 0.5)])
+def test_native_ddp_matches_full_batch(world, bucket_mb):
+    res = spawn_workers(_ddp_worker, world, {"bucket_mb": bucket_mb}, backend="gloo", timeout=300)
+    for r in (x.value for x in res):
+        assert abs(r["loss"] - r["ref_loss"]) < 1e-5 * r["ref_loss"], r
+        assert r["worst"] < 1e-4, r
+        # every gradient byte is reduced exactly once per step, in both counters
+        assert r["payload"] == r["device_bytes"] == r["grad_bytes"], r
+    if bucket_mb < 1:
+        assert res[0].value["buckets"] > 1
