@@ -560,7 +560,7 @@ int tp_embed_bwd_launch(TpArgs a, cudaStream_t s) {
 }
 
 int tp_ce_stats_launch(TpArgs a, cudaStream_t s) {
-  if (a.rows <= 0 || a.vocab_valid <= 0) return -1;
+  if (a.rows <= 0 || a.vocab_valid < 0) return -1;  // 0: a slice of padding only
   tp_ce_stats_kernel<<<(unsigned)a.rows, CE_T, 0, s>>>(a);
   count_launches(1);
   return launch_succeeded() ? 0 : -11;

@@ -345,6 +345,120 @@ def allreduce_p2p(peer_bufs, peer_flags, rank, world, offset, n, dtype, scale, e
     dist.barrier()
 
 
+# ------------------------------------------- tensor-parallel row collectives --
+def _peers(d, key="peer_bufs"):
+    return _ptr_list(d[key], d["world"])
+
+
+def tp_ag_rows(d, stream=0):
+    rank, world, rows, cols = d["rank"], d["world"], d["rows"], d["cols"]
+    bufs = [_at(p, world * rows * cols, torch.bfloat16).view(world * rows, cols) for p in _peers(d)]
+    dist.barrier()
+    for q in range(world):
+        if q != rank:
+            bufs[rank][q * rows:(q + 1) * rows] = bufs[q][q * rows:(q + 1) * rows]
+    dist.barrier()
+
+
+def tp_rs_rows(d, stream=0):
+    rank, world, rows, cols = d["rank"], d["world"], d["rows"], d["cols"]
+    bufs = [_at(p, world * rows * cols, torch.bfloat16).view(world * rows, cols) for p in _peers(d)]
+    dist.barrier()
+    acc = torch.zeros(rows, cols)
+    for q in range(world):
+        acc += bufs[q][rank * rows:(rank + 1) * rows].float()
+    if d.get("bias"):
+        acc += _at(d["bias"], cols, torch.bfloat16).float()
+    if d.get("resid"):
+        acc += _at(d["resid"], rows * cols, torch.float32).view(rows, cols)
+    if d.get("out_f32"):
+        _at(d["out_f32"], rows * cols, torch.float32).view(rows, cols).copy_(acc)
+    if d.get("out_bf16"):
+        _at(d["out_bf16"], rows * cols, torch.bfloat16).view(rows, cols).copy_(acc)
+    dist.barrier()
+
+
+def tp_embed_fwd(d, stream=0):
+    rank, world, rows, cols, T, vpr = d["rank"], d["world"], d["rows"], d["cols"], d["T"], d["vocab_per_rank"]
+    tables = [_at(p, vpr * cols, torch.bfloat16).view(vpr, cols) for p in _peers(d)]
+    idx = _at(d["idx"], world * rows, torch.int64)
+    wpe = _at(d["wpe"], T * cols, torch.bfloat16).view(T, cols)
+    out = _at(d["out_f32"], rows * cols, torch.float32).view(rows, cols)
+    dist.barrier()
+    for i in range(rows):
+        m = rank * rows + i
+        tok = int(idx[m])
+        out[i] = tables[tok // vpr][tok % vpr].float() + wpe[m % T].float()
+    dist.barrier()
+
+
+def tp_embed_bwd(d, stream=0):
+    rank, world, rows, cols, T, vpr = d["rank"], d["world"], d["rows"], d["cols"], d["T"], d["vocab_per_rank"]
+    grads = [_at(p, vpr * cols, torch.float32).view(vpr, cols) for p in _peers(d)]
+    idx = _at(d["idx"], world * rows, torch.int64)
+    dx = _at(d["resid"], rows * cols, torch.float32).view(rows, cols)
+    wpe_g = _at(d["out_f32"], T * cols, torch.float32).view(T, cols)
+    dist.barrier()
+    for r in range(world):          # one rank at a time: the kernel's atomics
+        if r == rank:
+            for i in range(rows):
+                m = rank * rows + i
+                tok = int(idx[m])
+                grads[tok // vpr][tok % vpr] += dx[i]
+                wpe_g[m % T] += dx[i]
+        dist.barrier()
+
+
+def tp_ce_stats(d, stream=0):
+    rows, ld, vv, v0 = d["rows"], d["ld"], d["vocab_valid"], d["vocab_start"]
+    lg = _at(d["logits"], rows * ld, torch.bfloat16).view(rows, ld)[:, :vv].float()
+    tgt = _at(d["idx"], rows, torch.int64)
+    st = _at(d["stats"], rows * 4, torch.float32).view(rows, 4)
+    if vv == 0:   # a slice of padding only
+        st.copy_(torch.tensor([float("-inf"), 0.0, 0.0, 0.0]).expand(rows, 4))
+        return
+    m = lg.max(-1).values
+    st[:, 0] = m
+    st[:, 1] = torch.exp(lg - m[:, None]).sum(-1)
+    t = tgt - v0
+    local = (tgt != -100) & (t >= 0) & (t < vv)
+    tt = torch.where(local, t, torch.zeros_like(t))
+    st[:, 2] = torch.where(local, lg.gather(1, tt[:, None])[:, 0], torch.zeros(rows))
+    st[:, 3] = local.float()
+
+
+def tp_ce_finish(d, stream=0):
+    rows, world, ld, vv, v0 = d["rows"], d["world"], d["ld"], d["vocab_valid"], d["vocab_start"]
+    stats = [_at(p, rows * 4, torch.float32).view(rows, 4) for p in _peers(d)]
+    tgt = _at(d["idx"], rows, torch.int64)
+    logits = _at(d["logits"], rows * ld, torch.bfloat16).view(rows, ld)
+    loss_rows = _at(d["loss_rows"], rows, torch.float32)
+    dist.barrier()
+    S = torch.stack([s.clone() for s in stats])          # [world, rows, 4]
+    gm = S[:, :, 0].max(0).values
+    lse = gm + torch.log((S[:, :, 1] * torch.exp(S[:, :, 0] - gm)).sum(0))
+    tl = (S[:, :, 2] * S[:, :, 3]).sum(0)
+    ignore = tgt == -100
+    loss_rows.copy_(torch.where(ignore, torch.zeros(rows), lse - tl))
+    g = torch.exp(logits[:, :vv].float() - lse[:, None])
+    t = tgt - v0
+    hit = (~ignore) & (t >= 0) & (t < vv)
+    g[hit.nonzero()[:, 0], t[hit]] -= 1.0
+    g[ignore] = 0.0
+    logits[:, :vv] = g.to(torch.bfloat16)
+    logits[:, vv:] = 0
+    dist.barrier()
+
+
+def loss_reduce(loss_rows, targets, M, out, stream=0):
+    lr = _at(loss_rows, M, torch.float32)
+    tg = _at(targets, M, torch.int64)
+    o = _at(out, 2, torch.float32)
+    count = max(int((tg != -100).sum()), 1)
+    o[0] = lr.sum() / count
+    o[1] = 1.0 / count
+
+
 class _Stream:
     cuda_stream = 0
 
@@ -384,7 +498,9 @@ OPS = {
 }
 
 LIB = SimpleNamespace(cp_kv_gather=cp_kv_gather, cp_kv_reduce=cp_kv_reduce, tp_flag_words=lambda: 16,
-                      allreduce_p2p=allreduce_p2p, comm_flag_words=lambda: 16)
+                      allreduce_p2p=allreduce_p2p, comm_flag_words=lambda: 16, tp_ag_rows=tp_ag_rows,
+                      tp_rs_rows=tp_rs_rows, tp_embed_fwd=tp_embed_fwd, tp_embed_bwd=tp_embed_bwd,
+                      tp_ce_stats=tp_ce_stats, tp_ce_finish=tp_ce_finish, loss_reduce=loss_reduce)
 
 
 @contextmanager
@@ -395,7 +511,7 @@ def installed(monkeypatch):
 
     for name, fn in OPS.items():
         monkeypatch.setattr(N, name, fn)
-    from gpt2_harness_b200.parallel import cp_native, ddp_native, symm
+    from gpt2_harness_b200.parallel import cp_native, ddp_native, symm, tp_native
 
     monkeypatch.setattr(N, "lib", lambda: LIB)
     monkeypatch.setattr(N, "check_errors", lambda *a, **k: None)
@@ -403,6 +519,7 @@ def installed(monkeypatch):
     monkeypatch.setattr(cp_native, "SymmetricBuffer", FakeSymmetricBuffer)
     monkeypatch.setattr(ddp_native, "SymmetricBuffer", FakeSymmetricBuffer)
     monkeypatch.setattr(symm, "SymmetricBuffer", FakeSymmetricBuffer)
+    monkeypatch.setattr(tp_native, "SymmetricBuffer", FakeSymmetricBuffer)
     monkeypatch.setattr(torch.cuda, "current_stream", lambda *a, **k: _Stream())
     monkeypatch.setattr(torch.cuda, "Stream", _Stream)
     monkeypatch.setattr(torch.cuda, "stream", _stream_ctx)

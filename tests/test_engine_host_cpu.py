@@ -189,3 +189,41 @@ def test_native_ddp_matches_full_batch(world, bucket_mb):
         assert r["payload"] == r["device_bytes"] == r["grad_bytes"], r
     if bucket_mb < 1:
         assert res[0].value["buckets"] > 1
+
+
+def _tp_worker(rank, world):
+    import native_fake as nf
+    from gpt2_harness_b200.config import GPTConfig
+    from gpt2_harness_b200.models.engine import Engine, OptimConfig
+    from gpt2_harness_b200.parallel import comms
+    from gpt2_harness_b200.parallel.tp_native import TPEngine
+
+    nf.install_in_process()
+    cfg = GPTConfig(vocab_size=256, n_positions=64, n_layer=2, n_head=3, n_embd=192)  # 3 heads: uneven at p=2
+    B, T = world, 64
+    tp = TPEngine(cfg, B, T, device="cpu", optim=OptimConfig(lr=1e-3), seed=0)
+    ref = Engine(cfg, "cpu", optim=OptimConfig(lr=1e-3), seed=0)
+    ref.fuse_bias_grad_into_ln = False
+    g = torch.Generator().manual_seed(7)
+    idx = torch.randint(0, cfg.vocab_size, (B, T), generator=g)
+    tgt = torch.randint(0, cfg.vocab_size, (B, T), generator=g)
+    with comms.counter_scope(world) as ctr:
+        loss = float(tp.forward(idx, tgt))
+        tp.backward()
+        ctr.steps += 1
+        payload = ctr.summary()["payload_bytes_per_step"]
+    ref_loss = float(ref.forward(idx, tgt))
+    ref.backward(idx)
+    grads = tp.full_state("grad")
+    errs = {n: float((gv - ref.g32(n)).norm() / (ref.g32(n).norm() + 1e-12)) for n, gv in grads.items()}
+    return {"loss": loss, "ref_loss": ref_loss, "worst": max(errs.values()),
+            "worst_name": max(errs, key=errs.get), "payload": payload}
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_tensor_parallel_matches_single_engine(world):
+    res = spawn_workers(_tp_worker, world, {}, backend="gloo", timeout=300)
+    for r in (x.value for x in res):
+        assert abs(r["loss"] - r["ref_loss"]) < 1e-3 * r["ref_loss"], r
+        # row-parallel partials are rounded to bf16 before the reduction
+        assert r["worst"] < 2e-2, r
