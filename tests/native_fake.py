@@ -459,6 +459,105 @@ def loss_reduce(loss_rows, targets, M, out, stream=0):
     o[1] = 1.0 / count
 
 
+# ---------------------------------------------------------------- ZeRO-2/3 --
+def _zero_table(d):
+    t = _at(d["buckets"], 4 * d["nb"], torch.int64).view(d["nb"], 4)
+    return [tuple(int(x) for x in row) for row in t]
+
+
+def _zero_slice(row, rank):
+    lo, hi, s, off = row
+    f0 = lo + rank * s
+    return f0, max(0, min(hi, f0 + s) - f0), off
+
+
+def _bump(counter, nbytes):
+    if counter:
+        c = _at(counter, 1, torch.int64)
+        c += int(nbytes)
+
+
+def zero_rs(d, stream=0):
+    """This rank's slice of bucket `bucket`, summed over the ranks in rank
+    order and scaled, into its gradient shard; per-bucket sum of squares."""
+    rank, world = d["rank"], d["world"]
+    tab = _zero_table(d)
+    ext = max(r[1] for r in tab)
+    grads = [_at(p, ext, torch.float32) for p in _ptr_list(d["peer_grad"], world)]
+    b = d["bucket"]
+    f0, n, off = _zero_slice(tab[b], rank)
+    dist.barrier()
+    parts = (_at(d["sumsq_parts"], d["nb"] * d["rs_blocks"], torch.float32) if d.get("sumsq_parts")
+             else None)
+    if parts is not None:
+        parts[b * d["rs_blocks"]:(b + 1) * d["rs_blocks"]] = 0
+    if n:
+        acc = torch.zeros(n)
+        for q in range(world):
+            acc += grads[q][f0:f0 + n]
+        acc *= d["scale"]
+        _at(d["gsh"], off + n, torch.float32)[off:off + n] = acc
+        if parts is not None:
+            parts[b * d["rs_blocks"]] = (acc * acc).sum()
+    _bump(d.get("byte_counter"), (tab[b][1] - tab[b][0]) * 4)
+    dist.barrier()
+
+
+def zero_adamw_ag(d, nblocks, stream=0):
+    """Global norm from every rank's sums of squares, clip, AdamW on the
+    owned slices, the bf16 result written into every rank's parameters."""
+    rank, world = d["rank"], d["world"]
+    tab = _zero_table(d)
+    ext = max(r[1] for r in tab)
+    shard = max(off + s for (_, _, s, off) in tab)
+    local = _at(d["sumsq_parts"], d["nb"] * d["rs_blocks"], torch.float32).sum().reshape(1)
+    allss = [torch.zeros(1) for _ in range(world)]
+    dist.all_gather(allss, local)
+    norm = math.sqrt(float(sum(float(x) for x in allss)))
+    clip = min(d["max_norm"] / (norm + 1e-6), 1.0) if d["max_norm"] > 0 else 1.0
+    if d.get("norm_out"):
+        _at(d["norm_out"], 1, torch.float32)[0] = norm
+    hp = _at(d["hp"], 8, torch.float32)
+    master, gsh = _at(d["master"], shard, torch.float32), _at(d["gsh"], shard, torch.float32)
+    m, v = _at(d["exp_avg"], shard, torch.float32), _at(d["exp_avg_sq"], shard, torch.float32)
+    ranges = _at(d["decay_ranges"], 2 * d["nr"], torch.int64).tolist() if d["nr"] else []
+    shadows = [_at(p, ext, torch.bfloat16) for p in _ptr_list(d["peer_shadow"], world)]
+    dist.barrier()
+    for row in tab:
+        f0, n, off = _zero_slice(row, rank)
+        if not n:
+            continue
+        sl = slice(off, off + n)
+        decay = torch.zeros(n, dtype=torch.bool)
+        for lo, hi in zip(ranges[::2], ranges[1::2]):
+            a, b = max(lo, f0), min(hi, f0 + n)
+            if a < b:
+                decay[a - f0:b - f0] = True
+        lr, b1, b2, eps, wd, bc1, bc2s, gsc = [float(hp[i]) for i in range(8)]
+        gj = gsh[sl] * (gsc * clip)
+        pm, mm, vv = master[sl], m[sl], v[sl]
+        pm.mul_(torch.where(decay, 1.0 - lr * wd, 1.0))
+        mm.add_((gj - mm) * (1.0 - b1))
+        vv.mul_(b2).add_((1.0 - b2) * gj * gj)
+        pm.add_(-(lr / bc1) * (mm / (vv.sqrt() / bc2s + eps)))
+        for r in range(world):
+            shadows[r][f0:f0 + n] = master[sl].to(torch.bfloat16)
+    _bump(d.get("byte_counter"), sum(r[1] - r[0] for r in tab) * 2 + 4)
+    dist.barrier()
+
+
+def zero_ag(d, nblocks, stream=0):
+    world, span, slc, off = d["world"], d["ag_span"], d["ag_slice"], d["ag_offset"]
+    shards = [_at(p + off * 2, slc, torch.bfloat16) for p in _ptr_list(d["peer_shard"], world)]
+    dst = _at(d["gather_dst"], span, torch.bfloat16)
+    dist.barrier()
+    for e0 in range(0, span, slc):
+        n = min(slc, span - e0)
+        dst[e0:e0 + n] = shards[e0 // slc][:n]
+    _bump(d.get("byte_counter"), span * 2)
+    dist.barrier()
+
+
 class _Stream:
     cuda_stream = 0
 
@@ -497,7 +596,9 @@ OPS = {
     "adamw_step": adamw_step, "cast_f32_bf16": cast_f32_bf16,
 }
 
-LIB = SimpleNamespace(cp_kv_gather=cp_kv_gather, cp_kv_reduce=cp_kv_reduce, tp_flag_words=lambda: 16,
+LIB = SimpleNamespace(zero_rs=zero_rs, zero_adamw_ag=zero_adamw_ag, zero_ag=zero_ag,
+                      zero_flag_words=lambda: 16, zero_norm_words=lambda: 16, zero_max_blocks=lambda: 160,
+                      cp_kv_gather=cp_kv_gather, cp_kv_reduce=cp_kv_reduce, tp_flag_words=lambda: 16,
                       allreduce_p2p=allreduce_p2p, comm_flag_words=lambda: 16, tp_ag_rows=tp_ag_rows,
                       tp_rs_rows=tp_rs_rows, tp_embed_fwd=tp_embed_fwd, tp_embed_bwd=tp_embed_bwd,
                       tp_ce_stats=tp_ce_stats, tp_ce_finish=tp_ce_finish, loss_reduce=loss_reduce)
@@ -511,7 +612,7 @@ def installed(monkeypatch):
 
     for name, fn in OPS.items():
         monkeypatch.setattr(N, name, fn)
-    from gpt2_harness_b200.parallel import cp_native, ddp_native, symm, tp_native
+    from gpt2_harness_b200.parallel import cp_native, ddp_native, symm, tp_native, zero3_native, zero_native
 
     monkeypatch.setattr(N, "lib", lambda: LIB)
     monkeypatch.setattr(N, "check_errors", lambda *a, **k: None)
@@ -520,6 +621,8 @@ def installed(monkeypatch):
     monkeypatch.setattr(ddp_native, "SymmetricBuffer", FakeSymmetricBuffer)
     monkeypatch.setattr(symm, "SymmetricBuffer", FakeSymmetricBuffer)
     monkeypatch.setattr(tp_native, "SymmetricBuffer", FakeSymmetricBuffer)
+    monkeypatch.setattr(zero_native, "SymmetricBuffer", FakeSymmetricBuffer)
+    monkeypatch.setattr(zero3_native, "SymmetricBuffer", FakeSymmetricBuffer)
     monkeypatch.setattr(torch.cuda, "current_stream", lambda *a, **k: _Stream())
     monkeypatch.setattr(torch.cuda, "Stream", _Stream)
     monkeypatch.setattr(torch.cuda, "stream", _stream_ctx)

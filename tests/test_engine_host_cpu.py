@@ -227,3 +227,54 @@ def test_tensor_parallel_matches_single_engine(world):
         assert abs(r["loss"] - r["ref_loss"]) < 1e-3 * r["ref_loss"], r
         # row-parallel partials are rounded to bf16 before the reduction
         assert r["worst"] < 2e-2, r
+
+
+def _zero_worker(rank, world, strategy):
+    import torch.distributed as dist
+
+    import native_fake as nf
+    from gpt2_harness_b200.config import GPTConfig, TrainConfig
+    from gpt2_harness_b200.models.engine import Engine, OptimConfig
+    from gpt2_harness_b200.trainer import Trainer
+
+    nf.install_in_process()
+    cfg = GPTConfig(**CFG)
+    B, T = 2, 32
+    tc = TrainConfig()
+    tr = Trainer(cfg, B, T, strategy=strategy, device="cpu")
+    g = torch.Generator().manual_seed(13)
+    idx = torch.randint(0, CFG["vocab_size"], (B * world, T), generator=g)
+    tgt = torch.randint(0, CFG["vocab_size"], (B * world, T), generator=g)
+    sl = slice(rank * B, (rank + 1) * B)
+    loss = tr.step_async(idx[sl], tgt[sl]).clone()
+    dist.all_reduce(loss)
+    out = {"loss": float(loss) / world}
+    if strategy == "zero2":
+        full_grad = tr.ddp.gather_full(tr.ddp.gsh)
+    full = tr.ddp.full_master()
+    ref = Engine(cfg, "cpu", optim=OptimConfig(lr=tc.lr, betas=tuple(tc.betas), eps=tc.eps,
+                                               weight_decay=tc.weight_decay, grad_clip=tc.grad_clip), seed=0)
+    out["ref_loss"] = float(ref.forward(idx, tgt))
+    ref.backward(idx)
+    if strategy == "zero2":
+        out["grad_err"] = float((full_grad - ref.grad).norm() / ref.grad.norm())
+    ref.optimizer_step()
+    diff = (full - ref.master).abs()
+    out.update(max_diff=float(diff.max()), mean_diff=float(diff.mean()), lr=tc.lr,
+               norm=float(tr.ddp.grad_norm.item()) if hasattr(tr.ddp, "grad_norm") else None,
+               ref_norm=float(ref.grad_norm.item()), device_bytes=int(tr.ddp.byte_counter.item()))
+    return out
+
+
+@pytest.mark.parametrize("strategy,world", [("zero2", 2), ("zero2", 4), ("zero3", 2)])
+def test_native_zero_matches_full_batch_step(strategy, world):
+    res = spawn_workers(_zero_worker, world, {"strategy": strategy}, backend="gloo", timeout=300)
+    for r in (x.value for x in res):
+        assert abs(r["loss"] - r["ref_loss"]) < 1e-5 * r["ref_loss"], r
+        if "grad_err" in r:
+            assert r["grad_err"] < 1e-4, r
+        # Adam moves every element by about lr; only near-zero gradients can
+        # flip sign between summation orders
+        assert r["max_diff"] <= 2.5 * r["lr"] and r["mean_diff"] < 1e-2 * r["lr"], r
+        if r["norm"] is not None:
+            assert abs(r["norm"] - r["ref_norm"]) < 1e-4 * r["ref_norm"], r
