@@ -241,6 +241,9 @@ class FakeSymmetricBuffer:
     the same attributes (peer_ptrs / peer_ptrs_dev hold this process's
     addresses of every rank's mapping)."""
 
+    #: peer_ptrs_dev address -> buffer (to find a kernel call's process group)
+    by_ptrs: dict = {}
+
     def __init__(self, nbytes: int, group=None, device=None) -> None:
         self.group = group
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
@@ -260,6 +263,7 @@ class FakeSymmetricBuffer:
         self.peer_ptrs = [m.data_ptr() for m in self._maps]
         self.ptr = self.peer_ptrs[self.rank]
         self.peer_ptrs_dev = torch.tensor(self.peer_ptrs, dtype=torch.int64)
+        FakeSymmetricBuffer.by_ptrs[self.peer_ptrs_dev.data_ptr()] = self
 
     def view(self, dtype, numel=None, offset_bytes: int = 0):
         esz = torch.empty((), dtype=dtype).element_size()
@@ -268,6 +272,16 @@ class FakeSymmetricBuffer:
 
     def close(self) -> None:
         self._maps = []
+
+
+def _group(flags_ptr):
+    """The process group of the symmetric flag buffer a kernel call names."""
+    buf = FakeSymmetricBuffer.by_ptrs.get(int(flags_ptr))
+    return None if buf is None else buf.group
+
+
+def _barrier(flags_ptr):
+    dist.barrier(group=_group(flags_ptr))
 
 
 # ---------------------------------------- context-parallel gather / reduce --
@@ -293,16 +307,16 @@ def cp_kv_gather(d, stream=0):
     rows = torch.as_strided(src, (B, Tl, cols), (Tl * d["src_ld"], d["src_ld"], 1), C)
     for g0, l0, n in segs:
         bufs[rank][:, g0:g0 + n] = rows[:, l0:l0 + n]
-    dist.barrier()
+    dist.barrier(group=_group(d["peer_flags"]))
     for g0, n, q in needed:
         bufs[rank][:, g0:g0 + n] = bufs[q][:, g0:g0 + n]
-    dist.barrier()
+    dist.barrier(group=_group(d["peer_flags"]))
 
 
 def cp_kv_reduce(d, stream=0):
     rank, world, B, Tl, cols, T, segs, _ = _cp_layout(d)
     C = cols // 2
-    dist.barrier()
+    dist.barrier(group=_group(d["peer_flags"]))
     parts1 = [_at(p, B * T * cols, torch.bfloat16).view(B, T, cols) for p in _ptr_list(d["peer_bufs"], world)]
     parts2 = ([_at(p, B * T * cols, torch.bfloat16).view(B, T, cols) for p in _ptr_list(d["peer_bufs2"], world)]
               if d.get("zigzag", 0) else None)
@@ -322,7 +336,7 @@ def cp_kv_reduce(d, stream=0):
             if k <= 2 * world - 1 - q:
                 acc += parts2[q][:, g0:g0 + n].float()
         dst[:, l0:l0 + n] = acc.to(torch.bfloat16)
-    dist.barrier()
+    dist.barrier(group=_group(d["peer_flags"]))
 
 
 # ------------------------------------------------------ fused all-reduce --
@@ -335,14 +349,14 @@ def allreduce_p2p(peer_bufs, peer_flags, rank, world, offset, n, dtype, scale, e
     dt = torch.float32 if dtype == 0 else torch.bfloat16
     esz = 4 if dtype == 0 else 2
     bufs = [_at(p + offset * esz, n, dt) for p in _ptr_list(peer_bufs, world)]
-    dist.barrier()
+    dist.barrier(group=_group(peer_flags))
     total = sum(b.float() for b in bufs) * scale
-    dist.barrier()
+    dist.barrier(group=_group(peer_flags))
     bufs[rank].copy_(total)
     if counter:
         c = _at(counter, 1, torch.int64)
         c += n * esz
-    dist.barrier()
+    dist.barrier(group=_group(peer_flags))
 
 
 # ------------------------------------------- tensor-parallel row collectives --
@@ -353,17 +367,17 @@ def _peers(d, key="peer_bufs"):
 def tp_ag_rows(d, stream=0):
     rank, world, rows, cols = d["rank"], d["world"], d["rows"], d["cols"]
     bufs = [_at(p, world * rows * cols, torch.bfloat16).view(world * rows, cols) for p in _peers(d)]
-    dist.barrier()
+    dist.barrier(group=_group(d["peer_flags"]))
     for q in range(world):
         if q != rank:
             bufs[rank][q * rows:(q + 1) * rows] = bufs[q][q * rows:(q + 1) * rows]
-    dist.barrier()
+    dist.barrier(group=_group(d["peer_flags"]))
 
 
 def tp_rs_rows(d, stream=0):
     rank, world, rows, cols = d["rank"], d["world"], d["rows"], d["cols"]
     bufs = [_at(p, world * rows * cols, torch.bfloat16).view(world * rows, cols) for p in _peers(d)]
-    dist.barrier()
+    dist.barrier(group=_group(d["peer_flags"]))
     acc = torch.zeros(rows, cols)
     for q in range(world):
         acc += bufs[q][rank * rows:(rank + 1) * rows].float()
@@ -375,7 +389,7 @@ def tp_rs_rows(d, stream=0):
         _at(d["out_f32"], rows * cols, torch.float32).view(rows, cols).copy_(acc)
     if d.get("out_bf16"):
         _at(d["out_bf16"], rows * cols, torch.bfloat16).view(rows, cols).copy_(acc)
-    dist.barrier()
+    dist.barrier(group=_group(d["peer_flags"]))
 
 
 def tp_embed_fwd(d, stream=0):
@@ -384,12 +398,12 @@ def tp_embed_fwd(d, stream=0):
     idx = _at(d["idx"], world * rows, torch.int64)
     wpe = _at(d["wpe"], T * cols, torch.bfloat16).view(T, cols)
     out = _at(d["out_f32"], rows * cols, torch.float32).view(rows, cols)
-    dist.barrier()
+    dist.barrier(group=_group(d["peer_flags"]))
     for i in range(rows):
         m = rank * rows + i
         tok = int(idx[m])
         out[i] = tables[tok // vpr][tok % vpr].float() + wpe[m % T].float()
-    dist.barrier()
+    dist.barrier(group=_group(d["peer_flags"]))
 
 
 def tp_embed_bwd(d, stream=0):
@@ -398,7 +412,7 @@ def tp_embed_bwd(d, stream=0):
     idx = _at(d["idx"], world * rows, torch.int64)
     dx = _at(d["resid"], rows * cols, torch.float32).view(rows, cols)
     wpe_g = _at(d["out_f32"], T * cols, torch.float32).view(T, cols)
-    dist.barrier()
+    dist.barrier(group=_group(d["peer_flags"]))
     for r in range(world):          # one rank at a time: the kernel's atomics
         if r == rank:
             for i in range(rows):
@@ -406,7 +420,7 @@ def tp_embed_bwd(d, stream=0):
                 tok = int(idx[m])
                 grads[tok // vpr][tok % vpr] += dx[i]
                 wpe_g[m % T] += dx[i]
-        dist.barrier()
+        dist.barrier(group=_group(d["peer_flags"]))
 
 
 def tp_ce_stats(d, stream=0):
@@ -433,7 +447,7 @@ def tp_ce_finish(d, stream=0):
     tgt = _at(d["idx"], rows, torch.int64)
     logits = _at(d["logits"], rows * ld, torch.bfloat16).view(rows, ld)
     loss_rows = _at(d["loss_rows"], rows, torch.float32)
-    dist.barrier()
+    dist.barrier(group=_group(d["peer_flags"]))
     S = torch.stack([s.clone() for s in stats])          # [world, rows, 4]
     gm = S[:, :, 0].max(0).values
     lse = gm + torch.log((S[:, :, 1] * torch.exp(S[:, :, 0] - gm)).sum(0))
@@ -447,7 +461,7 @@ def tp_ce_finish(d, stream=0):
     g[ignore] = 0.0
     logits[:, :vv] = g.to(torch.bfloat16)
     logits[:, vv:] = 0
-    dist.barrier()
+    dist.barrier(group=_group(d["peer_flags"]))
 
 
 def loss_reduce(loss_rows, targets, M, out, stream=0):
@@ -486,7 +500,7 @@ def zero_rs(d, stream=0):
     grads = [_at(p, ext, torch.float32) for p in _ptr_list(d["peer_grad"], world)]
     b = d["bucket"]
     f0, n, off = _zero_slice(tab[b], rank)
-    dist.barrier()
+    dist.barrier(group=_group(d["peer_flags"]))
     parts = (_at(d["sumsq_parts"], d["nb"] * d["rs_blocks"], torch.float32) if d.get("sumsq_parts")
              else None)
     if parts is not None:
@@ -500,7 +514,7 @@ def zero_rs(d, stream=0):
         if parts is not None:
             parts[b * d["rs_blocks"]] = (acc * acc).sum()
     _bump(d.get("byte_counter"), (tab[b][1] - tab[b][0]) * 4)
-    dist.barrier()
+    dist.barrier(group=_group(d["peer_flags"]))
 
 
 def zero_adamw_ag(d, nblocks, stream=0):
@@ -512,7 +526,7 @@ def zero_adamw_ag(d, nblocks, stream=0):
     shard = max(off + s for (_, _, s, off) in tab)
     local = _at(d["sumsq_parts"], d["nb"] * d["rs_blocks"], torch.float32).sum().reshape(1)
     allss = [torch.zeros(1) for _ in range(world)]
-    dist.all_gather(allss, local)
+    dist.all_gather(allss, local, group=_group(d["peer_flags"]))
     norm = math.sqrt(float(sum(float(x) for x in allss)))
     clip = min(d["max_norm"] / (norm + 1e-6), 1.0) if d["max_norm"] > 0 else 1.0
     if d.get("norm_out"):
@@ -522,7 +536,7 @@ def zero_adamw_ag(d, nblocks, stream=0):
     m, v = _at(d["exp_avg"], shard, torch.float32), _at(d["exp_avg_sq"], shard, torch.float32)
     ranges = _at(d["decay_ranges"], 2 * d["nr"], torch.int64).tolist() if d["nr"] else []
     shadows = [_at(p, ext, torch.bfloat16) for p in _ptr_list(d["peer_shadow"], world)]
-    dist.barrier()
+    dist.barrier(group=_group(d["peer_flags"]))
     for row in tab:
         f0, n, off = _zero_slice(row, rank)
         if not n:
@@ -543,19 +557,19 @@ def zero_adamw_ag(d, nblocks, stream=0):
         for r in range(world):
             shadows[r][f0:f0 + n] = master[sl].to(torch.bfloat16)
     _bump(d.get("byte_counter"), sum(r[1] - r[0] for r in tab) * 2 + 4)
-    dist.barrier()
+    dist.barrier(group=_group(d["peer_flags"]))
 
 
 def zero_ag(d, nblocks, stream=0):
     world, span, slc, off = d["world"], d["ag_span"], d["ag_slice"], d["ag_offset"]
     shards = [_at(p + off * 2, slc, torch.bfloat16) for p in _ptr_list(d["peer_shard"], world)]
     dst = _at(d["gather_dst"], span, torch.bfloat16)
-    dist.barrier()
+    dist.barrier(group=_group(d["peer_flags"]))
     for e0 in range(0, span, slc):
         n = min(slc, span - e0)
         dst[e0:e0 + n] = shards[e0 // slc][:n]
     _bump(d.get("byte_counter"), span * 2)
-    dist.barrier()
+    dist.barrier(group=_group(d["peer_flags"]))
 
 
 class _Stream:

@@ -278,3 +278,40 @@ def test_native_zero_matches_full_batch_step(strategy, world):
         assert r["max_diff"] <= 2.5 * r["lr"] and r["mean_diff"] < 1e-2 * r["lr"], r
         if r["norm"] is not None:
             assert abs(r["norm"] - r["ref_norm"]) < 1e-4 * r["ref_norm"], r
+
+
+def _launch_worker(rank, world, strategy, tmp, extra_args):
+    import native_fake as nf
+    from gpt2_harness_b200 import launch
+
+    nf.install_in_process()
+    tiny = '{"vocab_size": 256, "n_positions": 64, "n_layer": 4, "n_head": 2, "n_embd": 128}'
+    base = ["--model", "gpt2", "--config", tiny, "--batch", "2", "--seq", "64", "--warmup", "1",
+            "--lr", "1e-3", "--strategy", strategy, *extra_args]
+
+    def run(ckpt, every, stop_at=0):
+        launch.LOSSES = []
+        launch.main([*base, "--steps", "6", "--ckpt-dir", ckpt, "--ckpt-every", str(every),
+                     "--stop-at", str(stop_at)], device="cpu")
+        return list(launch.LOSSES)
+
+    whole = run(f"{tmp}/a", 100)
+    first = run(f"{tmp}/b", 2, stop_at=4)   # pre-empted after step 4
+    rest = run(f"{tmp}/b", 100)             # resumes from the step-4 checkpoint
+    return {"whole": whole, "first": first, "rest": rest}
+
+
+@pytest.mark.parametrize("strategy,world,extra", [
+    ("pp", 2, ["--micro-batches", "2"]),
+    ("pp", 4, ["--micro-batches", "2", "--cp", "2", "--seq", "512"]),
+    ("cp", 2, ["--seq", "512"]),
+])
+def test_launch_resume_reproduces_the_uninterrupted_run(tmp_path, strategy, world, extra):
+    res = spawn_workers(_launch_worker, world,
+                        {"strategy": strategy, "tmp": str(tmp_path), "extra_args": extra},
+                        backend="gloo", timeout=600)
+    for r in (x.value for x in res):
+        assert len(r["whole"]) == 6 and len(r["first"]) == 4 and len(r["rest"]) == 2
+        assert r["first"] == r["whole"][:4]
+        assert r["rest"] == r["whole"][4:], r
+        assert r["whole"][-1] < r["whole"][0]
