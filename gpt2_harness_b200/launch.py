@@ -14,8 +14,9 @@ atomically. ``SIGUSR1`` / ``SIGTERM`` (the pre-emption warning of most
 schedulers) trigger a checkpoint at the next step boundary, then a clean exit.
 
 Strategies: ``ddp`` / ``zero2`` / ``zero3`` (each rank reads its own shard of
-the token stream, ``--batch`` per GPU); ``cp`` (context parallelism: every
-rank reads the same ``--batch`` sequences and computes its part of each);
+the token stream, ``--batch`` per GPU); ``tp`` (tensor + sequence
+parallelism) and ``cp`` (context parallelism): every rank reads the same
+``--batch`` sequences;
 ``pp`` (pipeline x context parallelism over a ``--pp`` x ``--cp`` mesh: every
 rank reads the same ``--micro-batches`` x ``--batch`` sequences per step). A
 pipeline checkpoint holds the full model with the untied ``lm_head.weight``
@@ -98,6 +99,25 @@ def _pipeline_checkpoint(trainer: "PipelineTrainer", world: int) -> tuple[dict, 
     return model, {"step": parts[0]["optim"]["step"], "exp_avg": ea, "exp_avg_sq": eq}
 
 
+def _load_tp(engine, full: dict, extra: dict) -> None:
+    """Restore a tensor-parallel engine from a full-model checkpoint (and the
+    AdamW moments a tensor-parallel checkpoint carries)."""
+    from .models.engine import ParamLayout
+
+    layout = ParamLayout(engine.config)
+
+    def flat(named):
+        v = torch.zeros(layout.total, dtype=torch.float32, device=engine.device)
+        for s in layout.specs:
+            layout.view(v, s.name).copy_(named[s.name].to(v.device, torch.float32).view(s.shape))
+        return v
+
+    m = extra.get("tp_exp_avg")
+    engine.load_full(layout, flat(full), flat(m) if m else None,
+                     flat(extra["tp_exp_avg_sq"]) if m else None)
+    engine.step_count = int(extra.get("optim_step", engine.step_count))
+
+
 def main(argv=None, device: Optional[torch.device] = None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--model", default="gpt2")
@@ -111,7 +131,7 @@ def main(argv=None, device: Optional[torch.device] = None) -> int:
     ap.add_argument("--ckpt-dir", default=None)
     ap.add_argument("--ckpt-every", type=int, default=500)
     ap.add_argument("--log", default=None, help="JSONL metrics (rank 0)")
-    ap.add_argument("--strategy", choices=["ddp", "zero2", "zero3", "cp", "pp"], default="ddp")
+    ap.add_argument("--strategy", choices=["ddp", "zero2", "zero3", "tp", "cp", "pp"], default="ddp")
     ap.add_argument("--pp", type=int, default=0, help="pipeline stages (pp; default WORLD_SIZE / --cp)")
     ap.add_argument("--cp", type=int, default=1, help="context-parallel ranks per stage (pp)")
     ap.add_argument("--micro-batches", type=int, default=8, help="micro-batches per step (pp)")
@@ -159,7 +179,7 @@ def main(argv=None, device: Optional[torch.device] = None) -> int:
                           strategy=a.strategy, cp_balance=a.cp_balance)
     # data-parallel ranks read disjoint shards of the stream; the ranks of a
     # context-parallel group or a pipeline all read the same sequences
-    shared = a.strategy in ("cp", "pp")
+    shared = a.strategy in ("tp", "cp", "pp")
     s_rank, s_world = (0, 1) if shared else (rank, world)
     rows = a.micro_batches * a.batch if pipeline else a.batch
     src = TokenShardSource(a.data, a.seq) if a.data else _SyntheticTokens(cfg.vocab_size, a.seq, seed=a.seed)
@@ -170,6 +190,8 @@ def main(argv=None, device: Optional[torch.device] = None) -> int:
         (full, _), extra = load_full(ck), load_extra(ck, 0)
         if pipeline:
             trainer.load_state_dict({"model": full, "optim": extra.get("pipeline_optim")})
+        elif a.strategy == "tp":
+            _load_tp(trainer.engine, full, extra)
         else:
             zero = trainer.ddp if trainer.strategy in ("zero2", "zero3") else None
             load_into_engine(trainer.engine, {k: v.to(dev) for k, v in full.items()}, extra, zero=zero)
@@ -204,6 +226,17 @@ def main(argv=None, device: Optional[torch.device] = None) -> int:
                 if rank == 0:
                     extra = {"step": step, "stream": stream.state_dict([stream.position]),
                              "pipeline_optim": popt, "optim_step": popt["step"]}
+                    ckpt.save(Path(a.ckpt_dir) / f"step_{step}", sd, plan={}, rank=0, world_size=1, step=step,
+                              global_shapes={k: list(v.shape) for k, v in sd.items()}, extra=extra)
+                if world > 1:
+                    dist.barrier()
+            elif due and a.strategy == "tp":
+                st = trainer.state_dict()          # collective: every rank gathers the shards
+                if rank == 0:
+                    extra = {"step": step, "stream": stream.state_dict([stream.position]),
+                             "optim_step": st["optim_step"], "tp_exp_avg": st["exp_avg"],
+                             "tp_exp_avg_sq": st["exp_avg_sq"]}
+                    sd = st["model"]
                     ckpt.save(Path(a.ckpt_dir) / f"step_{step}", sd, plan={}, rank=0, world_size=1, step=step,
                               global_shapes={k: list(v.shape) for k, v in sd.items()}, extra=extra)
                 if world > 1:

@@ -273,6 +273,9 @@ class TPEngine:
         self.init_weights(seed)
 
     # ----------------------------------------------------------- weights --
+    def set_lr(self, lr: float) -> None:
+        self.optim.lr = lr
+
     def p16(self, name: str) -> torch.Tensor:
         return self.lay.view(self.shadow, name)
 
@@ -280,11 +283,15 @@ class TPEngine:
         return self.lay.view(self.grad, name)
 
     @torch.no_grad()
-    def load_full(self, full_layout: ParamLayout, full: torch.Tensor) -> None:
-        """Take this rank's pieces of a full flat fp32 vector in the
-        single-GPU engine layout."""
-        for name in self.lay.specs:
-            self.lay.view(self.master, name).copy_(self.lay.shard_of(name, full_layout.view(full, name)))
+    def load_full(self, full_layout: ParamLayout, full: torch.Tensor, exp_avg: Optional[torch.Tensor] = None,
+                  exp_avg_sq: Optional[torch.Tensor] = None) -> None:
+        """Take this rank's pieces of full flat fp32 vectors in the
+        single-GPU engine layout (weights, and optionally the AdamW moments)."""
+        for dst, src in ((self.master, full), (self.exp_avg, exp_avg), (self.exp_avg_sq, exp_avg_sq)):
+            if src is None:
+                continue
+            for name in self.lay.specs:
+                self.lay.view(dst, name).copy_(self.lay.shard_of(name, full_layout.view(src, name)))
         self.shadow.copy_(self.master)
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
