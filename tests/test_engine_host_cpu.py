@@ -304,6 +304,9 @@ def _launch_worker(rank, world, strategy, tmp, extra_args):
 
 
 @pytest.mark.parametrize("strategy,world,extra", [
+    ("ddp", 2, []),
+    ("zero2", 2, []),
+    ("zero3", 2, []),
     ("pp", 2, ["--micro-batches", "2"]),
     ("pp", 4, ["--micro-batches", "2", "--cp", "2", "--seq", "512"]),
     ("cp", 2, ["--seq", "512"]),
