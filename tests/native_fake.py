@@ -191,6 +191,38 @@ def attention_bwd(q, k, v, o, dout, dq, dk, dv, lse, delta, B, H, Tq, Tk=None, q
         dv[b * kr: b * kr + Tk].copy_(gv.reshape(Tk, H * 64))
 
 
+# ------------------------------------------------------------------ decode --
+def decode_embed(tok, lens, wte, wpe, x):
+    x.copy_(wte.float()[tok] + wpe.float()[lens.long()])
+
+
+def decode_partials(B, H, Tmax, device):
+    return torch.empty(1, device=device), torch.empty(1, device=device)
+
+
+def decode_attn(qkv, k_cache, v_cache, lens, part_o, part_ml, out, H, Hkv, scale=None):
+    """Append this step's k/v at lens[b], then attend over positions 0..lens[b]."""
+    scale = 1.0 / 8.0 if scale is None else scale
+    rep = H // Hkv
+    for b in range(qkv.shape[0]):
+        pos = int(lens[b])
+        q = qkv[b, :H * 64].float().view(H, 64)
+        k_cache[b, :, pos] = qkv[b, H * 64:(H + Hkv) * 64].view(Hkv, 64)
+        v_cache[b, :, pos] = qkv[b, (H + Hkv) * 64:(H + 2 * Hkv) * 64].view(Hkv, 64)
+        K = k_cache[b, :, :pos + 1].float().repeat_interleave(rep, 0)
+        V = v_cache[b, :, :pos + 1].float().repeat_interleave(rep, 0)
+        p = torch.softmax(torch.einsum("hd,htd->ht", q, K) * scale, -1)
+        out[b, :H * 64] = torch.einsum("ht,htd->hd", p, V).reshape(-1)
+
+
+def decode_argmax(logits, vocab, tok, lens, hist):
+    a = logits[:, :vocab].float().argmax(-1)
+    tok.copy_(a)
+    for b in range(logits.shape[0]):
+        hist[b, int(lens[b]) + 1] = a[b]
+    lens += 1
+
+
 def grad_sumsq(g, ws, out):
     out[0] = g.double().pow(2).sum().float()
 
@@ -607,7 +639,8 @@ OPS = {
     "embedding_fwd": embedding_fwd, "embedding_bwd": embedding_bwd,
     "cross_entropy_fwd_bwd": cross_entropy_fwd_bwd, "attention_fwd": attention_fwd,
     "attention_bwd": attention_bwd, "grad_sumsq": grad_sumsq, "clip_coef": clip_coef,
-    "adamw_step": adamw_step, "cast_f32_bf16": cast_f32_bf16,
+    "adamw_step": adamw_step, "cast_f32_bf16": cast_f32_bf16, "decode_embed": decode_embed,
+    "decode_partials": decode_partials, "decode_attn": decode_attn, "decode_argmax": decode_argmax,
 }
 
 LIB = SimpleNamespace(zero_rs=zero_rs, zero_adamw_ag=zero_adamw_ag, zero_ag=zero_ag,

@@ -321,3 +321,42 @@ def test_launch_resume_reproduces_the_uninterrupted_run(tmp_path, strategy, worl
         assert r["first"] == r["whole"][:4]
         assert r["rest"] == r["whole"][4:], r
         assert all(math.isfinite(x) for x in r["whole"])
+
+
+# ------------------------------------------------------------------ decode --
+def _decode_model(n_kv_head=None, **kw):
+    from gpt2_harness_b200.models.gpt import GPT
+
+    torch.manual_seed(0)
+    return GPT(GPTConfig(**{**dict(vocab_size=96, n_positions=160, n_layer=2, n_head=4, n_embd=256,
+                                   n_kv_head=n_kv_head), **kw})).eval()
+
+
+@pytest.mark.parametrize("n_kv_head", [None, 2, 1])
+def test_decode_engine_teacher_forced_logits(monkeypatch, n_kv_head):
+    from gpt2_harness_b200.inference.decode import DecodeEngine
+
+    with native_fake.installed(monkeypatch):
+        m = _decode_model(n_kv_head)
+        toks = torch.randint(0, 96, (2, 40))
+        eng = DecodeEngine.from_model(m, batch=2, device="cpu")
+        got = eng.forced_logits(toks)
+        with torch.no_grad():
+            ref = m(toks)["logits"]
+        assert (got - ref).abs().max() < 3e-2
+
+
+def test_decode_engine_greedy_follows_the_oracle(monkeypatch):
+    from gpt2_harness_b200.inference.decode import DecodeEngine
+
+    with native_fake.installed(monkeypatch):
+        m = _decode_model()
+        prompt = torch.randint(0, 96, (2, 7))
+        out = DecodeEngine.from_model(m, batch=2, device="cpu").generate(prompt, 20)
+        assert out.shape == (2, 27) and torch.equal(out[:, :7], prompt)
+        with torch.no_grad():
+            logits = m(out[:, :-1])["logits"][:, 6:]
+        top2 = logits.topk(2, -1).values
+        chosen = logits.gather(-1, out[:, 7:, None])[..., 0]
+        # every generated token is the oracle's argmax up to bf16 ties
+        assert torch.all(top2[..., 0] - chosen < 3e-2)
