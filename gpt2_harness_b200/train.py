@@ -167,8 +167,9 @@ def train(model_config: GPTConfig, train_config: TrainConfig, dataset: TokenData
 
 
 def _train_native(mcfg, cfg, dataset, device, train_gen, eval_seed, progress):
+    from .models import engine as engine_mod
     from .models.engine import Engine, OptimConfig
-    if device.type != "cuda":
+    if device.type not in engine_mod.DEVICE_TYPES:
         raise RuntimeError("the native backend needs a CUDA device")
     eng = Engine(mcfg, device, optim=OptimConfig(lr=cfg.lr, betas=tuple(cfg.betas), eps=cfg.eps,
                                                  weight_decay=cfg.weight_decay, grad_clip=cfg.grad_clip),

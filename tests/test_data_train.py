@@ -98,3 +98,19 @@ def test_native_training_learns(corpus):
     eng, r = train(m, t, ds, device="cuda", backend="native")
     assert not r.diverged and r.history[-1]["val_loss"] < math.log(tok.vocab_size) - 1.0
     assert len(r.grad_norms) == 60 and all(math.isfinite(g) for g in r.grad_norms)
+
+
+def test_native_training_loop_on_cpu(corpus, monkeypatch):
+    """The native backend's loop (grad accumulation, LR schedule, clipping,
+    evaluation) on the torch versions of the kernel contracts."""
+    import native_fake
+
+    text, tok = corpus
+    ds = TokenDataset(encode_corpus(tok, text, cache=False), 64)
+    m = GPTConfig(vocab_size=tok.vocab_size, n_positions=64, n_layer=2, n_head=2, n_embd=128)
+    t = TrainConfig(steps=30, batch_size=4, block_size=64, lr=2e-3, warmup_steps=3, eval_interval=15,
+                    eval_batches=2, grad_accum=2)
+    with native_fake.installed(monkeypatch):
+        eng, r = train(m, t, ds, device="cpu", backend="native")
+    assert not r.diverged and len(r.grad_norms) == 30 and all(math.isfinite(g) for g in r.grad_norms)
+    assert r.history[-1]["val_loss"] < r.history[0]["val_loss"]
