@@ -376,6 +376,8 @@ class TPEngine:
                        wpe=p("wpe.weight").data_ptr(), T=T, vocab_per_rank=lay.Vl,
                        out_f32=self.x[0].data_ptr())
         d["peer_bufs"] = self._offset_ptrs(self._p16, wte_off).data_ptr()
+        # each rank receives its rows' token embeddings from their owners
+        comms.record_external("all_to_all", self.Ms * C, self.Ms * C * 2)
         N.lib().tp_embed_fwd(d, self._stream())
         for l in range(NL):
             pre = f"h.{l}."
@@ -408,6 +410,8 @@ class TPEngine:
         d = self._args(self._stats, rows=self.M, logits=self.logits.data_ptr(), ld=self.ld,
                        vocab_valid=lay.vocab_valid, vocab_start=lay.v0, idx=self._targets.data_ptr(),
                        loss_rows=self.loss_rows.data_ptr())
+        # every rank reads every peer's [M, 4] row statistics (max, sum, target)
+        comms.record_external("all_gather", self.world * self.M * 4, self.world * self.M * 4 * 4)
         L.tp_ce_finish(d, self._stream())
         L.loss_reduce(self.loss_rows.data_ptr(), self._targets.data_ptr(), self.M,
                       self.loss_out.data_ptr(), self._stream())
@@ -475,6 +479,8 @@ class TPEngine:
         d = self._args(self._g32, rows=self.Ms, cols=C, idx=self._idx.data_ptr(), T=T,
                        vocab_per_rank=lay.Vl, resid=self.dres.data_ptr(), out_f32=wpe_g.data_ptr())
         d["peer_bufs"] = self._offset_ptrs(self._g32, wte_off).data_ptr()
+        # each rank pushes its rows' fp32 gradients to the embedding owners
+        comms.record_external("all_to_all", self.Ms * C, self.Ms * C * 4)
         N.lib().tp_embed_bwd(d, self._stream())
         # replicated parameters: sum the per-rank partial gradients
         n = lay.repl_hi

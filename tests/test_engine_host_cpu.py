@@ -122,8 +122,13 @@ def _cp_worker(rank, world, balance):
     tgt = torch.randint(0, CFG["vocab_size"], (B, T), generator=g)
     il = cp.local_tokens(idx, torch.empty(B, T // world, dtype=torch.int64))
     tl = cp.local_tokens(tgt, torch.empty(B, T // world, dtype=torch.int64))
-    loss = eng.forward(il, tl).clone()
-    eng.backward(il)
+    from gpt2_harness_b200.parallel import comms
+
+    with comms.counter_scope(world) as ctr:
+        loss = eng.forward(il, tl).clone()
+        eng.backward(il)
+        ctr.steps += 1
+        payload = ctr.summary()["payload_bytes_per_step"]
     dist.all_reduce(eng.grad)
     eng.grad /= world
     dist.all_reduce(loss)
@@ -133,8 +138,11 @@ def _cp_worker(rank, world, balance):
     errs = {s.name: float((eng.g32(s.name) - ref.g32(s.name)).norm() / (ref.g32(s.name).norm() + 1e-12))
             for s in ref.layout.specs}
     cp.close()
+    # the reference convention: per layer the gather is charged its output and
+    # the reduce-scatter its input, 2 x B x T x C bf16 each (K and V)
+    closed = cfg.n_layer * 2 * (2 * B * T * cfg.n_embd * 2)
     return {"loss": float(loss) / world, "ref_loss": ref_loss, "worst": max(errs.values()),
-            "worst_name": max(errs, key=errs.get)}
+            "worst_name": max(errs, key=errs.get), "payload": payload, "closed_form": closed}
 
 
 @pytest.mark.parametrize("world,balance", [(2, "contiguous"), (2, "zigzag"), (4, "zigzag")])
@@ -144,6 +152,7 @@ def test_context_parallel_matches_full_sequence(world, balance):
         assert abs(r["loss"] - r["ref_loss"]) < 1e-4 * r["ref_loss"], r
         # bf16 rounding of the summed dK/dV partials is the only difference
         assert r["worst"] < 1e-2, r
+        assert r["payload"] == r["closed_form"], r
 
 
 def _ddp_worker(rank, world, bucket_mb):
@@ -194,6 +203,8 @@ def test_native_ddp_matches_full_batch(world, bucket_mb):
 
 
 def _tp_worker(rank, world):
+    import math
+
     import native_fake as nf
     from gpt2_harness_b200.config import GPTConfig
     from gpt2_harness_b200.models.engine import Engine, OptimConfig
@@ -218,8 +229,14 @@ def _tp_worker(rank, world):
     ref.backward(idx)
     grads = tp.full_state("grad")
     errs = {n: float((gv - ref.g32(n)).norm() / (ref.g32(n).norm() + 1e-12)) for n, gv in grads.items()}
+    # closed form: 4L+1 row all-gathers and 4L+1 reduce-scatters of [M, C] bf16,
+    # the embedding rows in (bf16) and their gradients out (fp32), the [M, 4]
+    # statistics of every rank, and one all-reduce of the replicated tensors
+    M, C, L = B * T, cfg.n_embd, cfg.n_layer
+    repl = sum(math.prod(shape) for off, shape, _ in tp.lay.specs.values() if off < tp.lay.repl_hi)
+    closed = (8 * L + 2) * M * C * 2 + (M // world) * C * (2 + 4) + world * M * 16 + repl * 4
     return {"loss": loss, "ref_loss": ref_loss, "worst": max(errs.values()),
-            "worst_name": max(errs, key=errs.get), "payload": payload}
+            "worst_name": max(errs, key=errs.get), "payload": payload, "closed_form": closed}
 
 
 @pytest.mark.parametrize("world", [2, 3])
@@ -229,6 +246,7 @@ def test_tensor_parallel_matches_single_engine(world):
         assert abs(r["loss"] - r["ref_loss"]) < 1e-3 * r["ref_loss"], r
         # row-parallel partials are rounded to bf16 before the reduction
         assert r["worst"] < 2e-2, r
+        assert r["payload"] == r["closed_form"], r
 
 
 def _zero_worker(rank, world, strategy):
