@@ -266,9 +266,23 @@ def _zero_worker(rank, world, strategy):
     idx = torch.randint(0, CFG["vocab_size"], (B * world, T), generator=g)
     tgt = torch.randint(0, CFG["vocab_size"], (B * world, T), generator=g)
     sl = slice(rank * B, (rank + 1) * B)
-    loss = tr.step_async(idx[sl], tgt[sl]).clone()
+    from gpt2_harness_b200.parallel import comms
+
+    with comms.counter_scope(world) as ctr:
+        loss = tr.step_async(idx[sl], tgt[sl]).clone()
+        ctr.steps += 1
+        payload = ctr.summary()["payload_bytes_per_step"]
     dist.all_reduce(loss)
-    out = {"loss": float(loss) / world}
+    lay = tr.engine.layout
+    if strategy == "zero2":
+        # fp32 reduce-scatter + bf16 all-gather of the padded flat vector + the 4-byte norm
+        closed = lay.total * 4 + lay.total * 2 + 4
+    else:
+        # per unit: two bf16 gathers and one fp32 reduce-scatter of its span;
+        # root tensors all-reduced one by one in fp32; the 4-byte norm
+        closed = sum(2 * 2 * u["span"] + 4 * u["span"] for u in tr.ddp.units)
+        closed += sum(s.numel * 4 for s in lay.specs if s.group == "root") + 4
+    out = {"loss": float(loss) / world, "payload": payload, "closed_form": closed}
     if strategy == "zero2":
         full_grad = tr.ddp.gather_full(tr.ddp.gsh)
     full = tr.ddp.full_master()
@@ -298,6 +312,9 @@ def test_native_zero_matches_full_batch_step(strategy, world):
         assert r["max_diff"] <= 2.5 * r["lr"] and r["mean_diff"] < 1e-2 * r["lr"], r
         if r["norm"] is not None:
             assert abs(r["norm"] - r["ref_norm"]) < 1e-4 * r["ref_norm"], r
+        assert r["payload"] == r["closed_form"], r
+        if strategy == "zero2":
+            assert r["device_bytes"] == r["payload"], r
 
 
 def _launch_worker(rank, world, strategy, tmp, extra_args):
