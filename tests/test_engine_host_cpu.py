@@ -66,7 +66,16 @@ def _pp_worker(rank, world, schedule, m):
     tr = PipelineTrainer(cfg, B, T, m, pp=world, schedule=schedule, device="cpu", seed=0)
     st = tr.engine
     idx, tgt = _batches(m, B, T)
-    loss = tr.step_async(torch.cat(idx), torch.cat(tgt))
+    from gpt2_harness_b200.parallel import comms
+    from gpt2_harness_b200.parallel.pipeline_parallel import pipeline_payload_bytes
+
+    with comms.counter_scope(world) as ctr:
+        loss = tr.step_async(torch.cat(idx), torch.cat(tgt))
+        ctr.steps += 1
+        sends = ctr.summary()["per_collective"].get("send", {}).get("payload_bytes", 0)
+    per_dir = pipeline_payload_bytes(m, B, T, CFG["n_embd"])
+    ends = int(st.lay.first) + int(st.lay.last)
+    want_sends = 0 if world == 1 else per_dir * (2 - ends)
     ref = Engine(cfg, "cpu", seed=0)
     ref_losses = []
     for i in range(m):
@@ -84,7 +93,7 @@ def _pp_worker(rank, world, schedule, m):
         r = ref.g32("wte.weight") / m
         errs["wte+lm_head"] = float((st.g32("wte.weight") + head - r).norm() / r.norm())
     return {"last": st.lay.last, "loss": float(loss), "ref_loss": sum(ref_losses) / m,
-            "worst": max(errs.values()), "slots": len(st.slots)}
+            "worst": max(errs.values()), "slots": len(st.slots), "sends": sends, "want_sends": want_sends}
 
 
 @pytest.mark.parametrize("world,schedule,m", [(1, "1f1b", 4), (2, "1f1b", 4), (2, "gpipe", 2),
@@ -96,6 +105,8 @@ def test_pipeline_matches_accumulated_engine(world, schedule, m):
     # copy of the received gradient (the engine from the fp32 one), ~1e-3.
     for r in (x.value for x in res):
         assert r["worst"] < 5e-3, r
+        # m activations forward and m gradients back per boundary, fp32
+        assert r["sends"] == r["want_sends"], r
         if r["last"]:
             assert abs(r["loss"] - r["ref_loss"]) < 1e-5 * r["ref_loss"], r
     slots = [x.value["slots"] for x in sorted(res, key=lambda x: x.rank)]
