@@ -40,8 +40,24 @@ def _gelu_grad(z):
     return 0.5 * (1 + t) + 0.5 * z * (1 - t * t) * _SQRT_2_OVER_PI * (1 + 3 * 0.044715 * z * z)
 
 
+def _require(ok, what):
+    """The launchers' host-side preconditions (a violation is a host bug the
+    real kernel would reject)."""
+    if not ok:
+        raise AssertionError(f"native precondition violated: {what}")
+
+
+def _row_bytes_ok(t, esz):
+    return t.dim() == 2 and t.stride(1) == 1 and (t.stride(0) * esz) % 16 == 0 and t.data_ptr() % 16 == 0
+
+
 def gemm(a, b, out, *, a_t=False, b_t=False, epilogue=N.EPI_BF16, bias=None, aux=None, alpha=1.0,
          alpha_ptr=None, accumulate=False, splits=1, workspace=None, bn=256, max_ctas=0):
+    # operand loads are TMA: 16-byte aligned bases and row strides (csrc/gemm.cu)
+    _require(a.dtype == torch.bfloat16 and b.dtype == torch.bfloat16, "gemm operands bf16")
+    _require(_row_bytes_ok(a, 2) and _row_bytes_ok(b, 2), "gemm operand alignment")
+    _require(bn in (128, 256), "gemm tile width")
+    _require(splits <= 1 or epilogue == N.EPI_F32, "split-K needs the fp32 epilogue")
     A = (a.t() if a_t else a).float()
     Bm = (b.t() if b_t else b).float()
     r = A @ Bm.t() * alpha
@@ -69,6 +85,7 @@ def gemm(a, b, out, *, a_t=False, b_t=False, epilogue=N.EPI_BF16, bias=None, aux
 
 
 def layernorm_fwd(x, gamma, beta, y, mean, rstd, eps=1e-5):
+    _require(x.shape[-1] % 4 == 0 and x.dtype == torch.float32 and y.dtype == torch.bfloat16, "layernorm shapes")
     xf = x.float()
     mu = xf.mean(-1)
     var = ((xf - mu[:, None]) ** 2).mean(-1)
@@ -132,6 +149,7 @@ def embedding_bwd(idx, dx, wte_grad, wpe_grad, vocab, pos0=0, pos_split=None, po
 
 
 def cross_entropy_fwd_bwd(logits, targets, loss_rows, loss_out, vocab):
+    _require(_row_bytes_ok(logits, 2) and logits.shape[1] % 8 == 0, "logits rows 16-byte aligned")
     lf = logits[:, :vocab].float()
     t = targets.reshape(-1)
     valid = t != -100
@@ -235,6 +253,8 @@ def clip_coef(sumsq, max_norm, clip, norm_out=None, scale2=1.0):
 
 
 def adamw_step(p, g, m, v, p_bf16, n_decay, hp, clip=None, decay_ranges=None):
+    _require(all(t.data_ptr() % 16 == 0 for t in (p, g, m, v)), "adamw buffers 16-byte aligned")
+    _require(p_bf16 is None or p_bf16.data_ptr() % 8 == 0, "adamw bf16 copy 8-byte aligned")
     lr, b1, b2, eps, wd, bc1, bc2s, gsc = [float(x) for x in hp[:8]]
     gs = gsc * (float(clip[0]) if clip is not None else 1.0)
     decay = torch.zeros(p.numel(), dtype=torch.bool, device=p.device)
