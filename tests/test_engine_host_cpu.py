@@ -213,18 +213,22 @@ def test_native_ddp_matches_full_batch(world, bucket_mb):
         assert res[0].value["buckets"] > 1
 
 
-def _tp_worker(rank, world):
+def _tp_worker(rank, world, xl=False):
     import math
 
     import native_fake as nf
-    from gpt2_harness_b200.config import GPTConfig
+    from gpt2_harness_b200.config import GPTConfig, gpt2_config
     from gpt2_harness_b200.models.engine import Engine, OptimConfig
     from gpt2_harness_b200.parallel import comms
     from gpt2_harness_b200.parallel.tp_native import TPEngine
 
     nf.install_in_process()
-    cfg = GPTConfig(vocab_size=256, n_positions=64, n_layer=2, n_head=3, n_embd=192)  # 3 heads: uneven at p=2
-    B, T = world, 64
+    if xl:   # GPT-2 XL widths (25 heads over 8 ranks, padded vocabulary), one block
+        cfg = gpt2_config("gpt2-xl", n_layer=1, n_positions=64)
+        B, T = 1, 64
+    else:
+        cfg = GPTConfig(vocab_size=256, n_positions=64, n_layer=2, n_head=3, n_embd=192)  # uneven at p=2
+        B, T = world, 64
     tp = TPEngine(cfg, B, T, device="cpu", optim=OptimConfig(lr=1e-3), seed=0)
     ref = Engine(cfg, "cpu", optim=OptimConfig(lr=1e-3), seed=0)
     ref.fuse_bias_grad_into_ln = False
@@ -250,9 +254,9 @@ def _tp_worker(rank, world):
             "worst_name": max(errs, key=errs.get), "payload": payload, "closed_form": closed}
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_tensor_parallel_matches_single_engine(world):
-    res = spawn_workers(_tp_worker, world, {}, backend="gloo", timeout=300)
+@pytest.mark.parametrize("world,xl", [(2, False), (3, False), (8, True)])
+def test_tensor_parallel_matches_single_engine(world, xl):
+    res = spawn_workers(_tp_worker, world, {"xl": xl}, backend="gloo", timeout=600)
     for r in (x.value for x in res):
         assert abs(r["loss"] - r["ref_loss"]) < 1e-3 * r["ref_loss"], r
         # row-parallel partials are rounded to bf16 before the reduction
