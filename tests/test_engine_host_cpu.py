@@ -410,3 +410,42 @@ def test_decode_engine_greedy_follows_the_oracle(monkeypatch):
         chosen = logits.gather(-1, out[:, 7:, None])[..., 0]
         # every generated token is the oracle's argmax up to bf16 ties
         assert torch.all(top2[..., 0] - chosen < 3e-2)
+
+
+def _ppcp_worker(rank, world):
+    import torch.distributed as dist
+
+    import native_fake as nf
+    from gpt2_harness_b200.config import gpt2_config
+    from gpt2_harness_b200.models.engine import Engine
+    from gpt2_harness_b200.trainer import PipelineTrainer
+
+    nf.install_in_process()
+    # GPT-2 large widths on the BASELINE PP=4 x CP=2 mesh, one block per stage
+    cfg = gpt2_config("gpt2-large", n_layer=4, n_positions=1024)
+    B, T, m = 1, 1024, 2
+    tr = PipelineTrainer(cfg, B, T, m, pp=4, cp=2, device="cpu", seed=0)
+    st = tr.engine
+    g = torch.Generator().manual_seed(21)
+    idx = torch.randint(0, cfg.vocab_size, (m * B, T), generator=g)
+    tgt = torch.randint(0, cfg.vocab_size, (m * B, T), generator=g)
+    loss = tr.step_async(idx, tgt).reshape(1).clone()
+    dist.all_reduce(loss)
+    ref = Engine(cfg, "cpu", seed=0)
+    ref_losses = []
+    for i in range(m):
+        ref_losses.append(float(ref.forward(idx[i:i + 1], tgt[i:i + 1])))
+        ref.backward(idx[i:i + 1], accumulate=i > 0)
+    errs = {n: float((st.g32(n) - ref.g32(n) / m).norm() / (ref.g32(n).norm() / m + 1e-12))
+            for n in st.lay.specs if n not in ("wte.weight", "lm_head.weight")}
+    return {"loss": float(loss) / 2, "ref_loss": sum(ref_losses) / m, "worst": max(errs.values()),
+            "stage": tr.mesh.stage, "cp_rank": tr.mesh.cp_rank}
+
+
+@pytest.mark.slow
+def test_pipeline_x_context_parallel_at_large_widths():
+    res = spawn_workers(_ppcp_worker, 8, {}, backend="gloo", timeout=900)
+    assert sorted((r.value["stage"], r.value["cp_rank"]) for r in res) == [(s, c) for s in range(4) for c in range(2)]
+    for r in (x.value for x in res):
+        assert abs(r["loss"] - r["ref_loss"]) < 1e-3 * r["ref_loss"], r
+        assert r["worst"] < 2e-2, r
