@@ -264,16 +264,17 @@ def test_tensor_parallel_matches_single_engine(world, xl):
         assert r["payload"] == r["closed_form"], r
 
 
-def _zero_worker(rank, world, strategy):
+def _zero_worker(rank, world, strategy, medium=False):
     import torch.distributed as dist
 
     import native_fake as nf
-    from gpt2_harness_b200.config import GPTConfig, TrainConfig
+    from gpt2_harness_b200.config import GPTConfig, TrainConfig, gpt2_config
     from gpt2_harness_b200.models.engine import Engine, OptimConfig
     from gpt2_harness_b200.trainer import Trainer
 
     nf.install_in_process()
-    cfg = GPTConfig(**CFG)
+    # GPT-2 medium widths (two blocks) for the BASELINE ZeRO-3 mesh, else tiny
+    cfg = gpt2_config("gpt2-medium", n_layer=2, n_positions=64) if medium else GPTConfig(**CFG)
     B, T = 2, 32
     tc = TrainConfig()
     tr = Trainer(cfg, B, T, strategy=strategy, device="cpu")
@@ -315,9 +316,11 @@ def _zero_worker(rank, world, strategy):
     return out
 
 
-@pytest.mark.parametrize("strategy,world", [("zero2", 2), ("zero2", 4), ("zero3", 2)])
-def test_native_zero_matches_full_batch_step(strategy, world):
-    res = spawn_workers(_zero_worker, world, {"strategy": strategy}, backend="gloo", timeout=300)
+@pytest.mark.parametrize("strategy,world,medium", [("zero2", 2, False), ("zero2", 4, False),
+                                                   ("zero3", 2, False), ("zero3", 8, True)])
+def test_native_zero_matches_full_batch_step(strategy, world, medium):
+    res = spawn_workers(_zero_worker, world, {"strategy": strategy, "medium": medium}, backend="gloo",
+                        timeout=600)
     for r in (x.value for x in res):
         assert abs(r["loss"] - r["ref_loss"]) < 1e-5 * r["ref_loss"], r
         if "grad_err" in r:
