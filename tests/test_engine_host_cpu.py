@@ -204,7 +204,7 @@ def _ddp_worker(rank, world, bucket_mb, small=False):
 
 
 @pytest.mark.parametrize("world,bucket_mb,small", [(2, 0.25, False), (2, 25.0, False), (4, 0.5, False),
-                                                   (8, 25.0, True)])
+                                                   pytest.param(8, 25.0, True, marks=pytest.mark.slow)])
 def test_native_ddp_matches_full_batch(world, bucket_mb, small):
     res = spawn_workers(_ddp_worker, world, {"bucket_mb": bucket_mb, "small": small}, backend="gloo",
                         timeout=600)
@@ -261,7 +261,7 @@ def _tp_worker(rank, world, xl=False):
             "worst_name": max(errs, key=errs.get), "payload": payload, "closed_form": closed}
 
 
-@pytest.mark.parametrize("world,xl", [(2, False), (3, False), (8, True)])
+@pytest.mark.parametrize("world,xl", [(2, False), (3, False), pytest.param(8, True, marks=pytest.mark.slow)])
 def test_tensor_parallel_matches_single_engine(world, xl):
     res = spawn_workers(_tp_worker, world, {"xl": xl}, backend="gloo", timeout=600)
     for r in (x.value for x in res):
@@ -324,7 +324,8 @@ def _zero_worker(rank, world, strategy, medium=False):
 
 
 @pytest.mark.parametrize("strategy,world,medium", [("zero2", 2, False), ("zero2", 4, False),
-                                                   ("zero3", 2, False), ("zero3", 8, True)])
+                                                   ("zero3", 2, False),
+                                                   pytest.param("zero3", 8, True, marks=pytest.mark.slow)])
 def test_native_zero_matches_full_batch_step(strategy, world, medium):
     res = spawn_workers(_zero_worker, world, {"strategy": strategy, "medium": medium}, backend="gloo",
                         timeout=600)
