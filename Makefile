@@ -8,7 +8,7 @@ TORCHRUN = $(PY) -m torch.distributed.run --nnodes=1 --nproc-per-node $(NPROC) -
 
 .PHONY: help build test test-fast gpu-test verify ablate induction kv quantize prune distill \
         parallel roofline diagnose cluster collectives preflight dry-run smoke bench bench-scaling \
-        compare figures all clean
+        bench-ref baseline-ref compare figures all clean
 
 help:
 	@grep -E '^[a-z-]+:.*?## ' $(MAKEFILE_LIST) | sed 's/:.*## /\t/'
@@ -76,6 +76,16 @@ bench: ## headline benchmark, one GPU
 
 bench-scaling: ## headline benchmark on NPROC GPUs
 	$(TORCHRUN) bench.py --gpus $(NPROC)
+
+REF_SRC ?= ../reference
+baseline-ref: ## install the unmodified reference into baseline/_ref (offline, from REF_SRC)
+	rm -rf /tmp/g2b_ref_src && cp -r $(REF_SRC) /tmp/g2b_ref_src
+	$(PY) -m pip install --no-index --no-build-isolation --no-deps --find-links /opt/wheelhouse \
+	    --target baseline/_ref --upgrade /tmp/g2b_ref_src
+	test -d baseline/_ref/transformer_internals
+
+bench-ref: ## the reference arm of the headline benchmark, one GPU
+	$(PY) bench.py --impl reference
 
 compare: ## gate a results tree against the committed one
 	$(PY) -m gpt2_harness_b200.compare_results --baseline-git HEAD --current results

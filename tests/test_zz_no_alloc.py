@@ -1,6 +1,7 @@
 """The allocation-free bias-gradient entry point, called through its exported
 C symbol the way a caller that cannot allocate device memory would call it,
-against the library's regular (workspace-taking) column sum.
+against a plain PyTorch fp32 column sum and against the library's regular
+(workspace-taking) column sum.
 
 Collected last on purpose (file name), so a run that stops at the first
 failure has already run every other test."""
@@ -44,6 +45,9 @@ def test_no_alloc_bias_grad_matches_regular_entry_point():
         torch.cuda.synchronize()
         err = ((got - want).abs().max() / (want.abs().max() + 1e-6)).item()
         assert err < 1e-5, (call, err)
+        ref = dy.float().sum(0)  # fp32 reference of the same op
+        err_ref = ((got - ref).abs().max() / (ref.abs().max() + 1e-6)).item()
+        assert err_ref < 1e-5, (call, err_ref)
         # accumulate mode adds onto the existing output
         rc = f(dy.data_ptr(), dy.stride(0), M, C, got.data_ptr(), 1, stream.cuda_stream)
         assert rc == 0
