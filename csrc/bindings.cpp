@@ -60,7 +60,7 @@ PYBIND11_MODULE(_C, m) {
       [](int64_t A, int64_t lda, int a_mn, int64_t B, int64_t ldb, int b_mn, int M, int N, int K,
          int epi, int64_t out, int64_t ldo, int64_t aux, int64_t ldaux, int64_t bias, float alpha,
          int64_t alpha_ptr, int accumulate, int splits, int64_t workspace, int bn, int max_ctas,
-         int64_t err, int64_t stream) {
+         int pair, int64_t err, int64_t stream) {
         GemmArgs g;
         g.A = P<void>(A);
         g.lda = lda;
@@ -84,6 +84,7 @@ PYBIND11_MODULE(_C, m) {
         g.workspace = P<void>(workspace);
         g.bn = bn;
         g.max_ctas = max_ctas;
+        g.pair = pair;
         g.err = P<uint32_t>(err);
         check(gemm_bf16_launch(g, S(stream)), "gemm_bf16");
       });
@@ -262,6 +263,27 @@ PYBIND11_MODULE(_C, m) {
           c.nblocks = nblocks;
           c.wait_budget_ns = wait_budget_ns;
           check(comm_allreduce_launch(c, S(stream)), "allreduce_p2p");
+        });
+  m.def("allreduce_p2p_slim",
+        [](int64_t peer_bufs, int64_t peer_flags, int rank, int world, int64_t offset, int64_t n,
+           int dtype, float scale, uint32_t epoch, int64_t counter, int64_t err, int nblocks,
+           int64_t wait_budget_ns, int64_t stream) {
+          CommArgs c;
+          c.peer_bufs = P<void*>(peer_bufs);
+          c.peer_flags = P<uint32_t*>(peer_flags);
+          c.rank = rank;
+          c.world = world;
+          c.offset = offset;
+          c.n = n;
+          c.dtype = dtype;
+          c.scale = scale;
+          c.epoch = epoch;
+          c.byte_counter = P<unsigned long long>(counter);
+          c.err = P<uint32_t>(err);
+          c.nblocks = nblocks;
+          c.wait_budget_ns = wait_budget_ns;
+          c.threads = 128;
+          check(comm_allreduce_launch(c, S(stream)), "allreduce_p2p_slim");
         });
   // ZeRO-2 kernels: every argument is passed by name in a dict (int pointers,
   // ints, floats); see csrc/zero.cuh for their meaning.

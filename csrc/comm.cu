@@ -117,8 +117,8 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
   return __float2bfloat16(x);
 }
 
-template <typename T, int W>
-__global__ void __launch_bounds__(512) allreduce_p2p_kernel(const CommArgs a) {
+template <typename T, int W, int NT>
+__global__ void __launch_bounds__(NT, NT == 128 ? 6 : 1) allreduce_p2p_kernel(const CommArgs a) {
   __shared__ int fail;
   if (threadIdx.x == 0) fail = 0;
   __syncthreads();
@@ -189,18 +189,26 @@ __global__ void __launch_bounds__(512) allreduce_p2p_kernel(const CommArgs a) {
   handshake(a, 1, &fail);
 }
 
+template <typename T, int NT>
+void launch_allreduce_nt(const CommArgs& a, cudaStream_t s) {
+  switch (a.world) {
+    case 1: allreduce_p2p_kernel<T, 1, NT><<<a.nblocks, NT, 0, s>>>(a); break;
+    case 2: allreduce_p2p_kernel<T, 2, NT><<<a.nblocks, NT, 0, s>>>(a); break;
+    case 3: allreduce_p2p_kernel<T, 3, NT><<<a.nblocks, NT, 0, s>>>(a); break;
+    case 4: allreduce_p2p_kernel<T, 4, NT><<<a.nblocks, NT, 0, s>>>(a); break;
+    case 5: allreduce_p2p_kernel<T, 5, NT><<<a.nblocks, NT, 0, s>>>(a); break;
+    case 6: allreduce_p2p_kernel<T, 6, NT><<<a.nblocks, NT, 0, s>>>(a); break;
+    case 7: allreduce_p2p_kernel<T, 7, NT><<<a.nblocks, NT, 0, s>>>(a); break;
+    default: allreduce_p2p_kernel<T, 8, NT><<<a.nblocks, NT, 0, s>>>(a); break;
+  }
+}
+
 template <typename T>
 void launch_allreduce(const CommArgs& a, cudaStream_t s) {
-  switch (a.world) {
-    case 1: allreduce_p2p_kernel<T, 1><<<a.nblocks, 512, 0, s>>>(a); break;
-    case 2: allreduce_p2p_kernel<T, 2><<<a.nblocks, 512, 0, s>>>(a); break;
-    case 3: allreduce_p2p_kernel<T, 3><<<a.nblocks, 512, 0, s>>>(a); break;
-    case 4: allreduce_p2p_kernel<T, 4><<<a.nblocks, 512, 0, s>>>(a); break;
-    case 5: allreduce_p2p_kernel<T, 5><<<a.nblocks, 512, 0, s>>>(a); break;
-    case 6: allreduce_p2p_kernel<T, 6><<<a.nblocks, 512, 0, s>>>(a); break;
-    case 7: allreduce_p2p_kernel<T, 7><<<a.nblocks, 512, 0, s>>>(a); break;
-    default: allreduce_p2p_kernel<T, 8><<<a.nblocks, 512, 0, s>>>(a); break;
-  }
+  if (a.threads == 128)
+    launch_allreduce_nt<T, 128>(a, s);
+  else
+    launch_allreduce_nt<T, 512>(a, s);
 }
 
 __global__ void flag_wait_test_kernel(uint32_t* flag, uint32_t value, int64_t budget,
@@ -213,6 +221,7 @@ __global__ void flag_wait_test_kernel(uint32_t* flag, uint32_t value, int64_t bu
 int comm_allreduce_launch(const CommArgs& a, cudaStream_t s) {
   if (a.world < 1 || a.world > kCommMaxRanks || a.nblocks < 1 || a.nblocks > kCommMaxBlocks)
     return -1;
+  if (a.threads != 128 && a.threads != 512) return -3;
   if (a.n <= 0) return 0;
   const int esz = a.dtype == 0 ? 4 : 2;
   if ((a.offset * esz) % 16) return -2;  // bucket starts must be 16-byte aligned

@@ -6,7 +6,7 @@
 
 namespace g2b {
 
-constexpr int kCommMaxBlocks = 128;  // flag slots per (phase, rank)
+constexpr int kCommMaxBlocks = 160;  // flag slots per (phase, rank)
 constexpr int kCommMaxRanks = 8;
 
 // One fused all-reduce over NVLink peer memory. Every rank owns a symmetric
@@ -27,6 +27,12 @@ struct CommArgs {
   uint32_t* err = nullptr;
   int nblocks = 32;
   int64_t wait_budget_ns = 2000000000ll;
+  // Threads per CTA: 512 (the wide kernel, for a GPU with nothing else to
+  // run) or 128 (the slim kernel: <= 80 registers a thread and no dynamic
+  // shared memory, so one CTA fits on an SM beside a resident persistent GEMM
+  // or attention CTA and the reduction overlaps backward without taking SMs
+  // away from it).
+  int threads = 512;
 };
 
 int comm_allreduce_launch(const CommArgs& a, cudaStream_t s);

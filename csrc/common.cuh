@@ -373,6 +373,106 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// ------------------------------------------------------ CTA pairs (2-SM) ---
+// Helpers for kernels launched as clusters of two CTAs that share one
+// tcgen05.mma of M = 256 (cta_group::2): the even CTA of the pair (cluster
+// rank 0) issues the MMAs, each CTA holds its half of A and of B in its own
+// shared memory and its half of the accumulator in its own TMEM.
+
+// Shared::cluster address of this CTA's object `p` as seen from CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  return map_shared_rank(smem_u32(p), rank);
+}
+
+// mbarrier wait whose acquire is at cluster scope: data that another CTA of
+// the cluster wrote before a release-arrive on this barrier is visible after.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(0x989680u)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_bounded_cluster(uint64_t* bar, uint32_t parity,
+                                                          uint32_t* err, uint32_t code,
+                                                          volatile int* abort) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (abort && *abort) return false;
+    if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+      report_error(err, code);
+      if (abort) *abort = 1;
+      return false;
+    }
+  }
+}
+
+// Arrive (release, cluster scope) on an mbarrier given by its cluster address
+// (this CTA's or the peer's).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                   bar_cluster_addr)
+               : "memory");
+}
+
+__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr_, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr_), "r"(v) : "memory");
+}
+
+// 2-D tiled TMA load into THIS CTA's shared memory whose completion bytes are
+// counted on the mbarrier at `bar_cluster_addr` (the pair leader's). Not a
+// multicast load: the source is one tile of this GPU's own global memory.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* tmap,
+                                                 uint32_t bar_cluster_addr, int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster_addr), "r"(x), "r"(y)
+      : "memory");
+}
+
+// One tcgen05.mma of the pair (issued by the leader CTA only).
+__device__ __forceinline__ void umma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// Arrive on the mbarrier at the same shared-memory offset as `bar` in every
+// CTA of `cta_mask` (bit r = cluster rank r) once every pair MMA issued so far
+// by this thread completes. This is the commit of tcgen05 (a signal, not a
+// data copy).
+__device__ __forceinline__ void umma_commit_pair_mask(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
+}
+
+// TMEM allocation for a pair: one warp of EACH CTA (same warp index) issues it.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(smem_slot)),
+               "r"(ncols));
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+
 // ------------------------------------------------------------ math bits ---
 // Hardware tanh approximation (PTX tanh.approx.f32; max relative error ~2^-11,
 // below the bf16 rounding of every tensor it feeds).

@@ -35,6 +35,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdio.h>
+#include <stdlib.h>
 
 #include <algorithm>
 #include <atomic>
@@ -535,6 +536,334 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------- CTA pairs ---
+// The same GEMM with one 256x256 output tile per PAIR of CTAs (a cluster of
+// two on neighbouring SMs) and one tcgen05.mma.cta_group::2 of M = 256,
+// N = 256 per 16-wide k slice. Each CTA loads its own 128 rows of A and its
+// own 128 rows of B per k-block (32 KB instead of the 48 KB a 128x256 tile of
+// one CTA needs), so the operand bytes streamed from L2 per FLOP fall by a
+// third; each CTA's TMEM holds its 128 rows of the accumulator and its
+// epilogue is the single-CTA one.
+//   leader (cluster rank 0): claims tiles and publishes them to both CTAs'
+//     queues; its full barriers count both CTAs' TMA bytes; its MMA warp
+//     issues the pair MMAs and commits to the barriers of both CTAs.
+//   peer (rank 1): its producer streams its halves into its own stages,
+//     signalling the leader's full barrier; its epilogue drains its TMEM and
+//     releases the accumulator on the leader's barrier.
+// No load is a multicast: every TMA copy writes the issuing CTA's own shared
+// memory from this GPU's global memory.
+constexpr int kPairStages = 6;
+// Launches that pass the shape policy in use_pairs() run on CTA pairs unless
+// the caller or G2B_GEMM_PAIR says otherwise.
+constexpr bool kPairDefault = true;
+
+struct PairCfg {
+  static constexpr int BN = 256;                     // tile N of the pair
+  static constexpr int STAGES = kPairStages;
+  static constexpr int A_BYTES = BM * BK * 2;        // this CTA's 128 rows of A
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;  // this CTA's 128 rows of B
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int EPI_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFFSET = EPI_OFFSET + kEpiWarps * kStageBuf;
+  static constexpr int SMEM_BYTES = BAR_OFFSET + 256 + 1024;
+};
+static_assert(PairCfg::SMEM_BYTES <= 232448, "pair GEMM exceeds the shared-memory limit");
+
+// Arrivals a tile-queue slot needs before the leader may reuse it: the
+// leader's MMA warp and 8 epilogue warps, the peer's producer and 8 epilogue
+// warps.
+constexpr int kPairQueueArrivals = 2 + 2 * kEpiWarps;
+
+template <int EPI, int A_MN, int B_MN, int TMA_ST>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmO,
+                     const __grid_constant__ CUtensorMap tmX, const GemmDev p) {
+  using Cfg = PairCfg;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr int BN = Cfg::BN;
+  constexpr bool F32_OUT = (EPI == EPI_RESID_F32 || EPI == EPI_F32);
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFFSET);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* tq_full = tempty_bar + 2;
+  uint64_t* tq_empty = tq_full + 4;
+  int* tile_q = reinterpret_cast<int*>(tq_empty + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_q + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = (int)(blockIdx.x >> 1);
+  const int npairs = (int)(gridDim.x >> 1);
+  const int m_tiles = (p.M + 2 * BM - 1) / (2 * BM);  // 256-row tiles
+  const int tiles_per_split = m_tiles * p.n_tiles;
+  const int num_tiles = tiles_per_split * p.splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);   // used on the leader: its arrive.expect_tx
+      mbar_init(&empty_bar[s], 1);  // the leader's MMA commit, in both CTAs
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 2 * kEpiWarps);  // leader only: both CTAs' warps
+    }
+    for (int q = 0; q < 4; ++q) {
+      mbar_init(&tq_full[q], 1);
+      mbar_init(&tq_empty[q], kPairQueueArrivals);  // leader only
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane_id() == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (TMA_ST) {
+      tma_prefetch_desc(&tmO);
+      if (EPI == EPI_BIAS_GELU) tma_prefetch_desc(&tmX);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  // both CTAs' barriers are initialised before either touches the other's
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int tile = pair;
+      const uint32_t lead_full0 = cluster_addr(&full_bar[0], 0);
+      for (int r = 0; ok; ++r) {
+        const int slot = r & 3;
+        int cur;
+        if (leader) {
+          if (!mbar_wait_bounded(&tq_empty[slot], ((r >> 2) & 1) ^ 1, p.err, ERR_TIMEOUT_PRODUCER,
+                                 abort_flag))
+            break;
+          cur = tile < num_tiles ? tile : -1;
+          tile_q[slot] = cur;
+          st_cluster_u32(cluster_addr(&tile_q[slot], 1), (uint32_t)cur);
+          mbar_arrive(&tq_full[slot]);
+          mbar_arrive_cluster(cluster_addr(&tq_full[slot], 1));
+          if (cur < 0) break;
+          tile = p.sched ? npairs + atomicAdd(p.sched, 1) : tile + npairs;
+        } else {
+          if (!mbar_wait_bounded_cluster(&tq_full[slot], (r >> 2) & 1, p.err, ERR_TIMEOUT_PRODUCER,
+                                         abort_flag))
+            break;
+          cur = tile_q[slot];
+          mbar_arrive_cluster(cluster_addr(&tq_empty[slot], 0));
+          if (cur < 0) break;
+        }
+        const int split = cur / tiles_per_split;
+        const int rem = cur % tiles_per_split;
+        const int m0 = (rem / p.n_tiles) * 2 * BM + (int)rank * BM;
+        const int nb = (rem % p.n_tiles) * BN + (int)rank * (BN / 2);
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1, p.err, ERR_TIMEOUT_PRODUCER,
+                                 abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
+          uint8_t* sb = sa + Cfg::A_BYTES;
+          const uint32_t fb = lead_full0 + stage * 8;
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::STAGE_BYTES);
+          const int k0 = kb * BK;
+          if (A_MN) {
+            tma_load_2d_pair(sa, &tmA, fb, m0, k0);
+            tma_load_2d_pair(sa + 64 * BK * 2, &tmA, fb, m0 + 64, k0);
+          } else {
+            tma_load_2d_pair(sa, &tmA, fb, k0, m0);
+          }
+          if (B_MN) {
+            tma_load_2d_pair(sb, &tmB, fb, nb, k0);
+            tma_load_2d_pair(sb + 64 * BK * 2, &tmB, fb, nb + 64, k0);
+          } else {
+            tma_load_2d_pair(sb, &tmB, fb, k0, nb);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer (leader)
+    if (leader && elect_one()) {
+      constexpr uint32_t idesc = umma_idesc_bf16(2 * BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int r = 0; ok; ++r) {
+        const int slot = r & 3;
+        if (!mbar_wait_bounded(&tq_full[slot], (r >> 2) & 1, p.err, ERR_TIMEOUT_MMA, abort_flag))
+          break;
+        const int tile = tile_q[slot];
+        mbar_arrive(&tq_empty[slot]);
+        if (tile < 0) break;
+        const int split = tile / tiles_per_split;
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1, p.err, ERR_TIMEOUT_MMA,
+                               abort_flag))
+          break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait_bounded(&full_bar[stage], phase, p.err, ERR_TIMEOUT_MMA, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t sb = sa + Cfg::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? umma_desc_sw128(sa + kk * 2048, 64 * BK * 2, 1024)
+                                     : umma_desc_sw128(sa + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? umma_desc_sw128(sb + kk * 2048, 64 * BK * 2, 1024)
+                                     : umma_desc_sw128(sb + kk * 32, 16, 1024);
+            umma_bf16_pair(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          // the stage is free in both CTAs once these MMAs have read it
+          umma_commit_pair_mask(&empty_bar[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair_mask(&tfull_bar[acc], 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // --------------------------------------------------------- epilogue
+    const int ew = warp - 2;
+    const int lg = warp & 3;
+    const int col_half = ew >> 2;
+    const int lane = (int)lane_id();
+    const int r_local = lg * 32 + lane;
+    constexpr int CHUNKS = BN / 64;
+    uint8_t* box = smem + Cfg::EPI_OFFSET + ew * kStageBuf;
+    const uint32_t lead_tempty0 = cluster_addr(&tempty_bar[0], 0);
+    const uint32_t lead_tq_empty0 = cluster_addr(&tq_empty[0], 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    float alpha = p.alpha;
+    if (p.alpha_ptr) alpha *= *p.alpha_ptr;
+    EpiIn in_next;
+    for (int r = 0;; ++r) {
+      const int slot = r & 3;
+      const bool got = leader ? mbar_wait_bounded(&tq_full[slot], (r >> 2) & 1, p.err,
+                                                  ERR_TIMEOUT_EPILOGUE, abort_flag)
+                              : mbar_wait_bounded_cluster(&tq_full[slot], (r >> 2) & 1, p.err,
+                                                          ERR_TIMEOUT_EPILOGUE, abort_flag);
+      if (!got) break;
+      const int tile = tile_q[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(lead_tq_empty0 + slot * 8);
+      if (tile < 0) break;
+      const int split = tile / tiles_per_split;
+      const int rem = tile % tiles_per_split;
+      const int m0 = (rem / p.n_tiles) * 2 * BM + (int)rank * BM;
+      const int n0 = (rem % p.n_tiles) * BN;
+      const int row = m0 + r_local;
+      const int c0 = n0 + col_half * (BN / 2);
+      load_epi_in<EPI>(p, row, c0, in_next);
+      if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, p.err, ERR_TIMEOUT_EPILOGUE, abort_flag))
+        break;
+      tc_fence_after();
+      const uint32_t t_row =
+          tmem_base + ((uint32_t)(lg * 32) << 16) + acc * BN + col_half * (BN / 2);
+#pragma unroll 1
+      for (int c = 0; c < CHUNKS; ++c) {
+        float v[32], z[32];
+        tmem_ld32(t_row + c * 32, v);
+        tmem_wait_ld();
+        if (c == CHUNKS - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(lead_tempty0 + acc * 8);
+        }
+        EpiIn in = in_next;
+        if (c + 1 < CHUNKS) load_epi_in<EPI>(p, row, c0 + (c + 1) * 32, in_next);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] *= alpha;
+        epi_math<EPI>(p, c0 + c * 32, v, in, z);
+        if (TMA_ST) {
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+          if (F32_OUT) {
+            stage_f32(box, lane, v);
+          } else {
+            stage_bf16(box, lane, v);
+            if (EPI == EPI_BIAS_GELU) stage_bf16(box + 2048, lane, z);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tmO, box, c0 + c * 32, m0 + lg * 32, split);
+            if (EPI == EPI_BIAS_GELU) tma_store_3d(&tmX, box + 2048, c0 + c * 32, m0 + lg * 32, 0);
+            bulk_commit();
+          }
+        } else {
+          store_direct<EPI>(p, row, c0 + c * 32, v, z, split);
+        }
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+    if (TMA_ST && lane == 0) bulk_wait0();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  // neither CTA leaves while the other may still signal its barriers or the
+  // leader's MMAs may still read its shared memory
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+  if (leader && p.sched && threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(p.sched + 1, 1) == npairs - 1) {
+      p.sched[0] = 0;
+      p.sched[1] = 0;
+      __threadfence();
+    }
+  }
+}
+
 // ------------------------------------------------------------------ host ---
 // Device address of a scheduling slot (the symbol's address on the current
 // device, looked up once per device).
@@ -660,6 +989,93 @@ int dispatch_epi(int epi, int tma_st, int amn, int bmn, const Maps& m, const Gem
   return -3;
 }
 
+// Largest number of CTA pairs of the pair kernel that can be resident at
+// once (a pair needs two free SMs of one GPC), looked up once per
+// instantiation; falls back to half the SMs.
+template <typename K>
+int max_pairs(K kern, int smem) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * (num_sms() / 2), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, (void*)kern, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = num_sms() / 2;
+  }
+  return std::min(n, num_sms() / 2);
+}
+
+template <int EPI, int A_MN, int B_MN, int TMA_ST>
+int launch_pair_cfg(const Maps& m, GemmDev d, int tiles, int max_ctas, cudaStream_t s) {
+  auto kern = gemm_pair_kernel<EPI, A_MN, B_MN, TMA_ST>;
+  constexpr int smem = PairCfg::SMEM_BYTES;
+  static int pairs_cap = 0;
+  if (!pairs_cap) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return -10;
+    pairs_cap = max_pairs(kern, smem);
+  }
+  int pairs = pairs_cap;
+  if (max_ctas > 0) pairs = std::max(1, std::min(pairs, max_ctas / 2));
+  if (pairs > tiles) pairs = tiles;
+  d.sched = tiles > pairs ? gemm_sched_slot() : nullptr;
+  kern<<<2 * pairs, kThreads, smem, s>>>(m.a, m.b, m.o, m.x, d);
+  count_launches(1);
+  return launch_succeeded() ? 0 : -11;
+}
+
+template <int EPI, int TMA_ST>
+int pair_major(int amn, int bmn, const Maps& m, const GemmDev& d, int tiles, int max_ctas,
+               cudaStream_t s) {
+  if (!amn && !bmn) return launch_pair_cfg<EPI, 0, 0, TMA_ST>(m, d, tiles, max_ctas, s);
+  if (!amn && bmn) return launch_pair_cfg<EPI, 0, 1, TMA_ST>(m, d, tiles, max_ctas, s);
+  if (amn && bmn) return launch_pair_cfg<EPI, 1, 1, TMA_ST>(m, d, tiles, max_ctas, s);
+  return launch_pair_cfg<EPI, 1, 0, TMA_ST>(m, d, tiles, max_ctas, s);
+}
+
+template <int EPI>
+int pair_st(int tma_st, int amn, int bmn, const Maps& m, const GemmDev& d, int tiles,
+            int max_ctas, cudaStream_t s) {
+  return tma_st ? pair_major<EPI, 1>(amn, bmn, m, d, tiles, max_ctas, s)
+                : pair_major<EPI, 0>(amn, bmn, m, d, tiles, max_ctas, s);
+}
+
+int pair_epi(int epi, int tma_st, int amn, int bmn, const Maps& m, const GemmDev& d, int tiles,
+             int max_ctas, cudaStream_t s) {
+  switch (epi) {
+    case EPI_BF16: return pair_st<EPI_BF16>(tma_st, amn, bmn, m, d, tiles, max_ctas, s);
+    case EPI_BIAS_GELU: return pair_st<EPI_BIAS_GELU>(tma_st, amn, bmn, m, d, tiles, max_ctas, s);
+    case EPI_RESID_F32: return pair_st<EPI_RESID_F32>(tma_st, amn, bmn, m, d, tiles, max_ctas, s);
+    case EPI_F32: return pair_st<EPI_F32>(tma_st, amn, bmn, m, d, tiles, max_ctas, s);
+    case EPI_GELU_BWD: return pair_st<EPI_GELU_BWD>(tma_st, amn, bmn, m, d, tiles, max_ctas, s);
+  }
+  return -3;
+}
+
+// Whether a launch runs on CTA pairs: the caller's choice (0 / 1), else the
+// G2B_GEMM_PAIR environment variable (0 / 1), else the built-in policy.
+bool use_pairs(const GemmArgs& a) {
+  static int env = -2;
+  if (env == -2) {
+    const char* e = getenv("G2B_GEMM_PAIR");
+    env = (e && (e[0] == '0' || e[0] == '1')) ? e[0] - '0' : -1;
+  }
+  int want = a.pair >= 0 ? a.pair : env;
+  if (a.bn != 256 || a.M < 2 * BM) return false;  // needs a full 256-row pair tile
+  if (want >= 0) return want == 1;
+  // Measured on B200 at GPT-2 shapes (CUDA events, same box): pairs win where
+  // the epilogue is light and operand streaming dominates -- weight
+  // gradients (fp32 out), data gradients (B MN-major), the residual-add
+  // forward and the wide lm_head GEMMs -- and lose where the GELU epilogues
+  // (forward and backward) set the pace, since a pair's accumulator is
+  // released only when both CTAs' epilogues have drained it.
+  if (a.epilogue == EPI_BIAS_GELU || a.epilogue == EPI_GELU_BWD) return false;
+  if (a.epilogue == EPI_BF16 && !a.b_mn_major && a.N < 8192) return false;
+  return kPairDefault;
+}
+
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits,
                                      int64_t split_stride, float* __restrict__ out, int64_t ldo,
                                      int M, int N, int accumulate) {
@@ -704,8 +1120,9 @@ int gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   bool ok = a.a_mn_major ? make_tmap_2d(&maps.a, a.A, a.M, a.K, a.lda, BK)
                          : make_tmap_2d(&maps.a, a.A, a.K, a.M, a.lda, BM);
   if (!ok) return -7;
+  const bool pairs = use_pairs(a);
   ok = a.b_mn_major ? make_tmap_2d(&maps.b, a.B, a.N, a.K, a.ldb, BK)
-                    : make_tmap_2d(&maps.b, a.B, a.K, a.N, a.ldb, BN);
+                    : make_tmap_2d(&maps.b, a.B, a.K, a.N, a.ldb, pairs ? BN / 2 : BN);
   if (!ok) return -8;
 
   GemmDev d;
@@ -755,6 +1172,15 @@ int gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
     maps.x = maps.o;
   }
 
+  if (pairs) {
+    const int ptiles = (a.M + 2 * BM - 1) / (2 * BM) * d.n_tiles * d.splits;
+    int rc = pair_epi(a.epilogue, tma_st, a.a_mn_major, a.b_mn_major, maps, d, ptiles, a.max_ctas,
+                      stream);
+    if (rc != 0 || !split_mode) return rc;
+    return splitk_reduce_launch(reinterpret_cast<const float*>(a.workspace), d.splits,
+                                d.split_stride, reinterpret_cast<float*>(a.out), a.ldo, a.M, a.N,
+                                a.accumulate, stream);
+  }
   const int tiles = d.m_tiles * d.n_tiles * d.splits;
   int grid = a.max_ctas > 0 ? a.max_ctas : num_sms();
   if (grid > tiles) grid = tiles;

@@ -37,6 +37,8 @@ struct GemmArgs {
   void* workspace = nullptr;        // fp32 [splits, M, N] when splits > 1
   int bn = 256;                     // tile N: 256 or 128
   int max_ctas = 0;                 // 0 = one CTA per SM
+  int pair = -1;                    // 1: 256x256 tiles on CTA pairs (cta_group::2), 0: one
+                                    // CTA per 128xbn tile, -1: library default
   uint32_t* err = nullptr;          // error word (device)
 };
 

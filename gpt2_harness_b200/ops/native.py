@@ -145,12 +145,15 @@ def gemm(
     workspace: Optional[torch.Tensor] = None,
     bn: int = 256,
     max_ctas: int = 0,
+    pair: int = -1,
 ) -> torch.Tensor:
     """out[M,N] (epilogue) = op(a) @ op(b)^T on the tcgen05 tensor cores.
 
     ``a`` is [M, K] (or [K, M] with ``a_t``), ``b`` is [N, K] (or [K, N] with
     ``b_t``), both bf16 row-major views. ``a_t``/``b_t`` select the MN-major
     operand layout in the kernel: no transpose is ever materialised.
+    ``pair`` = 1 runs 256x256 tiles on pairs of CTAs (one cta_group::2 MMA per
+    pair), 0 one CTA per 128 x ``bn`` tile, -1 the library's default.
     """
     _check_cuda(a, b, out, bias, aux, alpha_ptr, workspace)
     if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
@@ -182,7 +185,8 @@ def gemm(
         a.data_ptr(), _row_stride(a), int(a_t), b.data_ptr(), _row_stride(b), int(b_t),
         M, N, K, epilogue, out.data_ptr(), _row_stride(out), _ptr(aux),
         0 if aux is None else _row_stride(aux), _ptr(bias), float(alpha), _ptr(alpha_ptr),
-        int(accumulate), int(splits), _ptr(workspace), int(bn), int(max_ctas), _err_ptr(), _stream(),
+        int(accumulate), int(splits), _ptr(workspace), int(bn), int(max_ctas), int(pair), _err_ptr(),
+        _stream(),
     )
     return out
 

@@ -95,7 +95,7 @@ class NativeDDP:
     """
 
     def __init__(self, layout: ParamLayout, group=None, comm: str = "p2p",
-                 bucket_bytes: int = DEFAULT_BUCKET_BYTES, nblocks: int = 128,
+                 bucket_bytes: int = DEFAULT_BUCKET_BYTES, nblocks: int = 148,
                  device: Optional[torch.device] = None, tail_blocks: int = 128) -> None:
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -107,11 +107,16 @@ class NativeDDP:
         self.layout = layout
         self.buckets = build_layout_buckets(layout, bucket_bytes)
         self.order = {g: i for i, g in enumerate(group_order(layout))}
-        # Buckets completed during backward share the GPU with it and use
-        # `nblocks` CTAs; the buckets completed by the last gradient group are
-        # reduced while nothing else runs, so they get `tail_blocks`.
+        # Buckets completed during backward share the GPU with it: they run on
+        # the slim kernel (`nblocks` CTAs of 128 threads, small enough to sit
+        # on an SM next to a resident GEMM or attention CTA instead of
+        # displacing it). The buckets completed by the last gradient group
+        # are reduced while nothing else runs: the wide kernel with
+        # `tail_blocks` CTAs of 512 threads.
         self.nblocks = nblocks
         self.tail_blocks = tail_blocks
+        # G2B_COMM_SLIM=0 puts every bucket on the wide kernel (for comparison)
+        self.slim = os.environ.get("G2B_COMM_SLIM", "1") != "0"
         self.last_group = len(self.order) - 1
         self.symm: Optional[SymmetricBuffer] = None
         self.flags: Optional[SymmetricBuffer] = None
@@ -148,12 +153,12 @@ class NativeDDP:
         if self.comm == "none":
             return
         idx = self.order[group]
-        blocks = self.tail_blocks if idx == self.last_group else self.nblocks
+        tail = idx == self.last_group or not self.slim
         while self._next < len(self.buckets) and self.buckets[self._next].ready <= idx:
-            self._launch(self.buckets[self._next], blocks)
+            self._launch(self.buckets[self._next], slim=not tail)
             self._next += 1
 
-    def _launch(self, b: Bucket, nblocks: Optional[int] = None) -> None:
+    def _launch(self, b: Bucket, slim: bool = False) -> None:
         ev = torch.cuda.Event()
         ev.record()
         self.stream.wait_event(ev)
@@ -161,11 +166,11 @@ class NativeDDP:
         with torch.cuda.stream(self.stream):
             if self.comm == "p2p":
                 self.epoch += 1
-                N.lib().allreduce_p2p(
-                    self.symm.peer_ptrs_dev.data_ptr(), self.flags.peer_ptrs_dev.data_ptr(),
-                    self.rank, self.world, b.lo, b.hi - b.lo, 0, 1.0 / self.world,
-                    self.epoch & 0xFFFFFFFF, self.byte_counter.data_ptr(), N.error_word().data_ptr(),
-                    nblocks or self.nblocks, 2_000_000_000, self.stream.cuda_stream)
+                fn = N.lib().allreduce_p2p_slim if slim else N.lib().allreduce_p2p
+                fn(self.symm.peer_ptrs_dev.data_ptr(), self.flags.peer_ptrs_dev.data_ptr(),
+                   self.rank, self.world, b.lo, b.hi - b.lo, 0, 1.0 / self.world,
+                   self.epoch & 0xFFFFFFFF, self.byte_counter.data_ptr(), N.error_word().data_ptr(),
+                   self.nblocks if slim else self.tail_blocks, 2_000_000_000, self.stream.cuda_stream)
             else:
                 dist.all_reduce(self.grad_buffer[b.lo:b.hi], group=self.group)
 
@@ -177,7 +182,7 @@ class NativeDDP:
             # backward did not announce every group (e.g. a frozen tail):
             # launch the rest now so every rank issues the same sequence.
             while self._next < len(self.buckets):
-                self._launch(self.buckets[self._next], self.tail_blocks)
+                self._launch(self.buckets[self._next])
                 self._next += 1
         torch.cuda.current_stream().wait_stream(self.stream)
         self._next = 0

@@ -52,7 +52,7 @@ def _row_bytes_ok(t, esz):
 
 
 def gemm(a, b, out, *, a_t=False, b_t=False, epilogue=N.EPI_BF16, bias=None, aux=None, alpha=1.0,
-         alpha_ptr=None, accumulate=False, splits=1, workspace=None, bn=256, max_ctas=0):
+         alpha_ptr=None, accumulate=False, splits=1, workspace=None, bn=256, max_ctas=0, pair=-1):
     # operand loads are TMA: 16-byte aligned bases and row strides (csrc/gemm.cu)
     _require(a.dtype == torch.bfloat16 and b.dtype == torch.bfloat16, "gemm operands bf16")
     _require(_row_bytes_ok(a, 2) and _row_bytes_ok(b, 2), "gemm operand alignment")
@@ -411,6 +411,9 @@ def allreduce_p2p(peer_bufs, peer_flags, rank, world, offset, n, dtype, scale, e
     dist.barrier(group=_group(peer_flags))
 
 
+allreduce_p2p_slim = allreduce_p2p  # same contract, fewer threads per CTA on the GPU
+
+
 # ------------------------------------------- tensor-parallel row collectives --
 def _peers(d, key="peer_bufs"):
     return _ptr_list(d[key], d["world"])
@@ -666,7 +669,7 @@ OPS = {
 LIB = SimpleNamespace(zero_rs=zero_rs, zero_adamw_ag=zero_adamw_ag, zero_ag=zero_ag,
                       zero_flag_words=lambda: 16, zero_norm_words=lambda: 16, zero_max_blocks=lambda: 160,
                       cp_kv_gather=cp_kv_gather, cp_kv_reduce=cp_kv_reduce, tp_flag_words=lambda: 16,
-                      allreduce_p2p=allreduce_p2p, comm_flag_words=lambda: 16, tp_ag_rows=tp_ag_rows,
+                      allreduce_p2p=allreduce_p2p, allreduce_p2p_slim=allreduce_p2p_slim, comm_flag_words=lambda: 16, tp_ag_rows=tp_ag_rows,
                       tp_rs_rows=tp_rs_rows, tp_embed_fwd=tp_embed_fwd, tp_embed_bwd=tp_embed_bwd,
                       tp_ce_stats=tp_ce_stats, tp_ce_finish=tp_ce_finish, loss_reduce=loss_reduce)
 

@@ -33,7 +33,7 @@ WORKER = textwrap.dedent(r'''
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
-    cfg = gpt2_config("gpt2", n_layer=2, n_positions=1024)
+    cfg = gpt2_config("gpt2", **json.loads(os.environ.get("G2B_CFG", '{"n_layer": 2, "n_positions": 1024}')))
     B, T = 2, 1024
     Tl = T // world
     cp = NativeCP(cfg, B, T, balance=os.environ["G2B_BALANCE"])
@@ -77,7 +77,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _run(world: int, balance: str):
+def _run(world: int, balance: str, cfg: dict | None = None):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     port = _free_port()
@@ -86,6 +86,8 @@ def _run(world: int, balance: str):
         env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r),
                    MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), G2B_ROOT=ROOT,
                    NCCL_NVLS_ENABLE="0", G2B_BALANCE=balance)
+        if cfg is not None:
+            env["G2B_CFG"] = json.dumps(cfg)
         procs.append(subprocess.Popen([sys.executable, "-c", WORKER], env=env, stdout=subprocess.PIPE,
                                       stderr=subprocess.STDOUT, text=True))
     results = []
@@ -104,9 +106,13 @@ def _run(world: int, balance: str):
     return results
 
 
-@pytest.mark.parametrize("world,balance", [(1, "zigzag"), (2, "contiguous"), (2, "zigzag")])
-def test_native_cp_matches_single_gpu(world, balance):
-    res = _run(world, balance)
+LARGE = {"n_layer": 2, "n_embd": 1280, "n_head": 20, "n_positions": 1024}
+
+
+@pytest.mark.parametrize("world,balance,cfg", [(1, "zigzag", None), (2, "contiguous", None),
+                                               (2, "zigzag", None), (8, "zigzag", LARGE)])
+def test_native_cp_matches_single_gpu(world, balance, cfg):
+    res = _run(world, balance, cfg)
     print(res)
     for r in res:
         assert abs(r["loss"] - r["ref_loss"]) < 1e-3 * abs(r["ref_loss"]), r

@@ -31,7 +31,7 @@ WORKER = textwrap.dedent(r'''
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     comm = os.environ["G2B_COMM"]
-    cfg = gpt2_config("gpt2", n_layer=2, n_positions=256)
+    cfg = gpt2_config("gpt2", **json.loads(os.environ.get("G2B_CFG", '{"n_layer": 2, "n_positions": 256}')))
     layout = ParamLayout(cfg)
     ddp = NativeDDP(layout, comm=comm, bucket_bytes=4 * 1024 * 1024)
     eng = Engine(cfg, "cuda", grad_buffer=ddp.grad_buffer, seed=0)
@@ -71,15 +71,18 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _run(comm: str, world: int = 2):
+def _run(comm: str, world: int = 2, cfg: dict | None = None):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
+    import json
     port = _free_port()
     procs = []
     for r in range(world):
         env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r),
                    MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), G2B_ROOT=ROOT, G2B_COMM=comm,
                    NCCL_NVLS_ENABLE="0")
+        if cfg is not None:
+            env["G2B_CFG"] = json.dumps(cfg)
         procs.append(subprocess.Popen([sys.executable, "-c", WORKER], env=env, stdout=subprocess.PIPE,
                                       stderr=subprocess.STDOUT, text=True))
     results = []
@@ -88,14 +91,15 @@ def _run(comm: str, world: int = 2):
         assert p.returncode == 0, out[-3000:]
         line = [l for l in out.splitlines() if l.startswith("RESULT ")]
         assert line, out[-3000:]
-        import json
         results.append(json.loads(line[-1][7:]))
     return results
 
 
-@pytest.mark.parametrize("comm", ["p2p", "nccl"])
-def test_native_ddp_two_gpus(comm):
-    res = _run(comm)
+# 2 ranks on a 2-layer GPT-2 small; the BASELINE data-parallel mesh (8 ranks)
+# at GPT-2 small widths with 2 of its 12 layers
+@pytest.mark.parametrize("comm,world", [("p2p", 2), ("nccl", 2), ("p2p", 8)])
+def test_native_ddp_two_gpus(comm, world):
+    res = _run(comm, world)
     for r in res:
         assert r["rel_err"] < 1e-5, r
         assert r["ranks_equal"], r

@@ -113,6 +113,77 @@ def test_gemm_large_vocab_shape():
     assert rel_err(logits[:, :V], ref) < 1e-2
 
 
+# ------------------------------------------------- GEMM on CTA pairs (2-SM) --
+PAIR_SHAPES = [(256, 256, 64), (512, 512, 128), (264, 136, 72), (768, 768, 768), (1000, 520, 264),
+               (2048, 3072, 768)]
+
+
+@pytest.mark.parametrize("M,Nn,K", PAIR_SHAPES)
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, False), (True, True)])
+def test_gemm_pair_layouts(M, Nn, K, a_t, b_t):
+    """256x256 tiles on CTA pairs (cta_group::2) against fp32 torch, and
+    against the single-CTA kernel (same k order per output: equal to fp32
+    rounding)."""
+    g = torch.Generator(device="cpu").manual_seed(M * 5 + Nn + K)
+    A = torch.randn(M, K, generator=g).to(dev(), torch.bfloat16)
+    B = torch.randn(Nn, K, generator=g).to(dev(), torch.bfloat16)
+    a_in = A.t().contiguous() if a_t else A
+    b_in = B.t().contiguous() if b_t else B
+    out = torch.empty(M, Nn, dtype=torch.float32, device=dev())
+    N.gemm(a_in, b_in, out, a_t=a_t, b_t=b_t, epilogue=N.EPI_F32, pair=1)
+    ref = A.float() @ B.float().t()
+    assert rel_err(out, ref) < 1e-5
+    single = torch.empty_like(out)
+    N.gemm(a_in, b_in, single, a_t=a_t, b_t=b_t, epilogue=N.EPI_F32, pair=0)
+    assert rel_err(out, single) < 1e-6
+
+
+def test_gemm_pair_epilogues():
+    M, Nn, K = 1280, 1024, 512
+    A = torch.randn(M, K, device=dev()).bfloat16()
+    W = (torch.randn(Nn, K, device=dev()) * 0.05).bfloat16()
+    bias = torch.randn(Nn, device=dev()).bfloat16()
+    pre = torch.empty(M, Nn, dtype=torch.bfloat16, device=dev())
+    act = torch.empty_like(pre)
+    N.gemm(A, W, act, epilogue=N.EPI_BIAS_GELU, bias=bias, aux=pre, pair=1)
+    ref_pre = A.float() @ W.float().t() + bias.float()
+    ref_act = 0.5 * ref_pre * (1 + torch.tanh(math.sqrt(2 / math.pi) * (ref_pre + 0.044715 * ref_pre**3)))
+    assert rel_err(pre, ref_pre) < 1e-2
+    assert rel_err(act, ref_act) < 1e-2
+    G = torch.randn(M, 256, device=dev()).bfloat16()
+    W2 = (torch.randn(Nn, 256, device=dev()) * 0.05).bfloat16()
+    dact = torch.empty(M, Nn, dtype=torch.bfloat16, device=dev())
+    N.gemm(G, W2, dact, epilogue=N.EPI_GELU_BWD, aux=pre, pair=1)
+    x = pre.float().requires_grad_(True)
+    y = 0.5 * x * (1 + torch.tanh(math.sqrt(2 / math.pi) * (x + 0.044715 * x**3)))
+    (gx,) = torch.autograd.grad(y, x, G.float() @ W2.float().t())
+    assert rel_err(dact, gx) < 2e-2
+    resid = torch.randn(M, Nn, device=dev())
+    ref = resid + A.float() @ W.float().t() + bias.float()
+    N.gemm(A, W, resid, epilogue=N.EPI_RESID_F32, bias=bias, pair=1)
+    assert rel_err(resid, ref) < 1e-4
+    # weight-gradient form: both MN-major, accumulate, split-K 3, device alpha
+    X = torch.randn(4096, 768, device=dev()).bfloat16()
+    dY = torch.randn(4096, 2304, device=dev()).bfloat16()
+    gw = torch.randn(2304, 768, device=dev())
+    a = torch.tensor([0.5], device=dev())
+    ref = gw + 0.5 * (dY.float().t() @ X.float())
+    ws = torch.empty(3 * 2304 * 768, device=dev())
+    N.gemm(dY, X, gw, a_t=True, b_t=True, epilogue=N.EPI_F32, accumulate=True, splits=3,
+           workspace=ws, alpha_ptr=a, pair=1)
+    assert rel_err(gw, ref) < 1e-4
+
+
+def test_gemm_pair_lm_head_shape():
+    M, V, C = 1024, 50257, 768
+    x = torch.randn(M, C, device=dev()).bfloat16()
+    w = (torch.randn(V, C, device=dev()) * 0.02).bfloat16()
+    logits = torch.zeros(M, 50304, dtype=torch.bfloat16, device=dev())
+    N.gemm(x, w, logits[:, :V], pair=1)
+    assert rel_err(logits[:, :V], x.float() @ w.float().t()) < 1e-2
+    assert logits[:, V:].abs().max().item() == 0.0  # the padding columns are never written
+
+
 # -------------------------------------------------------------- attention --
 def ref_attention(q, k, v, causal=True, q_offset=0):
     # q: [B, H, Tq, 64], k/v: [B, H, Tk, 64] fp32

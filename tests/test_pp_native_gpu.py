@@ -35,7 +35,7 @@ WORKER = textwrap.dedent(r'''
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
-    cfg = gpt2_config("gpt2", n_layer=4, n_positions=1024)
+    cfg = gpt2_config("gpt2", **json.loads(os.environ.get("G2B_CFG", '{"n_layer": 4, "n_positions": 1024}')))
     B, T, m = 2, 1024, 4
     tr = PipelineTrainer(cfg, B, T, m, pp=pp, cp=cp, schedule=schedule, seed=0)
     st = tr.engine
@@ -90,7 +90,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _run(world: int, pp: int, cp: int, schedule: str):
+def _run(world: int, pp: int, cp: int, schedule: str, cfg: dict | None = None):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     port = _free_port()
@@ -99,6 +99,8 @@ def _run(world: int, pp: int, cp: int, schedule: str):
         env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r),
                    MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), G2B_ROOT=ROOT,
                    G2B_SCHEDULE=schedule, G2B_PP=str(pp), G2B_CP=str(cp), NCCL_NVLS_ENABLE="0")
+        if cfg is not None:
+            env["G2B_CFG"] = json.dumps(cfg)
         procs.append(subprocess.Popen([sys.executable, "-c", WORKER], env=env, stdout=subprocess.PIPE,
                                       stderr=subprocess.STDOUT, text=True))
     results = []
@@ -117,10 +119,16 @@ def _run(world: int, pp: int, cp: int, schedule: str):
     return results
 
 
-@pytest.mark.parametrize("pp,cp,schedule", [(1, 1, "1f1b"), (2, 1, "1f1b"), (2, 1, "gpipe"),
-                                           (1, 2, "1f1b"), (2, 2, "1f1b")])
-def test_native_pp_matches_single_gpu(pp, cp, schedule):
-    res = _run(pp * cp, pp, cp, schedule)
+# the BASELINE pipeline mesh: PP = 4 x CP = 2 at GPT-2 large widths (one of
+# its 36 blocks per stage)
+LARGE = {"n_layer": 4, "n_embd": 1280, "n_head": 20, "n_positions": 1024}
+
+
+@pytest.mark.parametrize("pp,cp,schedule,cfg", [(1, 1, "1f1b", None), (2, 1, "1f1b", None),
+                                               (2, 1, "gpipe", None), (1, 2, "1f1b", None),
+                                               (2, 2, "1f1b", None), (4, 2, "1f1b", LARGE)])
+def test_native_pp_matches_single_gpu(pp, cp, schedule, cfg):
+    res = _run(pp * cp, pp, cp, schedule, cfg)
     print(res)
     for r in res:
         assert r["worst_err"] < 2e-2, r

@@ -32,7 +32,7 @@ WORKER = textwrap.dedent(r'''
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
-    cfg = gpt2_config("gpt2", n_layer=2, n_embd=192, n_head=3, n_positions=256)
+    cfg = gpt2_config("gpt2", **json.loads(os.environ.get("G2B_CFG", '{"n_layer": 2, "n_embd": 192, "n_head": 3, "n_positions": 256}')))
     B, T = 2, 256
     opt = OptimConfig(lr=1e-3, grad_clip=1.0)
     tp = TPEngine(cfg, B, T, optim=opt, seed=0)
@@ -86,7 +86,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _run(world: int):
+def _run(world: int, cfg: dict | None = None):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     port = _free_port()
@@ -95,6 +95,8 @@ def _run(world: int):
         env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r),
                    MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), G2B_ROOT=ROOT,
                    NCCL_NVLS_ENABLE="0")
+        if cfg is not None:
+            env["G2B_CFG"] = json.dumps(cfg)
         procs.append(subprocess.Popen([sys.executable, "-c", WORKER], env=env, stdout=subprocess.PIPE,
                                       stderr=subprocess.STDOUT, text=True))
     results = []
@@ -113,9 +115,14 @@ def _run(world: int):
     return results
 
 
-@pytest.mark.parametrize("world", [1, 2])
-def test_native_tp_matches_single_gpu(world):
-    res = _run(world)
+# the BASELINE tensor-parallel mesh: 8 ranks at GPT-2 XL widths (25 heads split
+# 4 + 3 x 7, 2 of its 48 layers)
+XL = {"n_layer": 2, "n_embd": 1600, "n_head": 25, "n_positions": 256}
+
+
+@pytest.mark.parametrize("world,cfg", [(1, None), (2, None), (8, XL)])
+def test_native_tp_matches_single_gpu(world, cfg):
+    res = _run(world, cfg)
     print(res)
     for r in res:
         assert abs(r["loss"] - r["ref_loss"]) < 2e-3 * abs(r["ref_loss"]), r

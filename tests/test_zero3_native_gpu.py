@@ -32,7 +32,7 @@ WORKER = textwrap.dedent(r'''
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
-    cfg = gpt2_config("gpt2", n_layer=3, n_positions=256)
+    cfg = gpt2_config("gpt2", **json.loads(os.environ.get("G2B_CFG", '{"n_layer": 3, "n_positions": 256}')))
     layout = ParamLayout(cfg)
     opt = dict(lr=1e-3, grad_clip=0.5)
     z = NativeZeRO3(layout)
@@ -84,7 +84,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _run(world: int):
+def _run(world: int, cfg: dict | None = None):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     port = _free_port()
@@ -93,6 +93,8 @@ def _run(world: int):
         env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r),
                    MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), G2B_ROOT=ROOT,
                    NCCL_NVLS_ENABLE="0")
+        if cfg is not None:
+            env["G2B_CFG"] = json.dumps(cfg)
         procs.append(subprocess.Popen([sys.executable, "-c", WORKER], env=env, stdout=subprocess.PIPE,
                                       stderr=subprocess.STDOUT, text=True))
     results = []
@@ -105,9 +107,13 @@ def _run(world: int):
     return results
 
 
-@pytest.mark.parametrize("world", [1, 2])
-def test_native_zero3_matches_unsharded(world):
-    res = _run(world)
+# the BASELINE ZeRO-3 mesh: 8 ranks at GPT-2 medium widths (3 of its 24 layers)
+MEDIUM = {"n_layer": 3, "n_embd": 1024, "n_head": 16, "n_positions": 256}
+
+
+@pytest.mark.parametrize("world,cfg", [(1, None), (2, None), (8, MEDIUM)])
+def test_native_zero3_matches_unsharded(world, cfg):
+    res = _run(world, cfg)
     print(res)
     for r in res:
         for row in r["rows"]:

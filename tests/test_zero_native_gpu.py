@@ -32,7 +32,7 @@ WORKER = textwrap.dedent(r'''
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
-    cfg = gpt2_config("gpt2", n_layer=2, n_positions=256)
+    cfg = gpt2_config("gpt2", **json.loads(os.environ.get("G2B_CFG", '{"n_layer": 2, "n_positions": 256}')))
     layout = ParamLayout(cfg)
     opt = dict(lr=1e-3, grad_clip=0.5)   # small enough that clipping is active
     zero = NativeZeRO(layout, bucket_bytes=4 * 1024 * 1024)
@@ -95,7 +95,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _run(world: int):
+def _run(world: int, cfg: dict | None = None):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     port = _free_port()
@@ -104,6 +104,8 @@ def _run(world: int):
         env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r),
                    MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), G2B_ROOT=ROOT,
                    NCCL_NVLS_ENABLE="0")
+        if cfg is not None:
+            env["G2B_CFG"] = json.dumps(cfg)
         procs.append(subprocess.Popen([sys.executable, "-c", WORKER], env=env, stdout=subprocess.PIPE,
                                       stderr=subprocess.STDOUT, text=True))
     results = []
@@ -116,7 +118,7 @@ def _run(world: int):
     return results
 
 
-@pytest.mark.parametrize("world", [1, 2])
+@pytest.mark.parametrize("world", [1, 2, 8])
 def test_native_zero2_matches_unsharded(world):
     res = _run(world)
     print(res)
