@@ -481,6 +481,7 @@ def finish_line(args, world, cfg, ms, ms_e2e, bi, bo, sampler, impl):
                 "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
                 "ms_per_step": round(ms_e2e, 3)},
         "clocks": {k: clocks.get(k) for k in ("sm_mhz", "sm_max_mhz", "reasons")},
+        "peak_mem_gb": round(max_over_ranks(torch.cuda.max_memory_allocated() / 1e9, world), 2),
         "impl": impl,
     }
     return line

@@ -60,7 +60,8 @@ PYBIND11_MODULE(_C, m) {
       [](int64_t A, int64_t lda, int a_mn, int64_t B, int64_t ldb, int b_mn, int M, int N, int K,
          int epi, int64_t out, int64_t ldo, int64_t aux, int64_t ldaux, int64_t bias, float alpha,
          int64_t alpha_ptr, int accumulate, int splits, int64_t workspace, int bn, int max_ctas,
-         int pair, int64_t err, int64_t stream) {
+         int pair, int64_t ce_stats, int64_t ce_targets, int64_t ce_tgt_logit, int ce_vocab_offset,
+         int64_t owner_out, int owner_rows, int64_t err, int64_t stream) {
         GemmArgs g;
         g.A = P<void>(A);
         g.lda = lda;
@@ -85,6 +86,12 @@ PYBIND11_MODULE(_C, m) {
         g.bn = bn;
         g.max_ctas = max_ctas;
         g.pair = pair;
+        g.ce_stats = P<void>(ce_stats);
+        g.ce_targets = P<int64_t>(ce_targets);
+        g.ce_tgt_logit = P<float>(ce_tgt_logit);
+        g.ce_vocab_offset = ce_vocab_offset;
+        g.owner_out = P<void*>(owner_out);
+        g.owner_rows = owner_rows;
         g.err = P<uint32_t>(err);
         check(gemm_bf16_launch(g, S(stream)), "gemm_bf16");
       });
@@ -144,20 +151,30 @@ PYBIND11_MODULE(_C, m) {
   m.def("attn_get_impl", []() { return attn_get_impl(); });
 
   m.def("layernorm_fwd", [](int64_t x, int64_t ldx, int64_t g, int64_t b, int64_t y, int64_t ldy,
-                            int64_t mean, int64_t rstd, int M, int C, float eps, int64_t stream) {
+                            int64_t mean, int64_t rstd, int M, int C, float eps, int64_t push_bases,
+                            int push_n, int64_t push_local, int64_t stream) {
+    RowPush push;
+    push.bases = P<void*>(push_bases);
+    push.n = push_n;
+    push.local = P<void>(push_local);
     check(layernorm_fwd_launch(P<float>(x), ldx, P<void>(g), P<void>(b), P<void>(y), ldy,
-                               P<float>(mean), P<float>(rstd), M, C, eps, S(stream)),
+                               P<float>(mean), P<float>(rstd), M, C, eps, S(stream), push),
           "layernorm_fwd");
   });
 
   m.def("layernorm_bwd", [](int64_t dy, int64_t x, int64_t mean, int64_t rstd, int64_t g,
                             int64_t dres, int64_t dres_bf16, int64_t partials, int64_t dgamma,
                             int64_t dbeta, int64_t dsum, int M, int C, int accumulate,
-                            int acc_params, int acc_sum, int64_t stream) {
+                            int acc_params, int acc_sum, int64_t push_bases, int push_n,
+                            int64_t push_local, int64_t stream) {
+    RowPush push;
+    push.bases = P<void*>(push_bases);
+    push.n = push_n;
+    push.local = P<void>(push_local);
     check(layernorm_bwd_launch(P<void>(dy), P<float>(x), P<float>(mean), P<float>(rstd),
                                P<void>(g), P<float>(dres), P<void>(dres_bf16), P<float>(partials),
                                P<float>(dgamma), P<float>(dbeta), P<float>(dsum), M, C,
-                               accumulate, acc_params, acc_sum, S(stream)),
+                               accumulate, acc_params, acc_sum, S(stream), push),
           "layernorm_bwd");
   });
 
@@ -194,6 +211,18 @@ PYBIND11_MODULE(_C, m) {
           "cross_entropy");
   });
 
+  m.def("ce_combine", [](int64_t stats, int nparts, int M, int64_t targets, int64_t tgt_logit,
+                         int64_t lse, int64_t loss_rows, int64_t stream) {
+    check(ce_combine_launch(P<void>(stats), nparts, M, P<int64_t>(targets), P<float>(tgt_logit),
+                            P<float>(lse), P<float>(loss_rows), S(stream)),
+          "ce_combine");
+  });
+  m.def("ce_grad", [](int64_t logits, int64_t ld, int M, int V, int64_t lse, int64_t targets,
+                      int vocab_offset, int64_t stream) {
+    check(ce_grad_launch(P<void>(logits), ld, M, V, P<float>(lse), P<int64_t>(targets),
+                         vocab_offset, S(stream)),
+          "ce_grad");
+  });
   m.def("loss_reduce", [](int64_t loss_rows, int64_t targets, int M, int64_t out, int64_t stream) {
     check(loss_reduce_launch(P<float>(loss_rows), P<int64_t>(targets), M, P<float>(out),
                              S(stream)),
@@ -368,6 +397,8 @@ PYBIND11_MODULE(_C, m) {
     t.B = (int)I("B");
     t.Tl = (int)I("Tl");
     t.zigzag = (int)I("zigzag");
+    t.pushed = (int)I("pushed");
+    t.inbox = P<const __nv_bfloat16>(I("inbox"));
     t.peer_bufs2 = P<void*>(I("peer_bufs2"));
     return t;
   };

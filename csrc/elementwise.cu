@@ -12,6 +12,7 @@
 #include <cuda_bf16.h>
 #include <math.h>
 
+#include <algorithm>
 #include <type_traits>
 
 #include "common.cuh"
@@ -19,6 +20,15 @@
 
 namespace g2b {
 namespace {
+
+// Store an 8-byte chunk of an output row into every peer copy (RowPush).
+__device__ __forceinline__ void push_store(const RowPush& push, const __nv_bfloat16* local_ptr,
+                                           uint2 v) {
+  const int64_t off = reinterpret_cast<const char*>(local_ptr) -
+                      reinterpret_cast<const char*>(push.local);
+  for (int j = 0; j < push.n; ++j)
+    *reinterpret_cast<uint2*>(reinterpret_cast<char*>(push.bases[j]) + off) = v;
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -62,7 +72,7 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x
                                                      __nv_bfloat16* __restrict__ y, int64_t ldy,
                                                      float* __restrict__ mean,
                                                      float* __restrict__ rstd, int M, int C,
-                                                     float eps) {
+                                                     float eps, const RowPush push) {
   const int warps = blockDim.x >> 5;
   const int row = blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -104,12 +114,14 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x
       o.x = pack_bf16x2((v[i].x - mu) * rs * g01.x + b01.x, (v[i].y - mu) * rs * g01.y + b01.y);
       o.y = pack_bf16x2((v[i].z - mu) * rs * g23.x + b23.x, (v[i].w - mu) * rs * g23.y + b23.y);
       *reinterpret_cast<uint2*>(yr + 4 * c) = o;
+      push_store(push, yr + 4 * c, o);
     }
   }
   if (lane == 0) {
     mean[row] = mu;
     rstd[row] = rs;
   }
+  if (push.n) __threadfence_system();  // pushed rows visible before any later signal
 }
 
 // LayerNorm backward, one warp per row, CTAs in clusters of LNB_CLUSTER.
@@ -134,7 +146,7 @@ __global__ void __cluster_dims__(LNB_CLUSTER, 1, 1) __launch_bounds__(256) ln_bw
     const float* __restrict__ mean, const float* __restrict__ rstd,
     const __nv_bfloat16* __restrict__ g, float* __restrict__ dres,
     __nv_bfloat16* __restrict__ dres_bf16, float* __restrict__ partials, int M, int C,
-    int accumulate, int with_dsum) {
+    int accumulate, int with_dsum, const RowPush push) {
   extern __shared__ float4 sacc[];  // [LNB_WARPS][LNB_NSUM][C/4]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C4 = C >> 2;
@@ -205,6 +217,7 @@ __global__ void __cluster_dims__(LNB_CLUSTER, 1, 1) __launch_bounds__(256) ln_bw
           w.x = pack_bf16x2(d.x, d.y);
           w.y = pack_bf16x2(d.z, d.w);
           *reinterpret_cast<uint2*>(db16 + 4 * c) = w;
+          push_store(push, db16 + 4 * c, w);
         }
         float4 a = my[c];
         a.x += d01.x * xh.x;
@@ -229,6 +242,7 @@ __global__ void __cluster_dims__(LNB_CLUSTER, 1, 1) __launch_bounds__(256) ln_bw
       }
     }
   }
+  if (push.n) __threadfence_system();  // pushed rows visible before any later signal
   __syncthreads();
   // CTA: fold the 8 warps' sums into warp 0's slot (fixed order).
   for (int c = threadIdx.x; c < nsum4; c += blockDim.x) {
@@ -503,6 +517,63 @@ __global__ void __launch_bounds__(CE_THREADS) ce_kernel(__nv_bfloat16* __restric
   }
 }
 
+// Fused lm_head + cross-entropy, step 2 (step 1 is the lm_head GEMM with the
+// EPI_CE_STATS epilogue): one thread per row folds the row's (max, sum exp)
+// partials, in tile order, into its log-sum-exp and loss.
+__global__ void __launch_bounds__(256) ce_combine_kernel(const float2* __restrict__ stats,
+                                                         int nparts, int M,
+                                                         const int64_t* __restrict__ targets,
+                                                         const float* __restrict__ tgt_logit,
+                                                         float* __restrict__ lse_out,
+                                                         float* __restrict__ loss_rows) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= M) return;
+  float m = -INFINITY, s = 0.f;
+  for (int j = 0; j < nparts; ++j) {
+    const float2 p = __ldcs(stats + (int64_t)j * M + row);
+    if (p.x == -INFINITY) continue;
+    const float nm = fmaxf(m, p.x);
+    s = s * __expf(m - nm) + p.y * __expf(p.x - nm);
+    m = nm;
+  }
+  const float lse = m + __logf(s);
+  lse_out[row] = lse;
+  loss_rows[row] = targets[row] == -100 ? 0.f : lse - tgt_logit[row];
+}
+
+// Step 3: logits -> (softmax - onehot) in place, one 16-byte vector (8 bf16)
+// per thread and iteration: one read and one write of the logits. Ignored
+// rows and the padded columns [V, ld) become 0.
+__global__ void __launch_bounds__(256) ce_grad_kernel(__nv_bfloat16* __restrict__ logits,
+                                                      int64_t ld, int M, int V,
+                                                      const float* __restrict__ lse,
+                                                      const int64_t* __restrict__ targets,
+                                                      int vocab_offset) {
+  const int64_t per_row = ld / 8;
+  const int64_t total = (int64_t)M * per_row;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / per_row;
+    const int col0 = (int)(i - row * per_row) * 8;
+    const int64_t t = __ldg(targets + row);
+    const bool ignore = t == -100;
+    const int64_t tl = t - vocab_offset;
+    const float L = __ldg(lse + row);
+    uint4* ptr = reinterpret_cast<uint4*>(logits + row * ld + col0);
+    const uint4 w = __ldcs(ptr);
+    uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(ws[j]);
+      const int c = col0 + 2 * j;
+      float a = (ignore || c >= V) ? 0.f : __expf(f.x - L) - (c == tl ? 1.f : 0.f);
+      float b = (ignore || c + 1 >= V) ? 0.f : __expf(f.y - L) - (c + 1 == tl ? 1.f : 0.f);
+      ws[j] = pack_bf16x2(a, b);
+    }
+    __stcs(ptr, make_uint4(ws[0], ws[1], ws[2], ws[3]));
+  }
+}
+
 __global__ void loss_reduce_kernel(const float* __restrict__ loss_rows,
                                    const int64_t* __restrict__ targets, int M,
                                    float* __restrict__ out) {
@@ -670,12 +741,12 @@ inline int ok() { return launch_succeeded() ? 0 : -11; }
 
 int layernorm_fwd_launch(const float* x, int64_t ldx, const void* gamma, const void* beta, void* y,
                          int64_t ldy, float* mean, float* rstd, int M, int C, float eps,
-                         cudaStream_t s) {
+                         cudaStream_t s, RowPush push) {
   if (C % 4 || C > 4 * 32 * LN_MAXV_CAP) return -1;
   return ln_dispatch(C, [&](auto nv) {
     ln_fwd_kernel<decltype(nv)::value><<<(M + 7) / 8, 256, 0, s>>>(
         x, ldx, (const __nv_bfloat16*)gamma, (const __nv_bfloat16*)beta, (__nv_bfloat16*)y, ldy,
-        mean, rstd, M, C, eps);
+        mean, rstd, M, C, eps, push);
         count_launches(1);
     return ok();
   });
@@ -706,7 +777,7 @@ int layernorm_bwd_partial_rows(int M) { return layernorm_bwd_ctas(M) / LNB_CLUST
 int layernorm_bwd_launch(const void* dy, const float* x, const float* mean, const float* rstd,
                          const void* gamma, float* dres, void* dres_bf16, float* partials,
                          float* dgamma, float* dbeta, float* dsum, int M, int C, int accumulate,
-                         int acc_params, int acc_sum, cudaStream_t s) {
+                         int acc_params, int acc_sum, cudaStream_t s, RowPush push) {
   if (C % 4 || C > 4 * 32 * LN_MAXV_CAP || M <= 0) return -1;
   const int nblk = layernorm_bwd_ctas(M);
   const int smem = LNB_WARPS * LNB_NSUM * C * (int)sizeof(float);
@@ -716,7 +787,7 @@ int layernorm_bwd_launch(const void* dy, const float* x, const float* mean, cons
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     kern<<<nblk, 256, smem, s>>>((const __nv_bfloat16*)dy, x, mean, rstd,
                                  (const __nv_bfloat16*)gamma, dres, (__nv_bfloat16*)dres_bf16,
-                                 partials, M, C, accumulate, dsum != nullptr);
+                                 partials, M, C, accumulate, dsum != nullptr, push);
     count_launches(1);
     return ok();
   });
@@ -779,6 +850,30 @@ int cross_entropy_fwd_bwd_launch(void* logits, int64_t ld, const int64_t* target
                                      vocab_offset);
                                      count_launches(1);
   return ok();
+}
+
+int ce_combine_launch(const void* stats, int nparts, int M, const int64_t* targets,
+                      const float* tgt_logit, float* lse, float* loss_rows, cudaStream_t s) {
+  if (M <= 0 || nparts <= 0) return -1;
+  ce_combine_kernel<<<(M + 255) / 256, 256, 0, s>>>(reinterpret_cast<const float2*>(stats),
+                                                     nparts, M, targets, tgt_logit, lse,
+                                                     loss_rows);
+  count_launches(1);
+  return launch_succeeded() ? 0 : -11;
+}
+
+int ce_grad_launch(void* logits, int64_t ld, int M, int V, const float* lse,
+                   const int64_t* targets, int vocab_offset, cudaStream_t s) {
+  if (M <= 0 || ld % 8 || V > ld || (reinterpret_cast<uintptr_t>(logits) & 15)) return -1;
+  int sms = 0, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t total = (int64_t)M * (ld / 8);
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)sms * 8);
+  ce_grad_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld, M, V, lse,
+                                        targets, vocab_offset);
+  count_launches(1);
+  return launch_succeeded() ? 0 : -11;
 }
 
 int loss_reduce_launch(const float* loss_rows, const int64_t* targets, int M, float* loss_out,

@@ -6,11 +6,21 @@
 
 namespace g2b {
 
+// Rows a kernel also stores into other GPUs' copies of its output buffer
+// (tensor parallelism pushes each rank's LayerNorm rows to every peer): the
+// row at address p in the local buffer goes to bases[j] + (p - local) too.
+struct RowPush {
+  void* const* bases = nullptr;  // device array of n peer base addresses
+  int n = 0;
+  const void* local = nullptr;   // local base the offsets are taken from
+};
+
+
 // LayerNorm over rows of an fp32 residual stream x[M, C] (row stride ldx) with
 // bf16 gamma/beta; writes bf16 y (row stride ldy) and fp32 mean/rstd [M].
 int layernorm_fwd_launch(const float* x, int64_t ldx, const void* gamma, const void* beta,
                          void* y, int64_t ldy, float* mean, float* rstd, int M, int C, float eps,
-                         cudaStream_t s);
+                         cudaStream_t s, RowPush push = RowPush());
 
 // LayerNorm backward. dy bf16 [M,C]; x fp32; writes/accumulates the fp32
 // residual gradient dres[M,C] (dres = (accumulate ? dres : 0) + dx) and its bf16
@@ -22,7 +32,7 @@ int layernorm_fwd_launch(const float* x, int64_t ldx, const void* gamma, const v
 int layernorm_bwd_launch(const void* dy, const float* x, const float* mean, const float* rstd,
                          const void* gamma, float* dres, void* dres_bf16, float* partials,
                          float* dgamma, float* dbeta, float* dsum, int M, int C, int accumulate,
-                         int acc_params, int acc_sum, cudaStream_t s);
+                         int acc_params, int acc_sum, cudaStream_t s, RowPush push = RowPush());
 int layernorm_bwd_partial_rows(int M);
 
 // out[c] (+)= sum_r in[r, c] for fp32 in[R, C] (deterministic, row order).
@@ -54,6 +64,14 @@ int cross_entropy_fwd_bwd_launch(void* logits, int64_t ld, const int64_t* target
 
 // loss_out[0] = sum(loss_rows)/count ; loss_out[1] = 1/count (count = non-ignored
 // targets, clamped to >= 1); deterministic single-block reduction.
+// Fused lm_head + cross-entropy (after the EPI_CE_STATS GEMM): per-row
+// log-sum-exp and loss from the GEMM's partials, then the in-place gradient
+// logits -> softmax - onehot (0 for ignored rows and padded columns).
+int ce_combine_launch(const void* stats, int nparts, int M, const int64_t* targets,
+                      const float* tgt_logit, float* lse, float* loss_rows, cudaStream_t s);
+int ce_grad_launch(void* logits, int64_t ld, int M, int V, const float* lse,
+                   const int64_t* targets, int vocab_offset, cudaStream_t s);
+
 int loss_reduce_launch(const float* loss_rows, const int64_t* targets, int M, float* loss_out,
                        cudaStream_t s);
 

@@ -80,7 +80,59 @@ struct GemmDev {
   int vec_ok;
   uint32_t* err;
   int* sched;  // {next tile - gridDim.x, finished CTAs}: dynamic scheduling, or null
+  float2* ce_stats;
+  const int64_t* ce_targets;
+  float* ce_tgt_logit;
+  int ce_vocab_offset;
+  void* const* owner_out;
+  int owner_rows;
 };
+
+// Online (max, sum exp) of one epilogue thread's row over its chunks of one
+// tile (EPI_CE_STATS): the logits are rounded to bf16 first, as stored.
+struct CeRow {
+  float m, s;
+  int64_t tgt;  // target column relative to this launch's column 0, or -1
+};
+
+__device__ __forceinline__ void ce_begin(const GemmDev& p, int row, CeRow& st) {
+  st.m = -INFINITY;
+  st.s = 0.f;
+  st.tgt = -1;
+  if (row < p.M) {
+    const int64_t t = p.ce_targets[row];
+    st.tgt = t < 0 ? -1 : t - p.ce_vocab_offset;
+  }
+}
+
+__device__ __forceinline__ void ce_chunk(const GemmDev& p, int row, int n0, float* v, CeRow& st) {
+  float cm = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    v[i] = __bfloat162float(__float2bfloat16_rn(v[i]));
+    if (n0 + i < p.N) cm = fmaxf(cm, v[i]);
+  }
+  if (cm != -INFINITY) {
+    const float nm = fmaxf(st.m, cm);
+    float acc = st.s * __expf(st.m - nm);
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (n0 + i < p.N) acc += __expf(v[i] - nm);
+    st.m = nm;
+    st.s = acc;
+  }
+  if (st.tgt >= n0 && st.tgt < n0 + 32 && st.tgt < p.N && row < p.M) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (n0 + i == st.tgt) t = v[i];
+    p.ce_tgt_logit[row] = t;
+  }
+}
+
+__device__ __forceinline__ void ce_end(const GemmDev& p, int row, int slot, const CeRow& st) {
+  if (row < p.M) p.ce_stats[(int64_t)slot * p.M + row] = make_float2(st.m, st.s);
+}
 
 // Per-launch tile counters for dynamic scheduling (see gemm_tcgen05_kernel).
 // Launches take slots round-robin; the last CTA of a launch resets its slot,
@@ -242,6 +294,11 @@ __device__ __forceinline__ void store_direct(const GemmDev& p, int row, int n0, 
     }
   } else {
     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo + n0;
+    if (p.owner_out) {
+      const int q = row / p.owner_rows;
+      o = reinterpret_cast<__nv_bfloat16*>(p.owner_out[q]) +
+          (int64_t)(row - q * p.owner_rows) * p.ldo + n0;
+    }
     __nv_bfloat16* a = EPI == EPI_BIAS_GELU
                            ? reinterpret_cast<__nv_bfloat16*>(p.aux) + (int64_t)row * p.ldaux + n0
                            : nullptr;
@@ -470,6 +527,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = m0 + r_local;
       const int c0 = n0 + col_half * (BN / 2);
       load_epi_in<EPI>(p, row, c0, in_next);
+      CeRow ce;
+      if (EPI == EPI_CE_STATS) ce_begin(p, row, ce);
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, p.err, ERR_TIMEOUT_EPILOGUE, abort_flag))
         break;
       tc_fence_after();
@@ -489,6 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] *= alpha;
         epi_math<EPI>(p, c0 + c * 32, v, in, z);
+        if (EPI == EPI_CE_STATS) ce_chunk(p, row, c0 + c * 32, v, ce);
         if (TMA_ST) {
           // the previous chunk's bulk store must have finished reading the box
           if (lane == 0) bulk_wait_read0();
@@ -510,12 +570,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           store_direct<EPI>(p, row, c0 + c * 32, v, z, split);
         }
       }
+      if (EPI == EPI_CE_STATS) ce_end(p, row, 2 * (n0 / BN) + col_half, ce);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
       }
     }
     if (TMA_ST && lane == 0) bulk_wait0();
+    // rows stored into other GPUs' memory are visible before a later signal
+    if (p.owner_out) __threadfence_system();
   }
 
   tc_fence_before();
@@ -797,6 +860,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int row = m0 + r_local;
       const int c0 = n0 + col_half * (BN / 2);
       load_epi_in<EPI>(p, row, c0, in_next);
+      CeRow ce;
+      if (EPI == EPI_CE_STATS) ce_begin(p, row, ce);
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, p.err, ERR_TIMEOUT_EPILOGUE, abort_flag))
         break;
       tc_fence_after();
@@ -817,6 +882,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] *= alpha;
         epi_math<EPI>(p, c0 + c * 32, v, in, z);
+        if (EPI == EPI_CE_STATS) ce_chunk(p, row, c0 + c * 32, v, ce);
         if (TMA_ST) {
           if (lane == 0) bulk_wait_read0();
           __syncwarp();
@@ -837,12 +903,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           store_direct<EPI>(p, row, c0 + c * 32, v, z, split);
         }
       }
+      if (EPI == EPI_CE_STATS) ce_end(p, row, 2 * (n0 / BN) + col_half, ce);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
       }
     }
     if (TMA_ST && lane == 0) bulk_wait0();
+    // rows stored into other GPUs' memory are visible before a later signal
+    if (p.owner_out) __threadfence_system();
   }
 
   tc_fence_before();
@@ -985,6 +1054,7 @@ int dispatch_epi(int epi, int tma_st, int amn, int bmn, const Maps& m, const Gem
     case EPI_RESID_F32: return dispatch_st<BN, EPI_RESID_F32>(tma_st, amn, bmn, m, d, grid, s);
     case EPI_F32: return dispatch_st<BN, EPI_F32>(tma_st, amn, bmn, m, d, grid, s);
     case EPI_GELU_BWD: return dispatch_st<BN, EPI_GELU_BWD>(tma_st, amn, bmn, m, d, grid, s);
+    case EPI_CE_STATS: return dispatch_st<BN, EPI_CE_STATS>(tma_st, amn, bmn, m, d, grid, s);
   }
   return -3;
 }
@@ -1050,6 +1120,7 @@ int pair_epi(int epi, int tma_st, int amn, int bmn, const Maps& m, const GemmDev
     case EPI_RESID_F32: return pair_st<EPI_RESID_F32>(tma_st, amn, bmn, m, d, tiles, max_ctas, s);
     case EPI_F32: return pair_st<EPI_F32>(tma_st, amn, bmn, m, d, tiles, max_ctas, s);
     case EPI_GELU_BWD: return pair_st<EPI_GELU_BWD>(tma_st, amn, bmn, m, d, tiles, max_ctas, s);
+    case EPI_CE_STATS: return pair_st<EPI_CE_STATS>(tma_st, amn, bmn, m, d, tiles, max_ctas, s);
   }
   return -3;
 }
@@ -1150,6 +1221,16 @@ int gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   d.accumulate = split_mode ? 0 : a.accumulate;
   d.split_stride = split_mode ? (int64_t)a.M * a.N : 0;
   d.err = a.err;
+  d.ce_stats = reinterpret_cast<float2*>(a.ce_stats);
+  d.ce_targets = a.ce_targets;
+  d.ce_tgt_logit = a.ce_tgt_logit;
+  d.ce_vocab_offset = a.ce_vocab_offset;
+  d.owner_out = a.owner_out;
+  d.owner_rows = a.owner_rows;
+  if (a.owner_out && (a.owner_rows <= 0 || (a.epilogue != EPI_BF16) || split_mode)) return -13;
+  if (a.epilogue == EPI_CE_STATS &&
+      (!a.ce_stats || !a.ce_targets || !a.ce_tgt_logit || split_mode || a.bias))
+    return -12;
   const int esz = (a.epilogue == EPI_F32 || a.epilogue == EPI_RESID_F32) ? 4 : 2;
   bool vec = aligned16(d.out) && ((d.ldo * esz) % 16 == 0);
   if (a.aux)
@@ -1158,8 +1239,9 @@ int gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   if (a.bias) vec = vec && aligned16(a.bias);
   d.vec_ok = vec ? 1 : 0;
 
-  // TMA stores need the same alignment as the vector path.
-  int tma_st = vec ? 1 : 0;
+  // TMA stores need the same alignment as the vector path; row-owner output
+  // uses the direct (per-thread vector) stores.
+  int tma_st = (vec && !a.owner_out) ? 1 : 0;
   if (tma_st) {
     ok = make_tmap_out(&maps.o, d.out, a.N, a.M, d.splits, d.ldo, esz);
     if (ok && a.epilogue == EPI_BIAS_GELU) ok = make_tmap_out(&maps.x, a.aux, a.N, a.M, 1, a.ldaux, 2);

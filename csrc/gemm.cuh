@@ -13,6 +13,13 @@ enum GemmEpilogue : int {
   EPI_RESID_F32 = 2,   // out(fp32) = (aux or out)(fp32) + acc + b   (residual add)
   EPI_F32 = 3,         // out(fp32)  = acc (+ out if accumulate) ; split-K partials
   EPI_GELU_BWD = 4,    // out(bf16)  = acc * gelu_tanh'(aux)
+  // Cross-entropy statistics (the lm_head forward): out(bf16) = acc (the
+  // logits); for every row and every 128-column half of a 256-wide tile
+  // column n_tile, ce_stats[(2 * n_tile + half) * M + row] = (max, sum exp(x -
+  // max)) of that half's bf16-rounded logits below N; ce_tgt_logit[row] = the
+  // bf16-rounded logit of column ce_targets[row] - ce_vocab_offset when this
+  // launch covers it.
+  EPI_CE_STATS = 5,
 };
 
 struct GemmArgs {
@@ -40,6 +47,17 @@ struct GemmArgs {
   int pair = -1;                    // 1: 256x256 tiles on CTA pairs (cta_group::2), 0: one
                                     // CTA per 128xbn tile, -1: library default
   uint32_t* err = nullptr;          // error word (device)
+  // EPI_CE_STATS only
+  void* ce_stats = nullptr;             // float2 [2 * ceil(N / 256), M]
+  const int64_t* ce_targets = nullptr;  // int64 [M] (ignore_index -100 never matches)
+  float* ce_tgt_logit = nullptr;        // fp32 [M]
+  int ce_vocab_offset = 0;              // first vocabulary id of column 0
+  // Row-owner output (tensor-parallel GEMM -> reduce-scatter): when set, row
+  // m of the result is stored at owner_out[m / owner_rows] + (m % owner_rows)
+  // * ldo -- device array of base addresses, typically in other GPUs' memory
+  // (plain peer stores, one 16-byte vector at a time). bf16 epilogues only.
+  void* const* owner_out = nullptr;
+  int owner_rows = 0;
 };
 
 // Returns 0 on success, a negative code for unsupported arguments.

@@ -93,20 +93,66 @@ __device__ __forceinline__ void finish(const TpArgs& a, int* fail) {
 }
 
 // ------------------------------------------------------------- all-gather --
+constexpr int kAgUnroll = 8;
+
+// Copy `total` 16-byte vectors from peers into this rank's buffer: element
+// `locate(i, q, off)` of the copy is peer q's vector at bf16 offset `off`,
+// stored at the same offset here. kAgUnroll independent peer loads are in
+// flight per thread before any store.
+template <typename F>
+__device__ __forceinline__ void peer_copy_unrolled(const TpArgs& a, __nv_bfloat16* mine,
+                                                   int64_t total, F locate) {
+  const int64_t span = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < total;
+       i0 += span * kAgUnroll) {
+    uint4 w[kAgUnroll];
+    int64_t off[kAgUnroll];
+#pragma unroll
+    for (int u = 0; u < kAgUnroll; ++u) {
+      const int64_t i = i0 + u * span;
+      off[u] = -1;
+      if (i < total) {
+        int q;
+        locate(i, q, off[u]);
+        w[u] = __ldcg(reinterpret_cast<const uint4*>(
+            reinterpret_cast<const __nv_bfloat16*>(a.peer_bufs[q]) + off[u]));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kAgUnroll; ++u)
+      if (off[u] >= 0) *reinterpret_cast<uint4*>(mine + off[u]) = w[u];
+  }
+}
+
 __global__ void __launch_bounds__(512) tp_ag_rows_kernel(const TpArgs a) {
   __shared__ int fail;
   if (threadIdx.x == 0) fail = 0;
   __syncthreads();
   if (!tp_handshake(a, 0, &fail)) return;
   const int64_t blk_vec = a.rows * a.cols / 8;  // 16-byte vectors per row block
-  const int64_t total = blk_vec * (a.world - 1);
+  const int64_t total = a.pushed ? 0 : blk_vec * (a.world - 1);
   uint4* mine = reinterpret_cast<uint4*>(a.peer_bufs[a.rank]);
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int q = (int)(i / blk_vec);
-    q += q >= a.rank;  // skip this rank's own block
-    const int64_t off = (int64_t)q * blk_vec + i % blk_vec;
-    mine[off] = __ldcg(reinterpret_cast<const uint4*>(a.peer_bufs[q]) + off);
+  // kAgUnroll independent peer loads in flight per thread before any store:
+  // NVLink latency is covered by the loads of one wave of the grid
+  const int64_t span = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < total;
+       i0 += span * kAgUnroll) {
+    uint4 w[kAgUnroll];
+    int64_t off[kAgUnroll];
+#pragma unroll
+    for (int u = 0; u < kAgUnroll; ++u) {
+      const int64_t i = i0 + u * span;
+      off[u] = -1;
+      if (i < total) {
+        int q = (int)(i / blk_vec);
+        q += q >= a.rank;  // skip this rank's own block
+        off[u] = (int64_t)q * blk_vec + i % blk_vec;
+        w[u] = __ldcg(reinterpret_cast<const uint4*>(a.peer_bufs[q]) + off[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kAgUnroll; ++u)
+      if (off[u] >= 0) mine[off[u]] = w[u];
   }
   if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
     atomicAdd(a.byte_counter, (unsigned long long)(a.rows * a.cols * 2 * a.world));
@@ -114,6 +160,52 @@ __global__ void __launch_bounds__(512) tp_ag_rows_kernel(const TpArgs a) {
 }
 
 // --------------------------------------------------------- reduce-scatter --
+// One 8-element vector of the reduce-scatter: the fixed-rank-order fp32 sum
+// of the W peers' bf16 partials, + bias + fp32 residual, stored as fp32
+// and/or bf16.
+template <int W>
+__device__ __forceinline__ void rs_finish_vec(const TpArgs& a, int64_t v, const uint4 (&w)[W]) {
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll
+  for (int q = 0; q < W; ++q) {
+    const uint32_t ws[4] = {w[q].x, w[q].y, w[q].z, w[q].w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack_bf16x2(ws[i]);
+      acc[2 * i] += f.x;
+      acc[2 * i + 1] += f.y;
+    }
+  }
+  const int64_t e0 = v * 8;
+  const int col = (int)(e0 % a.cols);
+  if (a.bias) {
+    const uint4 bw = *reinterpret_cast<const uint4*>(a.bias + col);
+    const uint32_t bs[4] = {bw.x, bw.y, bw.z, bw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack_bf16x2(bs[i]);
+      acc[2 * i] += f.x;
+      acc[2 * i + 1] += f.y;
+    }
+  }
+  if (a.resid) {
+    const float4 r0 = reinterpret_cast<const float4*>(a.resid + e0)[0];
+    const float4 r1 = reinterpret_cast<const float4*>(a.resid + e0)[1];
+    acc[0] += r0.x; acc[1] += r0.y; acc[2] += r0.z; acc[3] += r0.w;
+    acc[4] += r1.x; acc[5] += r1.y; acc[6] += r1.z; acc[7] += r1.w;
+  }
+  if (a.out_f32) {
+    reinterpret_cast<float4*>(a.out_f32 + e0)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    reinterpret_cast<float4*>(a.out_f32 + e0)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+  }
+  if (a.out_bf16)
+    *reinterpret_cast<uint4*>(a.out_bf16 + e0) =
+        make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                   pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+}
+
 template <int W>
 __global__ void __launch_bounds__(512) tp_rs_rows_kernel(const TpArgs a) {
   __shared__ int fail;
@@ -121,53 +213,33 @@ __global__ void __launch_bounds__(512) tp_rs_rows_kernel(const TpArgs a) {
   __syncthreads();
   if (!tp_handshake(a, 0, &fail)) return;
   const int64_t nvec = a.rows * a.cols / 8;  // 8 bf16 per vector
-  const int64_t base = (int64_t)a.rank * a.rows * a.cols;
-  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
-       v += (int64_t)gridDim.x * blockDim.x) {
-    uint4 w[W];
+  // source q: peer q's partial of this rank's rows, or slot q of the local
+  // inbox that peer q's GEMM filled
+  const int64_t base = a.inbox ? 0 : (int64_t)a.rank * a.rows * a.cols;
+  const __nv_bfloat16* src[W];
 #pragma unroll
-    for (int q = 0; q < W; ++q)
-      w[q] = __ldcg(reinterpret_cast<const uint4*>(
-                        reinterpret_cast<const __nv_bfloat16*>(a.peer_bufs[q]) + base) + v);
-    float acc[8];
+  for (int q = 0; q < W; ++q)
+    src[q] = a.inbox ? a.inbox + (int64_t)q * a.rows * a.cols
+                     : reinterpret_cast<const __nv_bfloat16*>(a.peer_bufs[q]) + base;
+  // U vectors x W peers = 8 (or W) independent peer loads in flight per
+  // thread before any arithmetic
+  constexpr int U = W >= 8 ? 1 : 8 / W;
+  const int64_t span = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v0 < nvec; v0 += span * U) {
+    uint4 w[U][W];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = v0 + u * span;
+      if (v < nvec) {
 #pragma unroll
-    for (int q = 0; q < W; ++q) {
-      const uint32_t ws[4] = {w[q].x, w[q].y, w[q].z, w[q].w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = unpack_bf16x2(ws[i]);
-        acc[2 * i] += f.x;
-        acc[2 * i + 1] += f.y;
+        for (int q = 0; q < W; ++q) w[u][q] = __ldcg(reinterpret_cast<const uint4*>(src[q]) + v);
       }
     }
-    const int64_t e0 = v * 8;
-    const int col = (int)(e0 % a.cols);
-    if (a.bias) {
-      const uint4 bw = *reinterpret_cast<const uint4*>(a.bias + col);
-      const uint32_t bs[4] = {bw.x, bw.y, bw.z, bw.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = unpack_bf16x2(bs[i]);
-        acc[2 * i] += f.x;
-        acc[2 * i + 1] += f.y;
-      }
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = v0 + u * span;
+      if (v < nvec) rs_finish_vec<W>(a, v, w[u]);
     }
-    if (a.resid) {
-      const float4 r0 = reinterpret_cast<const float4*>(a.resid + e0)[0];
-      const float4 r1 = reinterpret_cast<const float4*>(a.resid + e0)[1];
-      acc[0] += r0.x; acc[1] += r0.y; acc[2] += r0.z; acc[3] += r0.w;
-      acc[4] += r1.x; acc[5] += r1.y; acc[6] += r1.z; acc[7] += r1.w;
-    }
-    if (a.out_f32) {
-      reinterpret_cast<float4*>(a.out_f32 + e0)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      reinterpret_cast<float4*>(a.out_f32 + e0)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-    }
-    if (a.out_bf16)
-      *reinterpret_cast<uint4*>(a.out_bf16 + e0) =
-          make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
-                     pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
   }
   if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
     atomicAdd(a.byte_counter, (unsigned long long)(a.rows * a.cols * 2 * W));
@@ -373,19 +445,14 @@ __global__ void __launch_bounds__(512) cp_kv_gather_zz_kernel(const TpArgs a) {
   // chunks 0..2w-1-r except the own ones (r and 2w-1-r): e -> e (e < r) or e + 1
   const int nk = 2 * a.world - 2 - a.rank;
   const int64_t cvec = (int64_t)a.B * h * vpr;      // vectors per chunk
-  const int64_t total = cvec * nk;
-  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < total;
-       v += (int64_t)gridDim.x * blockDim.x) {
+  peer_copy_unrolled(a, mine, cvec * nk, [&](int64_t v, int& q, int64_t& off) {
     const int e = (int)(v / cvec);
     const int k = e < a.rank ? e : e + 1;
-    const int q = k < a.world ? k : 2 * a.world - 1 - k;
+    q = k < a.world ? k : 2 * a.world - 1 - k;
     const int64_t vv = v % cvec;
     const int64_t row = vv / vpr;                   // b * h + t
-    const int c = (int)(vv % vpr) * 8;
-    const int64_t off = zz_row(a, k, row / h, row % h) * a.cols + c;
-    *reinterpret_cast<uint4*>(mine + off) =
-        __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.peer_bufs[q]) + off));
-  }
+    off = zz_row(a, k, row / h, row % h) * a.cols + (int)(vv % vpr) * 8;
+  });
   if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
     atomicAdd(a.byte_counter, (unsigned long long)(cvec * 16 * (nk + 2)));
   finish(a, &fail);
@@ -456,17 +523,11 @@ __global__ void __launch_bounds__(512) cp_kv_gather_kernel(const TpArgs a) {
   __syncthreads();
   if (!tp_handshake(a, 0, &fail)) return;
   // 2. blocks of the earlier ranks from their buffers
-  const int64_t total = nvec * a.rank;
-  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < total;
-       v += (int64_t)gridDim.x * blockDim.x) {
-    const int q = (int)(v / nvec);
+  peer_copy_unrolled(a, mine, nvec * a.rank, [&](int64_t v, int& q, int64_t& off) {
+    q = (int)(v / nvec);
     const int64_t vv = v % nvec;
-    const int64_t i = vv / vpr;
-    const int c = (int)(vv % vpr) * 8;
-    const int64_t off = cp_row(a, q, i) * a.cols + c;
-    *reinterpret_cast<uint4*>(mine + off) =
-        __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.peer_bufs[q]) + off));
-  }
+    off = cp_row(a, q, vv / vpr) * a.cols + (int)(vv % vpr) * 8;
+  });
   if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
     atomicAdd(a.byte_counter, (unsigned long long)(nvec * 16 * (a.rank + 1)));
   finish(a, &fail);
@@ -488,10 +549,17 @@ __global__ void __launch_bounds__(512) cp_kv_reduce_kernel(const TpArgs a) {
     float acc[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) acc[k] = 0.f;
-    for (int q = a.rank; q < a.world; ++q) {
-      const uint4 w = __ldcg(reinterpret_cast<const uint4*>(
-          reinterpret_cast<const __nv_bfloat16*>(a.peer_bufs[q]) + off));
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    // every source's load is issued before the first sum (rank order kept)
+    uint4 w[kTpMaxRanks];
+#pragma unroll
+    for (int j = 0; j < kTpMaxRanks; ++j)
+      if (a.rank + j < a.world)
+        w[j] = __ldcg(reinterpret_cast<const uint4*>(
+            reinterpret_cast<const __nv_bfloat16*>(a.peer_bufs[a.rank + j]) + off));
+#pragma unroll
+    for (int j = 0; j < kTpMaxRanks; ++j) {
+      if (a.rank + j >= a.world) break;
+      const uint32_t ws[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const float2 f = unpack_bf16x2(ws[k]);

@@ -56,6 +56,13 @@ struct TpArgs {
   // (queries of the first half) and peer_bufs2 (queries of the second half).
   int zigzag = 0;
   void** peer_bufs2 = nullptr;
+  // Fused forms. pushed (gather): the rows were already stored into every
+  // rank's buffer by the kernel that produced them (RowPush), so the gather
+  // only synchronises. inbox (reduce-scatter): every rank's GEMM stored its
+  // partial of this rank's rows into this rank's inbox, [world][rows][cols]
+  // bf16 (slot = source rank), so the sum reads local memory only.
+  int pushed = 0;
+  const __nv_bfloat16* inbox = nullptr;
 };
 
 int tp_ag_rows_launch(TpArgs a, cudaStream_t s);

@@ -15,9 +15,10 @@ kernels with no autograd and no per-step allocation:
   attention straight on the fused qkv buffer -> c_proj GEMM whose epilogue adds
   bias and the fp32 residual out of place -> LN2 -> c_fc GEMM with fused
   bias+GELU (pre-activation kept) -> mlp c_proj GEMM with fused residual add ->
-  ln_f -> lm_head GEMM into a padded-vocab bf16 logits buffer -> one
-  cross-entropy kernel that writes the loss and overwrites logits with
-  dlogits = softmax - onehot.
+  ln_f -> lm_head GEMM into a padded-vocab bf16 logits buffer whose epilogue
+  also keeps per-row (max, sum exp) partials and the target logit -> a
+  per-row log-sum-exp / loss fold -> one streaming pass that overwrites the
+  logits with dlogits = softmax - onehot.
 * **Backward.** dgrad GEMMs read weights MN-major (no transposes), the
   mlp dgrad fuses GELU backward, wgrad GEMMs read activations MN-major and
   split K over tokens with a deterministic reduction, LayerNorm backward adds
@@ -42,8 +43,10 @@ import torch
 
 from gpt2_harness_b200.config import GPTConfig
 from gpt2_harness_b200.ops import native as N
+from gpt2_harness_b200.utils.nvtx import nvtx_range
 
-__all__ = ["ParamSpec", "ParamLayout", "Engine", "OptimConfig", "choose_splits", "init_flat_weights"]
+__all__ = ["ParamSpec", "ParamLayout", "CompactLayout", "Engine", "OptimConfig", "choose_splits",
+           "init_flat_weights"]
 
 ALIGN = 64  # elements; 128 bytes of bf16, 256 bytes of fp32
 #: Device types the engine accepts. Only CUDA runs the native kernels; the
@@ -141,6 +144,52 @@ class ParamLayout:
         return [(s.offset, s.numel, s.decay) for s in self.specs]
 
 
+class CompactLayout:
+    """The tensors of a :class:`ParamLayout` that `keep` selects, packed in
+    the same order with the same alignment: flat storage for a subset of the
+    parameters. ZeRO-3 keeps only the replicated root tensors (ln_f, wte, wpe)
+    in the engine's own buffers; block tensors come from the gathered shards.
+
+    ``segments`` lists (full_lo, full_hi, lo) for every stored tensor: its
+    aligned range in the full layout and its start here."""
+
+    def __init__(self, full: ParamLayout, keep: Callable[[ParamSpec], bool]) -> None:
+        self.config = full.config
+        self.full = full
+        self.specs: list[ParamSpec] = []
+        self.segments: list[tuple[int, int, int]] = []
+        off = 0
+        for s in full.specs:
+            if not keep(s):
+                continue
+            span = (s.numel + ALIGN - 1) // ALIGN * ALIGN
+            self.specs.append(ParamSpec(s.name, s.shape, off, s.decay, s.group))
+            self.segments.append((s.offset, s.offset + span, off))
+            off += span
+        self.total = off
+        self.by_name = {s.name: s for s in self.specs}
+
+    @property
+    def num_parameters(self) -> int:
+        return self.full.num_parameters
+
+    def view(self, flat: torch.Tensor, name: str) -> torch.Tensor:
+        s = self.by_name[name]
+        return flat[s.offset : s.offset + s.numel].view(s.shape)
+
+    def gather_from_full(self, full: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """out[compact] = full[layout] for every stored tensor."""
+        for a, b, o in self.segments:
+            out[o : o + b - a].copy_(full[a:b])
+        return out
+
+    def scatter_to_full(self, compact: torch.Tensor, full: torch.Tensor) -> torch.Tensor:
+        """full[layout] = compact for every stored tensor."""
+        for a, b, o in self.segments:
+            full[a:b].copy_(compact[o : o + b - a])
+        return full
+
+
 @torch.no_grad()
 def init_flat_weights(layout: ParamLayout, flat: torch.Tensor, seed: int = 0) -> torch.Tensor:
     """Fill `flat` (fp32, ``layout.total`` elements, on a CUDA device) with the
@@ -210,7 +259,8 @@ class _Acts:
         self.hf = torch.empty(M, C, dtype=bf, device=dev)
         vp = cfg.padded_vocab_size()
         self.logits = torch.empty(M, vp, dtype=bf, device=dev)
-        self.loss_rows = torch.empty(M, dtype=f32, device=dev)
+        self.ce = N.CEWorkspace(M, cfg.vocab_size, dev)
+        self.loss_rows = self.ce.loss_rows
         self.loss_out = torch.zeros(2, dtype=f32, device=dev)
         # backward scratch (reused across layers)
         self.dres = torch.empty(M, C, dtype=f32, device=dev)
@@ -254,15 +304,19 @@ class Engine:
     def __init__(self, config: GPTConfig, device: torch.device | str = "cuda", *,
                  optim: Optional[OptimConfig] = None, grad_buffer: Optional[torch.Tensor] = None,
                  shadow_buffer: Optional[torch.Tensor] = None, seed: Optional[int] = 0,
-                 optimizer_state: bool = True) -> None:
+                 optimizer_state: bool = True, storage: Optional[CompactLayout] = None) -> None:
         self.config = config
         self.device = torch.device(device)
         if self.device.type not in DEVICE_TYPES:
             raise ValueError("the native engine runs on CUDA devices")
         N.lib()  # fail loudly if the extension is missing
         self.layout = ParamLayout(config)
+        # the layout of the engine's own flat buffers: every tensor, or the
+        # subset a parameter-sharding strategy leaves here (ZeRO-3: the root)
+        self.storage = storage if storage is not None else self.layout
+        self.init_seed = seed
         self.optim = optim or OptimConfig()
-        n = self.layout.total
+        n = self.storage.total
         dev = self.device
         self.master = torch.zeros(n, dtype=torch.float32, device=dev)
         if shadow_buffer is not None:
@@ -333,7 +387,7 @@ class Engine:
     # ------------------------------------------------------------ weights --
     def _merge_segments(self):
         segs = []
-        for s in self.layout.specs:
+        for s in self.storage.specs:
             lo = s.offset
             hi = s.offset + (s.numel + ALIGN - 1) // ALIGN * ALIGN
             if segs and segs[-1][2] == s.decay and segs[-1][1] == lo:
@@ -343,28 +397,36 @@ class Engine:
         return segs
 
     def p32(self, name: str) -> torch.Tensor:
-        return self.layout.view(self.master, name)
+        return self.storage.view(self.master, name)
 
     def p16(self, name: str) -> torch.Tensor:
         if self.param_source is not None:
             v = self.param_source(name)
             if v is not None:
                 return v
-        return self.layout.view(self.shadow, name)
+        return self.storage.view(self.shadow, name)
 
     def g32(self, name: str) -> torch.Tensor:
         if self.grad_source is not None:
             v = self.grad_source(name)
             if v is not None:
                 return v
-        return self.layout.view(self.grad, name)
+        return self.storage.view(self.grad, name)
 
     @torch.no_grad()
     def init_weights(self, seed: int = 0) -> None:
         """GPT-2 init on the device: N(0, 0.02) for matmul weights and
         embeddings, N(0, 0.02/sqrt(2L)) for the two residual projections,
         zero biases, unit LayerNorm gains (reference model.py:488-518)."""
-        init_flat_weights(self.layout, self.master, seed)
+        self.init_seed = seed
+        if self.storage is self.layout:
+            init_flat_weights(self.layout, self.master, seed)
+        else:
+            # the same values as the full layout's init (one generator in
+            # layout order), kept for the stored tensors only
+            full = torch.empty(self.layout.total, dtype=torch.float32, device=self.device)
+            self.storage.gather_from_full(init_flat_weights(self.layout, full, seed), self.master)
+            del full
         self.sync_shadow()
 
     @torch.no_grad()
@@ -374,7 +436,7 @@ class Engine:
     @torch.no_grad()
     def load_state_dict(self, sd: dict) -> None:
         """Load a reference-named state dict (GPT.state_dict())."""
-        for s in self.layout.specs:
+        for s in self.storage.specs:
             src = sd[s.name] if s.name in sd else sd.get("lm_head.weight") if s.name == "wte.weight" else None
             if src is None:
                 raise KeyError(s.name)
@@ -383,7 +445,7 @@ class Engine:
 
     def state_dict(self) -> dict:
         """Reference-named fp32 state dict (``lm_head.weight`` tied to wte)."""
-        out = {s.name: self.p32(s.name).detach().clone() for s in self.layout.specs}
+        out = {s.name: self.p32(s.name).detach().clone() for s in self.storage.specs}
         out["lm_head.weight"] = out["wte.weight"]
         return out
 
@@ -406,8 +468,7 @@ class Engine:
         """Forward pass; returns the device scalar loss (loss_out[0]).
         Also leaves dlogits in the logits buffer for :meth:`backward`."""
         targets = targets.contiguous()
-        A = self._forward_to_logits(idx)
-        N.cross_entropy_fwd_bwd(A.logits, targets.view(-1), A.loss_rows, A.loss_out, self.config.vocab_size)
+        A = self._forward_to_logits(idx, targets)
         return A.loss_out[0]
 
     @torch.no_grad()
@@ -416,7 +477,10 @@ class Engine:
         engine's buffer, valid until the next forward)."""
         return self._forward_to_logits(idx).logits[:, : self.config.vocab_size]
 
-    def _forward_to_logits(self, idx: torch.Tensor) -> _Acts:
+    def _forward_to_logits(self, idx: torch.Tensor, targets: Optional[torch.Tensor] = None) -> _Acts:
+        """Forward to the lm_head. With `targets`, the lm_head GEMM is the
+        fused cross-entropy (loss in loss_out, dlogits left in the logits
+        buffer); without, the buffer holds the logits."""
         cfg = self.config
         idx = idx.contiguous()
         B, T = idx.shape
@@ -435,6 +499,8 @@ class Engine:
             pre = f"h.{l}."
             if bh:
                 bh("fwd", l)
+            rng = nvtx_range(f"fwd/h.{l}")
+            rng.__enter__()
             N.layernorm_fwd(A.x[2 * l], p(pre + "ln_1.weight"), p(pre + "ln_1.bias"), A.h1[l],
                             A.mu[2 * l], A.rs[2 * l], eps)
             N.gemm(A.h1[l], p(pre + "attn.c_attn.weight"), A.qkv[l], bias=p(pre + "attn.c_attn.bias"))
@@ -451,8 +517,14 @@ class Engine:
                    bias=p(pre + "mlp.c_fc.bias"), aux=A.u[l])
             N.gemm(A.g[l], p(pre + "mlp.c_proj.weight"), A.x[2 * l + 2], epilogue=N.EPI_RESID_F32,
                    bias=p(pre + "mlp.c_proj.bias"), aux=A.x[2 * l + 1])
-        N.layernorm_fwd(A.x[2 * L], p("ln_f.weight"), p("ln_f.bias"), A.hf, A.mu[2 * L], A.rs[2 * L], eps)
-        N.gemm(A.hf, p("wte.weight"), A.logits[:, :V])
+            rng.__exit__(None, None, None)
+        with nvtx_range("lm_head+ce"):
+            N.layernorm_fwd(A.x[2 * L], p("ln_f.weight"), p("ln_f.bias"), A.hf, A.mu[2 * L], A.rs[2 * L],
+                            eps)
+            if targets is None:
+                N.gemm(A.hf, p("wte.weight"), A.logits[:, :V])
+            else:
+                N.lm_head_cross_entropy(A.hf, p("wte.weight"), A.logits, targets, A.ce, A.loss_out, V)
         return A
 
     # ------------------------------------------------------------ backward --
@@ -487,6 +559,8 @@ class Engine:
             pre = f"h.{l}."
             if bh:
                 bh("bwd", l)
+            rng = nvtx_range(f"bwd/h.{l}")
+            rng.__enter__()
             # mlp.c_proj
             N.gemm(A.dres16, p(pre + "mlp.c_proj.weight"), A.du, b_t=True, epilogue=N.EPI_GELU_BWD,
                    aux=A.u[l])
@@ -529,6 +603,7 @@ class Engine:
                             A.ln_parts, accumulate_dres=True, accumulate_params=acc,
                             dsum=g(f"h.{l - 1}.mlp.c_proj.bias") if (fuse and l > 0) else None,
                             accumulate_dsum=acc)
+            rng.__exit__(None, None, None)
             if hook:
                 hook(f"h.{l}")
         wpe_g = g("wpe.weight")
@@ -564,6 +639,11 @@ class Engine:
         ev = self._hp_events[slot] or torch.cuda.Event()
         ev.record()
         self._hp_events[slot] = ev
+        with nvtx_range("optimizer"):
+            self._optimizer_update()
+
+    def _optimizer_update(self) -> None:
+        o = self.optim
         if self.optimizer_impl is not None:
             self.optimizer_impl(self.hp)
             return

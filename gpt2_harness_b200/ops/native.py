@@ -38,10 +38,12 @@ __all__ = [
     "embedding_fwd",
     "embedding_bwd",
     "cross_entropy_fwd_bwd",
+    "CEWorkspace",
+    "lm_head_cross_entropy",
     "adamw_step",
 ]
 
-EPI_BF16, EPI_BIAS_GELU, EPI_RESID_F32, EPI_F32, EPI_GELU_BWD = 0, 1, 2, 3, 4
+EPI_BF16, EPI_BIAS_GELU, EPI_RESID_F32, EPI_F32, EPI_GELU_BWD, EPI_CE_STATS = 0, 1, 2, 3, 4, 5
 
 _LIB = None
 _LOAD_ERROR: Optional[BaseException] = None
@@ -146,6 +148,10 @@ def gemm(
     bn: int = 256,
     max_ctas: int = 0,
     pair: int = -1,
+    ce: Optional["CEWorkspace"] = None,
+    ce_targets: Optional[torch.Tensor] = None,
+    ce_vocab_offset: int = 0,
+    owner_out: Optional[tuple] = None,
 ) -> torch.Tensor:
     """out[M,N] (epilogue) = op(a) @ op(b)^T on the tcgen05 tensor cores.
 
@@ -154,6 +160,12 @@ def gemm(
     operand layout in the kernel: no transpose is ever materialised.
     ``pair`` = 1 runs 256x256 tiles on pairs of CTAs (one cta_group::2 MMA per
     pair), 0 one CTA per 128 x ``bn`` tile, -1 the library's default.
+    ``EPI_CE_STATS`` (the lm_head forward) also needs ``ce`` (a
+    :class:`CEWorkspace`) and the int64 ``ce_targets``.
+    ``owner_out = (bases, rows)`` stores row m of the (bf16) result at
+    bases[m // rows] + (m % rows) * ldo instead of into ``out`` (which then only
+    gives the shape and row stride): tensor parallelism's GEMM -> reduce-
+    scatter, each partial row written straight into its owner's inbox.
     """
     _check_cuda(a, b, out, bias, aux, alpha_ptr, workspace)
     if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
@@ -181,12 +193,24 @@ def gemm(
             raise ValueError("split-K needs the fp32 epilogue")
         if workspace is None or workspace.numel() < splits * M * N:
             raise ValueError("split-K workspace too small")
+    ce_ptrs = (0, 0, 0)
+    if epilogue == EPI_CE_STATS:
+        if ce is None or ce_targets is None or ce_targets.dtype != torch.int64:
+            raise TypeError("EPI_CE_STATS needs a CEWorkspace and int64 targets")
+        if ce.M != M or ce.nparts < CEWorkspace.parts(N) or ce_targets.numel() != M:
+            raise ValueError("CEWorkspace / targets do not match the GEMM shape")
+        if bias is not None or splits > 1:
+            raise ValueError("EPI_CE_STATS takes no bias and no split-K")
+        bn = 256
+        ce_ptrs = (ce.stats.data_ptr(), ce_targets.data_ptr(), ce.tgt_logit.data_ptr())
     lib().gemm(
         a.data_ptr(), _row_stride(a), int(a_t), b.data_ptr(), _row_stride(b), int(b_t),
         M, N, K, epilogue, out.data_ptr(), _row_stride(out), _ptr(aux),
         0 if aux is None else _row_stride(aux), _ptr(bias), float(alpha), _ptr(alpha_ptr),
-        int(accumulate), int(splits), _ptr(workspace), int(bn), int(max_ctas), int(pair), _err_ptr(),
-        _stream(),
+        int(accumulate), int(splits), _ptr(workspace), int(bn), int(max_ctas), int(pair),
+        ce_ptrs[0], ce_ptrs[1], ce_ptrs[2], int(ce_vocab_offset),
+        0 if owner_out is None else owner_out[0].data_ptr(),
+        0 if owner_out is None else int(owner_out[1]), _err_ptr(), _stream(),
     )
     return out
 
@@ -263,13 +287,27 @@ def attention_bwd(q, k, v, o, dout, dq, dk, dv, lse, delta, B: int, H: int, Tq: 
 
 
 # ----------------------------------------------------------------- layernorm --
+def _push_args(push) -> tuple:
+    """(device pointer array, count, local base) of a row push, or zeros."""
+    if push is None:
+        return 0, 0, 0
+    bases, n, local = push
+    return bases.data_ptr(), int(n), int(local)
+
+
 def layernorm_fwd(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, y: torch.Tensor,
-                  mean: torch.Tensor, rstd: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
-    """y(bf16) = LN(x fp32) * gamma + beta over the last dim; saves mean/rstd."""
+                  mean: torch.Tensor, rstd: torch.Tensor, eps: float = 1e-5,
+                  push: Optional[tuple] = None) -> torch.Tensor:
+    """y(bf16) = LN(x fp32) * gamma + beta over the last dim; saves mean/rstd.
+
+    ``push = (bases, n, local)`` also stores every output row into n peer
+    copies of the buffer (int64 device tensor of base addresses; the row at
+    address a goes to bases[j] + (a - local)): the all-gather of tensor
+    parallelism fused into the LayerNorm that produces the rows."""
     M, C = x.shape
     lib().layernorm_fwd(x.data_ptr(), _row_stride(x), gamma.data_ptr(), beta.data_ptr(),
                         y.data_ptr(), _row_stride(y), mean.data_ptr(), rstd.data_ptr(), M, C,
-                        float(eps), _stream())
+                        float(eps), *_push_args(push), _stream())
     return y
 
 
@@ -283,8 +321,12 @@ def layernorm_bwd(dy: torch.Tensor, x: torch.Tensor, mean: torch.Tensor, rstd: t
                   gamma: torch.Tensor, dres: torch.Tensor, dres_bf16: Optional[torch.Tensor],
                   dgamma: torch.Tensor, dbeta: torch.Tensor, partials: torch.Tensor,
                   accumulate_dres: bool, accumulate_params: bool = True,
-                  dsum: Optional[torch.Tensor] = None, accumulate_dsum: bool = False) -> None:
+                  dsum: Optional[torch.Tensor] = None, accumulate_dsum: bool = False,
+                  push: Optional[tuple] = None) -> None:
     """LN backward: dres (+)= dx (fp32, plus optional bf16 copy); dgamma/dbeta (+)=.
+
+    ``push`` (see :func:`layernorm_fwd`) also stores the bf16 copy's rows
+    into peer copies of its buffer.
 
     With ``dsum`` (fp32 [C]), also dsum (+)= the column sum of the written
     dres: the bias gradient of the projection whose output is this residual
@@ -297,7 +339,7 @@ def layernorm_bwd(dy: torch.Tensor, x: torch.Tensor, mean: torch.Tensor, rstd: t
                         gamma.data_ptr(), dres.data_ptr(), _ptr(dres_bf16), partials.data_ptr(),
                         dgamma.data_ptr(), dbeta.data_ptr(), _ptr(dsum), M, C,
                         int(accumulate_dres), int(accumulate_params), int(accumulate_dsum),
-                        _stream())
+                        *_push_args(push), _stream())
 
 
 def colsum_bf16(x: torch.Tensor, out: torch.Tensor, ws: torch.Tensor, accumulate: bool = True) -> None:
@@ -347,6 +389,50 @@ def cross_entropy_fwd_bwd(logits: torch.Tensor, targets: torch.Tensor, loss_rows
     L.cross_entropy(logits.data_ptr(), _row_stride(logits), targets.data_ptr(),
                     loss_rows.data_ptr(), M, vocab, 0, _stream())
     L.loss_reduce(loss_rows.data_ptr(), targets.data_ptr(), M, loss_out.data_ptr(), _stream())
+
+
+class CEWorkspace:
+    """Buffers of the fused lm_head + cross-entropy for M rows: the GEMM
+    epilogue's (max, sum exp) partials (2 per 256 vocabulary columns), the
+    target logits, the per-row log-sum-exp and loss."""
+
+    def __init__(self, M: int, vocab: int, device) -> None:
+        self.M = M
+        self.nparts = self.parts(vocab)
+        self.stats = torch.empty(self.nparts * M * 2, dtype=torch.float32, device=device)
+        self.tgt_logit = torch.zeros(M, dtype=torch.float32, device=device)
+        self.lse = torch.empty(M, dtype=torch.float32, device=device)
+        self.loss_rows = torch.empty(M, dtype=torch.float32, device=device)
+
+    @staticmethod
+    def parts(vocab: int) -> int:
+        return 2 * (-(-vocab // 256))
+
+
+def lm_head_cross_entropy(h: torch.Tensor, w: torch.Tensor, logits: torch.Tensor,
+                          targets: torch.Tensor, ws: CEWorkspace, loss_out: torch.Tensor,
+                          vocab: int) -> None:
+    """Fused lm_head + cross-entropy (reference model.py:585,593-598: logits
+    = ln_f(x) @ wte^T, then F.cross_entropy with ignore_index -100).
+
+    1. ``logits[:, :vocab] = h @ w^T`` on the tcgen05 GEMM whose epilogue also
+       keeps, per row, online (max, sum exp) partials of the bf16 logits and
+       picks out the target logit -- no separate statistics pass;
+    2. one thread per row folds the partials into log-sum-exp and the loss;
+    3. one streaming pass turns the logits into softmax - onehot in place.
+
+    loss_out[0] = mean loss over non-ignored targets, loss_out[1] = 1/count
+    (the scale the lm_head backward GEMMs apply through alpha_ptr).
+    """
+    M = h.shape[0]
+    t = targets.reshape(-1)
+    gemm(h, w, logits[:, :vocab], epilogue=EPI_CE_STATS, ce=ws, ce_targets=t)
+    L = lib()
+    L.ce_combine(ws.stats.data_ptr(), ws.nparts, M, t.data_ptr(), ws.tgt_logit.data_ptr(),
+                 ws.lse.data_ptr(), ws.loss_rows.data_ptr(), _stream())
+    L.loss_reduce(ws.loss_rows.data_ptr(), t.data_ptr(), M, loss_out.data_ptr(), _stream())
+    L.ce_grad(logits.data_ptr(), _row_stride(logits), M, vocab, ws.lse.data_ptr(), t.data_ptr(), 0,
+              _stream())
 
 
 def cast_f32_bf16(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:

@@ -33,6 +33,7 @@ import torch.distributed as dist
 
 from gpt2_harness_b200.models.engine import ALIGN, ParamLayout
 from gpt2_harness_b200.ops import native as N
+from gpt2_harness_b200.utils.nvtx import nvtx_range
 from gpt2_harness_b200.parallel import comms
 from gpt2_harness_b200.parallel.symm import SymmetricBuffer
 
@@ -163,7 +164,7 @@ class NativeDDP:
         ev.record()
         self.stream.wait_event(ev)
         comms.record_external("all_reduce", b.numel, b.numel * 4)
-        with torch.cuda.stream(self.stream):
+        with torch.cuda.stream(self.stream), nvtx_range(f"allreduce/bucket{self.buckets.index(b)}"):
             if self.comm == "p2p":
                 self.epoch += 1
                 fn = N.lib().allreduce_p2p_slim if slim else N.lib().allreduce_p2p

@@ -53,6 +53,7 @@ from gpt2_harness_b200.ops import native as N
 from gpt2_harness_b200.parallel import comms
 from gpt2_harness_b200.parallel.symm import SymmetricBuffer
 from gpt2_harness_b200.parallel.tensor_parallel import padded_vocab
+from gpt2_harness_b200.utils.nvtx import nvtx_range
 
 __all__ = ["head_partition", "TPLayout", "TPEngine"]
 
@@ -177,7 +178,7 @@ class TPEngine:
 
     def __init__(self, config: GPTConfig, B: int, T: int, device=None, *,
                  optim: Optional[OptimConfig] = None, group=None, seed: int = 0,
-                 nblocks: int = 128) -> None:
+                 nblocks: int = 128, fused: bool = True) -> None:
         if not dist.is_initialized():
             # a single process: a one-rank group over an in-memory store (the
             # peer-memory kernels then run with world 1)
@@ -215,8 +216,11 @@ class TPEngine:
         # cross-rank activation buffers
         nG = 2 * NL + 1
         self._G = SymmetricBuffer(nG * M * C * 2, group, dev)   # gathered LayerNorm outputs
-        self._P = SymmetricBuffer(M * C * 2, group, dev)        # row-parallel partials
-        self._D = SymmetricBuffer(M * C * 2, group, dev)        # gathered residual gradient
+        # Row-parallel partials and the gathered residual gradient are double
+        # buffered: use k+2 rewrites a buffer only after every rank has passed
+        # the handshake of use k+1, i.e. finished reading use k.
+        self._P = SymmetricBuffer(2 * M * C * 2, group, dev)    # row-parallel partials / inboxes
+        self._D = SymmetricBuffer(2 * M * C * 2, group, dev)    # gathered residual gradient
         self._stats = SymmetricBuffer(M * 4 * 4, group, dev)
         self._flags = SymmetricBuffer(L.tp_flag_words() * 4, group, dev)
         self._ar_flags = SymmetricBuffer(L.comm_flag_words() * 4, group, dev)
@@ -224,8 +228,23 @@ class TPEngine:
         self.G1 = [Gall[2 * l] for l in range(NL)]
         self.G2 = [Gall[2 * l + 1] for l in range(NL)]
         self.Gf = Gall[2 * NL]
-        self.P = self._P.view(bf, M * C).view(M, C)
-        self.Dg = self._D.view(bf, M * C).view(M, C)
+        Pall = self._P.view(bf, 2 * M * C).view(2, M, C)
+        Dall = self._D.view(bf, 2 * M * C).view(2, M, C)
+        self.Pbuf = [Pall[0], Pall[1]]
+        self.Dbuf = [Dall[0], Dall[1]]
+        self._pb = 0  # partial buffer of the next row-parallel GEMM
+        self._db = 0  # gradient buffer of the next residual-gradient gather
+        # Fused collectives (more than one rank): the LayerNorms store their
+        # rows into every rank's gather buffer (the gather kernels only
+        # synchronise) and the row-parallel GEMMs store each partial row into
+        # its owner's inbox, [p][Ms][C] in the partial buffer (the
+        # reduce-scatter kernels sum local memory).
+        self.fused = fused and self.world > 1
+        self._push_G = self._push_desc(self._G)
+        self._push_D = self._push_desc(self._D)
+        self._owner = [torch.tensor([self._P.peer_ptrs[q] + (b * M * C + self.rank * Ms * C) * 2
+                                     for q in range(self.world)], dtype=torch.int64, device=dev)
+                       for b in (0, 1)]
         self.stats = self._stats.view(f32, M * 4).view(M, 4)
         r0 = self.rank * Ms
         own = slice(r0, r0 + Ms)
@@ -330,10 +349,11 @@ class TPEngine:
         """All-gather of the row blocks of a [M, C] bf16 buffer."""
         C = self.config.n_embd
         comms.record_external("all_gather", self.M * C, self.M * C * 2)
-        d = self._args(sym, rows=self.Ms, cols=C)
+        d = self._args(sym, rows=self.Ms, cols=C, pushed=int(self.fused))
         if offset_bytes:
             d["peer_bufs"] = self._offset_ptrs(sym, offset_bytes).data_ptr()
-        N.lib().tp_ag_rows(d, self._stream())
+        with nvtx_range("tp/all_gather"):
+            N.lib().tp_ag_rows(d, self._stream())
 
     def _offset_ptrs(self, sym: SymmetricBuffer, offset_bytes: int) -> torch.Tensor:
         key = (id(sym), offset_bytes)
@@ -343,16 +363,51 @@ class TPEngine:
                                       device=self.device)
         return cache[key]
 
+    def _push_desc(self, sym: SymmetricBuffer) -> tuple:
+        """Row-push descriptor of a symmetric buffer: every other rank's base
+        address, their count and this rank's base (see N.layernorm_fwd)."""
+        others = [ptr for q, ptr in enumerate(sym.peer_ptrs) if q != self.rank]
+        return (torch.tensor(others or [0], dtype=torch.int64, device=self.device), len(others),
+                sym.peer_ptrs[self.rank])
+
+    def _row_gemm(self, a: torch.Tensor, w: torch.Tensor, **kw) -> None:
+        """A row-parallel GEMM into the current partial buffer; fused, every
+        row goes straight into its owner's inbox over NVLink."""
+        out = self.Pbuf[self._pb]
+        if self.fused:
+            N.gemm(a, w, out, owner_out=(self._owner[self._pb], self.Ms), **kw)
+        else:
+            N.gemm(a, w, out, **kw)
+
     def _rs(self, bias=None, resid=None, out_f32=None, out_bf16=None) -> None:
-        """Reduce-scatter of the bf16 partial buffer P into this rank's rows."""
-        C = self.config.n_embd
+        """Reduce-scatter of the current partial buffer into this rank's rows
+        (fused: the local inbox; else peers' partials by P2P loads)."""
+        C, b = self.config.n_embd, self._pb
         comms.record_external("reduce_scatter", self.M * C, self.M * C * 2)
         d = self._args(self._P, rows=self.Ms, cols=C,
                        bias=0 if bias is None else bias.data_ptr(),
                        resid=0 if resid is None else resid.data_ptr(),
                        out_f32=0 if out_f32 is None else out_f32.data_ptr(),
                        out_bf16=0 if out_bf16 is None else out_bf16.data_ptr())
-        N.lib().tp_rs_rows(d, self._stream())
+        if self.fused:
+            d["inbox"] = self.Pbuf[b].data_ptr()
+        elif b:
+            d["peer_bufs"] = self._offset_ptrs(self._P, b * self.M * C * 2).data_ptr()
+        with nvtx_range("tp/reduce_scatter"):
+            N.lib().tp_rs_rows(d, self._stream())
+        self._pb ^= 1
+
+    def _grad_rows(self) -> torch.Tensor:
+        """Where the next LayerNorm backward writes this rank's bf16 rows."""
+        return self.Dbuf[self._db][self.own]
+
+    def _gather_grad(self) -> torch.Tensor:
+        """All-gather of the residual-gradient rows just written; returns the
+        gathered [M, C] buffer (the next writes go to the other buffer)."""
+        b = self._db
+        self._ag(self._D, b * self.M * self.config.n_embd * 2)
+        self._db ^= 1
+        return self.Dbuf[b]
 
     def _g_offset(self, which: str, l: int = 0) -> int:
         C, M, NL = self.config.n_embd, self.M, self.config.n_layer
@@ -383,23 +438,23 @@ class TPEngine:
             pre = f"h.{l}."
             G1, G2 = self.G1[l], self.G2[l]
             N.layernorm_fwd(self.x[2 * l], p(pre + "ln_1.weight"), p(pre + "ln_1.bias"), G1[own],
-                            self.mu[2 * l], self.rs[2 * l], eps)
+                            self.mu[2 * l], self.rs[2 * l], eps, push=self._push_G if self.fused else None)
             self._ag(self._G, self._g_offset("G1", l))
             N.gemm(G1, p(pre + "attn.c_attn.weight"), self.qkv[l], bias=p(pre + "attn.c_attn.bias"))
             qkv = self.qkv[l]
             N.attention_fwd(qkv[:, :hd], qkv[:, hd:2 * hd], qkv[:, 2 * hd:], self.y[l], self.lse[l],
                             B, H, T)
-            N.gemm(self.y[l], p(pre + "attn.c_proj.weight"), self.P)
+            self._row_gemm(self.y[l], p(pre + "attn.c_proj.weight"))
             self._rs(bias=p(pre + "attn.c_proj.bias"), resid=self.x[2 * l], out_f32=self.x[2 * l + 1])
             N.layernorm_fwd(self.x[2 * l + 1], p(pre + "ln_2.weight"), p(pre + "ln_2.bias"), G2[own],
-                            self.mu[2 * l + 1], self.rs[2 * l + 1], eps)
+                            self.mu[2 * l + 1], self.rs[2 * l + 1], eps, push=self._push_G if self.fused else None)
             self._ag(self._G, self._g_offset("G2", l))
             N.gemm(G2, p(pre + "mlp.c_fc.weight"), self.g[l], epilogue=N.EPI_BIAS_GELU,
                    bias=p(pre + "mlp.c_fc.bias"), aux=self.u[l])
-            N.gemm(self.g[l], p(pre + "mlp.c_proj.weight"), self.P)
+            self._row_gemm(self.g[l], p(pre + "mlp.c_proj.weight"))
             self._rs(bias=p(pre + "mlp.c_proj.bias"), resid=self.x[2 * l + 1], out_f32=self.x[2 * l + 2])
         N.layernorm_fwd(self.x[2 * NL], p("ln_f.weight"), p("ln_f.bias"), self.Gf[own],
-                        self.mu[2 * NL], self.rs[2 * NL], eps)
+                        self.mu[2 * NL], self.rs[2 * NL], eps, push=self._push_G if self.fused else None)
         self._ag(self._G, self._g_offset("Gf"))
         N.gemm(self.Gf, p("wte.weight"), self.logits[:, :lay.Vl])
         # vocabulary-parallel cross-entropy
@@ -426,36 +481,37 @@ class TPEngine:
         hd = H * D
         inv = self.loss_out[1:2]
         dl = self.logits[:, :lay.Vl]
-        Dg, Down = self.Dg, self.Dg[own]
         ws = self.splitk_ws
         # lm_head (tied, vocabulary-parallel)
-        N.gemm(dl, p("wte.weight"), self.P, b_t=True, alpha_ptr=inv)
+        self._row_gemm(dl, p("wte.weight"), b_t=True, alpha_ptr=inv)
         N.gemm(dl, self.Gf, g("wte.weight"), a_t=True, b_t=True, epilogue=N.EPI_F32, alpha_ptr=inv)
         self._rs(out_bf16=self.dh)
+        Down = self._grad_rows()
         N.layernorm_bwd(self.dh, self.x[2 * NL], self.mu[2 * NL], self.rs[2 * NL], p("ln_f.weight"),
                         self.dres, Down, g("ln_f.weight"), g("ln_f.bias"), self.ln_parts,
-                        accumulate_dres=False, accumulate_params=False)
+                        accumulate_dres=False, accumulate_params=False, push=self._push_D if self.fused else None)
         for l in reversed(range(NL)):
             pre = f"h.{l}."
             # --- MLP
             N.colsum_bf16(Down, g(pre + "mlp.c_proj.bias"), self.col_ws, accumulate=False)
-            self._ag(self._D)
+            Dg = self._gather_grad()
             N.gemm(Dg, p(pre + "mlp.c_proj.weight"), self.du, b_t=True, epilogue=N.EPI_GELU_BWD,
                    aux=self.u[l])
             N.gemm(Dg, self.g[l], g(pre + "mlp.c_proj.weight"), a_t=True, b_t=True,
                    epilogue=N.EPI_F32, splits=self.splits["mlp_proj"], workspace=ws)
-            N.gemm(self.du, p(pre + "mlp.c_fc.weight"), self.P, b_t=True)
+            self._row_gemm(self.du, p(pre + "mlp.c_fc.weight"), b_t=True)
             N.gemm(self.du, self.G2[l], g(pre + "mlp.c_fc.weight"), a_t=True, b_t=True,
                    epilogue=N.EPI_F32, splits=self.splits["c_fc"], workspace=ws)
             N.colsum_bf16(self.du, g(pre + "mlp.c_fc.bias"), self.col_ws, accumulate=False)
             self._rs(out_bf16=self.dh)
+            Down = self._grad_rows()
             N.layernorm_bwd(self.dh, self.x[2 * l + 1], self.mu[2 * l + 1], self.rs[2 * l + 1],
                             p(pre + "ln_2.weight"), self.dres, Down, g(pre + "ln_2.weight"),
                             g(pre + "ln_2.bias"), self.ln_parts, accumulate_dres=True,
-                            accumulate_params=False)
+                            accumulate_params=False, push=self._push_D if self.fused else None)
             # --- attention
             N.colsum_bf16(Down, g(pre + "attn.c_proj.bias"), self.col_ws, accumulate=False)
-            self._ag(self._D)
+            Dg = self._gather_grad()
             N.gemm(Dg, p(pre + "attn.c_proj.weight"), self.dy, b_t=True)
             N.gemm(Dg, self.y[l], g(pre + "attn.c_proj.weight"), a_t=True, b_t=True,
                    epilogue=N.EPI_F32, splits=self.splits["c_proj"], workspace=ws)
@@ -463,15 +519,16 @@ class TPEngine:
             N.attention_bwd(qkv[:, :hd], qkv[:, hd:2 * hd], qkv[:, 2 * hd:], self.y[l], self.dy,
                             dqkv[:, :hd], dqkv[:, hd:2 * hd], dqkv[:, 2 * hd:], self.lse[l], self.delta,
                             B, H, T)
-            N.gemm(dqkv, p(pre + "attn.c_attn.weight"), self.P, b_t=True)
+            self._row_gemm(dqkv, p(pre + "attn.c_attn.weight"), b_t=True)
             N.gemm(dqkv, self.G1[l], g(pre + "attn.c_attn.weight"), a_t=True, b_t=True,
                    epilogue=N.EPI_F32, splits=self.splits["c_attn"], workspace=ws)
             N.colsum_bf16(dqkv, g(pre + "attn.c_attn.bias"), self.col_ws, accumulate=False)
             self._rs(out_bf16=self.dh)
+            Down = self._grad_rows()
             N.layernorm_bwd(self.dh, self.x[2 * l], self.mu[2 * l], self.rs[2 * l],
                             p(pre + "ln_1.weight"), self.dres, Down, g(pre + "ln_1.weight"),
                             g(pre + "ln_1.bias"), self.ln_parts, accumulate_dres=True,
-                            accumulate_params=False)
+                            accumulate_params=False, push=self._push_D if self.fused else None)
         # embedding: wte rows into their owners' gradient shards, wpe locally
         wpe_g = g("wpe.weight")
         wpe_g.zero_()

@@ -34,6 +34,12 @@ B200 design:
   and on the replicated root.
 * Activations are kept (no recompute): B200 memory holds them at the
   benchmark shapes, so the MFU numerator counts the model FLOPs actually run.
+* Nothing full-size stays resident: the engine is built on
+  :attr:`storage_layout` (only the root tensors in its fp32 master, bf16 copy
+  and fp32 gradient), block parameters exist as bf16 shards plus the two
+  gather buffers, block gradients as two max-unit fp32 buffers plus the fp32
+  shard. At GPT-2 medium on 8 ranks that leaves ~0.2 GB of root tensors where
+  the full-size bf16 copy and fp32 gradient took 2.1 GB.
 
 Payload per rank per step in the reference convention (all-gather = output,
 reduce-scatter = input): sum over units of (2 + 2 + 4) x span_u bytes for the
@@ -48,10 +54,11 @@ from typing import Optional
 import torch
 import torch.distributed as dist
 
-from gpt2_harness_b200.models.engine import ALIGN, ParamLayout
+from gpt2_harness_b200.models.engine import ALIGN, CompactLayout, ParamLayout, init_flat_weights
 from gpt2_harness_b200.ops import native as N
 from gpt2_harness_b200.parallel import comms
 from gpt2_harness_b200.parallel.symm import SymmetricBuffer
+from gpt2_harness_b200.utils.nvtx import nvtx_range
 
 __all__ = ["NativeZeRO3", "unit_plan"]
 
@@ -97,15 +104,20 @@ class NativeZeRO3:
         self.shard_numel = sum(u["slice"] for u in self.units)
         self.max_span = max(u["span"] for u in self.units)
         self.nblocks = nblocks
-        # root ranges: [0, a) = ln_f, [b, total) = wte, wpe
-        self.root_ranges = [(0, self.units[-1]["lo"]), (self.units[0]["hi"], layout.total)]
+        # The engine's flat buffers hold the root tensors only (ln_f, then
+        # wte and wpe), packed: root_ranges are [0, a) = ln_f (no decay) and
+        # [a, n_root) = wte, wpe (decay) in that packed storage.
+        self.storage_layout = CompactLayout(layout, lambda s: s.group == "root")
+        sto = self.storage_layout
+        a = sto.by_name["wte.weight"].offset
+        self.root_ranges = [(0, a), (a, sto.total)]
         # symmetric memory
-        self._grad_full = SymmetricBuffer(layout.total * 4, group, dev)    # root grads live here
+        self._grad_full = SymmetricBuffer(sto.total * 4, group, dev)        # root grads live here
         self._gbuf = SymmetricBuffer(2 * self.max_span * 4, group, dev)     # block grads, 2 slots
         self._pshard = SymmetricBuffer(self.shard_numel * 2, group, dev)    # bf16 shards
         self._flags = SymmetricBuffer(L.zero_flag_words() * 4, group, dev)
         self._ar_flags = SymmetricBuffer(L.comm_flag_words() * 4, group, dev)
-        self.grad_buffer = self._grad_full.view(torch.float32, layout.total)
+        self.grad_buffer = self._grad_full.view(torch.float32, sto.total)
         self.gbuf = self._gbuf.view(torch.float32, 2 * self.max_span)
         self.pshard = self._pshard.view(torch.bfloat16, self.shard_numel)
         self.gather = torch.zeros(2, self.max_span, dtype=torch.bfloat16, device=dev)
@@ -180,21 +192,30 @@ class NativeZeRO3:
         return torch.tensor(out, dtype=torch.int64, device=self.device)
 
     # -------------------------------------------------------------- setup --
-    def attach(self, engine) -> None:
+    def attach(self, engine, full_master: Optional[torch.Tensor] = None) -> None:
+        """Take over `engine` (built with ``grad_buffer=z.grad_buffer`` and
+        ``storage=z.storage_layout``). Block shards come from `full_master`
+        (a full fp32 vector in layout order, identical on every rank) or, by
+        default, from the engine's init seed (the same values its full-layout
+        init gives); the root from the engine's own buffers."""
         if engine.grad.data_ptr() != self.grad_buffer.data_ptr():
             raise ValueError("build the engine with grad_buffer=z.grad_buffer")
+        if engine.storage is not self.storage_layout:
+            raise ValueError("build the engine with storage=z.storage_layout")
         self.engine = engine
         with torch.no_grad():
+            full = full_master
+            if full is None:
+                full = torch.empty(self.layout.total, dtype=torch.float32, device=self.device)
+                init_flat_weights(self.layout, full, engine.init_seed or 0)
             for u in self.units:
                 f0 = u["lo"] + self.rank * u["slice"]
                 n = max(0, min(u["hi"], f0 + u["slice"]) - f0)
                 if n:
-                    self.master[u["off"]:u["off"] + n].copy_(engine.master[f0:f0 + n])
+                    self.master[u["off"]:u["off"] + n].copy_(full[f0:f0 + n])
+            del full
             self.pshard.copy_(self.master)
-            o = 0
-            for a, b in self.root_ranges:
-                self.root_master[o:o + b - a].copy_(engine.master[a:b])
-                o += b - a
+            self.root_master.copy_(engine.master[:self.storage_layout.total])
         engine.master = None
         engine.param_source = self._param
         engine.grad_source = self._grad
@@ -235,7 +256,8 @@ class NativeZeRO3:
         a["epoch"] = self.epoch & 0xFFFFFFFF
         a["gather_dst"] = self.gather[k % 2].data_ptr()
         a["ag_span"], a["ag_slice"], a["ag_offset"] = u["span"], u["slice"], u["off"]
-        N.lib().zero_ag(a, self.nblocks, self.stream.cuda_stream)
+        with nvtx_range(f"zero3/gather/h.{l}"):
+            N.lib().zero_ag(a, self.nblocks, self.stream.cuda_stream)
         ev = torch.cuda.Event()
         ev.record(self.stream)
         self._gathered[k] = ev
@@ -270,7 +292,8 @@ class NativeZeRO3:
         a = self._args
         a["epoch"] = self.epoch & 0xFFFFFFFF
         a["bucket"] = l
-        N.lib().zero_rs(a, self.stream.cuda_stream)
+        with nvtx_range(f"zero3/reduce_scatter/h.{l}"):
+            N.lib().zero_rs(a, self.stream.cuda_stream)
         done = torch.cuda.Event()
         done.record(self.stream)
         self._rs_done[self.L - 1 - l] = done
@@ -333,10 +356,7 @@ class NativeZeRO3:
                 n = max(0, min(u["hi"], f0 + u["slice"]) - f0)
                 if n:
                     full[f0:f0 + n].copy_(parts[r * S + u["off"]: r * S + u["off"] + n])
-        o = 0
-        for a, b in self.root_ranges:
-            full[a:b].copy_(root[o:o + b - a])
-            o += b - a
+        self.storage_layout.scatter_to_full(root, full)
         return full
 
     def full_master(self) -> torch.Tensor:
@@ -363,14 +383,12 @@ class NativeZeRO3:
                 self.exp_avg[sl].copy_(exp_avg[f0:f0 + n])
                 self.exp_avg_sq[sl].copy_(exp_avg_sq[f0:f0 + n])
         self.pshard.copy_(self.master)
-        o = 0
-        for a, b in self.root_ranges:
-            self.root_master[o:o + b - a].copy_(master[a:b])
-            if exp_avg is not None:
-                self.root_m[o:o + b - a].copy_(exp_avg[a:b])
-                self.root_v[o:o + b - a].copy_(exp_avg_sq[a:b])
-            self.engine.shadow[a:b].copy_(master[a:b])
-            o += b - a
+        sto = self.storage_layout
+        sto.gather_from_full(master, self.root_master)
+        if exp_avg is not None:
+            sto.gather_from_full(exp_avg, self.root_m)
+            sto.gather_from_full(exp_avg_sq, self.root_v)
+        self.engine.shadow.copy_(self.root_master)
 
     def close(self) -> None:
         torch.cuda.synchronize(self.device)

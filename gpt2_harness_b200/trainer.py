@@ -137,9 +137,11 @@ class Trainer:
                 self.ddp = NativeDDP(layout, comm=comm, bucket_bytes=bucket_bytes,
                                      device=self.device, nblocks=comm_blocks)
             grad_buffer = self.ddp.grad_buffer
+        storage = self.ddp.storage_layout if self.strategy == "zero3" else None
         self.engine = Engine(config, self.device, optim=optim, grad_buffer=grad_buffer,
                              shadow_buffer=shadow_buffer, seed=seed,
-                             optimizer_state=self.strategy not in ("zero2", "zero3"))
+                             optimizer_state=self.strategy not in ("zero2", "zero3"),
+                             storage=storage)
         if self.ddp is not None:
             dist.broadcast(self.engine.master, src=0)
             self.engine.sync_shadow()

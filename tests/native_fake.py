@@ -52,7 +52,8 @@ def _row_bytes_ok(t, esz):
 
 
 def gemm(a, b, out, *, a_t=False, b_t=False, epilogue=N.EPI_BF16, bias=None, aux=None, alpha=1.0,
-         alpha_ptr=None, accumulate=False, splits=1, workspace=None, bn=256, max_ctas=0, pair=-1):
+         alpha_ptr=None, accumulate=False, splits=1, workspace=None, bn=256, max_ctas=0, pair=-1,
+         ce=None, ce_targets=None, ce_vocab_offset=0, owner_out=None):
     # operand loads are TMA: 16-byte aligned bases and row strides (csrc/gemm.cu)
     _require(a.dtype == torch.bfloat16 and b.dtype == torch.bfloat16, "gemm operands bf16")
     _require(_row_bytes_ok(a, 2) and _row_bytes_ok(b, 2), "gemm operand alignment")
@@ -67,7 +68,17 @@ def gemm(a, b, out, *, a_t=False, b_t=False, epilogue=N.EPI_BF16, bias=None, aux
     dst = out[:, :n]
     if bias is not None and epilogue in (N.EPI_BF16, N.EPI_BIAS_GELU, N.EPI_RESID_F32):
         r = r + bias[:n].float()
-    if epilogue == N.EPI_BF16:
+    if epilogue == N.EPI_BF16 and owner_out is not None:
+        # row m goes to its owner's inbox: bases[m // rows] + (m % rows) * ldo
+        bases, rows = owner_out
+        ld = out.stride(0)
+        for q, base in enumerate(int(b) for b in bases.reshape(-1)):
+            blk = r[q * rows:(q + 1) * rows]
+            if blk.shape[0] == 0:
+                break
+            view = _at(base, rows * ld, torch.bfloat16).view(rows, ld)[:, :n]
+            view.copy_(blk)
+    elif epilogue == N.EPI_BF16:
         dst.copy_(r)
     elif epilogue == N.EPI_BIAS_GELU:
         aux[:, :n].copy_(r)
@@ -84,7 +95,17 @@ def gemm(a, b, out, *, a_t=False, b_t=False, epilogue=N.EPI_BF16, bias=None, aux
     return out
 
 
-def layernorm_fwd(x, gamma, beta, y, mean, rstd, eps=1e-5):
+def _push_rows(t, push):
+    """The kernels' row push: the rows of `t` also land in every peer copy."""
+    if push is None:
+        return
+    bases, n, local = push
+    _require(t.is_contiguous(), "pushed rows are contiguous")
+    for base in [int(b) for b in bases.reshape(-1)[:n]]:
+        _at(base + (t.data_ptr() - int(local)), t.numel(), t.dtype).copy_(t.reshape(-1))
+
+
+def layernorm_fwd(x, gamma, beta, y, mean, rstd, eps=1e-5, push=None):
     _require(x.shape[-1] % 4 == 0 and x.dtype == torch.float32 and y.dtype == torch.bfloat16, "layernorm shapes")
     xf = x.float()
     mu = xf.mean(-1)
@@ -93,6 +114,7 @@ def layernorm_fwd(x, gamma, beta, y, mean, rstd, eps=1e-5):
     mean.copy_(mu)
     rstd.copy_(rs)
     y.copy_((xf - mu[:, None]) * rs[:, None] * gamma.float() + beta.float())
+    _push_rows(y, push)
     return y
 
 
@@ -101,7 +123,7 @@ def layernorm_bwd_partials(M, C, device):
 
 
 def layernorm_bwd(dy, x, mean, rstd, gamma, dres, dres_bf16, dgamma, dbeta, partials, accumulate_dres,
-                  accumulate_params=True, dsum=None, accumulate_dsum=False):
+                  accumulate_params=True, dsum=None, accumulate_dsum=False, push=None):
     xhat = (x.float() - mean[:, None]) * rstd[:, None]
     g = dy.float()
     dxhat = g * gamma.float()
@@ -109,6 +131,7 @@ def layernorm_bwd(dy, x, mean, rstd, gamma, dres, dres_bf16, dgamma, dbeta, part
     dres.copy_(dres + dx if accumulate_dres else dx)
     if dres_bf16 is not None:
         dres_bf16.copy_(dres)
+        _push_rows(dres_bf16, push)
     dg, db = (g * xhat).sum(0), g.sum(0)
     dgamma.copy_(dgamma + dg if accumulate_params else dg)
     dbeta.copy_(dbeta + db if accumulate_params else db)
@@ -165,6 +188,13 @@ def cross_entropy_fwd_bwd(logits, targets, loss_rows, loss_out, vocab):
     grad = grad * valid[:, None]
     logits[:, :vocab].copy_(grad)
     logits[:, vocab:].zero_()
+
+
+def lm_head_cross_entropy(h, w, logits, targets, ws, loss_out, vocab):
+    # the fused path's contract: the GEMM, then the cross-entropy's loss and
+    # in-place gradient over the whole padded buffer
+    gemm(h, w, logits[:, :vocab])
+    cross_entropy_fwd_bwd(logits, targets.reshape(-1), ws.loss_rows, loss_out, vocab)
 
 
 def _heads(t, b, rows, T, H):
@@ -423,9 +453,10 @@ def tp_ag_rows(d, stream=0):
     rank, world, rows, cols = d["rank"], d["world"], d["rows"], d["cols"]
     bufs = [_at(p, world * rows * cols, torch.bfloat16).view(world * rows, cols) for p in _peers(d)]
     dist.barrier(group=_group(d["peer_flags"]))
-    for q in range(world):
-        if q != rank:
-            bufs[rank][q * rows:(q + 1) * rows] = bufs[q][q * rows:(q + 1) * rows]
+    if not d.get("pushed"):  # pushed: the producer already stored its rows everywhere
+        for q in range(world):
+            if q != rank:
+                bufs[rank][q * rows:(q + 1) * rows] = bufs[q][q * rows:(q + 1) * rows]
     dist.barrier(group=_group(d["peer_flags"]))
 
 
@@ -434,8 +465,13 @@ def tp_rs_rows(d, stream=0):
     bufs = [_at(p, world * rows * cols, torch.bfloat16).view(world * rows, cols) for p in _peers(d)]
     dist.barrier(group=_group(d["peer_flags"]))
     acc = torch.zeros(rows, cols)
-    for q in range(world):
-        acc += bufs[q][rank * rows:(rank + 1) * rows].float()
+    if d.get("inbox"):  # slot q of the local inbox holds peer q's partial of these rows
+        inbox = _at(d["inbox"], world * rows * cols, torch.bfloat16).view(world, rows, cols)
+        for q in range(world):
+            acc += inbox[q].float()
+    else:
+        for q in range(world):
+            acc += bufs[q][rank * rows:(rank + 1) * rows].float()
     if d.get("bias"):
         acc += _at(d["bias"], cols, torch.bfloat16).float()
     if d.get("resid"):
@@ -660,7 +696,8 @@ OPS = {
     "gemm": gemm, "layernorm_fwd": layernorm_fwd, "layernorm_bwd": layernorm_bwd,
     "layernorm_bwd_partials": layernorm_bwd_partials, "colsum_bf16": colsum_bf16,
     "embedding_fwd": embedding_fwd, "embedding_bwd": embedding_bwd,
-    "cross_entropy_fwd_bwd": cross_entropy_fwd_bwd, "attention_fwd": attention_fwd,
+    "cross_entropy_fwd_bwd": cross_entropy_fwd_bwd, "lm_head_cross_entropy": lm_head_cross_entropy,
+    "attention_fwd": attention_fwd,
     "attention_bwd": attention_bwd, "grad_sumsq": grad_sumsq, "clip_coef": clip_coef,
     "adamw_step": adamw_step, "cast_f32_bf16": cast_f32_bf16, "decode_embed": decode_embed,
     "decode_partials": decode_partials, "decode_attn": decode_attn, "decode_argmax": decode_argmax,

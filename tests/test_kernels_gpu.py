@@ -362,6 +362,48 @@ def test_cross_entropy():
     assert logits[:, V:].abs().max().item() == 0
 
 
+@pytest.mark.parametrize("M,V,ld,pair", [(300, 50257, 50304, 0), (1000, 50257, 50304, 1),
+                                          (520, 1000, 1024, 1), (264, 777, 784, 0)])
+def test_lm_head_cross_entropy_fused(M, V, ld, pair):
+    """GEMM epilogue statistics + log-sum-exp fold + in-place gradient against
+    torch fp32 F.cross_entropy on the same bf16 logits (odd M and V, ignored
+    rows, padded columns), on single CTAs and on CTA pairs."""
+    C = 768
+    g = torch.Generator(device="cpu").manual_seed(M + V)
+    h = torch.randn(M, C, generator=g).to(dev(), torch.bfloat16)
+    w = (torch.randn(V, C, generator=g) * 0.08).to(dev(), torch.bfloat16)
+    tgt = torch.randint(0, V, (M,), generator=g).to(dev())
+    tgt[::7] = -100
+    logits = torch.full((M, ld), 7.0, dtype=torch.bfloat16, device=dev())
+    ws = N.CEWorkspace(M, V, dev())
+    out = torch.empty(2, device=dev())
+    ref_logits = (h.float() @ w.float().t()).bfloat16().float().requires_grad_(True)
+    ref = torch.nn.functional.cross_entropy(ref_logits, tgt, ignore_index=-100)
+    (gref,) = torch.autograd.grad(ref, ref_logits)
+    N.gemm(h, w, logits[:, :V], epilogue=N.EPI_CE_STATS, ce=ws, ce_targets=tgt, pair=pair)
+    lib = N.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    lib.ce_combine(ws.stats.data_ptr(), ws.nparts, M, tgt.data_ptr(), ws.tgt_logit.data_ptr(),
+                   ws.lse.data_ptr(), ws.loss_rows.data_ptr(), stream)
+    lib.loss_reduce(ws.loss_rows.data_ptr(), tgt.data_ptr(), M, out.data_ptr(), stream)
+    # the logits the epilogue stored are the bf16 GEMM result
+    assert rel_err(logits[:, :V], ref_logits.detach()) < 1e-2
+    lse_ref = torch.logsumexp(ref_logits.detach(), -1)
+    assert (ws.lse - lse_ref).abs().max().item() < 2e-3
+    lib.ce_grad(logits.data_ptr(), ld, M, V, ws.lse.data_ptr(), tgt.data_ptr(), 0, stream)
+    assert abs(out[0].item() - ref.item()) < 1e-3 * abs(ref.item())
+    count = (tgt != -100).sum().item()
+    assert abs(out[1].item() - 1.0 / count) < 1e-9
+    assert rel_err(logits[:, :V].float() * out[1], gref) < 2e-2
+    assert logits[:, V:].abs().max().item() == 0
+    # the public entry point does the same three steps
+    logits2 = torch.zeros(M, ld, dtype=torch.bfloat16, device=dev())
+    out2 = torch.empty(2, device=dev())
+    N.lm_head_cross_entropy(h, w, logits2, tgt, N.CEWorkspace(M, V, dev()), out2, V)
+    assert abs(out2[0].item() - out[0].item()) < 1e-6 * abs(out[0].item())
+    assert torch.equal(logits2, logits)
+
+
 # ------------------------------------------------------------------- AdamW --
 def test_adamw_matches_torch():
     n = 10007

@@ -37,8 +37,11 @@ WORKER = textwrap.dedent(r'''
     opt = dict(lr=1e-3, grad_clip=0.5)
     z = NativeZeRO3(layout)
     eng = Engine(cfg, "cuda", optim=OptimConfig(**opt), grad_buffer=z.grad_buffer, seed=0,
-                 optimizer_state=False)
+                 optimizer_state=False, storage=z.storage_layout)
     z.attach(eng)
+    # nothing full-size: the engine's own buffers hold the root tensors only
+    resident = {"engine_shadow": eng.shadow.numel(), "engine_grad": eng.grad.numel(),
+                "storage_total": z.storage_layout.total, "layout_total": layout.total}
     ref = Engine(cfg, "cuda", optim=OptimConfig(**opt), seed=0)
     # ZeRO-3 computes each block's c_proj bias gradients inside that block
     # (column sums of the bf16 residual gradient); make the reference do the
@@ -71,7 +74,8 @@ WORKER = textwrap.dedent(r'''
         summary = ctr.summary()
     spans = sum(u["span"] for u in z.units)
     out = {"rank": rank, "rows": rows, "payload_per_step": summary["payload_bytes_per_step"],
-           "spans": spans, "root_numel": z.root_numel, "device_bytes": int(z.byte_counter.item())}
+           "spans": spans, "root_numel": z.root_numel, "device_bytes": int(z.byte_counter.item()),
+           **resident}
     print("RESULT " + json.dumps(out), flush=True)
     z.close()
     dist.destroy_process_group()
@@ -123,3 +127,6 @@ def test_native_zero3_matches_unsharded(world, cfg):
         # per unit: two bf16 gathers + one fp32 reduce-scatter of its span;
         # root all-reduced in fp32; 4-byte norm all-reduce
         assert r["payload_per_step"] == 8 * r["spans"] + 4 * r["root_numel"] + 4, r
+        # the engine keeps exactly the (aligned) root tensors, none of the blocks
+        assert r["engine_shadow"] == r["engine_grad"] == r["storage_total"], r
+        assert r["layout_total"] - r["storage_total"] == r["spans"], r
