@@ -505,7 +505,7 @@ def main():
     ap.add_argument("--cp-balance", choices=["zigzag", "contiguous"], default="zigzag",
                     help="context-parallel split (cp and pp strategies)")
     ap.add_argument("--bucket-mb", type=float, default=25.0, help="gradient bucket size (MiB)")
-    ap.add_argument("--comm-blocks", type=int, default=148,
+    ap.add_argument("--comm-blocks", type=int, default=128,
                     help="CTAs of each fused all-reduce that overlaps backward")
     args = ap.parse_args()
     if args.warmup < 3:

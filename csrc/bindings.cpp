@@ -198,11 +198,14 @@ PYBIND11_MODULE(_C, m) {
   });
 
   m.def("embedding_bwd", [](int64_t idx, int64_t dx, int64_t wte_grad, int64_t wpe_grad, int B,
-                            int T, int C, int V, int pos0, int split, int pos1, int64_t stream) {
+                            int T, int C, int V, int pos0, int split, int pos1, int64_t det_part,
+                            int64_t det_slots, int64_t stream) {
     check(embedding_bwd_launch(P<int64_t>(idx), P<float>(dx), P<float>(wte_grad),
-                               P<float>(wpe_grad), B, T, C, V, pos0, split, pos1, S(stream)),
+                               P<float>(wpe_grad), B, T, C, V, pos0, split, pos1, S(stream),
+                               P<float>(det_part), P<int>(det_slots)),
           "embedding_bwd");
   });
+  m.def("embedding_wte_det_chunks", [](int64_t M) { return embedding_wte_det_chunks(M); });
 
   m.def("cross_entropy", [](int64_t logits, int64_t ld, int64_t targets, int64_t loss_rows, int M,
                             int V, int vocab_offset, int64_t stream) {

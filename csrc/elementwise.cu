@@ -6,8 +6,9 @@
 //   model.py:593-598       F.cross_entropy(ignore -100)    -> cross_entropy_fwd_bwd
 //   zero.py:158-186        AdamW (torch single-tensor order) -> adamw
 //   zero.py:194-233        global grad norm + clip coef    -> sumsq / clip_coef
-// Every reduction is deterministic (fixed order, no float atomics) except the
-// token-embedding scatter, which uses fp32 atomics.
+// Every reduction is deterministic (fixed order, no float atomics); the
+// token-embedding scatter has an fp32-atomic form for callers that give it no
+// workspace and a deterministic two-pass form (emb_det_*) for those that do.
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <math.h>
@@ -425,6 +426,133 @@ __global__ void emb_bwd_wpe_kernel(const float* __restrict__ dx, float* __restri
   }
 }
 
+// Deterministic token-embedding gradient: wte_grad[v] += sum of dx[m] over
+// the positions m with idx[m] == v, always summed in the same order, so the
+// result is bit-reproducible (the atomic scatter above is not).
+//   pass A  one CTA per chunk of EMB_CHUNK consecutive positions: the first
+//           occurrence of each token in the chunk sums that token's rows of
+//           the chunk in position order into part[m_first] and records
+//           slots[chunk][token] = m_first;
+//   pass B  one warp per vocabulary row: adds its chunks' partials in chunk
+//           order into wte_grad and resets the slots it used to -1.
+// The slot table [chunks, V] must hold -1 everywhere before pass A; pass B
+// leaves it so.
+constexpr int EMB_CHUNK = 128;
+constexpr int EMB_MAXV4 = 13;  // float4 per lane: C <= 32 * 4 * 13 = 1664
+
+__global__ void __launch_bounds__(256) emb_det_partial_kernel(const int64_t* __restrict__ idx,
+                                                              const float* __restrict__ dx,
+                                                              int64_t M, int C, int V,
+                                                              float* __restrict__ part,
+                                                              int* __restrict__ slots) {
+  __shared__ int tok[EMB_CHUNK];
+  __shared__ int nxt[EMB_CHUNK];  // next position of the same token in the chunk, or -1
+  __shared__ int lead[EMB_CHUNK];
+  const int64_t m0 = (int64_t)blockIdx.x * EMB_CHUNK;
+  const int n = (int)min((int64_t)EMB_CHUNK, M - m0);
+  for (int i = threadIdx.x; i < EMB_CHUNK; i += blockDim.x) {
+    int t = -1;
+    if (i < n) {
+      const int64_t v = idx[m0 + i];
+      t = (v >= 0 && v < V) ? (int)v : -1;
+    }
+    tok[i] = t;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int t = tok[i];
+    int first = t >= 0, after = -1;
+    for (int j = 0; j < i && first; ++j) first = tok[j] != t;
+    for (int j = i + 1; j < n && t >= 0; ++j)
+      if (tok[j] == t) {
+        after = j;
+        break;
+      }
+    lead[i] = first;
+    nxt[i] = after;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int i = warp; i < n; i += nw) {
+    if (!lead[i]) continue;
+    float4 acc[EMB_MAXV4];
+#pragma unroll
+    for (int u = 0; u < EMB_MAXV4; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = i; j >= 0; j = nxt[j]) {  // this token's positions, ascending
+      const float4* row = reinterpret_cast<const float4*>(dx + (m0 + j) * C);
+#pragma unroll
+      for (int u = 0; u < EMB_MAXV4; ++u) {
+        const int c4 = lane + 32 * u;
+        if (c4 * 4 < C) {
+          const float4 w = __ldg(row + c4);
+          acc[u].x += w.x;
+          acc[u].y += w.y;
+          acc[u].z += w.z;
+          acc[u].w += w.w;
+        }
+      }
+    }
+    float4* out = reinterpret_cast<float4*>(part + (m0 + i) * C);
+#pragma unroll
+    for (int u = 0; u < EMB_MAXV4; ++u) {
+      const int c4 = lane + 32 * u;
+      if (c4 * 4 < C) out[c4] = acc[u];
+    }
+    if (lane == 0) slots[(int64_t)blockIdx.x * V + tok[i]] = (int)(m0 + i);
+  }
+}
+
+__global__ void __launch_bounds__(256) emb_det_reduce_kernel(const float* __restrict__ part,
+                                                             int* __restrict__ slots,
+                                                             int nchunks, int C, int V,
+                                                             float* __restrict__ wte_grad) {
+  const int v = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (v >= V) return;
+  float4 acc[EMB_MAXV4];
+#pragma unroll
+  for (int u = 0; u < EMB_MAXV4; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+  bool any = false;
+  for (int k0 = 0; k0 < nchunks; k0 += 32) {
+    const int k = k0 + lane;
+    const int sl = k < nchunks ? slots[(int64_t)k * V + v] : -1;
+    unsigned hit = __ballot_sync(0xffffffffu, sl >= 0);
+    if (sl >= 0) slots[(int64_t)k * V + v] = -1;  // ready for the next call
+    while (hit) {  // chunks in ascending order
+      const int b = __ffs(hit) - 1;
+      hit &= hit - 1;
+      const int s = __shfl_sync(0xffffffffu, sl, b);
+      const float4* row = reinterpret_cast<const float4*>(part + (int64_t)s * C);
+#pragma unroll
+      for (int u = 0; u < EMB_MAXV4; ++u) {
+        const int c4 = lane + 32 * u;
+        if (c4 * 4 < C) {
+          const float4 w = row[c4];
+          acc[u].x += w.x;
+          acc[u].y += w.y;
+          acc[u].z += w.z;
+          acc[u].w += w.w;
+        }
+      }
+      any = true;
+    }
+  }
+  if (!any) return;
+  float4* g = reinterpret_cast<float4*>(wte_grad + (int64_t)v * C);
+#pragma unroll
+  for (int u = 0; u < EMB_MAXV4; ++u) {
+    const int c4 = lane + 32 * u;
+    if (c4 * 4 < C) {
+      float4 o = g[c4];
+      o.x += acc[u].x;
+      o.y += acc[u].y;
+      o.z += acc[u].z;
+      o.w += acc[u].w;
+      g[c4] = o;
+    }
+  }
+}
+
 // ----------------------------------------------------------- cross-entropy ---
 constexpr int CE_THREADS = 512;
 
@@ -826,11 +954,20 @@ int embedding_fwd_launch(const int64_t* idx, const void* wte, const void* wpe, f
   return ok();
 }
 
+int embedding_wte_det_chunks(int64_t M) { return (int)((M + EMB_CHUNK - 1) / EMB_CHUNK); }
+
 int embedding_bwd_launch(const int64_t* idx, const float* dx, float* wte_grad, float* wpe_grad,
-                         int B, int T, int C, int V, int pos0, int split, int pos1, cudaStream_t s) {
+                         int B, int T, int C, int V, int pos0, int split, int pos1, cudaStream_t s,
+                         float* det_part, int* det_slots) {
   if (split < 0 || split > T || pos0 < 0 || pos1 < 0) return -1;
   const int64_t M = (int64_t)B * T;
-  if (wte_grad) {
+  if (wte_grad && det_part && det_slots) {
+    if (C % 4 || C > 4 * 32 * EMB_MAXV4) return -1;
+    const int nchunks = embedding_wte_det_chunks(M);
+    emb_det_partial_kernel<<<nchunks, 256, 0, s>>>(idx, dx, M, C, V, det_part, det_slots);
+    emb_det_reduce_kernel<<<(V + 7) / 8, 256, 0, s>>>(det_part, det_slots, nchunks, C, V, wte_grad);
+    count_launches(2);
+  } else if (wte_grad) {
     emb_bwd_wte_kernel<<<grid_for(M * C, 256), 256, 0, s>>>(idx, dx, wte_grad, M, C, V);
     count_launches(1);
   }

@@ -51,8 +51,14 @@ int embedding_fwd_launch(const int64_t* idx, const void* wte, const void* wpe, f
 
 // Embedding backward: wte_grad[idx[m]] += dx[m] (fp32 atomics), and
 // wpe_grad[pos(t)] (+)= sum_b dx[b*T+t] (deterministic; pos as above).
+// With det_part (fp32 [B*T, C]) and det_slots (int32 [embedding_wte_det_chunks(B*T), V],
+// all -1 before the first call, left so by every call) the token-embedding
+// gradient is summed in a fixed order (bit-reproducible); without, by fp32
+// atomics.
 int embedding_bwd_launch(const int64_t* idx, const float* dx, float* wte_grad, float* wpe_grad,
-                         int B, int T, int C, int V, int pos0, int split, int pos1, cudaStream_t s);
+                         int B, int T, int C, int V, int pos0, int split, int pos1, cudaStream_t s,
+                         float* det_part = nullptr, int* det_slots = nullptr);
+int embedding_wte_det_chunks(int64_t M);
 
 // Cross-entropy over bf16 logits [M, V] (row stride ld) against int64 targets
 // (ignore_index -100). Writes loss_rows[M] (0 for ignored rows) and overwrites

@@ -107,7 +107,13 @@ __device__ __forceinline__ Slice my_slice(const ZeroArgs& a, int b) {
   return {f0, n, off};
 }
 
-__global__ void __launch_bounds__(512) zero_rs_kernel(const ZeroArgs a) {
+// The reduce-scatter and the parameter gather overlap backward / the
+// previous block's compute on a side stream: 128-thread CTAs with at most 80
+// registers a thread and 4 bytes of shared memory, so one fits on an SM next
+// to a resident persistent GEMM or attention CTA.
+constexpr int kZeroThreads = 128;
+
+__global__ void __launch_bounds__(kZeroThreads, 6) zero_rs_kernel(const ZeroArgs a) {
   __shared__ int fail;
   __shared__ float red[16];
   if (threadIdx.x == 0) fail = 0;
@@ -119,13 +125,19 @@ __global__ void __launch_bounds__(512) zero_rs_kernel(const ZeroArgs a) {
   const int64_t v0 = min(nv, per * blockIdx.x), v1 = min(nv, v0 + per);
   float ss = 0.f;
   for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
+    // every rank's load is issued before the first sum (rank order kept)
+    float4 w[kCommMaxRanks];
+#pragma unroll
+    for (int q = 0; q < kCommMaxRanks; ++q)
+      if (q < a.world) w[q] = __ldcg(reinterpret_cast<const float4*>(a.peer_grad[q] + sl.f0) + v);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int q = 0; q < a.world; ++q) {
-      const float4 w = __ldcg(reinterpret_cast<const float4*>(a.peer_grad[q] + sl.f0) + v);
-      acc.x += w.x;
-      acc.y += w.y;
-      acc.z += w.z;
-      acc.w += w.w;
+#pragma unroll
+    for (int q = 0; q < kCommMaxRanks; ++q) {
+      if (q >= a.world) break;
+      acc.x += w[q].x;
+      acc.y += w[q].y;
+      acc.z += w[q].z;
+      acc.w += w[q].w;
     }
     acc.x *= a.scale;
     acc.y *= a.scale;
@@ -146,19 +158,31 @@ __global__ void __launch_bounds__(512) zero_rs_kernel(const ZeroArgs a) {
   }
 }
 
-__global__ void __launch_bounds__(512) zero_ag_kernel(const ZeroArgs a) {
+__global__ void __launch_bounds__(kZeroThreads, 6) zero_ag_kernel(const ZeroArgs a) {
   __shared__ int fail;
   if (threadIdx.x == 0) fail = 0;
   __syncthreads();
   if (!zero_handshake(a, 0, &fail)) return;
   const int64_t nv = a.ag_span / 8;
   const int64_t sv = a.ag_slice / 8;
-  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nv;
-       v += (int64_t)gridDim.x * blockDim.x) {
-    const int q = (int)(v / sv);
-    const int64_t i = v - (int64_t)q * sv;
-    const uint4 w = __ldcg(reinterpret_cast<const uint4*>(a.peer_shard[q] + a.ag_offset) + i);
-    reinterpret_cast<uint4*>(a.gather_dst)[v] = w;
+  // slice q of the unit comes from rank q; kAgLoads independent 16-byte peer
+  // loads in flight per thread
+  constexpr int kAgLoads = 8;
+  const int64_t span = (int64_t)gridDim.x * blockDim.x;
+  for (int q = 0; q < a.world; ++q) {
+    const uint4* src = reinterpret_cast<const uint4*>(a.peer_shard[q] + a.ag_offset);
+    uint4* dst = reinterpret_cast<uint4*>(a.gather_dst) + (int64_t)q * sv;
+    const int64_t n = min(sv, nv - (int64_t)q * sv);
+    for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < n;
+         i0 += span * kAgLoads) {
+      uint4 w[kAgLoads];
+#pragma unroll
+      for (int u = 0; u < kAgLoads; ++u)
+        if (i0 + u * span < n) w[u] = __ldcg(src + i0 + u * span);
+#pragma unroll
+      for (int u = 0; u < kAgLoads; ++u)
+        if (i0 + u * span < n) dst[i0 + u * span] = w[u];
+    }
   }
   if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
     atomicAdd(a.byte_counter, (unsigned long long)a.ag_span * 2ull);
@@ -283,7 +307,7 @@ int zero_rs_launch(const ZeroArgs& a, cudaStream_t s) {
   if (a.world < 1 || a.world > kCommMaxRanks || a.rs_blocks < 1 || a.rs_blocks > kZeroMaxBlocks ||
       a.bucket < 0 || a.bucket >= a.nb)
     return -1;
-  zero_rs_kernel<<<a.rs_blocks, 512, 0, s>>>(a);
+  zero_rs_kernel<<<a.rs_blocks, kZeroThreads, 0, s>>>(a);
   count_launches(1);
   return launch_succeeded() ? 0 : -11;
 }
@@ -293,7 +317,7 @@ int zero_ag_launch(const ZeroArgs& a, int nblocks, cudaStream_t s) {
       a.ag_slice <= 0 || a.ag_slice % 64 || a.ag_span % 64 || a.ag_offset % 8 ||
       (a.ag_span + a.ag_slice - 1) / a.ag_slice > a.world)
     return -1;
-  zero_ag_kernel<<<nblocks, 512, 0, s>>>(a);
+  zero_ag_kernel<<<nblocks, kZeroThreads, 0, s>>>(a);
   count_launches(1);
   return launch_succeeded() ? 0 : -11;
 }

@@ -260,6 +260,8 @@ class _Acts:
         vp = cfg.padded_vocab_size()
         self.logits = torch.empty(M, vp, dtype=bf, device=dev)
         self.ce = N.CEWorkspace(M, cfg.vocab_size, dev)
+        # deterministic token-embedding gradient (bit-reproducible steps)
+        self.emb_ws = N.EmbeddingGradWorkspace(M, C, cfg.vocab_size, dev)
         self.loss_rows = self.ce.loss_rows
         self.loss_out = torch.zeros(2, dtype=f32, device=dev)
         # backward scratch (reused across layers)
@@ -610,7 +612,7 @@ class Engine:
         if not acc:
             wpe_g.zero_()
         N.embedding_bwd(idx, A.dres, g("wte.weight"), wpe_g, V, pos0=self.pos0,
-                        pos_split=self.pos_split, pos1=self.pos1)
+                        pos_split=self.pos_split, pos1=self.pos1, det=A.emb_ws)
         if hook:
             hook("root_tail")
 

@@ -40,6 +40,7 @@ __all__ = [
     "cross_entropy_fwd_bwd",
     "CEWorkspace",
     "lm_head_cross_entropy",
+    "EmbeddingGradWorkspace",
     "adamw_step",
 ]
 
@@ -366,14 +367,30 @@ def embedding_fwd(idx: torch.Tensor, wte: torch.Tensor, wpe: torch.Tensor, x: to
     return x
 
 
+class EmbeddingGradWorkspace:
+    """Buffers of the deterministic token-embedding gradient for M tokens:
+    per-chunk partial rows (fp32 [M, C]) and the [chunks, V] slot table, which
+    starts at -1 and is left at -1 by every call."""
+
+    def __init__(self, M: int, C: int, vocab: int, device) -> None:
+        self.part = torch.empty(M, C, dtype=torch.float32, device=device)
+        chunks = lib().embedding_wte_det_chunks(M)
+        self.slots = torch.full((chunks, vocab), -1, dtype=torch.int32, device=device)
+
+
 def embedding_bwd(idx: torch.Tensor, dx: torch.Tensor, wte_grad: Optional[torch.Tensor],
                   wpe_grad: Optional[torch.Tensor], vocab: int, pos0: int = 0,
-                  pos_split: Optional[int] = None, pos1: int = 0) -> None:
+                  pos_split: Optional[int] = None, pos1: int = 0,
+                  det: Optional[EmbeddingGradWorkspace] = None) -> None:
+    """wte_grad[idx[m]] += dx[m] (token embedding) and wpe_grad[pos] += sum over
+    the batch (positions), both fp32. With `det` the token sums run in a fixed
+    order and are bit-reproducible; without, they use fp32 atomics."""
     B, T = idx.shape
     C = dx.shape[-1]
     split = T if pos_split is None else int(pos_split)
     lib().embedding_bwd(idx.data_ptr(), dx.data_ptr(), _ptr(wte_grad), _ptr(wpe_grad), B, T, C,
-                        vocab, pos0, split, pos1, _stream())
+                        vocab, pos0, split, pos1, 0 if det is None else det.part.data_ptr(),
+                        0 if det is None else det.slots.data_ptr(), _stream())
 
 
 # --------------------------------------------------------------- cross-entropy --

@@ -182,6 +182,9 @@ class StageEngine:
         C = cfg.n_embd
         bf = torch.bfloat16
         self.dres = torch.empty(M, C, dtype=f32, device=dev)
+        # the first stage sums its token-embedding gradient deterministically
+        self.emb_ws = (N.EmbeddingGradWorkspace(M, C, config.vocab_size, dev)
+                       if lay.first else None)
         self.dres16 = torch.empty(M, C, dtype=bf, device=dev)
         self.dh = torch.empty(M, C, dtype=bf, device=dev)
         self.dy = torch.empty(M, C, dtype=bf, device=dev)
@@ -353,7 +356,7 @@ class StageEngine:
                 g("wte.weight").zero_()
                 wpe_g.zero_()
             N.embedding_bwd(idx, self.dres, g("wte.weight"), wpe_g, V, pos0=self.pos0,
-                            pos_split=self.pos_split, pos1=self.pos1)
+                            pos_split=self.pos_split, pos1=self.pos1, det=self.emb_ws)
 
     # -------------------------------------------------------------- step --
     def train_step(self, micro_idx: list, micro_tgt: list) -> torch.Tensor:

@@ -42,6 +42,7 @@ M x C bf16 (forward 2 + 2, backward 2 + 2): in the reference convention
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
 import torch
@@ -239,7 +240,7 @@ class TPEngine:
         # synchronise) and the row-parallel GEMMs store each partial row into
         # its owner's inbox, [p][Ms][C] in the partial buffer (the
         # reduce-scatter kernels sum local memory).
-        self.fused = fused and self.world > 1
+        self.fused = fused and self.world > 1 and os.environ.get("G2B_TP_FUSED", "1") != "0"
         self._push_G = self._push_desc(self._G)
         self._push_D = self._push_desc(self._D)
         self._owner = [torch.tensor([self._P.peer_ptrs[q] + (b * M * C + self.rank * Ms * C) * 2

@@ -88,7 +88,7 @@ class NativeZeRO3:
     """
 
     def __init__(self, layout: ParamLayout, group=None, device: Optional[torch.device] = None,
-                 nblocks: int = 64, wait_budget_ns: int = 2_000_000_000) -> None:
+                 nblocks: int = 148, wait_budget_ns: int = 2_000_000_000) -> None:
         if not dist.is_initialized():
             raise RuntimeError("NativeZeRO3 needs an initialised process group")
         self.group = group

@@ -86,7 +86,7 @@ class NativeZeRO:
     """
 
     def __init__(self, layout: ParamLayout, group=None, bucket_bytes: int = DEFAULT_BUCKET_BYTES,
-                 device: Optional[torch.device] = None, rs_blocks: int = 64, opt_blocks: int = 148,
+                 device: Optional[torch.device] = None, rs_blocks: int = 148, opt_blocks: int = 148,
                  wait_budget_ns: int = 2_000_000_000) -> None:
         if not dist.is_initialized():
             raise RuntimeError("NativeZeRO needs an initialised process group")

@@ -102,6 +102,13 @@ def run_suite(batch: int = 16, seq: int = 1024, C: int = 768, H: int = 12, V: in
     vp = (V + 63) // 64 * 64
     logits = torch.empty(M, vp, device=dev, dtype=bf)
     add("gemm_lm_head_fwd", lambda: N.gemm(x, wte, logits[:, :V]), 2.0 * M * V * C)
+    tgt = torch.randint(0, V, (M,), device=dev)
+    lo = torch.empty(2, device=dev)
+    cews = N.CEWorkspace(M, V, dev)
+    # the whole fused lm_head + cross-entropy forward (GEMM with statistics
+    # epilogue, row fold, gradient pass); against gemm_lm_head_fwd + cross_entropy
+    add("lm_head_ce_fused", lambda: N.lm_head_cross_entropy(x, wte, logits, tgt, cews, lo, V),
+        2.0 * M * V * C)
 
     # attention (causal: half the dense FLOPs)
     lse = torch.empty(batch, H, seq, device=dev)
@@ -132,9 +139,7 @@ def run_suite(batch: int = 16, seq: int = 1024, C: int = 768, H: int = 12, V: in
     cws = torch.empty(N.colsum_ws_numel(M, 4 * C), device=dev)
     bg = torch.zeros(4 * C, device=dev)
     add("bias_grad_colsum", lambda: N.colsum_bf16(h4, bg, cws), bytes_=M * 4 * C * 2)
-    tgt = torch.randint(0, V, (M,), device=dev)
     rows_ = torch.empty(M, device=dev)
-    lo = torch.empty(2, device=dev)
     add("cross_entropy", lambda: N.cross_entropy_fwd_bwd(logits, tgt, rows_, lo, V), bytes_=3 * M * vp * 2)
     n = 124_439_808
     p = torch.zeros(n, device=dev)
@@ -144,8 +149,69 @@ def run_suite(batch: int = 16, seq: int = 1024, C: int = 768, H: int = 12, V: in
     pb = torch.empty(n, device=dev, dtype=bf)
     hp = torch.tensor([3e-4, 0.9, 0.95, 1e-8, 0.1, 0.1, 0.1, 1.0], device=dev)
     add("adamw", lambda: N.adamw_step(p, gg, m1, v1, pb, n, hp), bytes_=n * (4 * 7 + 2))
+    _comm_kernels(add, dev, M, C)
     N.check_errors()
     return rows
+
+
+def _comm_kernels(add, dev, M: int, C: int) -> None:
+    """The peer-memory collectives at world 1 on this GPU (their handshakes
+    reduce to this rank's own flags; the data path is the same code): what a
+    one-GPU ncu capture of comm.cu, tp.cu and zero.cu kernels measures."""
+    L = N.lib()
+    err = N.error_word(dev).data_ptr()
+    stream = lambda: torch.cuda.current_stream().cuda_stream  # noqa: E731
+    epoch = [0]
+
+    def nxt() -> int:
+        epoch[0] += 1
+        return epoch[0]
+
+    ptrs = lambda t: torch.tensor([t.data_ptr()], dtype=torch.int64, device=dev)  # noqa: E731
+    counter = torch.zeros(1, dtype=torch.int64, device=dev)
+    # fused all-reduce (the wide kernel DDP uses): one 25 MiB fp32 bucket
+    nb = 25 * 2**20 // 4
+    bucket = torch.randn(nb, device=dev)
+    cflags = torch.zeros(L.comm_flag_words(), dtype=torch.int32, device=dev)
+    pb, pf = ptrs(bucket), ptrs(cflags)
+    add("allreduce_p2p_w1",
+        lambda: L.allreduce_p2p(pb.data_ptr(), pf.data_ptr(), 0, 1, 0, nb, 0, 1.0, nxt(),
+                                counter.data_ptr(), err, 128, 2_000_000_000, stream()),
+        bytes_=nb * 4 * 2)
+    # tensor-parallel reduce-scatter from the local inbox (+ bias + fp32 residual)
+    inbox = torch.randn(M, C, device=dev).to(torch.bfloat16)
+    bias = torch.zeros(C, device=dev, dtype=torch.bfloat16)
+    resid = torch.randn(M, C, device=dev)
+    out = torch.empty(M, C, device=dev)
+    tflags = torch.zeros(L.tp_flag_words(), dtype=torch.int32, device=dev)
+    pi, ptf = ptrs(inbox), ptrs(tflags)
+
+    def tp_rs():
+        L.tp_rs_rows({"peer_bufs": pi.data_ptr(), "peer_flags": ptf.data_ptr(), "rank": 0, "world": 1,
+                      "rows": M, "cols": C, "nblocks": 128, "epoch": nxt(), "err": err,
+                      "bias": bias.data_ptr(), "resid": resid.data_ptr(), "out_f32": out.data_ptr(),
+                      "inbox": inbox.data_ptr()}, stream())
+
+    add("tp_rs_rows_w1", tp_rs, bytes_=M * C * (2 + 4 + 4))
+    # ZeRO-3 parameter gather: one GPT-2 small block (7.1M bf16 parameters)
+    span = 7_087_872
+    shard = torch.randn(span, device=dev).to(torch.bfloat16)
+    dst = torch.empty(span, device=dev, dtype=torch.bfloat16)
+    zflags = torch.zeros(L.zero_flag_words(), dtype=torch.int32, device=dev)
+    ps, pzf = ptrs(shard), ptrs(zflags)
+    zargs = {"peer_grad": 0, "peer_shadow": 0, "peer_flags": pzf.data_ptr(), "peer_norm": 0,
+             "rank": 0, "world": 1, "buckets": 0, "nb": 0, "bucket": 0, "rs_blocks": 148, "gsh": 0,
+             "master": 0, "exp_avg": 0, "exp_avg_sq": 0, "sumsq_parts": 0, "decay_ranges": 0,
+             "nr": 0, "hp": 0, "max_norm": 0.0, "scale": 1.0, "epoch": 0,
+             "byte_counter": counter.data_ptr(), "norm_out": 0, "err": err,
+             "wait_budget_ns": 2_000_000_000, "done_handshake": 0, "peer_shard": ps.data_ptr(),
+             "gather_dst": dst.data_ptr(), "ag_span": span, "ag_slice": span, "ag_offset": 0}
+
+    def zero_ag():
+        zargs["epoch"] = nxt()
+        L.zero_ag(zargs, 148, stream())
+
+    add("zero_ag_w1", zero_ag, bytes_=span * 2 * 2)
 
 
 def main() -> None:

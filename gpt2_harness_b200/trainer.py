@@ -60,8 +60,7 @@ class Trainer:
             ``batch_size`` full sequences of ``seq_len`` tokens and computes
             its contiguous ``seq_len / p`` slice of each.
         comm_blocks: CTAs of each fused peer-memory all-reduce that
-            overlaps backward (DDP and CP, p2p): 128-thread CTAs that share
-            SMs with the backward's kernels.
+            overlaps backward (DDP and CP, p2p).
         cp_balance: context-parallel split, ``"zigzag"`` (two chunks per rank,
             equal causal work) or ``"contiguous"`` (one slice per rank).
         seed: weight init seed (identical on every rank; rank 0's weights are
@@ -72,7 +71,7 @@ class Trainer:
                  train: Optional[TrainConfig] = None, comm: str = "p2p",
                  device: Optional[torch.device] = None, seed: int = 0,
                  bucket_bytes: int = 25 * 1024 * 1024, schedule: bool = True,
-                 strategy: str = "ddp", comm_blocks: int = 148, cp_balance: str = "zigzag") -> None:
+                 strategy: str = "ddp", comm_blocks: int = 128, cp_balance: str = "zigzag") -> None:
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device())
         self.device = torch.device(device)

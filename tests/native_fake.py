@@ -158,7 +158,7 @@ def embedding_fwd(idx, wte, wpe, x, pos0=0, pos_split=None, pos1=0):
     return x
 
 
-def embedding_bwd(idx, dx, wte_grad, wpe_grad, vocab, pos0=0, pos_split=None, pos1=0):
+def embedding_bwd(idx, dx, wte_grad, wpe_grad, vocab, pos0=0, pos_split=None, pos1=0, det=None):
     B, T = idx.shape
     C = dx.shape[-1]
     d = dx.reshape(B, T, C)
@@ -708,7 +708,8 @@ LIB = SimpleNamespace(zero_rs=zero_rs, zero_adamw_ag=zero_adamw_ag, zero_ag=zero
                       cp_kv_gather=cp_kv_gather, cp_kv_reduce=cp_kv_reduce, tp_flag_words=lambda: 16,
                       allreduce_p2p=allreduce_p2p, allreduce_p2p_slim=allreduce_p2p_slim, comm_flag_words=lambda: 16, tp_ag_rows=tp_ag_rows,
                       tp_rs_rows=tp_rs_rows, tp_embed_fwd=tp_embed_fwd, tp_embed_bwd=tp_embed_bwd,
-                      tp_ce_stats=tp_ce_stats, tp_ce_finish=tp_ce_finish, loss_reduce=loss_reduce)
+                      tp_ce_stats=tp_ce_stats, tp_ce_finish=tp_ce_finish, loss_reduce=loss_reduce,
+                      embedding_wte_det_chunks=lambda M: -(-M // 128))
 
 
 @contextmanager

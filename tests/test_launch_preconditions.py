@@ -28,18 +28,23 @@ def _rejected(fn, *args, name):
 
 def test_gemm_rejects_empty_and_bad_tile():
     # M = 0
+    # trailing: pair, ce_stats, ce_targets, ce_tgt_logit, ce_vocab_offset, owner_out,
+    # owner_rows, err, stream
+    tail = (-1, 0, 0, 0, 0, 0, 0, 0, 0)
     _rejected(L.gemm, A16, 64, 0, A16, 64, 0, 0, 64, 64, 0, A16, 64, 0, 0, 0, 1.0, 0, 0, 1, 0, 256, 0,
-              0, 0, name="gemm_bf16")
+              *tail, name="gemm_bf16")
     # unsupported N tile
     _rejected(L.gemm, A16, 64, 0, A16, 64, 0, 128, 128, 64, 0, A16, 128, 0, 0, 0, 1.0, 0, 0, 1, 0, 96,
-              0, 0, 0, name="gemm_bf16")
+              0, *tail, name="gemm_bf16")
 
 
 def test_norm_and_embedding_shapes():
     # LayerNorm width not a multiple of 4
-    _rejected(L.layernorm_fwd, A16, 6, A16, A16, A16, 6, A16, A16, 8, 6, 1e-5, 0, name="layernorm_fwd")
-    _rejected(L.layernorm_bwd, A16, A16, A16, A16, A16, A16, 0, A16, A16, A16, 0, 0, 768, 0, 0, 0, 0,
-              name="layernorm_bwd")
+    # (the three zeros before the stream: no row push)
+    _rejected(L.layernorm_fwd, A16, 6, A16, A16, A16, 6, A16, A16, 8, 6, 1e-5, 0, 0, 0, 0,
+              name="layernorm_fwd")
+    _rejected(L.layernorm_bwd, A16, A16, A16, A16, A16, A16, 0, A16, A16, A16, 0, 0, 768, 0, 0, 0,
+              0, 0, 0, 0, name="layernorm_bwd")
     # embedding: position split outside the sequence, negative offsets
     _rejected(L.embedding_fwd, A16, A16, A16, A16, 2, 16, 64, 0, 17, 0, 0, name="embedding_fwd")
     _rejected(L.embedding_bwd, A16, A16, A16, A16, 2, 16, 64, 100, -1, 16, 0, 0, name="embedding_bwd")
