@@ -164,7 +164,9 @@ __device__ __forceinline__ void ew_kv(uint32_t (&sv)[NC], uint32_t (&dv)[NC], co
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int ii = q * 4 + u;
-      float pr = ex2f(fmaf(__uint_as_float(sv[ii]), sl2, -la[u]));
+      // odd columns on the FMA pipe (exp2_fma), even ones on the exponential unit
+      const float e = fmaf(__uint_as_float(sv[ii]), sl2, -la[u]);
+      float pr = (u & 1) ? exp2_fma(e) : ex2f(e);
       if (MASK) {
         const int col = c0 + ii;
         const bool vis = col < Tq && row_in && (!causal || col >= min_q);
@@ -184,7 +186,8 @@ __device__ __forceinline__ void ew_q(const uint32_t (&sv)[NC], uint32_t (&dv)[NC
                                      int abs_row) {
 #pragma unroll
   for (int ii = 0; ii < NC; ++ii) {
-    float pr = ex2f(fmaf(__uint_as_float(sv[ii]), sl2, -lse));
+    const float e = fmaf(__uint_as_float(sv[ii]), sl2, -lse);
+    float pr = (ii & 1) ? exp2_fma(e) : ex2f(e);  // odd columns on the FMA pipe
     if (MASK) {
       const int col = c0 + ii;
       const bool vis = col < Tk && row_in && (!causal || col <= abs_row);

@@ -414,10 +414,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // All 64 exponentials first (in place, independent: the exponential
         // unit stays busy), then the masked row sum and the bf16 P tile.
+        // the exponential unit takes the first 32 keys, the FMA pipe the
+        // other 32 (exp2_fma): the two pipes run side by side
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           sa[i] = __float_as_uint(ex2f(fmaf(__uint_as_float(sa[i]), p.sl2, -base)));
-          sb[i] = __float_as_uint(ex2f(fmaf(__uint_as_float(sb[i]), p.sl2, -base)));
+          sb[i] = __float_as_uint(exp2_fma(fmaf(__uint_as_float(sb[i]), p.sl2, -base)));
         }
         if (need_mask) {
 #pragma unroll

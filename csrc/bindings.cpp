@@ -61,7 +61,7 @@ PYBIND11_MODULE(_C, m) {
          int epi, int64_t out, int64_t ldo, int64_t aux, int64_t ldaux, int64_t bias, float alpha,
          int64_t alpha_ptr, int accumulate, int splits, int64_t workspace, int bn, int max_ctas,
          int pair, int64_t ce_stats, int64_t ce_targets, int64_t ce_tgt_logit, int ce_vocab_offset,
-         int64_t owner_out, int owner_rows, int64_t err, int64_t stream) {
+         int64_t owner_out, int owner_rows, int owner_self, int64_t err, int64_t stream) {
         GemmArgs g;
         g.A = P<void>(A);
         g.lda = lda;
@@ -92,6 +92,7 @@ PYBIND11_MODULE(_C, m) {
         g.ce_vocab_offset = ce_vocab_offset;
         g.owner_out = P<void*>(owner_out);
         g.owner_rows = owner_rows;
+        g.owner_self = owner_self;
         g.err = P<uint32_t>(err);
         check(gemm_bf16_launch(g, S(stream)), "gemm_bf16");
       });
@@ -214,6 +215,9 @@ PYBIND11_MODULE(_C, m) {
           "cross_entropy");
   });
 
+  m.def("exp2_fma_test", [](int64_t x, int64_t y, int n, int64_t stream) {
+    check(exp2_fma_test_launch(P<float>(x), P<float>(y), n, S(stream)), "exp2_fma_test");
+  });
   m.def("ce_combine", [](int64_t stats, int nparts, int M, int64_t targets, int64_t tgt_logit,
                          int64_t lse, int64_t loss_rows, int64_t stream) {
     check(ce_combine_launch(P<void>(stats), nparts, M, P<int64_t>(targets), P<float>(tgt_logit),

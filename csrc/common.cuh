@@ -499,6 +499,29 @@ __device__ __forceinline__ float gelu_tanh_grad_f(float x) {
   return 0.5f * (1.0f + t) + 0.5f * x * dt;
 }
 
+// 2^x on the FMA pipe, for softmax kernels whose exponential unit (MUFU) is
+// the bottleneck: half of a row's exponentials go here, half to ex2.approx.
+// Cody-Waite range reduction x = n + f with n = round(x) (magic-number
+// rounding: adding 1.5 * 2^23 leaves n in the low mantissa bits) and
+// f in [-0.5, 0.5]; 2^f from a degree-4 polynomial whose coefficients are a
+// least-squares fit of 2^f, weighted for relative error, on 4000 Chebyshev
+// nodes of [-0.5, 0.5] (near-minimax; max relative error 2.7e-6 evaluated in
+// fp32); n is then added to the exponent field. Valid for x in [-125, 127];
+// smaller x are clamped to 2^-125 (callers zero masked entries themselves).
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -125.f);
+  const float magic = 12582912.f;  // 1.5 * 2^23
+  const float j = x + magic;
+  const float n = j - magic;
+  const float f = x - n;
+  float p = 0.009560510516166687f;
+  p = fmaf(p, f, 0.05591703951358795f);
+  p = fmaf(p, f, 0.24024981260299683f);
+  p = fmaf(p, f, 0.6931219696998596f);
+  p = fmaf(p, f, 0.9999991655349731f);
+  return __int_as_float(__float_as_int(p) + ((__float_as_int(j) - 0x4B400000) << 23));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);

@@ -66,7 +66,7 @@ int ln_dispatch(int C, F&& f) {
   return f(std::integral_constant<int, 16>{});
 }
 
-template <int LN_MAXV>
+template <int LN_MAXV, bool PUSH>
 __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x, int64_t ldx,
                                                      const __nv_bfloat16* __restrict__ g,
                                                      const __nv_bfloat16* __restrict__ bta,
@@ -115,14 +115,14 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x
       o.x = pack_bf16x2((v[i].x - mu) * rs * g01.x + b01.x, (v[i].y - mu) * rs * g01.y + b01.y);
       o.y = pack_bf16x2((v[i].z - mu) * rs * g23.x + b23.x, (v[i].w - mu) * rs * g23.y + b23.y);
       *reinterpret_cast<uint2*>(yr + 4 * c) = o;
-      push_store(push, yr + 4 * c, o);
+      if (PUSH) push_store(push, yr + 4 * c, o);
     }
   }
   if (lane == 0) {
     mean[row] = mu;
     rstd[row] = rs;
   }
-  if (push.n) __threadfence_system();  // pushed rows visible before any later signal
+  if (PUSH) __threadfence_system();  // pushed rows visible before any later signal
 }
 
 // LayerNorm backward, one warp per row, CTAs in clusters of LNB_CLUSTER.
@@ -141,7 +141,7 @@ constexpr int LNB_WARPS = 8;
 constexpr int LNB_CLUSTER = 8;
 constexpr int LNB_NSUM = 3;  // dgamma, dbeta, dsum
 
-template <int LN_MAXV>
+template <int LN_MAXV, bool PUSH>
 __global__ void __cluster_dims__(LNB_CLUSTER, 1, 1) __launch_bounds__(256) ln_bwd_kernel(
     const __nv_bfloat16* __restrict__ dy, const float* __restrict__ x,
     const float* __restrict__ mean, const float* __restrict__ rstd,
@@ -218,7 +218,7 @@ __global__ void __cluster_dims__(LNB_CLUSTER, 1, 1) __launch_bounds__(256) ln_bw
           w.x = pack_bf16x2(d.x, d.y);
           w.y = pack_bf16x2(d.z, d.w);
           *reinterpret_cast<uint2*>(db16 + 4 * c) = w;
-          push_store(push, db16 + 4 * c, w);
+          if (PUSH) push_store(push, db16 + 4 * c, w);
         }
         float4 a = my[c];
         a.x += d01.x * xh.x;
@@ -243,7 +243,7 @@ __global__ void __cluster_dims__(LNB_CLUSTER, 1, 1) __launch_bounds__(256) ln_bw
       }
     }
   }
-  if (push.n) __threadfence_system();  // pushed rows visible before any later signal
+  if (PUSH) __threadfence_system();  // pushed rows visible before any later signal
   __syncthreads();
   // CTA: fold the 8 warps' sums into warp 0's slot (fixed order).
   for (int c = threadIdx.x; c < nsum4; c += blockDim.x) {
@@ -669,36 +669,51 @@ __global__ void __launch_bounds__(256) ce_combine_kernel(const float2* __restric
   loss_rows[row] = targets[row] == -100 ? 0.f : lse - tgt_logit[row];
 }
 
-// Step 3: logits -> (softmax - onehot) in place, one 16-byte vector (8 bf16)
-// per thread and iteration: one read and one write of the logits. Ignored
-// rows and the padded columns [V, ld) become 0.
+// Step 3: logits -> (softmax - onehot) in place: one read and one write of
+// the logits. One warp per row (its log-sum-exp and target loaded once), each
+// lane with kCeGradLoads 16-byte vectors (8 bf16 each) in flight. Ignored rows
+// and the padded columns [V, ld) become 0.
+constexpr int kCeGradLoads = 4;
+
+__device__ __forceinline__ uint4 ce_grad_vec(uint4 w, int col0, int V, float L, int64_t tl,
+                                             bool ignore) {
+  uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = unpack_bf16x2(ws[j]);
+    const int c = col0 + 2 * j;
+    const float a = (ignore || c >= V) ? 0.f : __expf(f.x - L) - (c == tl ? 1.f : 0.f);
+    const float b = (ignore || c + 1 >= V) ? 0.f : __expf(f.y - L) - (c + 1 == tl ? 1.f : 0.f);
+    ws[j] = pack_bf16x2(a, b);
+  }
+  return make_uint4(ws[0], ws[1], ws[2], ws[3]);
+}
+
 __global__ void __launch_bounds__(256) ce_grad_kernel(__nv_bfloat16* __restrict__ logits,
                                                       int64_t ld, int M, int V,
                                                       const float* __restrict__ lse,
                                                       const int64_t* __restrict__ targets,
                                                       int vocab_offset) {
-  const int64_t per_row = ld / 8;
-  const int64_t total = (int64_t)M * per_row;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = i / per_row;
-    const int col0 = (int)(i - row * per_row) * 8;
+  const int lane = threadIdx.x & 31;
+  const int nvec = (int)(ld / 8);
+  for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < M;
+       row += gridDim.x * (blockDim.x >> 5)) {
     const int64_t t = __ldg(targets + row);
     const bool ignore = t == -100;
     const int64_t tl = t - vocab_offset;
     const float L = __ldg(lse + row);
-    uint4* ptr = reinterpret_cast<uint4*>(logits + row * ld + col0);
-    const uint4 w = __ldcs(ptr);
-    uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    uint4* rp = reinterpret_cast<uint4*>(logits + (int64_t)row * ld);
+    for (int v0 = lane; v0 < nvec; v0 += 32 * kCeGradLoads) {
+      uint4 w[kCeGradLoads];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = unpack_bf16x2(ws[j]);
-      const int c = col0 + 2 * j;
-      float a = (ignore || c >= V) ? 0.f : __expf(f.x - L) - (c == tl ? 1.f : 0.f);
-      float b = (ignore || c + 1 >= V) ? 0.f : __expf(f.y - L) - (c + 1 == tl ? 1.f : 0.f);
-      ws[j] = pack_bf16x2(a, b);
+      for (int u = 0; u < kCeGradLoads; ++u)
+        if (v0 + 32 * u < nvec) w[u] = __ldcs(rp + v0 + 32 * u);
+#pragma unroll
+      for (int u = 0; u < kCeGradLoads; ++u) {
+        const int v = v0 + 32 * u;
+        if (v < nvec) __stcs(rp + v, ce_grad_vec(w[u], v * 8, V, L, tl, ignore));
+      }
     }
-    __stcs(ptr, make_uint4(ws[0], ws[1], ws[2], ws[3]));
   }
 }
 
@@ -872,7 +887,9 @@ int layernorm_fwd_launch(const float* x, int64_t ldx, const void* gamma, const v
                          cudaStream_t s, RowPush push) {
   if (C % 4 || C > 4 * 32 * LN_MAXV_CAP) return -1;
   return ln_dispatch(C, [&](auto nv) {
-    ln_fwd_kernel<decltype(nv)::value><<<(M + 7) / 8, 256, 0, s>>>(
+    auto kern = push.n ? ln_fwd_kernel<decltype(nv)::value, true>
+                       : ln_fwd_kernel<decltype(nv)::value, false>;
+    kern<<<(M + 7) / 8, 256, 0, s>>>(
         x, ldx, (const __nv_bfloat16*)gamma, (const __nv_bfloat16*)beta, (__nv_bfloat16*)y, ldy,
         mean, rstd, M, C, eps, push);
         count_launches(1);
@@ -910,7 +927,8 @@ int layernorm_bwd_launch(const void* dy, const float* x, const float* mean, cons
   const int nblk = layernorm_bwd_ctas(M);
   const int smem = LNB_WARPS * LNB_NSUM * C * (int)sizeof(float);
   const int rc = ln_dispatch(C, [&](auto nv) {
-    auto kern = ln_bwd_kernel<decltype(nv)::value>;
+    auto kern = push.n ? ln_bwd_kernel<decltype(nv)::value, true>
+                       : ln_bwd_kernel<decltype(nv)::value, false>;
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     kern<<<nblk, 256, smem, s>>>((const __nv_bfloat16*)dy, x, mean, rstd,
@@ -989,6 +1007,18 @@ int cross_entropy_fwd_bwd_launch(void* logits, int64_t ld, const int64_t* target
   return ok();
 }
 
+__global__ void exp2_fma_test_kernel(const float* __restrict__ x, float* __restrict__ y, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = exp2_fma(x[i]);
+}
+
+// exp2_fma (common.cuh) elementwise, for the numerics test only.
+int exp2_fma_test_launch(const float* x, float* y, int n, cudaStream_t s) {
+  exp2_fma_test_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, y, n);
+  count_launches(1);
+  return launch_succeeded() ? 0 : -11;
+}
+
 int ce_combine_launch(const void* stats, int nparts, int M, const int64_t* targets,
                       const float* tgt_logit, float* lse, float* loss_rows, cudaStream_t s) {
   if (M <= 0 || nparts <= 0) return -1;
@@ -1005,8 +1035,7 @@ int ce_grad_launch(void* logits, int64_t ld, int M, int V, const float* lse,
   int sms = 0, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t total = (int64_t)M * (ld / 8);
-  const int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)sms * 8);
+  const int blocks = std::min((M + 7) / 8, sms * 8);  // 8 rows (warps) per block
   ce_grad_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld, M, V, lse,
                                         targets, vocab_offset);
   count_launches(1);

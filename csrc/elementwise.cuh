@@ -78,6 +78,9 @@ int ce_combine_launch(const void* stats, int nparts, int M, const int64_t* targe
 int ce_grad_launch(void* logits, int64_t ld, int M, int V, const float* lse,
                    const int64_t* targets, int vocab_offset, cudaStream_t s);
 
+// exp2_fma (the FMA-pipe 2^x of the softmax kernels) over n floats; tests only.
+int exp2_fma_test_launch(const float* x, float* y, int n, cudaStream_t s);
+
 int loss_reduce_launch(const float* loss_rows, const int64_t* targets, int M, float* loss_out,
                        cudaStream_t s);
 

@@ -86,7 +86,23 @@ struct GemmDev {
   int ce_vocab_offset;
   void* const* owner_out;
   int owner_rows;
+  int owner_self;
+  int m_fast;  // tile order: 1 = consecutive tiles walk M (wide-N GEMMs), 0 = walk N
 };
+
+// Row and column tile of linear tile `rem` (within one split). With more N
+// tiles than M tiles (the lm_head: 197 x 64), walking M first keeps the few
+// B tiles in flight and all of A in L2, so each operand streams from HBM once;
+// otherwise walking N first does the same for A.
+__device__ __forceinline__ void tile_mn(const GemmDev& p, int rem, int m_tiles, int& mi, int& ni) {
+  if (p.m_fast) {
+    mi = rem % m_tiles;
+    ni = rem / m_tiles;
+  } else {
+    mi = rem / p.n_tiles;
+    ni = rem % p.n_tiles;
+  }
+}
 
 // Online (max, sum exp) of one epilogue thread's row over its chunks of one
 // tile (EPI_CE_STATS): the logits are rounded to bf16 first, as stored.
@@ -408,8 +424,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tile = p.sched ? (int)gridDim.x + atomicAdd(p.sched, 1) : tile + (int)gridDim.x;
         const int split = cur / tiles_per_split;
         const int rem = cur % tiles_per_split;
-        const int m0 = (rem / p.n_tiles) * BM;
-        const int n0 = (rem % p.n_tiles) * BN;
+        int mi, ni;
+        tile_mn(p, rem, p.m_tiles, mi, ni);
+        const int m0 = mi * BM;
+        const int n0 = ni * BN;
         const int kb0 = split * p.kb_per_split;
         const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -522,13 +540,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (tile < 0) break;
       const int split = tile / tiles_per_split;
       const int rem = tile % tiles_per_split;
-      const int m0 = (rem / p.n_tiles) * BM;
-      const int n0 = (rem % p.n_tiles) * BN;
+      int mi, ni;
+      tile_mn(p, rem, p.m_tiles, mi, ni);
+      const int m0 = mi * BM;
+      const int n0 = ni * BN;
       const int row = m0 + r_local;
       const int c0 = n0 + col_half * (BN / 2);
       load_epi_in<EPI>(p, row, c0, in_next);
       CeRow ce;
       if (EPI == EPI_CE_STATS) ce_begin(p, row, ce);
+      // row-owner output: a tile owned by another GPU goes out by direct stores
+      const bool peer_tile = p.owner_out && (m0 / p.owner_rows) != p.owner_self;
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, p.err, ERR_TIMEOUT_EPILOGUE, abort_flag))
         break;
       tc_fence_after();
@@ -549,7 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 32; ++i) v[i] *= alpha;
         epi_math<EPI>(p, c0 + c * 32, v, in, z);
         if (EPI == EPI_CE_STATS) ce_chunk(p, row, c0 + c * 32, v, ce);
-        if (TMA_ST) {
+        if (TMA_ST && !peer_tile) {
           // the previous chunk's bulk store must have finished reading the box
           if (lane == 0) bulk_wait_read0();
           __syncwarp();
@@ -736,8 +758,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         const int split = cur / tiles_per_split;
         const int rem = cur % tiles_per_split;
-        const int m0 = (rem / p.n_tiles) * 2 * BM + (int)rank * BM;
-        const int nb = (rem % p.n_tiles) * BN + (int)rank * (BN / 2);
+        int mi, ni;
+        tile_mn(p, rem, m_tiles, mi, ni);
+        const int m0 = mi * 2 * BM + (int)rank * BM;
+        const int nb = ni * BN + (int)rank * (BN / 2);
         const int kb0 = split * p.kb_per_split;
         const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -855,13 +879,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (tile < 0) break;
       const int split = tile / tiles_per_split;
       const int rem = tile % tiles_per_split;
-      const int m0 = (rem / p.n_tiles) * 2 * BM + (int)rank * BM;
-      const int n0 = (rem % p.n_tiles) * BN;
+      int mi, ni;
+      tile_mn(p, rem, m_tiles, mi, ni);
+      const int m0 = mi * 2 * BM + (int)rank * BM;
+      const int n0 = ni * BN;
       const int row = m0 + r_local;
       const int c0 = n0 + col_half * (BN / 2);
       load_epi_in<EPI>(p, row, c0, in_next);
       CeRow ce;
       if (EPI == EPI_CE_STATS) ce_begin(p, row, ce);
+      // row-owner output: a tile owned by another GPU goes out by direct stores
+      const bool peer_tile = p.owner_out && (m0 / p.owner_rows) != p.owner_self;
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, p.err, ERR_TIMEOUT_EPILOGUE, abort_flag))
         break;
       tc_fence_after();
@@ -883,7 +911,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 32; ++i) v[i] *= alpha;
         epi_math<EPI>(p, c0 + c * 32, v, in, z);
         if (EPI == EPI_CE_STATS) ce_chunk(p, row, c0 + c * 32, v, ce);
-        if (TMA_ST) {
+        if (TMA_ST && !peer_tile) {
           if (lane == 0) bulk_wait_read0();
           __syncwarp();
           if (F32_OUT) {
@@ -1227,6 +1255,8 @@ int gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   d.ce_vocab_offset = a.ce_vocab_offset;
   d.owner_out = a.owner_out;
   d.owner_rows = a.owner_rows;
+  d.owner_self = a.owner_self;
+  d.m_fast = d.n_tiles > (pairs ? (a.M + 2 * BM - 1) / (2 * BM) : d.m_tiles) ? 1 : 0;
   if (a.owner_out && (a.owner_rows <= 0 || (a.epilogue != EPI_BF16) || split_mode)) return -13;
   if (a.epilogue == EPI_CE_STATS &&
       (!a.ce_stats || !a.ce_targets || !a.ce_tgt_logit || split_mode || a.bias))
@@ -1239,9 +1269,10 @@ int gemm_bf16_launch(const GemmArgs& a, cudaStream_t stream) {
   if (a.bias) vec = vec && aligned16(a.bias);
   d.vec_ok = vec ? 1 : 0;
 
-  // TMA stores need the same alignment as the vector path; row-owner output
-  // uses the direct (per-thread vector) stores.
-  int tma_st = (vec && !a.owner_out) ? 1 : 0;
+  // TMA stores need the same alignment as the vector path. Row-owner output:
+  // tiles of this GPU's rows (owner_self) are TMA-stored into `out`, which is
+  // this GPU's inbox, other tiles use direct stores into the owners' memory.
+  int tma_st = (vec && (!a.owner_out || a.owner_self >= 0)) ? 1 : 0;
   if (tma_st) {
     ok = make_tmap_out(&maps.o, d.out, a.N, a.M, d.splits, d.ldo, esz);
     if (ok && a.epilogue == EPI_BIAS_GELU) ok = make_tmap_out(&maps.x, a.aux, a.N, a.M, 1, a.ldaux, 2);

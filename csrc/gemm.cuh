@@ -58,6 +58,7 @@ struct GemmArgs {
   // (plain peer stores, one 16-byte vector at a time). bf16 epilogues only.
   void* const* owner_out = nullptr;
   int owner_rows = 0;
+  int owner_self = -1;  // this GPU's index in owner_out: its rows keep the TMA-store path
 };
 
 // Returns 0 on success, a negative code for unsupported arguments.

@@ -163,10 +163,11 @@ def gemm(
     pair), 0 one CTA per 128 x ``bn`` tile, -1 the library's default.
     ``EPI_CE_STATS`` (the lm_head forward) also needs ``ce`` (a
     :class:`CEWorkspace`) and the int64 ``ce_targets``.
-    ``owner_out = (bases, rows)`` stores row m of the (bf16) result at
-    bases[m // rows] + (m % rows) * ldo instead of into ``out`` (which then only
-    gives the shape and row stride): tensor parallelism's GEMM -> reduce-
-    scatter, each partial row written straight into its owner's inbox.
+    ``owner_out = (bases, rows[, self])`` stores row m of the (bf16) result at
+    bases[m // rows] + (m % rows) * ldo instead of into ``out``: tensor
+    parallelism's GEMM -> reduce-scatter, each partial row written straight
+    into its owner's inbox. With ``self``, ``out`` is this GPU's inbox and the
+    tiles of its own rows keep the TMA-store path.
     """
     _check_cuda(a, b, out, bias, aux, alpha_ptr, workspace)
     if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
@@ -211,7 +212,8 @@ def gemm(
         int(accumulate), int(splits), _ptr(workspace), int(bn), int(max_ctas), int(pair),
         ce_ptrs[0], ce_ptrs[1], ce_ptrs[2], int(ce_vocab_offset),
         0 if owner_out is None else owner_out[0].data_ptr(),
-        0 if owner_out is None else int(owner_out[1]), _err_ptr(), _stream(),
+        0 if owner_out is None else int(owner_out[1]),
+        -1 if owner_out is None or len(owner_out) < 3 else int(owner_out[2]), _err_ptr(), _stream(),
     )
     return out
 

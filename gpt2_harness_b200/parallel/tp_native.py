@@ -376,7 +376,7 @@ class TPEngine:
         row goes straight into its owner's inbox over NVLink."""
         out = self.Pbuf[self._pb]
         if self.fused:
-            N.gemm(a, w, out, owner_out=(self._owner[self._pb], self.Ms), **kw)
+            N.gemm(a, w, out, owner_out=(self._owner[self._pb], self.Ms, self.rank), **kw)
         else:
             N.gemm(a, w, out, **kw)
 

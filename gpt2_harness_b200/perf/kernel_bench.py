@@ -109,6 +109,17 @@ def run_suite(batch: int = 16, seq: int = 1024, C: int = 768, H: int = 12, V: in
     # epilogue, row fold, gradient pass); against gemm_lm_head_fwd + cross_entropy
     add("lm_head_ce_fused", lambda: N.lm_head_cross_entropy(x, wte, logits, tgt, cews, lo, V),
         2.0 * M * V * C)
+    # its three steps on their own
+    add("gemm_lm_head_ce_stats", lambda: N.gemm(x, wte, logits[:, :V], epilogue=N.EPI_CE_STATS,
+                                                ce=cews, ce_targets=tgt), 2.0 * M * V * C)
+    Lb = N.lib()
+    _st = lambda: torch.cuda.current_stream().cuda_stream  # noqa: E731
+    add("ce_combine", lambda: Lb.ce_combine(cews.stats.data_ptr(), cews.nparts, M, tgt.data_ptr(),
+                                            cews.tgt_logit.data_ptr(), cews.lse.data_ptr(),
+                                            cews.loss_rows.data_ptr(), _st()),
+        bytes_=cews.nparts * M * 8)
+    add("ce_grad", lambda: Lb.ce_grad(logits.data_ptr(), vp, M, V, cews.lse.data_ptr(), tgt.data_ptr(),
+                                      0, _st()), bytes_=2 * M * vp * 2)
 
     # attention (causal: half the dense FLOPs)
     lse = torch.empty(batch, H, seq, device=dev)

@@ -70,7 +70,7 @@ def gemm(a, b, out, *, a_t=False, b_t=False, epilogue=N.EPI_BF16, bias=None, aux
         r = r + bias[:n].float()
     if epilogue == N.EPI_BF16 and owner_out is not None:
         # row m goes to its owner's inbox: bases[m // rows] + (m % rows) * ldo
-        bases, rows = owner_out
+        bases, rows = owner_out[0], owner_out[1]
         ld = out.stride(0)
         for q, base in enumerate(int(b) for b in bases.reshape(-1)):
             blk = r[q * rows:(q + 1) * rows]

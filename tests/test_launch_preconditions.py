@@ -29,8 +29,8 @@ def _rejected(fn, *args, name):
 def test_gemm_rejects_empty_and_bad_tile():
     # M = 0
     # trailing: pair, ce_stats, ce_targets, ce_tgt_logit, ce_vocab_offset, owner_out,
-    # owner_rows, err, stream
-    tail = (-1, 0, 0, 0, 0, 0, 0, 0, 0)
+    # owner_rows, owner_self, err, stream
+    tail = (-1, 0, 0, 0, 0, 0, 0, -1, 0, 0)
     _rejected(L.gemm, A16, 64, 0, A16, 64, 0, 0, 64, 64, 0, A16, 64, 0, 0, 0, 1.0, 0, 0, 1, 0, 256, 0,
               *tail, name="gemm_bf16")
     # unsupported N tile
