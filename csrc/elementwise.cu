@@ -646,27 +646,39 @@ __global__ void __launch_bounds__(CE_THREADS) ce_kernel(__nv_bfloat16* __restric
 }
 
 // Fused lm_head + cross-entropy, step 2 (step 1 is the lm_head GEMM with the
-// EPI_CE_STATS epilogue): one thread per row folds the row's (max, sum exp)
-// partials, in tile order, into its log-sum-exp and loss.
+// EPI_CE_STATS epilogue): one warp per row folds the row's (max, sum exp)
+// partials into its log-sum-exp and loss. Lane j folds partials j, j+32, ...
+// in order, then the 32 lane results are combined in a fixed butterfly order.
 __global__ void __launch_bounds__(256) ce_combine_kernel(const float2* __restrict__ stats,
                                                          int nparts, int M,
                                                          const int64_t* __restrict__ targets,
                                                          const float* __restrict__ tgt_logit,
                                                          float* __restrict__ lse_out,
                                                          float* __restrict__ loss_rows) {
-  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
   if (row >= M) return;
   float m = -INFINITY, s = 0.f;
-  for (int j = 0; j < nparts; ++j) {
+  for (int j = lane; j < nparts; j += 32) {
     const float2 p = __ldcs(stats + (int64_t)j * M + row);
     if (p.x == -INFINITY) continue;
     const float nm = fmaxf(m, p.x);
     s = s * __expf(m - nm) + p.y * __expf(p.x - nm);
     m = nm;
   }
-  const float lse = m + __logf(s);
-  lse_out[row] = lse;
-  loss_rows[row] = targets[row] == -100 ? 0.f : lse - tgt_logit[row];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, o);
+    const float os = __shfl_xor_sync(0xffffffffu, s, o);
+    const float nm = fmaxf(m, om);
+    s = (m == -INFINITY ? 0.f : s * __expf(m - nm)) + (om == -INFINITY ? 0.f : os * __expf(om - nm));
+    m = nm;
+  }
+  if (lane == 0) {
+    const float lse = m + __logf(s);
+    lse_out[row] = lse;
+    loss_rows[row] = targets[row] == -100 ? 0.f : lse - tgt_logit[row];
+  }
 }
 
 // Step 3: logits -> (softmax - onehot) in place: one read and one write of
@@ -1022,7 +1034,7 @@ int exp2_fma_test_launch(const float* x, float* y, int n, cudaStream_t s) {
 int ce_combine_launch(const void* stats, int nparts, int M, const int64_t* targets,
                       const float* tgt_logit, float* lse, float* loss_rows, cudaStream_t s) {
   if (M <= 0 || nparts <= 0) return -1;
-  ce_combine_kernel<<<(M + 255) / 256, 256, 0, s>>>(reinterpret_cast<const float2*>(stats),
+  ce_combine_kernel<<<(M + 7) / 8, 256, 0, s>>>(reinterpret_cast<const float2*>(stats),
                                                      nparts, M, targets, tgt_logit, lse,
                                                      loss_rows);
   count_launches(1);

@@ -31,8 +31,8 @@ def make_batch(cfg, B, T, seed=0):
     return idx, tgt
 
 
-@pytest.mark.parametrize("B,T", [(2, 128), (3, 200)])
-def test_engine_loss_and_grads_match_oracle(B, T):
+@pytest.mark.parametrize("B,T,fused_ce", [(2, 128, False), (3, 200, False), (3, 200, True)])
+def test_engine_loss_and_grads_match_oracle(B, T, fused_ce):
     torch.manual_seed(0)
     cfg = small_config()
     model = GPT(cfg)
@@ -44,6 +44,7 @@ def test_engine_loss_and_grads_match_oracle(B, T):
 
     dev = torch.device("cuda", 0)
     eng = Engine.from_module(model, dev)
+    eng.fused_ce = fused_ce
     loss = eng.forward(idx.to(dev), tgt.to(dev))
     eng.backward(idx.to(dev))
     torch.cuda.synchronize()
