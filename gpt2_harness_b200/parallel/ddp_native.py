@@ -120,6 +120,9 @@ class NativeDDP:
         # than the SMs the wide CTAs hold for the short bucket reductions.
         # G2B_COMM_SLIM=1 selects the slim kernel for the overlapped buckets.
         self.slim = os.environ.get("G2B_COMM_SLIM", "0") == "1"
+        # G2B_TAIL_NCCL=1: the buckets of the last gradient group (reduced
+        # while nothing else runs) through NCCL instead of the P2P kernel
+        self.tail_nccl = os.environ.get("G2B_TAIL_NCCL", "0") == "1"
         self.last_group = len(self.order) - 1
         self.symm: Optional[SymmetricBuffer] = None
         self.flags: Optional[SymmetricBuffer] = None
@@ -156,18 +159,22 @@ class NativeDDP:
         if self.comm == "none":
             return
         idx = self.order[group]
-        tail = idx == self.last_group or not self.slim
+        last = idx == self.last_group
         while self._next < len(self.buckets) and self.buckets[self._next].ready <= idx:
-            self._launch(self.buckets[self._next], slim=not tail)
+            self._launch(self.buckets[self._next], slim=self.slim and not last, last=last)
             self._next += 1
 
-    def _launch(self, b: Bucket, slim: bool = False) -> None:
+    def _launch(self, b: Bucket, slim: bool = False, last: bool = False) -> None:
         ev = torch.cuda.Event()
         ev.record()
         self.stream.wait_event(ev)
         comms.record_external("all_reduce", b.numel, b.numel * 4)
         with torch.cuda.stream(self.stream), nvtx_range(f"allreduce/bucket{self.buckets.index(b)}"):
-            if self.comm == "p2p":
+            if self.comm == "p2p" and last and self.tail_nccl:
+                # the exposed last buckets through NCCL's all-reduce (NVLS in-switch
+                # reduction where the fabric offers it), averaged
+                dist.all_reduce(self.grad_buffer[b.lo:b.hi], op=dist.ReduceOp.AVG, group=self.group)
+            elif self.comm == "p2p":
                 self.epoch += 1
                 fn = N.lib().allreduce_p2p_slim if slim else N.lib().allreduce_p2p
                 fn(self.symm.peer_ptrs_dev.data_ptr(), self.flags.peer_ptrs_dev.data_ptr(),
@@ -185,7 +192,7 @@ class NativeDDP:
             # backward did not announce every group (e.g. a frozen tail):
             # launch the rest now so every rank issues the same sequence.
             while self._next < len(self.buckets):
-                self._launch(self.buckets[self._next])
+                self._launch(self.buckets[self._next], last=True)
                 self._next += 1
         torch.cuda.current_stream().wait_stream(self.stream)
         self._next = 0
