@@ -496,7 +496,7 @@ def main():
     ap.add_argument("--model", default="gpt2")
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--seq", type=int, default=1024)
-    ap.add_argument("--comm", choices=["p2p", "nccl"], default="p2p")
+    ap.add_argument("--comm", choices=["p2p", "mc", "nccl"], default="p2p")
     ap.add_argument("--strategy", choices=["ddp", "zero2", "zero3", "tp", "cp", "pp"], default="ddp")
     ap.add_argument("--pp", type=int, default=0, help="pipeline stages (pp strategy; default N / cp)")
     ap.add_argument("--cp", type=int, default=1, help="context-parallel ranks per stage (pp strategy)")

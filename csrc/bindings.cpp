@@ -280,46 +280,54 @@ PYBIND11_MODULE(_C, m) {
     return (int64_t)(uintptr_t)p;
   });
   m.def("symm_free", [](int64_t p) { comm_symm_free(P<void>(p)); });
+  // The three all-reduce forms share one argument list; `count` is the
+  // payload (elements) charged to the byte counter, < 0 = n.
+  auto comm_args = [](int64_t peer_bufs, int64_t peer_flags, int rank, int world, int64_t offset,
+                      int64_t n, int dtype, float scale, uint32_t epoch, int64_t counter,
+                      int64_t err, int nblocks, int64_t wait_budget_ns, int64_t count) {
+    CommArgs c;
+    c.peer_bufs = P<void*>(peer_bufs);
+    c.peer_flags = P<uint32_t*>(peer_flags);
+    c.rank = rank;
+    c.world = world;
+    c.offset = offset;
+    c.n = n;
+    c.dtype = dtype;
+    c.scale = scale;
+    c.epoch = epoch;
+    c.byte_counter = P<unsigned long long>(counter);
+    c.err = P<uint32_t>(err);
+    c.nblocks = nblocks;
+    c.wait_budget_ns = wait_budget_ns;
+    c.count = count;
+    return c;
+  };
   m.def("allreduce_p2p",
-        [](int64_t peer_bufs, int64_t peer_flags, int rank, int world, int64_t offset, int64_t n,
-           int dtype, float scale, uint32_t epoch, int64_t counter, int64_t err, int nblocks,
-           int64_t wait_budget_ns, int64_t stream) {
-          CommArgs c;
-          c.peer_bufs = P<void*>(peer_bufs);
-          c.peer_flags = P<uint32_t*>(peer_flags);
-          c.rank = rank;
-          c.world = world;
-          c.offset = offset;
-          c.n = n;
-          c.dtype = dtype;
-          c.scale = scale;
-          c.epoch = epoch;
-          c.byte_counter = P<unsigned long long>(counter);
-          c.err = P<uint32_t>(err);
-          c.nblocks = nblocks;
-          c.wait_budget_ns = wait_budget_ns;
+        [comm_args](int64_t peer_bufs, int64_t peer_flags, int rank, int world, int64_t offset,
+                    int64_t n, int dtype, float scale, uint32_t epoch, int64_t counter, int64_t err,
+                    int nblocks, int64_t wait_budget_ns, int64_t count, int64_t stream) {
+          CommArgs c = comm_args(peer_bufs, peer_flags, rank, world, offset, n, dtype, scale, epoch,
+                                 counter, err, nblocks, wait_budget_ns, count);
           check(comm_allreduce_launch(c, S(stream)), "allreduce_p2p");
         });
   m.def("allreduce_p2p_slim",
-        [](int64_t peer_bufs, int64_t peer_flags, int rank, int world, int64_t offset, int64_t n,
-           int dtype, float scale, uint32_t epoch, int64_t counter, int64_t err, int nblocks,
-           int64_t wait_budget_ns, int64_t stream) {
-          CommArgs c;
-          c.peer_bufs = P<void*>(peer_bufs);
-          c.peer_flags = P<uint32_t*>(peer_flags);
-          c.rank = rank;
-          c.world = world;
-          c.offset = offset;
-          c.n = n;
-          c.dtype = dtype;
-          c.scale = scale;
-          c.epoch = epoch;
-          c.byte_counter = P<unsigned long long>(counter);
-          c.err = P<uint32_t>(err);
-          c.nblocks = nblocks;
-          c.wait_budget_ns = wait_budget_ns;
+        [comm_args](int64_t peer_bufs, int64_t peer_flags, int rank, int world, int64_t offset,
+                    int64_t n, int dtype, float scale, uint32_t epoch, int64_t counter, int64_t err,
+                    int nblocks, int64_t wait_budget_ns, int64_t count, int64_t stream) {
+          CommArgs c = comm_args(peer_bufs, peer_flags, rank, world, offset, n, dtype, scale, epoch,
+                                 counter, err, nblocks, wait_budget_ns, count);
           c.threads = 128;
           check(comm_allreduce_launch(c, S(stream)), "allreduce_p2p_slim");
+        });
+  m.def("allreduce_mc",
+        [comm_args](int64_t peer_bufs, int64_t peer_flags, int64_t mc_base, int rank, int world,
+                    int64_t offset, int64_t n, int dtype, float scale, uint32_t epoch,
+                    int64_t counter, int64_t err, int nblocks, int64_t wait_budget_ns,
+                    int64_t count, int64_t stream) {
+          CommArgs c = comm_args(peer_bufs, peer_flags, rank, world, offset, n, dtype, scale, epoch,
+                                 counter, err, nblocks, wait_budget_ns, count);
+          c.mc_base = P<void>(mc_base);
+          check(comm_allreduce_mc_launch(c, S(stream)), "allreduce_mc");
         });
   // ZeRO-2 kernels: every argument is passed by name in a dict (int pointers,
   // ints, floats); see csrc/zero.cuh for their meaning.

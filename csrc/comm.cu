@@ -185,7 +185,83 @@ __global__ void __launch_bounds__(NT, NT == 128 ? 6 : 1) allreduce_p2p_kernel(co
   __threadfence_system();
   __syncthreads();
   if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
-    atomicAdd(a.byte_counter, (unsigned long long)a.n * sizeof(T));
+    atomicAdd(a.byte_counter, (unsigned long long)(a.count >= 0 ? a.count : a.n) * sizeof(T));
+  handshake(a, 1, &fail);
+}
+
+// ------------------------------------------------------ multimem (NVLS) --
+__device__ __forceinline__ uint4 mc_ld_reduce(const uint4* p, float) {
+  uint4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p)
+               : "memory");
+  return r;
+}
+__device__ __forceinline__ uint4 mc_ld_reduce(const uint4* p, __nv_bfloat16) {
+  uint4 r;
+  asm volatile(
+      "multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+      : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+      : "l"(p)
+      : "memory");
+  return r;
+}
+__device__ __forceinline__ void mc_st(uint4* p, const uint4& v, float) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void mc_st(uint4* p, const uint4& v, __nv_bfloat16) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(p),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+template <typename T, int NT>
+__global__ void __launch_bounds__(NT, 1) allreduce_mc_kernel(const CommArgs a) {
+  __shared__ int fail;
+  if (threadIdx.x == 0) fail = 0;
+  __syncthreads();
+  if (!handshake(a, 0, &fail)) return;
+
+  constexpr int VN = Vec<T>::N;
+  const T tag{};
+  const int64_t nvec = a.n / VN;  // the launch requires n % VN == 0
+  const int64_t s0 = nvec * a.rank / a.world, s1 = nvec * (a.rank + 1) / a.world;
+  const int64_t per_blk = (s1 - s0 + gridDim.x - 1) / gridDim.x;
+  const int64_t b0 = min(s1, s0 + per_blk * blockIdx.x), b1 = min(s1, b0 + per_blk);
+  uint4* mc = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.mc_base) + a.offset);
+  // U switch reductions in flight per thread before the first store
+  constexpr int U = 8;
+  for (int64_t v0 = b0 + threadIdx.x; v0 < b1; v0 += (int64_t)NT * U) {
+    uint4 w[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = v0 + (int64_t)u * NT;
+      if (v < b1) w[u] = mc_ld_reduce(mc + v, tag);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = v0 + (int64_t)u * NT;
+      if (v < b1) {
+        float acc[VN];
+#pragma unroll
+        for (int i = 0; i < VN; ++i) acc[i] = 0.f;
+        acc_vec(acc, w[u], tag);
+#pragma unroll
+        for (int i = 0; i < VN; ++i) acc[i] *= a.scale;
+        mc_st(mc + v, pack_vec(acc, tag), tag);
+      }
+    }
+  }
+  // the stores went out through the multicast alias; peers read the result
+  // through their own addresses after the handshake
+  asm volatile("fence.proxy.alias;" ::: "memory");
+  __threadfence_system();
+  __syncthreads();
+  if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
+    atomicAdd(a.byte_counter, (unsigned long long)(a.count >= 0 ? a.count : a.n) * sizeof(T));
   handshake(a, 1, &fail);
 }
 
@@ -229,6 +305,23 @@ int comm_allreduce_launch(const CommArgs& a, cudaStream_t s) {
     launch_allreduce<float>(a, s);
   else
     launch_allreduce<__nv_bfloat16>(a, s);
+  count_launches(1);
+  return launch_succeeded() ? 0 : -11;
+}
+
+int comm_allreduce_mc_launch(const CommArgs& a, cudaStream_t s) {
+  if (a.world < 1 || a.world > kCommMaxRanks || a.nblocks < 1 || a.nblocks > kCommMaxBlocks)
+    return -1;
+  if (!a.mc_base) return -4;
+  if (a.n <= 0) return 0;
+  const int esz = a.dtype == 0 ? 4 : 2;
+  // whole 16-byte vectors, 16-byte aligned: multimem.v4 moves exactly one
+  if ((a.offset * esz) % 16 || (a.n * esz) % 16 || (reinterpret_cast<uintptr_t>(a.mc_base) % 16))
+    return -2;
+  if (a.dtype == 0)
+    allreduce_mc_kernel<float, 512><<<a.nblocks, 512, 0, s>>>(a);
+  else
+    allreduce_mc_kernel<__nv_bfloat16, 512><<<a.nblocks, 512, 0, s>>>(a);
   count_launches(1);
   return launch_succeeded() ? 0 : -11;
 }

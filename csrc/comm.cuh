@@ -33,9 +33,24 @@ struct CommArgs {
   // or attention CTA and the reduction overlaps backward without taking SMs
   // away from it).
   int threads = 512;
+  // Payload elements charged to byte_counter (the reference convention: the
+  // parameters of the bucket, alignment padding excluded); < 0 = n.
+  int64_t count = -1;
+  // NVLink SHARP form (comm_allreduce_mc_launch): the multicast address of
+  // the same symmetric buffer, bound to every rank's copy.
+  void* mc_base = nullptr;
 };
 
 int comm_allreduce_launch(const CommArgs& a, cudaStream_t s);
+
+// The same all-reduce through the NVSwitch (multimem): CTA j of rank r reads
+// part j of slice r already summed over all ranks by the switch
+// (multimem.ld_reduce on the multicast address), scales it and writes it to
+// every rank's copy with one multimem.st. Each rank moves S/p in and S/p out
+// of its own slice plus (p-1)/p * S of the others' results arriving: about
+// half the NVLink bytes of the P2P form, with no reduction arithmetic on the
+// SMs. Same flags, epochs and bounded handshakes as the P2P form.
+int comm_allreduce_mc_launch(const CommArgs& a, cudaStream_t s);
 
 // Launch a single-thread kernel that waits (bounded) for *flag == value and
 // records ERR_TIMEOUT_PEER in *err when the budget expires. Used to test the

@@ -280,6 +280,9 @@ __global__ void __launch_bounds__(256) tp_embed_fwd_kernel(const TpArgs a) {
       reinterpret_cast<float4*>(out + c)[1] = make_float4(o[4], o[5], o[6], o[7]);
     }
   }
+  // an all-to-all of this rank's bf16 rows in the reference convention
+  if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
+    atomicAdd(a.byte_counter, (unsigned long long)(a.rows * a.cols * 2));
   finish(a, &fail);
 }
 
@@ -305,6 +308,9 @@ __global__ void __launch_bounds__(256) tp_embed_bwd_kernel(const TpArgs a) {
       atomicAdd(prow + c, g);
     }
   }
+  // an all-to-all of this rank's fp32 gradient rows
+  if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
+    atomicAdd(a.byte_counter, (unsigned long long)(a.rows * a.cols * 4));
   finish(a, &fail);
 }
 
@@ -394,11 +400,22 @@ __global__ void __launch_bounds__(CE_T) tp_ce_finish_kernel(const TpArgs a) {
     }
     __syncthreads();
   }
+  // an all-gather of every rank's [rows, 4] fp32 statistics (output bytes)
+  if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
+    atomicAdd(a.byte_counter, (unsigned long long)(a.world * a.rows * 16));
   finish(a, &fail);
 }
 
 // ---------------------------------------------------- context parallelism --
 // Row (b, t) of block q in a [B, world*Tl, cols] buffer.
+// Bytes charged per K/V gather or dK/dV reduce-scatter: the reference
+// convention (all-gather = output, reduce-scatter = input), i.e. the whole
+// [B, world * Tl, 2C] bf16 key/value tensor, whatever the causal split lets
+// the kernel skip.
+__device__ __forceinline__ unsigned long long cp_convention_bytes(const TpArgs& a) {
+  return (unsigned long long)a.B * a.world * a.Tl * a.cols * 2;
+}
+
 __device__ __forceinline__ int64_t cp_row(const TpArgs& a, int q, int64_t i) {
   const int64_t b = i / a.Tl, t = i % a.Tl;
   return b * (int64_t)a.world * a.Tl + (int64_t)q * a.Tl + t;
@@ -454,7 +471,7 @@ __global__ void __launch_bounds__(512) cp_kv_gather_zz_kernel(const TpArgs a) {
     off = zz_row(a, k, row / h, row % h) * a.cols + (int)(vv % vpr) * 8;
   });
   if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
-    atomicAdd(a.byte_counter, (unsigned long long)(cvec * 16 * (nk + 2)));
+    atomicAdd(a.byte_counter, cp_convention_bytes(a));
   finish(a, &fail);
 }
 
@@ -499,7 +516,7 @@ __global__ void __launch_bounds__(512) cp_kv_reduce_zz_kernel(const TpArgs a) {
   }
   // chunk r is read from 2w-r partials, chunk 2w-1-r from r+1
   if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
-    atomicAdd(a.byte_counter, (unsigned long long)(nvec / 2 * 16 * (2 * a.world + 1)));
+    atomicAdd(a.byte_counter, cp_convention_bytes(a));
   finish(a, &fail);
 }
 
@@ -529,7 +546,7 @@ __global__ void __launch_bounds__(512) cp_kv_gather_kernel(const TpArgs a) {
     off = cp_row(a, q, vv / vpr) * a.cols + (int)(vv % vpr) * 8;
   });
   if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
-    atomicAdd(a.byte_counter, (unsigned long long)(nvec * 16 * (a.rank + 1)));
+    atomicAdd(a.byte_counter, cp_convention_bytes(a));
   finish(a, &fail);
 }
 
@@ -572,7 +589,7 @@ __global__ void __launch_bounds__(512) cp_kv_reduce_kernel(const TpArgs a) {
                    pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
   }
   if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
-    atomicAdd(a.byte_counter, (unsigned long long)(nvec * 16 * (a.world - a.rank)));
+    atomicAdd(a.byte_counter, cp_convention_bytes(a));
   finish(a, &fail);
 }
 

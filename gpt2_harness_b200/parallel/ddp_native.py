@@ -17,9 +17,15 @@ B200 design:
   stream by an event. Communication overlaps the rest of backward.
 * ``comm="p2p"`` (default): one fused kernel per bucket
   (csrc/comm.cu ``allreduce_p2p``) performs reduce-scatter, the 1/p scale and
-  all-gather over NVLink with in-kernel flags; ``comm="nccl"``: the bucket is
-  a ``dist.all_reduce`` view of the flat buffer and the 1/p is folded into the
-  AdamW kernel. Both charge the same counter entries.
+  all-gather over NVLink with in-kernel flags; ``comm="mc"``: the gradient
+  buffer is also bound to an NVLink multicast object and one kernel per
+  bucket (``allreduce_mc``) reads each element of its slice already summed by
+  the NVSwitch (``multimem.ld_reduce``) and writes the scaled result to every
+  rank with one ``multimem.st`` -- half the NVLink bytes of the P2P form and
+  no reduction arithmetic on the SMs; ``comm="nccl"``: the bucket is a
+  ``dist.all_reduce`` view of the flat buffer and the 1/p is folded into the
+  AdamW kernel. All charge the same counter entries; the in-kernel counters
+  charge each bucket's parameters (padding excluded), the reference's 4N.
 """
 
 from __future__ import annotations
@@ -35,7 +41,7 @@ from gpt2_harness_b200.models.engine import ALIGN, ParamLayout
 from gpt2_harness_b200.ops import native as N
 from gpt2_harness_b200.utils.nvtx import nvtx_range
 from gpt2_harness_b200.parallel import comms
-from gpt2_harness_b200.parallel.symm import SymmetricBuffer
+from gpt2_harness_b200.parallel.symm import MulticastBuffer, SymmetricBuffer
 
 __all__ = ["Bucket", "build_layout_buckets", "NativeDDP", "DEFAULT_BUCKET_BYTES"]
 
@@ -103,7 +109,7 @@ class NativeDDP:
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.comm = comm if self.world > 1 else "none"
-        if self.comm not in ("p2p", "nccl", "none"):
+        if self.comm not in ("p2p", "mc", "nccl", "none"):
             raise ValueError(f"unknown comm {comm!r}")
         self.layout = layout
         self.buckets = build_layout_buckets(layout, bucket_bytes)
@@ -120,14 +126,12 @@ class NativeDDP:
         # than the SMs the wide CTAs hold for the short bucket reductions.
         # G2B_COMM_SLIM=1 selects the slim kernel for the overlapped buckets.
         self.slim = os.environ.get("G2B_COMM_SLIM", "0") == "1"
-        # G2B_TAIL_NCCL=1: the buckets of the last gradient group (reduced
-        # while nothing else runs) through NCCL instead of the P2P kernel
-        self.tail_nccl = os.environ.get("G2B_TAIL_NCCL", "0") == "1"
         self.last_group = len(self.order) - 1
-        self.symm: Optional[SymmetricBuffer] = None
+        self.symm = None
         self.flags: Optional[SymmetricBuffer] = None
-        if self.comm == "p2p":
-            self.symm = SymmetricBuffer(layout.total * 4, group, self.device)
+        if self.comm in ("p2p", "mc"):
+            self.symm = (MulticastBuffer if self.comm == "mc" else SymmetricBuffer)(
+                layout.total * 4, group, self.device)
             self.grad_buffer = self.symm.view(torch.float32, layout.total)
             words = N.lib().comm_flag_words()
             self.flags = SymmetricBuffer(words * 4, group, self.device)
@@ -170,17 +174,21 @@ class NativeDDP:
         self.stream.wait_event(ev)
         comms.record_external("all_reduce", b.numel, b.numel * 4)
         with torch.cuda.stream(self.stream), nvtx_range(f"allreduce/bucket{self.buckets.index(b)}"):
-            if self.comm == "p2p" and last and self.tail_nccl:
-                # the exposed last buckets through NCCL's all-reduce (NVLS in-switch
-                # reduction where the fabric offers it), averaged
-                dist.all_reduce(self.grad_buffer[b.lo:b.hi], op=dist.ReduceOp.AVG, group=self.group)
+            if self.comm == "mc":
+                self.epoch += 1
+                N.lib().allreduce_mc(self.symm.peer_ptrs_dev.data_ptr(), self.flags.peer_ptrs_dev.data_ptr(),
+                                     self.symm.mc_ptr, self.rank, self.world, b.lo, b.hi - b.lo, 0,
+                                     1.0 / self.world, self.epoch & 0xFFFFFFFF, self.byte_counter.data_ptr(),
+                                     N.error_word().data_ptr(), self.tail_blocks if last else self.nblocks,
+                                     2_000_000_000, b.numel, self.stream.cuda_stream)
             elif self.comm == "p2p":
                 self.epoch += 1
                 fn = N.lib().allreduce_p2p_slim if slim else N.lib().allreduce_p2p
                 fn(self.symm.peer_ptrs_dev.data_ptr(), self.flags.peer_ptrs_dev.data_ptr(),
                    self.rank, self.world, b.lo, b.hi - b.lo, 0, 1.0 / self.world,
                    self.epoch & 0xFFFFFFFF, self.byte_counter.data_ptr(), N.error_word().data_ptr(),
-                   self.nblocks if slim else self.tail_blocks, 2_000_000_000, self.stream.cuda_stream)
+                   self.nblocks if slim else self.tail_blocks, 2_000_000_000, b.numel,
+                   self.stream.cuda_stream)
             else:
                 dist.all_reduce(self.grad_buffer[b.lo:b.hi], group=self.group)
 

@@ -18,7 +18,7 @@ import torch.distributed as dist
 
 from gpt2_harness_b200.ops import native as N
 
-__all__ = ["SymmetricBuffer", "wrap_device_pointer"]
+__all__ = ["SymmetricBuffer", "MulticastBuffer", "multicast_supported", "wrap_device_pointer"]
 
 _TYPESTR = {torch.float32: "<f4", torch.bfloat16: "<V2", torch.int32: "<i4", torch.int64: "<i8",
             torch.uint8: "|u1"}
@@ -96,6 +96,69 @@ class SymmetricBuffer:
             self.ptr = 0
 
 
+def multicast_supported(device: Optional[torch.device] = None) -> bool:
+    """Whether this GPU can bind memory to an NVLink multicast object (an
+    NVSwitch system with a driver that exposes multicast)."""
+    if not torch.cuda.is_available():
+        return False
+    try:
+        from torch._C._distributed_c10d import _SymmetricMemory
+        from torch._C._autograd import DeviceType
+    except ImportError:
+        return False
+    idx = (device or torch.device("cuda", torch.cuda.current_device())).index or 0
+    return bool(_SymmetricMemory.has_multicast_support(DeviceType.CUDA, idx))
+
+
+class MulticastBuffer:
+    """A symmetric buffer that is also bound to an NVLink multicast object.
+
+    Same interface as :class:`SymmetricBuffer` (``local``, ``peer_ptrs``,
+    ``peer_ptrs_dev``, ``view``, ``close``) plus ``mc_ptr``: an address whose
+    ``multimem`` loads return the element summed over every rank's copy (the
+    reduction runs in the NVSwitch) and whose ``multimem`` stores land in every
+    rank's copy. Allocation, handle exchange and the multicast binding are
+    torch's symmetric memory (``torch.distributed._symmetric_memory``,
+    cuMem-backed); the kernels that use the addresses are this package's.
+    """
+
+    def __init__(self, nbytes: int, group=None, device: Optional[torch.device] = None) -> None:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.group = group or dist.group.WORLD
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.nbytes = int((nbytes + 255) // 256 * 256)
+        if not multicast_supported(self.device):
+            raise RuntimeError("NVLink multicast is not available on this GPU")
+        try:
+            symm_mem.enable_symm_mem_for_group(self.group.group_name)
+        except Exception:  # pragma: no cover - newer torch enables groups itself
+            pass
+        self._tensor = symm_mem.empty(self.nbytes, dtype=torch.uint8, device=self.device)
+        self._tensor.zero_()
+        self._handle = symm_mem.rendezvous(self._tensor, self.group)
+        self.mc_ptr = int(self._handle.multicast_ptr)
+        if not self.mc_ptr:
+            raise RuntimeError("symmetric memory has no multicast address on this system")
+        self.ptr = self._tensor.data_ptr()
+        self.peer_ptrs = [int(p) for p in self._handle.buffer_ptrs]
+        self.peer_ptrs_dev = torch.tensor(self.peer_ptrs, dtype=torch.int64, device=self.device)
+        self.local = self._tensor
+
+    def view(self, dtype: torch.dtype, numel: Optional[int] = None, offset_bytes: int = 0) -> torch.Tensor:
+        esz = torch.tensor([], dtype=dtype).element_size()
+        n = (self.nbytes - offset_bytes) // esz if numel is None else numel
+        return self._tensor[offset_bytes:offset_bytes + n * esz].view(dtype)
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.device)
+        self._handle = None
+        self._tensor = None
+        self.local = None
+
+
 class P2PAllReducer:
     """Standalone fused peer-memory all-reduce over a symmetric fp32 buffer.
 
@@ -119,7 +182,7 @@ class P2PAllReducer:
         self.epoch += 1
         N.lib().allreduce_p2p(self.data.peer_ptrs_dev.data_ptr(), self.flags.peer_ptrs_dev.data_ptr(), self.rank,
                               self.world, 0, n, 0, float(scale), self.epoch & 0xFFFFFFFF, self.counter.data_ptr(),
-                              N.error_word().data_ptr(), self.nblocks, 2_000_000_000,
+                              N.error_word().data_ptr(), self.nblocks, 2_000_000_000, -1,
                               torch.cuda.current_stream(self.device).cuda_stream)
         return self.tensor[:n]
 

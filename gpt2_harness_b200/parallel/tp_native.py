@@ -542,15 +542,17 @@ class TPEngine:
         N.lib().tp_embed_bwd(d, self._stream())
         # replicated parameters: sum the per-rank partial gradients
         n = lay.repl_hi
+        count = 0
         for name, (off, shape, _) in lay.specs.items():
             if off < n:
                 numel = math.prod(shape)
+                count += numel
                 comms.record_external("all_reduce", numel, numel * 4)
         self.ar_epoch += 1
         N.lib().allreduce_p2p(self._g32.peer_ptrs_dev.data_ptr(), self._ar_flags.peer_ptrs_dev.data_ptr(),
                               self.rank, self.world, 0, n, 0, 1.0, self.ar_epoch & 0xFFFFFFFF,
                               self.byte_counter.data_ptr(), N.error_word(self.device).data_ptr(),
-                              self.nblocks, 2_000_000_000, self._stream())
+                              self.nblocks, 2_000_000_000, count, self._stream())
 
     # --------------------------------------------------------- optimiser --
     def optimizer_step(self) -> None:

@@ -311,11 +311,13 @@ class NativeZeRO3:
         with torch.cuda.stream(self.stream):
             for a, b in self.root_ranges:
                 self.ar_epoch += 1
+                count = sum(s.numel for s in self.layout.specs
+                            if s.group == "root" and a <= s.offset < b)
                 N.lib().allreduce_p2p(
                     self._grad_full.peer_ptrs_dev.data_ptr(), self._ar_flags.peer_ptrs_dev.data_ptr(),
                     self.rank, self.world, a, b - a, 0, 1.0 / self.world, self.ar_epoch & 0xFFFFFFFF,
                     self.byte_counter.data_ptr(), N.error_word(self.device).data_ptr(), self.nblocks,
-                    self._args["wait_budget_ns"], self.stream.cuda_stream)
+                    self._args["wait_budget_ns"], count, self.stream.cuda_stream)
         torch.cuda.current_stream().wait_stream(self.stream)
         self._rs_done.clear()
         self._cur_unit = -1

@@ -187,7 +187,7 @@ def _comm_kernels(add, dev, M: int, C: int) -> None:
     pb, pf = ptrs(bucket), ptrs(cflags)
     add("allreduce_p2p_w1",
         lambda: L.allreduce_p2p(pb.data_ptr(), pf.data_ptr(), 0, 1, 0, nb, 0, 1.0, nxt(),
-                                counter.data_ptr(), err, 128, 2_000_000_000, stream()),
+                                counter.data_ptr(), err, 128, 2_000_000_000, -1, stream()),
         bytes_=nb * 4 * 2)
     # tensor-parallel reduce-scatter from the local inbox (+ bias + fp32 residual)
     inbox = torch.randn(M, C, device=dev).to(torch.bfloat16)

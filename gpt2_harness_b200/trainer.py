@@ -51,8 +51,10 @@ class Trainer:
             preallocated for it).
         train: optimiser settings and LR schedule (``TrainConfig``); ``None``
             uses a constant ``lr`` from its defaults.
-        comm: ``"p2p"`` (fused peer-memory all-reduce) or ``"nccl"`` when the
-            default process group has more than one rank (DDP only).
+        comm: ``"p2p"`` (fused peer-memory all-reduce), ``"mc"`` (the same
+            through NVLink SHARP: multimem loads reduced in the NVSwitch) or
+            ``"nccl"`` when the default process group has more than one rank
+            (DDP only).
         strategy: ``"ddp"``, ``"zero2"`` or ``"zero3"`` (ignored on one rank),
             or ``"tp"``: tensor + sequence parallelism over all ranks, where
             ``batch_size`` is the GLOBAL batch every rank receives, or

@@ -423,7 +423,7 @@ def cp_kv_reduce(d, stream=0):
 
 # ------------------------------------------------------ fused all-reduce --
 def allreduce_p2p(peer_bufs, peer_flags, rank, world, offset, n, dtype, scale, epoch, counter, err,
-                  nblocks, budget_ns, stream):
+                  nblocks, budget_ns, count, stream):
     """Sum of every rank's [offset, offset + n) elements, times `scale`,
     left in every rank's buffer (the fused kernel's contract)."""
     if n <= 0:
@@ -437,11 +437,23 @@ def allreduce_p2p(peer_bufs, peer_flags, rank, world, offset, n, dtype, scale, e
     bufs[rank].copy_(total)
     if counter:
         c = _at(counter, 1, torch.int64)
-        c += n * esz
+        c += (n if count < 0 else count) * esz
     dist.barrier(group=_group(peer_flags))
 
 
 allreduce_p2p_slim = allreduce_p2p  # same contract, fewer threads per CTA on the GPU
+
+
+def allreduce_mc(peer_bufs, peer_flags, mc_base, rank, world, offset, n, dtype, scale, epoch, counter,
+                 err, nblocks, budget_ns, count, stream):
+    """The multimem form: the same result through the switch."""
+    esz = 4 if dtype == 0 else 2
+    if not mc_base:
+        raise RuntimeError("allreduce_mc failed (code -4)")
+    if (n * esz) % 16:
+        raise RuntimeError("allreduce_mc failed (code -2)")
+    allreduce_p2p(peer_bufs, peer_flags, rank, world, offset, n, dtype, scale, epoch, counter, err,
+                  nblocks, budget_ns, count, stream)
 
 
 # ------------------------------------------- tensor-parallel row collectives --
@@ -706,7 +718,7 @@ OPS = {
 LIB = SimpleNamespace(zero_rs=zero_rs, zero_adamw_ag=zero_adamw_ag, zero_ag=zero_ag,
                       zero_flag_words=lambda: 16, zero_norm_words=lambda: 16, zero_max_blocks=lambda: 160,
                       cp_kv_gather=cp_kv_gather, cp_kv_reduce=cp_kv_reduce, tp_flag_words=lambda: 16,
-                      allreduce_p2p=allreduce_p2p, allreduce_p2p_slim=allreduce_p2p_slim, comm_flag_words=lambda: 16, tp_ag_rows=tp_ag_rows,
+                      allreduce_p2p=allreduce_p2p, allreduce_p2p_slim=allreduce_p2p_slim, allreduce_mc=allreduce_mc, comm_flag_words=lambda: 16, tp_ag_rows=tp_ag_rows,
                       tp_rs_rows=tp_rs_rows, tp_embed_fwd=tp_embed_fwd, tp_embed_bwd=tp_embed_bwd,
                       tp_ce_stats=tp_ce_stats, tp_ce_finish=tp_ce_finish, loss_reduce=loss_reduce,
                       embedding_wte_det_chunks=lambda M: -(-M // 128))

@@ -79,8 +79,9 @@ def _run(comm: str, world: int = 2, cfg: dict | None = None):
     procs = []
     for r in range(world):
         env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r),
-                   MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), G2B_ROOT=ROOT, G2B_COMM=comm,
-                   NCCL_NVLS_ENABLE="0")
+                   MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), G2B_ROOT=ROOT, G2B_COMM=comm)
+        if comm != "mc":
+            env["NCCL_NVLS_ENABLE"] = "0"
         if cfg is not None:
             env["G2B_CFG"] = json.dumps(cfg)
         procs.append(subprocess.Popen([sys.executable, "-c", WORKER], env=env, stdout=subprocess.PIPE,
@@ -97,14 +98,21 @@ def _run(comm: str, world: int = 2, cfg: dict | None = None):
 
 # 2 ranks on a 2-layer GPT-2 small; the BASELINE data-parallel mesh (8 ranks)
 # at GPT-2 small widths with 2 of its 12 layers
-@pytest.mark.parametrize("comm,world", [("p2p", 2), ("nccl", 2), ("p2p", 8)])
+@pytest.mark.parametrize("comm,world", [("p2p", 2), ("nccl", 2), ("mc", 2), ("p2p", 8), ("mc", 8)])
 def test_native_ddp_two_gpus(comm, world):
+    if comm == "mc" and not _multicast():
+        pytest.skip("no NVLink multicast on this system")
     res = _run(comm, world)
     for r in res:
         assert r["rel_err"] < 1e-5, r
         assert r["ranks_equal"], r
         # reference convention: one fp32 copy of every gradient per step
         assert r["payload_per_step"] == 4 * r["n_params"], r
-    if comm == "p2p":
-        # the in-kernel counter saw the same payload (padding included): >= 4N per step x 2 steps
-        assert res[0]["device_bytes"] >= 2 * 4 * res[0]["n_params"]
+    if comm in ("p2p", "mc"):
+        # the in-kernel counter charges the same payload: 4N per step x 2 steps
+        assert res[0]["device_bytes"] == 2 * 4 * res[0]["n_params"], res[0]
+
+
+def _multicast() -> bool:
+    from gpt2_harness_b200.parallel.symm import multicast_supported
+    return torch.cuda.device_count() > 1 and multicast_supported(torch.device("cuda", 0))

