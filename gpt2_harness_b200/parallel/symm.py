@@ -139,11 +139,20 @@ class MulticastBuffer:
         self._tensor = symm_mem.empty(self.nbytes, dtype=torch.uint8, device=self.device)
         self._tensor.zero_()
         self._handle = symm_mem.rendezvous(self._tensor, self.group)
-        self.mc_ptr = int(self._handle.multicast_ptr)
-        if not self.mc_ptr:
+        mc = int(self._handle.multicast_ptr)
+        if not mc:
             raise RuntimeError("symmetric memory has no multicast address on this system")
+        # The handle's addresses are those of each rank's whole allocation
+        # block; the tensor may sit at an offset inside it (pooled allocation),
+        # the same offset on every rank.
         self.ptr = self._tensor.data_ptr()
-        self.peer_ptrs = [int(p) for p in self._handle.buffer_ptrs]
+        bases = [int(p) for p in self._handle.buffer_ptrs]
+        off = self.ptr - bases[self.rank]
+        if off < 0 or off + self.nbytes > int(self._handle.buffer_size) or off % 16:
+            raise RuntimeError(f"symmetric tensor outside its block (offset {off}, "
+                               f"block {self._handle.buffer_size} B)")
+        self.mc_ptr = mc + off
+        self.peer_ptrs = [b + off for b in bases]
         self.peer_ptrs_dev = torch.tensor(self.peer_ptrs, dtype=torch.int64, device=self.device)
         self.local = self._tensor
 
