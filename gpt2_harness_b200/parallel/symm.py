@@ -132,10 +132,6 @@ class MulticastBuffer:
         self.nbytes = int((nbytes + 255) // 256 * 256)
         if not multicast_supported(self.device):
             raise RuntimeError("NVLink multicast is not available on this GPU")
-        try:
-            symm_mem.enable_symm_mem_for_group(self.group.group_name)
-        except Exception:  # pragma: no cover - newer torch enables groups itself
-            pass
         self._tensor = symm_mem.empty(self.nbytes, dtype=torch.uint8, device=self.device)
         self._tensor.zero_()
         self._handle = symm_mem.rendezvous(self._tensor, self.group)
