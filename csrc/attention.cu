@@ -548,12 +548,24 @@ static int g_attn_impl = 0;
 void attn_set_impl(int impl) { g_attn_impl = impl; }
 int attn_get_impl() { return g_attn_impl; }
 
+// Grouped key/value heads: 0 = plain multi-head, 1 = grouped (tensor-core
+// kernels only), -1 = invalid grouping.
+static int kv_grouping(const AttnArgs& a) {
+  const int hkv = a.Hkv > 0 ? a.Hkv : a.H;
+  if (hkv > a.H || a.H % hkv) return -1;
+  return hkv != a.H;
+}
+
 int attn_fwd_launch(const AttnArgs& a, cudaStream_t s) {
   if (a.B <= 0 || a.H <= 0 || a.Tq <= 0 || a.Tk <= 0) return -1;
+  const int grouped = kv_grouping(a);
+  if (grouped < 0) return -1;
+  if (grouped && g_attn_impl != 0) return -12;
   if (g_attn_impl == 0) {
     const int rc = attn_fwd_tc_launch(a, s);
     if (rc == 1) return 0;
     if (rc < 0) return rc;
+    if (grouped) return -12;  // grouped heads need TMA-compatible layouts
   }
   const int smem = (FWD_BQ + 4 * FWD_BK) * 128;
   dim3 grid((a.Tq + FWD_BQ - 1) / FWD_BQ, a.B * a.H);
@@ -564,6 +576,9 @@ int attn_fwd_launch(const AttnArgs& a, cudaStream_t s) {
 
 int attn_bwd_launch(const AttnArgs& a, cudaStream_t s) {
   if (a.B <= 0 || a.H <= 0 || a.Tq <= 0 || a.Tk <= 0) return -1;
+  const int grouped = kv_grouping(a);
+  if (grouped < 0) return -1;
+  if (grouped && g_attn_impl != 0) return -12;
   const int64_t rows = (int64_t)a.B * a.H * a.Tq;
   auto rows16 = [](const HeadView& v) {
     return (reinterpret_cast<uintptr_t>(v.base) & 15) == 0 && (v.st * 2) % 16 == 0 &&
@@ -580,6 +595,7 @@ int attn_bwd_launch(const AttnArgs& a, cudaStream_t s) {
       return launch_succeeded() ? 0 : -11;
     }
     if (rc < 0) return rc;
+    if (grouped) return -12;  // grouped heads need TMA-compatible layouts
   }
   const int smem_kv = 6 * BWD_B * 128 + 4 * BWD_B * 4;
   static bool attr = false;

@@ -18,6 +18,10 @@ struct AttnArgs {
   float* lse = nullptr;     // [B, H, Tq] log2-domain row log-sum-exp (fp32)
   float* delta = nullptr;   // [B, H, Tq] rowsum(dO * O) scratch (fp32)
   int B = 0, H = 0, Tq = 0, Tk = 0;
+  // Key/value heads (grouped-query / multi-query attention): query head h
+  // reads key/value head h / (H / Hkv); 0 means Hkv = H. Grouped heads run on
+  // the tensor-core kernels only.
+  int Hkv = 0;
   int q_offset = 0;         // absolute position of query 0 (context parallel)
   int causal = 1;
   float scale = 0.125f;     // softmax scale (1/sqrt(head_dim))

@@ -67,7 +67,10 @@ constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct BwdParams {
-  int H, BH, Tq, Tk, q_offset, causal, n_blk, n_tiles;
+  // H / BH: heads of the stationary operand (key/value heads in MODE_KV,
+  // query heads in MODE_Q); grp: query heads per key/value head; Hq: query
+  // heads (row blocks of lse / delta).
+  int H, BH, Tq, Tk, q_offset, causal, n_blk, n_tiles, grp, Hq;
   float sl2, scale;
   const float* lse;
   const float* delta;
@@ -85,9 +88,12 @@ __device__ __forceinline__ float ex2f(float x) {
 }
 
 // Tile t of the persistent schedule: (batch*head, first stationary row,
-// first streaming row, number of 64-row steps).
+// first streaming row, number of 64-row steps, steps per query head). In
+// MODE_KV with grouped heads the steps walk the visible queries of every
+// query head of the group in turn (step j: head j / nph of the group, rows
+// s0 + (j % nph) * 64), all accumulating into the same dK/dV.
 struct TileInfo {
-  int bh, r0, s0, n;
+  int bh, r0, s0, n, nph;
 };
 
 template <int MODE>
@@ -103,12 +109,14 @@ __device__ __forceinline__ TileInfo tile_info(const BwdParams& p, int t) {
     int q0 = p.causal ? max(0, ti.r0 - p.q_offset) : 0;
     q0 = (q0 / SB) * SB;
     ti.s0 = q0;
-    ti.n = (ti.r0 < p.Tk && q0 < p.Tq) ? (p.Tq - q0 + SB - 1) / SB : 0;
+    ti.nph = (ti.r0 < p.Tk && q0 < p.Tq) ? (p.Tq - q0 + SB - 1) / SB : 0;
+    ti.n = ti.nph * p.grp;
   } else {
     int kv_end = p.Tk;
     if (p.causal) kv_end = min(p.Tk, p.q_offset + ti.r0 + TB);
     ti.s0 = 0;
     ti.n = (ti.r0 < p.Tq && kv_end > 0) ? (kv_end + SB - 1) / SB : 0;
+    ti.nph = ti.n;
   }
   return ti;
 }
@@ -282,11 +290,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        const int row = ti.s0 + j * SB;
+        const int row = ti.s0 + (j % ti.nph) * SB;
+        // streaming operand's head: the step's query head (MODE_KV) or the
+        // tile's key/value head (MODE_Q)
+        const int hx = (MODE == MODE_KV) ? h * p.grp + j / ti.nph : h / p.grp;
         if (MODE == MODE_KV) {
           // stage the step's LSE and delta (queries row .. row+63)
           float* dst = ld_smem + st * 2 * SB;
-          const int64_t base = (int64_t)ti.bh * p.Tq;
+          const int64_t base = ((int64_t)b * p.Hq + hx) * p.Tq;
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int q = row + u * 32 + lane;
@@ -299,8 +310,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           mbar_arrive_expect_tx(&x_full[st], 2 * XTILE);
           uint8_t* xs = smem + RING_OFF + st * 2 * XTILE;
-          tma_load_4d(xs, &tmX, &x_full[st], 0, h, row, b);
-          tma_load_4d(xs + XTILE, &tmY, &x_full[st], 0, h, row, b);
+          tma_load_4d(xs, &tmX, &x_full[st], 0, hx, row, b);
+          tma_load_4d(xs + XTILE, &tmY, &x_full[st], 0, hx, row, b);
         }
         __syncwarp();
       }
@@ -452,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool rows_full = (MODE == MODE_KV) ? last_row < p.Tk : last_row < p.Tq;
       for (int j = 0; j < ti.n; ++j, ++g) {
         const uint32_t pb = g & 1, st = g % STAGES;
-        const int cst = ti.s0 + j * SB;               // step columns [cst, cst + 64)
+        const int cst = ti.s0 + (j % ti.nph) * SB;    // step columns [cst, cst + 64)
         const int c0 = cst + grp * NC;                // this thread's first column
         bool full;
         if (MODE == MODE_KV)
@@ -602,15 +613,20 @@ int attn_bwd_tc_launch(const AttnArgs& a, cudaStream_t s) {
       !out_ok(a.dk) || !out_ok(a.dv))
     return 0;
   if (a.B * a.H <= 0 || a.Tq <= 0 || a.Tk <= 0) return 0;
+  const int Hkv = a.Hkv > 0 ? a.Hkv : a.H;
+  if (Hkv > a.H || a.H % Hkv) return -1;
   CUtensorMap tq_a, tk_a, tv_a, tdo_a, tq_x, tk_x, tv_x, tdo_x;
-  if (!head_map(&tq_a, a.q, a.H, a.Tq, a.B, TB) || !head_map(&tk_a, a.k, a.H, a.Tk, a.B, TB) ||
-      !head_map(&tv_a, a.v, a.H, a.Tk, a.B, TB) || !head_map(&tdo_a, a.dout, a.H, a.Tq, a.B, TB) ||
-      !head_map(&tq_x, a.q, a.H, a.Tq, a.B, SB) || !head_map(&tk_x, a.k, a.H, a.Tk, a.B, SB) ||
-      !head_map(&tv_x, a.v, a.H, a.Tk, a.B, SB) || !head_map(&tdo_x, a.dout, a.H, a.Tq, a.B, SB))
+  if (!head_map(&tq_a, a.q, a.H, a.Tq, a.B, TB) || !head_map(&tk_a, a.k, Hkv, a.Tk, a.B, TB) ||
+      !head_map(&tv_a, a.v, Hkv, a.Tk, a.B, TB) || !head_map(&tdo_a, a.dout, a.H, a.Tq, a.B, TB) ||
+      !head_map(&tq_x, a.q, a.H, a.Tq, a.B, SB) || !head_map(&tk_x, a.k, Hkv, a.Tk, a.B, SB) ||
+      !head_map(&tv_x, a.v, Hkv, a.Tk, a.B, SB) || !head_map(&tdo_x, a.dout, a.H, a.Tq, a.B, SB))
     return 0;
   BwdParams p;
-  p.H = a.H;
-  p.BH = a.B * a.H;
+  // dK / dV tiles are per key/value head; each walks its group's query heads
+  p.H = Hkv;
+  p.BH = a.B * Hkv;
+  p.grp = a.H / Hkv;
+  p.Hq = a.H;
   p.Tq = a.Tq;
   p.Tk = a.Tk;
   p.q_offset = a.q_offset;
@@ -639,6 +655,9 @@ int attn_bwd_tc_launch(const AttnArgs& a, cudaStream_t s) {
   p.o1_st = a.dq.st;
   p.o1_sh = a.dq.sh;
   p.out2 = nullptr;
+  // dQ tiles are per query head, streaming their key/value head's blocks
+  p.H = a.H;
+  p.BH = a.B * a.H;
   p.n_blk = (a.Tq + TB - 1) / TB;
   p.n_tiles = p.n_blk * p.BH;
   rc = launch_mode<MODE_Q>(tq_a, tdo_a, tk_x, tv_x, p, s);

@@ -76,6 +76,7 @@ constexpr uint32_t kTmemCols = 512;
 struct TcParams {
   int B, H, Tq, Tk, q_offset, causal;
   int n_qpairs, n_items;
+  int grp;    // query heads per key/value head
   float sl2;  // softmax scale * log2(e)
   __nv_bfloat16* o;
   int64_t osb, ost, osh;
@@ -217,8 +218,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&kv_full[st], 2 * KVTILE);
-          tma_load_4d(smem + K_OFF + st * KVTILE, &tmK, &kv_full[st], 0, h, j * TKV, b);
-          tma_load_4d(smem + V_OFF + st * KVTILE, &tmV, &kv_full[st], 0, h, j * TKV, b);
+          tma_load_4d(smem + K_OFF + st * KVTILE, &tmK, &kv_full[st], 0, h / p.grp, j * TKV, b);
+          tma_load_4d(smem + V_OFF + st * KVTILE, &tmV, &kv_full[st], 0, h / p.grp, j * TKV, b);
         }
       }
     }
@@ -551,14 +552,17 @@ int attn_fwd_tc_launch(const AttnArgs& a, cudaStream_t s) {
   if (!head_view_tma_ok(a.q) || !head_view_tma_ok(a.k) || !head_view_tma_ok(a.v)) return 0;
   if ((a.o.sh * 2) % 16 || (a.o.st * 2) % 16 || (reinterpret_cast<uintptr_t>(a.o.base) & 15))
     return 0;
+  const int Hkv = a.Hkv > 0 ? a.Hkv : a.H;
+  if (Hkv > a.H || a.H % Hkv) return -1;
   CUtensorMap tq, tk, tv;
   if (!make_head_map(&tq, a.q, a.H, a.Tq, a.B, TQ) ||
-      !make_head_map(&tk, a.k, a.H, a.Tk, a.B, TKV) ||
-      !make_head_map(&tv, a.v, a.H, a.Tk, a.B, TKV))
+      !make_head_map(&tk, a.k, Hkv, a.Tk, a.B, TKV) ||
+      !make_head_map(&tv, a.v, Hkv, a.Tk, a.B, TKV))
     return 0;
   TcParams p;
   p.B = a.B;
   p.H = a.H;
+  p.grp = a.H / Hkv;
   p.Tq = a.Tq;
   p.Tk = a.Tk;
   p.q_offset = a.q_offset;

@@ -99,7 +99,7 @@ PYBIND11_MODULE(_C, m) {
 
   m.def("attn_fwd", [](int64_t q, int64_t k, int64_t v, int64_t o, int64_t sb, int64_t st,
                        int64_t sh, int64_t osb, int64_t ost, int64_t osh, int64_t lse, int B,
-                       int H, int Tq, int Tk, int q_offset, int causal, float scale,
+                       int H, int Hkv, int Tq, int Tk, int q_offset, int causal, float scale,
                        int64_t kv_sb, int64_t kv_st, int64_t kv_sh, int64_t err, int64_t stream) {
     AttnArgs a;
     a.q = hv(q, sb, st, sh);
@@ -109,6 +109,7 @@ PYBIND11_MODULE(_C, m) {
     a.lse = P<float>(lse);
     a.B = B;
     a.H = H;
+    a.Hkv = Hkv;
     a.Tq = Tq;
     a.Tk = Tk;
     a.q_offset = q_offset;
@@ -122,7 +123,7 @@ PYBIND11_MODULE(_C, m) {
         [](int64_t q, int64_t k, int64_t v, int64_t o, int64_t dout, int64_t dq, int64_t dk,
            int64_t dv, int64_t sb, int64_t st, int64_t sh, int64_t osb, int64_t ost, int64_t osh,
            int64_t dsb, int64_t dst, int64_t dsh, int64_t lse, int64_t delta, int B, int H,
-           int Tq, int Tk, int q_offset, int causal, float scale, int64_t kv_sb, int64_t kv_st,
+           int Hkv, int Tq, int Tk, int q_offset, int causal, float scale, int64_t kv_sb, int64_t kv_st,
            int64_t kv_sh, int64_t dkv_sb, int64_t dkv_st, int64_t dkv_sh, int64_t err,
            int64_t stream) {
           AttnArgs a;
@@ -138,6 +139,7 @@ PYBIND11_MODULE(_C, m) {
           a.delta = P<float>(delta);
           a.B = B;
           a.H = H;
+          a.Hkv = Hkv;
           a.Tq = Tq;
           a.Tk = Tk;
           a.q_offset = q_offset;

@@ -45,8 +45,8 @@ from gpt2_harness_b200.config import GPTConfig
 from gpt2_harness_b200.ops import native as N
 from gpt2_harness_b200.utils.nvtx import nvtx_range
 
-__all__ = ["ParamSpec", "ParamLayout", "CompactLayout", "Engine", "OptimConfig", "choose_splits",
-           "init_flat_weights"]
+__all__ = ["ParamSpec", "ParamLayout", "qkv_width", "qkv_views", "CompactLayout", "Engine",
+           "OptimConfig", "choose_splits", "init_flat_weights"]
 
 ALIGN = 64  # elements; 128 bytes of bf16, 256 bytes of fp32
 #: Device types the engine accepts. Only CUDA runs the native kernels; the
@@ -71,6 +71,19 @@ class ParamSpec:
         return n
 
 
+def qkv_width(config: GPTConfig) -> int:
+    """Columns of the fused c_attn output: C queries, then kv_heads x 64 keys
+    and as many values (3C for multi-head attention; reference model.py:
+    199-203)."""
+    return config.n_embd + 2 * config.kv_heads * config.head_dim
+
+
+def qkv_views(qkv: torch.Tensor, config: GPTConfig) -> tuple:
+    """(q, k, v) column views of a fused [M, qkv_width] buffer."""
+    C, kv = config.n_embd, config.kv_heads * config.head_dim
+    return qkv[:, :C], qkv[:, C:C + kv], qkv[:, C + kv:]
+
+
 class ParamLayout:
     """Flat, aligned layout of every GPT-2 parameter (tied weights once).
 
@@ -83,8 +96,8 @@ class ParamLayout:
             raise ValueError("the native engine implements GPT-2's tied lm_head")
         if config.pos_embedding != "learned" or config.norm_position != "pre":
             raise ValueError("the native engine implements pre-LN GPT-2 with learned positions")
-        if config.activation != "gelu_tanh" or config.head_dim != 64 or config.kv_heads != config.n_head:
-            raise ValueError("the native engine implements gelu_tanh, head_dim 64, MHA")
+        if config.activation != "gelu_tanh" or config.head_dim != 64:
+            raise ValueError("the native engine implements gelu_tanh, head_dim 64")
         if not (config.attn_bias and config.mlp_bias):
             raise ValueError("the native engine expects biased projections")
         self.config = config
@@ -99,8 +112,8 @@ class ParamLayout:
             specs += [
                 (p + "ln_1.weight", (C,), False, g),
                 (p + "ln_1.bias", (C,), False, g),
-                (p + "attn.c_attn.weight", (3 * C, C), True, g),
-                (p + "attn.c_attn.bias", (3 * C,), False, g),
+                (p + "attn.c_attn.weight", (qkv_width(config), C), True, g),
+                (p + "attn.c_attn.bias", (qkv_width(config),), False, g),
                 (p + "attn.c_proj.weight", (C, C), True, g),
                 (p + "attn.c_proj.bias", (C,), False, g),
                 (p + "ln_2.weight", (C,), False, g),
@@ -248,7 +261,8 @@ class _Acts:
         bf, f32 = torch.bfloat16, torch.float32
         self.x = [torch.empty(M, C, dtype=f32, device=dev) for _ in range(2 * L + 1)]
         self.h1 = [torch.empty(M, C, dtype=bf, device=dev) for _ in range(L)]
-        self.qkv = [torch.empty(M, 3 * C, dtype=bf, device=dev) for _ in range(L)]
+        W = qkv_width(cfg)
+        self.qkv = [torch.empty(M, W, dtype=bf, device=dev) for _ in range(L)]
         self.y = [torch.empty(M, C, dtype=bf, device=dev) for _ in range(L)]
         self.lse = [torch.empty(B, H, T, dtype=f32, device=dev) for _ in range(L)]
         self.h2 = [torch.empty(M, C, dtype=bf, device=dev) for _ in range(L)]
@@ -270,18 +284,18 @@ class _Acts:
         self.dh = torch.empty(M, C, dtype=bf, device=dev)
         self.dy = torch.empty(M, C, dtype=bf, device=dev)
         self.du = torch.empty(M, 4 * C, dtype=bf, device=dev)
-        self.dqkv = torch.empty(M, 3 * C, dtype=bf, device=dev)
+        self.dqkv = torch.empty(M, W, dtype=bf, device=dev)
         self.delta = torch.empty(B, H, T, dtype=f32, device=dev)
         self.ln_parts = N.layernorm_bwd_partials(M, C, dev)
         self.col_ws = torch.empty(N.colsum_ws_numel(M, 4 * C), dtype=f32, device=dev)
         # split-K plans for the four wgrad shapes
         self.splits = {
-            "c_attn": choose_splits(3 * C, C, M),
+            "c_attn": choose_splits(W, C, M),
             "c_proj": choose_splits(C, C, M),
             "c_fc": choose_splits(4 * C, C, M),
             "mlp_proj": choose_splits(C, 4 * C, M),
         }
-        ws = max(self.splits["c_attn"] * 3 * C * C, self.splits["c_proj"] * C * C,
+        ws = max(self.splits["c_attn"] * W * C, self.splits["c_proj"] * C * C,
                  self.splits["c_fc"] * 4 * C * C, self.splits["mlp_proj"] * 4 * C * C)
         self.splitk_ws = torch.empty(ws, dtype=f32, device=dev)
 
@@ -518,7 +532,7 @@ class Engine:
             if self.attn_fwd_hook is not None:
                 self.attn_fwd_hook(l, qkv, A.y[l], A.lse[l], B, H, T)
             else:
-                N.attention_fwd(qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:], A.y[l], A.lse[l], B, H, T)
+                N.attention_fwd(*qkv_views(qkv, cfg), A.y[l], A.lse[l], B, H, T, kv_heads=cfg.kv_heads)
             N.gemm(A.y[l], p(pre + "attn.c_proj.weight"), A.x[2 * l + 1], epilogue=N.EPI_RESID_F32,
                    bias=p(pre + "attn.c_proj.bias"), aux=A.x[2 * l])
             N.layernorm_fwd(A.x[2 * l + 1], p(pre + "ln_2.weight"), p(pre + "ln_2.bias"), A.h2[l],
@@ -602,9 +616,8 @@ class Engine:
             if self.attn_bwd_hook is not None:
                 self.attn_bwd_hook(l, qkv, A.y[l], A.dy, dqkv, A.lse[l], A.delta, B, H, T)
             else:
-                N.attention_bwd(qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:], A.y[l], A.dy,
-                                dqkv[:, :C], dqkv[:, C:2 * C], dqkv[:, 2 * C:], A.lse[l], A.delta,
-                                B, H, T)
+                N.attention_bwd(*qkv_views(qkv, cfg), A.y[l], A.dy, *qkv_views(dqkv, cfg), A.lse[l],
+                                A.delta, B, H, T, kv_heads=cfg.kv_heads)
             # attn.c_attn
             N.gemm(dqkv, p(pre + "attn.c_attn.weight"), A.dh, b_t=True)
             N.gemm(dqkv, A.h1[l], g(pre + "attn.c_attn.weight"), a_t=True, b_t=True,

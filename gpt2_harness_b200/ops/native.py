@@ -234,11 +234,15 @@ def _head_strides(t: torch.Tensor, T: int, H: int):
 def attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor,
                   lse: torch.Tensor, B: int, H: int, Tq: int, Tk: Optional[int] = None,
                   q_offset: int = 0, causal: bool = True, scale: Optional[float] = None,
-                  kv_rows: Optional[int] = None, q_rows: Optional[int] = None) -> None:
+                  kv_rows: Optional[int] = None, q_rows: Optional[int] = None,
+                  kv_heads: Optional[int] = None) -> None:
     """Causal flash attention on head_dim 64.
 
     q, o: [B*Tq, ...] row-major views whose columns h*64..h*64+63 hold head h
     (e.g. the q section of the fused qkv buffer); k, v: [B*Tk, ...] likewise.
+    kv_heads: key/value heads (grouped-query attention, reference model.py:
+    272-278): query head h reads key/value head h // (H // kv_heads) by index,
+    nothing is repeated in memory. Defaults to H.
     lse: fp32 [B, H, Tq] (log2-domain log-sum-exp, saved for backward).
     kv_rows: rows per sequence in the k/v buffers when they hold more than the
     Tk keys attended (context parallelism: a full-length key buffer of which
@@ -256,18 +260,20 @@ def attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Te
         raise ValueError("k and v must share strides")
     osb, ost, osh = _head_strides(o, qr, H)
     lib().attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), qsb, qst, qsh,
-                   osb, ost, osh, lse.data_ptr(), B, H, Tq, Tk, q_offset, int(causal),
-                   float(scale), ksb, kst, ksh, _err_ptr(), _stream())
+                   osb, ost, osh, lse.data_ptr(), B, H, kv_heads or H, Tq, Tk, q_offset,
+                   int(causal), float(scale), ksb, kst, ksh, _err_ptr(), _stream())
 
 
 def attention_bwd(q, k, v, o, dout, dq, dk, dv, lse, delta, B: int, H: int, Tq: int,
                   Tk: Optional[int] = None, q_offset: int = 0, causal: bool = True,
                   scale: Optional[float] = None, kv_rows: Optional[int] = None,
-                  q_rows: Optional[int] = None) -> None:
+                  q_rows: Optional[int] = None, kv_heads: Optional[int] = None) -> None:
     """Deterministic flash-attention backward (dK/dV pass, then dQ pass).
 
     dout shares o's strides; dq shares q's layout family; dk/dv share a layout.
-    delta: fp32 scratch [B, H, Tq]. kv_rows / q_rows as in :func:`attention_fwd`.
+    delta: fp32 scratch [B, H, Tq]. kv_rows / q_rows / kv_heads as in
+    :func:`attention_fwd`; with grouped heads each key/value tile sums the
+    gradients of every query head of its group in one pass (no atomics).
     """
     Tk = Tq if Tk is None else Tk
     kr = Tk if kv_rows is None else kv_rows
@@ -284,8 +290,8 @@ def attention_bwd(q, k, v, o, dout, dq, dk, dv, lse, delta, B: int, H: int, Tq: 
         raise ValueError("dk and dv must share strides")
     lib().attn_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dout.data_ptr(),
                    dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), qsb, qst, qsh, osb, ost, osh,
-                   dsb, dst, dsh, lse.data_ptr(), delta.data_ptr(), B, H, Tq, Tk, q_offset,
-                   int(causal), float(scale), ksb, kst, ksh, dksb, dkst, dksh, _err_ptr(),
+                   dsb, dst, dsh, lse.data_ptr(), delta.data_ptr(), B, H, kv_heads or H, Tq, Tk,
+                   q_offset, int(causal), float(scale), ksb, kst, ksh, dksb, dkst, dksh, _err_ptr(),
                    _stream())
 
 

@@ -77,6 +77,8 @@ class NativeCP:
                  layers: Optional[list] = None, slots: int = 1, balance: str = "zigzag") -> None:
         if not dist.is_initialized():
             raise RuntimeError("NativeCP needs an initialised process group")
+        if config.kv_heads != config.n_head:
+            raise ValueError("NativeCP gathers 2C-wide key/value rows: multi-head attention only")
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)

@@ -42,7 +42,8 @@ import torch
 import torch.distributed as dist
 
 from gpt2_harness_b200.config import GPTConfig
-from gpt2_harness_b200.models.engine import ALIGN, OptimConfig, ParamLayout, choose_splits, init_flat_weights
+from gpt2_harness_b200.models.engine import (ALIGN, OptimConfig, ParamLayout, choose_splits, init_flat_weights,
+                                            qkv_views, qkv_width)
 from gpt2_harness_b200.ops import native as N
 from gpt2_harness_b200.parallel import comms
 from gpt2_harness_b200.parallel.pipeline_parallel import schedule_order
@@ -108,7 +109,7 @@ class _Slot:
         self.mu = [torch.empty(M, dtype=f32, device=dev) for _ in range(2 * n + 1)]
         self.rs = [torch.empty(M, dtype=f32, device=dev) for _ in range(2 * n + 1)]
         self.h1 = [torch.empty(M, C, dtype=bf, device=dev) for _ in range(n)]
-        self.qkv = [torch.empty(M, 3 * C, dtype=bf, device=dev) for _ in range(n)]
+        self.qkv = [torch.empty(M, qkv_width(cfg), dtype=bf, device=dev) for _ in range(n)]
         self.y = [torch.empty(M, C, dtype=bf, device=dev) for _ in range(n)]
         self.lse = [torch.empty(B, H, T, dtype=f32, device=dev) for _ in range(n)]
         self.h2 = [torch.empty(M, C, dtype=bf, device=dev) for _ in range(n)]
@@ -189,13 +190,14 @@ class StageEngine:
         self.dh = torch.empty(M, C, dtype=bf, device=dev)
         self.dy = torch.empty(M, C, dtype=bf, device=dev)
         self.du = torch.empty(M, 4 * C, dtype=bf, device=dev)
-        self.dqkv = torch.empty(M, 3 * C, dtype=bf, device=dev)
+        W = qkv_width(config)
+        self.dqkv = torch.empty(M, W, dtype=bf, device=dev)
         self.delta = torch.empty(micro_batch, cfg.n_head, seq_len, dtype=f32, device=dev)
         self.ln_parts = N.layernorm_bwd_partials(M, C, dev)
         self.col_ws = torch.empty(N.colsum_ws_numel(M, 4 * C), dtype=f32, device=dev)
-        self.splits = {"c_attn": choose_splits(3 * C, C, M), "c_proj": choose_splits(C, C, M),
+        self.splits = {"c_attn": choose_splits(W, C, M), "c_proj": choose_splits(C, C, M),
                        "c_fc": choose_splits(4 * C, C, M), "mlp_proj": choose_splits(C, 4 * C, M)}
-        ws = max(self.splits["c_attn"] * 3 * C * C, self.splits["c_proj"] * C * C,
+        ws = max(self.splits["c_attn"] * W * C, self.splits["c_proj"] * C * C,
                  self.splits["c_fc"] * 4 * C * C, self.splits["mlp_proj"] * 4 * C * C)
         self.splitk_ws = torch.empty(ws, dtype=f32, device=dev)
         self.hp = torch.zeros(8, dtype=f32, device=dev)
@@ -275,7 +277,7 @@ class StageEngine:
             if self.attn_fwd_hook is not None:
                 self.attn_fwd_hook(lay.l0 + j, qkv, S.y[j], S.lse[j], B, H, T)
             else:
-                N.attention_fwd(qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:], S.y[j], S.lse[j], B, H, T)
+                N.attention_fwd(*qkv_views(qkv, cfg), S.y[j], S.lse[j], B, H, T, kv_heads=cfg.kv_heads)
             N.gemm(S.y[j], p(pre + "attn.c_proj.weight"), S.x[2 * j + 1], epilogue=N.EPI_RESID_F32,
                    bias=p(pre + "attn.c_proj.bias"), aux=S.x[2 * j])
             N.layernorm_fwd(S.x[2 * j + 1], p(pre + "ln_2.weight"), p(pre + "ln_2.bias"), S.h2[j],
@@ -336,9 +338,8 @@ class StageEngine:
             if self.attn_bwd_hook is not None:
                 self.attn_bwd_hook(l0 + j, qkv, S.y[j], self.dy, dqkv, S.lse[j], self.delta, B, H, T)
             else:
-                N.attention_bwd(qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:], S.y[j], self.dy,
-                                dqkv[:, :C], dqkv[:, C:2 * C], dqkv[:, 2 * C:], S.lse[j], self.delta,
-                                B, H, T)
+                N.attention_bwd(*qkv_views(qkv, cfg), S.y[j], self.dy, *qkv_views(dqkv, cfg), S.lse[j],
+                                self.delta, B, H, T, kv_heads=cfg.kv_heads)
             N.gemm(dqkv, p(pre + "attn.c_attn.weight"), self.dh, b_t=True)
             N.gemm(dqkv, S.h1[j], g(pre + "attn.c_attn.weight"), a_t=True, b_t=True,
                    epilogue=N.EPI_F32, accumulate=acc, splits=self.splits["c_attn"], workspace=ws)

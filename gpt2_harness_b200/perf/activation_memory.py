@@ -261,7 +261,7 @@ def native_activation_bytes(cfg: GPTConfig, batch: int, seq: int) -> dict[str, f
         "residual_stream_fp32": 2 * M * C * 4,  # x_in and x_mid per block
         "ln_stats_fp32": 2 * 2 * M * 4,
         "ln1_out_bf16": M * C * 2,
-        "qkv_bf16": M * 3 * C * 2,
+        "qkv_bf16": M * (C + 2 * cfg.kv_heads * cfg.head_dim) * 2,
         "attn_out_bf16": M * C * 2,
         "attn_lse_fp32": batch * H * seq * 4,
         "ln2_out_bf16": M * C * 2,

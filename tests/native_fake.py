@@ -202,13 +202,16 @@ def _heads(t, b, rows, T, H):
 
 
 def attention_fwd(q, k, v, o, lse, B, H, Tq, Tk=None, q_offset=0, causal=True, scale=None,
-                  kv_rows=None, q_rows=None):
+                  kv_rows=None, q_rows=None, kv_heads=None):
     Tk = Tq if Tk is None else Tk
     qr = Tq if q_rows is None else q_rows
     kr = Tk if kv_rows is None else kv_rows
     scale = 1.0 / 8.0 if scale is None else scale
+    G = H // (kv_heads or H)
     for b in range(B):
-        Q, K, V = _heads(q, b, qr, Tq, H), _heads(k, b, kr, Tk, H), _heads(v, b, kr, Tk, H)
+        Q = _heads(q, b, qr, Tq, H)
+        K = _heads(k, b, kr, Tk, H // G).repeat_interleave(G, 1)
+        V = _heads(v, b, kr, Tk, H // G).repeat_interleave(G, 1)
         s = torch.einsum("thd,shd->hts", Q, K) * scale
         if causal:
             mask = torch.arange(Tk)[None, :] > (torch.arange(Tq)[:, None] + q_offset)
@@ -218,25 +221,26 @@ def attention_fwd(q, k, v, o, lse, B, H, Tq, Tk=None, q_offset=0, causal=True, s
 
 
 def attention_bwd(q, k, v, o, dout, dq, dk, dv, lse, delta, B, H, Tq, Tk=None, q_offset=0, causal=True,
-                  scale=None, kv_rows=None, q_rows=None):
+                  scale=None, kv_rows=None, q_rows=None, kv_heads=None):
     Tk = Tq if Tk is None else Tk
     qr = Tq if q_rows is None else q_rows
     kr = Tk if kv_rows is None else kv_rows
     scale = 1.0 / 8.0 if scale is None else scale
+    G = H // (kv_heads or H)
     for b in range(B):
         Q = _heads(q, b, qr, Tq, H).requires_grad_(True)
-        K = _heads(k, b, kr, Tk, H).requires_grad_(True)
-        V = _heads(v, b, kr, Tk, H).requires_grad_(True)
+        K = _heads(k, b, kr, Tk, H // G).requires_grad_(True)
+        V = _heads(v, b, kr, Tk, H // G).requires_grad_(True)
         with torch.enable_grad():
-            s = torch.einsum("thd,shd->hts", Q, K) * scale
+            s = torch.einsum("thd,shd->hts", Q, K.repeat_interleave(G, 1)) * scale
             if causal:
                 mask = torch.arange(Tk)[None, :] > (torch.arange(Tq)[:, None] + q_offset)
                 s = s.masked_fill(mask[None], float("-inf"))
-            out = torch.einsum("hts,shd->thd", torch.softmax(s, -1), V)
+            out = torch.einsum("hts,shd->thd", torch.softmax(s, -1), V.repeat_interleave(G, 1))
             gq, gk, gv = torch.autograd.grad(out, (Q, K, V), _heads(dout, b, qr, Tq, H))
         dq[b * qr: b * qr + Tq].copy_(gq.reshape(Tq, H * 64))
-        dk[b * kr: b * kr + Tk].copy_(gk.reshape(Tk, H * 64))
-        dv[b * kr: b * kr + Tk].copy_(gv.reshape(Tk, H * 64))
+        dk[b * kr: b * kr + Tk].copy_(gk.reshape(Tk, H // G * 64))
+        dv[b * kr: b * kr + Tk].copy_(gv.reshape(Tk, H // G * 64))
 
 
 # ------------------------------------------------------------------ decode --

@@ -31,10 +31,12 @@ def make_batch(cfg, B, T, seed=0):
     return idx, tgt
 
 
-@pytest.mark.parametrize("B,T,fused_ce", [(2, 128, False), (3, 200, False), (3, 200, True)])
-def test_engine_loss_and_grads_match_oracle(B, T, fused_ce):
+@pytest.mark.parametrize("B,T,fused_ce,kv", [(2, 128, False, None), (3, 200, False, None),
+                                              (3, 200, True, None), (2, 256, False, 2), (2, 128, False, 1)])
+def test_engine_loss_and_grads_match_oracle(B, T, fused_ce, kv):
+    """kv: key/value heads (grouped-query / multi-query attention) or None."""
     torch.manual_seed(0)
-    cfg = small_config()
+    cfg = small_config(n_kv_head=kv)
     model = GPT(cfg)
     idx, tgt = make_batch(cfg, B, T)
     tgt[0, :5] = -100

@@ -24,12 +24,15 @@ def _batches(m, B, T, seed=3):
     return idx, tgt
 
 
-def test_engine_matches_autograd_oracle(monkeypatch):
+@pytest.mark.parametrize("n_kv_head", [None, 1])
+def test_engine_matches_autograd_oracle(monkeypatch, n_kv_head):
+    """n_kv_head: grouped key/value heads (here multi-query) through the same
+    fused qkv layout as the torch model."""
     from gpt2_harness_b200.models.engine import Engine, OptimConfig
     from gpt2_harness_b200.models.gpt import GPT
 
     with native_fake.installed(monkeypatch):
-        cfg = GPTConfig(**CFG)
+        cfg = GPTConfig(**CFG, n_kv_head=n_kv_head)
         eng = Engine(cfg, "cpu", optim=OptimConfig(lr=1e-3), seed=0)
         model = GPT(cfg)
         model.load_state_dict(eng.state_dict(), strict=False)

@@ -224,6 +224,42 @@ def test_attention_fwd_bwd(B, H, T):
         assert rel_err(heads(got_g), ref_g) < 3e-2
 
 
+@pytest.mark.parametrize("B,H,KV,T", [(2, 4, 2, 256), (2, 12, 4, 1024), (1, 8, 1, 384), (2, 6, 3, 200)])
+def test_attention_grouped_kv_heads(B, H, KV, T):
+    """Grouped-query (and multi-query) attention: query head h reads key/value
+    head h // (H // KV) by index; dK/dV sum over the group's query heads.
+    Against fp32 torch with the key/value heads repeated (reference model.py:
+    272-278)."""
+    C, D = H * 64, KV * 64
+    torch.manual_seed(H * 7 + KV)
+    qkv = torch.randn(B * T, C + 2 * D, device=dev()).bfloat16()
+    q, k, v = qkv[:, :C], qkv[:, C:C + D], qkv[:, C + D:]
+    o = torch.empty(B * T, C, dtype=torch.bfloat16, device=dev())
+    lse = torch.empty(B, H, T, device=dev())
+    N.attention_fwd(q, k, v, o, lse, B, H, T, kv_heads=KV)
+
+    def heads(x, n):
+        return x.float().view(B, T, n, 64).transpose(1, 2)
+
+    qh = heads(q, H).requires_grad_(True)
+    kh = heads(k, KV).requires_grad_(True)
+    vh = heads(v, KV).requires_grad_(True)
+    G = H // KV
+    ref = ref_attention(qh, kh.repeat_interleave(G, 1), vh.repeat_interleave(G, 1))
+    assert rel_err(heads(o, H), ref.detach()) < 2e-2
+
+    do = torch.randn(B * T, C, device=dev()).bfloat16()
+    dqkv = torch.empty_like(qkv)
+    delta = torch.empty(B, H, T, device=dev())
+    N.attention_bwd(q, k, v, o, do, dqkv[:, :C], dqkv[:, C:C + D], dqkv[:, C + D:], lse, delta,
+                    B, H, T, kv_heads=KV)
+    N.check_errors()
+    gq, gk, gv = torch.autograd.grad(ref, (qh, kh, vh), heads(do, H))
+    assert rel_err(heads(dqkv[:, :C], H), gq) < 3e-2
+    assert rel_err(heads(dqkv[:, C:C + D], KV), gk) < 3e-2
+    assert rel_err(heads(dqkv[:, C + D:], KV), gv) < 3e-2
+
+
 def test_attention_q_offset():
     # context-parallel shard: 64 local queries at absolute offset 128 vs 256 keys
     B, H, Tq, Tk, off = 1, 2, 64, 256, 128
