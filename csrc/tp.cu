@@ -360,7 +360,7 @@ __global__ void __launch_bounds__(CE_T) tp_ce_stats_kernel(const TpArgs a) {
 // (padded columns get 0).
 __global__ void __launch_bounds__(CE_T) tp_ce_finish_kernel(const TpArgs a) {
   __shared__ int fail;
-  __shared__ float s_lse;
+  __shared__ float s_gm, s_inv;
   __shared__ int64_t s_t;
   if (threadIdx.x == 0) fail = 0;
   __syncthreads();
@@ -382,18 +382,21 @@ __global__ void __launch_bounds__(CE_T) tp_ce_finish_kernel(const TpArgs a) {
       const float lse = gm + __logf(tot);
       const int64_t tgt = a.idx[row];
       a.loss_rows[row] = tgt == -100 ? 0.f : lse - tl;
-      s_lse = lse;
+      s_gm = gm;
+      s_inv = 1.f / tot;
       s_t = tgt == -100 ? -1 : tgt - a.vocab_start;
     }
     __syncthreads();
-    const float lse = s_lse;
+    // softmax as the single-GPU cross-entropy kernel forms it:
+    // exp(l - global max) x (1 / global sum)
+    const float gm = s_gm, inv = s_inv;
     const int64_t t = s_t;
     const bool ignore = a.idx[row] == -100;
     __nv_bfloat16* lr = a.logits + row * a.ld;
     for (int c = threadIdx.x; c < a.ld; c += blockDim.x) {
       float g = 0.f;
       if (!ignore && c < a.vocab_valid) {
-        g = __expf(__bfloat162float(lr[c]) - lse);
+        g = __expf(__bfloat162float(lr[c]) - gm) * inv;
         if (c == t) g -= 1.f;
       }
       lr[c] = __float2bfloat16(g);
@@ -616,6 +619,19 @@ int tp_ag_rows_launch(TpArgs a, cudaStream_t s) {
 
 int tp_rs_rows_launch(TpArgs a, cudaStream_t s) {
   if (!common_ok(a) || a.cols % 8 || a.rows <= 0) return -1;
+  switch (a.world) {
+      case 1: tp_rs_rows_f32_kernel<1><<<a.nblocks, 512, 0, s>>>(a); break;
+      case 2: tp_rs_rows_f32_kernel<2><<<a.nblocks, 512, 0, s>>>(a); break;
+      case 3: tp_rs_rows_f32_kernel<3><<<a.nblocks, 512, 0, s>>>(a); break;
+      case 4: tp_rs_rows_f32_kernel<4><<<a.nblocks, 512, 0, s>>>(a); break;
+      case 5: tp_rs_rows_f32_kernel<5><<<a.nblocks, 512, 0, s>>>(a); break;
+      case 6: tp_rs_rows_f32_kernel<6><<<a.nblocks, 512, 0, s>>>(a); break;
+      case 7: tp_rs_rows_f32_kernel<7><<<a.nblocks, 512, 0, s>>>(a); break;
+      default: tp_rs_rows_f32_kernel<8><<<a.nblocks, 512, 0, s>>>(a); break;
+    }
+    count_launches(1);
+    return launch_succeeded() ? 0 : -11;
+  }
   switch (a.world) {
     case 1: tp_rs_rows_kernel<1><<<a.nblocks, 512, 0, s>>>(a); break;
     case 2: tp_rs_rows_kernel<2><<<a.nblocks, 512, 0, s>>>(a); break;

@@ -358,6 +358,14 @@ def colsum_bf16(x: torch.Tensor, out: torch.Tensor, ws: torch.Tensor, accumulate
                       int(accumulate), _stream())
 
 
+def colsum_f32(x: torch.Tensor, out: torch.Tensor, accumulate: bool = True) -> None:
+    """out (+)= x.sum(0) for a contiguous fp32 [R, C] tensor (fixed order)."""
+    R, C = x.shape
+    if not x.is_contiguous():
+        raise ValueError("colsum_f32 needs a contiguous input")
+    lib().colsum_f32(x.data_ptr(), R, C, out.data_ptr(), int(accumulate), _stream())
+
+
 def colsum_ws_numel(M: int, C: int) -> int:
     return ((M + 127) // 128) * C
 

@@ -314,9 +314,10 @@ class StageEngine:
                             accumulate_dsum=acc)
         else:
             # self.dres holds the gradient received from the next stage; its
-            # column sum is the bias gradient of this stage's last projection
+            # column sum is the bias gradient of this stage's last projection,
+            # summed in fp32 as the single-GPU engine's LayerNorm backward does
             N.cast_f32_bf16(self.dres, self.dres16)
-            N.colsum_bf16(self.dres16, top_bias, self.col_ws, accumulate=acc)
+            N.colsum_f32(self.dres, top_bias, accumulate=acc)
         for j in reversed(range(n)):
             pre = f"h.{l0 + j}."
             N.gemm(self.dres16, p(pre + "mlp.c_proj.weight"), self.du, b_t=True, epilogue=N.EPI_GELU_BWD,

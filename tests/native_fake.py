@@ -145,6 +145,11 @@ def colsum_bf16(x, out, ws, accumulate=True):
     out.copy_(out + s if accumulate else s)
 
 
+def colsum_f32(x, out, accumulate=True):
+    s = x.sum(0)
+    out.copy_(out + s if accumulate else s)
+
+
 def _positions(T, pos0, pos_split, pos1, device):
     split = T if pos_split is None else pos_split
     t = torch.arange(T, device=device)
@@ -557,11 +562,12 @@ def tp_ce_finish(d, stream=0):
     dist.barrier(group=_group(d["peer_flags"]))
     S = torch.stack([s.clone() for s in stats])          # [world, rows, 4]
     gm = S[:, :, 0].max(0).values
-    lse = gm + torch.log((S[:, :, 1] * torch.exp(S[:, :, 0] - gm)).sum(0))
+    tot = (S[:, :, 1] * torch.exp(S[:, :, 0] - gm)).sum(0)
+    lse = gm + torch.log(tot)
     tl = (S[:, :, 2] * S[:, :, 3]).sum(0)
     ignore = tgt == -100
     loss_rows.copy_(torch.where(ignore, torch.zeros(rows), lse - tl))
-    g = torch.exp(logits[:, :vv].float() - lse[:, None])
+    g = torch.exp(logits[:, :vv].float() - gm[:, None]) / tot[:, None]
     t = tgt - v0
     hit = (~ignore) & (t >= 0) & (t < vv)
     g[hit.nonzero()[:, 0], t[hit]] -= 1.0
@@ -710,7 +716,7 @@ class _Event:
 
 OPS = {
     "gemm": gemm, "layernorm_fwd": layernorm_fwd, "layernorm_bwd": layernorm_bwd,
-    "layernorm_bwd_partials": layernorm_bwd_partials, "colsum_bf16": colsum_bf16,
+    "layernorm_bwd_partials": layernorm_bwd_partials, "colsum_bf16": colsum_bf16, "colsum_f32": colsum_f32,
     "embedding_fwd": embedding_fwd, "embedding_bwd": embedding_bwd,
     "cross_entropy_fwd_bwd": cross_entropy_fwd_bwd, "lm_head_cross_entropy": lm_head_cross_entropy,
     "attention_fwd": attention_fwd,

@@ -103,11 +103,13 @@ def _pp_worker(rank, world, schedule, m):
                                               (4, "1f1b", 8)])
 def test_pipeline_matches_accumulated_engine(world, schedule, m):
     res = spawn_workers(_pp_worker, world, {"schedule": schedule, "m": m}, backend="gloo", timeout=240)
-    # Same op contracts on both sides, so only rounding points differ: a
-    # non-last stage takes its top projection's bias gradient from the bf16
-    # copy of the received gradient (the engine from the fp32 one), ~1e-3.
+    # Same ops on the same operands on both sides (the top projection's bias
+    # gradient is the fp32 column sum of the received gradient, as in the
+    # engine): only the tied embedding's two halves are added in another
+    # order, so every gradient agrees to the reference's 1e-5 class (measured
+    # here: 0 for every block tensor, 5e-8 for the embedding).
     for r in (x.value for x in res):
-        assert r["worst"] < 5e-3, r
+        assert r["worst"] < 1e-6, r
         # m activations forward and m gradients back per boundary, fp32
         assert r["sends"] == r["want_sends"], r
         if r["last"]:
@@ -269,7 +271,10 @@ def test_tensor_parallel_matches_single_engine(world, xl):
     res = spawn_workers(_tp_worker, world, {"xl": xl}, backend="gloo", timeout=600)
     for r in (x.value for x in res):
         assert abs(r["loss"] - r["ref_loss"]) < 1e-3 * r["ref_loss"], r
-        # row-parallel partials are rounded to bf16 before the reduction
+        # The row-parallel GEMMs split their K sums across ranks, so bf16
+        # activations downstream round differently in a few elements; that,
+        # not the bf16 partials, sets this bound (fp32 partials measured
+        # 3.3e-3 at 3 ranks against 6.8e-3 with bf16 ones).
         assert r["worst"] < 2e-2, r
         assert r["payload"] == r["closed_form"], r
 

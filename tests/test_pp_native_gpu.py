@@ -131,7 +131,8 @@ def test_native_pp_matches_single_gpu(pp, cp, schedule, cfg):
     res = _run(pp * cp, pp, cp, schedule, cfg)
     print(res)
     for r in res:
-        assert r["worst_err"] < 2e-2, r
+        # the same kernels on the same operands: the reference's 1e-5 class
+        assert r["worst_err"] < 1e-5, r
         assert abs(r["mean_loss"] - r["ref_loss"]) < 1e-3 * r["ref_loss"], r
         if r["last"]:
             assert r["loss"][-1] < r["loss"][0], r
