@@ -620,19 +620,6 @@ int tp_ag_rows_launch(TpArgs a, cudaStream_t s) {
 int tp_rs_rows_launch(TpArgs a, cudaStream_t s) {
   if (!common_ok(a) || a.cols % 8 || a.rows <= 0) return -1;
   switch (a.world) {
-      case 1: tp_rs_rows_f32_kernel<1><<<a.nblocks, 512, 0, s>>>(a); break;
-      case 2: tp_rs_rows_f32_kernel<2><<<a.nblocks, 512, 0, s>>>(a); break;
-      case 3: tp_rs_rows_f32_kernel<3><<<a.nblocks, 512, 0, s>>>(a); break;
-      case 4: tp_rs_rows_f32_kernel<4><<<a.nblocks, 512, 0, s>>>(a); break;
-      case 5: tp_rs_rows_f32_kernel<5><<<a.nblocks, 512, 0, s>>>(a); break;
-      case 6: tp_rs_rows_f32_kernel<6><<<a.nblocks, 512, 0, s>>>(a); break;
-      case 7: tp_rs_rows_f32_kernel<7><<<a.nblocks, 512, 0, s>>>(a); break;
-      default: tp_rs_rows_f32_kernel<8><<<a.nblocks, 512, 0, s>>>(a); break;
-    }
-    count_launches(1);
-    return launch_succeeded() ? 0 : -11;
-  }
-  switch (a.world) {
     case 1: tp_rs_rows_kernel<1><<<a.nblocks, 512, 0, s>>>(a); break;
     case 2: tp_rs_rows_kernel<2><<<a.nblocks, 512, 0, s>>>(a); break;
     case 3: tp_rs_rows_kernel<3><<<a.nblocks, 512, 0, s>>>(a); break;
