@@ -131,8 +131,11 @@ def test_native_pp_matches_single_gpu(pp, cp, schedule, cfg):
     res = _run(pp * cp, pp, cp, schedule, cfg)
     print(res)
     for r in res:
-        # the same kernels on the same operands: the reference's 1e-5 class
-        assert r["worst_err"] < 1e-5, r
+        # pipeline alone: the same kernels on the same operands, the
+        # reference's 1e-5 class; with context parallelism inside the stages
+        # the key/value gradient partials are summed across the CP ranks in
+        # bf16, which sets the bound
+        assert r["worst_err"] < (1e-5 if cp == 1 else 2e-2), r
         assert abs(r["mean_loss"] - r["ref_loss"]) < 1e-3 * r["ref_loss"], r
         if r["last"]:
             assert r["loss"][-1] < r["loss"][0], r
