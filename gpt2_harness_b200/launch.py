@@ -127,7 +127,7 @@ def main(argv=None, device: Optional[torch.device] = None) -> int:
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--lr", type=float, default=6e-4)
     ap.add_argument("--warmup", type=int, default=100)
-    ap.add_argument("--comm", choices=["p2p", "nccl"], default="p2p")
+    ap.add_argument("--comm", choices=["p2p", "mc", "nccl"], default="p2p")
     ap.add_argument("--ckpt-dir", default=None)
     ap.add_argument("--ckpt-every", type=int, default=500)
     ap.add_argument("--log", default=None, help="JSONL metrics (rank 0)")
