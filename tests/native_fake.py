@@ -365,6 +365,15 @@ class FakeSymmetricBuffer:
         self._maps = []
 
 
+class FakeMulticastBuffer(FakeSymmetricBuffer):
+    """The multicast form's stand-in: the same shared host buffers, and an
+    ``mc_ptr`` the fake all-reduce only checks for being set."""
+
+    def __init__(self, nbytes: int, group=None, device=None) -> None:
+        super().__init__(nbytes, group, device)
+        self.mc_ptr = self.ptr
+
+
 def _group(flags_ptr):
     """The process group of the symmetric flag buffer a kernel call names."""
     buf = FakeSymmetricBuffer.by_ptrs.get(int(flags_ptr))
@@ -749,6 +758,7 @@ def installed(monkeypatch):
     monkeypatch.setattr(N, "error_word", lambda *a, **k: torch.zeros(1, dtype=torch.int32))
     monkeypatch.setattr(cp_native, "SymmetricBuffer", FakeSymmetricBuffer)
     monkeypatch.setattr(ddp_native, "SymmetricBuffer", FakeSymmetricBuffer)
+    monkeypatch.setattr(ddp_native, "MulticastBuffer", FakeMulticastBuffer)
     monkeypatch.setattr(symm, "SymmetricBuffer", FakeSymmetricBuffer)
     monkeypatch.setattr(tp_native, "SymmetricBuffer", FakeSymmetricBuffer)
     monkeypatch.setattr(zero_native, "SymmetricBuffer", FakeSymmetricBuffer)

@@ -171,7 +171,7 @@ def test_context_parallel_matches_full_sequence(world, balance):
         assert r["payload"] == r["closed_form"], r
 
 
-def _ddp_worker(rank, world, bucket_mb, small=False):
+def _ddp_worker(rank, world, bucket_mb, small=False, comm="p2p"):
     import torch.distributed as dist
 
     import native_fake as nf
@@ -184,7 +184,7 @@ def _ddp_worker(rank, world, bucket_mb, small=False):
     # GPT-2 small widths (two blocks) for the BASELINE DDP mesh, else tiny
     cfg = gpt2_config("gpt2", n_layer=2, n_positions=64) if small else GPTConfig(**CFG)
     B, T = 2, 32
-    tr = Trainer(cfg, B, T, strategy="ddp", device="cpu", bucket_bytes=int(bucket_mb * 2**20))
+    tr = Trainer(cfg, B, T, strategy="ddp", device="cpu", bucket_bytes=int(bucket_mb * 2**20), comm=comm)
     g = torch.Generator().manual_seed(11)
     idx = torch.randint(0, CFG["vocab_size"], (B * world, T), generator=g)
     tgt = torch.randint(0, CFG["vocab_size"], (B * world, T), generator=g)
@@ -208,11 +208,12 @@ def _ddp_worker(rank, world, bucket_mb, small=False):
             "buckets": len(tr.ddp.buckets), "grad_bytes": eng.layout.total * 4}
 
 
-@pytest.mark.parametrize("world,bucket_mb,small", [(2, 0.25, False), (2, 25.0, False), (4, 0.5, False),
-                                                   pytest.param(8, 25.0, True, marks=pytest.mark.slow)])
-def test_native_ddp_matches_full_batch(world, bucket_mb, small):
-    res = spawn_workers(_ddp_worker, world, {"bucket_mb": bucket_mb, "small": small}, backend="gloo",
-                        timeout=600)
+@pytest.mark.parametrize("world,bucket_mb,small,comm", [(2, 0.25, False, "p2p"), (2, 25.0, False, "p2p"),
+                                                        (4, 0.5, False, "p2p"), (2, 0.25, False, "mc"),
+                                                        pytest.param(8, 25.0, True, "p2p", marks=pytest.mark.slow)])
+def test_native_ddp_matches_full_batch(world, bucket_mb, small, comm):
+    res = spawn_workers(_ddp_worker, world, {"bucket_mb": bucket_mb, "small": small, "comm": comm},
+                        backend="gloo", timeout=600)
     for r in (x.value for x in res):
         assert abs(r["loss"] - r["ref_loss"]) < 1e-5 * r["ref_loss"], r
         # a row's fp32 GEMM result depends on the batch the BLAS sees; a last-bit
