@@ -148,8 +148,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* kv_empty = kv_full + KS;    // KS
   uint64_t* s_full = kv_empty + KS;     // NG x 2 (S double buffer)
   uint64_t* p_full = s_full + 2 * NG;   // NG
-  uint64_t* o_full = p_full + NG;       // NG
-  uint64_t* turn = o_full + NG;         // 2: exp-phase turn-taking of the two groups
+  // o_full[2g + b]: P.V of tile g's blocks with count parity b is complete
+  // (phase k of barrier b = the P.V of block count 2k + b)
+  uint64_t* o_full = p_full + NG;       // NG x 2
+  uint64_t* turn = o_full + 2 * NG;     // 2: exp-phase turn-taking of the two groups
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(turn + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -168,7 +170,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_full[2 * g], 1);
       mbar_init(&s_full[2 * g + 1], 1);
       mbar_init(&p_full[g], 128);
-      mbar_init(&o_full[g], 1);
+      mbar_init(&o_full[2 * g], 1);
+      mbar_init(&o_full[2 * g + 1], 1);
     }
     mbar_init(&turn[0], 128);
     mbar_init(&turn[1], 128);
@@ -294,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               umma_bf16(tmem + 256 + g * 64, umma_desc_sw128(pa + ks * 32, 16, 1024),
                         umma_desc_sw128(vb + ks * 2048, 8192, 1024), idesc_pv,
                         (ks > 0 || j > 0) ? 1u : 0u);
-            umma_commit(&o_full[g]);
+            umma_commit(&o_full[2 * g + (c & 1)]);
             if (j + 2 < it.nblk[g]) issue_s(g, c + 2, (kc + 2) % KS);
           }
           umma_commit(&kv_empty[st]);
@@ -429,6 +432,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (i + 32 >= valid) sb[i] = 0u;
           }
         }
+        // P buffer c%2 was last read by P.V(c-2): wait for it (long done in
+        // the steady state; an earlier item's P.V was already waited for)
+        if (c >= 2 && !mbar_wait_bounded(&o_full[2 * g + (c & 1)], ((c - 2) >> 1) & 1, p.err,
+                                         ERR_TIMEOUT_ATTN, abort_flag)) {
+          ok = false;
+          break;
+        }
         float rs8[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) rs8[i] = 0.f;
@@ -447,10 +457,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         // hand the exponential unit to the other group
         if (alt && (g == 0 || j + 1 < m_alt)) mbar_arrive(&turn[g ^ 1]);
         if (tr) FTR(g, c, 5);
-        // P.V(c-1) is complete (consumed every block so the phase parity never
-        // aliases); after it O is safe to rescale.
-        if (j > 0 &&
-            !mbar_wait_bounded(&o_full[g], (c - 1) & 1, p.err, ERR_TIMEOUT_ATTN, abort_flag)) {
+        // O is rescaled only once P.V(c-1) is complete; otherwise P.V(c-1)
+        // is not waited for here, so the tensor core runs it while this
+        // group turns the next S into P. Each parity barrier is still
+        // waited for phase by phase (P.V(k) at block k+2), never more than
+        // one phase behind, so its parity cannot alias.
+        if (rescale &&
+            !mbar_wait_bounded(&o_full[2 * g + ((c - 1) & 1)], ((c - 1) >> 1) & 1, p.err,
+                               ERR_TIMEOUT_ATTN, abort_flag)) {
           ok = false;
           break;
         }
@@ -479,7 +493,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       // epilogue: O = (sum over blocks of P.V) / l, read once the last P.V is done
-      if (!mbar_wait_bounded(&o_full[g], (cnt + n - 1) & 1, p.err, ERR_TIMEOUT_ATTN,
+      const int c_end = cnt + n - 1;  // the item's last block: its P.V completes after all others
+      if (!mbar_wait_bounded(&o_full[2 * g + (c_end & 1)], (c_end >> 1) & 1, p.err, ERR_TIMEOUT_ATTN,
                              abort_flag)) {
         ok = false;
         break;
