@@ -160,6 +160,10 @@ __device__ __forceinline__ void put_row(uint8_t* tile, int r, int grp, const uin
 // and (causal) the query position is >= min_q (= key position - q_offset).
 // The mask test sits outside the element loop so each variant is one
 // straight-line block the compiler can interleave across elements.
+// Every exponential runs on the exponential unit: the FMA and ALU pipes carry
+// the rest of the elementwise work here. Measured on a B200 (16x1024, 12
+// heads, both kernels): 2 of every 4 on the FMA pipe (exp2_fma) 0.268 ms, 1 of
+// 4 0.259 ms, none 0.2525 ms.
 template <bool MASK>
 __device__ __forceinline__ void ew_kv(uint32_t (&sv)[NC], uint32_t (&dv)[NC], const float* lse_s,
                                       float sl2, int c0, int Tq, bool row_in, int causal, int min_q) {
@@ -172,9 +176,8 @@ __device__ __forceinline__ void ew_kv(uint32_t (&sv)[NC], uint32_t (&dv)[NC], co
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int ii = q * 4 + u;
-      // odd columns on the FMA pipe (exp2_fma), even ones on the exponential unit
       const float e = fmaf(__uint_as_float(sv[ii]), sl2, -la[u]);
-      float pr = (u & 1) ? exp2_fma(e) : ex2f(e);
+      float pr = ex2f(e);
       if (MASK) {
         const int col = c0 + ii;
         const bool vis = col < Tq && row_in && (!causal || col >= min_q);
@@ -195,7 +198,7 @@ __device__ __forceinline__ void ew_q(const uint32_t (&sv)[NC], uint32_t (&dv)[NC
 #pragma unroll
   for (int ii = 0; ii < NC; ++ii) {
     const float e = fmaf(__uint_as_float(sv[ii]), sl2, -lse);
-    float pr = (ii & 1) ? exp2_fma(e) : ex2f(e);  // odd columns on the FMA pipe
+    float pr = ex2f(e);
     if (MASK) {
       const int col = c0 + ii;
       const bool vis = col < Tk && row_in && (!causal || col <= abs_row);
