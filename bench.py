@@ -285,9 +285,10 @@ def run_native(args, world, rank):
     # learned positions extended to the benchmark context when it is longer
     cfg = gpt2_config(args.model, n_positions=max(args.seq, gpt2_config(args.model).n_positions))
     tc = TrainConfig(lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, grad_clip=1.0, warmup_steps=0)
+    graph = args.graph == "on" and world == 1 and args.strategy == "ddp"
     trainer = Trainer(cfg, args.batch, args.seq, train=tc, comm=args.comm, schedule=False,
                       strategy=args.strategy, bucket_bytes=int(args.bucket_mb * 2**20),
-                      comm_blocks=args.comm_blocks, cp_balance=args.cp_balance)
+                      comm_blocks=args.comm_blocks, cp_balance=args.cp_balance, graph=graph)
     # tensor and context parallel ranks all take the same global batch
     host, dev = make_data(cfg, args.batch, args.seq, 0 if args.strategy in ("tp", "cp") else rank)
     L = N.lib()
@@ -312,6 +313,9 @@ def run_native(args, world, rank):
     ms = timed(dev_step, args.steps, args.warmup, world, start, stop)
     trainer.check()
     n_launch = sum_over_ranks(launches["b"] - launches["a"], world)
+    if graph:
+        # replays launch the captured kernels without passing the launchers
+        n_launch = trainer.graph_launches * args.steps
 
     def e2e_step(i):
         idx, tgt = host[i % len(host)]
@@ -324,6 +328,7 @@ def run_native(args, world, rank):
     out = finish_line(args, world, cfg, ms, ms_e2e, bi, bo, sampler, impl="native")
     out["gpu_launches"] = int(n_launch)
     out["config"]["comm"] = (args.comm if args.strategy == "ddp" else "p2p") if world > 1 else "none"
+    out["config"]["cuda_graph"] = graph
     if args.strategy == "cp":
         out["config"]["cp_balance"] = args.cp_balance
     if args.strategy == "zero3":
@@ -497,6 +502,8 @@ def main():
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--seq", type=int, default=1024)
     ap.add_argument("--comm", choices=["p2p", "mc", "nccl"], default="p2p")
+    ap.add_argument("--graph", choices=["on", "off"], default="off",
+                    help="one rank: replay the step (forward, backward, optimiser) as one CUDA graph")
     ap.add_argument("--strategy", choices=["ddp", "zero2", "zero3", "tp", "cp", "pp"], default="ddp")
     ap.add_argument("--pp", type=int, default=0, help="pipeline stages (pp strategy; default N / cp)")
     ap.add_argument("--cp", type=int, default=1, help="context-parallel ranks per stage (pp strategy)")

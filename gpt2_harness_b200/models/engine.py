@@ -645,6 +645,14 @@ class Engine:
 
     def optimizer_step(self) -> None:
         """Clip (global norm) + AdamW over the whole flat buffer."""
+        self.stage_hyperparams()
+        with nvtx_range("optimizer"):
+            self._optimizer_update()
+
+    def stage_hyperparams(self) -> None:
+        """The host half of a step: advance the step count and copy this
+        step's AdamW scalars (lr, bias corrections, gradient scale) into the
+        device buffer the update kernels read (stream-ordered)."""
         o = self.optim
         self.step_count += 1
         t = self.step_count
@@ -664,8 +672,6 @@ class Engine:
         ev = self._hp_events[slot] or torch.cuda.Event()
         ev.record()
         self._hp_events[slot] = ev
-        with nvtx_range("optimizer"):
-            self._optimizer_update()
 
     def _optimizer_update(self) -> None:
         o = self.optim

@@ -73,7 +73,8 @@ class Trainer:
                  train: Optional[TrainConfig] = None, comm: str = "p2p",
                  device: Optional[torch.device] = None, seed: int = 0,
                  bucket_bytes: int = 25 * 1024 * 1024, schedule: bool = True,
-                 strategy: str = "ddp", comm_blocks: int = 128, cp_balance: str = "zigzag") -> None:
+                 strategy: str = "ddp", comm_blocks: int = 128, cp_balance: str = "zigzag",
+                 graph: bool = False) -> None:
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device())
         self.device = torch.device(device)
@@ -91,6 +92,13 @@ class Trainer:
             raise ValueError(f"unknown strategy {strategy!r}")
         self.strategy = strategy if (self.world > 1 or strategy == "tp") else "single"
         self.cp = None
+        # One CUDA graph for forward + backward + optimiser update (one rank:
+        # no collective carries a per-launch epoch); set below when allowed
+        self.graph = False
+        self._graph: Optional[torch.cuda.CUDAGraph] = None
+        self._graph_loss: Optional[torch.Tensor] = None
+        self._eager_steps = 0
+        self.graph_launches = 0
         if strategy == "tp":
             # tensor + sequence parallelism: every rank takes the same global
             # batch (batch_size x seq_len) and holds 1/p of every block
@@ -157,6 +165,9 @@ class Trainer:
         self.tgt = torch.zeros(batch_size, seq_len, dtype=torch.int64, device=self.device)
         self.step_num = 0
         self.h2d_done = torch.cuda.Event()
+        if graph and self.ddp is not None:
+            raise ValueError("graph=True replays a one-rank step only")
+        self.graph = graph
 
     @property
     def num_parameters(self) -> int:
@@ -190,6 +201,8 @@ class Trainer:
         eng = self.engine
         if self.schedule:
             eng.set_lr(lr_at_step(self.step_num, self.train_cfg))
+        if self.graph:
+            return self._graph_step(idx, targets)
         i, t = self._load_inputs(idx, targets)
         loss = eng.forward(i, t)
         if self.strategy == "tp":
@@ -201,6 +214,40 @@ class Trainer:
         eng.optimizer_step()
         self.step_num += 1
         return loss
+
+    def _graph_step(self, idx: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        """The step as one CUDA graph replay. Outside the graph, on the same
+        stream: the batch is copied into the static input buffers and the
+        step's AdamW scalars into the device buffer the update reads. The
+        first step runs eagerly (kernel attributes are set, workspaces sized),
+        the second is captured, then replayed every step; the kernels and
+        their order are the eager step's, so the results are bit-identical."""
+        eng = self.engine
+        self.idx.copy_(idx, non_blocking=True)
+        self.tgt.copy_(targets, non_blocking=True)
+        self.h2d_done.record()
+        eng.stage_hyperparams()
+        if self._graph is None:
+            if self._eager_steps == 0:
+                self._eager_steps += 1
+                loss = eng.forward(self.idx, self.tgt)
+                eng.backward(self.idx)
+                eng._optimizer_update()
+                self.step_num += 1
+                return loss
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            n0 = N.lib().launch_count()
+            with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                self._graph_loss = eng.forward(self.idx, self.tgt)
+                eng.backward(self.idx)
+                eng._optimizer_update()
+            # native kernels in the graph: each replay launches them all
+            self.graph_launches = N.lib().launch_count() - n0
+            self._graph = g
+        self._graph.replay()
+        self.step_num += 1
+        return self._graph_loss
 
     def step(self, idx: torch.Tensor, targets: torch.Tensor) -> float:
         """One optimiser step; returns this rank's loss as a Python float."""
@@ -236,6 +283,7 @@ class Trainer:
         if self.strategy == "tp":
             self.engine.close()
             return
+        self._graph = None
         if self.cp is not None:
             self.cp.close()
         if self.ddp is not None:

@@ -61,7 +61,7 @@ def test_data_parallel_line(bench_env, capsys, monkeypatch):
     assert out["value"] > 0 and out["higher_is_better"] is True and out["scaling"] == "weak"
     assert out["e2e"]["h2d_bytes_per_step"] == 2 * 64 * 8 and out["e2e"]["d2h_bytes_per_step"] == 4
     assert out["config"]["parallelism"] == "dp1" and out["dtype"] == "bf16"
-    assert out["value"] == pytest.approx(64 / (out["ms_per_step"] / 1e3), rel=1e-3)
+    assert out["value"] == pytest.approx(64 / (out["ms_per_step"] / 1e3), rel=1e-3, abs=0.06)  # value has one decimal
 
 
 def test_pipeline_line(bench_env, capsys, monkeypatch):
