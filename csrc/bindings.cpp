@@ -447,7 +447,7 @@ PYBIND11_MODULE(_C, m) {
   m.def("zero_flag_words", []() { return 2 * kCommMaxRanks * kZeroMaxBlocks; });
   m.def("zero_norm_words", []() { return 2 * kZeroMaxBlocks * kCommMaxRanks; });
   m.def("zero_max_blocks", []() { return kZeroMaxBlocks; });
-  m.def("comm_flag_words", []() { return 2 * kCommMaxRanks * kCommMaxBlocks; });
+  m.def("comm_flag_words", []() { return kCommFlagWords; });
   m.def("flag_wait_test", [](int64_t flag, uint32_t value, int64_t budget_ns, int64_t err,
                              int64_t stream) {
     check(comm_flag_wait_test_launch(P<uint32_t>(flag), value, budget_ns, P<uint32_t>(err),

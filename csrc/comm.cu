@@ -54,21 +54,45 @@ __device__ __forceinline__ uint32_t* flag_slot(uint32_t* base, int phase, int sr
 }
 
 // Arrive/wait handshake of one CTA against the same CTA index on every peer.
-__device__ bool handshake(const CommArgs& a, int phase, int* fail) {
+__device__ bool handshake(const CommArgs& a, uint32_t epoch, int phase, int* fail) {
   const int j = blockIdx.x;
   if (threadIdx.x < a.world) {
     const int q = threadIdx.x;
-    st_release_sys(flag_slot(a.peer_flags[q], phase, a.rank, j), a.epoch);
+    st_release_sys(flag_slot(a.peer_flags[q], phase, a.rank, j), epoch);
   }
   if (threadIdx.x < a.world) {
     const int q = threadIdx.x;
-    if (!wait_flag(flag_slot(a.peer_flags[a.rank], phase, q, j), a.epoch, a.wait_budget_ns)) {
+    if (!wait_flag(flag_slot(a.peer_flags[a.rank], phase, q, j), epoch, a.wait_budget_ns)) {
       *fail = 1;
       report_error(a.err, ERR_TIMEOUT_PEER);
     }
   }
   __syncthreads();
   return *fail == 0;
+}
+
+// The launch's epoch: the caller's, or (epoch 0) this rank's device counter
+// + 1. The counter advances when the launch's last CTA finishes, so the next
+// launch on the stream reads the new value whichever path launched it (a
+// captured graph replays launches with their recorded arguments).
+__device__ __forceinline__ uint32_t* epoch_words(const CommArgs& a) {
+  return a.peer_flags[a.rank] + 2 * kCommMaxRanks * kCommMaxBlocks;
+}
+__device__ __forceinline__ uint32_t launch_epoch(const CommArgs& a) {
+  if (a.epoch) return a.epoch;
+  return *reinterpret_cast<volatile uint32_t*>(epoch_words(a)) + 1;
+}
+// Thread 0 of every CTA, after the CTA's last use of the epoch (also on the
+// error path, so a failed launch cannot leave the next one with its epoch).
+__device__ __forceinline__ void launch_done(const CommArgs& a, uint32_t epoch) {
+  if (a.epoch || threadIdx.x != 0) return;
+  uint32_t* w = epoch_words(a);
+  __threadfence();
+  if (atomicAdd(w + 1, 1u) == gridDim.x - 1) {
+    w[1] = 0;
+    w[0] = epoch;
+    __threadfence();
+  }
 }
 
 template <typename T>
@@ -117,13 +141,9 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
   return __float2bfloat16(x);
 }
 
-template <typename T, int W, int NT>
-__global__ void __launch_bounds__(NT, NT == 128 ? 6 : 1) allreduce_p2p_kernel(const CommArgs a) {
-  __shared__ int fail;
-  if (threadIdx.x == 0) fail = 0;
-  __syncthreads();
-  if (!handshake(a, 0, &fail)) return;
-
+// The data path of one launch (between the arrive and done handshakes).
+template <typename T, int W>
+__device__ __forceinline__ void allreduce_p2p_body(const CommArgs& a) {
   constexpr int VN = Vec<T>::N;
   // Vectorised part: slices of whole 16-byte vectors; the scalar tail (< VN
   // elements per rank boundary) is handled by rank 0's last CTA.
@@ -186,8 +206,23 @@ __global__ void __launch_bounds__(NT, NT == 128 ? 6 : 1) allreduce_p2p_kernel(co
   __syncthreads();
   if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
     atomicAdd(a.byte_counter, (unsigned long long)(a.count >= 0 ? a.count : a.n) * sizeof(T));
-  handshake(a, 1, &fail);
 }
+
+template <typename T, int W, int NT>
+__global__ void __launch_bounds__(NT, NT == 128 ? 6 : 1) allreduce_p2p_kernel(const CommArgs a) {
+  __shared__ int fail;
+  __shared__ uint32_t s_epoch;
+  if (threadIdx.x == 0) {
+    fail = 0;
+    s_epoch = launch_epoch(a);
+  }
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  if (handshake(a, epoch, 0, &fail)) allreduce_p2p_body<T, W>(a);
+  if (!fail) handshake(a, epoch, 1, &fail);
+  launch_done(a, epoch);
+}
+
 
 // ------------------------------------------------------ multimem (NVLS) --
 __device__ __forceinline__ uint4 mc_ld_reduce(const uint4* p, float) {
@@ -219,12 +254,7 @@ __device__ __forceinline__ void mc_st(uint4* p, const uint4& v, __nv_bfloat16) {
 }
 
 template <typename T, int NT>
-__global__ void __launch_bounds__(NT, 1) allreduce_mc_kernel(const CommArgs a) {
-  __shared__ int fail;
-  if (threadIdx.x == 0) fail = 0;
-  __syncthreads();
-  if (!handshake(a, 0, &fail)) return;
-
+__device__ __forceinline__ void allreduce_mc_body(const CommArgs& a) {
   constexpr int VN = Vec<T>::N;
   const T tag{};
   const int64_t nvec = a.n / VN;  // the launch requires n % VN == 0
@@ -262,7 +292,21 @@ __global__ void __launch_bounds__(NT, 1) allreduce_mc_kernel(const CommArgs a) {
   __syncthreads();
   if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
     atomicAdd(a.byte_counter, (unsigned long long)(a.count >= 0 ? a.count : a.n) * sizeof(T));
-  handshake(a, 1, &fail);
+}
+
+template <typename T, int NT>
+__global__ void __launch_bounds__(NT, 1) allreduce_mc_kernel(const CommArgs a) {
+  __shared__ int fail;
+  __shared__ uint32_t s_epoch;
+  if (threadIdx.x == 0) {
+    fail = 0;
+    s_epoch = launch_epoch(a);
+  }
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  if (handshake(a, epoch, 0, &fail)) allreduce_mc_body<T, NT>(a);
+  if (!fail) handshake(a, epoch, 1, &fail);
+  launch_done(a, epoch);
 }
 
 template <typename T, int NT>

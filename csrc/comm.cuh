@@ -8,6 +8,10 @@ namespace g2b {
 
 constexpr int kCommMaxBlocks = 160;  // flag slots per (phase, rank)
 constexpr int kCommMaxRanks = 8;
+// A rank's flag buffer: [2][kCommMaxRanks][kCommMaxBlocks] handshake words,
+// then the device epoch counter and the launch's finished-CTA count (used
+// when a launch passes epoch 0).
+constexpr int kCommFlagWords = 2 * kCommMaxRanks * kCommMaxBlocks + 2;
 
 // One fused all-reduce over NVLink peer memory. Every rank owns a symmetric
 // buffer (same size, same element offsets on every rank); peer_bufs[q] is rank
@@ -22,7 +26,10 @@ struct CommArgs {
   int64_t offset = 0, n = 0;        // elements
   int dtype = 0;                    // 0 = fp32 buffer, 1 = bf16 buffer
   float scale = 1.f;
-  uint32_t epoch = 0;               // strictly increasing per call, same on all ranks
+  // strictly increasing per call, same on all ranks; 0 = take it from the
+  // device counter in this rank's flag buffer (previous launch's + 1), so a
+  // captured CUDA graph replays with fresh epochs
+  uint32_t epoch = 0;
   unsigned long long* byte_counter = nullptr;  // payload bytes (reference convention)
   uint32_t* err = nullptr;
   int nblocks = 32;

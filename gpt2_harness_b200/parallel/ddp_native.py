@@ -174,19 +174,19 @@ class NativeDDP:
         self.stream.wait_event(ev)
         comms.record_external("all_reduce", b.numel, b.numel * 4)
         with torch.cuda.stream(self.stream), nvtx_range(f"allreduce/bucket{self.buckets.index(b)}"):
+            # epoch 0: each launch takes its epoch from the device counter in
+            # this rank's flag buffer, so a captured step replays correctly
             if self.comm == "mc":
-                self.epoch += 1
                 N.lib().allreduce_mc(self.symm.peer_ptrs_dev.data_ptr(), self.flags.peer_ptrs_dev.data_ptr(),
                                      self.symm.mc_ptr, self.rank, self.world, b.lo, b.hi - b.lo, 0,
-                                     1.0 / self.world, self.epoch & 0xFFFFFFFF, self.byte_counter.data_ptr(),
+                                     1.0 / self.world, 0, self.byte_counter.data_ptr(),
                                      N.error_word().data_ptr(), self.tail_blocks if last else self.nblocks,
                                      2_000_000_000, b.numel, self.stream.cuda_stream)
             elif self.comm == "p2p":
-                self.epoch += 1
                 fn = N.lib().allreduce_p2p_slim if slim else N.lib().allreduce_p2p
                 fn(self.symm.peer_ptrs_dev.data_ptr(), self.flags.peer_ptrs_dev.data_ptr(),
                    self.rank, self.world, b.lo, b.hi - b.lo, 0, 1.0 / self.world,
-                   self.epoch & 0xFFFFFFFF, self.byte_counter.data_ptr(), N.error_word().data_ptr(),
+                   0, self.byte_counter.data_ptr(), N.error_word().data_ptr(),
                    self.nblocks if slim else self.tail_blocks, 2_000_000_000, b.numel,
                    self.stream.cuda_stream)
             else:

@@ -92,8 +92,9 @@ class Trainer:
             raise ValueError(f"unknown strategy {strategy!r}")
         self.strategy = strategy if (self.world > 1 or strategy == "tp") else "single"
         self.cp = None
-        # One CUDA graph for forward + backward + optimiser update (one rank:
-        # no collective carries a per-launch epoch); set below when allowed
+        # One CUDA graph for forward + backward (+ the DDP bucket all-reduces,
+        # whose epochs come from a device counter) + optimiser update; set
+        # below when allowed
         self.graph = False
         self._graph: Optional[torch.cuda.CUDAGraph] = None
         self._graph_loss: Optional[torch.Tensor] = None
@@ -165,8 +166,9 @@ class Trainer:
         self.tgt = torch.zeros(batch_size, seq_len, dtype=torch.int64, device=self.device)
         self.step_num = 0
         self.h2d_done = torch.cuda.Event()
-        if graph and self.ddp is not None:
-            raise ValueError("graph=True replays a one-rank step only")
+        if graph and self.ddp is not None and not (
+                self.strategy == "ddp" and getattr(self.ddp, "comm", None) in ("p2p", "mc")):
+            raise ValueError("graph=True replays one-rank and native-DDP steps only")
         self.graph = graph
 
     @property
@@ -216,12 +218,13 @@ class Trainer:
         return loss
 
     def _graph_step(self, idx: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
-        """The step as one CUDA graph replay. Outside the graph, on the same
-        stream: the batch is copied into the static input buffers and the
-        step's AdamW scalars into the device buffer the update reads. The
-        first step runs eagerly (kernel attributes are set, workspaces sized),
-        the second is captured, then replayed every step; the kernels and
-        their order are the eager step's, so the results are bit-identical."""
+        """The step as one CUDA graph replay (one rank, or native DDP).
+        Outside the graph, on the same stream: the batch is copied into the
+        static input buffers and the step's AdamW scalars into the device
+        buffer the update reads. The first step runs eagerly (kernel
+        attributes are set, workspaces sized), the second is captured, then
+        replayed every step; the kernels and their order are the eager
+        step's, so the results are bit-identical."""
         eng = self.engine
         self.idx.copy_(idx, non_blocking=True)
         self.tgt.copy_(targets, non_blocking=True)
@@ -232,6 +235,8 @@ class Trainer:
                 self._eager_steps += 1
                 loss = eng.forward(self.idx, self.tgt)
                 eng.backward(self.idx)
+                if self.ddp is not None:
+                    self.ddp.finish()
                 eng._optimizer_update()
                 self.step_num += 1
                 return loss
@@ -240,7 +245,9 @@ class Trainer:
             n0 = N.lib().launch_count()
             with torch.cuda.graph(g, capture_error_mode="thread_local"):
                 self._graph_loss = eng.forward(self.idx, self.tgt)
-                eng.backward(self.idx)
+                eng.backward(self.idx)  # DDP buckets fork onto the comm stream
+                if self.ddp is not None:
+                    self.ddp.finish()   # ... and join back before the update
                 eng._optimizer_update()
             # native kernels in the graph: each replay launches them all
             self.graph_launches = N.lib().launch_count() - n0

@@ -116,3 +116,68 @@ def test_native_ddp_two_gpus(comm, world):
 def _multicast() -> bool:
     from gpt2_harness_b200.parallel.symm import multicast_supported
     return torch.cuda.device_count() > 1 and multicast_supported(torch.device("cuda", 0))
+
+
+GRAPH_WORKER = textwrap.dedent(r'''
+    import os, sys, json, datetime
+    import torch, torch.distributed as dist
+    sys.path.insert(0, os.environ["G2B_ROOT"])
+    from gpt2_harness_b200.config import gpt2_config, TrainConfig
+    from gpt2_harness_b200.trainer import Trainer
+
+    rank = int(os.environ["RANK"]); world = int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    cfg = gpt2_config("gpt2", n_layer=2, n_positions=256)
+    tc = TrainConfig(lr=1e-3, warmup_steps=0)
+    out = {"rank": rank}
+    for graph in (False, True):
+        tr = Trainer(cfg, 2, 256, train=tc, schedule=False, seed=0, comm=os.environ["G2B_COMM"],
+                     bucket_bytes=4 * 1024 * 1024, graph=graph)
+        losses = []
+        for step in range(5):
+            g = torch.Generator().manual_seed(100 * step + rank)
+            idx = torch.randint(0, cfg.vocab_size, (2, 256), generator=g).pin_memory()
+            tgt = torch.randint(0, cfg.vocab_size, (2, 256), generator=g).pin_memory()
+            losses.append(tr.step(idx, tgt))
+        tr.check()
+        out["graph" if graph else "eager"] = losses
+        out["master_" + ("graph" if graph else "eager")] = float(tr.engine.master.double().sum().item())
+        out["launches"] = tr.graph_launches
+        tr.close()
+    print("RESULT " + json.dumps(out), flush=True)
+    dist.destroy_process_group()
+''')
+
+
+@pytest.mark.parametrize("comm", ["p2p", "mc"])
+def test_ddp_graph_replay_matches_eager(comm):
+    """The DDP step captured as one CUDA graph (bucket all-reduces on the comm
+    stream, device-side epochs) replays the eager step exactly on 2 ranks."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    if comm == "mc" and not _multicast():
+        pytest.skip("no NVLink multicast on this system")
+    import json
+    port = _free_port()
+    procs = []
+    for r in range(2):
+        env = dict(os.environ, RANK=str(r), WORLD_SIZE="2", LOCAL_RANK=str(r), MASTER_ADDR="127.0.0.1",
+                   MASTER_PORT=str(port), G2B_ROOT=ROOT, G2B_COMM=comm)
+        if comm != "mc":
+            env["NCCL_NVLS_ENABLE"] = "0"
+        procs.append(subprocess.Popen([sys.executable, "-c", GRAPH_WORKER], env=env,
+                                      stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True))
+    for p in procs:
+        out, _ = p.communicate(timeout=300)
+        assert p.returncode == 0, out[-3000:]
+        line = [l for l in out.splitlines() if l.startswith("RESULT ")]
+        assert line, out[-3000:]
+        r = json.loads(line[-1][7:])
+        if comm == "p2p":  # fixed-order sums: bit-identical
+            assert r["graph"] == r["eager"], r
+            assert r["master_graph"] == r["master_eager"], r
+        else:              # the switch's summation order is its own
+            assert all(abs(a - b) <= 1e-5 * abs(b) for a, b in zip(r["graph"], r["eager"])), r
+        assert r["launches"] > 0, r
