@@ -285,7 +285,8 @@ def run_native(args, world, rank):
     # learned positions extended to the benchmark context when it is longer
     cfg = gpt2_config(args.model, n_positions=max(args.seq, gpt2_config(args.model).n_positions))
     tc = TrainConfig(lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, grad_clip=1.0, warmup_steps=0)
-    graph = args.graph == "on" and args.strategy == "ddp" and (world == 1 or args.comm != "nccl")
+    graph = (args.graph == "on" and args.strategy == "ddp" and (world == 1 or args.comm != "nccl")
+             and torch.cuda.is_available())
     trainer = Trainer(cfg, args.batch, args.seq, train=tc, comm=args.comm, schedule=False,
                       strategy=args.strategy, bucket_bytes=int(args.bucket_mb * 2**20),
                       comm_blocks=args.comm_blocks, cp_balance=args.cp_balance, graph=graph)
@@ -315,7 +316,7 @@ def run_native(args, world, rank):
     n_launch = sum_over_ranks(launches["b"] - launches["a"], world)
     if graph:
         # replays launch the captured kernels without passing the launchers
-        n_launch = trainer.graph_launches * args.steps
+        n_launch = sum_over_ranks(trainer.graph_launches * args.steps, world)
 
     def e2e_step(i):
         idx, tgt = host[i % len(host)]
@@ -502,7 +503,7 @@ def main():
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--seq", type=int, default=1024)
     ap.add_argument("--comm", choices=["p2p", "mc", "nccl"], default="p2p")
-    ap.add_argument("--graph", choices=["on", "off"], default="off",
+    ap.add_argument("--graph", choices=["on", "off"], default="on",
                     help="DDP: replay the step (forward, backward, bucket all-reduces, optimiser) "
                          "as one CUDA graph")
     ap.add_argument("--strategy", choices=["ddp", "zero2", "zero3", "tp", "cp", "pp"], default="ddp")
