@@ -169,6 +169,9 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 __device__ __forceinline__ void bulk_wait_read0() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
+__device__ __forceinline__ void bulk_wait_read1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -525,6 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lane = (int)lane_id();
     const int r_local = lg * 32 + lane;   // row within the tile
     constexpr int CHUNKS = BN / 64;       // 32-column chunks per warp
+    constexpr bool kDblBox = !F32_OUT && EPI != EPI_BIAS_GELU;  // two bf16 boxes per warp
     uint8_t* box = smem + Cfg::EPI_OFFSET + ew * kStageBuf;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -572,19 +576,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         epi_math<EPI>(p, c0 + c * 32, v, in, z);
         if (EPI == EPI_CE_STATS) ce_chunk(p, row, c0 + c * 32, v, ce);
         if (TMA_ST && !peer_tile) {
-          // the previous chunk's bulk store must have finished reading the box
-          if (lane == 0) bulk_wait_read0();
+          // A bf16 box (2 KB) is half the warp's staging buffer: alternate
+          // halves, so only the store of two chunks ago must have finished
+          // reading its box; an fp32 box (or GELU's output + input pair)
+          // fills it and waits for the previous chunk's store.
+          uint8_t* bx = kDblBox ? box + (c & 1) * 2048 : box;
+          if (lane == 0) {
+            if (kDblBox) bulk_wait_read1();
+            else bulk_wait_read0();
+          }
           __syncwarp();
           if (F32_OUT) {
-            stage_f32(box, lane, v);
+            stage_f32(bx, lane, v);
           } else {
-            stage_bf16(box, lane, v);
+            stage_bf16(bx, lane, v);
             if (EPI == EPI_BIAS_GELU) stage_bf16(box + 2048, lane, z);
           }
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_3d(&tmO, box, c0 + c * 32, m0 + lg * 32, split);
+            tma_store_3d(&tmO, bx, c0 + c * 32, m0 + lg * 32, split);
             if (EPI == EPI_BIAS_GELU) tma_store_3d(&tmX, box + 2048, c0 + c * 32, m0 + lg * 32, 0);
             bulk_commit();
           }
@@ -858,6 +869,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int lane = (int)lane_id();
     const int r_local = lg * 32 + lane;
     constexpr int CHUNKS = BN / 64;
+    constexpr bool kDblBox = !F32_OUT && EPI != EPI_BIAS_GELU;
     uint8_t* box = smem + Cfg::EPI_OFFSET + ew * kStageBuf;
     const uint32_t lead_tempty0 = cluster_addr(&tempty_bar[0], 0);
     const uint32_t lead_tq_empty0 = cluster_addr(&tq_empty[0], 0);
@@ -912,18 +924,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         epi_math<EPI>(p, c0 + c * 32, v, in, z);
         if (EPI == EPI_CE_STATS) ce_chunk(p, row, c0 + c * 32, v, ce);
         if (TMA_ST && !peer_tile) {
-          if (lane == 0) bulk_wait_read0();
+          uint8_t* bx = kDblBox ? box + (c & 1) * 2048 : box;  // as in the single-CTA kernel
+          if (lane == 0) {
+            if (kDblBox) bulk_wait_read1();
+            else bulk_wait_read0();
+          }
           __syncwarp();
           if (F32_OUT) {
-            stage_f32(box, lane, v);
+            stage_f32(bx, lane, v);
           } else {
-            stage_bf16(box, lane, v);
+            stage_bf16(bx, lane, v);
             if (EPI == EPI_BIAS_GELU) stage_bf16(box + 2048, lane, z);
           }
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_3d(&tmO, box, c0 + c * 32, m0 + lg * 32, split);
+            tma_store_3d(&tmO, bx, c0 + c * 32, m0 + lg * 32, split);
             if (EPI == EPI_BIAS_GELU) tma_store_3d(&tmX, box + 2048, c0 + c * 32, m0 + lg * 32, 0);
             bulk_commit();
           }
@@ -1172,6 +1188,9 @@ bool use_pairs(const GemmArgs& a) {
   // released only when both CTAs' epilogues have drained it.
   if (a.epilogue == EPI_BIAS_GELU || a.epilogue == EPI_GELU_BWD) return false;
   if (a.epilogue == EPI_BF16 && !a.b_mn_major && a.N < 8192) return false;
+  // Short, narrow GEMMs (attn c_proj forward and data gradient: K = N = 768)
+  // lose on pairs: 0.0489 vs 0.0442 ms and 0.0284 vs 0.0251 ms.
+  if (a.K <= 1024 && a.N < 8192 && a.splits <= 1) return false;
   return kPairDefault;
 }
 
