@@ -143,7 +143,6 @@ class NativeDDP:
         prio = int(os.environ.get("G2B_COMM_PRIORITY", "-1"))
         self.stream = (torch.cuda.Stream(device=self.device, priority=prio)
                        if self.world > 1 else None)
-        self.epoch = 0
         self.byte_counter = torch.zeros(1, dtype=torch.int64, device=self.device)
         self._next = 0
         self.engine = None
