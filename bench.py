@@ -285,8 +285,11 @@ def run_native(args, world, rank):
     # learned positions extended to the benchmark context when it is longer
     cfg = gpt2_config(args.model, n_positions=max(args.seq, gpt2_config(args.model).n_positions))
     tc = TrainConfig(lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, grad_clip=1.0, warmup_steps=0)
-    graph = (args.graph == "on" and args.strategy == "ddp" and (world == 1 or args.comm != "nccl")
-             and torch.cuda.is_available())
+    # default: one rank replays its step as a CUDA graph; several ranks only
+    # with --graph on (measured at 2 ranks; at 8 its one run stalled)
+    graph = (args.strategy == "ddp" and torch.cuda.is_available()
+             and (args.graph == "on" or (args.graph == "auto" and world == 1))
+             and (world == 1 or args.comm != "nccl"))
     trainer = Trainer(cfg, args.batch, args.seq, train=tc, comm=args.comm, schedule=False,
                       strategy=args.strategy, bucket_bytes=int(args.bucket_mb * 2**20),
                       comm_blocks=args.comm_blocks, cp_balance=args.cp_balance, graph=graph)
@@ -503,9 +506,9 @@ def main():
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--seq", type=int, default=1024)
     ap.add_argument("--comm", choices=["p2p", "mc", "nccl"], default="p2p")
-    ap.add_argument("--graph", choices=["on", "off"], default="on",
+    ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",
                     help="DDP: replay the step (forward, backward, bucket all-reduces, optimiser) "
-                         "as one CUDA graph")
+                         "as one CUDA graph; auto = one rank only")
     ap.add_argument("--strategy", choices=["ddp", "zero2", "zero3", "tp", "cp", "pp"], default="ddp")
     ap.add_argument("--pp", type=int, default=0, help="pipeline stages (pp strategy; default N / cp)")
     ap.add_argument("--cp", type=int, default=1, help="context-parallel ranks per stage (pp strategy)")

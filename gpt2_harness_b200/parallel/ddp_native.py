@@ -144,6 +144,12 @@ class NativeDDP:
         self.stream = (torch.cuda.Stream(device=self.device, priority=prio)
                        if self.world > 1 else None)
         self.byte_counter = torch.zeros(1, dtype=torch.int64, device=self.device)
+        # Handshake epochs: host-side, strictly increasing (eager steps), or
+        # -- set before the first launch for a captured CUDA graph, whose
+        # replays repeat their recorded arguments -- read by each launch from
+        # a device counter in this rank's flag buffer (epoch argument 0).
+        self.device_epochs = False
+        self.epoch = 0
         self._next = 0
         self.engine = None
 
@@ -173,19 +179,22 @@ class NativeDDP:
         self.stream.wait_event(ev)
         comms.record_external("all_reduce", b.numel, b.numel * 4)
         with torch.cuda.stream(self.stream), nvtx_range(f"allreduce/bucket{self.buckets.index(b)}"):
-            # epoch 0: each launch takes its epoch from the device counter in
-            # this rank's flag buffer, so a captured step replays correctly
+            if self.device_epochs:
+                epoch = 0
+            else:
+                self.epoch += 1
+                epoch = self.epoch & 0xFFFFFFFF
             if self.comm == "mc":
                 N.lib().allreduce_mc(self.symm.peer_ptrs_dev.data_ptr(), self.flags.peer_ptrs_dev.data_ptr(),
                                      self.symm.mc_ptr, self.rank, self.world, b.lo, b.hi - b.lo, 0,
-                                     1.0 / self.world, 0, self.byte_counter.data_ptr(),
+                                     1.0 / self.world, epoch, self.byte_counter.data_ptr(),
                                      N.error_word().data_ptr(), self.tail_blocks if last else self.nblocks,
                                      2_000_000_000, b.numel, self.stream.cuda_stream)
             elif self.comm == "p2p":
                 fn = N.lib().allreduce_p2p_slim if slim else N.lib().allreduce_p2p
                 fn(self.symm.peer_ptrs_dev.data_ptr(), self.flags.peer_ptrs_dev.data_ptr(),
                    self.rank, self.world, b.lo, b.hi - b.lo, 0, 1.0 / self.world,
-                   0, self.byte_counter.data_ptr(), N.error_word().data_ptr(),
+                   epoch, self.byte_counter.data_ptr(), N.error_word().data_ptr(),
                    self.nblocks if slim else self.tail_blocks, 2_000_000_000, b.numel,
                    self.stream.cuda_stream)
             else:

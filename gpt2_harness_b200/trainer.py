@@ -169,6 +169,8 @@ class Trainer:
         if graph and self.ddp is not None and not (
                 self.strategy == "ddp" and getattr(self.ddp, "comm", None) in ("p2p", "mc")):
             raise ValueError("graph=True replays one-rank and native-DDP steps only")
+        if graph and self.ddp is not None:
+            self.ddp.device_epochs = True  # before any launch
         self.graph = graph
 
     @property
