@@ -242,7 +242,13 @@ class Trainer:
                 eng._optimizer_update()
                 self.step_num += 1
                 return loss
+            # Ranks capture at different speeds (host work: launch encoding,
+            # graph instantiation); a rank that starts replaying more than a
+            # handshake's wait budget before a peer would time out its bucket
+            # all-reduces and leave them out of step. Align before and after.
             torch.cuda.synchronize(self.device)
+            if self.ddp is not None:
+                dist.barrier(device_ids=[self.device.index])
             g = torch.cuda.CUDAGraph()
             n0 = N.lib().launch_count()
             with torch.cuda.graph(g, capture_error_mode="thread_local"):
@@ -253,6 +259,8 @@ class Trainer:
                 eng._optimizer_update()
             # native kernels in the graph: each replay launches them all
             self.graph_launches = N.lib().launch_count() - n0
+            if self.ddp is not None:
+                dist.barrier(device_ids=[self.device.index])
             self._graph = g
         self._graph.replay()
         self.step_num += 1
