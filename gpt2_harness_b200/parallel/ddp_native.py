@@ -103,7 +103,8 @@ class NativeDDP:
 
     def __init__(self, layout: ParamLayout, group=None, comm: str = "p2p",
                  bucket_bytes: int = DEFAULT_BUCKET_BYTES, nblocks: int = 128,
-                 device: Optional[torch.device] = None, tail_blocks: int = 128) -> None:
+                 device: Optional[torch.device] = None, tail_blocks: int = 128,
+                 wait_budget_s: float = 30.0) -> None:
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -150,6 +151,10 @@ class NativeDDP:
         # a device counter in this rank's flag buffer (epoch argument 0).
         self.device_epochs = False
         self.epoch = 0
+        # How long a bucket kernel waits for a peer before it records a
+        # timeout and gives up (a rank held up by host work -- a checkpoint
+        # write, a collection pause -- must not trip it)
+        self.wait_budget_ns = int(wait_budget_s * 1e9)
         self._next = 0
         self.engine = None
 
@@ -189,13 +194,13 @@ class NativeDDP:
                                      self.symm.mc_ptr, self.rank, self.world, b.lo, b.hi - b.lo, 0,
                                      1.0 / self.world, epoch, self.byte_counter.data_ptr(),
                                      N.error_word().data_ptr(), self.tail_blocks if last else self.nblocks,
-                                     2_000_000_000, b.numel, self.stream.cuda_stream)
+                                     self.wait_budget_ns, b.numel, self.stream.cuda_stream)
             elif self.comm == "p2p":
                 fn = N.lib().allreduce_p2p_slim if slim else N.lib().allreduce_p2p
                 fn(self.symm.peer_ptrs_dev.data_ptr(), self.flags.peer_ptrs_dev.data_ptr(),
                    self.rank, self.world, b.lo, b.hi - b.lo, 0, 1.0 / self.world,
                    epoch, self.byte_counter.data_ptr(), N.error_word().data_ptr(),
-                   self.nblocks if slim else self.tail_blocks, 2_000_000_000, b.numel,
+                   self.nblocks if slim else self.tail_blocks, self.wait_budget_ns, b.numel,
                    self.stream.cuda_stream)
             else:
                 dist.all_reduce(self.grad_buffer[b.lo:b.hi], group=self.group)
