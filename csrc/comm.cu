@@ -62,9 +62,21 @@ __device__ bool handshake(const CommArgs& a, uint32_t epoch, int phase, int* fai
   }
   if (threadIdx.x < a.world) {
     const int q = threadIdx.x;
-    if (!wait_flag(flag_slot(a.peer_flags[a.rank], phase, q, j), epoch, a.wait_budget_ns)) {
+    const uint32_t* f = flag_slot(a.peer_flags[a.rank], phase, q, j);
+    if (!wait_flag(f, epoch, a.wait_budget_ns)) {
       *fail = 1;
       report_error(a.err, ERR_TIMEOUT_PEER);
+      // the first give-up on this rank, for the host to read back
+      uint32_t* rec = a.peer_flags[a.rank] + kCommTimeoutWord;
+      if (atomicCAS(rec, 0u, 1u) == 0u) {
+        rec[1] = (uint32_t)phase;
+        rec[2] = (uint32_t)j;
+        rec[3] = (uint32_t)q;
+        rec[4] = epoch;
+        rec[5] = ld_acquire_sys(f);
+        rec[6] = (uint32_t)a.rank;
+        __threadfence_system();
+      }
     }
   }
   __syncthreads();
@@ -76,7 +88,7 @@ __device__ bool handshake(const CommArgs& a, uint32_t epoch, int phase, int* fai
 // launch on the stream reads the new value whichever path launched it (a
 // captured graph replays launches with their recorded arguments).
 __device__ __forceinline__ uint32_t* epoch_words(const CommArgs& a) {
-  return a.peer_flags[a.rank] + 2 * kCommMaxRanks * kCommMaxBlocks;
+  return a.peer_flags[a.rank] + kCommEpochWord;
 }
 __device__ __forceinline__ uint32_t launch_epoch(const CommArgs& a) {
   if (a.epoch) return a.epoch;

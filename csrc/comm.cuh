@@ -10,8 +10,12 @@ constexpr int kCommMaxBlocks = 160;  // flag slots per (phase, rank)
 constexpr int kCommMaxRanks = 8;
 // A rank's flag buffer: [2][kCommMaxRanks][kCommMaxBlocks] handshake words,
 // then the device epoch counter and the launch's finished-CTA count (used
-// when a launch passes epoch 0).
-constexpr int kCommFlagWords = 2 * kCommMaxRanks * kCommMaxBlocks + 2;
+// when a launch passes epoch 0), then the record of the first handshake that
+// gave up on this rank: {recorded, phase, CTA, peer, epoch waited for, flag
+// value seen, this rank, 0}.
+constexpr int kCommEpochWord = 2 * kCommMaxRanks * kCommMaxBlocks;
+constexpr int kCommTimeoutWord = kCommEpochWord + 2;
+constexpr int kCommFlagWords = kCommTimeoutWord + 8;
 
 // One fused all-reduce over NVLink peer memory. Every rank owns a symmetric
 // buffer (same size, same element offsets on every rank); peer_bufs[q] is rank

@@ -205,6 +205,19 @@ class NativeDDP:
             else:
                 dist.all_reduce(self.grad_buffer[b.lo:b.hi], group=self.group)
 
+    def timeout_record(self) -> Optional[dict]:
+        """Where this rank's first bucket handshake gave up (synchronises), or
+        None: the phase (0 arrive, 1 done), CTA, peer, the epoch it waited for
+        and the flag value it last saw."""
+        if self.flags is None:
+            return None
+        words = N.lib().comm_flag_words()
+        rec = [int(x) for x in self.flags.view(torch.int32, words)[words - 8:words - 1].cpu()]
+        if not rec[0]:
+            return None
+        return {"phase": rec[1], "cta": rec[2], "peer": rec[3], "epoch": rec[4] & 0xFFFFFFFF,
+                "flag_seen": rec[5] & 0xFFFFFFFF, "rank": rec[6]}
+
     def finish(self) -> None:
         """Make the compute stream wait for every launched bucket."""
         if self.comm == "none":

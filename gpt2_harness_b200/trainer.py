@@ -271,8 +271,15 @@ class Trainer:
         return float(self.step_async(idx, targets).item())
 
     def check(self) -> None:
-        """Raise if any native kernel recorded an error (synchronises)."""
-        N.check_errors(self.device)
+        """Raise if any native kernel recorded an error (synchronises); a
+        DDP handshake timeout names the first bucket wait that gave up."""
+        try:
+            N.check_errors(self.device)
+        except RuntimeError as e:
+            rec = self.ddp.timeout_record() if hasattr(self.ddp, "timeout_record") else None
+            if rec:
+                raise RuntimeError(f"{e}; first all-reduce handshake that gave up: {rec}") from e
+            raise
 
     def state_dict(self) -> dict:
         """Model (reference names, fp32), step counters and optimiser state.

@@ -202,7 +202,14 @@ def _ddp_worker(rank, world, bucket_mb, small=False, comm="p2p"):
     ref.backward(idx)
     errs = {s.name: float((eng.g32(s.name) - ref.g32(s.name)).norm() / (ref.g32(s.name).norm() + 1e-12))
             for s in ref.layout.specs}
+    # the handshake timeout record: none after a clean step; the host reads
+    # back what a kernel that gave up wrote (last 8 words of the flag buffer)
+    clean = tr.ddp.timeout_record()
+    words = tr.ddp.flags.view(torch.int32, 16)
+    words[8:15] = torch.tensor([1, 1, 5, (rank + 1) % world, 42, 41, rank], dtype=torch.int32)
+    rec = tr.ddp.timeout_record()
     return {"loss": float(loss) / world, "ref_loss": ref_loss, "worst": max(errs.values()),
+            "timeout_clean": clean, "timeout_rec": rec, "rank": rank,
             "worst_name": max(errs, key=errs.get),
             "payload": payload, "device_bytes": int(tr.ddp.byte_counter.item()),
             "buckets": len(tr.ddp.buckets), "grad_bytes": eng.layout.total * 4}
@@ -222,6 +229,9 @@ def test_native_ddp_matches_full_batch(world, bucket_mb, small, comm):
         assert r["worst"] < 5e-3, r
         # every gradient byte is reduced exactly once per step, in both counters
         assert r["payload"] == r["device_bytes"] == r["grad_bytes"], r
+        assert r["timeout_clean"] is None, r
+        assert r["timeout_rec"] == {"phase": 1, "cta": 5, "peer": (r["rank"] + 1) % world,
+                                    "epoch": 42, "flag_seen": 41, "rank": r["rank"]}, r
     if bucket_mb < 1:
         assert res[0].value["buckets"] > 1
 
