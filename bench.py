@@ -292,7 +292,8 @@ def run_native(args, world, rank):
              and (world == 1 or args.comm != "nccl"))
     trainer = Trainer(cfg, args.batch, args.seq, train=tc, comm=args.comm, schedule=False,
                       strategy=args.strategy, bucket_bytes=int(args.bucket_mb * 2**20),
-                      comm_blocks=args.comm_blocks, cp_balance=args.cp_balance, graph=graph)
+                      comm_blocks=args.comm_blocks, cp_balance=args.cp_balance, graph=graph,
+                      reduce_dtype=args.reduce_dtype)
     # tensor and context parallel ranks all take the same global batch
     host, dev = make_data(cfg, args.batch, args.seq, 0 if args.strategy in ("tp", "cp") else rank)
     L = N.lib()
@@ -337,6 +338,7 @@ def run_native(args, world, rank):
         out["config"]["cp_balance"] = args.cp_balance
     if args.strategy == "zero3":
         out["config"]["activations"] = "kept (no recompute): MFU counts the model FLOPs run"
+        out["config"]["reduce_dtype"] = args.reduce_dtype
     trainer.close()
     return out
 
@@ -510,6 +512,8 @@ def main():
                     help="DDP: replay the step (forward, backward, bucket all-reduces, optimiser) "
                          "as one CUDA graph; auto = one rank only")
     ap.add_argument("--strategy", choices=["ddp", "zero2", "zero3", "tp", "cp", "pp"], default="ddp")
+    ap.add_argument("--reduce-dtype", choices=["fp32", "bf16"], default="fp32",
+                    help="ZeRO-3 gradient reduce-scatter / root all-reduce wire")
     ap.add_argument("--pp", type=int, default=0, help="pipeline stages (pp strategy; default N / cp)")
     ap.add_argument("--cp", type=int, default=1, help="context-parallel ranks per stage (pp strategy)")
     ap.add_argument("--micro-batches", type=int, default=8, help="micro-batches per step (pp strategy)")

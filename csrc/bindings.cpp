@@ -337,6 +337,7 @@ PYBIND11_MODULE(_C, m) {
     auto I = [&](const char* k) { return d[k].cast<int64_t>(); };
     ZeroArgs z;
     z.peer_grad = P<float*>(I("peer_grad"));
+    z.peer_grad16 = P<__nv_bfloat16*>(d.contains("peer_grad16") ? I("peer_grad16") : 0);
     z.peer_shadow = P<__nv_bfloat16*>(I("peer_shadow"));
     z.peer_flags = P<uint32_t*>(I("peer_flags"));
     z.peer_norm = P<unsigned long long*>(I("peer_norm"));

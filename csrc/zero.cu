@@ -113,6 +113,19 @@ __device__ __forceinline__ Slice my_slice(const ZeroArgs& a, int b) {
 // to a resident persistent GEMM or attention CTA.
 constexpr int kZeroThreads = 128;
 
+// Four gradient elements of rank q at vector v of the slice: fp32, or (BF16)
+// the rank's bf16 copy.
+template <bool BF16>
+__device__ __forceinline__ float4 rs_load(const ZeroArgs& a, int q, int64_t f0, int64_t v) {
+  if (BF16) {
+    const uint2 w = __ldcg(reinterpret_cast<const uint2*>(a.peer_grad16[q] + f0) + v);
+    const float2 lo = unpack_bf16x2(w.x), hi = unpack_bf16x2(w.y);
+    return make_float4(lo.x, lo.y, hi.x, hi.y);
+  }
+  return __ldcg(reinterpret_cast<const float4*>(a.peer_grad[q] + f0) + v);
+}
+
+template <bool BF16>
 __global__ void __launch_bounds__(kZeroThreads, 6) zero_rs_kernel(const ZeroArgs a) {
   __shared__ int fail;
   __shared__ float red[16];
@@ -129,7 +142,7 @@ __global__ void __launch_bounds__(kZeroThreads, 6) zero_rs_kernel(const ZeroArgs
     float4 w[kCommMaxRanks];
 #pragma unroll
     for (int q = 0; q < kCommMaxRanks; ++q)
-      if (q < a.world) w[q] = __ldcg(reinterpret_cast<const float4*>(a.peer_grad[q] + sl.f0) + v);
+      if (q < a.world) w[q] = rs_load<BF16>(a, q, sl.f0, v);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int q = 0; q < kCommMaxRanks; ++q) {
@@ -151,7 +164,7 @@ __global__ void __launch_bounds__(kZeroThreads, 6) zero_rs_kernel(const ZeroArgs
     a.sumsq_parts[(int64_t)a.bucket * a.rs_blocks + blockIdx.x] = t;
   if (blockIdx.x == 0 && threadIdx.x == 0 && a.byte_counter)
     atomicAdd(a.byte_counter, (unsigned long long)(a.buckets[4 * a.bucket + 1] -
-                                                   a.buckets[4 * a.bucket]) * 4ull);
+                                                   a.buckets[4 * a.bucket]) * (BF16 ? 2ull : 4ull));
   if (a.done_handshake) {
     __syncthreads();
     zero_handshake(a, 1, &fail);
@@ -307,7 +320,10 @@ int zero_rs_launch(const ZeroArgs& a, cudaStream_t s) {
   if (a.world < 1 || a.world > kCommMaxRanks || a.rs_blocks < 1 || a.rs_blocks > kZeroMaxBlocks ||
       a.bucket < 0 || a.bucket >= a.nb)
     return -1;
-  zero_rs_kernel<<<a.rs_blocks, kZeroThreads, 0, s>>>(a);
+  if (a.peer_grad16)
+    zero_rs_kernel<true><<<a.rs_blocks, kZeroThreads, 0, s>>>(a);
+  else
+    zero_rs_kernel<false><<<a.rs_blocks, kZeroThreads, 0, s>>>(a);
   count_launches(1);
   return launch_succeeded() ? 0 : -11;
 }

@@ -18,6 +18,9 @@ constexpr int kZeroMaxBlocks = 160;  // flag / norm slots per (phase, rank)
 // {lo, hi, slice, shard_offset}.
 struct ZeroArgs {
   float** peer_grad = nullptr;
+  // zero_rs with a bf16 wire: when set, the ranks' gradients are read from
+  // these bf16 copies (same offsets as peer_grad) instead, summed in fp32
+  __nv_bfloat16** peer_grad16 = nullptr;
   __nv_bfloat16** peer_shadow = nullptr;
   uint32_t** peer_flags = nullptr;
   unsigned long long** peer_norm = nullptr;

@@ -476,6 +476,14 @@ def cast_f32_bf16(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def cast_bf16_f32(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out(fp32) = x(bf16), elementwise over contiguous buffers."""
+    if x.numel() != out.numel():
+        raise ValueError("cast_bf16_f32: sizes differ")
+    lib().cast_bf16_f32(x.data_ptr(), out.data_ptr(), x.numel(), _stream())
+    return out
+
+
 # ---------------------------------------------------------------- optimiser --
 def adamw_step(p: torch.Tensor, g: torch.Tensor, m: torch.Tensor, v: torch.Tensor,
                p_bf16: Optional[torch.Tensor], n_decay: int, hp: torch.Tensor,

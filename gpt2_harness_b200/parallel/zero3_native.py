@@ -42,9 +42,13 @@ B200 design:
   the full-size bf16 copy and fp32 gradient took 2.1 GB.
 
 Payload per rank per step in the reference convention (all-gather = output,
-reduce-scatter = input): sum over units of (2 + 2 + 4) x span_u bytes for the
-two bf16 gathers and the fp32 reduce-scatter, 4 x N_root for the root
-all-reduces and 4 bytes for the norm. span_u is the unit's 64-aligned length.
+reduce-scatter = input): sum over units of (2 + 2 + e) x span_u bytes for the
+two bf16 gathers and the reduce-scatter, e x N_root for the root all-reduces
+and 4 bytes for the norm, with e = 4 (fp32 wire, the default) or 2
+(``reduce_dtype="bf16"``: the block and root gradients are cast to bf16
+copies that the peers read, the sums stay fp32; at GPT-2 medium on 8 ranks
+that is the reference's bf16-everywhere 1,918,883,840 B plus the norm).
+span_u is the unit's 64-aligned length.
 """
 
 from __future__ import annotations
@@ -88,7 +92,8 @@ class NativeZeRO3:
     """
 
     def __init__(self, layout: ParamLayout, group=None, device: Optional[torch.device] = None,
-                 nblocks: int = 148, wait_budget_ns: int = 2_000_000_000) -> None:
+                 nblocks: int = 148, wait_budget_ns: int = 2_000_000_000,
+                 reduce_dtype: str = "fp32") -> None:
         if not dist.is_initialized():
             raise RuntimeError("NativeZeRO3 needs an initialised process group")
         self.group = group
@@ -114,11 +119,24 @@ class NativeZeRO3:
         # symmetric memory
         self._grad_full = SymmetricBuffer(sto.total * 4, group, dev)        # root grads live here
         self._gbuf = SymmetricBuffer(2 * self.max_span * 4, group, dev)     # block grads, 2 slots
+        # bf16 reduce wire (reference param_dtype/reduce_dtype, zero.py:594-631):
+        # the block gradient and the root gradients are cast to bf16 copies
+        # that the peers read; sums stay fp32
+        if reduce_dtype not in ("fp32", "bf16"):
+            raise ValueError(f"reduce_dtype must be fp32 or bf16, not {reduce_dtype!r}")
+        self.reduce_dtype = reduce_dtype
+        self._re = 2 if reduce_dtype == "bf16" else 4  # wire bytes per reduced element
+        self._gbuf16 = self._root16 = None
+        if reduce_dtype == "bf16":
+            self._gbuf16 = SymmetricBuffer(2 * self.max_span * 2, group, dev)
+            self._root16 = SymmetricBuffer(sto.total * 2, group, dev)
         self._pshard = SymmetricBuffer(self.shard_numel * 2, group, dev)    # bf16 shards
         self._flags = SymmetricBuffer(L.zero_flag_words() * 4, group, dev)
         self._ar_flags = SymmetricBuffer(L.comm_flag_words() * 4, group, dev)
         self.grad_buffer = self._grad_full.view(torch.float32, sto.total)
         self.gbuf = self._gbuf.view(torch.float32, 2 * self.max_span)
+        self.gbuf16 = self._gbuf16.view(torch.bfloat16, 2 * self.max_span) if self._gbuf16 else None
+        self.root16 = self._root16.view(torch.bfloat16, sto.total) if self._root16 else None
         self.pshard = self._pshard.view(torch.bfloat16, self.shard_numel)
         self.gather = torch.zeros(2, self.max_span, dtype=torch.bfloat16, device=dev)
         S = self.shard_numel
@@ -168,6 +186,7 @@ class NativeZeRO3:
             "err": N.error_word(dev).data_ptr(), "wait_budget_ns": int(wait_budget_ns),
             "done_handshake": 1, "peer_shard": self._pshard.peer_ptrs_dev.data_ptr(),
             "gather_dst": 0, "ag_span": 0, "ag_slice": 0, "ag_offset": 0,
+            "peer_grad16": self._gbuf16.peer_ptrs_dev.data_ptr() if self._gbuf16 else 0,
         }
         self.ar_epoch = 0
 
@@ -287,12 +306,15 @@ class NativeZeRO3:
         ev = torch.cuda.Event()
         ev.record()
         self.stream.wait_event(ev)
-        comms.record_external("reduce_scatter", u["span"], u["span"] * 4)
+        comms.record_external("reduce_scatter", u["span"], u["span"] * self._re)
         self.epoch += 1
         a = self._args
         a["epoch"] = self.epoch & 0xFFFFFFFF
         a["bucket"] = l
-        with nvtx_range(f"zero3/reduce_scatter/h.{l}"):
+        with torch.cuda.stream(self.stream), nvtx_range(f"zero3/reduce_scatter/h.{l}"):
+            if self.gbuf16 is not None:
+                base = ((self.L - 1 - l) % 2) * self.max_span
+                N.cast_f32_bf16(self.gbuf[base:base + u["span"]], self.gbuf16[base:base + u["span"]])
             N.lib().zero_rs(a, self.stream.cuda_stream)
         done = torch.cuda.Event()
         done.record(self.stream)
@@ -307,17 +329,24 @@ class NativeZeRO3:
         self.stream.wait_event(ev)
         for s in self.layout.specs:
             if s.group == "root":
-                comms.record_external("all_reduce", s.numel, s.numel * 4)
+                comms.record_external("all_reduce", s.numel, s.numel * self._re)
+        bf16 = self.root16 is not None
         with torch.cuda.stream(self.stream):
+            if bf16:
+                N.cast_f32_bf16(self.grad_buffer, self.root16)
+            buf = self._root16 if bf16 else self._grad_full
             for a, b in self.root_ranges:
                 self.ar_epoch += 1
                 count = sum(s.numel for s in self.layout.specs
                             if s.group == "root" and a <= s.offset < b)
                 N.lib().allreduce_p2p(
-                    self._grad_full.peer_ptrs_dev.data_ptr(), self._ar_flags.peer_ptrs_dev.data_ptr(),
-                    self.rank, self.world, a, b - a, 0, 1.0 / self.world, self.ar_epoch & 0xFFFFFFFF,
-                    self.byte_counter.data_ptr(), N.error_word(self.device).data_ptr(), self.nblocks,
-                    self._args["wait_budget_ns"], count, self.stream.cuda_stream)
+                    buf.peer_ptrs_dev.data_ptr(), self._ar_flags.peer_ptrs_dev.data_ptr(),
+                    self.rank, self.world, a, b - a, int(bf16), 1.0 / self.world,
+                    self.ar_epoch & 0xFFFFFFFF, self.byte_counter.data_ptr(),
+                    N.error_word(self.device).data_ptr(), self.nblocks, self._args["wait_budget_ns"],
+                    count, self.stream.cuda_stream)
+            if bf16:
+                N.cast_bf16_f32(self.root16, self.grad_buffer)
         torch.cuda.current_stream().wait_stream(self.stream)
         self._rs_done.clear()
         self._cur_unit = -1
@@ -394,5 +423,8 @@ class NativeZeRO3:
 
     def close(self) -> None:
         torch.cuda.synchronize(self.device)
-        for b in (self._grad_full, self._gbuf, self._pshard, self._flags, self._ar_flags):
+        for b in (self._grad_full, self._gbuf, self._pshard, self._flags, self._ar_flags,
+                  self._gbuf16, self._root16):
+            if b is None:
+                continue
             b.close()

@@ -65,6 +65,9 @@ class Trainer:
             overlaps backward (DDP and CP, p2p).
         cp_balance: context-parallel split, ``"zigzag"`` (two chunks per rank,
             equal causal work) or ``"contiguous"`` (one slice per rank).
+        graph: replay the step as one CUDA graph (one rank, or native DDP).
+        reduce_dtype: ZeRO-3 gradient wire, ``"fp32"`` or ``"bf16"`` (unit
+            reduce-scatters and root all-reduces on bf16 copies, fp32 sums).
         seed: weight init seed (identical on every rank; rank 0's weights are
             broadcast to make sure).
     """
@@ -74,7 +77,7 @@ class Trainer:
                  device: Optional[torch.device] = None, seed: int = 0,
                  bucket_bytes: int = 25 * 1024 * 1024, schedule: bool = True,
                  strategy: str = "ddp", comm_blocks: int = 128, cp_balance: str = "zigzag",
-                 graph: bool = False) -> None:
+                 graph: bool = False, reduce_dtype: str = "fp32") -> None:
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device())
         self.device = torch.device(device)
@@ -140,7 +143,7 @@ class Trainer:
             elif strategy == "zero3":
                 from gpt2_harness_b200.parallel.zero3_native import NativeZeRO3
 
-                self.ddp = NativeZeRO3(layout, device=self.device)
+                self.ddp = NativeZeRO3(layout, device=self.device, reduce_dtype=reduce_dtype)
             else:
                 from gpt2_harness_b200.parallel.ddp_native import NativeDDP
 

@@ -315,6 +315,11 @@ def cast_f32_bf16(x, out):
     return out.copy_(x)
 
 
+def cast_bf16_f32(x, out):
+    out.copy_(x.float())
+    return out
+
+
 # ------------------------------------------------------ symmetric memory --
 def _at(ptr: int, numel: int, dtype: torch.dtype) -> torch.Tensor:
     """A CPU tensor aliasing ``numel`` elements at address ``ptr``."""
@@ -619,7 +624,9 @@ def zero_rs(d, stream=0):
     rank, world = d["rank"], d["world"]
     tab = _zero_table(d)
     ext = max(r[1] for r in tab)
-    grads = [_at(p, ext, torch.float32) for p in _ptr_list(d["peer_grad"], world)]
+    wire16 = bool(d.get("peer_grad16"))
+    grads = ([_at(p, ext, torch.bfloat16) for p in _ptr_list(d["peer_grad16"], world)] if wire16
+             else [_at(p, ext, torch.float32) for p in _ptr_list(d["peer_grad"], world)])
     b = d["bucket"]
     f0, n, off = _zero_slice(tab[b], rank)
     dist.barrier(group=_group(d["peer_flags"]))
@@ -630,12 +637,12 @@ def zero_rs(d, stream=0):
     if n:
         acc = torch.zeros(n)
         for q in range(world):
-            acc += grads[q][f0:f0 + n]
+            acc += grads[q][f0:f0 + n].float()
         acc *= d["scale"]
         _at(d["gsh"], off + n, torch.float32)[off:off + n] = acc
         if parts is not None:
             parts[b * d["rs_blocks"]] = (acc * acc).sum()
-    _bump(d.get("byte_counter"), (tab[b][1] - tab[b][0]) * 4)
+    _bump(d.get("byte_counter"), (tab[b][1] - tab[b][0]) * (2 if wire16 else 4))
     dist.barrier(group=_group(d["peer_flags"]))
 
 
@@ -730,7 +737,7 @@ OPS = {
     "cross_entropy_fwd_bwd": cross_entropy_fwd_bwd, "lm_head_cross_entropy": lm_head_cross_entropy,
     "attention_fwd": attention_fwd,
     "attention_bwd": attention_bwd, "grad_sumsq": grad_sumsq, "clip_coef": clip_coef,
-    "adamw_step": adamw_step, "cast_f32_bf16": cast_f32_bf16, "decode_embed": decode_embed,
+    "adamw_step": adamw_step, "cast_f32_bf16": cast_f32_bf16, "cast_bf16_f32": cast_bf16_f32, "decode_embed": decode_embed,
     "decode_partials": decode_partials, "decode_attn": decode_attn, "decode_argmax": decode_argmax,
 }
 
