@@ -334,6 +334,8 @@ def run_native(args, world, rank):
     out["gpu_launches"] = int(n_launch)
     out["config"]["comm"] = (args.comm if args.strategy == "ddp" else "p2p") if world > 1 else "none"
     out["config"]["cuda_graph"] = graph
+    if args.reduce_dtype != "fp32":
+        out["config"]["reduce_dtype"] = args.reduce_dtype
     if args.strategy == "cp":
         out["config"]["cp_balance"] = args.cp_balance
     if args.strategy == "zero3":
@@ -513,7 +515,7 @@ def main():
                          "as one CUDA graph; auto = one rank only")
     ap.add_argument("--strategy", choices=["ddp", "zero2", "zero3", "tp", "cp", "pp"], default="ddp")
     ap.add_argument("--reduce-dtype", choices=["fp32", "bf16"], default="fp32",
-                    help="ZeRO-3 gradient reduce-scatter / root all-reduce wire")
+                    help="gradient wire of DDP buckets and ZeRO-3 reduce-scatters / root all-reduces")
     ap.add_argument("--pp", type=int, default=0, help="pipeline stages (pp strategy; default N / cp)")
     ap.add_argument("--cp", type=int, default=1, help="context-parallel ranks per stage (pp strategy)")
     ap.add_argument("--micro-batches", type=int, default=8, help="micro-batches per step (pp strategy)")

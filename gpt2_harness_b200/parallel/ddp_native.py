@@ -104,7 +104,7 @@ class NativeDDP:
     def __init__(self, layout: ParamLayout, group=None, comm: str = "p2p",
                  bucket_bytes: int = DEFAULT_BUCKET_BYTES, nblocks: int = 128,
                  device: Optional[torch.device] = None, tail_blocks: int = 128,
-                 wait_budget_s: float = 30.0) -> None:
+                 wait_budget_s: float = 30.0, reduce_dtype: str = "fp32") -> None:
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -138,6 +138,21 @@ class NativeDDP:
             self.flags = SymmetricBuffer(words * 4, group, self.device)
         else:
             self.grad_buffer = torch.zeros(layout.total, dtype=torch.float32, device=self.device)
+        # bf16 wire (reference data_parallel.py:136-151: cast the bucket down,
+        # reduce, cast up): each bucket is cast into a bf16 copy that the
+        # all-reduce works on (fp32 sums in the kernel) and cast back
+        if reduce_dtype not in ("fp32", "bf16"):
+            raise ValueError(f"reduce_dtype must be fp32 or bf16, not {reduce_dtype!r}")
+        if reduce_dtype == "bf16" and self.comm == "mc":
+            raise ValueError("the bf16 wire runs on the P2P or NCCL all-reduce")
+        self.reduce_dtype = reduce_dtype
+        self._wire16 = None
+        self.grad16 = None
+        if reduce_dtype == "bf16" and self.comm == "p2p":
+            self._wire16 = SymmetricBuffer(layout.total * 2, group, self.device)
+            self.grad16 = self._wire16.view(torch.bfloat16, layout.total)
+        elif reduce_dtype == "bf16" and self.comm == "nccl":
+            self.grad16 = torch.zeros(layout.total, dtype=torch.bfloat16, device=self.device)
         # The reduction kernels get a higher stream priority than the compute
         # stream: their CTAs are placed as soon as SMs free up, so each bucket
         # finishes (and hands its SMs back to the backward) as early as possible.
@@ -182,8 +197,11 @@ class NativeDDP:
         ev = torch.cuda.Event()
         ev.record()
         self.stream.wait_event(ev)
-        comms.record_external("all_reduce", b.numel, b.numel * 4)
+        wire16 = self.grad16 is not None
+        comms.record_external("all_reduce", b.numel, b.numel * (2 if wire16 else 4))
         with torch.cuda.stream(self.stream), nvtx_range(f"allreduce/bucket{self.buckets.index(b)}"):
+            if wire16:
+                N.cast_f32_bf16(self.grad_buffer[b.lo:b.hi], self.grad16[b.lo:b.hi])
             if self.device_epochs:
                 epoch = 0
             else:
@@ -197,13 +215,16 @@ class NativeDDP:
                                      self.wait_budget_ns, b.numel, self.stream.cuda_stream)
             elif self.comm == "p2p":
                 fn = N.lib().allreduce_p2p_slim if slim else N.lib().allreduce_p2p
-                fn(self.symm.peer_ptrs_dev.data_ptr(), self.flags.peer_ptrs_dev.data_ptr(),
-                   self.rank, self.world, b.lo, b.hi - b.lo, 0, 1.0 / self.world,
+                bufs = self._wire16 if wire16 else self.symm
+                fn(bufs.peer_ptrs_dev.data_ptr(), self.flags.peer_ptrs_dev.data_ptr(),
+                   self.rank, self.world, b.lo, b.hi - b.lo, int(wire16), 1.0 / self.world,
                    epoch, self.byte_counter.data_ptr(), N.error_word().data_ptr(),
                    self.nblocks if slim else self.tail_blocks, self.wait_budget_ns, b.numel,
                    self.stream.cuda_stream)
             else:
-                dist.all_reduce(self.grad_buffer[b.lo:b.hi], group=self.group)
+                dist.all_reduce((self.grad16 if wire16 else self.grad_buffer)[b.lo:b.hi], group=self.group)
+            if wire16:
+                N.cast_bf16_f32(self.grad16[b.lo:b.hi], self.grad_buffer[b.lo:b.hi])
 
     def timeout_record(self) -> Optional[dict]:
         """Where this rank's first bucket handshake gave up (synchronises), or
@@ -237,3 +258,5 @@ class NativeDDP:
             self.symm.close()
         if self.flags is not None:
             self.flags.close()
+        if self._wire16 is not None:
+            self._wire16.close()

@@ -66,8 +66,9 @@ class Trainer:
         cp_balance: context-parallel split, ``"zigzag"`` (two chunks per rank,
             equal causal work) or ``"contiguous"`` (one slice per rank).
         graph: replay the step as one CUDA graph (one rank, or native DDP).
-        reduce_dtype: ZeRO-3 gradient wire, ``"fp32"`` or ``"bf16"`` (unit
-            reduce-scatters and root all-reduces on bf16 copies, fp32 sums).
+        reduce_dtype: gradient wire of DDP and ZeRO-3, ``"fp32"`` or ``"bf16"``
+            (buckets / unit reduce-scatters and root all-reduces on bf16
+            copies; the P2P kernels sum in fp32).
         seed: weight init seed (identical on every rank; rank 0's weights are
             broadcast to make sure).
     """
@@ -148,7 +149,7 @@ class Trainer:
                 from gpt2_harness_b200.parallel.ddp_native import NativeDDP
 
                 self.ddp = NativeDDP(layout, comm=comm, bucket_bytes=bucket_bytes,
-                                     device=self.device, nblocks=comm_blocks)
+                                     device=self.device, nblocks=comm_blocks, reduce_dtype=reduce_dtype)
             grad_buffer = self.ddp.grad_buffer
         storage = self.ddp.storage_layout if self.strategy == "zero3" else None
         self.engine = Engine(config, self.device, optim=optim, grad_buffer=grad_buffer,
