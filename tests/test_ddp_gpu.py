@@ -33,7 +33,8 @@ WORKER = textwrap.dedent(r'''
     comm = os.environ["G2B_COMM"]
     cfg = gpt2_config("gpt2", **json.loads(os.environ.get("G2B_CFG", '{"n_layer": 2, "n_positions": 256}')))
     layout = ParamLayout(cfg)
-    ddp = NativeDDP(layout, comm=comm, bucket_bytes=4 * 1024 * 1024)
+    ddp = NativeDDP(layout, comm=comm, bucket_bytes=4 * 1024 * 1024,
+                    reduce_dtype=os.environ.get("G2B_REDUCE", "fp32"))
     eng = Engine(cfg, "cuda", grad_buffer=ddp.grad_buffer, seed=0)
     ddp.attach(eng)
     solo = Engine(cfg, "cuda", seed=0)      # same weights, no communication
@@ -71,7 +72,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _run(comm: str, world: int = 2, cfg: dict | None = None):
+def _run(comm: str, world: int = 2, cfg: dict | None = None, reduce_dtype: str = "fp32"):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     import json
@@ -79,7 +80,8 @@ def _run(comm: str, world: int = 2, cfg: dict | None = None):
     procs = []
     for r in range(world):
         env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r),
-                   MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), G2B_ROOT=ROOT, G2B_COMM=comm)
+                   MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), G2B_ROOT=ROOT, G2B_COMM=comm,
+                   G2B_REDUCE=reduce_dtype)
         if comm != "mc":
             env["NCCL_NVLS_ENABLE"] = "0"
         if cfg is not None:
@@ -111,6 +113,19 @@ def test_native_ddp_two_gpus(comm, world):
     if comm in ("p2p", "mc"):
         # the in-kernel counter charges the same payload: 4N per step x 2 steps
         assert res[0]["device_bytes"] == 2 * 4 * res[0]["n_params"], res[0]
+
+
+@pytest.mark.parametrize("comm", ["p2p", "nccl"])
+def test_native_ddp_bf16_wire(comm):
+    """The reference's bf16 gradient wire: buckets cast to bf16 copies, reduced
+    (the P2P kernel sums in fp32), cast back; 2N bytes a step."""
+    res = _run(comm, 2, reduce_dtype="bf16")
+    for r in res:
+        assert r["rel_err"] < 1e-2, r
+        assert r["ranks_equal"], r
+        assert r["payload_per_step"] == 2 * r["n_params"], r
+    if comm == "p2p":
+        assert res[0]["device_bytes"] == 2 * 2 * res[0]["n_params"], res[0]
 
 
 def _multicast() -> bool:
