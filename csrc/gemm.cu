@@ -529,7 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r_local = lg * 32 + lane;   // row within the tile
     constexpr int CHUNKS = BN / 64;       // 32-column chunks per warp
     // two bf16 boxes per warp (the cross-entropy statistics epilogue keeps
-    // one: measured 1.37 ms with one, 1.57 ms with two, in separate calls)
+    // one: measured 1.37 ms with one, 1.57 ms with two, on different machines)
     constexpr bool kDblBox = !F32_OUT && EPI != EPI_BIAS_GELU && EPI != EPI_CE_STATS;
     uint8_t* box = smem + Cfg::EPI_OFFSET + ew * kStageBuf;
     int acc = 0;
