@@ -560,12 +560,14 @@ int attn_fwd_launch(const AttnArgs& a, cudaStream_t s) {
   if (a.B <= 0 || a.H <= 0 || a.Tq <= 0 || a.Tk <= 0) return -1;
   const int grouped = kv_grouping(a);
   if (grouped < 0) return -1;
-  if (grouped && g_attn_impl != 0) return -12;
+  // grouped heads and keys/values streamed from their owners: tensor cores only
+  const bool streamed = a.peers && a.peers->world > 0;
+  if ((grouped || streamed) && g_attn_impl != 0) return -12;
   if (g_attn_impl == 0) {
     const int rc = attn_fwd_tc_launch(a, s);
     if (rc == 1) return 0;
     if (rc < 0) return rc;
-    if (grouped) return -12;  // grouped heads need TMA-compatible layouts
+    if (grouped || streamed) return -12;  // these need TMA-compatible layouts
   }
   const int smem = (FWD_BQ + 4 * FWD_BK) * 128;
   dim3 grid((a.Tq + FWD_BQ - 1) / FWD_BQ, a.B * a.H);
@@ -578,7 +580,9 @@ int attn_bwd_launch(const AttnArgs& a, cudaStream_t s) {
   if (a.B <= 0 || a.H <= 0 || a.Tq <= 0 || a.Tk <= 0) return -1;
   const int grouped = kv_grouping(a);
   if (grouped < 0) return -1;
-  if (grouped && g_attn_impl != 0) return -12;
+  // grouped heads and keys/values streamed from their owners: tensor cores only
+  const bool streamed = a.peers && a.peers->world > 0;
+  if ((grouped || streamed) && g_attn_impl != 0) return -12;
   const int64_t rows = (int64_t)a.B * a.H * a.Tq;
   auto rows16 = [](const HeadView& v) {
     return (reinterpret_cast<uintptr_t>(v.base) & 15) == 0 && (v.st * 2) % 16 == 0 &&
@@ -595,7 +599,7 @@ int attn_bwd_launch(const AttnArgs& a, cudaStream_t s) {
       return launch_succeeded() ? 0 : -11;
     }
     if (rc < 0) return rc;
-    if (grouped) return -12;  // grouped heads need TMA-compatible layouts
+    if (grouped || streamed) return -12;  // these need TMA-compatible layouts
   }
   const int smem_kv = 6 * BWD_B * 128 + 4 * BWD_B * 4;
   static bool attr = false;

@@ -12,6 +12,30 @@ struct HeadView {
   int64_t sb = 0, st = 0, sh = 0;
 };
 
+// Context-parallel keys and values read in place from their owners (the
+// streaming form of the all-gather-KV attention). Rank q of the group keeps
+// its own rows of every sequence in a symmetric buffer mapped into this
+// process at base[q]: [B, Tl, 2C] bf16, keys in columns [0, C), values in
+// [v_off, v_off + C). Key position k (natural order over the whole sequence)
+// belongs to
+//   contiguous split:  rank k / Tl, local row k % Tl;
+//   zig-zag split:     chunk c = k / (Tl/2), rank c (c < world) or
+//                      2*world-1-c, local row (c < world ? 0 : Tl/2) + k % (Tl/2).
+// Before its first read from rank q a kernel waits (bounded) until
+// flags[q] has reached `epoch`: rank q stores the epoch there with a system-
+// scope release once its rows are in place (cp_kv_publish).
+constexpr int kKvMaxOwners = 8;
+struct KvPeers {
+  int world = 0;            // 0: keys and values come from AttnArgs::k / v
+  int zigzag = 0;
+  int Tl = 0;               // rows per sequence in each owner's buffer
+  void* base[kKvMaxOwners] = {};
+  int64_t sb = 0, st = 0;   // element strides of an owner buffer (sequence, row)
+  int64_t v_off = 0;        // element offset of the value columns
+  const uint32_t* flags = nullptr;
+  uint32_t epoch = 0;
+};
+
 struct AttnArgs {
   HeadView q, k, v, o;      // forward inputs / output (bf16)
   HeadView dout, dq, dk, dv;  // backward (bf16)
@@ -26,6 +50,9 @@ struct AttnArgs {
   int causal = 1;
   float scale = 0.125f;     // softmax scale (1/sqrt(head_dim))
   uint32_t* err = nullptr;
+  // Set: keys and values are read from their owners (tensor-core kernels
+  // only; k / v are ignored). Tk still counts natural key positions.
+  const KvPeers* peers = nullptr;
 };
 
 int attn_fwd_launch(const AttnArgs& a, cudaStream_t s);

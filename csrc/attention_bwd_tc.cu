@@ -32,6 +32,7 @@
 #include <cuda_bf16.h>
 
 #include "attention.cuh"
+#include "attention_peers.cuh"
 #include "common.cuh"
 
 namespace g2b {
@@ -208,11 +209,14 @@ __device__ __forceinline__ void ew_q(const uint32_t (&sv)[NC], uint32_t (&dv)[NC
   }
 }
 
-template <int MODE>
+// KV = KvPeerMaps (context parallelism, streaming): the key/value operand --
+// stationary in MODE_KV (tmA / tmA2), streamed in MODE_Q (tmX / tmY) -- is
+// loaded through its owner's maps instead.
+template <int MODE, class KV>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
                        const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmY,
-                       const BwdParams p) {
+                       const BwdParams p, const __grid_constant__ KV kv) {
   // MODE_KV: A = K, A2 = V (stationary); X = Q, Y = dO (streaming)
   // MODE_Q : A = Q, A2 = dO (stationary); X = K, Y = V (streaming)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -271,6 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ producer
     const int lane = (int)lane_id();
     uint32_t g = 0, i = 0, a_issued = 0;
+    uint32_t owners_seen = 0;  // streaming: owners whose publish flag lane 0 saw
     bool ok = true;
     for (int t = blockIdx.x; t < p.n_tiles && ok; t += gridDim.x) {
       const TileInfo ti = tile_info<MODE>(p, t);
@@ -280,10 +285,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = false;
         break;
       }
-      if (lane == 0) {
-        mbar_arrive_expect_tx(a_full, 2 * ATILE);
-        tma_load_4d(smem + SA_OFF, &tmA, a_full, 0, h, ti.r0, b);
-        tma_load_4d(smem + SA2_OFF, &tmA2, a_full, 0, h, ti.r0, b);
+      if constexpr (KvStreaming<KV>::on && MODE == MODE_KV) {
+        int ready = 1, q = 0, row = 0;
+        if (lane == 0) {
+          q = kv_owner_row(kv, ti.r0, &row);
+          ready = kv_owner_ready(kv, q, &owners_seen, p.err, abort_flag);
+        }
+        if (!__shfl_sync(0xffffffffu, ready, 0)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(a_full, 2 * ATILE);
+          tma_load_4d(smem + SA_OFF, &kv.k[q], a_full, 0, h, row, b);
+          tma_load_4d(smem + SA2_OFF, &kv.v[q], a_full, 0, h, row, b);
+        }
+      } else {
+        if (lane == 0) {
+          mbar_arrive_expect_tx(a_full, 2 * ATILE);
+          tma_load_4d(smem + SA_OFF, &tmA, a_full, 0, h, ti.r0, b);
+          tma_load_4d(smem + SA2_OFF, &tmA2, a_full, 0, h, ti.r0, b);
+        }
       }
       ++a_issued;
       for (int j = 0; j < ti.n; ++j, ++g) {
@@ -310,11 +332,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           __syncwarp();
         }
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&x_full[st], 2 * XTILE);
-          uint8_t* xs = smem + RING_OFF + st * 2 * XTILE;
-          tma_load_4d(xs, &tmX, &x_full[st], 0, hx, row, b);
-          tma_load_4d(xs + XTILE, &tmY, &x_full[st], 0, hx, row, b);
+        if constexpr (KvStreaming<KV>::on && MODE == MODE_Q) {
+          int ready = 1, q = 0, krow = 0;
+          if (lane == 0) {
+            q = kv_owner_row(kv, row, &krow);
+            ready = kv_owner_ready(kv, q, &owners_seen, p.err, abort_flag);
+          }
+          if (!__shfl_sync(0xffffffffu, ready, 0)) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&x_full[st], 2 * XTILE);
+            uint8_t* xs = smem + RING_OFF + st * 2 * XTILE;
+            tma_load_4d(xs, &kv.k[q], &x_full[st], 0, hx, krow, b);
+            tma_load_4d(xs + XTILE, &kv.v[q], &x_full[st], 0, hx, krow, b);
+          }
+        } else {
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&x_full[st], 2 * XTILE);
+            uint8_t* xs = smem + RING_OFF + st * 2 * XTILE;
+            tma_load_4d(xs, &tmX, &x_full[st], 0, hx, row, b);
+            tma_load_4d(xs + XTILE, &tmY, &x_full[st], 0, hx, row, b);
+          }
         }
         __syncwarp();
       }
@@ -590,18 +630,18 @@ int num_sms() {
   return n;
 }
 
-template <int MODE>
+template <int MODE, class KV>
 int launch_mode(const CUtensorMap& a, const CUtensorMap& a2, const CUtensorMap& x,
-                const CUtensorMap& y, const BwdParams& p, cudaStream_t s) {
+                const CUtensorMap& y, const BwdParams& p, const KV& kv, cudaStream_t s) {
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(attn_bwd_tc_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             SMEM_BYTES) != cudaSuccess)
+    if (cudaFuncSetAttribute(attn_bwd_tc_kernel<MODE, KV>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
       return -10;
     attr = true;
   }
   const int grid = p.n_tiles < num_sms() ? p.n_tiles : num_sms();
-  attn_bwd_tc_kernel<MODE><<<grid, kThreads, SMEM_BYTES, s>>>(a, a2, x, y, p);
+  attn_bwd_tc_kernel<MODE, KV><<<grid, kThreads, SMEM_BYTES, s>>>(a, a2, x, y, p, kv);
   count_launches(1);
   return launch_succeeded() ? 0 : -11;
 }
@@ -611,19 +651,37 @@ int launch_mode(const CUtensorMap& a, const CUtensorMap& a2, const CUtensorMap& 
 
 // Tensor-core backward (after delta has been computed into a.delta): returns
 // 1 if it ran, 0 when a layout is not TMA-compatible, negative on failure.
+// Streaming launches (a.peers) return -12 instead of 0 when a layout does
+// not fit: they have no fallback kernel.
 int attn_bwd_tc_launch(const AttnArgs& a, cudaStream_t s) {
-  if (!tma_ok(a.q) || !tma_ok(a.k) || !tma_ok(a.v) || !tma_ok(a.dout) || !out_ok(a.dq) ||
-      !out_ok(a.dk) || !out_ok(a.dv))
-    return 0;
-  if (a.B * a.H <= 0 || a.Tq <= 0 || a.Tk <= 0) return 0;
+  const bool stream = a.peers && a.peers->world > 0;
+  const int no_fit = stream ? -12 : 0;
+  if (!tma_ok(a.q) || !tma_ok(a.dout) || !out_ok(a.dq) || !out_ok(a.dk) || !out_ok(a.dv))
+    return no_fit;
+  if (!stream && (!tma_ok(a.k) || !tma_ok(a.v))) return 0;
+  if (a.B * a.H <= 0 || a.Tq <= 0 || a.Tk <= 0) return no_fit;
   const int Hkv = a.Hkv > 0 ? a.Hkv : a.H;
   if (Hkv > a.H || a.H % Hkv) return -1;
   CUtensorMap tq_a, tk_a, tv_a, tdo_a, tq_x, tk_x, tv_x, tdo_x;
-  if (!head_map(&tq_a, a.q, a.H, a.Tq, a.B, TB) || !head_map(&tk_a, a.k, Hkv, a.Tk, a.B, TB) ||
-      !head_map(&tv_a, a.v, Hkv, a.Tk, a.B, TB) || !head_map(&tdo_a, a.dout, a.H, a.Tq, a.B, TB) ||
-      !head_map(&tq_x, a.q, a.H, a.Tq, a.B, SB) || !head_map(&tk_x, a.k, Hkv, a.Tk, a.B, SB) ||
-      !head_map(&tv_x, a.v, Hkv, a.Tk, a.B, SB) || !head_map(&tdo_x, a.dout, a.H, a.Tq, a.B, SB))
+  if (!head_map(&tq_a, a.q, a.H, a.Tq, a.B, TB) || !head_map(&tdo_a, a.dout, a.H, a.Tq, a.B, TB) ||
+      !head_map(&tq_x, a.q, a.H, a.Tq, a.B, SB) || !head_map(&tdo_x, a.dout, a.H, a.Tq, a.B, SB))
+    return no_fit;
+  // streaming: one set of owner maps per box height (128-row stationary
+  // tiles for dK/dV, 64-row streamed blocks for dQ); tk_* / tv_* not read
+  KvPeerMaps peers_a{}, peers_x{};
+  if (stream) {
+    auto enc = attn_get_encode_fn();
+    if (a.Tk % TB || !make_kv_peer_maps(&peers_a, *a.peers, Hkv, a.B, TB, enc) ||
+        !make_kv_peer_maps(&peers_x, *a.peers, Hkv, a.B, SB, enc))
+      return -12;
+    tk_a = peers_a.k[0];
+    tv_a = peers_a.v[0];
+    tk_x = peers_x.k[0];
+    tv_x = peers_x.v[0];
+  } else if (!head_map(&tk_a, a.k, Hkv, a.Tk, a.B, TB) || !head_map(&tv_a, a.v, Hkv, a.Tk, a.B, TB) ||
+             !head_map(&tk_x, a.k, Hkv, a.Tk, a.B, SB) || !head_map(&tv_x, a.v, Hkv, a.Tk, a.B, SB)) {
     return 0;
+  }
   BwdParams p;
   // dK / dV tiles are per key/value head; each walks its group's query heads
   p.H = Hkv;
@@ -650,7 +708,8 @@ int attn_bwd_tc_launch(const AttnArgs& a, cudaStream_t s) {
   p.o2_sh = a.dv.sh;
   p.n_blk = (a.Tk + TB - 1) / TB;
   p.n_tiles = p.n_blk * p.BH;
-  int rc = launch_mode<MODE_KV>(tk_a, tv_a, tq_x, tdo_x, p, s);
+  int rc = stream ? launch_mode<MODE_KV>(tk_a, tv_a, tq_x, tdo_x, p, peers_a, s)
+                  : launch_mode<MODE_KV>(tk_a, tv_a, tq_x, tdo_x, p, NoKvPeers{}, s);
   if (rc) return rc;
   // dQ
   p.out1 = reinterpret_cast<__nv_bfloat16*>(a.dq.base);
@@ -663,7 +722,8 @@ int attn_bwd_tc_launch(const AttnArgs& a, cudaStream_t s) {
   p.BH = a.B * a.H;
   p.n_blk = (a.Tq + TB - 1) / TB;
   p.n_tiles = p.n_blk * p.BH;
-  rc = launch_mode<MODE_Q>(tq_a, tdo_a, tk_x, tv_x, p, s);
+  rc = stream ? launch_mode<MODE_Q>(tq_a, tdo_a, tk_x, tv_x, p, peers_x, s)
+              : launch_mode<MODE_Q>(tq_a, tdo_a, tk_x, tv_x, p, NoKvPeers{}, s);
   return rc ? rc : 1;
 }
 

@@ -34,6 +34,7 @@
 #include <math.h>
 
 #include "attention.cuh"
+#include "attention_peers.cuh"
 #include "common.cuh"
 
 namespace g2b {
@@ -139,10 +140,14 @@ __device__ __forceinline__ int item_index(int r) {
 // 32 -> 0.0935 ms, 40 and 48 -> 0.0903 ms, 64 -> 0.0935 ms.
 constexpr int kMufu = 48;
 
+// KV = NoKvPeers: keys and values through tmK / tmV. KV = KvPeerMaps
+// (context parallelism, streaming): each key block through its owner's maps.
+template <class KV>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                        const __grid_constant__ CUtensorMap tmK,
-                       const __grid_constant__ CUtensorMap tmV, const TcParams p) {
+                       const __grid_constant__ CUtensorMap tmV, const TcParams p,
+                       const __grid_constant__ KV kv) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -199,6 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (elect_one()) {
       int kv_count = 0;  // K/V blocks issued by this CTA so far (ring position)
       int qi = 0;        // items loaded so far (Q buffer position)
+      uint32_t owners_seen = 0;  // streaming: owners whose publish flag was seen
       bool ok = true;
       for (int r = 0; ok; ++r) {
         const int w = item_index(r);
@@ -222,10 +228,31 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&kv_full[st], 2 * KVTILE);
-          tma_load_4d(smem + K_OFF + st * KVTILE, &tmK, &kv_full[st], 0, h / p.grp, j * TKV, b);
-          tma_load_4d(smem + V_OFF + st * KVTILE, &tmV, &kv_full[st], 0, h / p.grp, j * TKV, b);
+          if constexpr (KvStreaming<KV>::on) {
+            int row;
+            const int q = kv_owner_row(kv, j * TKV, &row);
+            if (!kv_owner_ready(kv, q, &owners_seen, p.err, abort_flag)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&kv_full[st], 2 * KVTILE);
+            tma_load_4d(smem + K_OFF + st * KVTILE, &kv.k[q], &kv_full[st], 0, h / p.grp, row, b);
+            tma_load_4d(smem + V_OFF + st * KVTILE, &kv.v[q], &kv_full[st], 0, h / p.grp, row, b);
+          } else {
+            mbar_arrive_expect_tx(&kv_full[st], 2 * KVTILE);
+            tma_load_4d(smem + K_OFF + st * KVTILE, &tmK, &kv_full[st], 0, h / p.grp, j * TKV, b);
+            tma_load_4d(smem + V_OFF + st * KVTILE, &tmV, &kv_full[st], 0, h / p.grp, j * TKV, b);
+          }
         }
+      }
+      if (*abort_flag) {
+        // A role gave up (this one on a peer's flag, or another on a
+        // barrier): wait (bounded) for this warp's copies still in flight
+        // before the CTA's shared memory is released.
+        if (qi) mbar_wait_bounded(&q_full[(qi - 1) % QB], ((qi - 1) / QB) & 1, p.err, ERR_TIMEOUT_ATTN,
+                                  nullptr);
+        for (int kc = kv_count > KS ? kv_count - KS : 0; kc < kv_count; ++kc)
+          mbar_wait_bounded(&kv_full[kc % KS], (kc / KS) & 1, p.err, ERR_TIMEOUT_ATTN, nullptr);
       }
     }
   } else if (warp == 1) {
@@ -554,17 +581,30 @@ unsigned long long* g_attn_fwd_trace = nullptr;  // set by a tracing harness
 
 // Returns 1 if the tensor-core path ran, 0 if the caller must use the
 // mma.sync kernel (layout not TMA-compatible), negative on launch failure.
+// Streaming launches (a.peers) return -12 instead of 0 when a layout does not
+// fit: they have no fallback kernel.
 int attn_fwd_tc_launch(const AttnArgs& a, cudaStream_t s) {
-  if (!head_view_tma_ok(a.q) || !head_view_tma_ok(a.k) || !head_view_tma_ok(a.v)) return 0;
+  const bool stream = a.peers && a.peers->world > 0;
+  const int no_fit = stream ? -12 : 0;
+  if (!head_view_tma_ok(a.q)) return no_fit;
+  if (!stream && (!head_view_tma_ok(a.k) || !head_view_tma_ok(a.v))) return 0;
   if ((a.o.sh * 2) % 16 || (a.o.st * 2) % 16 || (reinterpret_cast<uintptr_t>(a.o.base) & 15))
-    return 0;
+    return no_fit;
   const int Hkv = a.Hkv > 0 ? a.Hkv : a.H;
   if (Hkv > a.H || a.H % Hkv) return -1;
   CUtensorMap tq, tk, tv;
-  if (!make_head_map(&tq, a.q, a.H, a.Tq, a.B, TQ) ||
-      !make_head_map(&tk, a.k, Hkv, a.Tk, a.B, TKV) ||
-      !make_head_map(&tv, a.v, Hkv, a.Tk, a.B, TKV))
+  if (!make_head_map(&tq, a.q, a.H, a.Tq, a.B, TQ)) return no_fit;
+  KvPeerMaps peer_maps{};
+  if (stream) {
+    // key blocks never straddle two owners; tmK / tmV are not read
+    if (a.Tk % TKV || !make_kv_peer_maps(&peer_maps, *a.peers, Hkv, a.B, TKV, attn_get_encode_fn()))
+      return -12;
+    tk = peer_maps.k[0];
+    tv = peer_maps.v[0];
+  } else if (!make_head_map(&tk, a.k, Hkv, a.Tk, a.B, TKV) ||
+             !make_head_map(&tv, a.v, Hkv, a.Tk, a.B, TKV)) {
     return 0;
+  }
   TcParams p;
   p.B = a.B;
   p.H = a.H;
@@ -583,11 +623,12 @@ int attn_fwd_tc_launch(const AttnArgs& a, cudaStream_t s) {
 #ifdef G2B_ATTN_FWD_TRACE
   p.trace = g_attn_fwd_trace;
 #endif
-  auto kern = attn_fwd_tc_kernel;
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(attn_fwd_tc_kernel<NoKvPeers>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_fwd_tc_kernel<KvPeerMaps>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
       return -10;
     attr = true;
   }
@@ -601,7 +642,10 @@ int attn_fwd_tc_launch(const AttnArgs& a, cudaStream_t s) {
     if (sms <= 0) sms = 148;
   }
   const int grid = p.n_items < sms ? p.n_items : sms;  // persistent: one CTA per SM
-  kern<<<grid, kThreads, SMEM_BYTES, s>>>(tq, tk, tv, p);
+  if (stream)
+    attn_fwd_tc_kernel<KvPeerMaps><<<grid, kThreads, SMEM_BYTES, s>>>(tq, tk, tv, p, peer_maps);
+  else
+    attn_fwd_tc_kernel<NoKvPeers><<<grid, kThreads, SMEM_BYTES, s>>>(tq, tk, tv, p, NoKvPeers{});
   count_launches(1);
   return launch_succeeded() ? 1 : -11;
 }

@@ -149,6 +149,78 @@ PYBIND11_MODULE(_C, m) {
           check(attn_bwd_launch(a, S(stream)), "attn_bwd");
         });
 
+  // Context-parallel streaming forms: keys and values read in place from
+  // every owner's compact [B, Tl, 2C] buffer (peer_bases[q], this process's
+  // mapping), after owner q's publish word flags[q] reaches `epoch`.
+  auto kv_peers = [](const py::sequence& bases, int64_t kv_sb, int64_t kv_st, int64_t v_off,
+                     int Tl, int zigzag, int64_t flags, int64_t epoch) {
+    const size_t n = py::len(bases);
+    if (n == 0 || n > (size_t)kKvMaxOwners)
+      throw std::runtime_error("attention peers: 1 to 8 owner buffers");
+    KvPeers kp;
+    kp.world = (int)n;
+    for (size_t q = 0; q < n; ++q) kp.base[q] = reinterpret_cast<void*>(bases[q].cast<int64_t>());
+    kp.sb = kv_sb;
+    kp.st = kv_st;
+    kp.v_off = v_off;
+    kp.Tl = Tl;
+    kp.zigzag = zigzag;
+    kp.flags = P<const uint32_t>(flags);
+    kp.epoch = (uint32_t)epoch;
+    return kp;
+  };
+  m.def("attn_fwd_peers", [kv_peers](int64_t q, int64_t o, int64_t sb, int64_t st, int64_t sh, int64_t osb,
+                                     int64_t ost, int64_t osh, int64_t lse, int B, int H, int Hkv, int Tq,
+                                     int Tk, int q_offset, float scale, const py::sequence& bases,
+                                     int64_t kv_sb, int64_t kv_st, int64_t v_off, int Tl, int zigzag,
+                                     int64_t flags, int64_t epoch, int64_t err, int64_t stream) {
+    const KvPeers kp = kv_peers(bases, kv_sb, kv_st, v_off, Tl, zigzag, flags, epoch);
+    AttnArgs a;
+    a.q = hv(q, sb, st, sh);
+    a.o = hv(o, osb, ost, osh);
+    a.lse = P<float>(lse);
+    a.B = B;
+    a.H = H;
+    a.Hkv = Hkv;
+    a.Tq = Tq;
+    a.Tk = Tk;
+    a.q_offset = q_offset;
+    a.causal = 1;
+    a.scale = scale;
+    a.err = P<uint32_t>(err);
+    a.peers = &kp;
+    check(attn_fwd_launch(a, S(stream)), "attn_fwd_peers");
+  });
+  m.def("attn_bwd_peers",
+        [kv_peers](int64_t q, int64_t o, int64_t dout, int64_t dq, int64_t dk, int64_t dv, int64_t sb,
+                   int64_t st, int64_t sh, int64_t osb, int64_t ost, int64_t osh, int64_t dsb, int64_t dst,
+                   int64_t dsh, int64_t lse, int64_t delta, int B, int H, int Hkv, int Tq, int Tk,
+                   int q_offset, float scale, int64_t dkv_sb, int64_t dkv_st, int64_t dkv_sh,
+                   const py::sequence& bases, int64_t kv_sb, int64_t kv_st, int64_t v_off, int Tl,
+                   int zigzag, int64_t flags, int64_t epoch, int64_t err, int64_t stream) {
+          const KvPeers kp = kv_peers(bases, kv_sb, kv_st, v_off, Tl, zigzag, flags, epoch);
+          AttnArgs a;
+          a.q = hv(q, sb, st, sh);
+          a.o = hv(o, osb, ost, osh);
+          a.dout = hv(dout, osb, ost, osh);
+          a.dq = hv(dq, dsb, dst, dsh);
+          a.dk = hv(dk, dkv_sb, dkv_st, dkv_sh);
+          a.dv = hv(dv, dkv_sb, dkv_st, dkv_sh);
+          a.lse = P<float>(lse);
+          a.delta = P<float>(delta);
+          a.B = B;
+          a.H = H;
+          a.Hkv = Hkv;
+          a.Tq = Tq;
+          a.Tk = Tk;
+          a.q_offset = q_offset;
+          a.causal = 1;
+          a.scale = scale;
+          a.err = P<uint32_t>(err);
+          a.peers = &kp;
+          check(attn_bwd_launch(a, S(stream)), "attn_bwd_peers");
+        });
+
   m.def("attn_set_impl", [](int impl) { attn_set_impl(impl); },
         "0: tensor-core forward when the layout allows (default); 1: mma.sync forward");
   m.def("attn_get_impl", []() { return attn_get_impl(); });
@@ -423,6 +495,10 @@ PYBIND11_MODULE(_C, m) {
   m.def("cp_kv_gather", [tp_args](const py::dict& d, int64_t st) {
     check(cp_kv_gather_launch(tp_args(d), S(st)), "cp_kv_gather");
   });
+  m.def("cp_kv_publish", [tp_args](const py::dict& d, int64_t st) {
+    check(cp_kv_publish_launch(tp_args(d), S(st)), "cp_kv_publish");
+  });
+  m.def("kv_publish_words", []() { return kKvPublishWords; });
   m.def("cp_kv_reduce", [tp_args](const py::dict& d, int64_t st) {
     check(cp_kv_reduce_launch(tp_args(d), S(st)), "cp_kv_reduce");
   });

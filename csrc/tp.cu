@@ -553,6 +553,40 @@ __global__ void __launch_bounds__(512) cp_kv_gather_kernel(const TpArgs a) {
   finish(a, &fail);
 }
 
+// Streaming form of the gather: this rank's k/v rows (both halves of each
+// local sequence under the zig-zag split; the order is the local one) into
+// its own compact [B, Tl, 2C] symmetric buffer peer_bufs[rank], then, once
+// every CTA's stores are fenced at system scope, the launch's last CTA stores
+// `epoch` with release semantics into word `rank` of every peer's flag buffer
+// (peer_flags[q][rank]). The attention kernels of every rank read these rows
+// in place through TMA after seeing that word reach the epoch; no peer data
+// moves here. Word kKvPublishCount of this rank's flag buffer counts the
+// launch's finished CTAs. The buffer is rewritten one step later, after the
+// data-parallel gradient reduction every rank of the group takes part in:
+// no rank reaches it while a peer's backward may still read the rows.
+__global__ void __launch_bounds__(512) cp_kv_publish_kernel(const TpArgs a) {
+  const int C = a.cols / 2;
+  const int vpr = a.cols / 8;                       // 16-byte vectors per k/v row
+  const int64_t nvec = (int64_t)a.B * a.Tl * vpr;
+  __nv_bfloat16* mine = reinterpret_cast<__nv_bfloat16*>(a.peer_bufs[a.rank]);
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = v / vpr;
+    const int c = (int)(v % vpr) * 8;
+    const uint4 w = *reinterpret_cast<const uint4*>(a.src + i * a.src_ld + C + c);
+    *reinterpret_cast<uint4*>(mine + i * a.cols + c) = w;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  uint32_t* count = a.peer_flags[a.rank] + kKvPublishCount;
+  if (atomicAdd(count, 1u) != gridDim.x - 1) return;
+  *count = 0;
+  __threadfence_system();
+  for (int q = 0; q < a.world; ++q) st_release_sys(a.peer_flags[q] + a.rank, a.epoch);
+  if (a.byte_counter) atomicAdd(a.byte_counter, cp_convention_bytes(a));
+}
+
 __global__ void __launch_bounds__(512) cp_kv_reduce_kernel(const TpArgs a) {
   __shared__ int fail;
   if (threadIdx.x == 0) fail = 0;
@@ -663,6 +697,16 @@ int cp_kv_gather_launch(TpArgs a, cudaStream_t s) {
     return launch_succeeded() ? 0 : -11;
   }
   cp_kv_gather_kernel<<<a.nblocks, 512, 0, s>>>(a);
+  count_launches(1);
+  return launch_succeeded() ? 0 : -11;
+}
+
+int cp_kv_publish_launch(TpArgs a, cudaStream_t s) {
+  if (!common_ok(a) || a.cols % 16 || a.src_ld % 8 || a.B <= 0 || a.Tl <= 0 || !a.src ||
+      a.world > kKvPublishCount)
+    return -1;
+  if (a.zigzag && a.Tl % 2) return -1;
+  cp_kv_publish_kernel<<<a.nblocks, 512, 0, s>>>(a);
   count_launches(1);
   return launch_succeeded() ? 0 : -11;
 }

@@ -78,6 +78,14 @@ int tp_ce_finish_launch(TpArgs a, cudaStream_t s);
 // Zig-zag: own chunks to their natural rows, then every other chunk up to
 // 2*world-1-rank from its owner.
 int cp_kv_gather_launch(TpArgs a, cudaStream_t s);
+// Streaming form: copy this rank's k/v rows (local order) into its compact
+// [B, Tl, 2C] buffer peer_bufs[rank] and publish `epoch` into word `rank` of
+// every peer's flag buffer (system-scope release, after all rows are fenced).
+// The flag buffers here are the small publish buffers of kKvPublishWords
+// words, not the handshake arrays above.
+constexpr int kKvPublishCount = 8;                    // finished-CTA counter word
+constexpr int kKvPublishWords = kKvPublishCount + 8;  // words per rank
+int cp_kv_publish_launch(TpArgs a, cudaStream_t s);
 // Reduce-scatter of the key/value gradients: this rank's block summed over
 // ranks rank..world-1 (the ranks whose queries saw these keys), in rank
 // order, into columns [C, 3C) of the local dqkv rows (out_bf16, ld).

@@ -32,6 +32,8 @@ __all__ = [
     "linear_fwd",
     "attention_fwd",
     "attention_bwd",
+    "attention_fwd_peers",
+    "attention_bwd_peers",
     "layernorm_fwd",
     "layernorm_bwd",
     "colsum_bf16",
@@ -293,6 +295,57 @@ def attention_bwd(q, k, v, o, dout, dq, dk, dv, lse, delta, B: int, H: int, Tq: 
                    dsb, dst, dsh, lse.data_ptr(), delta.data_ptr(), B, H, kv_heads or H, Tq, Tk,
                    q_offset, int(causal), float(scale), ksb, kst, ksh, dksb, dkst, dksh, _err_ptr(),
                    _stream())
+
+
+def _peer_args(peers: dict) -> tuple:
+    return (list(peers["bases"]), int(peers["sb"]), int(peers["st"]), int(peers["v_off"]),
+            int(peers["Tl"]), int(peers["zigzag"]), int(peers["flags"]), int(peers["epoch"]) & 0xFFFFFFFF)
+
+
+def attention_fwd_peers(q: torch.Tensor, o: torch.Tensor, lse: torch.Tensor, B: int, H: int, Tq: int,
+                        Tk: int, q_offset: int, peers: dict, q_rows: Optional[int] = None,
+                        kv_heads: Optional[int] = None, scale: Optional[float] = None) -> None:
+    """Causal attention whose keys and values are read in place from their
+    owners (context parallelism, streaming form): ``peers`` describes every
+    rank's compact key/value buffer -- ``bases`` (this process's address of
+    rank q's [B, Tl, 2C] bf16 buffer), ``sb`` / ``st`` (element strides of a
+    sequence and a row), ``v_off`` (element offset of the value columns),
+    ``Tl``, ``zigzag``, ``flags`` (this rank's publish words) and ``epoch``
+    (the epoch the owners published these rows under). ``Tk`` counts natural
+    key positions; the kernel maps each 64-key block to its owner's rows.
+    Tensor-core kernel only: a layout it cannot take raises."""
+    qr = Tq if q_rows is None else q_rows
+    scale = 1.0 / math.sqrt(64) if scale is None else scale
+    qsb, qst, qsh = _head_strides(q, qr, H)
+    osb, ost, osh = _head_strides(o, qr, H)
+    lib().attn_fwd_peers(q.data_ptr(), o.data_ptr(), qsb, qst, qsh, osb, ost, osh, lse.data_ptr(), B, H,
+                         kv_heads or H, Tq, Tk, q_offset, float(scale), *_peer_args(peers), _err_ptr(),
+                         _stream())
+
+
+def attention_bwd_peers(q, o, dout, dq, dk, dv, lse, delta, B: int, H: int, Tq: int, Tk: int,
+                        q_offset: int, peers: dict, kv_rows: Optional[int] = None,
+                        q_rows: Optional[int] = None, kv_heads: Optional[int] = None,
+                        scale: Optional[float] = None) -> None:
+    """Backward of :func:`attention_fwd_peers`: keys and values read in place
+    from their owners; dK / dV of every key position seen are written to
+    ``dk`` / ``dv`` (natural order, ``kv_rows`` rows per sequence) as in
+    :func:`attention_bwd`."""
+    kr = Tk if kv_rows is None else kv_rows
+    qr = Tq if q_rows is None else q_rows
+    scale = 1.0 / math.sqrt(64) if scale is None else scale
+    qsb, qst, qsh = _head_strides(q, qr, H)
+    osb, ost, osh = _head_strides(o, qr, H)
+    if _head_strides(dout, qr, H) != (osb, ost, osh):
+        raise ValueError("dout must share o's strides")
+    dsb, dst, dsh = _head_strides(dq, qr, H)
+    dksb, dkst, dksh = _head_strides(dk, kr, H)
+    if _head_strides(dv, kr, H) != (dksb, dkst, dksh):
+        raise ValueError("dk and dv must share strides")
+    lib().attn_bwd_peers(q.data_ptr(), o.data_ptr(), dout.data_ptr(), dq.data_ptr(), dk.data_ptr(),
+                         dv.data_ptr(), qsb, qst, qsh, osb, ost, osh, dsb, dst, dsh, lse.data_ptr(),
+                         delta.data_ptr(), B, H, kv_heads or H, Tq, Tk, q_offset, float(scale), dksb, dkst,
+                         dksh, *_peer_args(peers), _err_ptr(), _stream())
 
 
 # ----------------------------------------------------------------- layernorm --

@@ -38,9 +38,26 @@ buffer keeps the natural order; the gather pulls every chunk up to 2p-1-r
 from its owner, and the reduce sums each own chunk over the two halves'
 dK/dV partials of every rank that saw it.
 
+Streaming form (``kv="stream"``): no gathered copy. ``cp_kv_publish``
+(csrc/tp.cu) copies this rank's k/v rows, in local order, into its own compact
+per-layer symmetric buffer ([B, T/p, 2C]: a p-th of the gathered one) and
+stores an epoch into word ``rank`` of every peer's publish buffer (system-scope
+release after the rows are fenced). The tensor-core attention kernels
+(``N.attention_fwd_peers`` / ``N.attention_bwd_peers``) then take one TMA map
+per owner over that owner's buffer: before its first load from rank q a
+producer waits (bounded) for rank q's word to reach the epoch, and every
+64-key block is loaded straight from its owner's memory over NVLink (plain
+tile loads, no cluster multicast), overlapped with the MMAs of the blocks
+already in shared memory. The backward reads the same buffers under the
+epoch the forward published; the dK/dV partials and their reduction are the
+gathered form's. A buffer is rewritten one step later, after the
+data-parallel gradient reduction of the same group, which no rank passes
+while a peer's backward may still read it.
+
 Payload per rank per layer in the reference convention: the gather is charged
 its output (2 x B x T x C x 2 bytes: K and V, bf16), the reduce-scatter its
-input (the same), as for ``_GatherSequence``.
+input (the same), as for ``_GatherSequence``; the streaming form is charged
+the same (the reference convention counts the logical collective).
 """
 
 from __future__ import annotations
@@ -74,7 +91,8 @@ class NativeCP:
 
     def __init__(self, config: GPTConfig, B: int, T: int, group=None,
                  device: Optional[torch.device] = None, nblocks: int = 128,
-                 layers: Optional[list] = None, slots: int = 1, balance: str = "zigzag") -> None:
+                 layers: Optional[list] = None, slots: int = 1, balance: str = "zigzag",
+                 kv: str = "gather") -> None:
         if not dist.is_initialized():
             raise RuntimeError("NativeCP needs an initialised process group")
         if config.kv_heads != config.n_head:
@@ -94,6 +112,12 @@ class NativeCP:
             raise ValueError(f"unknown balance {balance!r}")
         self.zigzag = balance == "zigzag"
         self.balance = balance
+        if kv not in ("gather", "stream"):
+            raise ValueError(f"unknown kv mode {kv!r} (gather or stream)")
+        self.stream = kv == "stream"
+        self.kv_mode = kv
+        if self.stream and not self.zigzag and self.Tl % 128:
+            raise ValueError(f"streamed keys need T / p a multiple of 128, got {self.Tl}")
         if self.zigzag:
             h = self.Tl // 2
             if self.Tl % 2 or h % 128:
@@ -114,17 +138,29 @@ class NativeCP:
         nl = len(layers) * slots
         self.slots = slots
         self.slot = 0
-        self._kv = SymmetricBuffer(nl * rows * 2 * C * 2, group, dev)     # per-layer gathered k/v
+        # per-layer k/v: the gathered sequence, or (streaming) this rank's rows only
+        kv_rows = B * self.Tl if self.stream else rows
+        self._kv_rows = kv_rows
+        self._kv = SymmetricBuffer(nl * kv_rows * 2 * C * 2, group, dev)
         self._dkv = SymmetricBuffer(rows * 2 * C * 2, group, dev)         # dk/dv partials (reused)
         # zig-zag: the second half's queries write their own partials
         self._dkv2 = SymmetricBuffer(rows * 2 * C * 2, group, dev) if self.zigzag else None
         self._flags = SymmetricBuffer(N.lib().tp_flag_words() * 4, group, dev)
-        kv = self._kv.view(bf, nl * rows * 2 * C).view(nl, rows, 2 * C)
+        kv = self._kv.view(bf, nl * kv_rows * 2 * C).view(nl, kv_rows, 2 * C)
         self.kv = [kv[i] for i in range(nl)]
         self.dkv = self._dkv.view(bf, rows * 2 * C).view(rows, 2 * C)
         self.dkv2 = self._dkv2.view(bf, rows * 2 * C).view(rows, 2 * C) if self.zigzag else None
-        self._kv_ptrs = [torch.tensor([p + i * rows * 2 * C * 2 for p in self._kv.peer_ptrs],
+        self._kv_ptrs = [torch.tensor([p + i * kv_rows * 2 * C * 2 for p in self._kv.peer_ptrs],
                                       dtype=torch.int64, device=dev) for i in range(nl)]
+        self._pub = None
+        if self.stream:
+            # word q: the last epoch rank q published; then the publish
+            # kernel's finished-CTA counter. Starts at zero on every rank.
+            self._pub = SymmetricBuffer(N.lib().kv_publish_words() * 4, group, dev)
+            self._pub.view(torch.int32).zero_()
+            dist.barrier(group=group)
+            self.pub_counter = 0
+            self.pub_epoch = [0] * nl
         self.byte_counter = torch.zeros(1, dtype=torch.int64, device=dev)
         self.epoch = 0
 
@@ -167,10 +203,43 @@ class NativeCP:
         d.update(kw)
         return d
 
+    def _peers(self, i: int, epoch: int) -> dict:
+        """Owner buffers of layer-slot i for the streaming attention calls."""
+        C = self.C
+        off = i * self._kv_rows * 2 * C * 2
+        return {"bases": [p + off for p in self._kv.peer_ptrs], "sb": self.Tl * 2 * C, "st": 2 * C,
+                "v_off": C, "Tl": self.Tl, "zigzag": int(self.zigzag), "flags": self._pub.ptr,
+                "epoch": epoch}
+
+    def _publish(self, i: int, qkv) -> int:
+        self.pub_counter += 1
+        ep = self.pub_counter & 0xFFFFFFFF
+        d = {"peer_bufs": self._kv_ptrs[i].data_ptr(), "peer_flags": self._pub.peer_ptrs_dev.data_ptr(),
+             "rank": self.rank, "world": self.world, "nblocks": self.nblocks, "epoch": ep,
+             "err": N.error_word(self.device).data_ptr(), "byte_counter": self.byte_counter.data_ptr(),
+             "cols": 2 * self.C, "B": self.B, "Tl": self.Tl, "src": qkv.data_ptr(),
+             "src_ld": qkv.stride(0), "zigzag": int(self.zigzag)}
+        N.lib().cp_kv_publish(d, torch.cuda.current_stream(self.device).cuda_stream)
+        self.pub_epoch[i] = ep
+        return ep
+
     # ------------------------------------------------------------ hooks --
     def attention_fwd(self, l: int, qkv, y, lse, B: int, H: int, Tl: int) -> None:
         C, T = self.C, self.T
         i = self._kv_index(l)
+        if self.stream:
+            comms.record_external("all_gather", B * T * 2 * C, B * T * 2 * C * 2)
+            peers = self._peers(i, self._publish(i, qkv))
+            if not self.zigzag:
+                N.attention_fwd_peers(qkv[:, :C], y, lse, B, H, Tl, (self.rank + 1) * self.Tl, self.pos0,
+                                      peers)
+                return
+            h = self.h
+            lse2 = lse.view(-1)[: 2 * B * H * h].view(2, B, H, h)
+            for half, k in enumerate(self.chunks):
+                N.attention_fwd_peers(qkv[half * h:, :C], y[half * h:], lse2[half], B, H, h, (k + 1) * h,
+                                      k * h, peers, q_rows=Tl)
+            return
         kv = self.kv[i]
         nbytes = B * T * 2 * C * 2
         comms.record_external("all_gather", B * T * 2 * C, nbytes)
@@ -190,7 +259,25 @@ class NativeCP:
 
     def attention_bwd(self, l: int, qkv, y, dy, dqkv, lse, delta, B: int, H: int, Tl: int) -> None:
         C, T = self.C, self.T
-        kv, dkv = self.kv[self._kv_index(l)], self.dkv
+        i = self._kv_index(l)
+        kv, dkv = self.kv[i], self.dkv
+        if self.stream:
+            peers = self._peers(i, self.pub_epoch[i])
+            if not self.zigzag:
+                N.attention_bwd_peers(qkv[:, :C], y, dy, dqkv[:, :C], dkv[:, :C], dkv[:, C:], lse, delta, B, H,
+                                      Tl, (self.rank + 1) * self.Tl, self.pos0, peers, kv_rows=T)
+                extra = {}
+            else:
+                h = self.h
+                lse2 = lse.view(-1)[: 2 * B * H * h].view(2, B, H, h)
+                delta2 = delta.view(-1)[: 2 * B * H * h].view(2, B, H, h)
+                for half, (k, part) in enumerate(zip(self.chunks, (self.dkv, self.dkv2))):
+                    N.attention_bwd_peers(qkv[half * h:, :C], y[half * h:], dy[half * h:], dqkv[half * h:, :C],
+                                          part[:, :C], part[:, C:], lse2[half], delta2[half], B, H, h,
+                                          (k + 1) * h, k * h, peers, kv_rows=T, q_rows=Tl)
+                extra = {"zigzag": 1, "peer_bufs2": self._dkv2.peer_ptrs_dev.data_ptr()}
+            self._reduce(B, T, C, dqkv, extra)
+            return
         if not self.zigzag:
             Tk = (self.rank + 1) * self.Tl
             N.attention_bwd(qkv[:, :C], kv[:, :C], kv[:, C:], y, dy, dqkv[:, :C], dkv[:, :C],
@@ -205,6 +292,9 @@ class NativeCP:
                                 dqkv[half * h:, :C], part[:, :C], part[:, C:], lse2[half], delta2[half],
                                 B, H, h, Tk=(k + 1) * h, q_offset=k * h, kv_rows=T, q_rows=Tl)
             extra = {"zigzag": 1, "peer_bufs2": self._dkv2.peer_ptrs_dev.data_ptr()}
+        self._reduce(B, T, C, dqkv, extra)
+
+    def _reduce(self, B: int, T: int, C: int, dqkv, extra: dict) -> None:
         nbytes = B * T * 2 * C * 2
         comms.record_external("reduce_scatter", B * T * 2 * C, nbytes)
         d = self._args(self._dkv.peer_ptrs_dev.data_ptr(), out_bf16=dqkv.data_ptr(), src_ld=dqkv.stride(0),
@@ -213,6 +303,6 @@ class NativeCP:
 
     def close(self) -> None:
         torch.cuda.synchronize(self.device)
-        for b in (self._kv, self._dkv, self._dkv2, self._flags):
+        for b in (self._kv, self._dkv, self._dkv2, self._flags, self._pub):
             if b is not None:
                 b.close()

@@ -18,6 +18,7 @@ import ctypes
 import math
 import os
 import tempfile
+import time
 from contextlib import contextmanager
 from types import SimpleNamespace
 
@@ -418,6 +419,66 @@ def cp_kv_gather(d, stream=0):
     dist.barrier(group=_group(d["peer_flags"]))
 
 
+def cp_kv_publish(d, stream=0):
+    """This rank's k/v rows (local order) into its compact buffer, then the
+    epoch into word ``rank`` of every peer's publish buffer."""
+    rank, world, B, Tl, cols = d["rank"], d["world"], d["B"], d["Tl"], d["cols"]
+    C = cols // 2
+    own = _at(_ptr_list(d["peer_bufs"], world)[rank], B * Tl * cols, torch.bfloat16).view(B, Tl, cols)
+    src = _at(d["src"], (B * Tl - 1) * d["src_ld"] + 3 * C, torch.bfloat16)
+    own.copy_(torch.as_strided(src, (B, Tl, cols), (Tl * d["src_ld"], d["src_ld"], 1), C))
+    for p in _ptr_list(d["peer_flags"], world):
+        _at(p, 16, torch.int32)[rank] = int(d["epoch"])
+
+
+def _owner_kv(peers, B, Tk):
+    """Natural-order [B, Tk, C] keys and values rebuilt from the owners'
+    compact buffers, once every owner's publish word has reached the epoch
+    (bounded wait: the owners are other processes)."""
+    bases, Tl, zz = peers["bases"], peers["Tl"], peers["zigzag"]
+    world, C, st = len(bases), peers["v_off"], peers["st"]
+    flags = _at(peers["flags"], world, torch.int32)
+    deadline = time.monotonic() + 60.0
+    while any(int(flags[q]) < peers["epoch"] for q in range(world)):
+        if time.monotonic() > deadline:
+            raise RuntimeError(f"publish words {flags.tolist()} never reached epoch {peers['epoch']}")
+        time.sleep(0.001)
+    bufs = [_at(b, B * peers["sb"], torch.bfloat16).view(B, Tl, st) for b in bases]
+    K = torch.zeros(B, Tk, C, dtype=torch.bfloat16)
+    V = torch.zeros(B, Tk, C, dtype=torch.bfloat16)
+    span = Tl // 2 if zz else Tl
+    for k0 in range(0, Tk, span):
+        c = k0 // span
+        if zz:
+            q, r0 = (c, 0) if c < world else (2 * world - 1 - c, span)
+        else:
+            q, r0 = c, 0
+        n = min(span, Tk - k0)
+        K[:, k0:k0 + n] = bufs[q][:, r0:r0 + n, :C]
+        V[:, k0:k0 + n] = bufs[q][:, r0:r0 + n, C:2 * C]
+    return K.reshape(B * Tk, C), V.reshape(B * Tk, C)
+
+
+def attention_fwd_peers(q, o, lse, B, H, Tq, Tk, q_offset, peers, q_rows=None, kv_heads=None, scale=None):
+    K, V = _owner_kv(peers, B, Tk)
+    attention_fwd(q, K, V, o, lse, B, H, Tq, Tk=Tk, q_offset=q_offset, scale=scale, q_rows=q_rows,
+                  kv_heads=kv_heads)
+
+
+def attention_bwd_peers(q, o, dout, dq, dk, dv, lse, delta, B, H, Tq, Tk, q_offset, peers, kv_rows=None,
+                        q_rows=None, kv_heads=None, scale=None):
+    K, V = _owner_kv(peers, B, Tk)
+    kr = Tk if kv_rows is None else kv_rows
+    # the kernels write dK / dV at their natural rows of a kr-row buffer
+    gk = torch.zeros(B * Tk, dk.shape[-1], dtype=dk.dtype)
+    gv = torch.zeros_like(gk)
+    attention_bwd(q, K, V, o, dout, dq, gk, gv, lse, delta, B, H, Tq, Tk=Tk, q_offset=q_offset, scale=scale,
+                  q_rows=q_rows, kv_heads=kv_heads)
+    for b in range(B):
+        dk[b * kr: b * kr + Tk].copy_(gk[b * Tk:(b + 1) * Tk])
+        dv[b * kr: b * kr + Tk].copy_(gv[b * Tk:(b + 1) * Tk])
+
+
 def cp_kv_reduce(d, stream=0):
     rank, world, B, Tl, cols, T, segs, _ = _cp_layout(d)
     C = cols // 2
@@ -736,7 +797,8 @@ OPS = {
     "embedding_fwd": embedding_fwd, "embedding_bwd": embedding_bwd,
     "cross_entropy_fwd_bwd": cross_entropy_fwd_bwd, "lm_head_cross_entropy": lm_head_cross_entropy,
     "attention_fwd": attention_fwd,
-    "attention_bwd": attention_bwd, "grad_sumsq": grad_sumsq, "clip_coef": clip_coef,
+    "attention_bwd": attention_bwd, "attention_fwd_peers": attention_fwd_peers,
+    "attention_bwd_peers": attention_bwd_peers, "grad_sumsq": grad_sumsq, "clip_coef": clip_coef,
     "adamw_step": adamw_step, "cast_f32_bf16": cast_f32_bf16, "cast_bf16_f32": cast_bf16_f32, "decode_embed": decode_embed,
     "decode_partials": decode_partials, "decode_attn": decode_attn, "decode_argmax": decode_argmax,
 }
@@ -744,6 +806,7 @@ OPS = {
 LIB = SimpleNamespace(zero_rs=zero_rs, zero_adamw_ag=zero_adamw_ag, zero_ag=zero_ag,
                       zero_flag_words=lambda: 16, zero_norm_words=lambda: 16, zero_max_blocks=lambda: 160,
                       cp_kv_gather=cp_kv_gather, cp_kv_reduce=cp_kv_reduce, tp_flag_words=lambda: 16,
+                      cp_kv_publish=cp_kv_publish, kv_publish_words=lambda: 16,
                       allreduce_p2p=allreduce_p2p, allreduce_p2p_slim=allreduce_p2p_slim, allreduce_mc=allreduce_mc, comm_flag_words=lambda: 16, tp_ag_rows=tp_ag_rows,
                       tp_rs_rows=tp_rs_rows, tp_embed_fwd=tp_embed_fwd, tp_embed_bwd=tp_embed_bwd,
                       tp_ce_stats=tp_ce_stats, tp_ce_finish=tp_ce_finish, loss_reduce=loss_reduce,

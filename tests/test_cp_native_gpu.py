@@ -36,7 +36,7 @@ WORKER = textwrap.dedent(r'''
     cfg = gpt2_config("gpt2", **json.loads(os.environ.get("G2B_CFG", '{"n_layer": 2, "n_positions": 1024}')))
     B, T = 2, int(os.environ.get("G2B_T", "1024"))
     Tl = T // world
-    cp = NativeCP(cfg, B, T, balance=os.environ["G2B_BALANCE"])
+    cp = NativeCP(cfg, B, T, balance=os.environ["G2B_BALANCE"], kv=os.environ.get("G2B_KV", "gather"))
     ddp = NativeDDP(ParamLayout(cfg), comm="p2p")
     eng = Engine(cfg, "cuda", grad_buffer=ddp.grad_buffer, seed=0)
     ddp.attach(eng)
@@ -78,7 +78,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _run(world: int, balance: str, cfg: dict | None = None):
+def _run(world: int, balance: str, cfg: dict | None = None, kv: str = "gather"):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     port = _free_port()
@@ -86,7 +86,7 @@ def _run(world: int, balance: str, cfg: dict | None = None):
     for r in range(world):
         env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r),
                    MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), G2B_ROOT=ROOT,
-                   NCCL_NVLS_ENABLE="0", G2B_BALANCE=balance)
+                   NCCL_NVLS_ENABLE="0", G2B_BALANCE=balance, G2B_KV=kv)
         if cfg is not None:
             env["G2B_CFG"] = json.dumps(cfg)
             env["G2B_T"] = str(cfg["n_positions"])
@@ -124,3 +124,20 @@ def test_native_cp_matches_single_gpu(world, balance, cfg):
             # K/V gathers, dK/dV reduce-scatters and the weight-gradient
             # all-reduce, charged by the kernels in the reference convention
             assert r["device_bytes"] == r["payload"], r
+
+
+# Keys and values streamed from their owners inside the attention kernels
+# (NativeCP(kv="stream")). These kernels have not yet run on a GPU; until
+# they have, the cases run only with G2B_CP_STREAM_GPU=1 (after the one-GPU
+# checks in test_cp_stream_gpu.py).
+@pytest.mark.skipif(os.environ.get("G2B_CP_STREAM_GPU") != "1",
+                    reason="streamed-KV kernels: set G2B_CP_STREAM_GPU=1 to run")
+@pytest.mark.parametrize("world,balance,cfg", [(2, "contiguous", None), (2, "zigzag", None),
+                                               (8, "zigzag", LARGE)])
+def test_native_cp_streamed_kv_matches_single_gpu(world, balance, cfg):
+    res = _run(world, balance, cfg, kv="stream")
+    print(res)
+    for r in res:
+        assert abs(r["loss"] - r["ref_loss"]) < 1e-3 * abs(r["ref_loss"]), r
+        assert r["worst_err"] < 2e-2, r
+        assert r["device_bytes"] == r["payload"], r

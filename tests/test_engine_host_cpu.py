@@ -119,7 +119,7 @@ def test_pipeline_matches_accumulated_engine(world, schedule, m):
     assert slots == want
 
 
-def _cp_worker(rank, world, balance):
+def _cp_worker(rank, world, balance, kv="gather"):
     import torch.distributed as dist
 
     import native_fake as nf
@@ -130,7 +130,7 @@ def _cp_worker(rank, world, balance):
     nf.install_in_process()
     cfg = GPTConfig(**{**CFG, "n_positions": 1024})
     B, T = 2, 256 * world
-    cp = NativeCP(cfg, B, T, device="cpu", balance=balance)
+    cp = NativeCP(cfg, B, T, device="cpu", balance=balance, kv=kv)
     eng = Engine(cfg, "cpu", seed=0)
     cp.attach(eng)
     g = torch.Generator().manual_seed(8)
@@ -153,22 +153,37 @@ def _cp_worker(rank, world, balance):
     ref.backward(idx)
     errs = {s.name: float((eng.g32(s.name) - ref.g32(s.name)).norm() / (ref.g32(s.name).norm() + 1e-12))
             for s in ref.layout.specs}
+    extra = {}
+    if kv == "stream":
+        # every rank published once per layer, in the same order
+        extra["pub_words"] = cp._pub.view(torch.int32)[:world].tolist()
+        extra["pub_counter"] = cp.pub_counter
+    extra["kv_bytes"] = cp._kv.nbytes
     cp.close()
     # the reference convention: per layer the gather is charged its output and
     # the reduce-scatter its input, 2 x B x T x C bf16 each (K and V)
     closed = cfg.n_layer * 2 * (2 * B * T * cfg.n_embd * 2)
     return {"loss": float(loss) / world, "ref_loss": ref_loss, "worst": max(errs.values()),
-            "worst_name": max(errs, key=errs.get), "payload": payload, "closed_form": closed}
+            "worst_name": max(errs, key=errs.get), "payload": payload, "closed_form": closed,
+            "layers": cfg.n_layer, "kv_row_bytes": 2 * cfg.n_embd * 2, "B": B, "T": T, **extra}
 
 
-@pytest.mark.parametrize("world,balance", [(2, "contiguous"), (2, "zigzag"), (4, "zigzag")])
-def test_context_parallel_matches_full_sequence(world, balance):
-    res = spawn_workers(_cp_worker, world, {"balance": balance}, backend="gloo", timeout=300)
+@pytest.mark.parametrize("world,balance,kv", [(2, "contiguous", "gather"), (2, "zigzag", "gather"),
+                                              (4, "zigzag", "gather"), (2, "contiguous", "stream"),
+                                              (2, "zigzag", "stream"), (4, "zigzag", "stream")])
+def test_context_parallel_matches_full_sequence(world, balance, kv):
+    res = spawn_workers(_cp_worker, world, {"balance": balance, "kv": kv}, backend="gloo", timeout=300)
     for r in (x.value for x in res):
         assert abs(r["loss"] - r["ref_loss"]) < 1e-4 * r["ref_loss"], r
         # bf16 rounding of the summed dK/dV partials is the only difference
         assert r["worst"] < 1e-2, r
         assert r["payload"] == r["closed_form"], r
+        # per layer: the gathered sequence, or (streaming) this rank's rows only
+        rows = r["B"] * r["T"] // (world if kv == "stream" else 1)
+        assert r["kv_bytes"] == -(-r["layers"] * rows * r["kv_row_bytes"] // 256) * 256, r
+        if kv == "stream":
+            assert r["pub_counter"] == r["layers"], r
+            assert r["pub_words"] == [r["layers"]] * world, r
 
 
 def _ddp_worker(rank, world, bucket_mb, small=False, comm="p2p", reduce_dtype="fp32"):

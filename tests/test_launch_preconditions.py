@@ -77,6 +77,33 @@ def test_collective_group_limits():
     _rejected(L.cp_kv_gather, dict(base, world=9), 0, name="cp_kv_gather")
     _rejected(L.cp_kv_gather, dict(base, world=2, Tl=3, zigzag=1), 0, name="cp_kv_gather")
     _rejected(L.cp_kv_reduce, dict(base, world=2, zigzag=1), 0, name="cp_kv_reduce")
+    # streaming publish: group too large, odd zig-zag length, rows not whole 16-byte vectors
+    _rejected(L.cp_kv_publish, dict(base, world=9), 0, name="cp_kv_publish")
+    _rejected(L.cp_kv_publish, dict(base, world=2, Tl=3, zigzag=1), 0, name="cp_kv_publish")
+    _rejected(L.cp_kv_publish, dict(base, world=2, cols=12), 0, name="cp_kv_publish")
     # tensor-parallel row gather with a row length that is not whole 16-byte vectors
     _rejected(L.tp_ag_rows, {"peer_bufs": A16, "peer_flags": A16, "rank": 0, "world": 2,
                              "rows": 4, "cols": 12}, 0, name="tp_ag_rows")
+
+
+def _peer_attn_args(bases, B=1, H=2, Tq=128, Tk=256):
+    # q, o, q strides, o strides, lse, B, H, Hkv, Tq, Tk, q_offset, scale,
+    # owner bases, kv strides, v_off, Tl, zigzag, flags, epoch, err, stream
+    return (A16, A16, 128 * 128, 128, 64, 128 * 128, 128, 64, A16, B, H, H, Tq, Tk, 128, 0.125, bases,
+            128 * 256, 256, 128, 128, 0, A16, 1, 0, 0)
+
+
+def test_streamed_attention_preconditions():
+    # one to eight owners
+    with pytest.raises(RuntimeError, match="1 to 8 owner buffers"):
+        L.attn_fwd_peers(*_peer_attn_args([A16] * 9))
+    with pytest.raises(RuntimeError, match="1 to 8 owner buffers"):
+        L.attn_fwd_peers(*_peer_attn_args([]))
+    # no mma.sync fallback for keys read from their owners
+    L.attn_set_impl(1)
+    try:
+        _rejected(L.attn_fwd_peers, *_peer_attn_args([A16, A16]), name="attn_fwd_peers")
+    finally:
+        L.attn_set_impl(0)
+    # empty problem
+    _rejected(L.attn_fwd_peers, *_peer_attn_args([A16, A16], Tq=0), name="attn_fwd_peers")
