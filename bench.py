@@ -231,7 +231,7 @@ def run_pipeline(args, world, rank):
     pp = args.pp or world // cp
     trainer = PipelineTrainer(cfg, args.batch, args.seq, args.micro_batches, pp=pp, cp=cp,
                               schedule=args.schedule, train=tc, comm_blocks=args.comm_blocks,
-                              cp_balance=args.cp_balance)
+                              cp_balance=args.cp_balance, cp_kv=args.cp_kv)
     trainer.schedule = False
     host, dev = make_data(cfg, args.micro_batches * args.batch, args.seq, 0, pool=2)
     L = N.lib()
@@ -270,6 +270,7 @@ def run_pipeline(args, world, rank):
     out["config"]["pp"], out["config"]["cp"] = pp, cp
     out["config"]["micro_batches"], out["config"]["schedule"] = args.micro_batches, args.schedule
     out["config"]["cp_balance"] = args.cp_balance if cp > 1 else None
+    out["config"]["cp_kv"] = args.cp_kv if cp > 1 else None
     trainer.close()
     return out
 
@@ -292,7 +293,7 @@ def run_native(args, world, rank):
              and (world == 1 or args.comm != "nccl"))
     trainer = Trainer(cfg, args.batch, args.seq, train=tc, comm=args.comm, schedule=False,
                       strategy=args.strategy, bucket_bytes=int(args.bucket_mb * 2**20),
-                      comm_blocks=args.comm_blocks, cp_balance=args.cp_balance, graph=graph,
+                      comm_blocks=args.comm_blocks, cp_balance=args.cp_balance, cp_kv=args.cp_kv, graph=graph,
                       reduce_dtype=args.reduce_dtype)
     # tensor and context parallel ranks all take the same global batch
     host, dev = make_data(cfg, args.batch, args.seq, 0 if args.strategy in ("tp", "cp") else rank)
@@ -338,6 +339,7 @@ def run_native(args, world, rank):
         out["config"]["reduce_dtype"] = args.reduce_dtype
     if args.strategy == "cp":
         out["config"]["cp_balance"] = args.cp_balance
+        out["config"]["cp_kv"] = args.cp_kv
     if args.strategy == "zero3":
         out["config"]["activations"] = "kept (no recompute): MFU counts the model FLOPs run"
         out["config"]["reduce_dtype"] = args.reduce_dtype
@@ -522,6 +524,9 @@ def main():
     ap.add_argument("--schedule", choices=["1f1b", "gpipe"], default="1f1b")
     ap.add_argument("--cp-balance", choices=["zigzag", "contiguous"], default="zigzag",
                     help="context-parallel split (cp and pp strategies)")
+    ap.add_argument("--cp-kv", choices=["gather", "stream"], default="gather",
+                    help="context-parallel keys/values: gathered before attention, or read in place "
+                         "from their owners by the attention kernels")
     ap.add_argument("--bucket-mb", type=float, default=25.0, help="gradient bucket size (MiB)")
     ap.add_argument("--comm-blocks", type=int, default=128,
                     help="CTAs of each fused all-reduce that overlaps backward")

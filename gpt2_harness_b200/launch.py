@@ -137,6 +137,8 @@ def main(argv=None, device: Optional[torch.device] = None) -> int:
     ap.add_argument("--micro-batches", type=int, default=8, help="micro-batches per step (pp)")
     ap.add_argument("--schedule", choices=["1f1b", "gpipe"], default="1f1b")
     ap.add_argument("--cp-balance", choices=["zigzag", "contiguous"], default="zigzag")
+    ap.add_argument("--cp-kv", choices=["gather", "stream"], default="gather",
+                    help="context-parallel keys/values: gathered, or streamed from their owners")
     ap.add_argument("--stop-at", type=int, default=0,
                     help="checkpoint and exit after this step (a time-boxed allocation); the LR "
                          "schedule still spans --steps")
@@ -173,10 +175,10 @@ def main(argv=None, device: Optional[torch.device] = None) -> int:
     if pipeline:
         trainer = PipelineTrainer(cfg, a.batch, a.seq, a.micro_batches, pp=a.pp or world // a.cp, cp=a.cp,
                                   schedule=a.schedule, train=tc, device=dev, seed=a.seed,
-                                  cp_balance=a.cp_balance)
+                                  cp_balance=a.cp_balance, cp_kv=a.cp_kv)
     else:
         trainer = Trainer(cfg, a.batch, a.seq, train=tc, comm=a.comm, device=dev, seed=a.seed,
-                          strategy=a.strategy, cp_balance=a.cp_balance)
+                          strategy=a.strategy, cp_balance=a.cp_balance, cp_kv=a.cp_kv)
     # data-parallel ranks read disjoint shards of the stream; the ranks of a
     # context-parallel group or a pipeline all read the same sequences
     shared = a.strategy in ("tp", "cp", "pp")

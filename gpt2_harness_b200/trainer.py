@@ -65,6 +65,9 @@ class Trainer:
             overlaps backward (DDP and CP, p2p).
         cp_balance: context-parallel split, ``"zigzag"`` (two chunks per rank,
             equal causal work) or ``"contiguous"`` (one slice per rank).
+        cp_kv: context-parallel keys and values, ``"gather"`` (every rank
+            copies the keys its queries see before attention) or ``"stream"``
+            (the attention kernels read them in place from their owners).
         graph: replay the step as one CUDA graph (one rank, or native DDP).
         reduce_dtype: gradient wire of DDP and ZeRO-3, ``"fp32"`` or ``"bf16"``
             (buckets / unit reduce-scatters and root all-reduces on bf16
@@ -78,6 +81,7 @@ class Trainer:
                  device: Optional[torch.device] = None, seed: int = 0,
                  bucket_bytes: int = 25 * 1024 * 1024, schedule: bool = True,
                  strategy: str = "ddp", comm_blocks: int = 128, cp_balance: str = "zigzag",
+                 cp_kv: str = "gather",
                  graph: bool = False, reduce_dtype: str = "fp32") -> None:
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device())
@@ -127,7 +131,7 @@ class Trainer:
             from gpt2_harness_b200.parallel.cp_native import NativeCP
             from gpt2_harness_b200.parallel.ddp_native import NativeDDP
 
-            self.cp = NativeCP(config, batch_size, seq_len, device=self.device, balance=cp_balance)
+            self.cp = NativeCP(config, batch_size, seq_len, device=self.device, balance=cp_balance, kv=cp_kv)
             self.ddp = NativeDDP(ParamLayout(config), comm=comm, bucket_bytes=bucket_bytes,
                                  device=self.device, nblocks=comm_blocks)
             grad_buffer = self.ddp.grad_buffer
@@ -338,7 +342,8 @@ class PipelineTrainer:
     def __init__(self, config: GPTConfig, micro_batch: int, seq_len: int, micro_batches: int, *,
                  pp: Optional[int] = None, cp: int = 1, schedule: str = "1f1b",
                  train: Optional[TrainConfig] = None, device: Optional[torch.device] = None,
-                 seed: int = 0, comm_blocks: int = 128, cp_balance: str = "zigzag") -> None:
+                 seed: int = 0, comm_blocks: int = 128, cp_balance: str = "zigzag",
+                 cp_kv: str = "gather") -> None:
         from gpt2_harness_b200.parallel.cp_native import NativeCP
         from gpt2_harness_b200.parallel.pp_native import StageEngine, make_mesh
 
@@ -370,7 +375,7 @@ class PipelineTrainer:
             lay = self.engine.lay
             self.cp = NativeCP(config, micro_batch, seq_len, group=mesh.cp_group, device=self.device,
                                nblocks=comm_blocks, layers=range(lay.l0, lay.l1),
-                               slots=len(self.engine.slots), balance=cp_balance)
+                               slots=len(self.engine.slots), balance=cp_balance, kv=cp_kv)
             self.cp.attach(self.engine)
         lay = self.engine.lay
         mB = micro_batches * micro_batch
