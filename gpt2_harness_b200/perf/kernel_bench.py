@@ -8,6 +8,7 @@ fraction "of measured". The same script is the small case used for ncu
 captures (``--only <name> --iters 1``).
 
     python -m gpt2_harness_b200.perf.kernel_bench [--batch 16 --seq 1024] [--only attn_fwd]
+    python -m gpt2_harness_b200.perf.kernel_bench --only cp_attn   # CP gathered vs streamed K/V
 """
 
 from __future__ import annotations
@@ -225,6 +226,69 @@ def _comm_kernels(add, dev, M: int, C: int) -> None:
     add("zero_ag_w1", zero_ag, bytes_=span * 2 * 2)
 
 
+def run_cp_stream(world: int = 8, Tl: int = 2048, H: int = 20, batch: int = 1, iters: int = 20) -> list[dict]:
+    """Context-parallel attention of one zig-zag rank (GPT-2 large widths,
+    16k tokens over 8 ranks by default), forward and backward, with keys and
+    values from a gathered natural-order buffer against streamed from their
+    owners' compact buffers. The owners are emulated as separate buffers on
+    this GPU, so the difference is the cost of the per-owner maps and publish
+    waits, not NVLink. Run only when named (``--only cp_attn``)."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    bf = torch.bfloat16
+    pk = _peaks()
+    C, T, h = H * 64, world * Tl, Tl // 2
+    owners = [torch.randn(batch, Tl, 2 * C, device=dev).to(bf) for _ in range(world)]
+    kvn = torch.empty(batch, T, 2 * C, device=dev, dtype=bf)
+    for c in range(2 * world):
+        q, r0 = (c, 0) if c < world else (2 * world - 1 - c, h)
+        kvn[:, c * h:(c + 1) * h] = owners[q][:, r0:r0 + h]
+    kvn = kvn.view(batch * T, 2 * C)
+    flags = torch.ones(16, dtype=torch.int32, device=dev)
+    peers = {"bases": [o.data_ptr() for o in owners], "sb": Tl * 2 * C, "st": 2 * C, "v_off": C, "Tl": Tl,
+             "zigzag": 1, "flags": flags.data_ptr(), "epoch": 1}
+    rank = 0
+    spans = [(half * h, k * h, (k + 1) * h) for half, k in enumerate((rank, 2 * world - 1 - rank))]
+    q = torch.randn(batch * Tl, C, device=dev).to(bf)
+    dy = torch.randn(batch * Tl, C, device=dev).to(bf)
+    o = torch.empty(batch * Tl, C, device=dev, dtype=bf)
+    dq = torch.empty_like(o)
+    lse = torch.empty(2, batch, H, h, device=dev)
+    delta = torch.empty_like(lse)
+    dkv = torch.empty(batch * T, 2 * C, device=dev, dtype=bf)
+    # causal area of the two halves: queries of chunk k see keys [0, (k+1)h)
+    area = sum(h * k0 + h * h / 2 for _, k0, _ in spans)
+    fl = 4.0 * batch * H * area * 64
+
+    def fwd(stream):
+        for i, (r0, q0, Tk) in enumerate(spans):
+            if stream:
+                N.attention_fwd_peers(q[r0:], o[r0:], lse[i], batch, H, h, Tk, q0, peers, q_rows=Tl)
+            else:
+                N.attention_fwd(q[r0:], kvn[:, :C], kvn[:, C:], o[r0:], lse[i], batch, H, h, Tk=Tk, q_offset=q0,
+                                kv_rows=T, q_rows=Tl)
+
+    def bwd(stream):
+        for i, (r0, q0, Tk) in enumerate(spans):
+            if stream:
+                N.attention_bwd_peers(q[r0:], o[r0:], dy[r0:], dq[r0:], dkv[:, :C], dkv[:, C:], lse[i], delta[i],
+                                      batch, H, h, Tk, q0, peers, kv_rows=T, q_rows=Tl)
+            else:
+                N.attention_bwd(q[r0:], kvn[:, :C], kvn[:, C:], o[r0:], dy[r0:], dq[r0:], dkv[:, :C], dkv[:, C:],
+                                lse[i], delta[i], batch, H, h, Tk=Tk, q_offset=q0, kv_rows=T, q_rows=Tl)
+
+    rows = []
+    for name, fn, f in (("cp_attn_fwd_gathered", lambda: fwd(False), fl),
+                        ("cp_attn_fwd_streamed", lambda: fwd(True), fl),
+                        ("cp_attn_bwd_gathered", lambda: bwd(False), 2.5 * fl),
+                        ("cp_attn_bwd_streamed", lambda: bwd(True), 2.5 * fl)):
+        ms = time_kernel(fn, iters=iters)
+        tf = f / (ms * 1e-3) / 1e12
+        rows.append({"kernel": name, "ms": round(ms, 4), "tflops": round(tf, 1),
+                     "frac": round(tf / pk["tflops"], 3), "peak": pk["label"]})
+    N.check_errors()
+    return rows
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--batch", type=int, default=16)
@@ -233,7 +297,10 @@ def main() -> None:
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--json", default=None)
     a = ap.parse_args()
-    rows = run_suite(a.batch, a.seq, only=a.only, iters=a.iters)
+    if a.only and a.only.startswith("cp_attn"):
+        rows = run_cp_stream(iters=a.iters)
+    else:
+        rows = run_suite(a.batch, a.seq, only=a.only, iters=a.iters)
     for r in rows:
         print(json.dumps(r))
     if a.json:
