@@ -513,6 +513,47 @@ def _ppcp_worker(rank, world):
             "stage": tr.mesh.stage, "cp_rank": tr.mesh.cp_rank}
 
 
+def _ppcp_small_worker(rank, world, kv):
+    import torch.distributed as dist
+
+    import native_fake as nf
+    from gpt2_harness_b200.config import GPTConfig
+    from gpt2_harness_b200.models.engine import Engine
+    from gpt2_harness_b200.trainer import PipelineTrainer
+
+    nf.install_in_process()
+    # PP=2 x CP=2 at toy widths: three micro-batches, so under 1F1B the first
+    # stage keeps two K/V slots in flight and each backward must read the
+    # slot (and, streamed, the publish epoch) of its own micro-batch
+    cfg = GPTConfig(**{**CFG, "n_positions": 512})
+    B, T, m = 1, 512, 3
+    tr = PipelineTrainer(cfg, B, T, m, pp=2, cp=2, device="cpu", seed=0, cp_kv=kv)
+    st = tr.engine
+    g = torch.Generator().manual_seed(23)
+    idx = torch.randint(0, cfg.vocab_size, (m * B, T), generator=g)
+    tgt = torch.randint(0, cfg.vocab_size, (m * B, T), generator=g)
+    loss = tr.step_async(idx, tgt).reshape(1).clone()
+    dist.all_reduce(loss)
+    ref = Engine(cfg, "cpu", seed=0)
+    ref_losses = []
+    for i in range(m):
+        ref_losses.append(float(ref.forward(idx[i:i + 1], tgt[i:i + 1])))
+        ref.backward(idx[i:i + 1], accumulate=i > 0)
+    errs = {n: float((st.g32(n) - ref.g32(n) / m).norm() / (ref.g32(n).norm() / m + 1e-12))
+            for n in st.lay.specs if n not in ("wte.weight", "lm_head.weight")}
+    return {"loss": float(loss) / 2, "ref_loss": sum(ref_losses) / m, "worst": max(errs.values()),
+            "slots": tr.cp.slots}
+
+
+@pytest.mark.parametrize("kv", ["gather", "stream"])
+def test_pipeline_x_context_parallel_slots(kv):
+    res = spawn_workers(_ppcp_small_worker, 4, {"kv": kv}, backend="gloo", timeout=300)
+    for r in (x.value for x in res):
+        assert abs(r["loss"] - r["ref_loss"]) < 1e-3 * r["ref_loss"], r
+        assert r["worst"] < 2e-2, r
+    assert max(x.value["slots"] for x in res) == 2
+
+
 @pytest.mark.slow
 def test_pipeline_x_context_parallel_at_large_widths():
     res = spawn_workers(_ppcp_worker, 8, {}, backend="gloo", timeout=900)
