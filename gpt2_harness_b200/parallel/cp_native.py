@@ -71,6 +71,7 @@ from gpt2_harness_b200.config import GPTConfig
 from gpt2_harness_b200.ops import native as N
 from gpt2_harness_b200.parallel import comms
 from gpt2_harness_b200.parallel.symm import SymmetricBuffer
+from gpt2_harness_b200.utils.nvtx import nvtx_range
 
 __all__ = ["NativeCP"]
 
@@ -219,7 +220,8 @@ class NativeCP:
              "err": N.error_word(self.device).data_ptr(), "byte_counter": self.byte_counter.data_ptr(),
              "cols": 2 * self.C, "B": self.B, "Tl": self.Tl, "src": qkv.data_ptr(),
              "src_ld": qkv.stride(0), "zigzag": int(self.zigzag)}
-        N.lib().cp_kv_publish(d, torch.cuda.current_stream(self.device).cuda_stream)
+        with nvtx_range(f"cp/publish/{i}"):
+            N.lib().cp_kv_publish(d, torch.cuda.current_stream(self.device).cuda_stream)
         self.pub_epoch[i] = ep
         return ep
 
@@ -245,7 +247,8 @@ class NativeCP:
         comms.record_external("all_gather", B * T * 2 * C, nbytes)
         d = self._args(self._kv_ptrs[i].data_ptr(), src=qkv.data_ptr(), src_ld=qkv.stride(0),
                        zigzag=int(self.zigzag))
-        N.lib().cp_kv_gather(d, torch.cuda.current_stream(self.device).cuda_stream)
+        with nvtx_range(f"cp/gather/{i}"):
+            N.lib().cp_kv_gather(d, torch.cuda.current_stream(self.device).cuda_stream)
         if not self.zigzag:
             Tk = (self.rank + 1) * self.Tl
             N.attention_fwd(qkv[:, :C], kv[:, :C], kv[:, C:], y, lse, B, H, Tl, Tk=Tk,
@@ -299,7 +302,8 @@ class NativeCP:
         comms.record_external("reduce_scatter", B * T * 2 * C, nbytes)
         d = self._args(self._dkv.peer_ptrs_dev.data_ptr(), out_bf16=dqkv.data_ptr(), src_ld=dqkv.stride(0),
                        **extra)
-        N.lib().cp_kv_reduce(d, torch.cuda.current_stream(self.device).cuda_stream)
+        with nvtx_range("cp/reduce_scatter"):
+            N.lib().cp_kv_reduce(d, torch.cuda.current_stream(self.device).cuda_stream)
 
     def close(self) -> None:
         torch.cuda.synchronize(self.device)

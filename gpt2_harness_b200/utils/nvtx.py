@@ -6,7 +6,8 @@ context manager, so the training step pays nothing measurable. Set
 ``G2B_NVTX=1`` in the environment (before the first import) to emit ranges:
 ``fwd/h.<l>``, ``bwd/h.<l>``, ``lm_head+ce``, ``optimizer``, and on the
 communication side ``allreduce/bucket<i>``, ``tp/all_gather``,
-``tp/reduce_scatter``, ``zero3/gather/h.<l>``, ``zero3/reduce_scatter/h.<l>``.
+``tp/reduce_scatter``, ``zero3/gather/h.<l>``, ``zero3/reduce_scatter/h.<l>``,
+``cp/gather/<i>`` or ``cp/publish/<i>`` (layer-slot i) and ``cp/reduce_scatter``.
 """
 
 from __future__ import annotations
