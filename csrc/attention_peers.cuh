@@ -37,8 +37,9 @@ struct KvStreaming<KvPeerMaps> {
   static constexpr bool on = true;
 };
 
-// Owner rank of natural key position k and its row in the owner's buffer.
-__device__ __forceinline__ int kv_owner_row(const KvPeerMaps& kv, int k, int* local_row) {
+// Owner rank of natural key position k and its row in the owner's buffer
+// (host-callable too, for the CPU check of this arithmetic).
+__host__ __device__ __forceinline__ int kv_owner_row(const KvPeerMaps& kv, int k, int* local_row) {
   if (kv.zigzag) {
     const int h = kv.Tl >> 1;
     const int c = k / h;
