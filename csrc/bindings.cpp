@@ -545,6 +545,9 @@ m.def("decode_embed", [](int64_t tok, int64_t lens, int64_t wte, int64_t wpe, in
           "decode_attn");
   });
   m.def("decode_partials_numel", [](int B, int H, int Tmax) { return decode_partials_numel(B, H, Tmax); });
+  m.def("decode_set_impl", [](int impl) { decode_set_impl(impl); },
+        "decode attention kernel: 1 = one position a warp (default), 2 = four positions a warp");
+  m.def("decode_get_impl", []() { return decode_get_impl(); });
   m.def("decode_argmax", [](int64_t logits, int64_t ld, int V, int64_t tok, int64_t lens, int64_t hist,
                             int Tmax, int B, int64_t stream) {
     check(decode_argmax_launch(P<void>(logits), ld, V, P<int64_t>(tok), P<int>(lens), P<int64_t>(hist), Tmax,

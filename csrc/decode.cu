@@ -164,6 +164,159 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeArgs a) {
   }
 }
 
+// Restructured form of decode_attn_kernel (same append, same per-split
+// partials, so decode_combine is shared). Selected with decode_set_impl(2);
+// the default stays decode_attn_kernel until this one has been A/B-tested on
+// a GPU. A warp covers four positions at once: 8 lanes a position, each lane
+// one 16-byte vector (8 dims) of the key or value row, so a score needs a
+// 3-step shuffle tree (5 steps for one position a warp before) and every
+// load moves 16 bytes (4 before). Query groups of up to kMaxGroupV2 heads.
+constexpr int kMaxGroupV2 = 4;
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& w, float* f) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[i]));
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__global__ void __launch_bounds__(128) decode_attn_v2_kernel(const DecodeArgs a) {
+  __shared__ __align__(16) float q_s[kMaxGroupV2][64];
+  __shared__ float p_s[kMaxGroupV2][kChunk];
+  __shared__ float red[4][kMaxGroupV2][64];
+  __shared__ float ml_s[kMaxGroupV2][2];
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int G = a.H / a.Hkv;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane >> 3;      // position slot of this lane within the warp
+  const int d0 = (lane & 7) * 8;  // this lane's 8 dims
+  const int len = a.lens[b];
+  const int p_end = len + 1;
+  const int p0 = split * kChunk;
+  const int p1 = min(p0 + kChunk, p_end);
+  const __nv_bfloat16* row = a.qkv + (int64_t)b * a.ld;
+  const __nv_bfloat16* k_new = row + a.H * 64 + kvh * 64;
+  const __nv_bfloat16* v_new = row + (a.H + a.Hkv) * 64 + kvh * 64;
+  const int64_t cache_base = ((int64_t)b * a.Hkv + kvh) * a.Tmax * 64;
+  const int64_t ml_base = ((int64_t)b * a.H + kvh * G) * a.S + split;
+
+  if (split == len / kChunk && len < a.Tmax) {
+    if (threadIdx.x < 64)
+      a.kc[cache_base + (int64_t)len * 64 + threadIdx.x] = k_new[threadIdx.x];
+    else
+      a.vc[cache_base + (int64_t)len * 64 + threadIdx.x - 64] = v_new[threadIdx.x - 64];
+  }
+  if (p0 >= p1) {
+    if (threadIdx.x < G) {
+      a.part_ml[(ml_base + (int64_t)threadIdx.x * a.S) * 2 + 0] = -FLT_MAX;
+      a.part_ml[(ml_base + (int64_t)threadIdx.x * a.S) * 2 + 1] = 0.f;
+    }
+    return;
+  }
+  for (int i = threadIdx.x; i < G * 64; i += blockDim.x)
+    q_s[i / 64][i % 64] = bf(row[(kvh * G + i / 64) * 64 + (i % 64)]) * a.scale_log2;
+  __syncthreads();
+
+  // scores: warp w, iteration t -> positions p0 + 16 t + 4 w + sub
+  for (int pb = p0 + warp * 4; pb < p1; pb += 16) {
+    const int p = pb + sub;
+    const bool valid = p < p1;
+    uint4 kw = make_uint4(0u, 0u, 0u, 0u);
+    if (valid)
+      kw = (p == len) ? *reinterpret_cast<const uint4*>(k_new + d0)
+                      : *reinterpret_cast<const uint4*>(a.kc + cache_base + (int64_t)p * 64 + d0);
+    float kf[8];
+    bf16x8_to_f32(kw, kf);
+#pragma unroll
+    for (int g = 0; g < kMaxGroupV2; ++g) {
+      if (g < G) {
+        const float4 qa = *reinterpret_cast<const float4*>(&q_s[g][d0]);
+        const float4 qb = *reinterpret_cast<const float4*>(&q_s[g][d0 + 4]);
+        float s = qa.x * kf[0] + qa.y * kf[1] + qa.z * kf[2] + qa.w * kf[3] + qb.x * kf[4] +
+                  qb.y * kf[5] + qb.z * kf[6] + qb.w * kf[7];
+        s += __shfl_xor_sync(0xffffffffu, s, 4);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        if (valid && (lane & 7) == 0) p_s[g][p - p0] = s;
+      }
+    }
+  }
+  __syncthreads();
+  const int n = p1 - p0;
+  for (int g = warp; g < G; g += 4) {
+    const float s0 = lane < n ? p_s[g][lane] : -FLT_MAX;
+    const float s1 = lane + 32 < n ? p_s[g][lane + 32] : -FLT_MAX;
+    float m = fmaxf(s0, s1);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    const float e0 = lane < n ? exp2f(s0 - m) : 0.f;
+    const float e1 = lane + 32 < n ? exp2f(s1 - m) : 0.f;
+    if (lane < n) p_s[g][lane] = e0;
+    if (lane + 32 < n) p_s[g][lane + 32] = e1;
+    float l = e0 + e1;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+    if (lane == 0) {
+      ml_s[g][0] = m;
+      ml_s[g][1] = l;
+    }
+  }
+  __syncthreads();
+  // P V: the same position slots; each lane accumulates its 8 value dims
+  float acc[kMaxGroupV2][8];
+#pragma unroll
+  for (int g = 0; g < kMaxGroupV2; ++g)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[g][i] = 0.f;
+  for (int pb = p0 + warp * 4; pb < p1; pb += 16) {
+    const int p = pb + sub;
+    if (p < p1) {
+      const uint4 vw = (p == len) ? *reinterpret_cast<const uint4*>(v_new + d0)
+                                  : *reinterpret_cast<const uint4*>(a.vc + cache_base + (int64_t)p * 64 + d0);
+      float vf[8];
+      bf16x8_to_f32(vw, vf);
+#pragma unroll
+      for (int g = 0; g < kMaxGroupV2; ++g) {
+        if (g < G) {
+          const float pr = p_s[g][p - p0];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[g][i] = fmaf(pr, vf[i], acc[g][i]);
+        }
+      }
+    }
+  }
+  // the warp's four position slots hold the same dims: fold them
+#pragma unroll
+  for (int g = 0; g < kMaxGroupV2; ++g) {
+    if (g < G) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        acc[g][i] += __shfl_xor_sync(0xffffffffu, acc[g][i], 8);
+        acc[g][i] += __shfl_xor_sync(0xffffffffu, acc[g][i], 16);
+      }
+      if (sub == 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) red[warp][g][d0 + i] = acc[g][i];
+      }
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * 64; i += blockDim.x) {
+    const int g = i / 64, d = i % 64;
+    const float o = red[0][g][d] + red[1][g][d] + red[2][g][d] + red[3][g][d];
+    a.part_o[(ml_base + (int64_t)g * a.S) * 64 + d] = o;
+  }
+  if (threadIdx.x < G) {
+    a.part_ml[(ml_base + (int64_t)threadIdx.x * a.S) * 2 + 0] = ml_s[threadIdx.x][0];
+    a.part_ml[(ml_base + (int64_t)threadIdx.x * a.S) * 2 + 1] = ml_s[threadIdx.x][1];
+  }
+}
+
+int g_decode_impl = 1;
+
 __global__ void decode_combine_kernel(const DecodeArgs a) {
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;  // 64 threads
   const int64_t base = ((int64_t)b * a.H + h) * a.S;
@@ -264,11 +417,21 @@ int decode_attn_launch(const void* qkv, int64_t ld, void* kc, void* vc, const in
   a.Tmax = Tmax;
   a.S = (Tmax + kChunk - 1) / kChunk;
   a.scale_log2 = scale * 1.4426950408889634f;
-  decode_attn_kernel<<<dim3(a.S, Hkv, B), 128, 0, s>>>(a);
+  // the restructured kernel reads 16-byte vectors of the projection row
+  const bool v2 = g_decode_impl == 2 && H / Hkv <= kMaxGroupV2 && ld % 8 == 0 &&
+                  (reinterpret_cast<uintptr_t>(qkv) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(kc) & 15) == 0 && (reinterpret_cast<uintptr_t>(vc) & 15) == 0;
+  if (v2)
+    decode_attn_v2_kernel<<<dim3(a.S, Hkv, B), 128, 0, s>>>(a);
+  else
+    decode_attn_kernel<<<dim3(a.S, Hkv, B), 128, 0, s>>>(a);
   decode_combine_kernel<<<dim3(H, B), 64, 0, s>>>(a);
   count_launches(2);
   return launch_succeeded() ? 0 : -11;
 }
+
+void decode_set_impl(int impl) { g_decode_impl = impl == 2 ? 2 : 1; }
+int decode_get_impl() { return g_decode_impl; }
 
 int decode_partials_numel(int B, int H, int Tmax) {
   return B * H * ((Tmax + kChunk - 1) / kChunk) * 64;

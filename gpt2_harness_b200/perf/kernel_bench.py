@@ -9,6 +9,7 @@ captures (``--only <name> --iters 1``).
 
     python -m gpt2_harness_b200.perf.kernel_bench [--batch 16 --seq 1024] [--only attn_fwd]
     python -m gpt2_harness_b200.perf.kernel_bench --only cp_attn   # CP gathered vs streamed K/V
+    python -m gpt2_harness_b200.perf.kernel_bench --only decode_attn_v2   # restructured decode kernel
 """
 
 from __future__ import annotations
@@ -161,6 +162,25 @@ def run_suite(batch: int = 16, seq: int = 1024, C: int = 768, H: int = 12, V: in
     pb = torch.empty(n, device=dev, dtype=bf)
     hp = torch.tensor([3e-4, 0.9, 0.95, 1e-8, 0.1, 0.1, 0.1, 1.0], device=dev)
     add("adamw", lambda: N.adamw_step(p, gg, m1, v1, pb, n, hp), bytes_=n * (4 * 7 + 2))
+    # KV-cached decode attention: 32 sequences x H heads x 1000 cached positions
+    Bd, Td, pos = 32, 1024, 1000
+    qkv_d = torch.randn(Bd, 3 * H * 64, device=dev).to(bf)
+    kc_d = torch.randn(Bd, H, Td, 64, device=dev).to(bf)
+    vc_d = torch.randn(Bd, H, Td, 64, device=dev).to(bf)
+    lens_d = torch.full((Bd,), pos, dtype=torch.int32, device=dev)
+    Sd = (Td + 63) // 64
+    po = torch.empty(Bd * H * Sd * 64, device=dev)
+    pml = torch.empty(Bd * H * Sd * 2, device=dev)
+    od = torch.empty(Bd, H * 64, device=dev, dtype=bf)
+    kv_bytes = 2 * Bd * H * (pos + 1) * 64 * 2
+    dec = lambda: N.decode_attn(qkv_d, kc_d, vc_d, lens_d, po, pml, od, H, H)  # noqa: E731
+    add("decode_attn", dec, bytes_=kv_bytes)
+    if only == "decode_attn_v2":  # the restructured kernel, timed only when named
+        N.lib().decode_set_impl(2)
+        try:
+            add("decode_attn_v2", dec, bytes_=kv_bytes)
+        finally:
+            N.lib().decode_set_impl(1)
     _comm_kernels(add, dev, M, C)
     N.check_errors()
     return rows
