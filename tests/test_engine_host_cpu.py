@@ -431,6 +431,7 @@ def _launch_worker(rank, world, strategy, tmp, extra_args):
     ("pp", 2, ["--micro-batches", "2"]),
     ("pp", 4, ["--micro-batches", "2", "--cp", "2", "--seq", "512"]),
     ("cp", 2, ["--seq", "512"]),
+    ("cp", 2, ["--seq", "512", "--cp-kv", "stream"]),
     ("tp", 2, ["--config", '{"vocab_size": 256, "n_positions": 64, "n_layer": 2, "n_head": 3, "n_embd": 192}']),
 ])
 def test_launch_resume_reproduces_the_uninterrupted_run(tmp_path, strategy, world, extra):
